@@ -1,0 +1,361 @@
+"""Benchmark of the sparse-pooling training step (driver contract).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (the headline metric's config): a Mode-A fp32
+layer of N = 100,663,296 neurons, fan-in 8, D = 4096 inputs, G = 4096 mean-ReLU
+pooling groups of 24,576 neurons, batch B = 1024; one step = forward + backward
+(dX, dW, db) + fused Adam (beta = (0.9, 0.999), eps = 1e-8, lr = 1e-3, fp32
+moments).  Inputs are synthetic: x ~ N(0,1), upstream gradient ~ N(0,1),
+parameters from the layer's seeded init (seed 2 + rank, bias_std 0.1).
+
+Multi-GPU (torchrun, one rank per GPU): rank r owns a contiguous slice of
+groups; the pooled output is all-gathered and dX all-reduced over NCCL.  The
+total work is fixed, so scaling is "strong"; ``value`` is the whole-job
+throughput B*N / (max over ranks of the step time).
+
+``value`` is device-timed (CUDA events, K steps, barrier + synchronize on both
+sides) with inputs resident in HBM; parameters (5.2 GB) are far larger than
+L2, so every pass streams them from HBM.  ``e2e`` is the same metric through
+the public API with pinned host buffers (x and dy copied in, y copied out
+every step).  ``roofline`` is for the dominant kernel (the backward), timed
+with CUDA events on its launch stream.  ``cpu_baseline`` times the C oracle on
+a bounded slice of the same workload on the host cores (rank 0, N = 1).
+
+``--impl reference`` times the reference's CPU path (the oracle port: the
+reference's materialising PyTorch path does not fit 100M neurons) on the same
+config, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from datetime import timedelta
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+D, N, G, B = 4096, 100_663_296, 4096, 1024
+K_FAN = 8
+IDX_BYTES = 2
+METRIC = "neuron-samples/s fwd+bwd+opt @100M fan-in-8, B=1024; % HBM roofline; 1/2/4/8 GPU"
+UNIT = "neuron-samples/s"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def param_bytes(n):
+    return n * (K_FAN * 4 + K_FAN * IDX_BYTES + 4)
+
+
+def gather_bytes(b, n):
+    return b * n * K_FAN * 4
+
+
+def peak_hbm():
+    p = ROOT / "MEASURED_PEAKS.json"
+    try:
+        return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def config_dict(world):
+    return {"workload": "100M-neuron fan-in-8 Mode-A fp32 mean-ReLU layer: fwd+bwd+fused Adam step "
+                        "(D=4096, N=100,663,296, G=4096 groups of 24,576, B=1024)",
+            "D": D, "N": N, "G": G, "global_batch": B, "fan_in": K_FAN, "pool": "mean", "activation": "relu",
+            "indices": "int16, distinct sorted per neuron (reference init rule)",
+            "l2": "inputs larger than L2: 5.2 GB of parameters streamed from HBM every pass",
+            "parallelism": f"group-shard x{world}" if world > 1 else "single GPU"}
+
+
+class ClockSampler:
+    """Samples SM clock and clock-event reasons via NVML (read-only) in a thread."""
+
+    REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+               0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+               0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting"}
+
+    def __init__(self, index):
+        self.index = index
+        self.samples, self.reasons = [], set()
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._t = None
+        self.ok = False
+
+    def __enter__(self):
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        except Exception as e:  # noqa: BLE001
+            self.error = f"{type(e).__name__}: {e}"
+        return self
+
+    def _run(self):
+        nv = self._nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+                r = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                for bit, name in self.REASONS.items():
+                    if r & bit:
+                        self.reasons.add(name)
+            except Exception:  # noqa: BLE001
+                pass
+            self._stop.wait(0.2)
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self._t:
+            self._t.join(timeout=2)
+
+    def summary(self):
+        if not self.ok or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [],
+                    "note": getattr(self, "error", "no samples")}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons - {"gpu_idle"}), "samples": len(self.samples)}
+
+
+def cpu_baseline(target_s=12.0, steps=1):
+    """Time the C oracle (fwd + bwd + Adam) on a slice of whole groups of this workload."""
+    from granulelayer_b200.layout import SparseLayout, init_parameters
+    from oracle import oracle as O
+
+    cores = os.cpu_count() or 1
+    threads = max(1, min(cores, int(2e9 // (B * D * 8))))
+    n_g = N // G
+
+    def run(groups):
+        L = SparseLayout(D, n_g * groups, groups, 8, 8, False)
+        idx, w, b = init_parameters(L, "cpu", dtype=torch.float32, seed=2, bias_std=0.1)
+        gen = torch.Generator().manual_seed(5)
+        x = torch.randn(B, D, generator=gen).numpy()
+        dy = torch.randn(B, groups, generator=gen).numpy()
+        c = L.counts_tensor("cpu").numpy()
+        idx, w, b = idx.numpy(), w.numpy(), b.numpy()
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            O.forward(x, idx, w, b, c, "mean", "relu", threads)
+            _, dw, db = O.backward(x, idx, w, b, c, dy, "mean", "relu", threads)
+            O.adam_step(w.ravel(), dw.ravel(), np.zeros(w.size), np.zeros(w.size), 1e-3, 0.9, 0.999, 1e-8, 0.0, 1)
+            O.adam_step(b.ravel(), db.ravel(), np.zeros(b.size), np.zeros(b.size), 1e-3, 0.9, 0.999, 1e-8, 0.0, 1)
+        return (time.perf_counter() - t0) / steps
+
+    t1 = run(1)
+    groups = int(max(1, min(64, target_s / max(t1, 1e-3))))
+    dt = run(groups) if groups > 1 else t1
+    value = B * n_g * groups / dt
+    return {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{groups} of {G} groups (x{n_g} neurons) x {B} tokens of this workload, fwd+bwd+Adam, "
+                      f"float64 C oracle, {threads} threads of {cores} host CPUs; {dt:.2f} s per step",
+            "seconds_per_sample": dt}
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    cb = cpu_baseline(target_s=args.ref_seconds, steps=1)
+    groups = int(cb["sample"].split(" of ")[0])
+    from granulelayer_b200.layout import SparseLayout, init_parameters
+    from oracle import oracle as O
+
+    n_g = N // G
+    L = SparseLayout(D, n_g * groups, groups, 8, 8, False)
+    idx, w, b = init_parameters(L, "cpu", dtype=torch.float32, seed=2, bias_std=0.1)
+    gen = torch.Generator().manual_seed(5)
+    x = torch.randn(B, D, generator=gen).numpy()
+    dy = torch.randn(B, groups, generator=gen).numpy()
+    c = L.counts_tensor("cpu").numpy()
+    idx, w, b = idx.numpy(), w.numpy(), b.numpy()
+    threads = cb["cores"]
+    mw, vw, mb, vb = np.zeros(w.size), np.zeros(w.size), np.zeros(b.size), np.zeros(b.size)
+    wf, bf = w.ravel().astype(np.float64), b.ravel().astype(np.float64)
+    times = []
+    for s in range(args.warmup + args.steps):
+        t0 = time.perf_counter()
+        O.forward(x, idx, w, b, c, "mean", "relu", threads)
+        _, dw, db = O.backward(x, idx, w, b, c, dy, "mean", "relu", threads)
+        wf, mw, vw = O.adam_step(wf, dw.ravel(), mw, vw, 1e-3, 0.9, 0.999, 1e-8, 0.0, s + 1)
+        bf, mb, vb = O.adam_step(bf, db.ravel(), mb, vb, 1e-3, 0.9, 0.999, 1e-8, 0.0, s + 1)
+        w, b = wf.reshape(w.shape).astype(np.float32), bf.reshape(b.shape).astype(np.float32)
+        if s >= args.warmup:
+            times.append(time.perf_counter() - t0)
+    dt = sum(times) / len(times)
+    value = B * n_g * groups / dt
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+            "config": config_dict(world),
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                             "sample": cb["sample"].split(";")[0]},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "note": "reference CPU path = float64 C oracle restating the reference's algorithm on a bounded "
+                    "slice of whole groups; the reference's own PyTorch path materialises [B, H]"}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ref-seconds", type=float, default=4.0)
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        print("warning: fewer than 3 warm-up steps", file=sys.stderr)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+
+    import torch.distributed as dist
+
+    from granulelayer_b200 import FusedAdamW, SparsePoolingLayer, _native
+    from granulelayer_b200.distributed import GroupShardedLayer, ShardedTrainStep
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1 or "MASTER_ADDR" in os.environ:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    else:
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        os.environ.setdefault("MASTER_PORT", str(29500 + (os.getpid() % 1000)))
+        dist.init_process_group("nccl", rank=0, world_size=1, timeout=timedelta(seconds=300), device_id=dev)
+
+    lay = GroupShardedLayer(D, N, G, pooling="mean", device=dev, seed=2 + 0, bias_std=0.1)
+    opt = FusedAdamW([lay.weight, lay.bias], lr=1e-3, betas=(0.9, 0.999), eps=1e-8, moments="fp32")
+    trainer = ShardedTrainStep(lay, opt)
+    n_local = int(lay.counts.sum())
+    gen = torch.Generator(device=dev).manual_seed(1234)
+    x = torch.randn(B, D, device=dev, generator=gen)
+    dy = torch.randn(B, G, device=dev, generator=gen)
+    rt = lay.runtime()
+
+    # per-kernel timing: events around the forward and backward launches on their stream
+    ev = {"fwd": [], "bwd": []}
+    orig_fwd, orig_bwd = rt.forward, rt.backward
+
+    def timed(name, fn):
+        def wrap(*a, **k):
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            out = fn(*a, **k)
+            e.record()
+            ev[name].append((s, e))
+            return out
+        return wrap
+
+    for _ in range(args.warmup):
+        trainer.step(x, dy)
+    torch.cuda.synchronize(dev)
+    rt.forward, rt.backward = timed("fwd", orig_fwd), timed("bwd", orig_bwd)
+    dist.barrier()
+    torch.cuda.synchronize(dev)
+    n0 = _native.launch_count()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev.index) as clk:
+        start.record()
+        for _ in range(args.steps):
+            trainer.step(x, dy)
+        end.record()
+        torch.cuda.synchronize(dev)
+    dist.barrier()
+    launches = _native.launch_count() - n0
+    rt.forward, rt.backward = orig_fwd, orig_bwd
+    ms_local = start.elapsed_time(end) / args.steps
+    fwd_ms = statistics.mean(s.elapsed_time(e) for s, e in ev["fwd"])
+    bwd_ms = statistics.mean(s.elapsed_time(e) for s, e in ev["bwd"])
+    t = torch.tensor([ms_local, fwd_ms, bwd_ms], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, fwd_max, bwd_max = t.tolist()
+
+    # end to end through the public API: pinned host buffers in, pooled output out, every step
+    e2e = None
+    if not args.no_e2e:
+        xh = torch.randn(B, D, generator=torch.Generator().manual_seed(7)).pin_memory()
+        dyh = torch.randn(B, G, generator=torch.Generator().manual_seed(8)).pin_memory()
+        yh = torch.empty(B, G).pin_memory()
+        xd = torch.empty(B, D, device=dev)
+        dyd = torch.empty(B, G, device=dev)
+
+        def api_step():
+            xd.copy_(xh, non_blocking=True)
+            dyd.copy_(dyh, non_blocking=True)
+            xin = xd.detach().requires_grad_(True)
+            y = lay(xin)
+            y.backward(dyd)
+            opt.step()
+            yh.copy_(y.detach(), non_blocking=True)
+
+        for _ in range(2):
+            api_step()
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s2.record()
+        for _ in range(args.steps):
+            api_step()
+        e2.record()
+        torch.cuda.synchronize(dev)
+        t2 = torch.tensor([s2.elapsed_time(e2) / args.steps], device=dev)
+        dist.all_reduce(t2, op=dist.ReduceOp.MAX)
+        e2e = {"value": B * N / (t2.item() / 1e3), "unit": UNIT,
+               "h2d_bytes_per_step": xh.numel() * 4 + dyh.numel() * 4, "d2h_bytes_per_step": yh.numel() * 4,
+               "ms_per_step": t2.item()}
+
+    cb = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cb = cpu_baseline()
+        cb.pop("seconds_per_sample", None)
+
+    if rank == 0:
+        peak, peak_kind = peak_hbm()
+        bwd_bytes = param_bytes(n_local) + gather_bytes(B, n_local)
+        achieved = bwd_bytes / (bwd_ms * 1e-3) / 1e9
+        step_bytes = 2 * param_bytes(N) + 2 * gather_bytes(B, N)
+        traffic = os.environ.get("GL_BWD_DRAM_BYTES")
+        line = {
+            "metric": METRIC, "value": B * N / (ms / 1e3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": config_dict(world),
+            "hbm_roofline_step_frac": (step_bytes / (peak * 1e9)) / (ms / 1e3),
+            "roofline": {"bound": "hbm", "kernel": "gl_bwd_f32 (bwd_kernel<4,relu>)", "achieved": achieved,
+                         "peak": peak, "unit": "GB/s", "frac": achieved / peak, "peak_source": peak_kind,
+                         "traffic": float(traffic) if traffic else None,
+                         "algorithmic_bytes_per_launch": bwd_bytes,
+                         "definition": "(param + x-gather bytes) per launch / CUDA-event launch time; "
+                                       "gathers count as logical HBM bytes per the baseline definition"},
+            "kernels_ms": {"fwd": fwd_ms, "bwd": bwd_ms, "fwd_max_rank": fwd_max, "bwd_max_rank": bwd_max},
+            "clocks": clk.summary(), "gpu_launches": launches,
+            "e2e": e2e, "cpu_baseline": cb,
+        }
+        print(json.dumps(line), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,155 @@
+"""ctypes binding of the C ABI in ``include/granule_b200.h``.
+
+The library is loaded from ``granulelayer_b200/_lib/libgranule_b200.so`` (built
+in-tree by ``granulelayer_b200.build``).  There is no fallback: if the library
+is missing or its ABI version differs, every GPU entry point raises
+``NativeLibraryError``.  Launch helpers take torch tensors only to read their
+device pointers, strides and the current CUDA stream of their device; the
+library itself sees plain pointers and sizes.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+from pathlib import Path
+
+import torch
+
+ABI_VERSION = 1
+LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libgranule_b200.so"
+
+POOL_MEAN, POOL_SUM = 0, 1
+ACT_IDS = {"identity": 0, "relu": 1, "gelu": 2}
+
+# The exported entry points, in header order (checked by the CPU test suite).
+EXPORTS = ("gl_abi_version", "gl_status_string", "gl_last_cuda_error", "gl_fwd_f32", "gl_bwd_f32",
+           "gl_adam_f32", "gl_launch_count", "gl_fwd_auto_tokens", "gl_bwd_auto_tokens")
+
+
+class NativeLibraryError(RuntimeError):
+    """The sm_100a library is missing, stale or failed a call."""
+
+
+class GlFwdArgs(ctypes.Structure):
+    _fields_ = [("x", ctypes.c_void_p), ("idx", ctypes.c_void_p), ("w", ctypes.c_void_p), ("b", ctypes.c_void_p),
+                ("counts", ctypes.c_void_p), ("pre", ctypes.c_void_p),
+                ("B", ctypes.c_int64), ("D", ctypes.c_int64), ("NB", ctypes.c_int64),
+                ("g0", ctypes.c_int64), ("g1", ctypes.c_int64), ("ldx", ctypes.c_int64), ("ldp", ctypes.c_int64),
+                ("pool", ctypes.c_int32), ("act", ctypes.c_int32), ("tokens", ctypes.c_int32),
+                ("groups_per_cta", ctypes.c_int32)]
+
+
+class GlBwdArgs(ctypes.Structure):
+    _fields_ = [("x", ctypes.c_void_p), ("idx", ctypes.c_void_p), ("w", ctypes.c_void_p), ("b", ctypes.c_void_p),
+                ("counts", ctypes.c_void_p), ("gpre", ctypes.c_void_p), ("dx", ctypes.c_void_p),
+                ("dw", ctypes.c_void_p), ("db", ctypes.c_void_p),
+                ("B", ctypes.c_int64), ("D", ctypes.c_int64), ("NB", ctypes.c_int64),
+                ("g0", ctypes.c_int64), ("g1", ctypes.c_int64),
+                ("ldx", ctypes.c_int64), ("ldg", ctypes.c_int64), ("lddx", ctypes.c_int64),
+                ("pool", ctypes.c_int32), ("act", ctypes.c_int32), ("tokens", ctypes.c_int32),
+                ("groups_per_cta", ctypes.c_int32)]
+
+
+class GlAdamArgs(ctypes.Structure):
+    _fields_ = [("p", ctypes.c_void_p), ("g", ctypes.c_void_p), ("m", ctypes.c_void_p), ("v", ctypes.c_void_p),
+                ("n", ctypes.c_int64),
+                ("lr", ctypes.c_float), ("beta1", ctypes.c_float), ("beta2", ctypes.c_float),
+                ("eps", ctypes.c_float), ("weight_decay", ctypes.c_float), ("bc1", ctypes.c_float),
+                ("bc2", ctypes.c_float), ("zero_grad", ctypes.c_int32)]
+
+
+_lock = threading.Lock()
+_lib = None
+
+
+def library_path() -> Path:
+    return Path(os.environ.get("GRANULE_B200_LIB", LIB_PATH))
+
+
+def load(path=None) -> ctypes.CDLL:
+    """Load (once) and version-check the library; raise if unavailable."""
+    global _lib
+    with _lock:
+        if _lib is not None and path is None:
+            return _lib
+        p = Path(path) if path else library_path()
+        if not p.exists():
+            raise NativeLibraryError(f"{p} not found: build it with `python -m granulelayer_b200.build`")
+        lib = ctypes.CDLL(str(p))
+        lib.gl_abi_version.restype = ctypes.c_int
+        if lib.gl_abi_version() != ABI_VERSION:
+            raise NativeLibraryError(f"{p}: ABI version {lib.gl_abi_version()} != {ABI_VERSION}; rebuild it")
+        lib.gl_status_string.restype = ctypes.c_char_p
+        lib.gl_status_string.argtypes = [ctypes.c_int]
+        lib.gl_last_cuda_error.restype = ctypes.c_int
+        lib.gl_launch_count.restype = ctypes.c_int64
+        for name, st in (("gl_fwd_f32", GlFwdArgs), ("gl_bwd_f32", GlBwdArgs), ("gl_adam_f32", GlAdamArgs)):
+            fn = getattr(lib, name)
+            fn.restype = ctypes.c_int
+            fn.argtypes = [ctypes.POINTER(st), ctypes.c_void_p]
+        for name in ("gl_fwd_auto_tokens", "gl_bwd_auto_tokens"):
+            getattr(lib, name).restype = ctypes.c_int
+            getattr(lib, name).argtypes = [ctypes.c_int64]
+        if path is None:
+            _lib = lib
+        return lib
+
+
+def launch_count() -> int:
+    """Kernels the library has launched in this process (gl_launch_count)."""
+    return int(load().gl_launch_count())
+
+
+def _check(lib, rc: int, what: str):
+    if rc != 0:
+        msg = lib.gl_status_string(rc).decode()
+        cu = lib.gl_last_cuda_error()
+        extra = f" (cudaError {cu})" if cu else ""
+        raise NativeLibraryError(f"{what} failed: {msg} [{rc}]{extra}")
+
+
+def _ptr(t) -> int:
+    return 0 if t is None else t.data_ptr()
+
+
+def _stream(dev: torch.device) -> int:
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def _require_cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise NativeLibraryError("the B200 kernels need CUDA tensors (no CPU fallback on this path)")
+
+
+def fwd(x, idx, w, b, counts, pre, NB: int, g0: int, g1: int, pool: int, act: int, tokens: int = 0,
+        groups_per_cta: int = 0):
+    """pre[:, :g1-g0] = pooled act(z) of groups [g0, g1).  See GlFwdArgs."""
+    _require_cuda(x, idx, w, b, counts, pre)
+    lib = load()
+    a = GlFwdArgs(_ptr(x), _ptr(idx), _ptr(w), _ptr(b), _ptr(counts), _ptr(pre), x.shape[0], x.shape[1], NB,
+                  g0, g1, x.stride(0), pre.stride(0), pool, act, tokens, groups_per_cta)
+    with torch.cuda.device(x.device):
+        _check(lib, lib.gl_fwd_f32(ctypes.byref(a), _stream(x.device)), "gl_fwd_f32")
+
+
+def bwd(x, idx, w, b, counts, gpre, dx, dw, db, NB: int, g0: int, g1: int, pool: int, act: int, tokens: int = 0,
+        groups_per_cta: int = 0):
+    """dx += ..., dw += ..., db += ... for groups [g0, g1).  See GlBwdArgs."""
+    _require_cuda(x, idx, w, b, counts, gpre, dx, dw, db)
+    lib = load()
+    a = GlBwdArgs(_ptr(x), _ptr(idx), _ptr(w), _ptr(b), _ptr(counts), _ptr(gpre), _ptr(dx), _ptr(dw), _ptr(db),
+                  x.shape[0], x.shape[1], NB, g0, g1, x.stride(0), gpre.stride(0), dx.stride(0), pool, act,
+                  tokens, groups_per_cta)
+    with torch.cuda.device(x.device):
+        _check(lib, lib.gl_bwd_f32(ctypes.byref(a), _stream(x.device)), "gl_bwd_f32")
+
+
+def adam(p, g, m, v, lr, beta1, beta2, eps, weight_decay, bc1, bc2, zero_grad=True):
+    _require_cuda(p, g, m, v)
+    lib = load()
+    a = GlAdamArgs(_ptr(p), _ptr(g), _ptr(m), _ptr(v), p.numel(), lr, beta1, beta2, eps, weight_decay, bc1, bc2,
+                   int(bool(zero_grad)))
+    with torch.cuda.device(p.device):
+        _check(lib, lib.gl_adam_f32(ctypes.byref(a), _stream(p.device)), "gl_adam_f32")

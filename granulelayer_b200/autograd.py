@@ -1,0 +1,204 @@
+"""Autograd contract and launch orchestration (mirror of sparse_pooling/autograd.py).
+
+``SparsePoolFunction`` keeps the reference's contract (autograd.py:380-414):
+forward saves ``(x, w, b, pre)`` and nothing of size [B, H]; backward forms
+``g_pre = dy * out_act'(pre)``, accumulates dW/db into the FP32 ``main_grad``
+buffers when present (returning None for them), else into temporary FP32
+buffers returned in the parameter dtype, and returns dX in ``x.dtype``.
+
+``Level1Runtime`` replaces the reference's runtime (autograd.py:68-300) for
+the B200 path.  Its ``forward`` returns ``{"pre": [B, G] fp32}`` and its
+``backward`` returns dX [B, D] fp32 after accumulating dW/db, the same
+protocol the reference's backends implement (autograd.py:220-223, 265-267).
+Both call the sm_100a library through its C ABI; there is no Triton, no
+backend dispatch and no CPU fallback: an unsupported layer or a CPU tensor
+raises.
+"""
+from __future__ import annotations
+
+from typing import Dict, Optional
+
+import torch
+
+from . import _native
+from .config import B200_POOLS, LevelSpec, PhysicalPlan, resolve_reduction
+from .layout import SparseLayout
+
+# checkpoint policy per operator when "auto" (autograd.py:31-38)
+AUTO_POLICY = {"max": "save_winners", "topk_mean": "save_winners", "mean": "minimal_stats",
+               "logmeanexp": "minimal_stats", "power_mean": "minimal_stats", "softmax_weighted": "minimal_stats",
+               "sum": "minimal_stats"}
+
+
+def resolve_policy(level: LevelSpec, requested: str) -> str:
+    """autograd.py:60-65: "auto" maps per operator; save_winners needs winners."""
+    if requested == "auto":
+        return AUTO_POLICY[level.type]
+    if requested == "save_winners" and level.type not in ("max", "topk_mean"):
+        return "minimal_stats"
+    return requested
+
+
+def act_torch(x: torch.Tensor, name: str) -> torch.Tensor:
+    """Activation of the pooled value (kernels/ops.py:165-170)."""
+    if name == "identity":
+        return x
+    if name == "relu":
+        return torch.relu(x)
+    return torch.nn.functional.gelu(x)
+
+
+def dact_torch(x: torch.Tensor, name: str) -> torch.Tensor:
+    """Derivative of ``act_torch`` (kernels/ops.py:173-179)."""
+    if name == "identity":
+        return torch.ones_like(x)
+    if name == "relu":
+        return (x > 0).to(x.dtype)
+    cdf = 0.5 * (1 + torch.erf(x * 0.7071067811865476))
+    return cdf + x * 0.3989422804014327 * torch.exp(-0.5 * x * x)
+
+
+class UnsupportedOnB200(NotImplementedError):
+    """The layer configuration is outside the sm_100a hot path."""
+
+
+def check_supported(layout: SparseLayout, level: LevelSpec, dtype: torch.dtype):
+    if layout.shared_indices or layout.block != 8:
+        raise UnsupportedOnB200("the B200 kernels run Mode A (shared_neurons=None): independent indices per neuron")
+    if level.type not in B200_POOLS:
+        raise UnsupportedOnB200(f"pooling {level.type!r} is not on the B200 path (supported: {B200_POOLS})")
+    if level.neurons_per_shard is not None:
+        raise UnsupportedOnB200("semantic two-level pooling is not on the B200 path")
+    if dtype != torch.float32:
+        raise UnsupportedOnB200(f"the B200 kernels compute in float32 (layer dtype {dtype})")
+
+
+class Level1Runtime:
+    """Launches the B200 kernels for one single-level layer (or one group shard).
+
+    ``counts`` holds the valid-neuron count of each local group; ``g0:g1`` of the
+    parameter tensors are processed (the whole tensor by default).
+    """
+
+    def __init__(self, layout: SparseLayout, idx: torch.Tensor, level: LevelSpec, plan: PhysicalPlan,
+                 counts: Optional[torch.Tensor] = None):
+        self.layout = layout
+        self.idx = idx
+        self.level = level
+        self.plan = plan
+        G = idx.shape[0]
+        self.counts_i32 = (counts if counts is not None else layout.counts_tensor(idx.device)).to(
+            device=idx.device, dtype=torch.int32).contiguous()
+        if self.counts_i32.numel() != G:
+            raise ValueError(f"counts has {self.counts_i32.numel()} entries for {G} groups")
+        self.counts_f32 = self.counts_i32.to(torch.float32)
+        self.pool = _native.POOL_MEAN if level.type == "mean" else _native.POOL_SUM
+        self.act = _native.ACT_IDS[level.activation]
+        self.last_info: Dict = {}
+        self.det = False
+
+    @property
+    def groups(self) -> int:
+        return self.idx.shape[0]
+
+    def check_devices(self, *tensors):
+        dev = self.idx.device
+        for t in tensors:
+            if t is not None and t.device != dev:
+                raise ValueError(f"tensor on {t.device} but the layer's parameters are on {dev} "
+                                 "(move the input or the layer)")
+
+    def resolve_reduction(self, B: int) -> bool:
+        mode, why, strict = resolve_reduction(self.plan)
+        if mode == "deterministic":
+            msg = (f"reduction='deterministic' ({why}) is unsupported by the B200 kernels: "
+                   "dX is flushed with FP32 atomics")
+            if strict:
+                raise ValueError(msg)
+            import warnings
+
+            warnings.warn(msg + "; running reduction='fast'", stacklevel=4)
+            mode, why = "fast", why + " -> fast (warn_only)"
+        self.det = False
+        self.last_info["reduction"] = {"mode": mode, "reason": why}
+        return self.det
+
+    def describe_execution(self, B: int) -> Dict:
+        lib = _native.load()
+        D = self.layout.input_dim
+        return {
+            "backend": "b200",
+            "library": str(_native.library_path()),
+            "forward": {"kernel": "gl_fwd_f32", "tokens": self.plan.b200_fwd_tokens or lib.gl_fwd_auto_tokens(D)},
+            "backward": {"kernel": "gl_bwd_f32", "tokens": self.plan.b200_dx_tokens or lib.gl_bwd_auto_tokens(D)},
+            "optimizer": {"kernel": "gl_adam_f32"},
+            "batch": B,
+        }
+
+    def forward(self, x: torch.Tensor, w: torch.Tensor, b: torch.Tensor, track_ids: bool = False):
+        B = x.shape[0]
+        self.check_devices(x, w, b)
+        self.resolve_reduction(B)
+        pre = torch.empty((B, self.groups), device=x.device, dtype=torch.float32)
+        _native.fwd(x, self.idx, w, b, self.counts_i32, pre, self.layout.blocks_per_group, 0, self.groups,
+                    self.pool, self.act, tokens=self.plan.b200_fwd_tokens)
+        self.last_info.update(forward_backend="b200", workspace_bytes=0)
+        return {"pre": pre}
+
+    def backward(self, x, w, b, g_pre: torch.Tensor, saved: Dict, policy: str, dw_buf: torch.Tensor,
+                 db_buf: torch.Tensor, recomputed: bool = False) -> torch.Tensor:
+        B, D = x.shape
+        self.last_info["policy"] = policy
+        self.last_info["recomputed_stats"] = recomputed
+        self.check_devices(x, w, b, g_pre, dw_buf, db_buf)
+        self.resolve_reduction(B)
+        dx = torch.zeros((B, D), device=x.device, dtype=torch.float32)
+        _native.bwd(x, self.idx, w, b, self.counts_i32, g_pre, dx, dw_buf, db_buf, self.layout.blocks_per_group,
+                    0, self.groups, self.pool, self.act, tokens=self.plan.b200_dx_tokens)
+        self.last_info["backward_backend"] = "b200"
+        return dx
+
+
+def _compute_operands(x, w, b):
+    """The kernels read fp32, unit-stride rows (autograd.py:349-354 casts the same way)."""
+    xc = x.to(torch.float32)
+    if xc.dim() != 2 or xc.stride(1) != 1:
+        xc = xc.contiguous()
+    return xc, w.contiguous(), b.contiguous()
+
+
+def _grad_buffers(w, b):
+    """main_grad when both exist (accumulate), else zeroed temporaries (autograd.py:357-363)."""
+    mg_w = getattr(w, "main_grad", None)
+    mg_b = getattr(b, "main_grad", None)
+    if mg_w is not None and mg_b is not None:
+        return mg_w, mg_b, True
+    return (torch.zeros(w.shape, device=w.device, dtype=torch.float32),
+            torch.zeros(b.shape, device=b.device, dtype=torch.float32), False)
+
+
+class SparsePoolFunction(torch.autograd.Function):
+    """y [B, G] = out_act(pool(act(sparse_projection(x)))) (autograd.py:380-414)."""
+
+    @staticmethod
+    def forward(ctx, x, w, b, rt: Level1Runtime, policy: str, compute_dtype):
+        xc, wc, bc = _compute_operands(x, w, b)
+        out = rt.forward(xc, wc, bc, track_ids=False)
+        pre = out["pre"]
+        y = act_torch(pre, rt.level.out_activation)
+        ctx.rt, ctx.policy = rt, policy
+        ctx.save_for_backward(x, w, b, pre)
+        rt.last_info["checkpoint_bytes"] = pre.numel() * pre.element_size()
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, w, b, pre = ctx.saved_tensors
+        rt: Level1Runtime = ctx.rt
+        xc, wc, bc = _compute_operands(x, w, b)
+        g_pre = (dy.float() * dact_torch(pre, rt.level.out_activation)).contiguous()
+        dw_buf, db_buf, use_main = _grad_buffers(w, b)
+        dx = rt.backward(xc, wc, bc, g_pre, {"pre": pre}, ctx.policy, dw_buf, db_buf)
+        gw = None if use_main else dw_buf.to(w.dtype)
+        gb = None if use_main else db_buf.to(b.dtype)
+        return dx.to(x.dtype, memory_format=torch.contiguous_format), gw, gb, None, None, None

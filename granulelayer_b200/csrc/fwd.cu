@@ -1,0 +1,206 @@
+// Forward: fused sparse projection + activation + group pooling (Mode A, fan-in 8, fp32).
+//
+// Replaces the reference's Triton fwd_pool_kernel (sparse_pooling/kernels/triton_fused.py:289-358,
+// Mode-A tile math at :253-264, mean update at :174-178) and the host merge
+// (kernels/ops.py:182-199).  The [B, H] hidden tensor never exists: every
+// z[t, n] lives in registers for the few instructions between its gathers and
+// its pooled sum.
+//
+// Work decomposition.  A thread block owns one token tile of T tokens and a
+// contiguous chunk of whole pooling groups.  It stages its token tile once in
+// shared memory, feature-major (xs[d * T + t], D*T*4 bytes; 128 KiB at
+// D = 4096, T = 8), then streams the groups' neuron records (16-byte index
+// record, 32-byte weight row, bias) straight from HBM/L2 with 128-bit loads.
+// Each warp step covers 32 / (T/4) neurons: a neuron's T tokens are split over
+// T/4 lanes holding 4 tokens each, so every gather is one LDS.128 of a
+// 4-token slice of the feature's row.  Lanes accumulate act(z) per token;
+// the block reduces per group with warp shuffles plus one shared-memory
+// pass, and writes pre[t, g] once (no atomics, deterministic).
+//
+// Consecutive blocks are consecutive token tiles of the same group chunk, so
+// the chunk's parameters are fetched from HBM once and re-served from L2 to
+// the other token tiles.
+#include "common.cuh"
+
+namespace gl {
+
+constexpr int kFwdThreads = 512;
+
+template <int T, int ACT>
+__global__ void __launch_bounds__(kFwdThreads, 1)
+    fwd_kernel(const float* __restrict__ x, const int16_t* __restrict__ idx, const float* __restrict__ w,
+               const float* __restrict__ bias, const int32_t* __restrict__ counts, float* __restrict__ pre,
+               int B, int D, int64_t NB, int64_t g0, int64_t g1, int64_t ldx, int64_t ldp, int pool, int gpc) {
+  constexpr int V = T < 4 ? T : 4;   // tokens per lane
+  constexpr int LPN = T / V;         // lanes per neuron
+  constexpr int NPW = 32 / LPN;      // neurons per warp step
+  constexpr int NW = kFwdThreads / 32;
+  constexpr int UNR = 2;             // neurons in flight per lane
+  extern __shared__ __align__(16) float xs[];
+  __shared__ float red[NW][T];
+
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int t0 = blockIdx.x * T;
+  stage_tile<T, kFwdThreads>(xs, x, t0, B, D, ldx);
+  __syncthreads();
+
+  const int nsub = lane / LPN, q = lane % LPN;
+  const int slots = (int)(NB * 8);
+  const int64_t gb = g0 + (int64_t)blockIdx.y * gpc;
+  const int64_t ge = gb + gpc < g1 ? gb + gpc : g1;
+  const float* xq = xs + q * V;
+
+  for (int64_t g = gb; g < ge; ++g) {
+    const int ng = min(counts[g], slots);
+    const int64_t fbase = g * (int64_t)slots;
+    float acc[V];
+#pragma unroll
+    for (int v = 0; v < V; ++v) acc[v] = 0.f;
+
+    for (int s0 = warp * NPW * UNR; s0 < ng; s0 += NW * NPW * UNR) {
+      Rec8 r[UNR];
+      W8 wr[UNR];
+      float bb[UNR];
+      bool ok[UNR];
+#pragma unroll
+      for (int u = 0; u < UNR; ++u) {
+        const int s = s0 + u * NPW + nsub;
+        ok[u] = s < ng;
+        const int64_t f = fbase + (ok[u] ? s : 0);
+        r[u] = load_rec8(idx + f * 8, D - 1);
+        wr[u] = load_w8(w + f * 8);
+        bb[u] = __ldg(bias + f);
+      }
+#pragma unroll
+      for (int u = 0; u < UNR; ++u) {
+        float z[V];
+#pragma unroll
+        for (int v = 0; v < V; ++v) z[v] = bb[u];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const float* row = xq + r[u].i[k] * T;
+          if constexpr (V == 4) {
+            const float4 xv = *reinterpret_cast<const float4*>(row);
+            z[0] = fmaf(wr[u].w[k], xv.x, z[0]);
+            z[1] = fmaf(wr[u].w[k], xv.y, z[1]);
+            z[2] = fmaf(wr[u].w[k], xv.z, z[2]);
+            z[3] = fmaf(wr[u].w[k], xv.w, z[3]);
+          } else if constexpr (V == 2) {
+            const float2 xv = *reinterpret_cast<const float2*>(row);
+            z[0] = fmaf(wr[u].w[k], xv.x, z[0]);
+            z[1] = fmaf(wr[u].w[k], xv.y, z[1]);
+          } else {
+            z[0] = fmaf(wr[u].w[k], row[0], z[0]);
+          }
+        }
+        if (ok[u]) {
+#pragma unroll
+          for (int v = 0; v < V; ++v) acc[v] += act_f<ACT>(z[v]);
+        }
+      }
+    }
+    // reduce over the neurons of the warp (lanes with equal q), then over warps
+#pragma unroll
+    for (int off = LPN; off < 32; off <<= 1)
+#pragma unroll
+      for (int v = 0; v < V; ++v) acc[v] += __shfl_xor_sync(kFullMask, acc[v], off);
+    if (lane < LPN)
+#pragma unroll
+      for (int v = 0; v < V; ++v) red[warp][lane * V + v] = acc[v];
+    __syncthreads();
+    if (threadIdx.x < T) {
+      float s = 0.f;
+#pragma unroll
+      for (int i = 0; i < NW; ++i) s += red[i][threadIdx.x];
+      const int t = t0 + threadIdx.x;
+      if (t < B) pre[(int64_t)t * ldp + (g - g0)] = (pool == GL_POOL_MEAN) ? s / (float)ng : s;
+    }
+    __syncthreads();
+  }
+}
+
+template <int T, int ACT>
+static int launch_fwd(const GlFwdArgs& a, int gpc, cudaStream_t st) {
+  const size_t smem = (size_t)a.D * T * sizeof(float);
+  auto kern = fwd_kernel<T, ACT>;
+  int rc = ensure_dynamic_smem((const void*)kern, smem);
+  if (rc) return rc;
+  const int64_t tiles = (a.B + T - 1) / T;
+  const int64_t chunks = (a.g1 - a.g0 + gpc - 1) / gpc;
+  if (tiles > 2147483647LL || chunks > 65535) return GL_ERR_SHAPE;
+  dim3 grid((unsigned)tiles, (unsigned)chunks);
+  kern<<<grid, kFwdThreads, smem, st>>>(a.x, a.idx, a.w, a.b, a.counts, a.pre, (int)a.B, (int)a.D, a.NB, a.g0,
+                                        a.g1, a.ldx, a.ldp, a.pool, gpc);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_cuda_error(e);
+  count_launches(1);
+  return GL_OK;
+}
+
+template <int T>
+static int dispatch_act_fwd(const GlFwdArgs& a, int gpc, cudaStream_t st) {
+  switch (a.act) {
+    case GL_ACT_IDENTITY: return launch_fwd<T, GL_ACT_IDENTITY>(a, gpc, st);
+    case GL_ACT_RELU: return launch_fwd<T, GL_ACT_RELU>(a, gpc, st);
+    case GL_ACT_GELU: return launch_fwd<T, GL_ACT_GELU>(a, gpc, st);
+    default: return GL_ERR_UNSUPPORTED;
+  }
+}
+
+// Largest token tile in {8, 4, 2, 1} whose staged input fits the opt-in
+// shared memory (leaving room for the static reduction buffer).
+static int pick_fwd_tokens(int64_t D, int smem_optin) {
+  for (int T = 8; T >= 1; T >>= 1)
+    if ((int64_t)D * T * 4 + 2048 <= smem_optin) return T;
+  return GL_ERR_SMEM;
+}
+
+}  // namespace gl
+
+using namespace gl;
+
+extern "C" int gl_fwd_auto_tokens(int64_t D) {
+  int optin = 0;
+  int rc = device_smem_optin(&optin);
+  if (rc) return rc;
+  return pick_fwd_tokens(D, optin);
+}
+
+extern "C" int gl_fwd_f32(const GlFwdArgs* args, void* stream) {
+  if (!args) return GL_ERR_NULL;
+  const GlFwdArgs& a = *args;
+  if (a.B < 0 || a.D < 1 || a.D > 32767 || a.NB < 1 || a.g0 < 0 || a.g1 < a.g0) return GL_ERR_SHAPE;
+  if (a.B == 0 || a.g1 == a.g0) return GL_OK;
+  if (!a.x || !a.idx || !a.w || !a.b || !a.counts || !a.pre) return GL_ERR_NULL;
+  if (a.B > 2147483647LL || a.ldx < a.D || a.ldp < a.g1 - a.g0) return GL_ERR_SHAPE;
+  if (((uintptr_t)a.idx & 15) || ((uintptr_t)a.w & 15)) return GL_ERR_ALIGN;
+  if (a.pool != GL_POOL_MEAN && a.pool != GL_POOL_SUM) return GL_ERR_UNSUPPORTED;
+  int optin = 0, sms = 0;
+  int rc = device_smem_optin(&optin);
+  if (rc) return rc;
+  if ((rc = device_sm_count(&sms))) return rc;
+  int T = a.tokens;
+  if (T == 0) {
+    T = pick_fwd_tokens(a.D, optin);
+    if (T < 0) return T;
+  } else if (T != 1 && T != 2 && T != 4 && T != 8) {
+    return GL_ERR_UNSUPPORTED;
+  }
+  if ((int64_t)a.D * T * 4 + 2048 > optin) return GL_ERR_SMEM;
+  const int64_t G = a.g1 - a.g0;
+  int gpc = a.groups_per_cta;
+  if (gpc <= 0) {
+    const int64_t tiles = (a.B + T - 1) / T;
+    const int64_t units = tiles * G;
+    int64_t want = units / ((int64_t)sms * 32);
+    gpc = (int)(want < 1 ? 1 : (want > 8 ? 8 : want));
+  }
+  while ((G + gpc - 1) / gpc > 65535) gpc *= 2;
+  cudaStream_t st = (cudaStream_t)stream;
+  switch (T) {
+    case 8: return dispatch_act_fwd<8>(a, gpc, st);
+    case 4: return dispatch_act_fwd<4>(a, gpc, st);
+    case 2: return dispatch_act_fwd<2>(a, gpc, st);
+    default: return dispatch_act_fwd<1>(a, gpc, st);
+  }
+}

@@ -1,0 +1,196 @@
+"""Group sharding of the sparse-pooling layer across the GPUs of one node.
+
+The reference is single-GPU.  Here rank r of P owns the contiguous pooling
+groups ``[g0, g1) = shard_range(G, r, P)``, i.e. contiguous slices of the
+``indices``/``weight``/``bias`` tensors (and of their gradients and Adam
+moments).  Groups are independent in the forward pass, in dW/db and in the
+optimizer; the two exchanges are
+
+    forward : pre_r [B, g1-g0]  --all_gather-->  pre [B, G]   (replicated)
+    backward: dX_r  [B, D]      --all_reduce(SUM)-->  dX       (replicated)
+
+both NCCL collectives over NVLink (any torch.distributed backend works; the
+CPU tests use gloo).  ``ShardedTrainStep`` issues the all-gather right after
+the forward kernel and lets the backward kernel run under it, and issues the
+dX all-reduce before the optimizer kernels so that they overlap it.
+
+Nothing here touches another GPU's memory directly: remote data arrives only
+through the collectives into local buffers.
+"""
+from __future__ import annotations
+
+from typing import Callable, Optional
+
+import torch
+import torch.distributed as dist
+from torch import nn
+
+from .autograd import Level1Runtime, _compute_operands, _grad_buffers, act_torch, check_supported, dact_torch
+from .config import PhysicalPlan, PoolingConfig
+from .layout import SparseLayout, init_parameters
+
+
+def shard_range(G: int, rank: int, world: int):
+    """Contiguous near-equal split of G groups: rank r gets [g0, g1)."""
+    if not 0 <= rank < world:
+        raise ValueError(f"rank {rank} outside world of {world}")
+    base, rem = divmod(G, world)
+    g0 = rank * base + min(rank, rem)
+    return g0, g0 + base + (1 if rank < rem else 0)
+
+
+def gather_columns(local: torch.Tensor, G: int, group=None) -> torch.Tensor:
+    """All-gather per-rank column blocks [B, g1-g0] into [B, G] (uneven shards padded)."""
+    world = dist.get_world_size(group)
+    B = local.shape[0]
+    width = -(-G // world)
+    buf = local.new_zeros((B, width))
+    buf[:, :local.shape[1]] = local
+    out = local.new_empty((world, B, width))
+    dist.all_gather_into_tensor(out, buf, group=group)
+    cols = [out[r, :, :shard_range(G, r, world)[1] - shard_range(G, r, world)[0]] for r in range(world)]
+    return torch.cat(cols, dim=1)
+
+
+class _ShardedPoolFunction(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, w, b, rt, G, g0, g1, group):
+        xc, wc, bc = _compute_operands(x, w, b)
+        pre_l = rt.forward(xc, wc, bc)["pre"]
+        pre = gather_columns(pre_l, G, group)
+        ctx.rt, ctx.g0, ctx.g1, ctx.group = rt, g0, g1, group
+        ctx.save_for_backward(x, w, b, pre_l)
+        return act_torch(pre, rt.level.out_activation)
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, w, b, pre_l = ctx.saved_tensors
+        rt = ctx.rt
+        xc, wc, bc = _compute_operands(x, w, b)
+        g_pre = (dy[:, ctx.g0:ctx.g1].float() * dact_torch(pre_l, rt.level.out_activation)).contiguous()
+        dw_buf, db_buf, use_main = _grad_buffers(w, b)
+        dx = rt.backward(xc, wc, bc, g_pre, {"pre": pre_l}, "minimal_stats", dw_buf, db_buf)
+        dist.all_reduce(dx, group=ctx.group)
+        gw = None if use_main else dw_buf.to(w.dtype)
+        gb = None if use_main else db_buf.to(b.dtype)
+        return dx.to(x.dtype), gw, gb, None, None, None, None, None
+
+
+class GroupShardedLayer(nn.Module):
+    """The groups ``[g0, g1)`` of a Mode-A ``SparsePoolingLayer`` on this rank.
+
+    ``forward(x)`` returns the full pooled output [.., G] on every rank (all-gather);
+    the input gradient is all-reduced so every rank sees the full dX.  Parameters
+    are the local slices; ``from_full`` cuts them from a full layer (bit-identical
+    to the single-GPU layer), the constructor draws them locally with
+    ``seed + rank`` (statistically identical, for benchmarks at full scale).
+    ``runtime_factory`` lets tests substitute the launch backend.
+    """
+
+    def __init__(self, input_dim: int, hidden_dim: int, output_dim: int, pooling="mean",
+                 plan: Optional[PhysicalPlan] = None, device=None, seed: int = 0, bias_std: float = 0.0,
+                 group=None, runtime_factory: Optional[Callable] = None, _params=None):
+        super().__init__()
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.cfg = PoolingConfig.parse(pooling)
+        self.layout = SparseLayout(input_dim, hidden_dim, output_dim, 8, 8, False)
+        self.plan = plan or PhysicalPlan()
+        self.g0, self.g1 = shard_range(output_dim, self.rank, self.world)
+        check_supported(self.layout, self.cfg.levels[0], torch.float32)
+        counts = self.layout.counts_tensor("cpu")[self.g0:self.g1]
+        if _params is None:
+            G_l = self.g1 - self.g0
+            NB = self.layout.blocks_per_group
+            # local draw: a layout of G_l groups with this shard's slot count per group
+            loc = SparseLayout(input_dim, int(counts.sum()), G_l, 8, 8, False)
+            if loc.blocks_per_group != NB or not torch.equal(loc.counts_tensor("cpu"), counts):
+                raise ValueError("local initialisation needs equal group sizes; use GroupShardedLayer.from_full")
+            idx, w, b = init_parameters(loc, device or "cpu", dtype=torch.float32, seed=seed + self.rank,
+                                        bias_std=bias_std)
+        else:
+            idx, w, b = _params
+        self.register_buffer("indices", idx)
+        self.weight = nn.Parameter(w)
+        self.bias = nn.Parameter(b)
+        self.register_buffer("counts", counts.to(idx.device))
+        factory = runtime_factory or (lambda lay: Level1Runtime(lay.layout, lay.indices, lay.cfg.levels[0],
+                                                                lay.plan, counts=lay.counts))
+        self._factory = factory
+        self._rt = None
+
+    @classmethod
+    def from_full(cls, layer, group=None, runtime_factory=None):
+        """Shard an existing (full) ``SparsePoolingLayer``: slices of its tensors."""
+        L = layer.layout
+        world, rank = dist.get_world_size(group), dist.get_rank(group)
+        g0, g1 = shard_range(L.groups, rank, world)
+        params = (layer.indices[g0:g1].clone(), layer.weight.detach()[g0:g1].clone(),
+                  layer.bias.detach()[g0:g1].clone())
+        return cls(L.input_dim, L.hidden_dim, L.groups, pooling=layer.cfg, plan=layer.plan, group=group,
+                   runtime_factory=runtime_factory, _params=params)
+
+    def runtime(self):
+        if self._rt is None or self._rt.idx is not self.indices:
+            self._rt = self._factory(self)
+        return self._rt
+
+    def enable_main_grad(self):
+        for p in (self.weight, self.bias):
+            if getattr(p, "main_grad", None) is None:
+                p.main_grad = torch.zeros(p.shape, device=p.device, dtype=torch.float32)
+
+    def forward(self, x):
+        lead = x.shape[:-1]
+        x2 = x.reshape(-1, x.shape[-1])
+        y = _ShardedPoolFunction.apply(x2, self.weight, self.bias, self.runtime(), self.layout.groups, self.g0,
+                                       self.g1, self.group)
+        return y.reshape(*lead, y.shape[-1])
+
+
+class ShardedTrainStep:
+    """One training step of a ``GroupShardedLayer`` with the collectives overlapped.
+
+    step(x, dy): forward kernel -> async all-gather of pre -> backward kernel
+    (dW/db into main_grad, partial dX) -> async all-reduce of dX -> optimizer
+    kernels -> wait.  Returns (y [B, G], dx [B, D]).
+    """
+
+    def __init__(self, layer: GroupShardedLayer, optimizer):
+        self.layer = layer
+        self.opt = optimizer
+        layer.enable_main_grad()
+
+    def step(self, x: torch.Tensor, dy: torch.Tensor):
+        lay = self.layer
+        rt = lay.runtime()
+        G = lay.layout.groups
+        w, b = lay.weight.detach(), lay.bias.detach()
+        pre_l = rt.forward(x, w, b)["pre"]
+        world = lay.world
+        width = -(-G // world)
+        if world > 1:
+            buf = pre_l.new_zeros((x.shape[0], width)) if pre_l.shape[1] != width else pre_l
+            if buf is not pre_l:
+                buf[:, :pre_l.shape[1]] = pre_l
+            gathered = pre_l.new_empty((world, x.shape[0], width))
+            ag = dist.all_gather_into_tensor(gathered, buf, group=lay.group, async_op=True)
+        out_act = lay.cfg.levels[0].out_activation
+        g_pre = dy[:, lay.g0:lay.g1]
+        if out_act != "identity":
+            g_pre = g_pre * dact_torch(pre_l, out_act)
+        g_pre = g_pre.contiguous()
+        dx = rt.backward(x, w, b, g_pre, {"pre": pre_l}, "minimal_stats", lay.weight.main_grad, lay.bias.main_grad)
+        if world > 1:
+            ar = dist.all_reduce(dx, group=lay.group, async_op=True)
+        self.opt.step()
+        if world > 1:
+            ag.wait()
+            ar.wait()
+            cols = [gathered[r, :, :shard_range(G, r, world)[1] - shard_range(G, r, world)[0]]
+                    for r in range(world)]
+            pre = torch.cat(cols, dim=1)
+        else:
+            pre = pre_l
+        return act_torch(pre, out_act), dx

@@ -1,0 +1,134 @@
+"""PyTorch-facing module (mirror of sparse_pooling/layer.py).
+
+``SparsePoolingLayer`` keeps the reference's constructor (layer.py:40-58),
+parameter/buffer names and shapes (``indices``, ``weight``, ``bias``),
+``forward`` (layer.py:186-197), ``explain``, ``last_info``,
+``enable_main_grad``/``zero_main_grad`` and ``effective_policy``, so that
+model code and state dicts move between the two unchanged.
+
+Execution is the B200 path only: Mode A (``shared_neurons=None``), fp32,
+single-level ``mean`` or ``sum`` pooling with identity/ReLU/GELU neuron
+activation.  Any other configuration still constructs (so checkpoints load)
+but ``forward`` raises ``UnsupportedOnB200`` instead of falling back.
+"""
+from __future__ import annotations
+
+from typing import Optional, Union
+
+import torch
+from torch import nn
+
+from .autograd import Level1Runtime, SparsePoolFunction, check_supported, resolve_policy
+from .config import DEFAULT_WORKSPACE_BUDGET, PhysicalPlan, PoolingConfig
+from .layout import SparseLayout, init_parameters
+
+
+class SparsePoolingLayer(nn.Module):
+    """Weight-sparse projection to ``hidden_dim`` logical neurons (fan-in 8)
+    fused with pooling into ``output_dim`` contiguous groups.
+
+    Args mirror the reference (layer.py:16-58): ``shared_neurons=None`` selects
+    Mode A (independent indices per neuron, the B200 path); ``pooling`` is an
+    operator name, a level dict or a ``PoolingConfig``; ``plan`` is an
+    execution-only ``PhysicalPlan``; ``seed`` and ``bias_std`` drive the
+    bit-exact seeded initialisation of ``layout.init_parameters``.
+    ``backend``, ``weight_layout`` and ``workspace_budget`` are accepted for
+    compatibility; ``connectivity`` (input supergroups) is a Mode-B feature of
+    the reference and raises here.
+    """
+
+    def __init__(self, input_dim: int = 1024, hidden_dim: int = 100_000_000, output_dim: int = 1024,
+                 fan_in: int = 8, shared_neurons: Optional[int] = 8,
+                 pooling: Union[str, dict, PoolingConfig] = "max", checkpoint_policy: str = "auto",
+                 dtype: torch.dtype = torch.bfloat16, plan: Optional[PhysicalPlan] = None,
+                 workspace_budget: int = DEFAULT_WORKSPACE_BUDGET, device=None, seed: int = 0,
+                 bias_std: float = 0.0, backend: str = "auto", weight_layout: str = "auto", connectivity=None):
+        super().__init__()
+        self.cfg = PoolingConfig.parse(pooling, checkpoint_policy)
+        if isinstance(pooling, (str, PoolingConfig)) or "checkpoint_policy" not in (pooling or {}):
+            self.cfg.checkpoint_policy = checkpoint_policy
+        mode_b = shared_neurons is not None
+        if weight_layout == "auto":
+            weight_layout = "packed" if (mode_b and backend != "triton") else "canonical"
+        if weight_layout not in ("packed", "canonical"):
+            raise ValueError("weight_layout must be 'auto', 'packed' or 'canonical'")
+        if connectivity is not None:
+            raise NotImplementedError("input-supergroup connectivity is a Mode-B layer option of the reference; "
+                                      "it is not part of the B200 path")
+        self.layout = SparseLayout(input_dim, hidden_dim, output_dim, fan_in, shared_neurons if mode_b else 8,
+                                   mode_b, packed=(weight_layout == "packed"))
+        self.compute_dtype = dtype
+        self.plan = plan or PhysicalPlan()
+        self.backend_name = backend
+        self.workspace_budget = workspace_budget
+        self.connectivity = None
+        self.graph_stats = None
+        idx, w, b = init_parameters(self.layout, device or "cpu", dtype=dtype, seed=seed, bias_std=bias_std)
+        self.register_buffer("indices", idx)
+        self.weight = nn.Parameter(w)
+        self.bias = nn.Parameter(b)
+        self._tnames = []
+        self._rt = None
+        self._rt_key = None
+
+    def _runtime(self) -> Level1Runtime:
+        key = (self.indices.device, self.indices.data_ptr(), id(self.plan))
+        if self._rt is None or self._rt_key != key:
+            check_supported(self.layout, self.cfg.levels[0] if not self.cfg.is_semantic_hierarchy
+                            else self.cfg.levels[0], self.compute_dtype)
+            if self.cfg.is_semantic_hierarchy:
+                from .autograd import UnsupportedOnB200
+
+                raise UnsupportedOnB200("semantic two-level pooling is not on the B200 path")
+            self._rt = Level1Runtime(self.layout, self.indices, self.cfg.levels[0], self.plan)
+            self._rt_key = key
+        return self._rt
+
+    def _load_from_state_dict(self, state_dict, prefix, *args, **kwargs):
+        if state_dict.get(prefix + "sg_plan") is not None:
+            raise ValueError("checkpoint uses input-supergroup connectivity, which this layer does not have")
+        super()._load_from_state_dict(state_dict, prefix, *args, **kwargs)
+        self._rt = None
+
+    @property
+    def last_info(self):
+        return {} if self._rt is None else dict(self._rt.last_info)
+
+    def explain(self, batch: int = 8192) -> dict:
+        """The execution the layer would use for ``batch`` tokens, without running it."""
+        out = dict(backend_requested=self.backend_name)
+        if not self.indices.is_cuda:
+            out["backend"] = "none (CPU parameters; the B200 path needs CUDA tensors)"
+            return out
+        rt = self._runtime()
+        out.update(rt.describe_execution(batch))
+        return out
+
+    @property
+    def effective_policy(self) -> str:
+        return resolve_policy(self.cfg.levels[0], self.cfg.checkpoint_policy)
+
+    def enable_main_grad(self):
+        """Accumulate W/b gradients into persistent FP32 ``main_grad`` buffers
+        (autograd then returns None for them; layer.py:174-179)."""
+        for p in (self.weight, self.bias):
+            if getattr(p, "main_grad", None) is None:
+                p.main_grad = torch.zeros(p.shape, device=p.device, dtype=torch.float32)
+
+    def zero_main_grad(self):
+        for p in (self.weight, self.bias):
+            if getattr(p, "main_grad", None) is not None:
+                p.main_grad.zero_()
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        lead = x.shape[:-1]
+        x2 = x.reshape(-1, x.shape[-1])
+        rt = self._runtime()
+        y = SparsePoolFunction.apply(x2, self.weight, self.bias, rt, self.effective_policy, self.compute_dtype)
+        return y.reshape(*lead, y.shape[-1])
+
+    def extra_repr(self) -> str:
+        L = self.layout
+        mode = f"B(C={L.block})" if L.shared_indices else "A(independent)"
+        return (f"in={L.input_dim}, hidden={L.hidden_dim:,}, out={L.groups}, fan_in={L.fan_in}, "
+                f"mode={mode}, pooling={self.cfg.describe()}, policy={self.effective_policy}")

@@ -1,0 +1,149 @@
+/*
+ * granule_b200.h — C ABI of the B200 (sm_100a) sparse-pooling kernels.
+ *
+ * The reference exposes this hot path only as a Python protocol between
+ * Level1Runtime and its backend objects, on top of Triton launches:
+ *   forward : sparse_pooling/autograd.py:213-233  (Level1Runtime.forward)
+ *             -> kernels/ops.py:104-154 fused_forward_states
+ *                (Triton fwd_pool_kernel, kernels/triton_fused.py:289-358)
+ *             -> kernels/ops.py:182-199 merge_finalize (mean: pre = s / n_g)
+ *   backward: sparse_pooling/autograd.py:236-300  (Level1Runtime.backward / _triton_backward)
+ *             -> kernels/ops.py:242-249 dense_coefficients (mean: c1 = g_pre / n_g)
+ *             -> kernels/ops.py:265-278 launch_dense_backward
+ *                (Triton bwd_dense_kernel, kernels/triton_fused.py:402-472)
+ *   optimizer: sparse_pooling/optim.py:26-64 _adamw_kernel, launched by FusedAdamW.step (optim.py:91-126)
+ * and its native library's ctypes ABI follows the same conventions this header
+ * keeps (sparse_pooling/kernels/cuda/abi.cu:9-62, sparse_pool.cu:12-44,
+ * backends/cuda/runtime.py:34-121): plain pointers and sizes, caller-owned
+ * memory, an explicit stream, a version query, and negative status codes
+ * instead of exceptions.
+ *
+ * Conventions
+ *   - Every entry point returns GL_OK (0) or a negative GlStatus; it never
+ *     throws and never exits.  gl_status_string() names a status.
+ *   - All buffers are caller-owned device memory.  No entry point allocates
+ *     device memory.
+ *   - Work is enqueued on `stream` (a cudaStream_t; NULL = legacy default) of the
+ *     current device; calls return before the GPU finishes.
+ *   - Parameters use the reference's Mode-A storage unchanged
+ *     (sparse_pooling/layout.py:5-8, 123-140), C = 8 neurons per block, fan-in 8:
+ *       idx  [G_total, NB, 8, 8] int16, w [G_total, NB, 8, 8] f32, b [G_total, NB, 8] f32
+ *     Neuron slot s of group g has flat index f = g*NB*8 + s; its record is
+ *     idx[8f .. 8f+7], w[8f .. 8f+7], b[f].  Slots s >= counts[g] are padding
+ *     and are masked out of every sum.
+ *   - Sharding: a call processes the contiguous group range [g0, g1) and reads
+ *     its pooled columns at y/gpre column (g - g0).
+ */
+#ifndef GRANULE_B200_H
+#define GRANULE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GL_ABI_VERSION 1
+
+typedef enum GlStatus {
+  GL_OK = 0,
+  GL_ERR_NULL = -1,          /* a required pointer is NULL */
+  GL_ERR_SHAPE = -2,         /* inconsistent sizes (B, D, NB, group range, strides) */
+  GL_ERR_ALIGN = -3,         /* a pointer is not aligned for vector access */
+  GL_ERR_UNSUPPORTED = -4,   /* pool/activation/tile combination not built */
+  GL_ERR_SMEM = -5,          /* the tile does not fit in shared memory */
+  GL_ERR_LAUNCH = -6,        /* the CUDA launch failed (see gl_last_cuda_error) */
+  GL_ERR_DEVICE = -7         /* no usable device / attribute query failed */
+} GlStatus;
+
+/* Pool ids: the reference's "mean" (sparse_pooling/config.py:22-29) and the
+   "sum" extension.  Activation ids follow config.py:33. */
+enum { GL_POOL_MEAN = 0, GL_POOL_SUM = 1 };
+enum { GL_ACT_IDENTITY = 0, GL_ACT_RELU = 1, GL_ACT_GELU = 2 };
+
+/* Forward: pre[t, g - g0] = pool_{valid s of g} act(z[t, g, s]),
+ *   z[t, g, s] = b[f] + sum_k w[8f+k] * x[t, idx[8f+k]],
+ * pool = mean (divide by counts[g]) or sum.  `pre` is written, not accumulated.
+ * Replaces fused_forward_states + merge_finalize (kernels/ops.py:104-199). */
+typedef struct GlFwdArgs {
+  const float* x;           /* [B, ldx] token-major input, D used columns */
+  const int16_t* idx;       /* Mode-A indices (see conventions), values in [0, D) */
+  const float* w;           /* weights */
+  const float* b;           /* bias */
+  const int32_t* counts;    /* [G_total] valid neurons per group */
+  float* pre;               /* [B, ldp] pooled output, columns 0 .. g1-g0-1 */
+  int64_t B, D, NB;         /* tokens, input features, blocks per group */
+  int64_t g0, g1;           /* group range processed by this call */
+  int64_t ldx, ldp;         /* row strides in elements */
+  int32_t pool;             /* GL_POOL_* */
+  int32_t act;              /* GL_ACT_* */
+  int32_t tokens;           /* token tile (0 = automatic; else 1, 2, 4 or 8) */
+  int32_t groups_per_cta;   /* groups per thread block (0 = automatic) */
+} GlFwdArgs;
+
+/* Backward: with c1[t, g] = gpre[t, g - g0] / counts[g] (mean) or gpre (sum) and
+ *   dz[t, f] = c1[t, g] * act'(z[t, f]) for valid slots (0 for padding):
+ *   dx[t, d]   += sum_{f, k: idx[8f+k] = d} dz[t, f] * w[8f+k]
+ *   dw[8f + k] += sum_t dz[t, f] * x[t, idx[8f+k]]
+ *   db[f]      += sum_t dz[t, f]
+ * dx, dw and db are accumulated (+=); dw/db use the weight/bias layout, so they
+ * can be the reference's FP32 `main_grad` buffers (autograd.py:357-363).
+ * Replaces dense_coefficients + launch_dense_backward (kernels/ops.py:242-278). */
+typedef struct GlBwdArgs {
+  const float* x;
+  const int16_t* idx;
+  const float* w;
+  const float* b;
+  const int32_t* counts;
+  const float* gpre;        /* [B, ldg] dL/dpre, columns 0 .. g1-g0-1 */
+  float* dx;                /* [B, lddx] fp32, accumulated */
+  float* dw;                /* weight-shaped fp32, accumulated */
+  float* db;                /* bias-shaped fp32, accumulated */
+  int64_t B, D, NB;
+  int64_t g0, g1;
+  int64_t ldx, ldg, lddx;
+  int32_t pool;
+  int32_t act;
+  int32_t tokens;           /* token tile (0 = automatic; else 1, 2, 4 or 8) */
+  int32_t groups_per_cta;   /* 0 = automatic */
+} GlBwdArgs;
+
+/* Adam(W) step over n fp32 elements, in place (sparse_pooling/optim.py:26-64):
+ *   m = b1 m + (1-b1) g ;  v = b2 v + (1-b2) g^2
+ *   p = p (1 - lr wd) - lr (m / bc1) / (sqrt(v / bc2) + eps)
+ *   g = 0 when zero_grad != 0 (the reference's fused zero_grad).
+ * bc1 = 1 - b1^t and bc2 = 1 - b2^t are passed in, as the reference does. */
+typedef struct GlAdamArgs {
+  float* p;
+  float* g;
+  float* m;
+  float* v;
+  int64_t n;
+  float lr, beta1, beta2, eps, weight_decay, bc1, bc2;
+  int32_t zero_grad;
+} GlAdamArgs;
+
+int gl_abi_version(void);
+const char* gl_status_string(int status);
+/* Last CUDA error code seen by a failed launch on this thread (0 if none). */
+int gl_last_cuda_error(void);
+
+int gl_fwd_f32(const GlFwdArgs* args, void* stream);
+int gl_bwd_f32(const GlBwdArgs* args, void* stream);
+int gl_adam_f32(const GlAdamArgs* args, void* stream);
+
+/* Number of kernels this library has launched successfully in this process
+   (all devices).  Benchmarks difference it around a timed region. */
+int64_t gl_launch_count(void);
+
+/* Token tile the automatic choice would use for input_dim D (forward / backward),
+   or a negative status when no tile fits in shared memory. */
+int gl_fwd_auto_tokens(int64_t D);
+int gl_bwd_auto_tokens(int64_t D);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GRANULE_B200_H */

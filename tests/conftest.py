@@ -1,0 +1,79 @@
+import json
+import os
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+ROOT = Path(__file__).resolve().parent.parent
+sys.path.insert(0, str(ROOT))
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA (B200) device and the sm_100a library")
+
+
+def pytest_collection_modifyitems(config, items):
+    if torch.cuda.is_available():
+        return
+    skip = pytest.mark.skip(reason="no CUDA device in this process")
+    for item in items:
+        if "gpu" in item.keywords:
+            item.add_marker(skip)
+
+
+def rel_err(a, b) -> float:
+    """Relative L2 error ||a - b|| / ||b|| (the reference's metric, tests/conftest.py:53-55)."""
+    a = torch.as_tensor(a).double().cpu()
+    b = torch.as_tensor(b).double().cpu()
+    return float((a - b).norm() / (b.norm() + 1e-30))
+
+
+def assert_close(actual, expected, rtol, atol, what=""):
+    """Elementwise |a - e| <= atol + rtol |e| (the tolerance form of the hot path's parity bar)."""
+    a = torch.as_tensor(actual).double().cpu()
+    e = torch.as_tensor(expected).double().cpu()
+    assert a.shape == e.shape, f"{what}: shape {tuple(a.shape)} != {tuple(e.shape)}"
+    bad = (a - e).abs() > atol + rtol * e.abs()
+    if bool(bad.any()):
+        i = int(bad.flatten().nonzero()[0])
+        raise AssertionError(f"{what}: {int(bad.sum())} of {a.numel()} elements outside rtol={rtol} atol={atol}; "
+                             f"first at flat {i}: {a.flatten()[i].item()!r} vs {e.flatten()[i].item()!r}")
+
+
+def load_case(name):
+    d = np.load(GOLDEN / f"fwdbwd_{name}.npz")
+    meta = json.loads(str(d["meta"]))
+    return meta, {k: d[k] for k in d.files if k != "meta"}
+
+
+def case_names():
+    return sorted(p.stem[len("fwdbwd_"):] for p in GOLDEN.glob("fwdbwd_*.npz"))
+
+
+def case_params(meta, arrays):
+    """(layout, idx, w, b) of a golden case, regenerated with the product's seeded init."""
+    from granulelayer_b200.layout import SparseLayout, init_parameters
+
+    L = SparseLayout(meta["D"], meta["H"], meta["G"], 8, 8, False)
+    idx, w, b = init_parameters(L, "cpu", dtype=torch.float32, seed=meta["seed"], bias_std=meta["bias_std"])
+    if meta["rule"] == "uniform":
+        idx = torch.from_numpy(arrays["idx"])
+    return L, idx, w, b
+
+
+@pytest.fixture
+def reference_path():
+    """Directory holding the reference's sparse_pooling package, when present
+    (GRANULE_REFERENCE); tests that need it are skipped elsewhere."""
+    p = os.environ.get("GRANULE_REFERENCE", "")
+    cand = [p] if p else []
+    cand.append(str(ROOT.parent / "reference"))
+    for c in cand:
+        if c and (Path(c) / "sparse_pooling" / "__init__.py").exists():
+            return c
+    pytest.skip("reference package not available on this host")

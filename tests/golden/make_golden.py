@@ -1,0 +1,148 @@
+"""Generate the golden fixtures of tests/golden/ from the reference implementation.
+
+Run in a checkout where the reference package ``sparse_pooling`` is importable:
+
+    python tests/golden/make_golden.py --reference <dir containing sparse_pooling/>
+
+What it writes (all from the reference's own code on the CPU):
+
+* ``init_hashes.json`` — sha256 of the (indices, weights, bias) bytes produced by
+  ``sparse_pooling.layout.init_parameters`` (layout.py:204-251) for a set of
+  layouts, seeds and chunk sizes, plus the layout shapes.  The product's
+  ``init_parameters`` must reproduce every hash bit for bit.
+* ``fwdbwd_<case>.npz`` — Mode-A layers rebuilt from the same seeds (their hash
+  is stored alongside), an input ``x`` and upstream gradient ``dy``, and the
+  reference's ``reference_forward`` output ``y`` with its autograd gradients
+  ``dx``, ``dw``, ``db``, computed in float64 (pytorch_reference.py:29-105) and
+  stored as float32 (dw/db for the first 32 groups).  The "sum" cases use the reference's
+  ``hidden_preactivations`` + activation + masked sum (the reference has no
+  sum operator).  One case draws indices uniformly with replacement
+  (duplicate indices inside a neuron).
+* ``adam.npz`` — five steps of ``torch.optim.AdamW``/``Adam`` in float64, the
+  recurrence the reference's optimizer test compares its fused kernel with
+  (tests/test_optim.py:11-28; optim.py:39-42).
+"""
+from __future__ import annotations
+
+import argparse
+import hashlib
+import json
+import sys
+from pathlib import Path
+
+import numpy as np
+import torch
+
+HERE = Path(__file__).resolve().parent
+GSUB = 32  # dw/db are stored for the first GSUB groups only (keeps the fixtures small)
+
+# (name, D, H, G, B, seed, bias_std, pooling, activation, index rule)
+CASES = [
+    ("cfg1_mean_relu", 256, 65536, 256, 64, 0, 0.0, "mean", "relu", "distinct"),
+    ("cfg1_sum_relu", 256, 65536, 256, 64, 0, 0.0, "sum", "relu", "distinct"),
+    ("ragged_b37", 64, 4099, 16, 37, 1, 0.3, "mean", "relu", "distinct"),
+    ("batch1", 64, 3000, 8, 1, 2, 0.2, "mean", "relu", "distinct"),
+    ("projection_identity", 128, 64, 64, 37, 3, 0.2, "mean", "identity", "distinct"),
+    ("gelu_mean", 64, 3000, 8, 16, 4, 0.2, "mean", "gelu", "distinct"),
+    ("sum_identity_ragged", 96, 1001, 7, 5, 5, 0.1, "sum", "identity", "distinct"),
+    ("uniform_dup_idx", 32, 2048, 8, 24, 6, 0.1, "mean", "relu", "uniform"),
+]
+
+INIT_CASES = [
+    # (D, H, G, C, shared, packed, seed, bias_std, chunk_records)
+    (256, 65536, 256, 8, False, False, 0, 0.0, 1 << 22),
+    (256, 65536, 256, 8, False, False, 7, 0.25, 1000),
+    (64, 4099, 16, 8, False, False, 1, 0.3, 1 << 22),
+    (64, 3001, 8, 16, True, False, 1, 0.5, 1 << 22),
+    (64, 7000, 8, 32, True, True, 2, 0.1, 999),
+    (1024, 30011, 16, 64, True, True, 3, 0.3, 1 << 22),
+    (4096, 98304, 4, 8, False, False, 1, 0.1, 1 << 14),
+]
+
+
+def sha(t: torch.Tensor) -> str:
+    return hashlib.sha256(t.contiguous().cpu().numpy().tobytes()).hexdigest()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", required=True, help="directory that contains the sparse_pooling package")
+    args = ap.parse_args()
+    sys.path.insert(0, args.reference)
+    from sparse_pooling.config import LevelSpec, PoolingConfig
+    from sparse_pooling.layout import SparseLayout, init_parameters
+    from sparse_pooling.reference import pytorch_reference as ref
+
+    torch.set_num_threads(8)
+    hashes = []
+    for D, H, G, C, shared, packed, seed, bstd, chunk in INIT_CASES:
+        L = SparseLayout(D, H, G, 8, C, shared, packed=packed)
+        i, w, b = init_parameters(L, "cpu", dtype=torch.float32, seed=seed, bias_std=bstd, chunk_records=chunk)
+        hashes.append(dict(layout=[D, H, G, 8, C, shared, packed], seed=seed, bias_std=bstd, chunk_records=chunk,
+                           dtype="float32", index_shape=list(L.index_shape), weight_shape=list(L.weight_shape),
+                           bias_shape=list(L.bias_shape), idx=sha(i), w=sha(w), b=sha(b)))
+        # bf16 storage (the reference's default dtype) draws the same indices
+        ib, wb, bb = init_parameters(L, "cpu", dtype=torch.bfloat16, seed=seed, bias_std=bstd, chunk_records=chunk)
+        hashes.append(dict(hashes[-1], dtype="bfloat16", idx=sha(ib), w=sha(wb.view(torch.int16)),
+                           b=sha(bb.view(torch.int16))))
+    (HERE / "init_hashes.json").write_text(json.dumps(hashes, indent=1))
+
+    for name, D, H, G, B, seed, bstd, pool, act, rule in CASES:
+        L = SparseLayout(D, H, G, 8, 8, False)
+        idx, w, b = init_parameters(L, "cpu", dtype=torch.float32, seed=seed, bias_std=bstd)
+        gen = torch.Generator().manual_seed(1000 + seed)
+        if rule == "uniform":
+            idx = torch.randint(0, D, idx.shape, generator=gen, dtype=torch.int64).to(torch.int16)
+            idx.view(G, -1, 8)[~L.valid_mask("cpu")] = 0
+        x = torch.randn(B, D, generator=gen)
+        xd = x.double().requires_grad_(True)
+        wd = w.double().requires_grad_(True)
+        bd = b.double().requires_grad_(True)
+        if pool == "mean":
+            cfg = PoolingConfig([LevelSpec("mean", activation=act)])
+            y = ref.reference_forward(xd, idx, wd, bd, L, cfg)
+        else:
+            z = ref.hidden_preactivations(xd, idx, wd, bd, L)
+            a = ref.activation(z, act)
+            y = torch.where(L.valid_mask("cpu")[None], a, torch.zeros_like(a)).sum(-1)
+        dy = torch.randn(y.shape, generator=gen)
+        (y * dy.double()).sum().backward()
+        # reference in float32 too: its deviation from the float64 values is recorded
+        x32 = x.clone().requires_grad_(True)
+        if pool == "mean":
+            y32 = ref.reference_forward(x32, idx, w, b, L, PoolingConfig([LevelSpec("mean", activation=act)]))
+        else:
+            z32 = ref.hidden_preactivations(x32, idx, w, b, L)
+            y32 = torch.where(L.valid_mask("cpu")[None], ref.activation(z32, act), torch.zeros_like(z32)).sum(-1)
+        dev32 = float((y32.detach().double() - y.detach()).abs().max() / (y.detach().abs().max() + 1e-30))
+        np.savez_compressed(
+            HERE / f"fwdbwd_{name}.npz",
+            meta=json.dumps(dict(name=name, D=D, H=H, G=G, B=B, seed=seed, bias_std=bstd, pool=pool, act=act,
+                                 rule=rule, idx_sha=sha(idx), w_sha=sha(w), b_sha=sha(b),
+                                 ref_fp32_vs_fp64_max_rel=dev32)),
+            idx=idx.numpy() if rule == "uniform" else np.zeros(0, np.int16),
+            x=x.numpy(), dy=dy.numpy(), y=y.detach().float().numpy(), dx=xd.grad.float().numpy(),
+            dw=wd.grad[:GSUB].float().numpy(), db=bd.grad[:GSUB].float().numpy())
+
+    torch.manual_seed(0)
+    out = {}
+    for tag, wdc in (("adamw", 0.1), ("adam", 0.0)):
+        p0 = torch.randn(1000, dtype=torch.float64)
+        q = torch.nn.Parameter(p0.clone())
+        opt = torch.optim.AdamW([q], lr=1e-2, betas=(0.9, 0.999), eps=1e-8, weight_decay=wdc)
+        gs, ps, ms, vs = [], [], [], []
+        for _ in range(5):
+            g = torch.randn(1000, dtype=torch.float64)
+            q.grad = g.clone()
+            opt.step()
+            gs.append(g.numpy()); ps.append(q.detach().clone().numpy())
+            ms.append(opt.state[q]["exp_avg"].clone().numpy()); vs.append(opt.state[q]["exp_avg_sq"].clone().numpy())
+        out.update({f"{tag}_p0": p0.numpy(), f"{tag}_g": np.stack(gs), f"{tag}_p": np.stack(ps),
+                    f"{tag}_m": np.stack(ms), f"{tag}_v": np.stack(vs), f"{tag}_wd": np.array(wdc)})
+    np.savez_compressed(HERE / "adam.npz", lr=np.array(1e-2), beta1=np.array(0.9), beta2=np.array(0.999),
+                        eps=np.array(1e-8), **out)
+    print("wrote", sorted(p.name for p in HERE.iterdir() if p.suffix in (".npz", ".json")))
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,70 @@
+"""The C-ABI library loads on a CPU-only host, exports every entry point
+include/granule_b200.h declares, and rejects bad arguments before touching a
+device (no compute calls here)."""
+import ctypes
+import re
+
+import pytest
+
+from conftest import ROOT
+from granulelayer_b200 import _native
+
+
+def _declared():
+    text = (ROOT / "include" / "granule_b200.h").read_text()
+    return sorted(set(re.findall(r"^\s*(?:int|int64_t|const char\*)\s+(gl_\w+)\s*\(", text, re.M)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _native.load()
+    names = _declared()
+    assert names, "no entry points parsed from the header"
+    for n in names:
+        assert hasattr(lib, n), f"{n} declared in include/granule_b200.h but not exported"
+    assert set(names) == set(_native.EXPORTS)
+
+
+def test_abi_version_and_status_strings():
+    lib = _native.load()
+    assert lib.gl_abi_version() == _native.ABI_VERSION
+    assert lib.gl_status_string(0) == b"ok"
+    for rc in range(-1, -8, -1):
+        assert lib.gl_status_string(rc) != b"unknown status"
+
+
+def test_argument_validation_needs_no_device():
+    lib = _native.load()
+    assert lib.gl_fwd_f32(None, None) == -1
+    assert lib.gl_bwd_f32(None, None) == -1
+    assert lib.gl_adam_f32(None, None) == -1
+    a = _native.GlFwdArgs()
+    a.B, a.D, a.NB, a.g0, a.g1 = 4, 0, 1, 0, 1           # D < 1
+    assert lib.gl_fwd_f32(ctypes.byref(a), None) == -2
+    a.D = 40000                                           # beyond int16 indices
+    assert lib.gl_fwd_f32(ctypes.byref(a), None) == -2
+    a.D, a.g0, a.g1 = 64, 3, 2                            # empty-reversed group range
+    assert lib.gl_fwd_f32(ctypes.byref(a), None) == -2
+    a.g0, a.g1, a.B = 0, 4, 0                             # empty batch: a no-op
+    assert lib.gl_fwd_f32(ctypes.byref(a), None) == 0
+    a.B = 4                                               # null pointers
+    assert lib.gl_fwd_f32(ctypes.byref(a), None) == -1
+    b = _native.GlBwdArgs()
+    b.B, b.D, b.NB, b.g0, b.g1 = 4, 64, 1, 0, 0           # empty group range: a no-op
+    assert lib.gl_bwd_f32(ctypes.byref(b), None) == 0
+    ad = _native.GlAdamArgs()
+    ad.n = -1
+    assert lib.gl_adam_f32(ctypes.byref(ad), None) == -2
+    ad.n = 0
+    assert lib.gl_adam_f32(ctypes.byref(ad), None) == 0
+
+
+def test_struct_layout_matches_header():
+    # field order and sizes of the ctypes mirrors (pointers 8 B, int64 8 B, int32/float 4 B)
+    assert ctypes.sizeof(_native.GlFwdArgs) == 6 * 8 + 7 * 8 + 4 * 4
+    assert ctypes.sizeof(_native.GlBwdArgs) == 9 * 8 + 8 * 8 + 4 * 4
+    assert ctypes.sizeof(_native.GlAdamArgs) == 4 * 8 + 8 + 8 * 4
+
+
+def test_missing_library_fails_loudly(tmp_path):
+    with pytest.raises(_native.NativeLibraryError):
+        _native.load(tmp_path / "nope.so")

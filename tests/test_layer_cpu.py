@@ -1,0 +1,86 @@
+"""Host-side behaviour of the drop-in layer (no GPU): construction, state dicts,
+and loud refusal of anything off the B200 path (no CPU or Triton fallback)."""
+import sys
+
+import pytest
+import torch
+
+from granulelayer_b200 import FusedAdamW, PhysicalPlan, SparsePoolingLayer
+from granulelayer_b200._native import NativeLibraryError
+from granulelayer_b200.autograd import UnsupportedOnB200
+
+
+def _layer(**kw):
+    args = dict(shared_neurons=None, pooling="mean", dtype=torch.float32, seed=0)
+    args.update(kw)
+    return SparsePoolingLayer(64, 3000, 8, **args)
+
+
+def test_shapes_and_repr():
+    lay = _layer()
+    assert lay.indices.shape == (8, 48, 8, 8) and lay.indices.dtype == torch.int16
+    assert lay.weight.shape == (8, 48, 8, 8) and lay.bias.shape == (8, 48, 8)
+    assert "A(independent)" in repr(lay) and "mean[relu]" in repr(lay)
+    assert lay.effective_policy == "minimal_stats"
+
+
+def test_cpu_forward_has_no_fallback():
+    lay = _layer()
+    with pytest.raises(NativeLibraryError):
+        lay(torch.randn(4, 64))
+
+
+@pytest.mark.parametrize("kw", [dict(shared_neurons=8), dict(pooling="max"), dict(dtype=torch.bfloat16),
+                                dict(pooling={"levels": [{"type": "mean", "neurons_per_shard": 128},
+                                                         {"type": "weighted_sum"}]})])
+def test_unsupported_configurations_raise(kw):
+    lay = _layer(**kw)
+    with pytest.raises(UnsupportedOnB200):
+        lay(torch.randn(2, 64))
+
+
+def test_main_grad_buffers():
+    lay = _layer()
+    lay.enable_main_grad()
+    assert lay.weight.main_grad.dtype == torch.float32 and lay.weight.main_grad.shape == lay.weight.shape
+    lay.weight.main_grad.fill_(1)
+    lay.zero_main_grad()
+    assert float(lay.weight.main_grad.abs().max()) == 0
+
+
+def test_state_dict_roundtrip():
+    a = _layer(seed=1)
+    b = _layer(seed=2)
+    assert not torch.equal(a.weight, b.weight)
+    b.load_state_dict(a.state_dict())
+    assert torch.equal(a.weight, b.weight) and torch.equal(a.indices, b.indices)
+    assert set(a.state_dict()) == {"indices", "weight", "bias"}
+
+
+def test_state_dict_interchanges_with_reference(reference_path):
+    sys.path.insert(0, reference_path)
+    from sparse_pooling import SparsePoolingLayer as RefLayer
+
+    ref = RefLayer(64, 3000, 8, shared_neurons=None, pooling="mean", dtype=torch.float32, seed=5, bias_std=0.1)
+    ours = _layer(seed=5, bias_std=0.1)
+    for k, v in ref.state_dict().items():
+        assert torch.equal(v, ours.state_dict()[k]), f"{k} differs from the reference's seeded layer"
+    ours2 = _layer(seed=9)
+    ours2.load_state_dict(ref.state_dict())
+    assert torch.equal(ours2.weight, ref.weight)
+
+
+def test_optimizer_refuses_unsupported_modes():
+    p = torch.nn.Parameter(torch.zeros(8))
+    p.main_grad = torch.zeros(8)
+    with pytest.raises(UnsupportedOnB200):
+        FusedAdamW([p], moments="bf16").step()
+
+
+def test_explain_on_cpu():
+    assert "CPU" in _layer().explain()["backend"]
+
+
+def test_plan_fields():
+    lay = _layer(plan=PhysicalPlan(b200_fwd_tokens=4, b200_dx_tokens=2))
+    assert lay.plan.b200_fwd_tokens == 4

@@ -1,0 +1,53 @@
+"""Pin the CPU oracle to the reference: every golden fixture (made by the
+reference's own code, tests/golden/make_golden.py) is reproduced by
+oracle/oracle.py on the same seeded inputs."""
+import numpy as np
+import pytest
+import torch
+
+from conftest import GOLDEN, assert_close, case_names, case_params, load_case
+from oracle import oracle as O
+
+
+@pytest.mark.parametrize("name", case_names())
+def test_oracle_matches_reference(name):
+    meta, arr = load_case(name)
+    L, idx, w, b = case_params(meta, arr)
+    if meta["rule"] != "uniform":
+        import hashlib
+
+        assert hashlib.sha256(idx.numpy().tobytes()).hexdigest() == meta["idx_sha"]
+        assert hashlib.sha256(w.numpy().tobytes()).hexdigest() == meta["w_sha"]
+    counts = L.counts_tensor("cpu").numpy()
+    x, dy = arr["x"], arr["dy"]
+    pre = O.forward(x, idx.numpy(), w.numpy(), b.numpy(), counts, meta["pool"], meta["act"])
+    # fixtures are float64 results rounded to float32: compare at float32 resolution
+    assert_close(pre, arr["y"], 2e-6, 1e-7, "y")
+    dx, dw, db = O.backward(x, idx.numpy(), w.numpy(), b.numpy(), counts, dy, meta["pool"], meta["act"])
+    gs = arr["dw"].shape[0]
+    assert_close(dx, arr["dx"], 2e-6, 1e-7, "dx")
+    assert_close(dw[:gs], arr["dw"], 2e-6, 1e-7, "dw")
+    assert_close(db[:gs], arr["db"], 2e-6, 1e-7, "db")
+
+
+@pytest.mark.parametrize("tag", ["adam", "adamw"])
+def test_oracle_adam_matches_torch(tag):
+    d = np.load(GOLDEN / "adam.npz")
+    p = d[f"{tag}_p0"].copy()
+    m = np.zeros_like(p)
+    v = np.zeros_like(p)
+    for s in range(5):
+        p, m, v = O.adam_step(p, d[f"{tag}_g"][s], m, v, float(d["lr"]), float(d["beta1"]), float(d["beta2"]),
+                              float(d["eps"]), float(d[f"{tag}_wd"]), s + 1)
+        np.testing.assert_allclose(p, d[f"{tag}_p"][s], rtol=1e-12, atol=1e-14)
+        np.testing.assert_allclose(m, d[f"{tag}_m"][s], rtol=1e-12, atol=1e-14)
+        np.testing.assert_allclose(v, d[f"{tag}_v"][s], rtol=1e-12, atol=1e-14)
+
+
+def test_oracle_sum_is_n_times_mean():
+    meta, arr = load_case("cfg1_mean_relu")
+    L, idx, w, b = case_params(meta, arr)
+    c = L.counts_tensor("cpu").numpy()
+    m = O.forward(arr["x"], idx.numpy(), w.numpy(), b.numpy(), c, "mean", "relu")
+    s = O.forward(arr["x"], idx.numpy(), w.numpy(), b.numpy(), c, "sum", "relu")
+    np.testing.assert_allclose(s, m * c[None, :], rtol=1e-12)
