@@ -220,7 +220,13 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ref-seconds", type=float, default=4.0)
+    ap.add_argument("--groups", type=int, default=G,
+                    help="pooling groups of 24,576 neurons (default 4096 = the full 100M layer; smaller values "
+                         "give the reduced cases used for ncu captures)")
     args = ap.parse_args()
+    global N, G
+    if args.groups != G:
+        N, G = args.groups * (N // G), args.groups
     if args.warmup < 3 and args.impl == "ours":
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
 

@@ -16,7 +16,7 @@ from pathlib import Path
 
 import torch
 
-ABI_VERSION = 1
+ABI_VERSION = 2
 LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libgranule_b200.so"
 
 POOL_MEAN, POOL_SUM = 0, 1
@@ -24,7 +24,8 @@ ACT_IDS = {"identity": 0, "relu": 1, "gelu": 2}
 
 # The exported entry points, in header order (checked by the CPU test suite).
 EXPORTS = ("gl_abi_version", "gl_status_string", "gl_last_cuda_error", "gl_fwd_f32", "gl_bwd_f32",
-           "gl_adam_f32", "gl_launch_count", "gl_fwd_auto_tokens", "gl_bwd_auto_tokens")
+           "gl_adam_f32", "gl_group_absmax_f32", "gl_group_index_maxcount", "gl_launch_count",
+           "gl_fwd_auto_tokens", "gl_bwd_auto_tokens")
 
 
 class NativeLibraryError(RuntimeError):
@@ -37,7 +38,7 @@ class GlFwdArgs(ctypes.Structure):
                 ("B", ctypes.c_int64), ("D", ctypes.c_int64), ("NB", ctypes.c_int64),
                 ("g0", ctypes.c_int64), ("g1", ctypes.c_int64), ("ldx", ctypes.c_int64), ("ldp", ctypes.c_int64),
                 ("pool", ctypes.c_int32), ("act", ctypes.c_int32), ("tokens", ctypes.c_int32),
-                ("groups_per_cta", ctypes.c_int32)]
+                ("groups_per_cta", ctypes.c_int32), ("wabsmax", ctypes.c_void_p)]
 
 
 class GlBwdArgs(ctypes.Structure):
@@ -48,7 +49,7 @@ class GlBwdArgs(ctypes.Structure):
                 ("g0", ctypes.c_int64), ("g1", ctypes.c_int64),
                 ("ldx", ctypes.c_int64), ("ldg", ctypes.c_int64), ("lddx", ctypes.c_int64),
                 ("pool", ctypes.c_int32), ("act", ctypes.c_int32), ("tokens", ctypes.c_int32),
-                ("groups_per_cta", ctypes.c_int32)]
+                ("groups_per_cta", ctypes.c_int32), ("wabsmax", ctypes.c_void_p), ("rowmax", ctypes.c_void_p)]
 
 
 class GlAdamArgs(ctypes.Structure):
@@ -88,6 +89,12 @@ def load(path=None) -> ctypes.CDLL:
             fn = getattr(lib, name)
             fn.restype = ctypes.c_int
             fn.argtypes = [ctypes.POINTER(st), ctypes.c_void_p]
+        lib.gl_group_absmax_f32.restype = ctypes.c_int
+        lib.gl_group_absmax_f32.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
+                                            ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p]
+        lib.gl_group_index_maxcount.restype = ctypes.c_int
+        lib.gl_group_index_maxcount.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
+                                                ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p]
         for name in ("gl_fwd_auto_tokens", "gl_bwd_auto_tokens"):
             getattr(lib, name).restype = ctypes.c_int
             getattr(lib, name).argtypes = [ctypes.c_int64]
@@ -124,26 +131,46 @@ def _require_cuda(*ts):
 
 
 def fwd(x, idx, w, b, counts, pre, NB: int, g0: int, g1: int, pool: int, act: int, tokens: int = 0,
-        groups_per_cta: int = 0):
-    """pre[:, :g1-g0] = pooled act(z) of groups [g0, g1).  See GlFwdArgs."""
-    _require_cuda(x, idx, w, b, counts, pre)
+        groups_per_cta: int = 0, wabsmax=None):
+    """pre[:, :g1-g0] = pooled act(z) of groups [g0, g1); optionally wabsmax[g-g0] = max |w|.
+    See GlFwdArgs."""
+    _require_cuda(x, idx, w, b, counts, pre, wabsmax)
     lib = load()
     a = GlFwdArgs(_ptr(x), _ptr(idx), _ptr(w), _ptr(b), _ptr(counts), _ptr(pre), x.shape[0], x.shape[1], NB,
-                  g0, g1, x.stride(0), pre.stride(0), pool, act, tokens, groups_per_cta)
+                  g0, g1, x.stride(0), pre.stride(0), pool, act, tokens, groups_per_cta, _ptr(wabsmax))
     with torch.cuda.device(x.device):
         _check(lib, lib.gl_fwd_f32(ctypes.byref(a), _stream(x.device)), "gl_fwd_f32")
 
 
 def bwd(x, idx, w, b, counts, gpre, dx, dw, db, NB: int, g0: int, g1: int, pool: int, act: int, tokens: int = 0,
-        groups_per_cta: int = 0):
-    """dx += ..., dw += ..., db += ... for groups [g0, g1).  See GlBwdArgs."""
-    _require_cuda(x, idx, w, b, counts, gpre, dx, dw, db)
+        groups_per_cta: int = 0, wabsmax=None, rowmax=None):
+    """dx += ..., dw += ..., db += ... for groups [g0, g1); fixed-point dX tiles when the
+    per-group bounds ``wabsmax``/``rowmax`` are given.  See GlBwdArgs."""
+    _require_cuda(x, idx, w, b, counts, gpre, dx, dw, db, wabsmax, rowmax)
     lib = load()
     a = GlBwdArgs(_ptr(x), _ptr(idx), _ptr(w), _ptr(b), _ptr(counts), _ptr(gpre), _ptr(dx), _ptr(dw), _ptr(db),
                   x.shape[0], x.shape[1], NB, g0, g1, x.stride(0), gpre.stride(0), dx.stride(0), pool, act,
-                  tokens, groups_per_cta)
+                  tokens, groups_per_cta, _ptr(wabsmax), _ptr(rowmax))
     with torch.cuda.device(x.device):
         _check(lib, lib.gl_bwd_f32(ctypes.byref(a), _stream(x.device)), "gl_bwd_f32")
+
+
+def group_absmax(w, counts, NB: int, g0: int, g1: int, out):
+    """out[g-g0] = max |w| over the valid slots of group g (gl_group_absmax_f32)."""
+    _require_cuda(w, counts, out)
+    lib = load()
+    with torch.cuda.device(w.device):
+        _check(lib, lib.gl_group_absmax_f32(_ptr(w), _ptr(counts), NB, g0, g1, _ptr(out), _stream(w.device)),
+               "gl_group_absmax_f32")
+
+
+def group_index_maxcount(idx, counts, D: int, NB: int, g0: int, g1: int, out):
+    """out[g-g0] = max records of group g sharing one feature (gl_group_index_maxcount)."""
+    _require_cuda(idx, counts, out)
+    lib = load()
+    with torch.cuda.device(idx.device):
+        _check(lib, lib.gl_group_index_maxcount(_ptr(idx), _ptr(counts), D, NB, g0, g1, _ptr(out),
+                                                _stream(idx.device)), "gl_group_index_maxcount")
 
 
 def adam(p, g, m, v, lr, beta1, beta2, eps, weight_decay, bc1, bc2, zero_grad=True):

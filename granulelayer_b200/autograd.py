@@ -96,6 +96,23 @@ class Level1Runtime:
         self.act = _native.ACT_IDS[level.activation]
         self.last_info: Dict = {}
         self.det = False
+        self._rowmax = None
+        self._rowmax_key = None
+
+    @property
+    def fixed_point(self) -> bool:
+        return self.plan.b200_dx_accum in ("auto", "fixed")
+
+    def rowmax(self) -> torch.Tensor:
+        """Per-group max number of records sharing one input feature (depends only on
+        the indices; recomputed when the index tensor changes)."""
+        key = (self.idx.data_ptr(), self.idx._version)
+        if self._rowmax is None or self._rowmax_key != key:
+            out = torch.empty(self.groups, device=self.idx.device, dtype=torch.int32)
+            _native.group_index_maxcount(self.idx, self.counts_i32, self.layout.input_dim,
+                                         self.layout.blocks_per_group, 0, self.groups, out)
+            self._rowmax, self._rowmax_key = out, key
+        return self._rowmax
 
     @property
     def groups(self) -> int:
@@ -136,14 +153,19 @@ class Level1Runtime:
         }
 
     def forward(self, x: torch.Tensor, w: torch.Tensor, b: torch.Tensor, track_ids: bool = False):
+        """{"pre": [B, G] pooled values, "wabsmax": [G] max |w| per group (for the backward)}."""
         B = x.shape[0]
         self.check_devices(x, w, b)
         self.resolve_reduction(B)
         pre = torch.empty((B, self.groups), device=x.device, dtype=torch.float32)
+        wabsmax = torch.empty(self.groups, device=x.device, dtype=torch.float32) if B > 0 else None
         _native.fwd(x, self.idx, w, b, self.counts_i32, pre, self.layout.blocks_per_group, 0, self.groups,
-                    self.pool, self.act, tokens=self.plan.b200_fwd_tokens)
+                    self.pool, self.act, tokens=self.plan.b200_fwd_tokens, wabsmax=wabsmax)
         self.last_info.update(forward_backend="b200", workspace_bytes=0)
-        return {"pre": pre}
+        out = {"pre": pre}
+        if wabsmax is not None:
+            out["wabsmax"] = wabsmax
+        return out
 
     def backward(self, x, w, b, g_pre: torch.Tensor, saved: Dict, policy: str, dw_buf: torch.Tensor,
                  db_buf: torch.Tensor, recomputed: bool = False) -> torch.Tensor:
@@ -153,9 +175,18 @@ class Level1Runtime:
         self.check_devices(x, w, b, g_pre, dw_buf, db_buf)
         self.resolve_reduction(B)
         dx = torch.zeros((B, D), device=x.device, dtype=torch.float32)
+        wabsmax = rowmax = None
+        if self.fixed_point and B > 0:
+            wabsmax = saved.get("wabsmax")
+            if wabsmax is None:
+                wabsmax = torch.empty(self.groups, device=x.device, dtype=torch.float32)
+                _native.group_absmax(w, self.counts_i32, self.layout.blocks_per_group, 0, self.groups, wabsmax)
+            rowmax = self.rowmax()
         _native.bwd(x, self.idx, w, b, self.counts_i32, g_pre, dx, dw_buf, db_buf, self.layout.blocks_per_group,
-                    0, self.groups, self.pool, self.act, tokens=self.plan.b200_dx_tokens)
+                    0, self.groups, self.pool, self.act, tokens=self.plan.b200_dx_tokens, wabsmax=wabsmax,
+                    rowmax=rowmax)
         self.last_info["backward_backend"] = "b200"
+        self.last_info["dx_accumulation"] = "int32 fixed point" if wabsmax is not None else "fp32 atomics"
         return dx
 
 
@@ -187,18 +218,22 @@ class SparsePoolFunction(torch.autograd.Function):
         pre = out["pre"]
         y = act_torch(pre, rt.level.out_activation)
         ctx.rt, ctx.policy = rt, policy
-        ctx.save_for_backward(x, w, b, pre)
+        ctx.has_wmax = "wabsmax" in out
+        ctx.save_for_backward(x, w, b, pre, *([out["wabsmax"]] if ctx.has_wmax else []))
         rt.last_info["checkpoint_bytes"] = pre.numel() * pre.element_size()
         return y
 
     @staticmethod
     def backward(ctx, dy):
-        x, w, b, pre = ctx.saved_tensors
+        x, w, b, pre, *rest = ctx.saved_tensors
         rt: Level1Runtime = ctx.rt
         xc, wc, bc = _compute_operands(x, w, b)
         g_pre = (dy.float() * dact_torch(pre, rt.level.out_activation)).contiguous()
         dw_buf, db_buf, use_main = _grad_buffers(w, b)
-        dx = rt.backward(xc, wc, bc, g_pre, {"pre": pre}, ctx.policy, dw_buf, db_buf)
+        saved = {"pre": pre}
+        if ctx.has_wmax:
+            saved["wabsmax"] = rest[0]
+        dx = rt.backward(xc, wc, bc, g_pre, saved, ctx.policy, dw_buf, db_buf)
         gw = None if use_main else dw_buf.to(w.dtype)
         gb = None if use_main else db_buf.to(b.dtype)
         return dx.to(x.dtype, memory_format=torch.contiguous_format), gw, gb, None, None, None

@@ -250,6 +250,9 @@ class PhysicalPlan:
     b200_fwd_tokens: int = 0       # tokens per forward tile (power of two, bounded by shared memory)
     b200_dx_tokens: int = 0        # tokens per dX tile
     b200_dx_splits: int = 0        # neuron-range splits of the dX kernel (global red flushes)
+    # block-private dX accumulation of the backward: "fixed" = int32 fixed point (faster; rounding
+    # well inside the dX tolerance), "fp32" = fp32 shared-memory atomics, "auto" = "fixed"
+    b200_dx_accum: str = "auto"
 
     def __post_init__(self):
         if self.input_layout not in ("feature_major", "token_major"):
@@ -270,6 +273,8 @@ class PhysicalPlan:
                 raise ValueError(f"{f} must be 0 or a power of two <= 32")
         if self.b200_dx_splits < 0:
             raise ValueError("b200_dx_splits must be >= 0")
+        if self.b200_dx_accum not in ("auto", "fixed", "fp32"):
+            raise ValueError("b200_dx_accum must be 'auto', 'fixed' or 'fp32'")
 
 
 def resolve_reduction(plan: PhysicalPlan):

@@ -30,7 +30,8 @@ template <int T, int ACT>
 __global__ void __launch_bounds__(kFwdThreads, 1)
     fwd_kernel(const float* __restrict__ x, const int16_t* __restrict__ idx, const float* __restrict__ w,
                const float* __restrict__ bias, const int32_t* __restrict__ counts, float* __restrict__ pre,
-               int B, int D, int64_t NB, int64_t g0, int64_t g1, int64_t ldx, int64_t ldp, int pool, int gpc) {
+               int B, int D, int64_t NB, int64_t g0, int64_t g1, int64_t ldx, int64_t ldp, int pool, int gpc,
+               float* __restrict__ wabsmax) {
   constexpr int V = T < 4 ? T : 4;   // tokens per lane
   constexpr int LPN = T / V;         // lanes per neuron
   constexpr int NPW = 32 / LPN;      // neurons per warp step
@@ -38,6 +39,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   constexpr int UNR = 2;             // neurons in flight per lane
   extern __shared__ __align__(16) float xs[];
   __shared__ float red[NW][T];
+  __shared__ float redw[NW];
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int t0 = blockIdx.x * T;
@@ -56,6 +58,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     float acc[V];
 #pragma unroll
     for (int v = 0; v < V; ++v) acc[v] = 0.f;
+    float wmx = 0.f;  // max |w| over the valid slots this lane reads (for the backward's fixed-point scale)
 
     for (int s0 = warp * NPW * UNR; s0 < ng; s0 += NW * NPW * UNR) {
       Rec8 r[UNR];
@@ -96,6 +99,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         if (ok[u]) {
 #pragma unroll
           for (int v = 0; v < V; ++v) acc[v] += act_f<ACT>(z[v]);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) wmx = fmaxf(wmx, fabsf(wr[u].w[k]));
         }
       }
     }
@@ -107,6 +112,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     if (lane < LPN)
 #pragma unroll
       for (int v = 0; v < V; ++v) red[warp][lane * V + v] = acc[v];
+    const bool want_w = wabsmax != nullptr && blockIdx.x == 0;
+    if (want_w) {
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) wmx = fmaxf(wmx, __shfl_xor_sync(kFullMask, wmx, off));
+      if (lane == 0) redw[warp] = wmx;
+    }
     __syncthreads();
     if (threadIdx.x < T) {
       float s = 0.f;
@@ -114,6 +125,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       for (int i = 0; i < NW; ++i) s += red[i][threadIdx.x];
       const int t = t0 + threadIdx.x;
       if (t < B) pre[(int64_t)t * ldp + (g - g0)] = (pool == GL_POOL_MEAN) ? s / (float)ng : s;
+    }
+    if (want_w && threadIdx.x == 32) {
+      float m = 0.f;
+#pragma unroll
+      for (int i = 0; i < NW; ++i) m = fmaxf(m, redw[i]);
+      wabsmax[g - g0] = m;
     }
     __syncthreads();
   }
@@ -130,7 +147,7 @@ static int launch_fwd(const GlFwdArgs& a, int gpc, cudaStream_t st) {
   if (tiles > 2147483647LL || chunks > 65535) return GL_ERR_SHAPE;
   dim3 grid((unsigned)tiles, (unsigned)chunks);
   kern<<<grid, kFwdThreads, smem, st>>>(a.x, a.idx, a.w, a.b, a.counts, a.pre, (int)a.B, (int)a.D, a.NB, a.g0,
-                                        a.g1, a.ldx, a.ldp, a.pool, gpc);
+                                        a.g1, a.ldx, a.ldp, a.pool, gpc, a.wabsmax);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_cuda_error(e);
   count_launches(1);

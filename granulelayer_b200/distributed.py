@@ -56,20 +56,25 @@ class _ShardedPoolFunction(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, w, b, rt, G, g0, g1, group):
         xc, wc, bc = _compute_operands(x, w, b)
-        pre_l = rt.forward(xc, wc, bc)["pre"]
+        out = rt.forward(xc, wc, bc)
+        pre_l = out["pre"]
         pre = gather_columns(pre_l, G, group)
         ctx.rt, ctx.g0, ctx.g1, ctx.group = rt, g0, g1, group
-        ctx.save_for_backward(x, w, b, pre_l)
+        ctx.has_wmax = "wabsmax" in out
+        ctx.save_for_backward(x, w, b, pre_l, *([out["wabsmax"]] if ctx.has_wmax else []))
         return act_torch(pre, rt.level.out_activation)
 
     @staticmethod
     def backward(ctx, dy):
-        x, w, b, pre_l = ctx.saved_tensors
+        x, w, b, pre_l, *rest = ctx.saved_tensors
         rt = ctx.rt
         xc, wc, bc = _compute_operands(x, w, b)
         g_pre = (dy[:, ctx.g0:ctx.g1].float() * dact_torch(pre_l, rt.level.out_activation)).contiguous()
         dw_buf, db_buf, use_main = _grad_buffers(w, b)
-        dx = rt.backward(xc, wc, bc, g_pre, {"pre": pre_l}, "minimal_stats", dw_buf, db_buf)
+        saved = {"pre": pre_l}
+        if ctx.has_wmax:
+            saved["wabsmax"] = rest[0]
+        dx = rt.backward(xc, wc, bc, g_pre, saved, "minimal_stats", dw_buf, db_buf)
         dist.all_reduce(dx, group=ctx.group)
         gw = None if use_main else dw_buf.to(w.dtype)
         gb = None if use_main else db_buf.to(b.dtype)
@@ -167,7 +172,8 @@ class ShardedTrainStep:
         rt = lay.runtime()
         G = lay.layout.groups
         w, b = lay.weight.detach(), lay.bias.detach()
-        pre_l = rt.forward(x, w, b)["pre"]
+        fout = rt.forward(x, w, b)
+        pre_l = fout["pre"]
         world = lay.world
         width = -(-G // world)
         if world > 1:
@@ -181,7 +187,7 @@ class ShardedTrainStep:
         if out_act != "identity":
             g_pre = g_pre * dact_torch(pre_l, out_act)
         g_pre = g_pre.contiguous()
-        dx = rt.backward(x, w, b, g_pre, {"pre": pre_l}, "minimal_stats", lay.weight.main_grad, lay.bias.main_grad)
+        dx = rt.backward(x, w, b, g_pre, fout, "minimal_stats", lay.weight.main_grad, lay.bias.main_grad)
         if world > 1:
             ar = dist.all_reduce(dx, group=lay.group, async_op=True)
         self.opt.step()

@@ -44,7 +44,7 @@
 extern "C" {
 #endif
 
-#define GL_ABI_VERSION 1
+#define GL_ABI_VERSION 2
 
 typedef enum GlStatus {
   GL_OK = 0,
@@ -80,6 +80,8 @@ typedef struct GlFwdArgs {
   int32_t act;              /* GL_ACT_* */
   int32_t tokens;           /* token tile (0 = automatic; else 1, 2, 4 or 8) */
   int32_t groups_per_cta;   /* groups per thread block (0 = automatic) */
+  float* wabsmax;           /* optional [g1-g0] output: max |w| over each group's valid slots
+                               (the backward's fixed-point bound); NULL = not computed */
 } GlFwdArgs;
 
 /* Backward: with c1[t, g] = gpre[t, g - g0] / counts[g] (mean) or gpre (sum) and
@@ -89,6 +91,11 @@ typedef struct GlFwdArgs {
  *   db[f]      += sum_t dz[t, f]
  * dx, dw and db are accumulated (+=); dw/db use the weight/bias layout, so they
  * can be the reference's FP32 `main_grad` buffers (autograd.py:357-363).
+ * With `wabsmax` and `rowmax` (both from the calls below, or the forward's
+ * wabsmax output) the block-private dX tile is accumulated in int32 fixed point
+ * (faster); with both NULL it is accumulated with fp32 atomics.  Non-finite
+ * coefficients or weights make the affected tokens' dx non-finite, as fp32
+ * arithmetic would.
  * Replaces dense_coefficients + launch_dense_backward (kernels/ops.py:242-278). */
 typedef struct GlBwdArgs {
   const float* x;
@@ -107,6 +114,8 @@ typedef struct GlBwdArgs {
   int32_t act;
   int32_t tokens;           /* token tile (0 = automatic; else 1, 2, 4 or 8) */
   int32_t groups_per_cta;   /* 0 = automatic */
+  const float* wabsmax;     /* [g1-g0] max |w| per group (gl_group_absmax_f32), or NULL */
+  const int32_t* rowmax;    /* [g1-g0] max records per input feature (gl_group_index_maxcount), or NULL */
 } GlBwdArgs;
 
 /* Adam(W) step over n fp32 elements, in place (sparse_pooling/optim.py:26-64):
@@ -132,6 +141,16 @@ int gl_last_cuda_error(void);
 int gl_fwd_f32(const GlFwdArgs* args, void* stream);
 int gl_bwd_f32(const GlBwdArgs* args, void* stream);
 int gl_adam_f32(const GlAdamArgs* args, void* stream);
+
+/* Per-group bounds of the fixed-point backward (no counterpart in the reference):
+ *   gl_group_absmax_f32:     out[g-g0] = max |w[8f+k]| over the valid slots f of group g
+ *   gl_group_index_maxcount: out[g-g0] = max over features d of the number of valid
+ *                            (slot, k) records of group g with idx == d
+ * The second depends only on the indices; callers compute it once per layer. */
+int gl_group_absmax_f32(const float* w, const int32_t* counts, int64_t NB, int64_t g0, int64_t g1, float* out,
+                        void* stream);
+int gl_group_index_maxcount(const int16_t* idx, const int32_t* counts, int64_t D, int64_t NB, int64_t g0,
+                            int64_t g1, int32_t* out, void* stream);
 
 /* Number of kernels this library has launched successfully in this process
    (all devices).  Benchmarks difference it around a timed region. */

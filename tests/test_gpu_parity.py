@@ -41,11 +41,14 @@ def _run(lay, x, dy):
     return y.detach().cpu(), xg.grad.cpu(), lay.weight.grad.cpu(), lay.bias.grad.cpu()
 
 
+@pytest.mark.parametrize("accum", ["fixed", "fp32"])
 @pytest.mark.parametrize("name", case_names())
-def test_matches_reference_golden(name):
+def test_matches_reference_golden(name, accum):
     meta, arr = load_case(name)
     L, idx, w, b = case_params(meta, arr)
-    y, dx, dw, db = _run(_layer_for(meta, idx, w, b), arr["x"], arr["dy"])
+    lay = _layer_for(meta, idx, w, b, plan=PhysicalPlan(b200_dx_accum=accum))
+    y, dx, dw, db = _run(lay, arr["x"], arr["dy"])
+    assert lay.last_info["dx_accumulation"] == ("int32 fixed point" if accum == "fixed" else "fp32 atomics")
     gs = arr["dw"].shape[0]
     assert_close(y, arr["y"], what="y", **FWD)
     assert_close(dx, arr["dx"], what="dx", **BWD)
@@ -58,12 +61,13 @@ def test_matches_reference_golden(name):
     assert_close(db, odb, what="db(all groups)", **BWD)
 
 
+@pytest.mark.parametrize("accum", ["fixed", "fp32"])
 @pytest.mark.parametrize("tf", [1, 2, 4, 8])
 @pytest.mark.parametrize("tb", [1, 2, 4, 8])
-def test_token_tiles(tf, tb):
+def test_token_tiles(tf, tb, accum):
     meta, arr = load_case("ragged_b37")
     L, idx, w, b = case_params(meta, arr)
-    lay = _layer_for(meta, idx, w, b, plan=PhysicalPlan(b200_fwd_tokens=tf, b200_dx_tokens=tb))
+    lay = _layer_for(meta, idx, w, b, plan=PhysicalPlan(b200_fwd_tokens=tf, b200_dx_tokens=tb, b200_dx_accum=accum))
     y, dx, dw, db = _run(lay, arr["x"], arr["dy"])
     assert_close(y, arr["y"], what="y", **FWD)
     assert_close(dx, arr["dx"], what="dx", **BWD)
@@ -90,19 +94,30 @@ def test_group_range_sharding(pool):
         assert torch.equal(part, full[:, g0:g1])
 
 
-def test_backward_group_range_sums_to_full():
+def _bounds(L, idx, w, counts, g0, g1):
+    wm = torch.empty(g1 - g0, device="cuda")
+    rm = torch.empty(g1 - g0, device="cuda", dtype=torch.int32)
+    _native.group_absmax(w, counts, L.blocks_per_group, g0, g1, wm)
+    _native.group_index_maxcount(idx, counts, L.input_dim, L.blocks_per_group, g0, g1, rm)
+    return wm, rm
+
+
+@pytest.mark.parametrize("fixed", [True, False])
+def test_backward_group_range_sums_to_full(fixed):
     L, idx, w, b = _rand_layer(96, 4000, 9, seed=4)
-    counts = L.counts_tensor("cuda")
+    counts = L.counts_tensor("cuda").to(torch.int32)
     x = torch.randn(33, 96, device="cuda")
     gp = torch.randn(33, 9, device="cuda")
     NB = L.blocks_per_group
     dx_full = torch.zeros(33, 96, device="cuda")
     dw_full, db_full = torch.zeros_like(w), torch.zeros_like(b)
-    _native.bwd(x, idx, w, b, counts, gp, dx_full, dw_full, db_full, NB, 0, 9, 0, 1)
+    kw = dict(zip(("wabsmax", "rowmax"), _bounds(L, idx, w, counts, 0, 9))) if fixed else {}
+    _native.bwd(x, idx, w, b, counts, gp, dx_full, dw_full, db_full, NB, 0, 9, 0, 1, **kw)
     dx_sum = torch.zeros_like(dx_full)
     dw_p, db_p = torch.zeros_like(w), torch.zeros_like(b)
     for g0, g1 in [(0, 4), (4, 9)]:
-        _native.bwd(x, idx, w, b, counts, gp[:, g0:g1].contiguous(), dx_sum, dw_p, db_p, NB, g0, g1, 0, 1)
+        kw = dict(zip(("wabsmax", "rowmax"), _bounds(L, idx, w, counts, g0, g1))) if fixed else {}
+        _native.bwd(x, idx, w, b, counts, gp[:, g0:g1].contiguous(), dx_sum, dw_p, db_p, NB, g0, g1, 0, 1, **kw)
     assert_close(dx_sum, dx_full, what="dx", **BWD)
     assert_close(dw_p, dw_full, what="dw", **BWD)
     assert_close(db_p, db_full, what="db", **BWD)
@@ -204,3 +219,38 @@ def test_no_hidden_activation_is_materialized():
     extra = torch.cuda.max_memory_allocated() - base
     assert extra < B * H * 4 / 20, f"peak extra {extra / 2**20:.0f} MiB suggests materialization"
     assert lay.last_info["checkpoint_bytes"] == B * 1024 * 4
+
+
+@pytest.mark.parametrize("D,H,G", [(64, 3001, 8), (4096, 200_000, 4), (777, 5000, 13)])
+def test_group_bounds_match_torch(D, H, G):
+    L, idx, w, b = _rand_layer(D, H, G, seed=11)
+    counts = L.counts_tensor("cuda").to(torch.int32)
+    wm, rm = _bounds(L, idx, w, counts, 0, G)
+    valid = L.valid_mask("cuda").view(G, -1)
+    w_valid = torch.where(valid[..., None], w.view(G, -1, 8).abs(), torch.zeros((), device="cuda"))
+    assert torch.equal(wm, w_valid.amax(dim=(1, 2)))
+    hist = torch.zeros(G, D, device="cuda", dtype=torch.int64)
+    iv = torch.where(valid[..., None], idx.view(G, -1, 8).long(), torch.full((), D, device="cuda"))
+    hist2 = torch.zeros(G, D + 1, device="cuda", dtype=torch.int64)
+    hist2.scatter_add_(1, iv.view(G, -1), torch.ones_like(iv.view(G, -1)))
+    assert torch.equal(rm.long(), hist2[:, :D].amax(1))
+    # the forward's optional output equals the standalone bound
+    pre = torch.empty(5, G, device="cuda")
+    wm2 = torch.empty(G, device="cuda")
+    _native.fwd(torch.randn(5, D, device="cuda"), idx, w, b, counts, pre, L.blocks_per_group, 0, G, 0, 1,
+                wabsmax=wm2)
+    assert torch.equal(wm2, wm)
+
+
+@pytest.mark.parametrize("accum", ["fixed", "fp32"])
+@pytest.mark.parametrize("bad", [float("nan"), float("inf")])
+def test_nonfinite_upstream_gradient_reaches_dx(accum, bad):
+    meta, arr = load_case("ragged_b37")
+    L, idx, w, b = case_params(meta, arr)
+    lay = _layer_for(meta, idx, w, b, plan=PhysicalPlan(b200_dx_accum=accum))
+    dy = arr["dy"].copy()
+    dy[3, 2] = bad
+    y, dx, dw, db = _run(lay, arr["x"], dy)
+    assert not bool(torch.isfinite(dx[3]).all()), "token 3 must see the non-finite coefficient"
+    keep = [t for t in range(dx.shape[0]) if t != 3]
+    assert_close(dx[keep], arr["dx"][keep], what="dx(other tokens)", **BWD)
