@@ -212,6 +212,7 @@ def run_reference(args, rank, world):
 
 
 def main():
+    global N, G
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
@@ -224,7 +225,6 @@ def main():
                     help="pooling groups of 24,576 neurons (default 4096 = the full 100M layer; smaller values "
                          "give the reduced cases used for ncu captures)")
     args = ap.parse_args()
-    global N, G
     if args.groups != G:
         N, G = args.groups * (N // G), args.groups
     if args.warmup < 3 and args.impl == "ours":

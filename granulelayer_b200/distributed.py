@@ -46,8 +46,9 @@ def gather_columns(local: torch.Tensor, G: int, group=None) -> torch.Tensor:
     width = -(-G // world)
     buf = local.new_zeros((B, width))
     buf[:, :local.shape[1]] = local
-    out = local.new_empty((world, B, width))
+    out = local.new_empty((world * B, width))
     dist.all_gather_into_tensor(out, buf, group=group)
+    out = out.view(world, B, width)
     cols = [out[r, :, :shard_range(G, r, world)[1] - shard_range(G, r, world)[0]] for r in range(world)]
     return torch.cat(cols, dim=1)
 
@@ -180,8 +181,9 @@ class ShardedTrainStep:
             buf = pre_l.new_zeros((x.shape[0], width)) if pre_l.shape[1] != width else pre_l
             if buf is not pre_l:
                 buf[:, :pre_l.shape[1]] = pre_l
-            gathered = pre_l.new_empty((world, x.shape[0], width))
+            gathered = pre_l.new_empty((world * x.shape[0], width))
             ag = dist.all_gather_into_tensor(gathered, buf, group=lay.group, async_op=True)
+            gathered = gathered.view(world, x.shape[0], width)
         out_act = lay.cfg.levels[0].out_activation
         g_pre = dy[:, lay.g0:lay.g1]
         if out_act != "identity":

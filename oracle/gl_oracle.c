@@ -90,10 +90,14 @@ int glo_bwd(const float* x, int64_t B, int64_t D, int64_t ldx, const int16_t* id
     me = omp_get_thread_num();
 #endif
     double* mydx = priv + (size_t)me * B * D;
+    /* work items: (group, chunk of 256 slots); each owns its slots' dw/db */
+    const int64_t chunks = (slots + 255) / 256;
 #pragma omp for schedule(dynamic, 1)
-    for (int64_t g = 0; g < G; ++g) {
+    for (int64_t item = 0; item < G * chunks; ++item) {
+      const int64_t g = item / chunks, c = item % chunks;
       const int64_t ng = counts[g] < slots ? counts[g] : slots;
-      for (int64_t j = 0; j < ng; ++j) {
+      const int64_t jend = (c + 1) * 256 < ng ? (c + 1) * 256 : ng;
+      for (int64_t j = c * 256; j < jend; ++j) {
         const int64_t f = g * slots + j;
         const int16_t* ir = idx + f * 8;
         const float* wr = w + f * 8;
