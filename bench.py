@@ -50,6 +50,10 @@ IDX_BYTES = 2
 METRIC = "neuron-samples/s fwd+bwd+opt @100M fan-in-8, B=1024; % HBM roofline; 1/2/4/8 GPU"
 UNIT = "neuron-samples/s"
 FALLBACK_HBM_GBS = 6650.0
+# DRAM bytes (read + write) per neuron per backward launch at B = 1024, from the ncu
+# capture in profiles/bwd_kernel_fixed_g512.md (1.79 GB for 512 x 24,576 neurons); the
+# traffic grows with the neuron count, so a full launch is this figure times N.
+BWD_DRAM_BYTES_PER_NEURON = 1.788315e9 / (512 * 24576)
 
 
 def param_bytes(n):
@@ -342,7 +346,7 @@ def main():
         bwd_bytes = param_bytes(n_local) + gather_bytes(B, n_local)
         achieved = bwd_bytes / (bwd_ms * 1e-3) / 1e9
         step_bytes = 2 * param_bytes(N) + 2 * gather_bytes(B, N)
-        traffic = os.environ.get("GL_BWD_DRAM_BYTES")
+        traffic = BWD_DRAM_BYTES_PER_NEURON * n_local if B == 1024 else None
         line = {
             "metric": METRIC, "value": B * N / (ms / 1e3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
@@ -350,7 +354,8 @@ def main():
             "hbm_roofline_step_frac": (step_bytes / (peak * 1e9)) / (ms / 1e3),
             "roofline": {"bound": "hbm", "kernel": "gl_bwd_f32 (bwd_kernel<4,relu>)", "achieved": achieved,
                          "peak": peak, "unit": "GB/s", "frac": achieved / peak, "peak_source": peak_kind,
-                         "traffic": float(traffic) if traffic else None,
+                         "traffic": traffic, "traffic_source": "ncu dram bytes of a 512-group capture, "
+                                                              "scaled by neuron count (profiles/bwd_kernel_fixed_g512.md)",
                          "algorithmic_bytes_per_launch": bwd_bytes,
                          "definition": "(param + x-gather bytes) per launch / CUDA-event launch time; "
                                        "gathers count as logical HBM bytes per the baseline definition"},
