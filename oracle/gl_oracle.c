@@ -72,16 +72,28 @@ int glo_fwd(const float* x, int64_t B, int64_t D, int64_t ldx, const int16_t* id
   return 0;
 }
 
-/* Overwrites dx [B, D], dw [G*NB*8*8], db [G*NB*8] (padding slots get 0). */
+/* Overwrites dx [B, D], dw [G*NB*8*8], db [G*NB*8] (padding slots get 0).
+ *
+ * Optional slack outputs (NULL = skip), same shapes as dx/dw/db: ReLU's derivative
+ * jumps at z = 0, and an fp32 evaluation of z can take either side when
+ * |z| <= 1e-6 * (|b| + sum_k |w_k x_k|) (twice the worst-case error, 8 * 2^-24 of the
+ * term magnitudes, of an fp32 fused multiply-add chain).  For
+ * such (token, neuron) pairs the slack arrays receive the magnitude of that pair's
+ * contribution (|c1| |w_k| to dx, |c1| |x_k| to dw, |c1| to db), so a checker can
+ * accept either side of the jump and nothing else. */
 int glo_bwd(const float* x, int64_t B, int64_t D, int64_t ldx, const int16_t* idx, const float* w, const float* b,
             const int32_t* counts, int64_t G, int64_t NB, int pool, int act, const double* gpre, double* dx,
-            double* dw, double* db, int nthreads) {
+            double* dw, double* db, int nthreads, double* sdx, double* sdw, double* sdb) {
   if (check(B, D, G, NB)) return -2;
   const int64_t slots = NB * 8;
   int nt = nthreads > 0 ? nthreads : 1;
   memset(dw, 0, sizeof(double) * G * slots * 8);
   memset(db, 0, sizeof(double) * G * slots);
-  double* priv = (double*)calloc((size_t)nt * B * D, sizeof(double));
+  const int slack = sdx != NULL && act == 1;
+  if (sdx) memset(sdx, 0, sizeof(double) * B * D);
+  if (sdw) memset(sdw, 0, sizeof(double) * G * slots * 8);
+  if (sdb) memset(sdb, 0, sizeof(double) * G * slots);
+  double* priv = (double*)calloc((size_t)nt * B * D * (slack ? 2 : 1), sizeof(double));
   if (!priv) return -8;
 #pragma omp parallel num_threads(nt)
   {
@@ -90,6 +102,7 @@ int glo_bwd(const float* x, int64_t B, int64_t D, int64_t ldx, const int16_t* id
     me = omp_get_thread_num();
 #endif
     double* mydx = priv + (size_t)me * B * D;
+    double* mysdx = slack ? priv + (size_t)(nt + me) * B * D : NULL;
     /* work items: (group, chunk of 256 slots); each owns its slots' dw/db */
     const int64_t chunks = (slots + 255) / 256;
 #pragma omp for schedule(dynamic, 1)
@@ -102,26 +115,49 @@ int glo_bwd(const float* x, int64_t B, int64_t D, int64_t ldx, const int16_t* id
         const int16_t* ir = idx + f * 8;
         const float* wr = w + f * 8;
         double dwl[8] = {0, 0, 0, 0, 0, 0, 0, 0}, dbl = 0;
+        double swl[8] = {0, 0, 0, 0, 0, 0, 0, 0}, sbl = 0;
         for (int64_t t = 0; t < B; ++t) {
           const float* xr = x + t * ldx;
           double c1 = gpre[t * G + g];
           if (pool == 0) c1 /= (double)ng;
-          const double dz = c1 * dact_d(zval(xr, ir, wr, b[f]), act);
+          const double z = zval(xr, ir, wr, b[f]);
+          const double dz = c1 * dact_d(z, act);
           dbl += dz;
           for (int k = 0; k < 8; ++k) {
             dwl[k] += dz * (double)xr[ir[k]];
             mydx[t * D + ir[k]] += dz * (double)wr[k];
           }
+          if (slack) {
+            double mag = fabs((double)b[f]);
+            for (int k = 0; k < 8; ++k) mag += fabs((double)wr[k] * (double)xr[ir[k]]);
+            if (fabs(z) <= 1e-6 * mag) {
+              const double a1 = fabs(c1);
+              sbl += a1;
+              for (int k = 0; k < 8; ++k) {
+                swl[k] += a1 * fabs((double)xr[ir[k]]);
+                mysdx[t * D + ir[k]] += a1 * fabs((double)wr[k]);
+              }
+            }
+          }
         }
         for (int k = 0; k < 8; ++k) dw[f * 8 + k] = dwl[k];
         db[f] = dbl;
+        if (slack) {
+          if (sdw)
+            for (int k = 0; k < 8; ++k) sdw[f * 8 + k] = swl[k];
+          if (sdb) sdb[f] = sbl;
+        }
       }
     }
   }
   for (int64_t e = 0; e < B * D; ++e) {
-    double s = 0;
+    double s = 0, sl = 0;
     for (int i = 0; i < nt; ++i) s += priv[(size_t)i * B * D + e];
     dx[e] = s;
+    if (slack) {
+      for (int i = 0; i < nt; ++i) sl += priv[(size_t)(nt + i) * B * D + e];
+      sdx[e] = sl;
+    }
   }
   free(priv);
   return 0;

@@ -35,7 +35,8 @@ def load():
             build()
         lib = ctypes.CDLL(str(LIB))
         lib.glo_fwd.argtypes = [_p, _i64, _i64, _i64, _p, _p, _p, _p, _i64, _i64, _int, _int, _p, _int]
-        lib.glo_bwd.argtypes = [_p, _i64, _i64, _i64, _p, _p, _p, _p, _i64, _i64, _int, _int, _p, _p, _p, _p, _int]
+        lib.glo_bwd.argtypes = [_p, _i64, _i64, _i64, _p, _p, _p, _p, _i64, _i64, _int, _int, _p, _p, _p, _p, _int,
+                                _p, _p, _p]
         lib.glo_adam.argtypes = [_p, _p, _p, _p, _i64, _dbl, _dbl, _dbl, _dbl, _dbl, _i64]
         for f in (lib.glo_fwd, lib.glo_bwd, lib.glo_adam):
             f.restype = _int
@@ -73,8 +74,13 @@ def forward(x, idx, w, b, counts, pool="mean", act="relu", nthreads=0):
     return pre
 
 
-def backward(x, idx, w, b, counts, gpre, pool="mean", act="relu", nthreads=0):
-    """(dx [B, D], dw like w, db like b), float64, for upstream dL/dpre ``gpre`` [B, G]."""
+def backward(x, idx, w, b, counts, gpre, pool="mean", act="relu", nthreads=0, slack=False):
+    """(dx [B, D], dw like w, db like b), float64, for upstream dL/dpre ``gpre`` [B, G].
+
+    With ``slack=True`` also returns (sdx, sdw, sdb): per element, the magnitude of
+    the contributions of (token, neuron) pairs whose ReLU argument is within
+    rounding of 0, where an fp32 kernel may legitimately take the other side of
+    the derivative's jump (zero for identity/GELU)."""
     lib = load()
     x = _c(x, np.float32)
     idx = _c(idx, np.int16)
@@ -87,12 +93,17 @@ def backward(x, idx, w, b, counts, gpre, pool="mean", act="relu", nthreads=0):
     dx = np.zeros((B, D), np.float64)
     dw = np.zeros(w.shape, np.float64)
     db = np.zeros(b.shape, np.float64)
+    sl = [np.zeros_like(a) for a in (dx, dw, db)] if slack else [None, None, None]
+    ptr = [a.ctypes.data if a is not None else None for a in sl]
+    nt = _threads(nthreads)
+    if slack:  # the slack pass keeps a second private dx copy per thread
+        nt = max(1, min(nt, int(2e9 // max(1, B * D * 16))))
     rc = lib.glo_bwd(x.ctypes.data, B, D, D, idx.ctypes.data, w.ctypes.data, b.ctypes.data, counts.ctypes.data,
                      G, NB, POOL[pool], ACT[act], gpre.ctypes.data, dx.ctypes.data, dw.ctypes.data, db.ctypes.data,
-                     _threads(nthreads))
+                     nt, *ptr)
     if rc:
         raise RuntimeError(f"glo_bwd failed {rc}")
-    return dx, dw, db
+    return (dx, dw, db, *sl) if slack else (dx, dw, db)
 
 
 def adam_step(p, g, m, v, lr, beta1, beta2, eps, weight_decay, step):

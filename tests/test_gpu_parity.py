@@ -50,15 +50,16 @@ def test_matches_reference_golden(name, accum):
     y, dx, dw, db = _run(lay, arr["x"], arr["dy"])
     assert lay.last_info["dx_accumulation"] == ("int32 fixed point" if accum == "fixed" else "fp32 atomics")
     gs = arr["dw"].shape[0]
-    assert_close(y, arr["y"], what="y", **FWD)
-    assert_close(dx, arr["dx"], what="dx", **BWD)
-    assert_close(dw[:gs], arr["dw"], what="dw", **BWD)
-    assert_close(db[:gs], arr["db"], what="db", **BWD)
-    # all groups against the oracle
     c = L.counts_tensor("cpu").numpy()
-    _, odw, odb = O.backward(arr["x"], idx.numpy(), w.numpy(), b.numpy(), c, arr["dy"], meta["pool"], meta["act"])
-    assert_close(dw, odw, what="dw(all groups)", **BWD)
-    assert_close(db, odb, what="db(all groups)", **BWD)
+    _, odw, odb, sdx, sdw, sdb = O.backward(arr["x"], idx.numpy(), w.numpy(), b.numpy(), c, arr["dy"],
+                                            meta["pool"], meta["act"], slack=True)
+    assert_close(y, arr["y"], what="y", **FWD)
+    assert_close(dx, arr["dx"], what="dx", slack=sdx, **BWD)
+    assert_close(dw[:gs], arr["dw"], what="dw", slack=sdw[:gs], **BWD)
+    assert_close(db[:gs], arr["db"], what="db", slack=sdb[:gs], **BWD)
+    # all groups against the oracle
+    assert_close(dw, odw, what="dw(all groups)", slack=sdw, **BWD)
+    assert_close(db, odb, what="db(all groups)", slack=sdb, **BWD)
 
 
 @pytest.mark.parametrize("accum", ["fixed", "fp32"])
@@ -69,9 +70,11 @@ def test_token_tiles(tf, tb, accum):
     L, idx, w, b = case_params(meta, arr)
     lay = _layer_for(meta, idx, w, b, plan=PhysicalPlan(b200_fwd_tokens=tf, b200_dx_tokens=tb, b200_dx_accum=accum))
     y, dx, dw, db = _run(lay, arr["x"], arr["dy"])
+    _, _, _, sdx, sdw, _ = O.backward(arr["x"], idx.numpy(), w.numpy(), b.numpy(), L.counts_tensor("cpu").numpy(),
+                                      arr["dy"], slack=True)
     assert_close(y, arr["y"], what="y", **FWD)
-    assert_close(dx, arr["dx"], what="dx", **BWD)
-    assert_close(dw[:16], arr["dw"], what="dw", **BWD)
+    assert_close(dx, arr["dx"], what="dx", slack=sdx, **BWD)
+    assert_close(dw[:16], arr["dw"], what="dw", slack=sdw[:16], **BWD)
 
 
 def _rand_layer(D, H, G, seed=0, bias_std=0.2, device="cuda"):
@@ -196,11 +199,12 @@ def test_wide_and_narrow_inputs_against_oracle(D):
                              bias_std=0.2).cuda()
     y, dx, dw, db = _run(lay, x.numpy(), dy.numpy())
     pre = O.forward(x.numpy(), idx.cpu().numpy(), w.cpu().numpy(), b.cpu().numpy(), counts)
-    odx, odw, odb = O.backward(x.numpy(), idx.cpu().numpy(), w.cpu().numpy(), b.cpu().numpy(), counts, dy.numpy())
+    odx, odw, odb, sdx, sdw, sdb = O.backward(x.numpy(), idx.cpu().numpy(), w.cpu().numpy(), b.cpu().numpy(),
+                                              counts, dy.numpy(), slack=True)
     assert_close(y, pre, what="y", **FWD)
-    assert_close(dx, odx, what="dx", **BWD)
-    assert_close(dw, odw, what="dw", **BWD)
-    assert_close(db, odb, what="db", **BWD)
+    assert_close(dx, odx, what="dx", slack=sdx, **BWD)
+    assert_close(dw, odw, what="dw", slack=sdw, **BWD)
+    assert_close(db, odb, what="db", slack=sdb, **BWD)
 
 
 def test_no_hidden_activation_is_materialized():
@@ -253,4 +257,6 @@ def test_nonfinite_upstream_gradient_reaches_dx(accum, bad):
     y, dx, dw, db = _run(lay, arr["x"], dy)
     assert not bool(torch.isfinite(dx[3]).all()), "token 3 must see the non-finite coefficient"
     keep = [t for t in range(dx.shape[0]) if t != 3]
-    assert_close(dx[keep], arr["dx"][keep], what="dx(other tokens)", **BWD)
+    sdx = O.backward(arr["x"], idx.numpy(), w.numpy(), b.numpy(), L.counts_tensor("cpu").numpy(), arr["dy"],
+                     slack=True)[3]
+    assert_close(dx[keep], arr["dx"][keep], what="dx(other tokens)", slack=sdx[keep], **BWD)
