@@ -18,6 +18,9 @@ What it writes (all from the reference's own code on the CPU):
   ``hidden_preactivations`` + activation + masked sum (the reference has no
   sum operator).  One case draws indices uniformly with replacement
   (duplicate indices inside a neuron).
+* ``graph_hashes.json`` — sha256 of the reference's input-supergroup graphs: Mode-B
+  ``supergroups.generate_indices`` (indices, feature sets, buckets) and the generalized
+  ``experimental/kgen_graph.generate`` (K = 64 / C = 256 envelope, K = 16 / C = 16).
 * ``adam.npz`` — five steps of ``torch.optim.AdamW``/``Adam`` in float64, the
   recurrence the reference's optimizer test compares its fused kernel with
   (tests/test_optim.py:11-28; optim.py:39-42).
@@ -46,6 +49,20 @@ CASES = [
     ("gelu_mean", 64, 3000, 8, 16, 4, 0.2, "mean", "gelu", "distinct"),
     ("sum_identity_ragged", 96, 1001, 7, 5, 5, 0.1, "sum", "identity", "distinct"),
     ("uniform_dup_idx", 32, 2048, 8, 24, 6, 0.1, "mean", "relu", "uniform"),
+]
+
+# (D, H, G, C, S, R, generation, seed): Mode-B input-supergroup graphs
+GRAPH_CASES = [
+    (256, 40000, 16, 8, 64, 2, "balanced_permutation", 0),
+    (256, 40000, 16, 64, 32, 3, "balanced_permutation", 7),
+    (128, 7777, 5, 16, 16, 1, "independent_subsets", 3),
+    (512, 100000, 64, 32, 128, 4, "balanced_permutation", 11),
+]
+# (D, H, G, C, K, S, R, seed): generalized graphs (quantum 1), incl. the K64/C256 Cover-TopK16 envelope
+KGEN_CASES = [
+    (256, 3452, 8, 256, 64, 64, 16, 0),
+    (1024, 65536, 64, 256, 64, 64, 8, 5),
+    (256, 20000, 16, 16, 16, 64, 4, 2),
 ]
 
 INIT_CASES = [
@@ -123,6 +140,31 @@ def main():
             idx=idx.numpy() if rule == "uniform" else np.zeros(0, np.int16),
             x=x.numpy(), dy=dy.numpy(), y=y.detach().float().numpy(), dx=xd.grad.float().numpy(),
             dw=wd.grad[:GSUB].float().numpy(), db=bd.grad[:GSUB].float().numpy())
+
+    # input-supergroup graphs (supergroups.py generate_indices; kgen_graph.py generate)
+    from sparse_pooling.experimental import kgen_graph as KG
+    from sparse_pooling.supergroups import ConnectivityPlan, generate_indices
+
+    graphs = []
+    for D, H, G, C, S, R, gen, seed in GRAPH_CASES:
+        L = SparseLayout(D, H, G, 8, C, True)
+        plan = ConnectivityPlan(S, R, gen, seed)
+        idx, graph, _ = generate_indices(L, plan, "cpu")
+        graphs.append(dict(kind="mode_b", layout=[D, H, G, 8, C, True], plan=json.loads(plan.to_json()),
+                           idx=sha(idx), feat=sha(graph.feat), buckets=sha(graph.buckets),
+                           shapes=[list(idx.shape), list(graph.feat.shape), list(graph.buckets.shape)]))
+    for D, H, G, C, K, S, R, seed in KGEN_CASES:
+        from sparse_pooling.experimental.kgen_layout import KLayout
+
+        KL = KLayout(D, H, G, K, C)
+        plan = ConnectivityPlan(S, R, "balanced_permutation", seed)
+        counts = KL.counts_tensor("cpu")
+        idx, feat, ubk, _ = KG.generate(D, counts, C, K, KL.blocks_per_group, 1, plan, "cpu")
+        bk = KG.unit_to_block_buckets(ubk, counts, C, 1)
+        graphs.append(dict(kind="kgen", layout=[D, H, G, K, C], plan=json.loads(plan.to_json()), idx=sha(idx),
+                           feat=sha(feat), buckets=sha(ubk), block_buckets=sha(bk),
+                           shapes=[list(idx.shape), list(feat.shape), list(ubk.shape), list(bk.shape)]))
+    (HERE / "graph_hashes.json").write_text(json.dumps(graphs, indent=1))
 
     torch.manual_seed(0)
     out = {}
