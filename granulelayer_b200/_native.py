@@ -16,7 +16,7 @@ from pathlib import Path
 
 import torch
 
-ABI_VERSION = 2
+ABI_VERSION = 3
 LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libgranule_b200.so"
 
 POOL_MEAN, POOL_SUM = 0, 1
@@ -25,7 +25,7 @@ ACT_IDS = {"identity": 0, "relu": 1, "gelu": 2}
 # The exported entry points, in header order (checked by the CPU test suite).
 EXPORTS = ("gl_abi_version", "gl_status_string", "gl_last_cuda_error", "gl_fwd_f32", "gl_bwd_f32",
            "gl_adam_f32", "gl_group_absmax_f32", "gl_group_index_maxcount", "gl_launch_count",
-           "gl_fwd_auto_tokens", "gl_bwd_auto_tokens")
+           "gl_fwd_auto_tokens", "gl_bwd_auto_tokens", "gl_k16_fwd_f32", "gl_k16_bwd_f32", "gl_k16_auto_tokens")
 
 
 class NativeLibraryError(RuntimeError):
@@ -60,6 +60,14 @@ class GlAdamArgs(ctypes.Structure):
                 ("bc2", ctypes.c_float), ("zero_grad", ctypes.c_int32)]
 
 
+class GlK16Args(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_void_p) for n in ("x", "env", "feat", "buckets", "q_off", "rec_off", "w", "b", "counts",
+                                                "pre", "c1t", "dx", "dw", "db")] + \
+               [(n, ctypes.c_int64) for n in ("B", "D", "G", "NB16", "Q", "S", "nbuckets", "ldx", "ldp",
+                                                 "ldc", "lddx")] + \
+               [("act", ctypes.c_int32), ("tokens", ctypes.c_int32)]
+
+
 _lock = threading.Lock()
 _lib = None
 
@@ -85,7 +93,8 @@ def load(path=None) -> ctypes.CDLL:
         lib.gl_status_string.argtypes = [ctypes.c_int]
         lib.gl_last_cuda_error.restype = ctypes.c_int
         lib.gl_launch_count.restype = ctypes.c_int64
-        for name, st in (("gl_fwd_f32", GlFwdArgs), ("gl_bwd_f32", GlBwdArgs), ("gl_adam_f32", GlAdamArgs)):
+        for name, st in (("gl_fwd_f32", GlFwdArgs), ("gl_bwd_f32", GlBwdArgs), ("gl_adam_f32", GlAdamArgs),
+                         ("gl_k16_fwd_f32", GlK16Args), ("gl_k16_bwd_f32", GlK16Args)):
             fn = getattr(lib, name)
             fn.restype = ctypes.c_int
             fn.argtypes = [ctypes.POINTER(st), ctypes.c_void_p]
@@ -98,6 +107,8 @@ def load(path=None) -> ctypes.CDLL:
         for name in ("gl_fwd_auto_tokens", "gl_bwd_auto_tokens"):
             getattr(lib, name).restype = ctypes.c_int
             getattr(lib, name).argtypes = [ctypes.c_int64]
+        lib.gl_k16_auto_tokens.restype = ctypes.c_int
+        lib.gl_k16_auto_tokens.argtypes = [ctypes.c_int64, ctypes.c_int64, ctypes.c_int32]
         if path is None:
             _lib = lib
         return lib
@@ -180,3 +191,37 @@ def adam(p, g, m, v, lr, beta1, beta2, eps, weight_decay, bc1, bc2, zero_grad=Tr
                    int(bool(zero_grad)))
     with torch.cuda.device(p.device):
         _check(lib, lib.gl_adam_f32(ctypes.byref(a), _stream(p.device)), "gl_adam_f32")
+
+
+def _k16_args(x, sched, w, b, counts, NB16: int, act: int, tokens: int):
+    feat = sched["feat"]
+    return GlK16Args(_ptr(x), _ptr(sched["env"]), _ptr(feat), _ptr(sched["buckets"]), _ptr(sched["q_off"]),
+                     _ptr(sched["rec_off"]), _ptr(w), _ptr(b), _ptr(counts), 0, 0, 0, 0, 0,
+                     x.shape[0], x.shape[1], counts.shape[0], NB16, feat.shape[0], feat.shape[1],
+                     sched["buckets"].shape[0], x.stride(0), 0, 0, 0, act, tokens)
+
+
+def k16_fwd(x, sched: dict, w, b, counts, pre, NB16: int, act: int = 1, tokens: int = 0):
+    """pre[t, g] += Mean-pooled act(z) of the K16/C16 layer (GlK16Args); ``sched`` holds env, feat,
+    buckets (sorted by set), q_off and rec_off."""
+    _require_cuda(x, w, b, counts, pre, *sched.values())
+    lib = load()
+    a = _k16_args(x, sched, w, b, counts, NB16, act, tokens)
+    a.pre, a.ldp = _ptr(pre), pre.stride(0)
+    with torch.cuda.device(x.device):
+        _check(lib, lib.gl_k16_fwd_f32(ctypes.byref(a), _stream(x.device)), "gl_k16_fwd_f32")
+
+
+def k16_bwd(x, sched: dict, w, b, counts, c1t, dx, dw, db, NB16: int, act: int = 1, tokens: int = 0):
+    """dx, dw, db += the K16/C16 layer's gradients for coefficients c1t [G, B] (GlK16Args)."""
+    _require_cuda(x, w, b, counts, c1t, dx, dw, db, *sched.values())
+    lib = load()
+    a = _k16_args(x, sched, w, b, counts, NB16, act, tokens)
+    a.c1t, a.dx, a.dw, a.db = _ptr(c1t), _ptr(dx), _ptr(dw), _ptr(db)
+    a.ldc, a.lddx = c1t.stride(0), dx.stride(0)
+    with torch.cuda.device(x.device):
+        _check(lib, lib.gl_k16_bwd_f32(ctypes.byref(a), _stream(x.device)), "gl_k16_bwd_f32")
+
+
+def k16_auto_tokens(B: int, S: int, backward: bool) -> int:
+    return int(load().gl_k16_auto_tokens(B, S, int(bool(backward))))

@@ -44,7 +44,7 @@
 extern "C" {
 #endif
 
-#define GL_ABI_VERSION 2
+#define GL_ABI_VERSION 3
 
 typedef enum GlStatus {
   GL_OK = 0,
@@ -151,6 +151,49 @@ int gl_group_absmax_f32(const float* w, const int32_t* counts, int64_t NB, int64
                         void* stream);
 int gl_group_index_maxcount(const int16_t* idx, const int32_t* counts, int64_t D, int64_t NB, int64_t g0,
                             int64_t g1, int32_t* out, void* stream);
+
+/* Compact K16/C16 execution of the Cover-TopK/16 layer, fp32.
+ * Replaces the reference's kgen entry points at K = 16 (experimental/kgen/kgen_abi.cu,
+ * kernels kgen.cuh:142-536), called by KgenFunction (experimental/kgen_layer.py:61-143) with
+ * the layer's lowered storage (experimental/kgen_lowered.py:147-201):
+ *   w [G, NB16, 16, 16] f32, b [G, NB16, 16] f32, record f = g*NB16 + j; neuron slot 16 j + n
+ *   of output g is valid iff it is < counts[g];
+ *   feat [Q, S] int16: the input features of set q;
+ *   env [G*NB16, 16] uint8: record f reads x[:, feat[q][env[f, k]]], q = its bucket's set;
+ *   buckets [nb, 4] int32 (q, g, first record j, records), sorted by q; q_off [Q+1] int32: the
+ *   bucket range of set q; rec_off [nb+1] int32: exclusive prefix sum of buckets[:, 3].
+ * Forward:  pre[t, g] += sum_{valid (f, n) of g} act(z[t, f, n]) / counts[g]
+ *           (accumulated: zero `pre` first), z = b[f, n] + sum_k w[f, n, k] x[t, idx(f, k)].
+ * Backward: with c1t[g, t] = dL/dpre[t, g] / counts[g] (the reference's c1T) and
+ *           dz = c1t * act'(z) on valid slots: dx[t, idx(f, k)] += sum_n dz w[f, n, k],
+ *           dw[f, n, k] += sum_t dz x[t, idx(f, k)], db[f, n] += sum_t dz (all accumulated).
+ * Activations: GL_ACT_RELU (the layer's Mean(ReLU)) or GL_ACT_IDENTITY. */
+typedef struct GlK16Args {
+  const float* x;           /* [B, ldx] */
+  const uint8_t* env;       /* [G*NB16, 16], 16-byte aligned */
+  const int16_t* feat;      /* [Q, S] */
+  const int32_t* buckets;   /* [nb, 4], 16-byte aligned */
+  const int32_t* q_off;     /* [Q+1] */
+  const int32_t* rec_off;   /* [nb+1] */
+  const float* w;
+  const float* b;
+  const int32_t* counts;    /* [G] */
+  float* pre;               /* forward: [B, ldp], accumulated */
+  const float* c1t;         /* backward: [G, ldc] */
+  float* dx;                /* backward: [B, lddx], accumulated */
+  float* dw;                /* backward: weight-shaped, accumulated */
+  float* db;                /* backward: bias-shaped, accumulated */
+  int64_t B, D, G, NB16, Q, S;
+  int64_t nbuckets;         /* rows of `buckets` (q_off values are clamped to it) */
+  int64_t ldx, ldp, ldc, lddx;
+  int32_t act;              /* GL_ACT_RELU or GL_ACT_IDENTITY */
+  int32_t tokens;           /* token chunk per block (0 = automatic; else a multiple of 16) */
+} GlK16Args;
+
+int gl_k16_fwd_f32(const GlK16Args* args, void* stream);
+int gl_k16_bwd_f32(const GlK16Args* args, void* stream);
+/* Token chunk the automatic choice would use (backward != 0: the backward's), or a negative status. */
+int gl_k16_auto_tokens(int64_t B, int64_t S, int32_t backward);
 
 /* Number of kernels this library has launched successfully in this process
    (all devices).  Benchmarks difference it around a timed region. */

@@ -21,6 +21,10 @@ What it writes (all from the reference's own code on the CPU):
 * ``graph_hashes.json`` — sha256 of the reference's input-supergroup graphs: Mode-B
   ``supergroups.generate_indices`` (indices, feature sets, buckets) and the generalized
   ``experimental/kgen_graph.generate`` (K = 64 / C = 256 envelope, K = 16 / C = 16).
+* ``kc_reference.npz`` — a small Cover-TopK/16 layer built by the reference
+  (``CoverTopK16Layer.from_envelope``, cover_topk16.py:80-146) with its lowered storage and
+  schedule buffers, an input, an upstream gradient, and the reference's float64 K/C model
+  ``experimental/reference.grads`` (reference.py:21-27) evaluated on it: y, dx, dw, db.
 * ``adam.npz`` — five steps of ``torch.optim.AdamW``/``Adam`` in float64, the
   recurrence the reference's optimizer test compares its fused kernel with
   (tests/test_optim.py:11-28; optim.py:39-42).
@@ -165,6 +169,27 @@ def main():
                            feat=sha(feat), buckets=sha(ubk), block_buckets=sha(bk),
                            shapes=[list(idx.shape), list(feat.shape), list(ubk.shape), list(bk.shape)]))
     (HERE / "graph_hashes.json").write_text(json.dumps(graphs, indent=1))
+
+    from sparse_pooling.cover_topk16 import CoverTopK16Layer
+    from sparse_pooling.experimental import reference as KREF
+    from sparse_pooling.experimental.kgen_layout import KLayout, init_parameters as init_envelope_parameters
+
+    D, H, G, R = 256, 3452, 8, 16
+    EL = KLayout(D, H, G, 64, 256)
+    w64, b64 = init_envelope_parameters(EL, "cpu", dtype=torch.bfloat16, seed=1, bias_std=0.1)
+    lay = CoverTopK16Layer.from_envelope(w64, b64, input_dim=D, hidden_dim=H, output_dim=G,
+                                         connectivity=ConnectivityPlan(64, R, seed=4), device="cpu")
+    gen = torch.Generator().manual_seed(11)
+    x = torch.randn(37, D, generator=gen)
+    gy = torch.randn(37, G, generator=gen)
+    counts = KLayout(D, H, G, 16, 16).counts_tensor("cpu")
+    y, dx, dw, db = KREF.grads(x.double(), lay.indices.long(), lay.weight.detach().float().double(), lay.bias.detach().float().double(),
+                               counts, gy.double())
+    np.savez_compressed(HERE / "kc_reference.npz", meta=json.dumps(dict(D=D, H=H, G=G, R=R, seed=1, graph_seed=4)),
+                        x=x.numpy(), gy=gy.numpy(), indices=lay.indices.numpy(), weight=lay.weight.detach().float().numpy(),
+                        bias=lay.bias.detach().float().numpy(), counts=counts.numpy(), sg_feat=lay.sg_feat.numpy(),
+                        kg_buckets=lay.kg_buckets.numpy(), env=lay.env.numpy(), y=y.numpy(), dx=dx.numpy(),
+                        dw=dw.numpy(), db=db.numpy())
 
     torch.manual_seed(0)
     out = {}

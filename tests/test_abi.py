@@ -56,6 +56,16 @@ def test_argument_validation_needs_no_device():
     assert lib.gl_adam_f32(ctypes.byref(ad), None) == -2
     ad.n = 0
     assert lib.gl_adam_f32(ctypes.byref(ad), None) == 0
+    assert lib.gl_k16_fwd_f32(None, None) == -1
+    assert lib.gl_k16_bwd_f32(None, None) == -1
+    k = _native.GlK16Args()
+    k.B, k.D, k.G, k.NB16, k.Q, k.S = 4, 64, 2, 3, 1, 300   # S beyond uint8 local positions
+    assert lib.gl_k16_fwd_f32(ctypes.byref(k), None) == -2
+    k.S = 64
+    assert lib.gl_k16_fwd_f32(ctypes.byref(k), None) == -1  # null pointers
+    k.B = 0                                                  # empty batch: a no-op
+    assert lib.gl_k16_bwd_f32(ctypes.byref(k), None) == 0
+    assert lib.gl_k16_auto_tokens(0, 64, 0) == -2
 
 
 def test_struct_layout_matches_header():
@@ -63,6 +73,7 @@ def test_struct_layout_matches_header():
     assert ctypes.sizeof(_native.GlFwdArgs) == 6 * 8 + 7 * 8 + 4 * 4 + 8
     assert ctypes.sizeof(_native.GlBwdArgs) == 9 * 8 + 8 * 8 + 4 * 4 + 2 * 8
     assert ctypes.sizeof(_native.GlAdamArgs) == 4 * 8 + 8 + 8 * 4
+    assert ctypes.sizeof(_native.GlK16Args) == 14 * 8 + 11 * 8 + 2 * 4
 
 
 def test_missing_library_fails_loudly(tmp_path):
