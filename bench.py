@@ -22,6 +22,11 @@ every step).  ``roofline`` is for the dominant kernel (the backward), timed
 with CUDA events on its launch stream.  ``cpu_baseline`` times the C oracle on
 a bounded slice of the same workload on the host cores (rank 0, N = 1).
 
+``--workload cover16`` times instead BASELINE config 4, the Cover-TopK/16 opt-in layer
+(N = 50,331,648 neurons selected from a K64 envelope with w64 ~ N(0, 1/64) in BF16, D = 4096,
+G = 2048 outputs, S = 64, R = 64, batch 512, seed 3): forward + backward through the layer on
+1 GPU, with the forward and backward (dX-carrying) kernels timed separately.
+
 ``--impl reference`` times the reference's CPU path (the oracle port: the
 reference's materialising PyTorch path does not fit 100M neurons) on the same
 config, rank 0 only.
@@ -215,6 +220,153 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+COVER_METRIC = "neuron-samples/s fwd+bwd, Cover-TopK16 K16/C16 layer (N=50,331,648, D=4096, G=2048, B=512)"
+FP32_FLOP_PER_SM_CLK = 128 * 2     # 128 fp32 FMA lanes per SM
+
+
+def cover16_cpu_baseline(lay, x, dy, target_s=8.0):
+    """The float64 K/C oracle (numpy) on a bounded slice: the first outputs of the layer, full batch."""
+    from oracle import kc_oracle
+
+    idx = lay.indices.cpu().numpy()
+    w = lay.weight.detach().cpu().numpy()
+    b = lay.bias.detach().cpu().numpy()
+    counts = lay.counts.cpu().numpy()
+    xs, dys = x.cpu().numpy(), dy.cpu().numpy()
+    Bs = 64
+    t0 = time.perf_counter()
+    kc_oracle.grads(xs[:Bs], idx[:1], w[:1], b[:1], counts[:1], dys[:Bs, :1])
+    t1 = max(time.perf_counter() - t0, 1e-3)
+    ng = int(max(1, min(lay.layout.groups, target_s / t1)))
+    t0 = time.perf_counter()
+    kc_oracle.grads(xs[:Bs], idx[:ng], w[:ng], b[:ng], counts[:ng], dys[:Bs, :ng])
+    dt = time.perf_counter() - t0
+    return {"value": Bs * int(counts[:ng].sum()) / dt, "unit": UNIT, "cores": 1, "kind": "port",
+            "sample": f"{ng} outputs x {Bs} tokens (fwd+bwd, float64 numpy, BLAS threads as configured)"}
+
+
+def bench_cover16(args, world):
+    """BASELINE config 4 (module docstring); rank 0 only."""
+    from granulelayer_b200 import _native
+    from granulelayer_b200.cover_topk16 import CoverTopK16Layer
+    from granulelayer_b200.kgen import KLayout, init_envelope_parameters
+    from granulelayer_b200.supergroups import ConnectivityPlan
+
+    Dc, Gc, Bc = 4096, args.cover_outputs, 512
+    Hc = Gc * 24576
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    t0 = time.perf_counter()
+    w64, b64 = init_envelope_parameters(KLayout(Dc, Hc, Gc, 64, 256), dev, dtype=torch.bfloat16, seed=3)
+    lay = CoverTopK16Layer.from_envelope(w64, b64, input_dim=Dc, hidden_dim=Hc, output_dim=Gc,
+                                         connectivity=ConnectivityPlan(64, 64, seed=3), device=dev)
+    del w64, b64
+    torch.cuda.synchronize(dev)
+    torch.cuda.empty_cache()
+    build_s = time.perf_counter() - t0
+    gen = torch.Generator(device=dev).manual_seed(3)
+    x = torch.randn(Bc, Dc, device=dev, generator=gen)
+    dy = torch.randn(Bc, Gc, device=dev, generator=gen)
+
+    ev = {"fwd": [], "bwd": []}
+    orig = {"fwd": _native.k16_fwd, "bwd": _native.k16_bwd}
+
+    def timed(name):
+        def wrap(*a, **k):
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            orig[name](*a, **k)
+            e.record()
+            ev[name].append((s, e))
+        return wrap
+
+    def step():
+        xin = x.detach().requires_grad_(True)
+        lay.weight.grad = lay.bias.grad = None
+        lay(xin).backward(dy)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    _native.k16_fwd, _native.k16_bwd = timed("fwd"), timed("bwd")
+    n0 = _native.launch_count()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    try:
+        with ClockSampler(dev.index) as clk:
+            start.record()
+            for _ in range(args.steps):
+                step()
+            end.record()
+            torch.cuda.synchronize(dev)
+    finally:
+        _native.k16_fwd, _native.k16_bwd = orig["fwd"], orig["bwd"]
+    launches = _native.launch_count() - n0
+    ms = start.elapsed_time(end) / args.steps
+    fwd_ms = statistics.mean(s.elapsed_time(e) for s, e in ev["fwd"])
+    bwd_ms = statistics.mean(s.elapsed_time(e) for s, e in ev["bwd"])
+
+    e2e = None
+    if not args.no_e2e:
+        xh = torch.randn(Bc, Dc, generator=torch.Generator().manual_seed(7)).pin_memory()
+        dyh = torch.randn(Bc, Gc, generator=torch.Generator().manual_seed(8)).pin_memory()
+        yh = torch.empty(Bc, Gc).pin_memory()
+        xd, dyd = torch.empty(Bc, Dc, device=dev), torch.empty(Bc, Gc, device=dev)
+
+        def api_step():
+            xd.copy_(xh, non_blocking=True)
+            dyd.copy_(dyh, non_blocking=True)
+            xin = xd.detach().requires_grad_(True)
+            lay.weight.grad = lay.bias.grad = None
+            y = lay(xin)
+            y.backward(dyd)
+            yh.copy_(y.detach(), non_blocking=True)
+
+        for _ in range(2):
+            api_step()
+        torch.cuda.synchronize(dev)
+        s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s2.record()
+        for _ in range(args.steps):
+            api_step()
+        e2.record()
+        torch.cuda.synchronize(dev)
+        t2 = s2.elapsed_time(e2) / args.steps
+        e2e = {"value": Bc * Hc / (t2 / 1e3), "unit": UNIT, "ms_per_step": t2,
+               "h2d_bytes_per_step": (xh.numel() + dyh.numel()) * 4, "d2h_bytes_per_step": yh.numel() * 4}
+
+    cb = None if (args.no_cpu_baseline or world > 1) else cover16_cpu_baseline(lay, x, dy)
+    clocks = clk.summary()
+    mhz = clocks.get("sm_mhz") or clocks.get("sm_max_mhz") or 1965
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    peak_tflops = sms * FP32_FLOP_PER_SM_CLK * mhz * 1e6 / 1e12
+    bwd_flop = 2 * 48 * Hc * Bc     # per neuron and token: 16 FMA for z, 16 for dW, 16 for dX
+    fwd_flop = 2 * 16 * Hc * Bc
+    achieved = bwd_flop / (bwd_ms * 1e-3) / 1e12
+    hbm, hbm_kind = peak_hbm()
+    wbytes = Hc * (16 * 4 + 4) + (Hc // 16) * 16
+    line = {
+        "metric": COVER_METRIC, "value": Bc * Hc / (ms / 1e3), "unit": UNIT, "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "none",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "Cover-TopK16 opt-in layer, compact K16/C16 execution, fwd+bwd (BASELINE config 4)",
+                   "D": Dc, "N": Hc, "G": Gc, "global_batch": Bc, "envelope": "K64/C256, w64 ~ N(0,1/64) BF16",
+                   "S": 64, "R": 64, "Q": int(lay.sg_feat.shape[0]), "records_16": int(Hc // 16),
+                   "l2": f"weights {Hc * 64 / 1e9:.1f} GB fp32 > L2: streamed from HBM every pass",
+                   "build_seconds": build_s},
+        "roofline": {"bound": "fp32", "kernel": "gl_k16_bwd_f32 (k16_bwd_kernel<relu>)", "achieved": achieved,
+                     "peak": peak_tflops, "unit": "TFLOP/s", "frac": achieved / peak_tflops,
+                     "peak_source": f"nominal fp32 FMA rate: {sms} SMs x 128 lanes x 2 flop at the median "
+                                    f"sampled SM clock {mhz} MHz",
+                     "algorithmic_flop_per_launch": bwd_flop,
+                     "hbm_fraction_bwd": (2 * wbytes) / (bwd_ms * 1e-3) / (hbm * 1e9), "hbm_peak_source": hbm_kind,
+                     "traffic": None},
+        "kernels_ms": {"fwd": fwd_ms, "bwd": bwd_ms,
+                       "fwd_tflops": fwd_flop / (fwd_ms * 1e-3) / 1e12, "bwd_tflops": achieved},
+        "clocks": clocks, "gpu_launches": launches, "e2e": e2e, "cpu_baseline": cb,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     global N, G
     ap = argparse.ArgumentParser()
@@ -225,6 +377,9 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ref-seconds", type=float, default=4.0)
+    ap.add_argument("--workload", default="layer100m", choices=["layer100m", "cover16"])
+    ap.add_argument("--cover-outputs", type=int, default=2048,
+                    help="cover16: outputs of 24,576 neurons (default 2048 = config 4; fewer for ncu captures)")
     ap.add_argument("--groups", type=int, default=G,
                     help="pooling groups of 24,576 neurons (default 4096 = the full 100M layer; smaller values "
                          "give the reduced cases used for ncu captures)")
@@ -237,6 +392,10 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.workload == "cover16":
+        if rank == 0:
+            bench_cover16(args, world)
+        return
     if args.impl == "reference":
         run_reference(args, rank, world)
         return

@@ -18,26 +18,28 @@
 // each record's weights are loaded once per token chunk and kept in registers while the
 // warp sweeps all TT tokens.  With one chunk (B <= TT) the weights stream from HBM once.
 //
-// Forward lanes: lane = (neuron pair p = lane >> 2, token quarter = lane & 3); a warp step
-// covers one record and 16 tokens, the four quarters read adjacent float4s of the same
-// shared-memory row (one wavefront per load).  The 16 neurons' activations are summed with a
-// transpose-reduction (4 shuffles per 16 tokens) and added to a per-bucket token row in shared
-// memory; rows are flushed to pre with one global reduction per (bucket, token).
-//
-// Backward lanes: lane = (token half h = lane >> 4, neuron n = lane & 15); a warp step covers one
-// record and 8 tokens.  Each lane recomputes z for its neuron, forms dz, accumulates its 16 dW
-// and db in registers across the chunk, and publishes dz to a per-warp shared slab; lane n then
-// acts as input k = n of the record: dX[k][t] = sum_m dz[m][t] w[m][k] (the column w[:, k] is
-// held in registers) is added to the block's dX tile with shared-memory atomics.  The block
-// ends with global reductions of dW/db (per record) and of the dX tile into dx.
+// Both are FMA kernels fed from shared memory.  A shared-memory load delivers at most 32 floats
+// per wavefront whatever the broadcast pattern, against 128 FMAs per clock per SM, so every x
+// value a lane loads must feed several FMAs from registers: the forward keeps 8 neurons per lane
+// (32 FMAs per 128-bit load), the backward 4 neurons per lane (8 FMAs per loaded value for z
+// and dW, plus the dX products from the same registers).  Lane layouts are described at each
+// kernel.  The forward adds per-bucket token sums into a shared row and flushes them with one
+// global reduction per (bucket, token); the backward keeps dW/db in registers across the token
+// chunk, adds dX into a shared [S][TT] tile with conflict-free shared atomics, and ends with
+// global reductions of dW/db (per record) and of the tile into dx.
 #include "common.cuh"
 
 namespace gl {
 
-constexpr int kK16FwdThreads = 512;
+constexpr int kK16FwdThreads = 256;
 constexpr int kK16BwdThreads = 256;
-constexpr int kK16Pass = 64;       // buckets resolved per pass (rows of the per-bucket token tiles)
+constexpr int kK16FwdStep = 64;    // tokens per forward warp step (16 token groups x 4)
+constexpr int kK16BwdStep = 16;    // tokens per backward warp step (8 token groups x 2)
+constexpr int kK16FwdPass = 32;    // buckets per forward pass (rows of the shared token-sum tile)
+constexpr int kK16BwdPass = 64;    // buckets per backward pass (rows of the shared coefficient tile)
+constexpr int kK16MaxPass = 64;
 constexpr int kK16MaxS = 256;      // env holds uint8 local positions
+constexpr int kK16MaxTT = 512;
 
 struct K16Params {
   const float* x;
@@ -60,10 +62,30 @@ struct K16Params {
 
 // Bucket rows of one pass: record start (relative to the pass), output, first 16-block.
 struct K16PassInfo {
-  int rstart[kK16Pass + 1];
-  int g[kK16Pass];
-  int first[kK16Pass];
+  int rstart[kK16MaxPass + 1];
+  int g[kK16MaxPass];
+  int first[kK16MaxPass];
 };
+
+// One record staged in shared memory by its warp (weights [16][16], bias [16], local positions).
+struct __align__(16) K16Stage {
+  float w[256];
+  float b[16];
+  uint32_t env[4];
+};
+
+struct K16Rec {
+  int i, g, j16;
+  bool ok;
+};
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  const unsigned d = (unsigned)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 __device__ __forceinline__ void k16_load_pass(K16PassInfo& ps, const K16Params& p, int p0, int np) {
   const int base = __ldg(p.rec_off + p0);
@@ -77,19 +99,39 @@ __device__ __forceinline__ void k16_load_pass(K16PassInfo& ps, const K16Params& 
   }
 }
 
-// Bucket row of pass-relative record r: the largest i with rstart[i] <= r (empty buckets skipped).
-__device__ __forceinline__ int k16_find(const K16PassInfo& ps, int np, int r) {
+// Bucket row of pass-relative record r: the largest i with rstart[i] <= r (empty buckets skipped),
+// and the record it names; `ok` is false for a malformed row (the record is then skipped).
+__device__ __forceinline__ K16Rec k16_meta(const K16PassInfo& ps, const K16Params& p, int np, int r) {
   int lo = 0, hi = np;
   while (hi - lo > 1) {
     const int mid = (lo + hi) >> 1;
     if (ps.rstart[mid] <= r) lo = mid; else hi = mid;
   }
-  return lo;
+  K16Rec m;
+  m.i = lo;
+  m.g = ps.g[lo];
+  m.j16 = ps.first[lo] + (r - ps.rstart[lo]);
+  m.ok = m.g >= 0 && m.g < p.G && m.j16 >= 0 && m.j16 < p.NB16;
+  return m;
 }
 
-// Stage x[t0 + t, feat[q][s]] into xs[s * TT + t] (zeros past the batch) and the clamped features.
-__device__ __forceinline__ void k16_stage_x(float* __restrict__ xs, int* __restrict__ fq, const K16Params& p,
-                                            int q, int t0, int ntok) {
+// Warp-cooperative asynchronous copy of a record's weights, bias and local positions into `st`
+// (one commit group per call, empty for a skipped record).
+__device__ __forceinline__ void k16_prefetch(K16Stage& st, const K16Params& p, const K16Rec& m, int lane) {
+  if (m.ok) {
+    const int64_t f = (int64_t)m.g * p.NB16 + m.j16;
+    const float* wsrc = p.w + f * 256 + lane * 8;
+    cp_async16(st.w + lane * 8, wsrc);
+    cp_async16(st.w + lane * 8 + 4, wsrc + 4);
+    if (lane < 4) cp_async16(st.b + lane * 4, p.b + f * 16 + lane * 4);
+    else if (lane == 4) cp_async16(st.env, p.env + f * 16);
+  }
+  cp_async_commit();
+}
+
+// Stage x[t0 + t, feat[q][s]] into xs[s * ld + t] (zeros past the batch, up to TT) and the features.
+__device__ __forceinline__ void k16_stage_x(float* __restrict__ xs, int ld, int* __restrict__ fq,
+                                            const K16Params& p, int q, int t0, int ntok) {
   for (int s = threadIdx.x; s < p.S; s += blockDim.x) {
     const int d = (int)(uint16_t)__ldg(p.feat + (int64_t)q * p.S + s);
     fq[s] = d < p.D ? d : p.D - 1;
@@ -98,92 +140,113 @@ __device__ __forceinline__ void k16_stage_x(float* __restrict__ xs, int* __restr
   const int n = p.S * p.TT;
   for (int e = threadIdx.x; e < n; e += blockDim.x) {
     const int s = e / p.TT, t = e - s * p.TT;
-    xs[e] = t < ntok ? __ldg(p.x + (int64_t)(t0 + t) * p.ldx + fq[s]) : 0.f;
+    xs[s * ld + t] = t < ntok ? __ldg(p.x + (int64_t)(t0 + t) * p.ldx + fq[s]) : 0.f;
   }
 }
 
-// The record's 16 local positions (clamped to the set), each times `mul` (a row stride).
-__device__ __forceinline__ void k16_env(const uint8_t* __restrict__ env, int64_t f, int smax, int mul,
-                                        int (&off)[16]) {
-  const uint4 e4 = __ldg(reinterpret_cast<const uint4*>(env + f * 16));
-  const unsigned ev[4] = {e4.x, e4.y, e4.z, e4.w};
-#pragma unroll
-  for (int j = 0; j < 4; ++j)
-#pragma unroll
-    for (int c = 0; c < 4; ++c) off[4 * j + c] = min((int)((ev[j] >> (8 * c)) & 0xffu), smax) * mul;
+// Local position k of a staged record (clamped to the set).
+__device__ __forceinline__ int k16_pos(const K16Stage& st, int k, int smax) {
+  return min((int)((st.env[k >> 2] >> (8 * (k & 3))) & 0xffu), smax);
 }
 
+// Forward.  lane = (token group tg = lane >> 1: 4 tokens, neuron octet no = lane & 1: 8 neurons);
+// a warp step covers one record and 64 tokens.  Each lane keeps its 8 neurons' 128 weights in
+// registers, so one 128-bit shared load of x feeds 32 FMAs.  The warp's next record is copied
+// into shared memory (cp.async) while the current one runs.
 template <int ACT>
 __global__ void __launch_bounds__(kK16FwdThreads, 1) k16_fwd_kernel(const K16Params p) {
   constexpr int NW = kK16FwdThreads / 32;
   extern __shared__ __align__(16) float sm[];
-  const int TT = p.TT;
+  const int TT = p.TT;                     // a multiple of kK16FwdStep
   float* xs = sm;                          // [S][TT]
-  float* ys = sm + (size_t)p.S * TT;       // [kK16Pass][TT] per-bucket token sums
+  float* ys = sm + (size_t)p.S * TT;       // [kK16FwdPass][TT] per-bucket token sums
   __shared__ K16PassInfo ps;
   __shared__ int fq[kK16MaxS];
+  __shared__ K16Stage stg[NW][2];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int q = blockIdx.x, t0 = blockIdx.y * TT;
   const int ntok = min(TT, p.B - t0);
-  k16_stage_x(xs, fq, p, q, t0, ntok);
-  for (int e = threadIdx.x; e < kK16Pass * TT; e += kK16FwdThreads) ys[e] = 0.f;
-  const int qtr = lane & 3, n0 = 2 * (lane >> 2);
+  k16_stage_x(xs, TT, fq, p, q, t0, ntok);
+  for (int e = threadIdx.x; e < kK16FwdPass * TT; e += kK16FwdThreads) ys[e] = 0.f;
+  const int no = lane & 1, tg = lane >> 1;
   const int b_hi = min(max(__ldg(p.q_off + q + 1), 0), p.nbk);
   const int b_lo = min(max(__ldg(p.q_off + q), 0), b_hi);
-  for (int p0 = b_lo; p0 < b_hi; p0 += kK16Pass) {
-    const int np = min(kK16Pass, b_hi - p0);
+  for (int p0 = b_lo; p0 < b_hi; p0 += kK16FwdPass) {
+    const int np = min(kK16FwdPass, b_hi - p0);
     __syncthreads();
     k16_load_pass(ps, p, p0, np);
     __syncthreads();
     const int nrec = ps.rstart[np];
+    K16Rec cur;
+    cur.ok = false;
+    if (warp < nrec) {
+      cur = k16_meta(ps, p, np, warp);
+      k16_prefetch(stg[warp][0], p, cur, lane);
+    }
+    int buf = 0;
     for (int r = warp; r < nrec; r += NW) {
-      const int i = k16_find(ps, np, r);
-      const int g = ps.g[i];
-      const int j16 = ps.first[i] + (r - ps.rstart[i]);
-      if (g < 0 || g >= p.G || j16 < 0 || j16 >= p.NB16) continue;  // warp-uniform: malformed bucket row
-      const int64_t f = (int64_t)g * p.NB16 + j16;
-      const int ng = __ldg(p.counts + g);
-      const bool ok0 = j16 * 16 + n0 < ng, ok1 = j16 * 16 + n0 + 1 < ng;
-      float w0[16], w1[16];
-      {
-        const float4* wp = reinterpret_cast<const float4*>(p.w + (f * 16 + n0) * 16);
+      K16Rec nxt;
+      nxt.ok = false;
+      if (r + NW < nrec) {
+        nxt = k16_meta(ps, p, np, r + NW);
+        k16_prefetch(stg[warp][buf ^ 1], p, nxt, lane);
+        cp_async_wait<1>();
+      } else {
+        cp_async_wait<0>();
+      }
+      __syncwarp();
+      if (cur.ok) {
+        const K16Stage& st = stg[warp][buf];
+        const int nv = min(max(__ldg(p.counts + cur.g) - (cur.j16 * 16 + no * 8), 0), 8);  // valid neurons
+        float wr[8][16], bb[8];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const float4 a = __ldg(wp + c), b = __ldg(wp + 4 + c);
-          w0[4 * c] = a.x; w0[4 * c + 1] = a.y; w0[4 * c + 2] = a.z; w0[4 * c + 3] = a.w;
-          w1[4 * c] = b.x; w1[4 * c + 1] = b.y; w1[4 * c + 2] = b.z; w1[4 * c + 3] = b.w;
+        for (int n = 0; n < 8; ++n)
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const float4 a = reinterpret_cast<const float4*>(st.w + (no * 8 + n) * 16)[c];
+            wr[n][4 * c] = a.x; wr[n][4 * c + 1] = a.y; wr[n][4 * c + 2] = a.z; wr[n][4 * c + 3] = a.w;
+          }
+#pragma unroll
+        for (int n = 0; n < 8; ++n) bb[n] = st.b[no * 8 + n];
+        int off[16];
+#pragma unroll
+        for (int k = 0; k < 16; ++k) off[k] = k16_pos(st, k, p.S - 1) * TT;
+        float* yrow = ys + cur.i * TT;
+        for (int tq = 0; tq < ntok; tq += kK16FwdStep) {
+          const int col = tq + 4 * tg;
+          float z[8][4];
+#pragma unroll
+          for (int n = 0; n < 8; ++n) z[n][0] = z[n][1] = z[n][2] = z[n][3] = bb[n];
+#pragma unroll
+          for (int k = 0; k < 16; ++k) {
+            const float4 v = *reinterpret_cast<const float4*>(xs + off[k] + col);
+#pragma unroll
+            for (int n = 0; n < 8; ++n) {
+              z[n][0] = fmaf(wr[n][k], v.x, z[n][0]);
+              z[n][1] = fmaf(wr[n][k], v.y, z[n][1]);
+              z[n][2] = fmaf(wr[n][k], v.z, z[n][2]);
+              z[n][3] = fmaf(wr[n][k], v.w, z[n][3]);
+            }
+          }
+          float a[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int n = 0; n < 8; ++n)
+            if (n < nv)
+#pragma unroll
+              for (int j = 0; j < 4; ++j) a[j] += act_f<ACT>(z[n][j]);
+          // sum the two octets (lane bit 0); lane `no` ends with tokens col + 2 no, col + 2 no + 1
+          const float s0 = no ? a[0] : a[2], s1 = no ? a[1] : a[3];
+          const float k0 = no ? a[2] : a[0], k1 = no ? a[3] : a[1];
+          const float v0 = k0 + __shfl_xor_sync(kFullMask, s0, 1);
+          const float v1 = k1 + __shfl_xor_sync(kFullMask, s1, 1);
+          const int t = col + 2 * no;
+          if (t < ntok) atomicAdd(yrow + t, v0);
+          if (t + 1 < ntok) atomicAdd(yrow + t + 1, v1);
         }
       }
-      const float b0 = __ldg(p.b + f * 16 + n0), b1 = __ldg(p.b + f * 16 + n0 + 1);
-      int off[16];
-      k16_env(p.env, f, p.S - 1, TT, off);
-      float* yrow = ys + i * TT;
-      for (int tq = 0; tq < ntok; tq += 16) {
-        const int col = tq + 4 * qtr;
-        float z0[4] = {b0, b0, b0, b0}, z1[4] = {b1, b1, b1, b1};
-#pragma unroll
-        for (int k = 0; k < 16; ++k) {
-          const float4 v = *reinterpret_cast<const float4*>(xs + off[k] + col);
-          z0[0] = fmaf(w0[k], v.x, z0[0]); z0[1] = fmaf(w0[k], v.y, z0[1]);
-          z0[2] = fmaf(w0[k], v.z, z0[2]); z0[3] = fmaf(w0[k], v.w, z0[3]);
-          z1[0] = fmaf(w1[k], v.x, z1[0]); z1[1] = fmaf(w1[k], v.y, z1[1]);
-          z1[2] = fmaf(w1[k], v.z, z1[2]); z1[3] = fmaf(w1[k], v.w, z1[3]);
-        }
-        float a[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) a[j] = (ok0 ? act_f<ACT>(z0[j]) : 0.f) + (ok1 ? act_f<ACT>(z1[j]) : 0.f);
-        // transpose-reduction over the 8 neuron pairs (lane bits 4, 3, 2); the 4 tokens end up
-        // split by lane bits 4 and 3
-        const bool hi = lane & 16, mid = lane & 8;
-        const float s0 = hi ? a[0] : a[2], s1 = hi ? a[1] : a[3];
-        const float k0 = hi ? a[2] : a[0], k1 = hi ? a[3] : a[1];
-        const float c0 = k0 + __shfl_xor_sync(kFullMask, s0, 16);
-        const float c1 = k1 + __shfl_xor_sync(kFullMask, s1, 16);
-        float v = (mid ? c1 : c0) + __shfl_xor_sync(kFullMask, mid ? c0 : c1, 8);
-        v += __shfl_xor_sync(kFullMask, v, 4);
-        const int t = col + (hi ? 2 : 0) + (mid ? 1 : 0);
-        if (!(lane & 4) && t < ntok) atomicAdd(yrow + t, v);
-      }
+      __syncwarp();
+      cur = nxt;
+      buf ^= 1;
     }
     __syncthreads();
     for (int e = threadIdx.x; e < np * TT; e += kK16FwdThreads) {
@@ -206,28 +269,39 @@ __device__ __forceinline__ float k16_dz(float c, float z) {
   }
 }
 
+// Backward.  lane bits: 4 = lo, 3..1 = token group tg (2 tokens), 0 = hi; the lane's neuron quad
+// is nq = lo + 2 hi (4 neurons).  A warp step covers one record and 16 tokens.  A lane keeps its
+// quad's 64 weights, 64 dW sums and the step's x values (16 inputs x 2 tokens) in registers, so
+// each x value feeds 8 FMAs (z and dW).  dX: the lane forms its quad's partial sums
+// sum_n dz[n][t] w[n][k]; a transpose-reduction over the 4 quads (lane bit 0 splits the 2 tokens,
+// lane bit 4 the 2 inputs of a pair) leaves one (k, t) per lane, and each half-warp adds 16
+// consecutive tokens of one row of the dX tile.  Lanes with lo set hold their record's inputs in
+// pair-swapped order (k ^ 1), which makes both reduction stages select-free and gives each
+// half-warp a single x row per load; the order is undone when dW is written.
 template <int ACT>
 __global__ void __launch_bounds__(kK16BwdThreads, 1) k16_bwd_kernel(const K16Params p) {
   constexpr int NW = kK16BwdThreads / 32;
   extern __shared__ __align__(16) float sm[];
-  const int TT = p.TT, TTD = TT + 1;        // dX rows padded by one word: distinct features spread over banks
-  float* xs = sm;                            // [S][TT]
-  float* c1s = xs + (size_t)p.S * TT;        // [kK16Pass][TT] per-bucket coefficients
-  float* dxs = c1s + (size_t)kK16Pass * TT;  // [S][TT + 1] dX tile
+  const int TT = p.TT;                          // a multiple of 32
+  const int LD = TT + 16;                       // row stride of the x and dX tiles
+  float* xs = sm;                               // [S][LD]
+  float* dxs = xs + (size_t)p.S * LD;           // [S][LD] dX tile
+  float* c1s = dxs + (size_t)p.S * LD;          // [kK16BwdPass][TT] per-bucket coefficients
   __shared__ K16PassInfo ps;
   __shared__ int fq[kK16MaxS];
-  __shared__ __align__(16) float dzs[NW][16][8];  // per warp: 16 neurons x 8 tokens of the current step
+  __shared__ K16Stage stg[NW][2];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int q = blockIdx.x, t0 = blockIdx.y * TT;
   const int ntok = min(TT, p.B - t0);
-  k16_stage_x(xs, fq, p, q, t0, ntok);
-  for (int e = threadIdx.x; e < p.S * TTD; e += kK16BwdThreads) dxs[e] = 0.f;
-  const int h = lane >> 4, n = lane & 15;
-  float* dzw = &dzs[warp][0][0];
+  k16_stage_x(xs, LD, fq, p, q, t0, ntok);
+  for (int e = threadIdx.x; e < p.S * LD; e += kK16BwdThreads) dxs[e] = 0.f;
+  const bool lo = lane & 16, hi = lane & 1;
+  const int tg = (lane >> 1) & 7;
+  const int nq = (lo ? 1 : 0) + (hi ? 2 : 0);
   const int b_hi = min(max(__ldg(p.q_off + q + 1), 0), p.nbk);
   const int b_lo = min(max(__ldg(p.q_off + q), 0), b_hi);
-  for (int p0 = b_lo; p0 < b_hi; p0 += kK16Pass) {
-    const int np = min(kK16Pass, b_hi - p0);
+  for (int p0 = b_lo; p0 < b_hi; p0 += kK16BwdPass) {
+    const int np = min(kK16BwdPass, b_hi - p0);
     __syncthreads();
     k16_load_pass(ps, p, p0, np);
     __syncthreads();
@@ -238,109 +312,185 @@ __global__ void __launch_bounds__(kK16BwdThreads, 1) k16_bwd_kernel(const K16Par
     }
     __syncthreads();
     const int nrec = ps.rstart[np];
+    K16Rec cur;
+    cur.ok = false;
+    if (warp < nrec) {
+      cur = k16_meta(ps, p, np, warp);
+      k16_prefetch(stg[warp][0], p, cur, lane);
+    }
+    int buf = 0;
     for (int r = warp; r < nrec; r += NW) {
-      const int i = k16_find(ps, np, r);
-      const int g = ps.g[i];
-      const int j16 = ps.first[i] + (r - ps.rstart[i]);
-      if (g < 0 || g >= p.G || j16 < 0 || j16 >= p.NB16) continue;  // warp-uniform
-      const int64_t f = (int64_t)g * p.NB16 + j16;
-      const bool ok = j16 * 16 + n < __ldg(p.counts + g);
-      float wr[16], wc[16];
-      {
-        const float4* wp = reinterpret_cast<const float4*>(p.w + (f * 16 + n) * 16);
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const float4 a = __ldg(wp + c);
-          wr[4 * c] = a.x; wr[4 * c + 1] = a.y; wr[4 * c + 2] = a.z; wr[4 * c + 3] = a.w;
-        }
-        const float* wcp = p.w + f * 256 + n;
-#pragma unroll
-        for (int m = 0; m < 16; ++m) wc[m] = __ldg(wcp + m * 16);
+      K16Rec nxt;
+      nxt.ok = false;
+      if (r + NW < nrec) {
+        nxt = k16_meta(ps, p, np, r + NW);
+        k16_prefetch(stg[warp][buf ^ 1], p, nxt, lane);
+        cp_async_wait<1>();
+      } else {
+        cp_async_wait<0>();
       }
-      const float bb = __ldg(p.b + f * 16 + n);
-      int off[16];
-      k16_env(p.env, f, p.S - 1, TT, off);
-      const int dxrow = min((int)__ldg(p.env + f * 16 + n), p.S - 1) * TTD;
-      float dwacc[16];
+      __syncwarp();
+      if (cur.ok) {
+        const K16Stage& st = stg[warp][buf];
+        const int64_t f = (int64_t)cur.g * p.NB16 + cur.j16;
+        const int nv = min(max(__ldg(p.counts + cur.g) - (cur.j16 * 16 + nq * 4), 0), 4);  // valid neurons
+        float wr[4][16], bb[4];
 #pragma unroll
-      for (int k = 0; k < 16; ++k) dwacc[k] = 0.f;
-      float dbacc = 0.f;
-      const float* crow = c1s + i * TT;
-      for (int tq = 0; tq < ntok; tq += 8) {
-        const int col = tq + 4 * h;
-        float xv[16][4];
+        for (int n = 0; n < 4; ++n)
 #pragma unroll
-        for (int k = 0; k < 16; ++k) {
-          const float4 v = *reinterpret_cast<const float4*>(xs + off[k] + col);
-          xv[k][0] = v.x; xv[k][1] = v.y; xv[k][2] = v.z; xv[k][3] = v.w;
+          for (int c = 0; c < 4; ++c) {
+            const float4 a = reinterpret_cast<const float4*>(st.w + (nq * 4 + n) * 16)[c];
+            wr[n][4 * c] = lo ? a.y : a.x;
+            wr[n][4 * c + 1] = lo ? a.x : a.y;
+            wr[n][4 * c + 2] = lo ? a.w : a.z;
+            wr[n][4 * c + 3] = lo ? a.z : a.w;
+          }
+        {
+          const float4 b4 = reinterpret_cast<const float4*>(st.b)[nq];
+          bb[0] = b4.x; bb[1] = b4.y; bb[2] = b4.z; bb[3] = b4.w;
         }
-        const float4 c4 = *reinterpret_cast<const float4*>(crow + col);
-        const float cc[4] = {c4.x, c4.y, c4.z, c4.w};
-        float z[4] = {bb, bb, bb, bb};
+        int off[16];
 #pragma unroll
-        for (int k = 0; k < 16; ++k)
+        for (int k = 0; k < 16; ++k) off[k] = k16_pos(st, lo ? (k ^ 1) : k, p.S - 1) * LD;
+        float dwacc[4][16], dbacc[4];
 #pragma unroll
-          for (int j = 0; j < 4; ++j) z[j] = fmaf(wr[k], xv[k][j], z[j]);
-        float dz[4];
+        for (int n = 0; n < 4; ++n) {
+          dbacc[n] = 0.f;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) dz[j] = ok ? k16_dz<ACT>(cc[j], z[j]) : 0.f;
-#pragma unroll
-        for (int k = 0; k < 16; ++k)
-#pragma unroll
-          for (int j = 0; j < 4; ++j) dwacc[k] = fmaf(dz[j], xv[k][j], dwacc[k]);
-        dbacc += (dz[0] + dz[1]) + (dz[2] + dz[3]);
-        *reinterpret_cast<float4*>(dzw + n * 8 + 4 * h) = make_float4(dz[0], dz[1], dz[2], dz[3]);
-        __syncwarp();
-        float dxk[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int m = 0; m < 16; ++m) {
-          const float4 d = *reinterpret_cast<const float4*>(dzw + m * 8 + 4 * h);
-          dxk[0] = fmaf(d.x, wc[m], dxk[0]);
-          dxk[1] = fmaf(d.y, wc[m], dxk[1]);
-          dxk[2] = fmaf(d.z, wc[m], dxk[2]);
-          dxk[3] = fmaf(d.w, wc[m], dxk[3]);
+          for (int k = 0; k < 16; ++k) dwacc[n][k] = 0.f;
         }
-        float* dst = dxs + dxrow + col;
+        const float* crow = c1s + cur.i * TT;
+        for (int tq = 0; tq < ntok; tq += kK16BwdStep) {
+          const int col = tq + 2 * tg;
+          float xv[16][2];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) atomicAdd(dst + j, dxk[j]);
-        __syncwarp();
+          for (int k = 0; k < 16; ++k) {
+            const float2 v = *reinterpret_cast<const float2*>(xs + off[k] + col);
+            xv[k][0] = v.x; xv[k][1] = v.y;
+          }
+          const float2 c2 = *reinterpret_cast<const float2*>(crow + col);
+          float z0[4], z1[4];
+#pragma unroll
+          for (int n = 0; n < 4; ++n) z0[n] = z1[n] = bb[n];
+#pragma unroll
+          for (int k = 0; k < 16; ++k)
+#pragma unroll
+            for (int n = 0; n < 4; ++n) {
+              z0[n] = fmaf(wr[n][k], xv[k][0], z0[n]);
+              z1[n] = fmaf(wr[n][k], xv[k][1], z1[n]);
+            }
+          float d0[4], d1[4];
+#pragma unroll
+          for (int n = 0; n < 4; ++n) {
+            d0[n] = n < nv ? k16_dz<ACT>(c2.x, z0[n]) : 0.f;
+            d1[n] = n < nv ? k16_dz<ACT>(c2.y, z1[n]) : 0.f;
+            dbacc[n] += d0[n] + d1[n];
+          }
+#pragma unroll
+          for (int k = 0; k < 16; ++k)
+#pragma unroll
+            for (int n = 0; n < 4; ++n) dwacc[n][k] = fmaf(d1[n], xv[k][1], fmaf(d0[n], xv[k][0], dwacc[n][k]));
+          // dX partials of the token this lane keeps (dk) and of the one it sends (ds), per input
+          float pk[16], ps_[16];
+#pragma unroll
+          for (int k = 0; k < 16; ++k) {
+            float a = 0.f, b = 0.f;
+#pragma unroll
+            for (int n = 0; n < 4; ++n) {
+              a = fmaf(hi ? d1[n] : d0[n], wr[n][k], a);
+              b = fmaf(hi ? d0[n] : d1[n], wr[n][k], b);
+            }
+            pk[k] = a;
+            ps_[k] = b;
+          }
+#pragma unroll
+          for (int k = 0; k < 16; ++k) pk[k] += __shfl_xor_sync(kFullMask, ps_[k], 1);
+          float* drow = dxs + col + (hi ? 1 : 0);
+#pragma unroll
+          for (int m = 0; m < 8; ++m)
+            atomicAdd(drow + off[2 * m], pk[2 * m] + __shfl_xor_sync(kFullMask, pk[2 * m + 1], 16));
+        }
+        // dW: transpose-reduce the 64 sums over the 8 token groups (lane bits 3, 2, 1); the lane ends
+        // with positions 2 tg, 2 tg + 1 of its 4 neurons (inputs swapped when lo)
+        float r8[4][8], r4[4][4], r2[4][2];
+        const bool b3 = lane & 8, b2 = lane & 4, b1 = lane & 2;
+#pragma unroll
+        for (int n = 0; n < 4; ++n)
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            const float keep = b3 ? dwacc[n][kk + 8] : dwacc[n][kk];
+            const float send = b3 ? dwacc[n][kk] : dwacc[n][kk + 8];
+            r8[n][kk] = keep + __shfl_xor_sync(kFullMask, send, 8);
+          }
+#pragma unroll
+        for (int n = 0; n < 4; ++n)
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const float keep = b2 ? r8[n][kk + 4] : r8[n][kk];
+            const float send = b2 ? r8[n][kk] : r8[n][kk + 4];
+            r4[n][kk] = keep + __shfl_xor_sync(kFullMask, send, 4);
+          }
+#pragma unroll
+        for (int n = 0; n < 4; ++n)
+#pragma unroll
+          for (int kk = 0; kk < 2; ++kk) {
+            const float keep = b1 ? r4[n][kk + 2] : r4[n][kk];
+            const float send = b1 ? r4[n][kk] : r4[n][kk + 2];
+            r2[n][kk] = keep + __shfl_xor_sync(kFullMask, send, 2);
+          }
+#pragma unroll
+        for (int n = 0; n < 4; ++n)
+#pragma unroll
+          for (int s = 2; s <= 8; s <<= 1) dbacc[n] += __shfl_xor_sync(kFullMask, dbacc[n], s);
+        if (nv > 0) {
+          float* dwp = p.dw + (f * 16 + nq * 4) * 16 + 2 * tg;
+#pragma unroll
+          for (int m = 0; m < 4; ++m) red_add2(dwp + 16 * m, lo ? r2[m][1] : r2[m][0], lo ? r2[m][0] : r2[m][1]);
+          if (tg == 0) red_add4(p.db + f * 16 + nq * 4, dbacc[0], dbacc[1], dbacc[2], dbacc[3]);
+        }
       }
-#pragma unroll
-      for (int k = 0; k < 16; ++k) dwacc[k] += __shfl_xor_sync(kFullMask, dwacc[k], 16);
-      dbacc += __shfl_xor_sync(kFullMask, dbacc, 16);
-      if (h == 0 && ok) {
-        float* dwp = p.dw + (f * 16 + n) * 16;
-#pragma unroll
-        for (int c = 0; c < 4; ++c)
-          red_add4(dwp + 4 * c, dwacc[4 * c], dwacc[4 * c + 1], dwacc[4 * c + 2], dwacc[4 * c + 3]);
-        red_add(p.db + f * 16 + n, dbacc);
-      }
+      __syncwarp();
+      cur = nxt;
+      buf ^= 1;
     }
   }
   __syncthreads();
   const int n_el = p.S * ntok;
   for (int e = threadIdx.x; e < n_el; e += kK16BwdThreads) {
     const int s = e / ntok, t = e - s * ntok;
-    const float v = dxs[s * TTD + t];
+    const float v = dxs[s * LD + t];
     if (v != 0.f) red_add(p.dx + (int64_t)(t0 + t) * p.lddx + fq[s], v);
   }
 }
 
-static size_t k16_fwd_smem(int S, int TT) { return ((size_t)S + kK16Pass) * TT * sizeof(float); }
+static size_t k16_fwd_smem(int S, int TT) { return ((size_t)S + kK16FwdPass) * TT * sizeof(float); }
 static size_t k16_bwd_smem(int S, int TT) {
-  return ((size_t)S * TT + (size_t)kK16Pass * TT + (size_t)S * (TT + 1)) * sizeof(float);
+  return ((size_t)2 * S * (TT + 16) + (size_t)kK16BwdPass * TT) * sizeof(float);
 }
 
-// Static shared memory of the kernels (pass info, feature list, dz slabs), with margin.
-constexpr int kK16StaticBytes = 8 * 1024;
+template <int ACT>
+static const void* k16_kernel(bool bwd) {
+  return bwd ? (const void*)k16_bwd_kernel<ACT> : (const void*)k16_fwd_kernel<ACT>;
+}
 
-// Token chunk: a multiple of 16 (the forward step), at most 256, the largest that fits.
-static int k16_pick_tt(int64_t B, int S, bool bwd, int optin) {
-  int64_t tt = (B + 15) / 16 * 16;
-  if (tt > 256) tt = 256;
-  for (; tt >= 16; tt -= 16) {
+// Static shared memory of a kernel (pass info, feature list, record stages).
+static int k16_static_smem(bool bwd, size_t* bytes) {
+  cudaFuncAttributes fa;
+  const cudaError_t e = cudaFuncGetAttributes(&fa, k16_kernel<GL_ACT_RELU>(bwd));
+  if (e != cudaSuccess) return set_cuda_error(e);
+  *bytes = fa.sharedSizeBytes;
+  return GL_OK;
+}
+
+// Token chunk: a multiple of 64 (forward) or 32 (backward), at most 512 / 256, the largest that fits.
+static int k16_pick_tt(int64_t B, int S, bool bwd, int optin, size_t stat) {
+  const int step = bwd ? 32 : kK16FwdStep;
+  int64_t tt = (B + step - 1) / step * step;
+  const int64_t cap = bwd ? 256 : kK16MaxTT;
+  if (tt > cap) tt = cap;
+  for (; tt >= step; tt -= step) {
     const size_t need = bwd ? k16_bwd_smem(S, (int)tt) : k16_fwd_smem(S, (int)tt);
-    if ((int64_t)need + kK16StaticBytes <= optin) return (int)tt;
+    if ((int64_t)(need + stat) <= optin) return (int)tt;
   }
   return -1;
 }
@@ -354,7 +504,8 @@ static int k16_check(const GlK16Args& a, bool bwd) {
   if (!a.x || !a.env || !a.feat || !a.buckets || !a.q_off || !a.rec_off || !a.w || !a.b || !a.counts)
     return GL_ERR_NULL;
   if (a.ldx < a.D) return GL_ERR_SHAPE;
-  if (((uintptr_t)a.env & 15) || ((uintptr_t)a.w & 15) || ((uintptr_t)a.buckets & 15)) return GL_ERR_ALIGN;
+  if (((uintptr_t)a.env & 15) || ((uintptr_t)a.w & 15) || ((uintptr_t)a.b & 15) || ((uintptr_t)a.buckets & 15))
+    return GL_ERR_ALIGN;
   if (a.act != GL_ACT_RELU && a.act != GL_ACT_IDENTITY) return GL_ERR_UNSUPPORTED;
   if (!bwd) {
     if (!a.pre) return GL_ERR_NULL;
@@ -362,7 +513,7 @@ static int k16_check(const GlK16Args& a, bool bwd) {
   } else {
     if (!a.c1t || !a.dx || !a.dw || !a.db) return GL_ERR_NULL;
     if (a.ldc < a.B || a.lddx < a.D) return GL_ERR_SHAPE;
-    if (((uintptr_t)a.dw & 15) || ((uintptr_t)a.c1t & 3)) return GL_ERR_ALIGN;
+    if (((uintptr_t)a.dw & 15) || ((uintptr_t)a.db & 15) || ((uintptr_t)a.c1t & 3)) return GL_ERR_ALIGN;
   }
   return GL_OK;
 }
@@ -373,16 +524,18 @@ static int k16_launch(const GlK16Args& a, void* stream, bool bwd) {
   if (a.B == 0 || a.Q == 0) return GL_OK;
   int optin = 0;
   if ((rc = device_smem_optin(&optin))) return rc;
-  const int TT = a.tokens ? (int)a.tokens : k16_pick_tt(a.B, (int)a.S, bwd, optin);
+  size_t stat = 0;
+  if ((rc = k16_static_smem(bwd, &stat))) return rc;
+  const int TT = a.tokens ? (int)a.tokens : k16_pick_tt(a.B, (int)a.S, bwd, optin, stat);
   if (TT < 0) return GL_ERR_SMEM;
-  if (TT < 16 || TT % 16 || TT > 1024) return GL_ERR_UNSUPPORTED;
+  const int step = bwd ? 32 : kK16FwdStep;
+  if (TT < step || TT % step || TT > 1024) return GL_ERR_UNSUPPORTED;
   const size_t smem = bwd ? k16_bwd_smem((int)a.S, TT) : k16_fwd_smem((int)a.S, TT);
-  if ((int64_t)smem + kK16StaticBytes > optin) return GL_ERR_SMEM;
+  if ((int64_t)(smem + stat) > optin) return GL_ERR_SMEM;
   const int64_t chunks = (a.B + TT - 1) / TT;
   if (a.Q > 2147483647LL || chunks > 65535) return GL_ERR_SHAPE;
   const bool relu = a.act == GL_ACT_RELU;
-  const void* kern = bwd ? (relu ? (const void*)k16_bwd_kernel<GL_ACT_RELU> : (const void*)k16_bwd_kernel<GL_ACT_IDENTITY>)
-                         : (relu ? (const void*)k16_fwd_kernel<GL_ACT_RELU> : (const void*)k16_fwd_kernel<GL_ACT_IDENTITY>);
+  const void* kern = relu ? k16_kernel<GL_ACT_RELU>(bwd) : k16_kernel<GL_ACT_IDENTITY>(bwd);
   if ((rc = ensure_dynamic_smem(kern, smem))) return rc;
   K16Params p;
   p.x = a.x; p.env = a.env; p.feat = a.feat; p.buckets = a.buckets; p.q_off = a.q_off; p.rec_off = a.rec_off;
@@ -421,6 +574,9 @@ extern "C" int gl_k16_auto_tokens(int64_t B, int64_t S, int32_t backward) {
   int optin = 0;
   const int rc = gl::device_smem_optin(&optin);
   if (rc) return rc;
-  const int tt = gl::k16_pick_tt(B, (int)S, backward != 0, optin);
+  size_t stat = 0;
+  const int rs = gl::k16_static_smem(backward != 0, &stat);
+  if (rs) return rs;
+  const int tt = gl::k16_pick_tt(B, (int)S, backward != 0, optin, stat);
   return tt < 0 ? GL_ERR_SMEM : tt;
 }

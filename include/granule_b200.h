@@ -175,19 +175,20 @@ typedef struct GlK16Args {
   const int32_t* buckets;   /* [nb, 4], 16-byte aligned */
   const int32_t* q_off;     /* [Q+1] */
   const int32_t* rec_off;   /* [nb+1] */
-  const float* w;
-  const float* b;
+  const float* w;           /* 16-byte aligned */
+  const float* b;           /* 16-byte aligned */
   const int32_t* counts;    /* [G] */
   float* pre;               /* forward: [B, ldp], accumulated */
   const float* c1t;         /* backward: [G, ldc] */
   float* dx;                /* backward: [B, lddx], accumulated */
   float* dw;                /* backward: weight-shaped, accumulated */
-  float* db;                /* backward: bias-shaped, accumulated */
+  float* db;                /* backward: bias-shaped, accumulated, 16-byte aligned */
   int64_t B, D, G, NB16, Q, S;
   int64_t nbuckets;         /* rows of `buckets` (q_off values are clamped to it) */
   int64_t ldx, ldp, ldc, lddx;
   int32_t act;              /* GL_ACT_RELU or GL_ACT_IDENTITY */
-  int32_t tokens;           /* token chunk per block (0 = automatic; else a multiple of 16) */
+  int32_t tokens;           /* token chunk per block (0 = automatic; else a multiple of 64 for the
+                               forward, of 32 for the backward, at most 1024) */
 } GlK16Args;
 
 int gl_k16_fwd_f32(const GlK16Args* args, void* stream);

@@ -79,11 +79,13 @@ def test_config4_shape_slice():
     _check_layer(lay, x, gy)
 
 
-@pytest.mark.parametrize("tokens", [16, 48, 128])
+@pytest.mark.parametrize("tokens", [(64, 32), (128, 96), (192, 128)])
 def test_token_chunks_and_identity(tokens):
+    """Explicit token chunks (forward: multiples of 64, backward: of 32) over a ragged batch of 200."""
+    ftok, btok = tokens
     lay = _layer(512, 20000, 16, 16)
     sched = lay._work()
-    gen = torch.Generator().manual_seed(tokens)
+    gen = torch.Generator().manual_seed(ftok + btok)
     B = 200
     x = torch.randn(B, 512, generator=gen)
     gy = torch.randn(B, 16, generator=gen)
@@ -95,13 +97,13 @@ def test_token_chunks_and_identity(tokens):
         xc = x.cuda()
         pre = torch.zeros(B, 16, device="cuda")
         _native.k16_fwd(xc, sched, lay.weight.detach(), lay.bias.detach(), lay.counts, pre, NB16, act=act,
-                        tokens=tokens)
+                        tokens=ftok)
         c1t = (gy.cuda() / lay.counts_f[None]).t().contiguous()
         dx = torch.zeros_like(xc)
         dw = torch.zeros_like(lay.weight.detach())
         db = torch.zeros_like(lay.bias.detach())
         _native.k16_bwd(xc, sched, lay.weight.detach(), lay.bias.detach(), lay.counts, c1t, dx, dw, db, NB16,
-                        act=act, tokens=tokens)
+                        act=act, tokens=btok)
         assert_close(pre, ry, what=f"y {act_name}", **FWD_TOL)
         assert_close(dx, rdx, what=f"dx {act_name}", slack=sdx, **GRAD_TOL)
         assert_close(dw, rdw, what=f"dw {act_name}", slack=sdw, **GRAD_TOL)
@@ -147,5 +149,5 @@ def test_bad_arguments_are_rejected_before_launch():
     with pytest.raises(_native.NativeLibraryError):
         _native.k16_fwd(x, sched, w, b, lay.counts, pre, NB16, act=2)     # GELU is not built for K16
     with pytest.raises(_native.NativeLibraryError):
-        _native.k16_fwd(x, sched, w, b, lay.counts, pre, NB16, tokens=24)  # not a multiple of 16
+        _native.k16_fwd(x, sched, w, b, lay.counts, pre, NB16, tokens=48)  # not a multiple of 64
     _native.k16_fwd(x[:0], sched, w, b, lay.counts, pre[:0], NB16)         # empty batch: no work
