@@ -27,6 +27,11 @@ a bounded slice of the same workload on the host cores (rank 0, N = 1).
 G = 2048 outputs, S = 64, R = 64, batch 512, seed 3): forward + backward through the layer on
 1 GPU, with the forward and backward (dX-carrying) kernels timed separately.
 
+``--workload locality`` runs BASELINE config 5: a Mode-A layer with D = 16384, N = 100,663,296,
+G = 8192 (seed 4), timed forward-only and forward + backward at batch 1, 32, 256, 1024 and 4096,
+once with the reference's uniform index rule and once with windowed indices (each supergroup of
+4096 consecutive neurons draws from its own random 512-wide input window; layout.windowed_indices).
+
 ``--impl reference`` times the reference's CPU path (the oracle port: the
 reference's materialising PyTorch path does not fit 100M neurons) on the same
 config, rank 0 only.
@@ -367,6 +372,75 @@ def bench_cover16(args, world):
     print(json.dumps(line), flush=True)
 
 
+LOC_METRIC = ("neuron-samples/s fwd+bwd at B=1024, windowed indices, locality/batch sweep "
+              "(D=16384, N=100,663,296, G=8192)")
+
+
+def bench_locality(args):
+    """BASELINE config 5 (module docstring); rank 0 only, 1 GPU."""
+    from granulelayer_b200 import SparsePoolingLayer, _native
+    from granulelayer_b200.layout import windowed_indices
+
+    Dl, Nl, Gl = 16384, 100_663_296, 8192
+    batches = [int(v) for v in args.batches.split(",") if v]
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    lay = SparsePoolingLayer(Dl, Nl, Gl, shared_neurons=None, pooling="mean", dtype=torch.float32, device=dev,
+                             seed=4)
+    lay.enable_main_grad()
+    uniform = lay.indices.clone()
+    windowed = windowed_indices(lay.layout, dev, window=512, supergroup=4096, seed=4)
+    gen = torch.Generator(device=dev).manual_seed(4)
+    rows = []
+    launches = 0
+    with ClockSampler(dev.index) as clk:
+        for mode, idx in (("uniform", uniform), ("windowed", windowed)):
+            with torch.no_grad():
+                lay.indices.copy_(idx)
+            for Bl in batches:
+                x = torch.randn(Bl, Dl, device=dev, generator=gen)
+                dy = torch.randn(Bl, Gl, device=dev, generator=gen)
+                steps = max(1, min(args.steps, 3 if Bl >= 1024 else args.steps))
+                res = {"indices": mode, "batch": Bl, "steps": steps}
+                for kind in ("fwd", "fwd+bwd"):
+                    def step():
+                        if kind == "fwd":
+                            with torch.no_grad():
+                                lay(x)
+                        else:
+                            lay(x.detach().requires_grad_(True)).backward(dy)
+                    for _ in range(max(3, args.warmup)):
+                        step()
+                    torch.cuda.synchronize(dev)
+                    n0 = _native.launch_count()
+                    s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    s_ev.record()
+                    for _ in range(steps):
+                        step()
+                    e_ev.record()
+                    torch.cuda.synchronize(dev)
+                    launches += _native.launch_count() - n0
+                    ms = s_ev.elapsed_time(e_ev) / steps
+                    res[kind] = {"ms": ms, "neuron_samples_per_s": Bl * Nl / (ms / 1e3)}
+                rows.append(res)
+                print(json.dumps({"locality_row": res}), file=sys.stderr, flush=True)
+    head = next((r for r in rows if r["indices"] == "windowed" and r["batch"] == 1024), rows[-1])
+    hbm, hbm_kind = peak_hbm()
+    step_bytes = 2 * param_bytes(Nl) + 2 * gather_bytes(head["batch"], Nl)
+    line = {
+        "metric": LOC_METRIC, "value": head["fwd+bwd"]["neuron_samples_per_s"], "unit": UNIT, "n_gpus": 1,
+        "steps": head["steps"], "warmup": max(3, args.warmup), "ms_per_step": head["fwd+bwd"]["ms"],
+        "higher_is_better": True, "scaling": "none", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "locality/batch sweep, Mode-A fan-in-8 mean-ReLU layer, fwd and fwd+bwd "
+                               "(BASELINE config 5)", "D": Dl, "N": Nl, "G": Gl, "batches": batches,
+                   "windowed": "supergroups of 4096 neurons, 512-wide random windows, seed 4",
+                   "l2": "parameters (5.2 GB) larger than L2"},
+        "hbm_roofline_step_frac": (step_bytes / (hbm * 1e9)) / (head["fwd+bwd"]["ms"] / 1e3),
+        "sweep": rows, "clocks": clk.summary(), "gpu_launches": launches,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     global N, G
     ap = argparse.ArgumentParser()
@@ -377,7 +451,8 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ref-seconds", type=float, default=4.0)
-    ap.add_argument("--workload", default="layer100m", choices=["layer100m", "cover16"])
+    ap.add_argument("--workload", default="layer100m", choices=["layer100m", "cover16", "locality"])
+    ap.add_argument("--batches", default="1,32,256,1024,4096", help="locality: batch sizes of the sweep")
     ap.add_argument("--cover-outputs", type=int, default=2048,
                     help="cover16: outputs of 24,576 neurons (default 2048 = config 4; fewer for ncu captures)")
     ap.add_argument("--groups", type=int, default=G,
@@ -395,6 +470,10 @@ def main():
     if args.workload == "cover16":
         if rank == 0:
             bench_cover16(args, world)
+        return
+    if args.workload == "locality":
+        if rank == 0:
+            bench_locality(args)
         return
     if args.impl == "reference":
         run_reference(args, rank, world)

@@ -245,6 +245,46 @@ def init_parameters(layout: SparseLayout, device, dtype=torch.bfloat16, seed: in
 
 
 @torch.no_grad()
+def windowed_indices(layout: SparseLayout, device, window: int = 512, supergroup: int = 4096, seed: int = 4,
+                     chunk_records: int = 1 << 22) -> torch.Tensor:
+    """Mode-A indices with input locality: the valid neurons, numbered group-major (global id
+    ``offset_g + slot``), form supergroups of ``supergroup`` consecutive neurons; supergroup s draws
+    every neuron's ``fan_in`` distinct sorted indices uniformly from its own window
+    ``[o_s, o_s + window)``.  Padded slots hold 0.
+
+    The reference has no Mode-A locality rule (its input supergroups are random feature subsets of
+    Mode-B layers, supergroups.py:58-482); this is the benchmark's own seeded rule: one
+    ``torch.Generator(device)`` seeded with ``seed`` draws all window offsets o_s ~ U{0 .. D - window}
+    first, then the records in chunks with the same distinct-and-sorted redraw rule as
+    ``init_parameters``.
+    """
+    if layout.shared_indices or layout.packed:
+        raise ValueError("windowed_indices builds canonical Mode-A index tensors")
+    D, K = layout.input_dim, layout.fan_in
+    window = min(window, D)
+    if window < K:
+        raise ValueError(f"window {window} < fan_in {K}")
+    gen = torch.Generator(device=device)
+    gen.manual_seed(seed)
+    n_valid = layout.hidden_dim
+    n_sg = -(-n_valid // supergroup)
+    offs = torch.randint(0, D - window + 1, (n_sg,), generator=gen, device=device, dtype=torch.int64)
+    recs = torch.empty((n_valid, K), dtype=torch.int16, device=device)
+    for lo in range(0, n_valid, chunk_records):
+        hi = min(lo + chunk_records, n_valid)
+        r = _distinct_sorted_records(hi - lo, window, K, gen, device)
+        sg = torch.arange(lo, hi, device=device) // supergroup
+        recs[lo:hi] = (r + offs[sg][:, None]).to(torch.int16)
+    idx = torch.zeros(layout.index_shape, dtype=torch.int16, device=device)
+    G, NB, C = layout.groups, layout.blocks_per_group, layout.block
+    counts = layout.counts_tensor(device).to(torch.int64)
+    slots = torch.arange(NB * C, device=device)
+    valid = (slots[None, :] < counts[:, None]).view(G, NB, C)
+    idx[valid] = recs
+    return idx
+
+
+@torch.no_grad()
 def zero_padding_(layout: SparseLayout, weights=None, bias=None, indices=None):
     """Zero the padded slots of weights, bias and Mode-A indices (layout.py:254-277).
 

@@ -260,3 +260,30 @@ def test_nonfinite_upstream_gradient_reaches_dx(accum, bad):
     sdx = O.backward(arr["x"], idx.numpy(), w.numpy(), b.numpy(), L.counts_tensor("cpu").numpy(), arr["dy"],
                      slack=True)[3]
     assert_close(dx[keep], arr["dx"][keep], what="dx(other tokens)", slack=sdx[keep], **BWD)
+
+
+@pytest.mark.parametrize("B", [1, 32, 67])
+def test_windowed_indices_against_oracle(B):
+    """Config-5 geometry, reduced: D = 16384, 12,288 neurons per group, supergroups of 4096 neurons
+    drawing from 512-wide windows (layout.windowed_indices)."""
+    from granulelayer_b200.layout import windowed_indices
+
+    D, G = 16384, 3
+    H = G * 12288
+    lay = SparsePoolingLayer(D, H, G, shared_neurons=None, pooling="mean", dtype=torch.float32, seed=4,
+                             bias_std=0.1)
+    with torch.no_grad():
+        lay.indices.copy_(windowed_indices(lay.layout, "cpu", window=512, supergroup=4096, seed=4))
+    idx, w, b = lay.indices.clone(), lay.weight.detach().clone(), lay.bias.detach().clone()
+    counts = lay.layout.counts_tensor("cpu").numpy()
+    gen = torch.Generator().manual_seed(B)
+    x = torch.randn(B, D, generator=gen)
+    dy = torch.randn(B, G, generator=gen)
+    y, dx, dw, db = _run(lay.cuda(), x.numpy(), dy.numpy())
+    pre = O.forward(x.numpy(), idx.numpy(), w.numpy(), b.numpy(), counts)
+    odx, odw, odb, sdx, sdw, sdb = O.backward(x.numpy(), idx.numpy(), w.numpy(), b.numpy(), counts, dy.numpy(),
+                                              slack=True)
+    assert_close(y, pre, what="y", **FWD)
+    assert_close(dx, odx, what="dx", slack=sdx, **BWD)
+    assert_close(dw, odw, what="dw", slack=sdw, **BWD)
+    assert_close(db, odb, what="db", slack=sdb, **BWD)

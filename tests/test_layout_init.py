@@ -97,3 +97,24 @@ def test_layout_validation():
         SparseLayout(64, 4, 8, 8, 8, False)
     with pytest.raises(ValueError):
         SparseLayout(64, 100, 8, 8, 8, False, packed=True)
+
+
+def test_windowed_indices_rule():
+    """Config-5 locality rule: sorted distinct records inside one window per supergroup; seeded."""
+    from granulelayer_b200.layout import SparseLayout, windowed_indices
+
+    L = SparseLayout(2048, 5000, 7, 8, 8, False)      # ragged groups: padding slots exist
+    idx = windowed_indices(L, "cpu", window=128, supergroup=512, seed=4)
+    assert idx.shape == L.index_shape and idx.dtype == torch.int16
+    assert torch.equal(idx, windowed_indices(L, "cpu", window=128, supergroup=512, seed=4))
+    assert not torch.equal(idx, windowed_indices(L, "cpu", window=128, supergroup=512, seed=5))
+    counts = L.counts_tensor("cpu")
+    valid = (torch.arange(L.blocks_per_group * 8)[None, :] < counts[:, None]).view(L.groups, L.blocks_per_group, 8)
+    rec = idx[valid].long()
+    assert rec.shape == (5000, 8)
+    assert bool((rec[:, 1:] > rec[:, :-1]).all())
+    assert int(idx[~valid].abs().max()) == 0
+    sg = torch.arange(5000) // 512
+    for s in range(int(sg.max()) + 1):
+        r = rec[sg == s]
+        assert int(r.max()) - int(r.min()) < 128 and int(r.min()) >= 0 and int(r.max()) < 2048
