@@ -98,6 +98,7 @@ class Level1Runtime:
         self.det = False
         self._rowmax = None
         self._rowmax_key = None
+        self._orders: Dict = {}
 
     @property
     def fixed_point(self) -> bool:
@@ -113,6 +114,31 @@ class Level1Runtime:
                                          self.layout.blocks_per_group, 0, self.groups, out)
             self._rowmax, self._rowmax_key = out, key
         return self._rowmax
+
+    def order(self, tokens: int) -> Optional[torch.Tensor]:
+        """Bank-aware processing order for a kernel running token tiles of ``tokens`` (one wavefront
+        serves 32 / tokens neurons; orders are built for 4 and 8), or None for slot order.  Depends
+        only on the indices; recomputed when the index tensor changes."""
+        unit = 32 // tokens if tokens > 0 else 0
+        if self.plan.b200_neuron_order == "identity" or unit not in (4, 8) or self.groups == 0:
+            return None
+        key = (self.idx.data_ptr(), self.idx._version, unit)
+        out = self._orders.get(unit)
+        if out is None or out[0] != key:
+            o = torch.empty((self.groups, self.layout.blocks_per_group * 8), device=self.idx.device,
+                            dtype=torch.int32)
+            _native.group_order(self.idx, self.counts_i32, self.layout.input_dim, self.layout.blocks_per_group, 0,
+                                self.groups, unit, o)
+            out = (key, o)
+            self._orders[unit] = out
+        return out[1]
+
+    def tokens(self, backward: bool) -> int:
+        lib = _native.load()
+        D = self.layout.input_dim
+        if backward:
+            return self.plan.b200_dx_tokens or lib.gl_bwd_auto_tokens(D)
+        return self.plan.b200_fwd_tokens or lib.gl_fwd_auto_tokens(D)
 
     @property
     def groups(self) -> int:
@@ -160,7 +186,8 @@ class Level1Runtime:
         pre = torch.empty((B, self.groups), device=x.device, dtype=torch.float32)
         wabsmax = torch.empty(self.groups, device=x.device, dtype=torch.float32) if B > 0 else None
         _native.fwd(x, self.idx, w, b, self.counts_i32, pre, self.layout.blocks_per_group, 0, self.groups,
-                    self.pool, self.act, tokens=self.plan.b200_fwd_tokens, wabsmax=wabsmax)
+                    self.pool, self.act, tokens=self.plan.b200_fwd_tokens, wabsmax=wabsmax,
+                    order=self.order(self.tokens(False)) if B > 0 else None)
         self.last_info.update(forward_backend="b200", workspace_bytes=0)
         out = {"pre": pre}
         if wabsmax is not None:
@@ -184,7 +211,7 @@ class Level1Runtime:
             rowmax = self.rowmax()
         _native.bwd(x, self.idx, w, b, self.counts_i32, g_pre, dx, dw_buf, db_buf, self.layout.blocks_per_group,
                     0, self.groups, self.pool, self.act, tokens=self.plan.b200_dx_tokens, wabsmax=wabsmax,
-                    rowmax=rowmax)
+                    rowmax=rowmax, order=self.order(self.tokens(True)) if B > 0 else None)
         self.last_info["backward_backend"] = "b200"
         self.last_info["dx_accumulation"] = "int32 fixed point" if wabsmax is not None else "fp32 atomics"
         return dx

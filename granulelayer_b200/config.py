@@ -253,6 +253,12 @@ class PhysicalPlan:
     # block-private dX accumulation of the backward: "fixed" = int32 fixed point (faster; rounding
     # well inside the dX tolerance), "fp32" = fp32 shared-memory atomics, "auto" = "fixed"
     b200_dx_accum: str = "auto"
+    # processing order of each group's neurons: "identity" = slot order (default); "auto" = the
+    # bank-aware order of gl_group_order (computed once per index tensor) where the token tile allows
+    # it.  The bank-aware order halves shared-memory bank conflicts but scatters the parameter-record
+    # loads of a warp step over ~6x more cache lines on the same L1 data path; measured at the
+    # 100M-neuron config it is slower (backward 835 ms vs 755 ms), so it is off by default.
+    b200_neuron_order: str = "identity"
 
     def __post_init__(self):
         if self.input_layout not in ("feature_major", "token_major"):
@@ -275,6 +281,8 @@ class PhysicalPlan:
             raise ValueError("b200_dx_splits must be >= 0")
         if self.b200_dx_accum not in ("auto", "fixed", "fp32"):
             raise ValueError("b200_dx_accum must be 'auto', 'fixed' or 'fp32'")
+        if self.b200_neuron_order not in ("auto", "identity"):
+            raise ValueError("b200_neuron_order must be 'auto' or 'identity'")
 
 
 def resolve_reduction(plan: PhysicalPlan):

@@ -91,6 +91,7 @@ struct BwdParams {
   float* db;
   const float* wabsmax;
   const int32_t* rowmax;
+  const int32_t* order;
   int B, D;
   int64_t NB, g0, g1, ldx, ldg, lddx;
   int pool, gpc;
@@ -150,7 +151,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const BwdParams p) 
       const int s = s0 + nsub;
       const unsigned active = __ballot_sync(kFullMask, s < ng);
       if (s < ng) {
-        const int64_t f = fbase + s;
+        const int slot =
+            p.order != nullptr ? min(max(__ldg(p.order + (g - p.g0) * (int64_t)slots + s), 0), slots - 1) : s;
+        const int64_t f = fbase + slot;
         const Rec8 r = load_rec8(p.idx + f * 8, D - 1);
         const W8 wr = load_w8(p.w + f * 8);
         float z = __ldg(p.bias + f);
@@ -332,7 +335,7 @@ extern "C" int gl_bwd_f32(const GlBwdArgs* args, void* stream) {
     gpc = (int)(want < 1 ? 1 : (want > 8 ? 8 : want));
   }
   while ((G + gpc - 1) / gpc > 65535) gpc *= 2;
-  BwdParams p{a.x, a.idx, a.w, a.b, a.counts, a.gpre, a.dx, a.dw, a.db, a.wabsmax, a.rowmax, (int)a.B, (int)a.D,
+  BwdParams p{a.x, a.idx, a.w, a.b, a.counts, a.gpre, a.dx, a.dw, a.db, a.wabsmax, a.rowmax, a.order, (int)a.B, (int)a.D,
               a.NB, a.g0, a.g1, a.ldx, a.ldg, a.lddx, a.pool, gpc};
   cudaStream_t st = (cudaStream_t)stream;
   return fixed ? dispatch_tokens_bwd<true>(p, a.B, a.act, T, st) : dispatch_tokens_bwd<false>(p, a.B, a.act, T, st);

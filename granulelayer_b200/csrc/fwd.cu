@@ -31,7 +31,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     fwd_kernel(const float* __restrict__ x, const int16_t* __restrict__ idx, const float* __restrict__ w,
                const float* __restrict__ bias, const int32_t* __restrict__ counts, float* __restrict__ pre,
                int B, int D, int64_t NB, int64_t g0, int64_t g1, int64_t ldx, int64_t ldp, int pool, int gpc,
-               float* __restrict__ wabsmax) {
+               float* __restrict__ wabsmax, const int32_t* __restrict__ order) {
   constexpr int V = T < 4 ? T : 4;   // tokens per lane
   constexpr int LPN = T / V;         // lanes per neuron
   constexpr int NPW = 32 / LPN;      // neurons per warp step
@@ -69,7 +69,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       for (int u = 0; u < UNR; ++u) {
         const int s = s0 + u * NPW + nsub;
         ok[u] = s < ng;
-        const int64_t f = fbase + (ok[u] ? s : 0);
+        int slot = ok[u] ? s : 0;
+        if (order != nullptr && ok[u]) slot = min(max(__ldg(order + (g - g0) * (int64_t)slots + s), 0), slots - 1);
+        const int64_t f = fbase + slot;
         r[u] = load_rec8(idx + f * 8, D - 1);
         wr[u] = load_w8(w + f * 8);
         bb[u] = __ldg(bias + f);
@@ -147,7 +149,7 @@ static int launch_fwd(const GlFwdArgs& a, int gpc, cudaStream_t st) {
   if (tiles > 2147483647LL || chunks > 65535) return GL_ERR_SHAPE;
   dim3 grid((unsigned)tiles, (unsigned)chunks);
   kern<<<grid, kFwdThreads, smem, st>>>(a.x, a.idx, a.w, a.b, a.counts, a.pre, (int)a.B, (int)a.D, a.NB, a.g0,
-                                        a.g1, a.ldx, a.ldp, a.pool, gpc, a.wabsmax);
+                                        a.g1, a.ldx, a.ldp, a.pool, gpc, a.wabsmax, a.order);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_cuda_error(e);
   count_launches(1);

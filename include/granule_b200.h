@@ -44,7 +44,7 @@
 extern "C" {
 #endif
 
-#define GL_ABI_VERSION 3
+#define GL_ABI_VERSION 4
 
 typedef enum GlStatus {
   GL_OK = 0,
@@ -82,6 +82,8 @@ typedef struct GlFwdArgs {
   int32_t groups_per_cta;   /* groups per thread block (0 = automatic) */
   float* wabsmax;           /* optional [g1-g0] output: max |w| over each group's valid slots
                                (the backward's fixed-point bound); NULL = not computed */
+  const int32_t* order;     /* optional [g1-g0, NB*8] processing order (gl_group_order): position p of
+                               group g processes slot order[g-g0][p]; NULL = slot order */
 } GlFwdArgs;
 
 /* Backward: with c1[t, g] = gpre[t, g - g0] / counts[g] (mean) or gpre (sum) and
@@ -116,6 +118,7 @@ typedef struct GlBwdArgs {
   int32_t groups_per_cta;   /* 0 = automatic */
   const float* wabsmax;     /* [g1-g0] max |w| per group (gl_group_absmax_f32), or NULL */
   const int32_t* rowmax;    /* [g1-g0] max records per input feature (gl_group_index_maxcount), or NULL */
+  const int32_t* order;     /* optional processing order, as in GlFwdArgs */
 } GlBwdArgs;
 
 /* Adam(W) step over n fp32 elements, in place (sparse_pooling/optim.py:26-64):
@@ -151,6 +154,15 @@ int gl_group_absmax_f32(const float* w, const int32_t* counts, int64_t NB, int64
                         void* stream);
 int gl_group_index_maxcount(const int16_t* idx, const int32_t* counts, int64_t D, int64_t NB, int64_t g0,
                             int64_t g1, int32_t* out, void* stream);
+
+/* Bank-aware processing order (no counterpart in the reference): out[g-g0][p], p < NB*8, is a
+ * permutation of group g's slots (valid slots first, padding slots in place) such that the
+ * `unit` consecutive positions served by one shared-memory wavefront read rows in distinct bank
+ * groups (row d mod unit) for as many of their 8 inputs as possible.  unit = 32 / token tile:
+ * 4 for the forward's tile of 8, 8 for the backward's tile of 4; 4 and 8 are supported.
+ * Depends only on the indices; callers compute it once per layer. */
+int gl_group_order(const int16_t* idx, const int32_t* counts, int64_t D, int64_t NB, int64_t g0, int64_t g1,
+                   int32_t unit, int32_t* out, void* stream);
 
 /* Compact K16/C16 execution of the Cover-TopK/16 layer, fp32.
  * Replaces the reference's kgen entry points at K = 16 (experimental/kgen/kgen_abi.cu,
