@@ -27,6 +27,10 @@ a bounded slice of the same workload on the host cores (rank 0, N = 1).
 G = 2048 outputs, S = 64, R = 64, batch 512, seed 3): forward + backward through the layer on
 1 GPU, with the forward and backward (dX-carrying) kernels timed separately.
 
+``--workload fwdbwd256`` times BASELINE config 2: the same 100M-neuron layer (seed 1, bias_std 0.1)
+forward + backward at batch 256 through the layer API (no optimizer), forward and backward
+kernels timed separately.
+
 ``--workload locality`` runs BASELINE config 5: a Mode-A layer with D = 16384, N = 100,663,296,
 G = 8192 (seed 4), timed forward-only and forward + backward at batch 1, 32, 256, 1024 and 4096,
 once with the reference's uniform index rule and once with windowed indices (each supergroup of
@@ -372,6 +376,76 @@ def bench_cover16(args, world):
     print(json.dumps(line), flush=True)
 
 
+FB_METRIC = "neuron-samples/s fwd+bwd @100M fan-in-8, B=256 (D=4096, G=4096)"
+
+
+def bench_fwdbwd256(args):
+    """BASELINE config 2 (module docstring); rank 0 only, 1 GPU."""
+    from granulelayer_b200 import SparsePoolingLayer, _native
+
+    Bc = 256
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    lay = SparsePoolingLayer(D, N, G, shared_neurons=None, pooling="mean", dtype=torch.float32, device=dev, seed=1,
+                             bias_std=0.1)
+    lay.enable_main_grad()
+    gen = torch.Generator(device=dev).manual_seed(1)
+    x = torch.randn(Bc, D, device=dev, generator=gen)
+    dy = torch.randn(Bc, G, device=dev, generator=gen)
+    ev = {"fwd": [], "bwd": []}
+    orig = {"fwd": _native.fwd, "bwd": _native.bwd}
+
+    def timed(name):
+        def wrap(*a, **k):
+            s_, e_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s_.record()
+            orig[name](*a, **k)
+            e_.record()
+            ev[name].append((s_, e_))
+        return wrap
+
+    def step():
+        lay(x.detach().requires_grad_(True)).backward(dy)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize(dev)
+    _native.fwd, _native.bwd = timed("fwd"), timed("bwd")
+    n0 = _native.launch_count()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    try:
+        with ClockSampler(dev.index) as clk:
+            start.record()
+            for _ in range(args.steps):
+                step()
+            end.record()
+            torch.cuda.synchronize(dev)
+    finally:
+        _native.fwd, _native.bwd = orig["fwd"], orig["bwd"]
+    launches = _native.launch_count() - n0
+    ms = start.elapsed_time(end) / args.steps
+    fwd_ms = statistics.mean(a.elapsed_time(b) for a, b in ev["fwd"])
+    bwd_ms = statistics.mean(a.elapsed_time(b) for a, b in ev["bwd"])
+    peak, peak_kind = peak_hbm()
+    pass_bytes = param_bytes(N) + gather_bytes(Bc, N)
+    achieved = pass_bytes / (bwd_ms * 1e-3) / 1e9
+    line = {
+        "metric": FB_METRIC, "value": Bc * N / (ms / 1e3), "unit": UNIT, "n_gpus": 1, "steps": args.steps,
+        "warmup": max(3, args.warmup), "ms_per_step": ms, "higher_is_better": True, "scaling": "none",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "100M-neuron fan-in-8 Mode-A fp32 mean-ReLU layer, fwd+bwd at B=256 "
+                               "(BASELINE config 2)", "D": D, "N": N, "G": G, "global_batch": Bc, "seed": 1,
+                   "bias_std": 0.1, "l2": "parameters (5.2 GB) larger than L2"},
+        "hbm_roofline_step_frac": (2 * pass_bytes / (peak * 1e9)) / (ms / 1e3),
+        "fwd_hbm_roofline_frac": (pass_bytes / (peak * 1e9)) / (fwd_ms / 1e3),
+        "roofline": {"bound": "hbm", "kernel": "gl_bwd_f32", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "peak_source": peak_kind, "traffic": None,
+                     "algorithmic_bytes_per_launch": pass_bytes},
+        "kernels_ms": {"fwd": fwd_ms, "bwd": bwd_ms}, "clocks": clk.summary(), "gpu_launches": launches,
+    }
+    print(json.dumps(line), flush=True)
+
+
 LOC_METRIC = ("neuron-samples/s fwd+bwd at B=1024, windowed indices, locality/batch sweep "
               "(D=16384, N=100,663,296, G=8192)")
 
@@ -451,7 +525,7 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ref-seconds", type=float, default=4.0)
-    ap.add_argument("--workload", default="layer100m", choices=["layer100m", "cover16", "locality"])
+    ap.add_argument("--workload", default="layer100m", choices=["layer100m", "fwdbwd256", "cover16", "locality"])
     ap.add_argument("--batches", default="1,32,256,1024,4096", help="locality: batch sizes of the sweep")
     ap.add_argument("--cover-outputs", type=int, default=2048,
                     help="cover16: outputs of 24,576 neurons (default 2048 = config 4; fewer for ncu captures)")
@@ -474,6 +548,10 @@ def main():
     if args.workload == "locality":
         if rank == 0:
             bench_locality(args)
+        return
+    if args.workload == "fwdbwd256":
+        if rank == 0:
+            bench_fwdbwd256(args)
         return
     if args.impl == "reference":
         run_reference(args, rank, world)
