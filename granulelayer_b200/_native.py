@@ -16,7 +16,7 @@ from pathlib import Path
 
 import torch
 
-ABI_VERSION = 4
+ABI_VERSION = 5
 LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libgranule_b200.so"
 
 POOL_MEAN, POOL_SUM = 0, 1
@@ -25,7 +25,8 @@ ACT_IDS = {"identity": 0, "relu": 1, "gelu": 2}
 # The exported entry points, in header order (checked by the CPU test suite).
 EXPORTS = ("gl_abi_version", "gl_status_string", "gl_last_cuda_error", "gl_fwd_f32", "gl_bwd_f32",
            "gl_adam_f32", "gl_group_absmax_f32", "gl_group_index_maxcount", "gl_group_order", "gl_launch_count",
-           "gl_fwd_auto_tokens", "gl_bwd_auto_tokens", "gl_k16_fwd_f32", "gl_k16_bwd_f32", "gl_k16_auto_tokens")
+           "gl_fwd_auto_tokens", "gl_bwd_auto_tokens", "gl_fwd_shared_f32", "gl_bwd_shared_f32",
+           "gl_shared_auto_tokens", "gl_k16_fwd_f32", "gl_k16_bwd_f32", "gl_k16_auto_tokens")
 
 
 class NativeLibraryError(RuntimeError):
@@ -59,6 +60,12 @@ class GlAdamArgs(ctypes.Structure):
                 ("lr", ctypes.c_float), ("beta1", ctypes.c_float), ("beta2", ctypes.c_float),
                 ("eps", ctypes.c_float), ("weight_decay", ctypes.c_float), ("bc1", ctypes.c_float),
                 ("bc2", ctypes.c_float), ("zero_grad", ctypes.c_int32)]
+
+
+class GlSharedArgs(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_void_p) for n in ("x", "idx", "w", "b", "counts", "pre", "gpre", "dx", "dw", "db")] + \
+               [(n, ctypes.c_int64) for n in ("B", "D", "NB", "C", "g0", "g1", "ldx", "ldp", "ldg", "lddx")] + \
+               [(n, ctypes.c_int32) for n in ("pool", "act", "packed", "tokens", "groups_per_cta", "reserved")]
 
 
 class GlK16Args(ctypes.Structure):
@@ -95,7 +102,8 @@ def load(path=None) -> ctypes.CDLL:
         lib.gl_last_cuda_error.restype = ctypes.c_int
         lib.gl_launch_count.restype = ctypes.c_int64
         for name, st in (("gl_fwd_f32", GlFwdArgs), ("gl_bwd_f32", GlBwdArgs), ("gl_adam_f32", GlAdamArgs),
-                         ("gl_k16_fwd_f32", GlK16Args), ("gl_k16_bwd_f32", GlK16Args)):
+                         ("gl_k16_fwd_f32", GlK16Args), ("gl_k16_bwd_f32", GlK16Args),
+                         ("gl_fwd_shared_f32", GlSharedArgs), ("gl_bwd_shared_f32", GlSharedArgs)):
             fn = getattr(lib, name)
             fn.restype = ctypes.c_int
             fn.argtypes = [ctypes.POINTER(st), ctypes.c_void_p]
@@ -112,6 +120,8 @@ def load(path=None) -> ctypes.CDLL:
         lib.gl_group_order.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
                                        ctypes.c_int64, ctypes.c_int64, ctypes.c_int32, ctypes.c_void_p,
                                        ctypes.c_void_p]
+        lib.gl_shared_auto_tokens.restype = ctypes.c_int
+        lib.gl_shared_auto_tokens.argtypes = [ctypes.c_int64, ctypes.c_int32]
         lib.gl_k16_auto_tokens.restype = ctypes.c_int
         lib.gl_k16_auto_tokens.argtypes = [ctypes.c_int64, ctypes.c_int64, ctypes.c_int32]
         if path is None:
@@ -169,6 +179,37 @@ def bwd(x, idx, w, b, counts, gpre, dx, dw, db, NB: int, g0: int, g1: int, pool:
                   tokens, groups_per_cta, _ptr(wabsmax), _ptr(rowmax), _ptr(order))
     with torch.cuda.device(x.device):
         _check(lib, lib.gl_bwd_f32(ctypes.byref(a), _stream(x.device)), "gl_bwd_f32")
+
+
+def _shared_args(x, idx, w, b, counts, NB, C, g0, g1, pool, act, packed, tokens, groups_per_cta):
+    a = GlSharedArgs()
+    a.x, a.idx, a.w, a.b, a.counts = _ptr(x), _ptr(idx), _ptr(w), _ptr(b), _ptr(counts)
+    a.B, a.D, a.NB, a.C, a.g0, a.g1, a.ldx = x.shape[0], x.shape[1], NB, C, g0, g1, x.stride(0)
+    a.pool, a.act, a.packed, a.tokens, a.groups_per_cta = pool, act, int(bool(packed)), tokens, groups_per_cta
+    return a
+
+
+def fwd_shared(x, idx, w, b, counts, pre, NB: int, C: int, g0: int, g1: int, pool: int, act: int, packed: bool,
+               tokens: int = 0, groups_per_cta: int = 0):
+    """Mode B forward: pre[:, :g1-g0] = pooled act(z) (GlSharedArgs)."""
+    _require_cuda(x, idx, w, b, counts, pre)
+    lib = load()
+    a = _shared_args(x, idx, w, b, counts, NB, C, g0, g1, pool, act, packed, tokens, groups_per_cta)
+    a.pre, a.ldp = _ptr(pre), pre.stride(0)
+    with torch.cuda.device(x.device):
+        _check(lib, lib.gl_fwd_shared_f32(ctypes.byref(a), _stream(x.device)), "gl_fwd_shared_f32")
+
+
+def bwd_shared(x, idx, w, b, counts, gpre, dx, dw, db, NB: int, C: int, g0: int, g1: int, pool: int, act: int,
+               packed: bool, tokens: int = 0, groups_per_cta: int = 0):
+    """Mode B backward: dx, dw, db += gradients for dL/dpre ``gpre`` (GlSharedArgs)."""
+    _require_cuda(x, idx, w, b, counts, gpre, dx, dw, db)
+    lib = load()
+    a = _shared_args(x, idx, w, b, counts, NB, C, g0, g1, pool, act, packed, tokens, groups_per_cta)
+    a.gpre, a.dx, a.dw, a.db = _ptr(gpre), _ptr(dx), _ptr(dw), _ptr(db)
+    a.ldg, a.lddx = gpre.stride(0), dx.stride(0)
+    with torch.cuda.device(x.device):
+        _check(lib, lib.gl_bwd_shared_f32(ctypes.byref(a), _stream(x.device)), "gl_bwd_shared_f32")
 
 
 def group_absmax(w, counts, NB: int, g0: int, g1: int, out):

@@ -63,8 +63,8 @@ class UnsupportedOnB200(NotImplementedError):
 
 
 def check_supported(layout: SparseLayout, level: LevelSpec, dtype: torch.dtype):
-    if layout.shared_indices or layout.block != 8:
-        raise UnsupportedOnB200("the B200 kernels run Mode A (shared_neurons=None): independent indices per neuron")
+    if not layout.shared_indices and layout.block != 8:
+        raise UnsupportedOnB200("Mode A layers store blocks of 8 neurons")
     if level.type not in B200_POOLS:
         raise UnsupportedOnB200(f"pooling {level.type!r} is not on the B200 path (supported: {B200_POOLS})")
     if level.neurons_per_shard is not None:
@@ -169,6 +169,18 @@ class Level1Runtime:
     def describe_execution(self, B: int) -> Dict:
         lib = _native.load()
         D = self.layout.input_dim
+        if self.layout.shared_indices:
+            return {
+                "backend": "b200",
+                "library": str(_native.library_path()),
+                "mode": f"B (C={self.layout.block}, {'packed' if self.layout.packed else 'canonical'})",
+                "forward": {"kernel": "gl_fwd_shared_f32",
+                            "tokens": self.plan.b200_fwd_tokens or lib.gl_shared_auto_tokens(D, 0)},
+                "backward": {"kernel": "gl_bwd_shared_f32",
+                             "tokens": self.plan.b200_dx_tokens or lib.gl_shared_auto_tokens(D, 1)},
+                "optimizer": {"kernel": "gl_adam_f32"},
+                "batch": B,
+            }
         return {
             "backend": "b200",
             "library": str(_native.library_path()),
@@ -184,6 +196,12 @@ class Level1Runtime:
         self.check_devices(x, w, b)
         self.resolve_reduction(B)
         pre = torch.empty((B, self.groups), device=x.device, dtype=torch.float32)
+        if self.layout.shared_indices:
+            _native.fwd_shared(x, self.idx, w, b, self.counts_i32, pre, self.layout.blocks_per_group,
+                               self.layout.block, 0, self.groups, self.pool, self.act, self.layout.packed,
+                               tokens=self.plan.b200_fwd_tokens)
+            self.last_info.update(forward_backend="b200", forward_kernel="gl_fwd_shared_f32", workspace_bytes=0)
+            return {"pre": pre}
         wabsmax = torch.empty(self.groups, device=x.device, dtype=torch.float32) if B > 0 else None
         _native.fwd(x, self.idx, w, b, self.counts_i32, pre, self.layout.blocks_per_group, 0, self.groups,
                     self.pool, self.act, tokens=self.plan.b200_fwd_tokens, wabsmax=wabsmax,
@@ -202,6 +220,13 @@ class Level1Runtime:
         self.check_devices(x, w, b, g_pre, dw_buf, db_buf)
         self.resolve_reduction(B)
         dx = torch.zeros((B, D), device=x.device, dtype=torch.float32)
+        if self.layout.shared_indices:
+            _native.bwd_shared(x, self.idx, w, b, self.counts_i32, g_pre, dx, dw_buf, db_buf,
+                               self.layout.blocks_per_group, self.layout.block, 0, self.groups, self.pool, self.act,
+                               self.layout.packed, tokens=self.plan.b200_dx_tokens)
+            self.last_info["backward_backend"] = "b200"
+            self.last_info["dx_accumulation"] = "fp32 shared-memory reductions (Mode B)"
+            return dx
         wabsmax = rowmax = None
         if self.fixed_point and B > 0:
             wabsmax = saved.get("wabsmax")

@@ -44,7 +44,7 @@
 extern "C" {
 #endif
 
-#define GL_ABI_VERSION 4
+#define GL_ABI_VERSION 5
 
 typedef enum GlStatus {
   GL_OK = 0,
@@ -163,6 +163,43 @@ int gl_group_index_maxcount(const int16_t* idx, const int32_t* counts, int64_t D
  * Depends only on the indices; callers compute it once per layer. */
 int gl_group_order(const int16_t* idx, const int32_t* counts, int64_t D, int64_t NB, int64_t g0, int64_t g1,
                    int32_t unit, int32_t* out, void* stream);
+
+/* Mode B (shared index records), fp32.  Block j of group g holds C neurons (C = 8, 16, 32 or 64)
+ * sharing one 8-input record; slot s = j*C + c is valid iff s < counts[g]:
+ *   z[t, g, j, c] = b[g][j][c] + sum_k w[g][j][c][k] * x[t, idx[g][j][k]]
+ * Storage is the reference's (sparse_pooling/layout.py:20-33, 123-179), canonical
+ *   idx [G, NB, 8] int16, w [G, NB, C, 8] f32, b [G, NB, C] f32,
+ * or fragment-packed (packed != 0), read in place.  Forward writes pre[t, g - g0] as
+ * gl_fwd_f32 does; backward accumulates dx, dw, db (dw/db in the storage layout) as gl_bwd_f32
+ * does, with fp32 shared-memory reductions.
+ * Replaces the reference's Mode-B CUDA kernels (kernels/cuda/sparse_pool_fwd.cuh:311,
+ * sparse_pool_bwd.cuh:387-876; entries sparse_pool.cu:12-44) for fp32 parameters. */
+typedef struct GlSharedArgs {
+  const float* x;           /* [B, ldx] */
+  const int16_t* idx;       /* 16-byte aligned */
+  const float* w;           /* 16-byte aligned */
+  const float* b;           /* 16-byte aligned */
+  const int32_t* counts;    /* [G_total] */
+  float* pre;               /* forward: [B, ldp] */
+  const float* gpre;        /* backward: [B, ldg] dL/dpre */
+  float* dx;                /* backward: [B, lddx], accumulated */
+  float* dw;                /* backward: weight-shaped, accumulated, 16-byte aligned */
+  float* db;                /* backward: bias-shaped, accumulated, 16-byte aligned */
+  int64_t B, D, NB, C;      /* tokens, input features, blocks per group, neurons per block */
+  int64_t g0, g1;
+  int64_t ldx, ldp, ldg, lddx;
+  int32_t pool;             /* GL_POOL_* */
+  int32_t act;              /* GL_ACT_* */
+  int32_t packed;           /* 0 = canonical storage, 1 = fragment-packed */
+  int32_t tokens;           /* token tile (0 = automatic; else 1, 2, 4 or 8) */
+  int32_t groups_per_cta;   /* 0 = automatic */
+  int32_t reserved;         /* 0 */
+} GlSharedArgs;
+
+int gl_fwd_shared_f32(const GlSharedArgs* args, void* stream);
+int gl_bwd_shared_f32(const GlSharedArgs* args, void* stream);
+/* Token tile the automatic choice would use for input_dim D, or a negative status. */
+int gl_shared_auto_tokens(int64_t D, int32_t backward);
 
 /* Compact K16/C16 execution of the Cover-TopK/16 layer, fp32.
  * Replaces the reference's kgen entry points at K = 16 (experimental/kgen/kgen_abi.cu,

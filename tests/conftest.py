@@ -59,7 +59,31 @@ def load_case(name):
 
 
 def case_names():
-    return sorted(p.stem[len("fwdbwd_"):] for p in GOLDEN.glob("fwdbwd_*.npz"))
+    """Mode-A golden cases."""
+    return sorted(p.stem[len("fwdbwd_"):] for p in GOLDEN.glob("fwdbwd_*.npz") if not p.stem.startswith("fwdbwd_modeb_"))
+
+
+def modeb_case_names():
+    """Mode-B golden cases (shared index records, canonical or fragment-packed storage)."""
+    return sorted(p.stem[len("fwdbwd_"):] for p in GOLDEN.glob("fwdbwd_modeb_*.npz"))
+
+
+def modeb_case_params(meta):
+    """(layout, idx, w, b) of a Mode-B golden case in the layer's storage layout, from the seeded init."""
+    from granulelayer_b200.layout import SparseLayout, init_parameters
+
+    L = SparseLayout(meta["D"], meta["H"], meta["G"], 8, meta["C"], True, packed=meta["packed"])
+    idx, w, b = init_parameters(L, "cpu", dtype=torch.float32, seed=meta["seed"], bias_std=meta["bias_std"])
+    return L, idx, w, b
+
+
+def modeb_as_mode_a(L, idx, w, b):
+    """A Mode-B layer written as the equivalent Mode-A tensors (each block's index record repeated
+    for its C neurons; C-neuron blocks split into blocks of 8) for the Mode-A oracle."""
+    idx, w, b = L.to_canonical(idx, w, b)
+    G, NB, C = L.groups, L.blocks_per_group, L.block
+    ia = idx[:, :, None, :].expand(G, NB, C, 8).reshape(G, NB * C // 8, 8, 8).contiguous()
+    return ia, w.reshape(G, NB * C // 8, 8, 8).contiguous(), b.reshape(G, NB * C // 8, 8).contiguous()
 
 
 def case_params(meta, arrays):

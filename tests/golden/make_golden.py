@@ -18,6 +18,10 @@ What it writes (all from the reference's own code on the CPU):
   ``hidden_preactivations`` + activation + masked sum (the reference has no
   sum operator).  One case draws indices uniformly with replacement
   (duplicate indices inside a neuron).
+* ``fwdbwd_modeb_<case>.npz`` — Mode-B layers (shared index records, canonical and
+  fragment-packed storage) rebuilt from seeds, with the reference's float64
+  ``reference_forward`` output and autograd gradients (dw/db in the layer's own
+  storage layout, first groups only).
 * ``graph_hashes.json`` — sha256 of the reference's input-supergroup graphs: Mode-B
   ``supergroups.generate_indices`` (indices, feature sets, buckets) and the generalized
   ``experimental/kgen_graph.generate`` (K = 64 / C = 256 envelope, K = 16 / C = 16).
@@ -53,6 +57,15 @@ CASES = [
     ("gelu_mean", 64, 3000, 8, 16, 4, 0.2, "mean", "gelu", "distinct"),
     ("sum_identity_ragged", 96, 1001, 7, 5, 5, 0.1, "sum", "identity", "distinct"),
     ("uniform_dup_idx", 32, 2048, 8, 24, 6, 0.1, "mean", "relu", "uniform"),
+]
+
+# Mode B (C neurons share one index record): (name, D, H, G, C, packed, B, seed, bias_std, pooling, activation)
+MODEB_CASES = [
+    ("modeb_c8", 256, 65536, 256, 8, False, 64, 5, 0.1, "mean", "relu"),
+    ("modeb_c64_packed_ragged", 512, 20000, 7, 64, True, 37, 6, 0.2, "mean", "relu"),
+    ("modeb_c16_gelu", 300, 5000, 3, 16, False, 19, 7, 0.2, "mean", "gelu"),
+    ("modeb_c32_packed_sum", 1024, 12288, 4, 32, True, 9, 8, 0.1, "sum", "relu"),
+    ("modeb_c8_packed_identity", 128, 3001, 5, 8, True, 1, 9, 0.3, "mean", "identity"),
 ]
 
 # (D, H, G, C, S, R, generation, seed): Mode-B input-supergroup graphs
@@ -144,6 +157,29 @@ def main():
             idx=idx.numpy() if rule == "uniform" else np.zeros(0, np.int16),
             x=x.numpy(), dy=dy.numpy(), y=y.detach().float().numpy(), dx=xd.grad.float().numpy(),
             dw=wd.grad[:GSUB].float().numpy(), db=bd.grad[:GSUB].float().numpy())
+
+    for name, D, H, G, C, packed, B, seed, bstd, pool, act in MODEB_CASES:
+        L = SparseLayout(D, H, G, 8, C, True, packed=packed)
+        idx, w, b = init_parameters(L, "cpu", dtype=torch.float32, seed=seed, bias_std=bstd)
+        gen = torch.Generator().manual_seed(2000 + seed)
+        x = torch.randn(B, D, generator=gen)
+        xd = x.double().requires_grad_(True)
+        wd = w.double().requires_grad_(True)
+        bd = b.double().requires_grad_(True)
+        if pool == "mean":
+            y = ref.reference_forward(xd, idx, wd, bd, L, PoolingConfig([LevelSpec("mean", activation=act)]))
+        else:
+            z = ref.hidden_preactivations(xd, idx, wd, bd, L)
+            y = torch.where(L.canonical.valid_mask("cpu")[None], ref.activation(z, act), torch.zeros_like(z)).sum(-1)
+        dy = torch.randn(y.shape, generator=gen)
+        (y * dy.double()).sum().backward()
+        np.savez_compressed(
+            HERE / f"fwdbwd_{name}.npz",
+            meta=json.dumps(dict(name=name, D=D, H=H, G=G, C=C, packed=packed, B=B, seed=seed, bias_std=bstd,
+                                 pool=pool, act=act, rule="distinct", mode="B", idx_sha=sha(idx), w_sha=sha(w),
+                                 b_sha=sha(b))),
+            idx=np.zeros(0, np.int16), x=x.numpy(), dy=dy.numpy(), y=y.detach().float().numpy(),
+            dx=xd.grad.float().numpy(), dw=wd.grad[:GSUB].float().numpy(), db=bd.grad[:GSUB].float().numpy())
 
     # input-supergroup graphs (supergroups.py generate_indices; kgen_graph.py generate)
     from sparse_pooling.experimental import kgen_graph as KG

@@ -56,6 +56,14 @@ def test_argument_validation_needs_no_device():
     assert lib.gl_adam_f32(ctypes.byref(ad), None) == -2
     ad.n = 0
     assert lib.gl_adam_f32(ctypes.byref(ad), None) == 0
+    assert lib.gl_fwd_shared_f32(None, None) == -1
+    sa = _native.GlSharedArgs()
+    sa.B, sa.D, sa.NB, sa.C, sa.g0, sa.g1 = 4, 64, 4, 12, 0, 1   # C must be 8, 16, 32 or 64
+    assert lib.gl_fwd_shared_f32(ctypes.byref(sa), None) == -2
+    sa.C = 8
+    assert lib.gl_bwd_shared_f32(ctypes.byref(sa), None) == -1  # null pointers
+    sa.B = 0
+    assert lib.gl_fwd_shared_f32(ctypes.byref(sa), None) == 0   # empty batch: a no-op
     assert lib.gl_k16_fwd_f32(None, None) == -1
     assert lib.gl_k16_bwd_f32(None, None) == -1
     k = _native.GlK16Args()
@@ -74,6 +82,7 @@ def test_struct_layout_matches_header():
     assert ctypes.sizeof(_native.GlBwdArgs) == 9 * 8 + 8 * 8 + 4 * 4 + 3 * 8
     assert ctypes.sizeof(_native.GlAdamArgs) == 4 * 8 + 8 + 8 * 4
     assert ctypes.sizeof(_native.GlK16Args) == 14 * 8 + 11 * 8 + 2 * 4
+    assert ctypes.sizeof(_native.GlSharedArgs) == 10 * 8 + 10 * 8 + 6 * 4
 
 
 def test_missing_library_fails_loudly(tmp_path):

@@ -30,7 +30,14 @@ def test_cpu_forward_has_no_fallback():
         lay(torch.randn(4, 64))
 
 
-@pytest.mark.parametrize("kw", [dict(shared_neurons=8), dict(pooling="max"), dict(dtype=torch.bfloat16),
+@pytest.mark.parametrize("kw", [dict(shared_neurons=8), dict(shared_neurons=64, weight_layout="canonical")])
+def test_mode_b_cpu_forward_has_no_fallback(kw):
+    lay = _layer(**kw)
+    with pytest.raises(NativeLibraryError):
+        lay(torch.randn(2, 64))
+
+
+@pytest.mark.parametrize("kw", [dict(pooling="max"), dict(dtype=torch.bfloat16),
                                 dict(pooling={"levels": [{"type": "mean", "neurons_per_shard": 128},
                                                          {"type": "weighted_sum"}]})])
 def test_unsupported_configurations_raise(kw):

@@ -5,7 +5,7 @@ import numpy as np
 import pytest
 import torch
 
-from conftest import GOLDEN, assert_close, case_names, case_params, load_case
+from conftest import GOLDEN, assert_close, case_names, case_params, load_case, modeb_as_mode_a, modeb_case_names, modeb_case_params
 from oracle import oracle as O
 
 
@@ -51,3 +51,31 @@ def test_oracle_sum_is_n_times_mean():
     m = O.forward(arr["x"], idx.numpy(), w.numpy(), b.numpy(), c, "mean", "relu")
     s = O.forward(arr["x"], idx.numpy(), w.numpy(), b.numpy(), c, "sum", "relu")
     np.testing.assert_allclose(s, m * c[None, :], rtol=1e-12)
+
+
+@pytest.mark.parametrize("name", modeb_case_names())
+def test_oracle_matches_reference_mode_b(name):
+    """Mode B (shared index records, canonical and fragment-packed storage): the oracle on the
+    equivalent Mode-A tensors reproduces the reference's float64 outputs and gradients."""
+    import hashlib
+
+    meta, arr = load_case(name)
+    L, idx, w, b = modeb_case_params(meta)
+    assert hashlib.sha256(idx.numpy().tobytes()).hexdigest() == meta["idx_sha"]
+    assert hashlib.sha256(w.numpy().tobytes()).hexdigest() == meta["w_sha"]
+    ia, wa, ba = modeb_as_mode_a(L, idx, w, b)
+    counts = L.counts_tensor("cpu").numpy()
+    pre = O.forward(arr["x"], ia.numpy(), wa.numpy(), ba.numpy(), counts, meta["pool"], meta["act"])
+    assert_close(pre, arr["y"], 2e-6, 1e-7, "y")
+    dx, dw, db = O.backward(arr["x"], ia.numpy(), wa.numpy(), ba.numpy(), counts, arr["dy"], meta["pool"],
+                            meta["act"])
+    assert_close(dx, arr["dx"], 2e-6, 1e-7, "dx")
+    # back to the layer's storage layout
+    C = L.block
+    dwc = torch.from_numpy(dw).reshape(L.groups, L.blocks_per_group, C, 8)
+    dbc = torch.from_numpy(db).reshape(L.groups, L.blocks_per_group, C)
+    if L.packed:
+        dwc, dbc = L.pack_weights(dwc), L.pack_bias(dbc)
+    gs = arr["dw"].shape[0]
+    assert_close(dwc[:gs], arr["dw"], 2e-6, 1e-7, "dw")
+    assert_close(dbc[:gs], arr["db"], 2e-6, 1e-7, "db")
