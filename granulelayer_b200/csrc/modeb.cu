@@ -27,7 +27,7 @@
 
 namespace gl {
 
-constexpr int kMbFwdThreads = 512;
+constexpr int kMbFwdThreads = 384;
 constexpr int kMbBwdThreads = 256;
 
 struct MbParams {
@@ -119,6 +119,35 @@ __device__ __forceinline__ void mb_load_w4(const MbParams& p, int64_t g, int j, 
   }
 }
 
+// Row strides of the shared tiles.  Rows of 32 or more bytes start every row on the same banks
+// when the stride is a multiple of 32 floats; the x tile pads rows by 4 floats (keeping the
+// 16-byte alignment of its vector reads) and the dX tile by 1 float (scalar atomics), so that
+// different rows read or add at different banks.
+template <int T>
+__host__ __device__ constexpr int mb_xld() { return T >= 8 ? T + 4 : T; }
+template <int T>
+__host__ __device__ constexpr int mb_dld() { return T >= 4 ? T + 1 : T; }
+
+// Stage x[t0 .. t0+T-1, :] into xs[d * LD + t] (tokens >= B read as 0): one thread per feature.
+template <int T, int LD, int NTHREADS>
+__device__ __forceinline__ void mb_stage(float* __restrict__ xs, const float* __restrict__ x, int t0, int B, int D,
+                                         int64_t ldx) {
+  for (int d = threadIdx.x; d < D; d += NTHREADS) {
+    float v[T];
+#pragma unroll
+    for (int t = 0; t < T; ++t) v[t] = (t0 + t < B) ? __ldg(x + (int64_t)(t0 + t) * ldx + d) : 0.f;
+    float* row = xs + (int64_t)d * LD;
+    if constexpr (T >= 4) {
+#pragma unroll
+      for (int q = 0; q < T / 4; ++q)
+        reinterpret_cast<float4*>(row)[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+    } else {
+#pragma unroll
+      for (int t = 0; t < T; ++t) row[t] = v[t];
+    }
+  }
+}
+
 // T consecutive floats of an xs row.
 template <int T>
 __device__ __forceinline__ void mb_row(const float* __restrict__ row, float (&v)[T]) {
@@ -139,11 +168,13 @@ __device__ __forceinline__ void mb_row(const float* __restrict__ row, float (&v)
 template <int T, int ACT, bool PACKED>
 __global__ void __launch_bounds__(kMbFwdThreads, 1) mb_fwd_kernel(const MbParams p) {
   constexpr int NW = kMbFwdThreads / 32;
+  constexpr int TS = T < 8 ? T : 8;  // tokens per sub-chunk (registers per lane stay fixed as T grows)
   extern __shared__ __align__(16) float xs[];
   __shared__ float red[NW][T];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int t0 = blockIdx.x * T;
-  stage_tile<T, kMbFwdThreads>(xs, p.x, t0, p.B, p.D, p.ldx);
+  constexpr int XLD = mb_xld<T>();
+  mb_stage<T, XLD, kMbFwdThreads>(xs, p.x, t0, p.B, p.D, p.ldx);
   __syncthreads();
   const int C = p.C, LPR = 1 << p.lgLPR, RPW = 32 >> p.lgLPR;
   const int r = lane >> p.lgLPR, nq = lane & (LPR - 1);
@@ -164,25 +195,28 @@ __global__ void __launch_bounds__(kMbFwdThreads, 1) mb_fwd_kernel(const MbParams
       float w[4][8], bb[4];
       mb_load_w4<PACKED>(p, g, jj, nq * 4, w, bb);
       const int nv = okr ? min(max(ng - (j * C + nq * 4), 0), 4) : 0;
-      float z[4][T];
 #pragma unroll
-      for (int n = 0; n < 4; ++n)
-#pragma unroll
-        for (int t = 0; t < T; ++t) z[n][t] = bb[n];
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        float v[T];
-        mb_row<T>(xs + rec.i[k] * T, v);
+      for (int tc = 0; tc < T; tc += TS) {
+        float z[4][TS];
 #pragma unroll
         for (int n = 0; n < 4; ++n)
 #pragma unroll
-          for (int t = 0; t < T; ++t) z[n][t] = fmaf(w[n][k], v[t], z[n][t]);
+          for (int t = 0; t < TS; ++t) z[n][t] = bb[n];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          float v[TS];
+          mb_row<TS>(xs + rec.i[k] * XLD + tc, v);
+#pragma unroll
+          for (int n = 0; n < 4; ++n)
+#pragma unroll
+            for (int t = 0; t < TS; ++t) z[n][t] = fmaf(w[n][k], v[t], z[n][t]);
+        }
+#pragma unroll
+        for (int n = 0; n < 4; ++n)
+          if (n < nv)
+#pragma unroll
+            for (int t = 0; t < TS; ++t) acc[tc + t] += act_f<ACT>(z[n][t]);
       }
-#pragma unroll
-      for (int n = 0; n < 4; ++n)
-        if (n < nv)
-#pragma unroll
-          for (int t = 0; t < T; ++t) acc[t] += act_f<ACT>(z[n][t]);
     }
 #pragma unroll
     for (int off = 16; off; off >>= 1)
@@ -206,14 +240,16 @@ __global__ void __launch_bounds__(kMbFwdThreads, 1) mb_fwd_kernel(const MbParams
 template <int T, int ACT, bool PACKED>
 __global__ void __launch_bounds__(kMbBwdThreads, 1) mb_bwd_kernel(const MbParams p) {
   constexpr int NW = kMbBwdThreads / 32;
-  constexpr int V = 8 * T;  // dX partials per lane: (k, t), index k*T + t
+  constexpr int TS = T < 4 ? T : 4;  // tokens per sub-chunk
+  constexpr int V = 8 * TS;          // dX partials per lane and sub-chunk: (k, t), index k*TS + t
   extern __shared__ __align__(16) float smem[];
   float* xs = smem;
-  float* dxs = smem + (((size_t)p.D * T + 3) & ~(size_t)3);
+  constexpr int XLD = mb_xld<T>(), DLD = mb_dld<T>();
+  float* dxs = smem + (((size_t)p.D * XLD + 3) & ~(size_t)3);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int t0 = blockIdx.x * T;
-  stage_tile<T, kMbBwdThreads>(xs, p.x, t0, p.B, p.D, p.ldx);
-  for (int e = threadIdx.x; e < p.D * T; e += kMbBwdThreads) dxs[e] = 0.f;
+  mb_stage<T, XLD, kMbBwdThreads>(xs, p.x, t0, p.B, p.D, p.ldx);
+  for (int e = threadIdx.x; e < p.D * DLD; e += kMbBwdThreads) dxs[e] = 0.f;
   __syncthreads();
   const int C = p.C, LPR = 1 << p.lgLPR, RPW = 32 >> p.lgLPR;
   const int r = lane >> p.lgLPR, nq = lane & (LPR - 1);
@@ -237,99 +273,98 @@ __global__ void __launch_bounds__(kMbBwdThreads, 1) mb_bwd_kernel(const MbParams
       float w[4][8], bb[4];
       mb_load_w4<PACKED>(p, g, jj, nq * 4, w, bb);
       const int nv = okr ? min(max(ng - (j * C + nq * 4), 0), 4) : 0;
-      float xv[8][T];
-#pragma unroll
-      for (int k = 0; k < 8; ++k) mb_row<T>(xs + rec.i[k] * T, xv[k]);
-      float dz[4][T];
+      float dwacc[4][8], dbacc[4];
 #pragma unroll
       for (int n = 0; n < 4; ++n) {
+        dbacc[n] = 0.f;
 #pragma unroll
-        for (int t = 0; t < T; ++t) {
-          float z = bb[n];
+        for (int k = 0; k < 8; ++k) dwacc[n][k] = 0.f;
+      }
 #pragma unroll
-          for (int k = 0; k < 8; ++k) z = fmaf(w[n][k], xv[k][t], z);
-          dz[n][t] = n < nv ? c1[t] * dact_f<ACT>(z) : 0.f;
+      for (int tc = 0; tc < T; tc += TS) {
+        float xv[8][TS];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) mb_row<TS>(xs + rec.i[k] * XLD + tc, xv[k]);
+        float dz[4][TS];
+#pragma unroll
+        for (int n = 0; n < 4; ++n) {
+#pragma unroll
+          for (int t = 0; t < TS; ++t) {
+            float z = bb[n];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) z = fmaf(w[n][k], xv[k][t], z);
+            dz[n][t] = n < nv ? c1[tc + t] * dact_f<ACT>(z) : 0.f;
+            dbacc[n] += dz[n][t];
+          }
+#pragma unroll
+          for (int k = 0; k < 8; ++k)
+#pragma unroll
+            for (int t = 0; t < TS; ++t) dwacc[n][k] = fmaf(dz[n][t], xv[k][t], dwacc[n][k]);
+        }
+        // dX partials of the quad, then a transpose-reduction over the record's LPR lanes
+        float a[V];
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+#pragma unroll
+          for (int t = 0; t < TS; ++t) {
+            float sum = 0.f;
+#pragma unroll
+            for (int n = 0; n < 4; ++n) sum = fmaf(dz[n][t], w[n][k], sum);
+            a[k * TS + t] = sum;
+          }
+        int vbase = 0;      // first partial index this lane holds
+        bool writer = true; // false on the upper lane of a plain (non-transposing) butterfly stage
+#pragma unroll
+        for (int s = 0; s < 4; ++s) {
+          const int width = V >> s;  // a compile-time constant once the loop is unrolled
+          if (s < p.lgLPR) {
+            const bool hi = (nq >> s) & 1;
+            if (width > 1) {
+#pragma unroll
+              for (int i = 0; i < width / 2; ++i) {
+                const float keep = hi ? a[i + width / 2] : a[i];
+                const float send = hi ? a[i] : a[i + width / 2];
+                a[i] = keep + __shfl_xor_sync(kFullMask, send, 1 << s);
+              }
+              if (hi) vbase += width / 2;
+            } else {
+              a[0] += __shfl_xor_sync(kFullMask, a[0], 1 << s);
+              if (hi) writer = false;
+            }
+          }
+        }
+        const int held = max(V >> p.lgLPR, 1);
+        if (okr && writer) {
+#pragma unroll
+          for (int i = 0; i < V; ++i) {
+            if (i < held) {
+              const int v = vbase + i, k = v / TS, t = v - k * TS;
+              int row = rec.i[0];  // rec.i[k] through selects: a dynamic index would place rec in local memory
+#pragma unroll
+              for (int q = 1; q < 8; ++q) row = k == q ? rec.i[q] : row;
+              atomicAdd(&dxs[row * DLD + tc + t], a[i]);
+            }
+          }
         }
       }
       if (nv > 0) {
-        // dW, db of the lane's 4 neurons, summed over the tile's tokens
-        float dwv[4][8], dbv[4];
-#pragma unroll
-        for (int n = 0; n < 4; ++n) {
-          dbv[n] = 0.f;
-#pragma unroll
-          for (int t = 0; t < T; ++t) dbv[n] += dz[n][t];
-#pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            float s = 0.f;
-#pragma unroll
-            for (int t = 0; t < T; ++t) s = fmaf(dz[n][t], xv[k][t], s);
-            dwv[n][k] = s;
-          }
-        }
         if constexpr (!PACKED) {
           float* dwp = p.dw + ((g * p.NB + j) * C + nq * 4) * 8;
 #pragma unroll
           for (int n = 0; n < 4; ++n) {
-            red_add4(dwp + 8 * n, dwv[n][0], dwv[n][1], dwv[n][2], dwv[n][3]);
-            red_add4(dwp + 8 * n + 4, dwv[n][4], dwv[n][5], dwv[n][6], dwv[n][7]);
+            red_add4(dwp + 8 * n, dwacc[n][0], dwacc[n][1], dwacc[n][2], dwacc[n][3]);
+            red_add4(dwp + 8 * n + 4, dwacc[n][4], dwacc[n][5], dwacc[n][6], dwacc[n][7]);
           }
-          red_add4(p.db + (g * p.NB + j) * C + nq * 4, dbv[0], dbv[1], dbv[2], dbv[3]);
+          red_add4(p.db + (g * p.NB + j) * C + nq * 4, dbacc[0], dbacc[1], dbacc[2], dbacc[3]);
         } else {
           const MbPacked m = mb_packed(C, p.NB);
 #pragma unroll
           for (int n = 0; n < 4; ++n)
 #pragma unroll
             for (int kh = 0; kh < 4; ++kh)
-              red_add2(p.dw + mb_packed_w(m, g, j, nq * 4 + n, kh), dwv[n][2 * kh], dwv[n][2 * kh + 1]);
-          red_add2(p.db + mb_packed_b(m, g, j, nq * 4), dbv[0], dbv[1]);
-          red_add2(p.db + mb_packed_b(m, g, j, nq * 4 + 2), dbv[2], dbv[3]);
-        }
-      }
-      // dX partials of the quad, then a transpose-reduction over the record's LPR lanes
-      float a[V];
-#pragma unroll
-      for (int k = 0; k < 8; ++k)
-#pragma unroll
-        for (int t = 0; t < T; ++t) {
-          float s = 0.f;
-#pragma unroll
-          for (int n = 0; n < 4; ++n) s = fmaf(dz[n][t], w[n][k], s);
-          a[k * T + t] = s;
-        }
-      int vbase = 0;      // first partial index this lane holds
-      bool writer = true; // false on the upper lane of a plain (non-transposing) butterfly stage
-#pragma unroll
-      for (int s = 0; s < 4; ++s) {
-        constexpr int kV = V;
-        const int width = kV >> s;  // a compile-time constant once the loop is unrolled
-        if (s < p.lgLPR) {
-          const bool hi = (nq >> s) & 1;
-          if (width > 1) {
-#pragma unroll
-            for (int i = 0; i < width / 2; ++i) {
-              const float keep = hi ? a[i + width / 2] : a[i];
-              const float send = hi ? a[i] : a[i + width / 2];
-              a[i] = keep + __shfl_xor_sync(kFullMask, send, 1 << s);
-            }
-            if (hi) vbase += width / 2;
-          } else {
-            a[0] += __shfl_xor_sync(kFullMask, a[0], 1 << s);
-            if (hi) writer = false;
-          }
-        }
-      }
-      const int held = max(V >> p.lgLPR, 1);
-      if (okr && writer) {
-#pragma unroll
-        for (int i = 0; i < V; ++i) {
-          if (i < held) {
-            const int v = vbase + i, k = v / T, t = v - k * T;
-            int row = rec.i[0];  // rec.i[k] through selects: a dynamic index would place rec in local memory
-#pragma unroll
-            for (int q = 1; q < 8; ++q) row = k == q ? rec.i[q] : row;
-            atomicAdd(&dxs[row * T + t], a[i]);
-          }
+              red_add2(p.dw + mb_packed_w(m, g, j, nq * 4 + n, kh), dwacc[n][2 * kh], dwacc[n][2 * kh + 1]);
+          red_add2(p.db + mb_packed_b(m, g, j, nq * 4), dbacc[0], dbacc[1]);
+          red_add2(p.db + mb_packed_b(m, g, j, nq * 4 + 2), dbacc[2], dbacc[3]);
         }
       }
     }
@@ -338,17 +373,21 @@ __global__ void __launch_bounds__(kMbBwdThreads, 1) mb_bwd_kernel(const MbParams
   for (int e = threadIdx.x; e < p.D * T; e += kMbBwdThreads) {
     const int tt = e / p.D, d = e - tt * p.D;
     if (t0 + tt < p.B) {
-      const float v = dxs[d * T + tt];
+      const float v = dxs[d * DLD + tt];
       if (v != 0.f) red_add(p.dx + (int64_t)(t0 + tt) * p.lddx + d, v);
     }
   }
 }
 
-static int64_t mb_tile_floats(int64_t D, int T) { return (D * T + 3) & ~3LL; }
+// Dynamic shared memory: the padded x tile, plus the padded dX tile for the backward.
+static int64_t mb_smem_bytes(int64_t D, int T, bool bwd) {
+  const int xld = T >= 8 ? T + 4 : T, dld = T >= 4 ? T + 1 : T;
+  return (((D * xld + 3) & ~3LL) + (bwd ? D * dld : 0)) * 4;
+}
 
 template <int T, int ACT, bool PACKED>
 static int mb_launch(const MbParams& p, bool bwd, cudaStream_t st) {
-  const size_t smem = (size_t)mb_tile_floats(p.D, T) * 4 * (bwd ? 2 : 1);
+  const size_t smem = (size_t)mb_smem_bytes(p.D, T, bwd);
   const void* kern = bwd ? (const void*)mb_bwd_kernel<T, ACT, PACKED> : (const void*)mb_fwd_kernel<T, ACT, PACKED>;
   int rc = ensure_dynamic_smem(kern, smem);
   if (rc) return rc;
@@ -379,10 +418,10 @@ static int mb_dispatch(const MbParams& p, int act, bool packed, bool bwd, cudaSt
   return packed ? mb_dispatch_act<T, true>(p, act, bwd, st) : mb_dispatch_act<T, false>(p, act, bwd, st);
 }
 
-// Largest token tile in {8, 4, 2, 1} whose tiles (1 forward, 2 backward) fit the opt-in shared memory.
+// Largest token tile in {32, 16, 8, 4, 2, 1} whose tiles (1 forward, 2 backward) fit the opt-in shared memory.
 static int mb_pick_tokens(int64_t D, bool bwd, int optin) {
-  for (int T = 8; T >= 1; T >>= 1)
-    if (mb_tile_floats(D, T) * 4 * (bwd ? 2 : 1) + 2048 <= optin) return T;
+  for (int T = 32; T >= 1; T >>= 1)
+    if (mb_smem_bytes(D, T, bwd) + 2048 <= optin) return T;
   return GL_ERR_SMEM;
 }
 
@@ -412,10 +451,10 @@ static int mb_run(const GlSharedArgs& a, bool bwd, void* stream) {
   if (T == 0) {
     T = mb_pick_tokens(a.D, bwd, optin);
     if (T < 0) return T;
-  } else if (T != 1 && T != 2 && T != 4 && T != 8) {
+  } else if (T != 1 && T != 2 && T != 4 && T != 8 && T != 16 && T != 32) {
     return GL_ERR_UNSUPPORTED;
   }
-  if (mb_tile_floats(a.D, T) * 4 * (bwd ? 2 : 1) + 2048 > optin) return GL_ERR_SMEM;
+  if (mb_smem_bytes(a.D, T, bwd) + 2048 > optin) return GL_ERR_SMEM;
   const int64_t G = a.g1 - a.g0;
   int gpc = a.groups_per_cta;
   if (gpc <= 0) {
@@ -434,6 +473,8 @@ static int mb_run(const GlSharedArgs& a, bool bwd, void* stream) {
   cudaStream_t st = (cudaStream_t)stream;
   const bool packed = a.packed != 0;
   switch (T) {
+    case 32: return mb_dispatch<32>(p, a.act, packed, bwd, st);
+    case 16: return mb_dispatch<16>(p, a.act, packed, bwd, st);
     case 8: return mb_dispatch<8>(p, a.act, packed, bwd, st);
     case 4: return mb_dispatch<4>(p, a.act, packed, bwd, st);
     case 2: return mb_dispatch<2>(p, a.act, packed, bwd, st);
