@@ -16,6 +16,14 @@ dX all-reduce before the optimizer kernels so that they overlap it.
 
 Nothing here touches another GPU's memory directly: remote data arrives only
 through the collectives into local buffers.
+
+Storage order.  A shard on a GPU stores its neurons, by default, in the bank-aware
+processing order of ``gl_group_order`` (unit 48): within each group the records are
+permuted so that the neurons one shared-memory wavefront serves read rows in distinct
+bank groups, which cuts the kernels' bank conflicts while keeping their record loads
+coalesced.  The permutation is within groups, so pooled outputs and dX are unchanged;
+``neuron_order[g][p]`` is the slot stored at position p, and ``canonical`` /
+``canonical_shard`` return tensors in slot order (the layout of ``SparsePoolingLayer``).
 """
 from __future__ import annotations
 
@@ -95,7 +103,7 @@ class GroupShardedLayer(nn.Module):
 
     def __init__(self, input_dim: int, hidden_dim: int, output_dim: int, pooling="mean",
                  plan: Optional[PhysicalPlan] = None, device=None, seed: int = 0, bias_std: float = 0.0,
-                 group=None, runtime_factory: Optional[Callable] = None, _params=None):
+                 group=None, runtime_factory: Optional[Callable] = None, _params=None, neuron_order: str = "bank"):
         super().__init__()
         self.group = group
         self.rank = dist.get_rank(group)
@@ -125,17 +133,62 @@ class GroupShardedLayer(nn.Module):
                                                                 lay.plan, counts=lay.counts))
         self._factory = factory
         self._rt = None
+        if neuron_order not in ("bank", "slot"):
+            raise ValueError("neuron_order must be 'bank' or 'slot'")
+        self.register_buffer("neuron_order", None)
+        if neuron_order == "bank":
+            self.reorder_neurons()
+
+    @torch.no_grad()
+    def reorder_neurons(self):
+        """Store this shard's neurons in bank-aware processing order (module docstring).  Needs CUDA
+        tensors (a no-op otherwise) and must run before optimizer state exists: parameters and any
+        ``main_grad`` buffers are permuted in place."""
+        if self.neuron_order is not None or not self.indices.is_cuda or self.indices.shape[0] == 0:
+            return
+        from . import _native
+
+        G_l, NB = self.indices.shape[0], self.layout.blocks_per_group
+        slots = NB * 8
+        o = torch.empty((G_l, slots), dtype=torch.int32, device=self.indices.device)
+        _native.group_order(self.indices, self.counts.to(torch.int32).contiguous(), self.layout.input_dim, NB, 0,
+                            G_l, 48, o)
+        ol = o.long()
+        for t in (self.indices, self.weight.data, self.bias.data, getattr(self.weight, "main_grad", None),
+                  getattr(self.bias, "main_grad", None)):
+            if t is not None:
+                per = t.numel() // (G_l * slots)
+                v = t.view(G_l, slots, per)
+                v.copy_(torch.gather(v, 1, ol[:, :, None].expand(G_l, slots, per)))
+        self.neuron_order = o
+        self._rt = None
+
+    def canonical(self, t: torch.Tensor) -> torch.Tensor:
+        """``t`` (indices-, weight- or bias-shaped, in this shard's storage order) in slot order."""
+        if self.neuron_order is None:
+            return t
+        G_l, slots = self.neuron_order.shape
+        per = t.numel() // (G_l * slots)
+        ol = self.neuron_order.long().to(t.device)[:, :, None].expand(G_l, slots, per)
+        out = torch.empty_like(t)
+        out.view(G_l, slots, per).scatter_(1, ol, t.reshape(G_l, slots, per))
+        return out
+
+    def canonical_shard(self):
+        """(indices, weight, bias) of this shard in slot order."""
+        return self.canonical(self.indices), self.canonical(self.weight.detach()), self.canonical(self.bias.detach())
 
     @classmethod
-    def from_full(cls, layer, group=None, runtime_factory=None):
-        """Shard an existing (full) ``SparsePoolingLayer``: slices of its tensors."""
+    def from_full(cls, layer, group=None, runtime_factory=None, neuron_order: str = "bank"):
+        """Shard an existing (full) ``SparsePoolingLayer``: slices of its tensors (reordered into the
+        bank-aware storage order when they are on a GPU; ``reorder_neurons`` after moving otherwise)."""
         L = layer.layout
         world, rank = dist.get_world_size(group), dist.get_rank(group)
         g0, g1 = shard_range(L.groups, rank, world)
         params = (layer.indices[g0:g1].clone(), layer.weight.detach()[g0:g1].clone(),
                   layer.bias.detach()[g0:g1].clone())
         return cls(L.input_dim, L.hidden_dim, L.groups, pooling=layer.cfg, plan=layer.plan, group=group,
-                   runtime_factory=runtime_factory, _params=params)
+                   runtime_factory=runtime_factory, _params=params, neuron_order=neuron_order)
 
     def runtime(self):
         if self._rt is None or self._rt.idx is not self.indices:

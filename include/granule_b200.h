@@ -159,7 +159,8 @@ int gl_group_index_maxcount(const int16_t* idx, const int32_t* counts, int64_t D
  * permutation of group g's slots (valid slots first, padding slots in place) such that the
  * `unit` consecutive positions served by one shared-memory wavefront read rows in distinct bank
  * groups (row d mod unit) for as many of their 8 inputs as possible.  unit = 32 / token tile:
- * 4 for the forward's tile of 8, 8 for the backward's tile of 4; 4 and 8 are supported.
+ * 4 for the forward's tile of 8, 8 for the backward's tile of 4; 4 and 8 are supported, and
+ * unit = 48 builds units of 8 (scored mod 8) whose halves are also scored mod 4, serving both.
  * Depends only on the indices; callers compute it once per layer. */
 int gl_group_order(const int16_t* idx, const int32_t* counts, int64_t D, int64_t NB, int64_t g0, int64_t g1,
                    int32_t unit, int32_t* out, void* stream);

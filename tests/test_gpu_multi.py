@@ -40,14 +40,16 @@ def _worker(rank, world, port, q):
         full = SparsePoolingLayer(256, 65536, 256, shared_neurons=None, pooling="mean", dtype=torch.float32,
                                   seed=0, bias_std=0.1)
         lay = GroupShardedLayer.from_full(full).to(dev)
+        lay.reorder_neurons()   # bank-aware storage order (the default for shards built on a GPU)
+        assert lay.neuron_order is not None
         gen = torch.Generator().manual_seed(3)
         x = torch.randn(64, 256, generator=gen)
         dy = torch.randn(64, 256, generator=gen)
         xr = x.to(dev).requires_grad_(True)
         y = lay(xr)
         (y * dy.to(dev)).sum().backward()
-        out = (y.detach().cpu().numpy(), xr.grad.cpu().numpy(), lay.weight.grad.cpu().numpy(),
-               lay.bias.grad.cpu().numpy(), lay.g0, lay.g1)
+        out = (y.detach().cpu().numpy(), xr.grad.cpu().numpy(), lay.canonical(lay.weight.grad).cpu().numpy(),
+               lay.canonical(lay.bias.grad).cpu().numpy(), lay.g0, lay.g1)
         # the overlapped train step gives the same pooled output and dX
         from granulelayer_b200 import FusedAdamW
 

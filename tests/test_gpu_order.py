@@ -88,3 +88,48 @@ def test_order_rejects_bad_unit():
     out = torch.empty((2, L.blocks_per_group * 8), dtype=torch.int32, device="cuda")
     with pytest.raises(_native.NativeLibraryError):
         _native.group_order(idx, counts, 256, L.blocks_per_group, 0, 2, 16, out)
+
+
+def _single_rank_group():
+    import socket
+
+    import torch.distributed as dist
+
+    if not dist.is_initialized():
+        with socket.socket() as s:
+            s.bind(("127.0.0.1", 0))
+            port = s.getsockname()[1]
+        dist.init_process_group("gloo", rank=0, world_size=1, init_method=f"tcp://127.0.0.1:{port}")
+    return dist
+
+
+def test_bank_ordered_shard_matches_layer():
+    """A GPU shard stores its neurons in bank-aware order; outputs, dX and the slot-order dW/db
+    equal the drop-in layer's, and the stored parameters are a per-group permutation."""
+    from granulelayer_b200.distributed import GroupShardedLayer
+
+    dist = _single_rank_group()
+    try:
+        D, H, G, B = 4096, 3 * 24576 + 100, 3, 24
+        full = SparsePoolingLayer(D, H, G, shared_neurons=None, pooling="mean", dtype=torch.float32, seed=5,
+                                  bias_std=0.1).cuda()
+        shard = GroupShardedLayer.from_full(full)
+        assert shard.neuron_order is not None, "shards built from GPU tensors are stored in bank order"
+        ci, cw, cb = shard.canonical_shard()
+        assert torch.equal(ci, full.indices) and torch.equal(cw, full.weight) and torch.equal(cb, full.bias)
+        assert not torch.equal(shard.indices, full.indices)
+        x = torch.randn(B, D, generator=torch.Generator().manual_seed(1)).cuda()
+        dy = torch.randn(B, G, generator=torch.Generator().manual_seed(2)).cuda()
+        outs = []
+        for lay in (full, shard):
+            xr = x.clone().requires_grad_(True)
+            y = lay(xr)
+            y.backward(dy)
+            gw = lay.weight.grad if lay is full else shard.canonical(lay.weight.grad)
+            gb = lay.bias.grad if lay is full else shard.canonical(lay.bias.grad)
+            outs.append((y.detach(), xr.grad, gw, gb))
+        for what, a, b, tol in zip(("y", "dx", "dw", "db"), outs[1], outs[0],
+                                   (dict(rtol=1e-5, atol=1e-6),) + (dict(rtol=1e-4, atol=1e-5),) * 3):
+            assert_close(a, b, what=what, **tol)
+    finally:
+        dist.destroy_process_group()
