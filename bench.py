@@ -70,9 +70,9 @@ METRIC = "neuron-samples/s fwd+bwd+opt @100M fan-in-8, B=1024; % HBM roofline; 1
 UNIT = "neuron-samples/s"
 FALLBACK_HBM_GBS = 6650.0
 # DRAM bytes (read + write) per neuron per backward launch at B = 1024, from the ncu
-# capture in profiles/bwd_kernel_fixed_g512.md (1.79 GB for 512 x 24,576 neurons); the
+# capture in profiles/bwd_kernel_fixed_g512.md (1.765 GB for 512 x 24,576 neurons); the
 # traffic grows with the neuron count, so a full launch is this figure times N.
-BWD_DRAM_BYTES_PER_NEURON = 1.788315e9 / (512 * 24576)
+BWD_DRAM_BYTES_PER_NEURON = 1.764587e9 / (512 * 24576)
 
 
 def param_bytes(n):
