@@ -178,6 +178,41 @@ class GroupShardedLayer(nn.Module):
         """(indices, weight, bias) of this shard in slot order."""
         return self.canonical(self.indices), self.canonical(self.weight.detach()), self.canonical(self.bias.detach())
 
+    @torch.no_grad()
+    def full_state_dict(self) -> dict:
+        """{"indices", "weight", "bias"} of the whole layer in slot order, gathered from every rank:
+        bit for bit the state dict of the equivalent single-GPU ``SparsePoolingLayer`` (its keys,
+        shapes and storage order), so checkpoints written here load into the drop-in layer and into
+        the reference's.  Collective: every rank calls it and receives the full tensors."""
+        G, world = self.layout.groups, self.world
+        width = -(-G // world)
+        out = {}
+        for name, t in zip(("indices", "weight", "bias"), self.canonical_shard()):
+            dtype = t.dtype
+            if dtype == torch.int16:   # not every backend gathers int16 (gloo does not): widen exactly
+                t = t.to(torch.int32)
+            pad = t.new_zeros((width,) + tuple(t.shape[1:]))
+            pad[:t.shape[0]] = t
+            parts = [torch.empty_like(pad) for _ in range(world)]
+            dist.all_gather(parts, pad.contiguous(), group=self.group)
+            out[name] = torch.cat([parts[r][:shard_range(G, r, world)[1] - shard_range(G, r, world)[0]]
+                                   for r in range(world)], dim=0).to(dtype)
+        return out
+
+    @torch.no_grad()
+    def load_full_state_dict(self, sd: dict):
+        """Load this rank's groups from a full (single-GPU layout) state dict, e.g. one written by
+        ``SparsePoolingLayer.state_dict()``, ``full_state_dict()`` or the reference's layer."""
+        for name, dst in (("indices", self.indices), ("weight", self.weight.data), ("bias", self.bias.data)):
+            src = sd[name]
+            if tuple(src.shape[1:]) != tuple(dst.shape[1:]) or src.shape[0] != self.layout.groups:
+                raise ValueError(f"{name}: full shape {tuple(src.shape)} does not match this layer")
+            dst.copy_(src[self.g0:self.g1])
+        order, self.neuron_order = self.neuron_order, None
+        self._rt = None
+        if order is not None:
+            self.reorder_neurons()
+
     @classmethod
     def from_full(cls, layer, group=None, runtime_factory=None, neuron_order: str = "bank"):
         """Shard an existing (full) ``SparsePoolingLayer``: slices of its tensors (reordered into the

@@ -91,6 +91,13 @@ def _worker(rank, world, port, mode, q):
                 y, dx = step.step(x, dy)
                 q.put((rank, "ok", (y.numpy(), dx.numpy(), lay.weight.main_grad.numpy(),
                                     lay.bias.main_grad.numpy(), lay.g0, lay.g1)))
+        elif mode == "state":
+            lay = GroupShardedLayer.from_full(full, runtime_factory=OracleRuntime)
+            sd = lay.full_state_dict()
+            other = GroupShardedLayer.from_full(_full_layer(D, H, G, seed=4), runtime_factory=OracleRuntime)
+            other.load_full_state_dict(sd)
+            same = all(torch.equal(a, b) for a, b in zip(other.canonical_shard(), lay.canonical_shard()))
+            q.put((rank, "ok", ({k: v.numpy() for k, v in sd.items()}, same)))
         elif mode == "dead_peer":
             if rank == 1:
                 q.put((rank, "ok", "left before the collective"))
@@ -171,6 +178,22 @@ def test_sharded_layer_equals_full_layer(mode):
         np.testing.assert_allclose(dxs, dx, rtol=1e-5, atol=1e-6)    # all-reduced dX
         np.testing.assert_allclose(dws, dw[g0:g1], rtol=1e-5, atol=1e-7)
         np.testing.assert_allclose(dbs, db[g0:g1], rtol=1e-5, atol=1e-7)
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_full_state_dict_is_the_single_gpu_state_dict(world):
+    """Sharded checkpoints gather to the drop-in layer's state dict, bit for bit, and load back."""
+    full = _full_layer(48, 2600, 5, seed=3)
+    ref = {k: v.numpy() for k, v in full.state_dict().items()}
+    out = _run("state", world=world)
+    for r in range(world):
+        status, payload = out[r]
+        assert status == "ok", payload
+        sd, same = payload
+        assert set(sd) == set(ref)
+        for k in ref:
+            np.testing.assert_array_equal(sd[k], ref[k])
+        assert same
 
 
 def test_dead_peer_fails_instead_of_hanging():

@@ -118,6 +118,9 @@ def test_bank_ordered_shard_matches_layer():
         ci, cw, cb = shard.canonical_shard()
         assert torch.equal(ci, full.indices) and torch.equal(cw, full.weight) and torch.equal(cb, full.bias)
         assert not torch.equal(shard.indices, full.indices)
+        sd = shard.full_state_dict()
+        for k, v in full.state_dict().items():
+            assert torch.equal(sd[k], v), f"{k}: gathered shard state differs from the single-GPU layer"
         x = torch.randn(B, D, generator=torch.Generator().manual_seed(1)).cuda()
         dy = torch.randn(B, G, generator=torch.Generator().manual_seed(2)).cuda()
         outs = []
