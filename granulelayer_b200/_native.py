@@ -16,7 +16,7 @@ from pathlib import Path
 
 import torch
 
-ABI_VERSION = 5
+ABI_VERSION = 6
 LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libgranule_b200.so"
 
 POOL_MEAN, POOL_SUM = 0, 1
@@ -24,7 +24,8 @@ ACT_IDS = {"identity": 0, "relu": 1, "gelu": 2}
 
 # The exported entry points, in header order (checked by the CPU test suite).
 EXPORTS = ("gl_abi_version", "gl_status_string", "gl_last_cuda_error", "gl_fwd_f32", "gl_bwd_f32",
-           "gl_adam_f32", "gl_group_absmax_f32", "gl_group_index_maxcount", "gl_group_order", "gl_launch_count",
+           "gl_adam_f32", "gl_group_absmax_f32", "gl_group_index_maxcount", "gl_group_feature_map",
+           "gl_group_order", "gl_launch_count",
            "gl_fwd_auto_tokens", "gl_bwd_auto_tokens", "gl_fwd_shared_f32", "gl_bwd_shared_f32",
            "gl_shared_auto_tokens", "gl_k16_fwd_f32", "gl_k16_bwd_f32", "gl_k16_auto_tokens")
 
@@ -39,7 +40,9 @@ class GlFwdArgs(ctypes.Structure):
                 ("B", ctypes.c_int64), ("D", ctypes.c_int64), ("NB", ctypes.c_int64),
                 ("g0", ctypes.c_int64), ("g1", ctypes.c_int64), ("ldx", ctypes.c_int64), ("ldp", ctypes.c_int64),
                 ("pool", ctypes.c_int32), ("act", ctypes.c_int32), ("tokens", ctypes.c_int32),
-                ("groups_per_cta", ctypes.c_int32), ("wabsmax", ctypes.c_void_p), ("order", ctypes.c_void_p)]
+                ("groups_per_cta", ctypes.c_int32), ("wabsmax", ctypes.c_void_p), ("order", ctypes.c_void_p),
+                ("lidx", ctypes.c_void_p), ("fmap", ctypes.c_void_p), ("nfeat", ctypes.c_void_p),
+                ("fcap", ctypes.c_int64)]
 
 
 class GlBwdArgs(ctypes.Structure):
@@ -51,7 +54,8 @@ class GlBwdArgs(ctypes.Structure):
                 ("ldx", ctypes.c_int64), ("ldg", ctypes.c_int64), ("lddx", ctypes.c_int64),
                 ("pool", ctypes.c_int32), ("act", ctypes.c_int32), ("tokens", ctypes.c_int32),
                 ("groups_per_cta", ctypes.c_int32), ("wabsmax", ctypes.c_void_p), ("rowmax", ctypes.c_void_p),
-                ("order", ctypes.c_void_p)]
+                ("order", ctypes.c_void_p), ("lidx", ctypes.c_void_p), ("fmap", ctypes.c_void_p),
+                ("nfeat", ctypes.c_void_p), ("fcap", ctypes.c_int64)]
 
 
 class GlAdamArgs(ctypes.Structure):
@@ -116,6 +120,10 @@ def load(path=None) -> ctypes.CDLL:
         for name in ("gl_fwd_auto_tokens", "gl_bwd_auto_tokens"):
             getattr(lib, name).restype = ctypes.c_int
             getattr(lib, name).argtypes = [ctypes.c_int64]
+        lib.gl_group_feature_map.restype = ctypes.c_int
+        lib.gl_group_feature_map.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
+                                             ctypes.c_int64, ctypes.c_int64, ctypes.c_int32, ctypes.c_void_p,
+                                             ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
         lib.gl_group_order.restype = ctypes.c_int
         lib.gl_group_order.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
                                        ctypes.c_int64, ctypes.c_int64, ctypes.c_int32, ctypes.c_void_p,
@@ -157,26 +165,32 @@ def _require_cuda(*ts):
 
 
 def fwd(x, idx, w, b, counts, pre, NB: int, g0: int, g1: int, pool: int, act: int, tokens: int = 0,
-        groups_per_cta: int = 0, wabsmax=None, order=None):
+        groups_per_cta: int = 0, wabsmax=None, order=None, local=None):
     """pre[:, :g1-g0] = pooled act(z) of groups [g0, g1); optionally wabsmax[g-g0] = max |w|; ``order``
-    is an optional processing order (group_order).  See GlFwdArgs."""
-    _require_cuda(x, idx, w, b, counts, pre, wabsmax, order)
+    is an optional processing order (group_order); ``local`` = (lidx, fmap, nfeat) from
+    group_feature_map turns on the per-group input staging.  See GlFwdArgs."""
+    lidx, fmap, nfeat = local if local is not None else (None, None, None)
+    _require_cuda(x, idx, w, b, counts, pre, wabsmax, order, lidx, fmap, nfeat)
     lib = load()
     a = GlFwdArgs(_ptr(x), _ptr(idx), _ptr(w), _ptr(b), _ptr(counts), _ptr(pre), x.shape[0], x.shape[1], NB,
-                  g0, g1, x.stride(0), pre.stride(0), pool, act, tokens, groups_per_cta, _ptr(wabsmax), _ptr(order))
+                  g0, g1, x.stride(0), pre.stride(0), pool, act, tokens, groups_per_cta, _ptr(wabsmax), _ptr(order),
+                  _ptr(lidx), _ptr(fmap), _ptr(nfeat), fmap.shape[1] if fmap is not None else 0)
     with torch.cuda.device(x.device):
         _check(lib, lib.gl_fwd_f32(ctypes.byref(a), _stream(x.device)), "gl_fwd_f32")
 
 
 def bwd(x, idx, w, b, counts, gpre, dx, dw, db, NB: int, g0: int, g1: int, pool: int, act: int, tokens: int = 0,
-        groups_per_cta: int = 0, wabsmax=None, rowmax=None, order=None):
+        groups_per_cta: int = 0, wabsmax=None, rowmax=None, order=None, local=None):
     """dx += ..., dw += ..., db += ... for groups [g0, g1); fixed-point dX tiles when the
-    per-group bounds ``wabsmax``/``rowmax`` are given; optional processing ``order``.  See GlBwdArgs."""
-    _require_cuda(x, idx, w, b, counts, gpre, dx, dw, db, wabsmax, rowmax, order)
+    per-group bounds ``wabsmax``/``rowmax`` are given; optional processing ``order`` and input
+    ``local``ity maps as in ``fwd``.  See GlBwdArgs."""
+    lidx, fmap, nfeat = local if local is not None else (None, None, None)
+    _require_cuda(x, idx, w, b, counts, gpre, dx, dw, db, wabsmax, rowmax, order, lidx, fmap, nfeat)
     lib = load()
     a = GlBwdArgs(_ptr(x), _ptr(idx), _ptr(w), _ptr(b), _ptr(counts), _ptr(gpre), _ptr(dx), _ptr(dw), _ptr(db),
                   x.shape[0], x.shape[1], NB, g0, g1, x.stride(0), gpre.stride(0), dx.stride(0), pool, act,
-                  tokens, groups_per_cta, _ptr(wabsmax), _ptr(rowmax), _ptr(order))
+                  tokens, groups_per_cta, _ptr(wabsmax), _ptr(rowmax), _ptr(order), _ptr(lidx), _ptr(fmap),
+                  _ptr(nfeat), fmap.shape[1] if fmap is not None else 0)
     with torch.cuda.device(x.device):
         _check(lib, lib.gl_bwd_f32(ctypes.byref(a), _stream(x.device)), "gl_bwd_f32")
 
@@ -228,6 +242,17 @@ def group_index_maxcount(idx, counts, D: int, NB: int, g0: int, g1: int, out):
     with torch.cuda.device(idx.device):
         _check(lib, lib.gl_group_index_maxcount(_ptr(idx), _ptr(counts), D, NB, g0, g1, _ptr(out),
                                                 _stream(idx.device)), "gl_group_index_maxcount")
+
+
+def group_feature_map(idx, counts, D: int, NB: int, g0: int, g1: int, nf, fmap=None, lidx=None):
+    """nf[g-g0] = distinct features of group g; optionally the sorted lists ``fmap`` [g1-g0, cap] and
+    the records as list positions ``lidx`` (gl_group_feature_map)."""
+    _require_cuda(idx, counts, nf, fmap, lidx)
+    lib = load()
+    cap = fmap.shape[1] if fmap is not None else 0
+    with torch.cuda.device(idx.device):
+        _check(lib, lib.gl_group_feature_map(_ptr(idx), _ptr(counts), D, NB, g0, g1, cap, _ptr(nf), _ptr(fmap),
+                                             _ptr(lidx), _stream(idx.device)), "gl_group_feature_map")
 
 
 def group_order(idx, counts, D: int, NB: int, g0: int, g1: int, unit: int, out):

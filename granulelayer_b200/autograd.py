@@ -99,6 +99,7 @@ class Level1Runtime:
         self._rowmax = None
         self._rowmax_key = None
         self._orders: Dict = {}
+        self._local = None
 
     @property
     def fixed_point(self) -> bool:
@@ -132,6 +133,30 @@ class Level1Runtime:
             out = (key, o)
             self._orders[unit] = out
         return out[1]
+
+    def locality(self):
+        """(lidx, fmap, nfeat) when every group reads at most a quarter of the input features (the
+        kernels then stage only each group's features), else None.  Built once per index tensor."""
+        if self.plan.b200_locality == "off" or self.layout.shared_indices or not self.idx.is_cuda:
+            return None
+        G, D, NB = self.groups, self.layout.input_dim, self.layout.blocks_per_group
+        if G == 0 or G > 65535 or D < 256:
+            return None
+        key = (self.idx.data_ptr(), self.idx._version)
+        if self._local is not None and self._local[0] == key:
+            return self._local[1]
+        nf = torch.empty(G, device=self.idx.device, dtype=torch.int32)
+        _native.group_feature_map(self.idx, self.counts_i32, D, NB, 0, G, nf)
+        fmax = int(nf.max())
+        maps = None
+        if fmax <= D // 4:
+            cap = -(-fmax // 8) * 8
+            fmap = torch.zeros((G, cap), device=self.idx.device, dtype=torch.int16)
+            lidx = torch.empty_like(self.idx)
+            _native.group_feature_map(self.idx, self.counts_i32, D, NB, 0, G, nf, fmap, lidx)
+            maps = (lidx, fmap, nf)
+        self._local = (key, maps)
+        return maps
 
     def tokens(self, backward: bool) -> int:
         lib = _native.load()
@@ -205,7 +230,8 @@ class Level1Runtime:
         wabsmax = torch.empty(self.groups, device=x.device, dtype=torch.float32) if B > 0 else None
         _native.fwd(x, self.idx, w, b, self.counts_i32, pre, self.layout.blocks_per_group, 0, self.groups,
                     self.pool, self.act, tokens=self.plan.b200_fwd_tokens, wabsmax=wabsmax,
-                    order=self.order(self.tokens(False)) if B > 0 else None)
+                    order=self.order(self.tokens(False)) if B > 0 else None,
+                    local=self.locality() if B > 0 else None)
         self.last_info.update(forward_backend="b200", workspace_bytes=0)
         out = {"pre": pre}
         if wabsmax is not None:
@@ -236,7 +262,8 @@ class Level1Runtime:
             rowmax = self.rowmax()
         _native.bwd(x, self.idx, w, b, self.counts_i32, g_pre, dx, dw_buf, db_buf, self.layout.blocks_per_group,
                     0, self.groups, self.pool, self.act, tokens=self.plan.b200_dx_tokens, wabsmax=wabsmax,
-                    rowmax=rowmax, order=self.order(self.tokens(True)) if B > 0 else None)
+                    rowmax=rowmax, order=self.order(self.tokens(True)) if B > 0 else None,
+                    local=self.locality() if B > 0 else None)
         self.last_info["backward_backend"] = "b200"
         self.last_info["dx_accumulation"] = "int32 fixed point" if wabsmax is not None else "fp32 atomics"
         return dx

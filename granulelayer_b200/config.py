@@ -259,6 +259,10 @@ class PhysicalPlan:
     # loads of a warp step over ~6x more cache lines on the same L1 data path; measured at the
     # 100M-neuron config it is slower (backward 835 ms vs 755 ms), so it is off by default.
     b200_neuron_order: str = "identity"
+    # input locality: "auto" = when every group reads at most a quarter of the input features, the
+    # kernels stage only each group's features (gl_group_feature_map, once per index tensor);
+    # "off" = always stage the whole input row
+    b200_locality: str = "auto"
 
     def __post_init__(self):
         if self.input_layout not in ("feature_major", "token_major"):
@@ -283,6 +287,8 @@ class PhysicalPlan:
             raise ValueError("b200_dx_accum must be 'auto', 'fixed' or 'fp32'")
         if self.b200_neuron_order not in ("auto", "identity"):
             raise ValueError("b200_neuron_order must be 'auto' or 'identity'")
+        if self.b200_locality not in ("auto", "off"):
+            raise ValueError("b200_locality must be 'auto' or 'off'")
 
 
 def resolve_reduction(plan: PhysicalPlan):

@@ -92,18 +92,20 @@ struct BwdParams {
   const float* wabsmax;
   const int32_t* rowmax;
   const int32_t* order;
+  LocalMap lm;
   int B, D;
   int64_t NB, g0, g1, ldx, ldg, lddx;
   int pool, gpc;
 };
 
-// FIXED = false: fp32 tile.  FIXED = true: int32 tile + fp32 fold tile.
-template <int T, int ACT, bool FIXED>
+// FIXED = false: fp32 tile.  FIXED = true: int32 tile + fp32 fold tile.  LOCAL: one group per block,
+// tiles over the group's feature map only (rows = its features, records read as positions).
+template <int T, int ACT, bool FIXED, bool LOCAL>
 __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const BwdParams p) {
   constexpr int NPW = 32 / T;
   constexpr int NW = kBwdThreads / 32;
   extern __shared__ __align__(16) float smem[];
-  const size_t tile = ((size_t)p.D * T + 3) & ~(size_t)3;  // tiles start on 16-byte boundaries
+  const size_t tile = ((size_t)(LOCAL ? p.lm.fcap : p.D) * T + 3) & ~(size_t)3;  // tiles start on 16-byte boundaries
   float* xs = smem;
   float* dxf = smem + tile;
   int* dxi = reinterpret_cast<int*>(smem + 2 * tile);
@@ -112,8 +114,18 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const BwdParams p) 
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int t0 = blockIdx.x * T;
-  const int D = p.D;
-  stage_tile<T, kBwdThreads>(xs, p.x, t0, p.B, D, p.ldx);
+  int D = p.D;  // rows of the tiles: the input features, or the group's feature map
+  const int16_t* ridx = p.idx;
+  const int16_t* cols = nullptr;
+  if constexpr (LOCAL) {
+    const int64_t gl = (int64_t)blockIdx.y * p.gpc;
+    D = min(max(__ldg(p.lm.nfeat + gl), 1), p.lm.fcap);
+    cols = p.lm.fmap + gl * p.lm.fcap;
+    ridx = p.lm.lidx;
+    stage_cols<T, kBwdThreads>(xs, p.x, t0, p.B, cols, D, p.ldx, p.D);
+  } else {
+    stage_tile<T, kBwdThreads>(xs, p.x, t0, p.B, D, p.ldx);
+  }
   for (int e = threadIdx.x; e < D * T; e += kBwdThreads) {
     dxf[e] = 0.f;
     if constexpr (FIXED) dxi[e] = 0;
@@ -154,7 +166,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const BwdParams p) 
         const int slot =
             p.order != nullptr ? min(max(__ldg(p.order + (g - p.g0) * (int64_t)slots + s), 0), slots - 1) : s;
         const int64_t f = fbase + slot;
-        const Rec8 r = load_rec8(p.idx + f * 8, D - 1);
+        const Rec8 r = load_rec8(ridx + f * 8, D - 1);
         const W8 wr = load_w8(p.w + f * 8);
         float z = __ldg(p.bias + f);
         float xv[8];
@@ -233,7 +245,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const BwdParams p) 
     const int tt = e / D, d = e - tt * D;
     if (t0 + tt < p.B) {
       const float v = (FIXED && bad[tt]) ? nan : dxf[d * T + tt];
-      if (v != 0.f) red_add(p.dx + (int64_t)(t0 + tt) * p.lddx + d, v);
+      int col = d;
+      if constexpr (LOCAL) col = min((int)(uint16_t)__ldg(cols + d), p.D - 1);
+      if (v != 0.f) red_add(p.dx + (int64_t)(t0 + tt) * p.lddx + col, v);
     }
   }
 }
@@ -242,10 +256,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const BwdParams p) 
 // each rounded up to 16 bytes.
 static int64_t bwd_smem(int64_t D, int T, bool fixed) { return ((D * T + 3) & ~3LL) * 4 * (fixed ? 3 : 2); }
 
-template <int T, int ACT, bool FIXED>
+template <int T, int ACT, bool FIXED, bool LOCAL>
 static int launch_bwd(const BwdParams& p, int64_t B, cudaStream_t st) {
-  const size_t smem = (size_t)bwd_smem(p.D, T, FIXED);
-  auto kern = bwd_kernel<T, ACT, FIXED>;
+  const size_t smem = (size_t)bwd_smem(LOCAL ? p.lm.fcap : p.D, T, FIXED);
+  auto kern = bwd_kernel<T, ACT, FIXED, LOCAL>;
   int rc = ensure_dynamic_smem((const void*)kern, smem);
   if (rc) return rc;
   const int64_t tiles = (B + T - 1) / T;
@@ -259,23 +273,23 @@ static int launch_bwd(const BwdParams& p, int64_t B, cudaStream_t st) {
   return GL_OK;
 }
 
-template <int T, bool FIXED>
+template <int T, bool FIXED, bool LOCAL>
 static int dispatch_act_bwd(const BwdParams& p, int64_t B, int act, cudaStream_t st) {
   switch (act) {
-    case GL_ACT_IDENTITY: return launch_bwd<T, GL_ACT_IDENTITY, FIXED>(p, B, st);
-    case GL_ACT_RELU: return launch_bwd<T, GL_ACT_RELU, FIXED>(p, B, st);
-    case GL_ACT_GELU: return launch_bwd<T, GL_ACT_GELU, FIXED>(p, B, st);
+    case GL_ACT_IDENTITY: return launch_bwd<T, GL_ACT_IDENTITY, FIXED, LOCAL>(p, B, st);
+    case GL_ACT_RELU: return launch_bwd<T, GL_ACT_RELU, FIXED, LOCAL>(p, B, st);
+    case GL_ACT_GELU: return launch_bwd<T, GL_ACT_GELU, FIXED, LOCAL>(p, B, st);
     default: return GL_ERR_UNSUPPORTED;
   }
 }
 
-template <bool FIXED>
+template <bool FIXED, bool LOCAL>
 static int dispatch_tokens_bwd(const BwdParams& p, int64_t B, int act, int T, cudaStream_t st) {
   switch (T) {
-    case 8: return dispatch_act_bwd<8, FIXED>(p, B, act, st);
-    case 4: return dispatch_act_bwd<4, FIXED>(p, B, act, st);
-    case 2: return dispatch_act_bwd<2, FIXED>(p, B, act, st);
-    default: return dispatch_act_bwd<1, FIXED>(p, B, act, st);
+    case 8: return dispatch_act_bwd<8, FIXED, LOCAL>(p, B, act, st);
+    case 4: return dispatch_act_bwd<4, FIXED, LOCAL>(p, B, act, st);
+    case 2: return dispatch_act_bwd<2, FIXED, LOCAL>(p, B, act, st);
+    default: return dispatch_act_bwd<1, FIXED, LOCAL>(p, B, act, st);
   }
 }
 
@@ -311,23 +325,31 @@ extern "C" int gl_bwd_f32(const GlBwdArgs* args, void* stream) {
   int rc = device_smem_optin(&optin);
   if (rc) return rc;
   if ((rc = device_sm_count(&sms))) return rc;
+  const bool local = a.lidx != nullptr;
+  if (local) {
+    if (!a.fmap || !a.nfeat) return GL_ERR_NULL;
+    if (a.fcap < 1 || a.fcap > a.D) return GL_ERR_SHAPE;
+    if ((uintptr_t)a.lidx & 15) return GL_ERR_ALIGN;
+    if (a.g1 - a.g0 > 65535) return GL_ERR_SHAPE;  // one group per block
+  }
+  const int64_t rows = local ? a.fcap : a.D;
   // fixed-point tiles when the caller supplied the two per-group bounds and they fit
   bool fixed = a.wabsmax != nullptr;
   int T = a.tokens;
   if (T == 0) {
-    T = pick_bwd_tokens(a.D, optin, fixed);
+    T = pick_bwd_tokens(rows, optin, fixed);
     if (T < 0 && fixed) {
       fixed = false;
-      T = pick_bwd_tokens(a.D, optin, false);
+      T = pick_bwd_tokens(rows, optin, false);
     }
     if (T < 0) return T;
   } else if (T != 1 && T != 2 && T != 4 && T != 8) {
     return GL_ERR_UNSUPPORTED;
   }
-  if (fixed && bwd_smem(a.D, T, true) > optin) fixed = false;
-  if (bwd_smem(a.D, T, false) > optin) return GL_ERR_SMEM;
+  if (fixed && bwd_smem(rows, T, true) > optin) fixed = false;
+  if (bwd_smem(rows, T, false) > optin) return GL_ERR_SMEM;
   const int64_t G = a.g1 - a.g0;
-  int gpc = a.groups_per_cta;
+  int gpc = local ? 1 : a.groups_per_cta;
   if (gpc <= 0) {
     const int64_t tiles = (a.B + T - 1) / T;
     const int64_t units = tiles * G;
@@ -335,8 +357,13 @@ extern "C" int gl_bwd_f32(const GlBwdArgs* args, void* stream) {
     gpc = (int)(want < 1 ? 1 : (want > 8 ? 8 : want));
   }
   while ((G + gpc - 1) / gpc > 65535) gpc *= 2;
-  BwdParams p{a.x, a.idx, a.w, a.b, a.counts, a.gpre, a.dx, a.dw, a.db, a.wabsmax, a.rowmax, a.order, (int)a.B, (int)a.D,
+  BwdParams p{a.x, a.idx, a.w, a.b, a.counts, a.gpre, a.dx, a.dw, a.db, a.wabsmax, a.rowmax, a.order,
+              LocalMap{a.lidx, a.fmap, a.nfeat, (int)a.fcap}, (int)a.B, (int)a.D,
               a.NB, a.g0, a.g1, a.ldx, a.ldg, a.lddx, a.pool, gpc};
   cudaStream_t st = (cudaStream_t)stream;
-  return fixed ? dispatch_tokens_bwd<true>(p, a.B, a.act, T, st) : dispatch_tokens_bwd<false>(p, a.B, a.act, T, st);
+  if (local)
+    return fixed ? dispatch_tokens_bwd<true, true>(p, a.B, a.act, T, st)
+                 : dispatch_tokens_bwd<false, true>(p, a.B, a.act, T, st);
+  return fixed ? dispatch_tokens_bwd<true, false>(p, a.B, a.act, T, st)
+               : dispatch_tokens_bwd<false, false>(p, a.B, a.act, T, st);
 }

@@ -105,6 +105,37 @@ __device__ __forceinline__ void stage_tile(float* __restrict__ xs, const float* 
   }
 }
 
+// Per-group input feature maps (gl_group_feature_map): when given, a block processes one group
+// and stages only the group's features, fmap[g][0 .. nfeat[g]-1], reading the records' inputs as
+// positions in that list (lidx, same shape as the indices).
+struct LocalMap {
+  const int16_t* lidx;
+  const int16_t* fmap;
+  const int32_t* nfeat;
+  int fcap;
+};
+
+// Stage x[t0 .. t0+T-1, cols[j]] into xs[j * T + t] for j < ncols (tokens >= B read as 0).
+template <int T, int NTHREADS>
+__device__ __forceinline__ void stage_cols(float* __restrict__ xs, const float* __restrict__ x, int t0, int B,
+                                           const int16_t* __restrict__ cols, int ncols, int64_t ldx, int D) {
+  for (int j = threadIdx.x; j < ncols; j += NTHREADS) {
+    const int d = min((int)(uint16_t)__ldg(cols + j), D - 1);
+    float v[T];
+#pragma unroll
+    for (int t = 0; t < T; ++t) v[t] = (t0 + t < B) ? __ldg(x + (int64_t)(t0 + t) * ldx + d) : 0.f;
+    float* row = xs + (int64_t)j * T;
+    if constexpr (T >= 4) {
+#pragma unroll
+      for (int q = 0; q < T / 4; ++q)
+        reinterpret_cast<float4*>(row)[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+    } else {
+#pragma unroll
+      for (int t = 0; t < T; ++t) row[t] = v[t];
+    }
+  }
+}
+
 }  // namespace gl
 
 // ---- host-side helpers (defined in abi.cu) ----

@@ -26,12 +26,12 @@ namespace gl {
 
 constexpr int kFwdThreads = 512;
 
-template <int T, int ACT>
+template <int T, int ACT, bool LOCAL>
 __global__ void __launch_bounds__(kFwdThreads, 1)
     fwd_kernel(const float* __restrict__ x, const int16_t* __restrict__ idx, const float* __restrict__ w,
                const float* __restrict__ bias, const int32_t* __restrict__ counts, float* __restrict__ pre,
                int B, int D, int64_t NB, int64_t g0, int64_t g1, int64_t ldx, int64_t ldp, int pool, int gpc,
-               float* __restrict__ wabsmax, const int32_t* __restrict__ order) {
+               float* __restrict__ wabsmax, const int32_t* __restrict__ order, const LocalMap lm) {
   constexpr int V = T < 4 ? T : 4;   // tokens per lane
   constexpr int LPN = T / V;         // lanes per neuron
   constexpr int NPW = 32 / LPN;      // neurons per warp step
@@ -43,7 +43,17 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int t0 = blockIdx.x * T;
-  stage_tile<T, kFwdThreads>(xs, x, t0, B, D, ldx);
+  int dmax = D - 1;
+  const int16_t* ridx = idx;
+  if constexpr (LOCAL) {  // one group per block: stage only its features
+    const int64_t gl = (int64_t)blockIdx.y * gpc;
+    const int nf = min(max(__ldg(lm.nfeat + gl), 1), lm.fcap);
+    stage_cols<T, kFwdThreads>(xs, x, t0, B, lm.fmap + gl * lm.fcap, nf, ldx, D);
+    dmax = nf - 1;
+    ridx = lm.lidx;
+  } else {
+    stage_tile<T, kFwdThreads>(xs, x, t0, B, D, ldx);
+  }
   __syncthreads();
 
   const int nsub = lane / LPN, q = lane % LPN;
@@ -72,7 +82,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         int slot = ok[u] ? s : 0;
         if (order != nullptr && ok[u]) slot = min(max(__ldg(order + (g - g0) * (int64_t)slots + s), 0), slots - 1);
         const int64_t f = fbase + slot;
-        r[u] = load_rec8(idx + f * 8, D - 1);
+        r[u] = load_rec8(ridx + f * 8, dmax);
         wr[u] = load_w8(w + f * 8);
         bb[u] = __ldg(bias + f);
       }
@@ -138,38 +148,40 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   }
 }
 
-template <int T, int ACT>
+template <int T, int ACT, bool LOCAL>
 static int launch_fwd(const GlFwdArgs& a, int gpc, cudaStream_t st) {
-  const size_t smem = (size_t)a.D * T * sizeof(float);
-  auto kern = fwd_kernel<T, ACT>;
+  const size_t smem = (size_t)(LOCAL ? a.fcap : a.D) * T * sizeof(float);
+  auto kern = fwd_kernel<T, ACT, LOCAL>;
   int rc = ensure_dynamic_smem((const void*)kern, smem);
   if (rc) return rc;
   const int64_t tiles = (a.B + T - 1) / T;
   const int64_t chunks = (a.g1 - a.g0 + gpc - 1) / gpc;
   if (tiles > 2147483647LL || chunks > 65535) return GL_ERR_SHAPE;
   dim3 grid((unsigned)tiles, (unsigned)chunks);
+  const LocalMap lm{a.lidx, a.fmap, a.nfeat, (int)a.fcap};
   kern<<<grid, kFwdThreads, smem, st>>>(a.x, a.idx, a.w, a.b, a.counts, a.pre, (int)a.B, (int)a.D, a.NB, a.g0,
-                                        a.g1, a.ldx, a.ldp, a.pool, gpc, a.wabsmax, a.order);
+                                        a.g1, a.ldx, a.ldp, a.pool, gpc, a.wabsmax, a.order, lm);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_cuda_error(e);
   count_launches(1);
   return GL_OK;
 }
 
-template <int T>
+template <int T, bool LOCAL>
 static int dispatch_act_fwd(const GlFwdArgs& a, int gpc, cudaStream_t st) {
   switch (a.act) {
-    case GL_ACT_IDENTITY: return launch_fwd<T, GL_ACT_IDENTITY>(a, gpc, st);
-    case GL_ACT_RELU: return launch_fwd<T, GL_ACT_RELU>(a, gpc, st);
-    case GL_ACT_GELU: return launch_fwd<T, GL_ACT_GELU>(a, gpc, st);
+    case GL_ACT_IDENTITY: return launch_fwd<T, GL_ACT_IDENTITY, LOCAL>(a, gpc, st);
+    case GL_ACT_RELU: return launch_fwd<T, GL_ACT_RELU, LOCAL>(a, gpc, st);
+    case GL_ACT_GELU: return launch_fwd<T, GL_ACT_GELU, LOCAL>(a, gpc, st);
     default: return GL_ERR_UNSUPPORTED;
   }
 }
 
-// Largest token tile in {8, 4, 2, 1} whose staged input fits the opt-in
-// shared memory (leaving room for the static reduction buffer).
-static int pick_fwd_tokens(int64_t D, int smem_optin) {
-  for (int T = 8; T >= 1; T >>= 1)
+// Largest token tile in {tmax, ..., 2, 1} whose staged input (D rows) fits the opt-in shared
+// memory (leaving room for the static reduction buffer).  tmax is 8 for the full input row and
+// 32 for a group's feature map.
+static int pick_fwd_tokens(int64_t D, int smem_optin, int tmax = 8) {
+  for (int T = tmax; T >= 1; T >>= 1)
     if ((int64_t)D * T * 4 + 2048 <= smem_optin) return T;
   return GL_ERR_SMEM;
 }
@@ -198,16 +210,24 @@ extern "C" int gl_fwd_f32(const GlFwdArgs* args, void* stream) {
   int rc = device_smem_optin(&optin);
   if (rc) return rc;
   if ((rc = device_sm_count(&sms))) return rc;
+  const bool local = a.lidx != nullptr;
+  if (local) {
+    if (!a.fmap || !a.nfeat) return GL_ERR_NULL;
+    if (a.fcap < 1 || a.fcap > a.D) return GL_ERR_SHAPE;
+    if ((uintptr_t)a.lidx & 15) return GL_ERR_ALIGN;
+    if (a.g1 - a.g0 > 65535) return GL_ERR_SHAPE;  // one group per block
+  }
+  const int64_t rows = local ? a.fcap : a.D;
   int T = a.tokens;
   if (T == 0) {
-    T = pick_fwd_tokens(a.D, optin);
+    T = pick_fwd_tokens(rows, optin, local ? 32 : 8);
     if (T < 0) return T;
-  } else if (T != 1 && T != 2 && T != 4 && T != 8) {
+  } else if (T != 1 && T != 2 && T != 4 && T != 8 && T != 16 && T != 32) {
     return GL_ERR_UNSUPPORTED;
   }
-  if ((int64_t)a.D * T * 4 + 2048 > optin) return GL_ERR_SMEM;
+  if (rows * T * 4 + 2048 > optin) return GL_ERR_SMEM;
   const int64_t G = a.g1 - a.g0;
-  int gpc = a.groups_per_cta;
+  int gpc = local ? 1 : a.groups_per_cta;
   if (gpc <= 0) {
     const int64_t tiles = (a.B + T - 1) / T;
     const int64_t units = tiles * G;
@@ -216,10 +236,22 @@ extern "C" int gl_fwd_f32(const GlFwdArgs* args, void* stream) {
   }
   while ((G + gpc - 1) / gpc > 65535) gpc *= 2;
   cudaStream_t st = (cudaStream_t)stream;
+  if (local) {
+    switch (T) {
+      case 32: return dispatch_act_fwd<32, true>(a, gpc, st);
+      case 16: return dispatch_act_fwd<16, true>(a, gpc, st);
+      case 8: return dispatch_act_fwd<8, true>(a, gpc, st);
+      case 4: return dispatch_act_fwd<4, true>(a, gpc, st);
+      case 2: return dispatch_act_fwd<2, true>(a, gpc, st);
+      default: return dispatch_act_fwd<1, true>(a, gpc, st);
+    }
+  }
   switch (T) {
-    case 8: return dispatch_act_fwd<8>(a, gpc, st);
-    case 4: return dispatch_act_fwd<4>(a, gpc, st);
-    case 2: return dispatch_act_fwd<2>(a, gpc, st);
-    default: return dispatch_act_fwd<1>(a, gpc, st);
+    case 32: return dispatch_act_fwd<32, false>(a, gpc, st);
+    case 16: return dispatch_act_fwd<16, false>(a, gpc, st);
+    case 8: return dispatch_act_fwd<8, false>(a, gpc, st);
+    case 4: return dispatch_act_fwd<4, false>(a, gpc, st);
+    case 2: return dispatch_act_fwd<2, false>(a, gpc, st);
+    default: return dispatch_act_fwd<1, false>(a, gpc, st);
   }
 }

@@ -44,7 +44,7 @@
 extern "C" {
 #endif
 
-#define GL_ABI_VERSION 5
+#define GL_ABI_VERSION 6
 
 typedef enum GlStatus {
   GL_OK = 0,
@@ -84,6 +84,10 @@ typedef struct GlFwdArgs {
                                (the backward's fixed-point bound); NULL = not computed */
   const int32_t* order;     /* optional [g1-g0, NB*8] processing order (gl_group_order): position p of
                                group g processes slot order[g-g0][p]; NULL = slot order */
+  const int16_t* lidx;      /* optional input locality (gl_group_feature_map): the records as positions */
+  const int16_t* fmap;      /*   in their group's feature list fmap [g1-g0, fcap], nfeat [g1-g0] entries */
+  const int32_t* nfeat;     /*   each; a block then stages only its group's features.  NULL = off */
+  int64_t fcap;             /* row length of fmap (>= max nfeat) */
 } GlFwdArgs;
 
 /* Backward: with c1[t, g] = gpre[t, g - g0] / counts[g] (mean) or gpre (sum) and
@@ -119,6 +123,10 @@ typedef struct GlBwdArgs {
   const float* wabsmax;     /* [g1-g0] max |w| per group (gl_group_absmax_f32), or NULL */
   const int32_t* rowmax;    /* [g1-g0] max records per input feature (gl_group_index_maxcount), or NULL */
   const int32_t* order;     /* optional processing order, as in GlFwdArgs */
+  const int16_t* lidx;      /* optional input locality, as in GlFwdArgs */
+  const int16_t* fmap;
+  const int32_t* nfeat;
+  int64_t fcap;
 } GlBwdArgs;
 
 /* Adam(W) step over n fp32 elements, in place (sparse_pooling/optim.py:26-64):
@@ -154,6 +162,13 @@ int gl_group_absmax_f32(const float* w, const int32_t* counts, int64_t NB, int64
                         void* stream);
 int gl_group_index_maxcount(const int16_t* idx, const int32_t* counts, int64_t D, int64_t NB, int64_t g0,
                             int64_t g1, int32_t* out, void* stream);
+
+/* Per-group input feature maps (no counterpart in the reference): nf[g-g0] = number of distinct
+ * features read by group g's valid records; with fmap (row length cap) also the sorted list
+ * fmap[g-g0][0 .. nf-1], and with lidx (indices-shaped) the records as positions in that list.
+ * Call once with fmap = lidx = NULL to size cap = max nf.  Depends only on the indices. */
+int gl_group_feature_map(const int16_t* idx, const int32_t* counts, int64_t D, int64_t NB, int64_t g0, int64_t g1,
+                         int32_t cap, int32_t* nf, int16_t* fmap, int16_t* lidx, void* stream);
 
 /* Bank-aware processing order (no counterpart in the reference): out[g-g0][p], p < NB*8, is a
  * permutation of group g's slots (valid slots first, padding slots in place) such that the

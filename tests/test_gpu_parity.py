@@ -287,3 +287,68 @@ def test_windowed_indices_against_oracle(B):
     assert_close(dx, odx, what="dx", slack=sdx, **BWD)
     assert_close(dw, odw, what="dw", slack=sdw, **BWD)
     assert_close(db, odb, what="db", slack=sdb, **BWD)
+
+
+def test_feature_map_matches_torch():
+    """gl_group_feature_map: the sorted distinct features of each group's valid records, and the
+    records as positions in that list."""
+    from granulelayer_b200.layout import windowed_indices
+
+    L = SparseLayout(16384, 3 * 12288 + 77, 4, 8, 8, False)
+    idx = windowed_indices(L, "cpu", window=512, supergroup=4096, seed=5)
+    counts = L.counts_tensor("cpu").to(torch.int32)
+    di, dc = idx.cuda(), counts.cuda()
+    nf = torch.empty(L.groups, dtype=torch.int32, device="cuda")
+    _native.group_feature_map(di, dc, L.input_dim, L.blocks_per_group, 0, L.groups, nf)
+    cap = int(nf.max())
+    fmap = torch.full((L.groups, cap), -1, dtype=torch.int16, device="cuda")
+    lidx = torch.empty_like(di)
+    _native.group_feature_map(di, dc, L.input_dim, L.blocks_per_group, 0, L.groups, nf, fmap, lidx)
+    valid = L.valid_mask("cpu").view(L.groups, L.blocks_per_group, 8)
+    for g in range(L.groups):
+        used = torch.unique(idx[g][valid[g]].long())
+        n_g = int(counts[g])
+        assert int(nf[g]) == used.numel() <= 512 * (n_g // 4096 + 2)   # windows a group can straddle
+        assert torch.equal(fmap[g, :used.numel()].cpu().long(), used)
+        pos = torch.searchsorted(used, idx[g][valid[g]].long())
+        assert torch.equal(lidx[g][valid[g]].cpu().long(), pos)
+
+
+@pytest.mark.parametrize("B", [1, 40, 300])
+@pytest.mark.parametrize("accum", ["fixed", "fp32"])
+def test_input_locality_path(B, accum):
+    """Windowed indices at D = 16384: the runtime stages only each group's features (token tiles of
+    32 forward / 8 backward instead of 2 / 1); results match the oracle and the full-row path."""
+    from granulelayer_b200.layout import windowed_indices
+
+    D, G = 16384, 3
+    H = G * 12288
+    outs = []
+    for loc in ("auto", "off"):
+        lay = SparsePoolingLayer(D, H, G, shared_neurons=None, pooling="mean", dtype=torch.float32, seed=6,
+                                 bias_std=0.1, plan=PhysicalPlan(b200_locality=loc, b200_dx_accum=accum))
+        with torch.no_grad():
+            lay.indices.copy_(windowed_indices(lay.layout, "cpu", window=512, supergroup=4096, seed=6))
+        idx, w, b = lay.indices.clone(), lay.weight.detach().clone(), lay.bias.detach().clone()
+        lay = lay.cuda()
+        gen = torch.Generator().manual_seed(B)
+        x = torch.randn(B, D, generator=gen)
+        dy = torch.randn(B, G, generator=gen)
+        outs.append(_run(lay, x.numpy(), dy.numpy()))
+        assert (lay._runtime().locality() is not None) == (loc == "auto")
+    counts = SparseLayout(D, H, G, 8, 8, False).counts_tensor("cpu").numpy()
+    pre = O.forward(x.numpy(), idx.numpy(), w.numpy(), b.numpy(), counts)
+    odx, odw, odb, sdx, sdw, sdb = O.backward(x.numpy(), idx.numpy(), w.numpy(), b.numpy(), counts, dy.numpy(),
+                                              slack=True)
+    for (y, dx, dw, db) in outs:
+        assert_close(y, pre, what="y", **FWD)
+        assert_close(dx, odx, what="dx", slack=sdx, **BWD)
+        assert_close(dw, odw, what="dw", slack=sdw, **BWD)
+        assert_close(db, odb, what="db", slack=sdb, **BWD)
+
+
+def test_uniform_indices_keep_the_full_row_path():
+    lay = SparsePoolingLayer(4096, 3 * 24576, 3, shared_neurons=None, pooling="mean", dtype=torch.float32,
+                             seed=1).cuda()
+    lay(torch.randn(4, 4096, device="cuda"))
+    assert lay._runtime().locality() is None
