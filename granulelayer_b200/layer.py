@@ -6,10 +6,12 @@ parameter/buffer names and shapes (``indices``, ``weight``, ``bias``),
 ``enable_main_grad``/``zero_main_grad`` and ``effective_policy``, so that
 model code and state dicts move between the two unchanged.
 
-Execution is the B200 path only: Mode A (``shared_neurons=None``), fp32,
-single-level ``mean`` or ``sum`` pooling with identity/ReLU/GELU neuron
-activation.  Any other configuration still constructs (so checkpoints load)
-but ``forward`` raises ``UnsupportedOnB200`` instead of falling back.
+Execution is the B200 path only: Mode A (``shared_neurons=None``) and Mode B
+(``shared_neurons=C``, canonical or fragment-packed storage, with or without
+input-supergroup ``connectivity``), fp32, single-level ``mean`` or ``sum``
+pooling with identity/ReLU/GELU neuron activation.  Any other configuration
+still constructs (so checkpoints load) but ``forward`` raises
+``UnsupportedOnB200`` instead of falling back.
 """
 from __future__ import annotations
 
@@ -33,8 +35,11 @@ class SparsePoolingLayer(nn.Module):
     execution-only ``PhysicalPlan``; ``seed`` and ``bias_std`` drive the
     bit-exact seeded initialisation of ``layout.init_parameters``.
     ``backend``, ``weight_layout`` and ``workspace_budget`` are accepted for
-    compatibility; ``connectivity`` (input supergroups) is a Mode-B feature of
-    the reference and raises here.
+    compatibility.  ``connectivity`` (a ``ConnectivityPlan``, Mode B only) draws
+    the indices from input supergroups with the reference's generator
+    (supergroups.py:200-271, bit-exact) and registers its ``sg_feat``,
+    ``sg_buckets`` and ``sg_plan`` buffers (layer.py:78-84); the kernels run such
+    layers as ordinary Mode-B layers.
     """
 
     def __init__(self, input_dim: int = 1024, hidden_dim: int = 100_000_000, output_dim: int = 1024,
@@ -52,18 +57,24 @@ class SparsePoolingLayer(nn.Module):
             weight_layout = "packed" if (mode_b and backend != "triton") else "canonical"
         if weight_layout not in ("packed", "canonical"):
             raise ValueError("weight_layout must be 'auto', 'packed' or 'canonical'")
-        if connectivity is not None:
-            raise NotImplementedError("input-supergroup connectivity is a Mode-B layer option of the reference; "
-                                      "it is not part of the B200 path")
         self.layout = SparseLayout(input_dim, hidden_dim, output_dim, fan_in, shared_neurons if mode_b else 8,
                                    mode_b, packed=(weight_layout == "packed"))
         self.compute_dtype = dtype
         self.plan = plan or PhysicalPlan()
         self.backend_name = backend
         self.workspace_budget = workspace_budget
-        self.connectivity = None
+        self.connectivity = connectivity
         self.graph_stats = None
         idx, w, b = init_parameters(self.layout, device or "cpu", dtype=dtype, seed=seed, bias_std=bias_std)
+        if connectivity is not None:
+            from .supergroups import generate_indices
+
+            idx_c, graph, self.graph_stats = generate_indices(self.layout.canonical, connectivity, device or "cpu")
+            idx = self.layout.pack_indices(idx_c) if self.layout.packed else idx_c
+            self.register_buffer("sg_feat", graph.feat)
+            self.register_buffer("sg_buckets", graph.buckets)
+            self.register_buffer("sg_plan", torch.frombuffer(bytearray(connectivity.to_json().encode()),
+                                                             dtype=torch.uint8).clone())
         self.register_buffer("indices", idx)
         self.weight = nn.Parameter(w)
         self.bias = nn.Parameter(b)
@@ -85,8 +96,16 @@ class SparsePoolingLayer(nn.Module):
         return self._rt
 
     def _load_from_state_dict(self, state_dict, prefix, *args, **kwargs):
-        if state_dict.get(prefix + "sg_plan") is not None:
-            raise ValueError("checkpoint uses input-supergroup connectivity, which this layer does not have")
+        """Connectivity must agree between checkpoint and layer (layer.py:133-142)."""
+        plan = state_dict.get(prefix + "sg_plan")
+        if self.connectivity is not None and plan is not None:
+            from .supergroups import ConnectivityPlan
+
+            got = ConnectivityPlan.from_json(bytes(plan.cpu().tolist()).decode())
+            if got != self.connectivity:
+                raise ValueError(f"checkpoint connectivity {got} != layer connectivity {self.connectivity}")
+        if (self.connectivity is None) != (plan is None):
+            raise ValueError("checkpoint and layer disagree on input-supergroup connectivity")
         super()._load_from_state_dict(state_dict, prefix, *args, **kwargs)
         self._rt = None
 

@@ -122,3 +122,23 @@ def test_padding_slots_get_no_gradient():
     gw = L.unpack_weights(lay.weight.grad)
     gb = L.unpack_bias(lay.bias.grad)
     assert float(gw[pad].abs().max()) == 0.0 and float(gb[pad].abs().max()) == 0.0
+
+
+@pytest.mark.parametrize("C,packed", [(8, True), (64, False)])
+def test_supergroup_connectivity_layer(C, packed):
+    """Mode-B layers with input-supergroup connectivity run on the Mode-B kernels."""
+    from granulelayer_b200.supergroups import ConnectivityPlan
+
+    D, H, G, B = 512, 30000, 6, 29
+    lay = SparsePoolingLayer(D, H, G, shared_neurons=C, weight_layout="packed" if packed else "canonical",
+                             pooling="mean", dtype=torch.float32, seed=2, bias_std=0.1,
+                             connectivity=ConnectivityPlan(64, 3, seed=7)).cuda()
+    gen = torch.Generator().manual_seed(C)
+    x = torch.randn(B, D, generator=gen).numpy()
+    dy = torch.randn(B, G, generator=gen).numpy()
+    y, dx, dw, db = _run(lay, x, dy)
+    pre, odx, odw, odb, sdx, sdw, sdb = _oracle(lay, x, dy)
+    assert_close(y, pre, what="y", **FWD)
+    assert_close(dx, odx, what="dx", slack=sdx, **BWD)
+    assert_close(dw, odw, what="dw", slack=sdw, **BWD)
+    assert_close(db, odb, what="db", slack=sdb, **BWD)

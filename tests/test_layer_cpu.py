@@ -91,3 +91,40 @@ def test_explain_on_cpu():
 def test_plan_fields():
     lay = _layer(plan=PhysicalPlan(b200_fwd_tokens=4, b200_dx_tokens=2))
     assert lay.plan.b200_fwd_tokens == 4
+
+
+def test_connectivity_layer_matches_reference(reference_path):
+    """Input-supergroup connectivity (Mode B): the reference's layer and ours hold identical
+    buffers (indices from the supergroup generator, sg_feat, sg_buckets, sg_plan) and parameters."""
+    sys.path.insert(0, reference_path)
+    from sparse_pooling import SparsePoolingLayer as RefLayer
+    from sparse_pooling.supergroups import ConnectivityPlan as RefPlan
+
+    from granulelayer_b200.supergroups import ConnectivityPlan
+
+    for C, wl in ((8, "packed"), (64, "canonical")):
+        kw = dict(shared_neurons=C, pooling="mean", dtype=torch.float32, seed=3, bias_std=0.1, weight_layout=wl)
+        ref = RefLayer(256, 40000, 16, connectivity=RefPlan(64, 2, seed=5), **kw)
+        ours = SparsePoolingLayer(256, 40000, 16, connectivity=ConnectivityPlan(64, 2, seed=5), **kw)
+        rs, os_ = ref.state_dict(), ours.state_dict()
+        assert set(rs) == set(os_) == {"indices", "weight", "bias", "sg_feat", "sg_buckets", "sg_plan"}
+        for k in rs:
+            assert torch.equal(rs[k], os_[k]), f"{k} differs (C={C}, {wl})"
+
+
+def test_connectivity_state_dict_checks():
+    from granulelayer_b200.supergroups import ConnectivityPlan
+
+    kw = dict(shared_neurons=8, pooling="mean", dtype=torch.float32)
+    a = SparsePoolingLayer(256, 20000, 8, connectivity=ConnectivityPlan(64, 2, seed=1), **kw)
+    b = SparsePoolingLayer(256, 20000, 8, connectivity=ConnectivityPlan(64, 2, seed=2), **kw)
+    plain = SparsePoolingLayer(256, 20000, 8, **kw)
+    with pytest.raises(ValueError, match="connectivity"):
+        b.load_state_dict(a.state_dict())
+    with pytest.raises(ValueError, match="connectivity"):
+        plain.load_state_dict(a.state_dict())
+    c = SparsePoolingLayer(256, 20000, 8, connectivity=ConnectivityPlan(64, 2, seed=1), seed=9, **kw)
+    c.load_state_dict(a.state_dict())
+    assert torch.equal(c.weight, a.weight)
+    with pytest.raises(ValueError):
+        SparsePoolingLayer(256, 20000, 8, shared_neurons=None, connectivity=ConnectivityPlan(64, 2, seed=1))
