@@ -16,17 +16,17 @@ from pathlib import Path
 
 import torch
 
-ABI_VERSION = 6
+ABI_VERSION = 7
 LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libgranule_b200.so"
 
-POOL_MEAN, POOL_SUM = 0, 1
+POOL_MEAN, POOL_SUM, POOL_MAX = 0, 1, 2
 ACT_IDS = {"identity": 0, "relu": 1, "gelu": 2}
 
 # The exported entry points, in header order (checked by the CPU test suite).
 EXPORTS = ("gl_abi_version", "gl_status_string", "gl_last_cuda_error", "gl_fwd_f32", "gl_bwd_f32",
            "gl_adam_f32", "gl_group_absmax_f32", "gl_group_index_maxcount", "gl_group_feature_map",
            "gl_group_order", "gl_launch_count",
-           "gl_fwd_auto_tokens", "gl_bwd_auto_tokens", "gl_fwd_shared_f32", "gl_bwd_shared_f32",
+           "gl_fwd_auto_tokens", "gl_bwd_auto_tokens", "gl_fwd_shared_f32", "gl_bwd_shared_f32", "gl_bwd_events_f32",
            "gl_shared_auto_tokens", "gl_k16_fwd_f32", "gl_k16_bwd_f32", "gl_k16_auto_tokens")
 
 
@@ -42,7 +42,7 @@ class GlFwdArgs(ctypes.Structure):
                 ("pool", ctypes.c_int32), ("act", ctypes.c_int32), ("tokens", ctypes.c_int32),
                 ("groups_per_cta", ctypes.c_int32), ("wabsmax", ctypes.c_void_p), ("order", ctypes.c_void_p),
                 ("lidx", ctypes.c_void_p), ("fmap", ctypes.c_void_p), ("nfeat", ctypes.c_void_p),
-                ("fcap", ctypes.c_int64)]
+                ("fcap", ctypes.c_int64), ("winners", ctypes.c_void_p), ("ldwin", ctypes.c_int64)]
 
 
 class GlBwdArgs(ctypes.Structure):
@@ -69,7 +69,14 @@ class GlAdamArgs(ctypes.Structure):
 class GlSharedArgs(ctypes.Structure):
     _fields_ = [(n, ctypes.c_void_p) for n in ("x", "idx", "w", "b", "counts", "pre", "gpre", "dx", "dw", "db")] + \
                [(n, ctypes.c_int64) for n in ("B", "D", "NB", "C", "g0", "g1", "ldx", "ldp", "ldg", "lddx")] + \
-               [(n, ctypes.c_int32) for n in ("pool", "act", "packed", "tokens", "groups_per_cta", "reserved")]
+               [(n, ctypes.c_int32) for n in ("pool", "act", "packed", "tokens", "groups_per_cta", "reserved")] + \
+               [("winners", ctypes.c_void_p), ("ldwin", ctypes.c_int64)]
+
+
+class GlEventArgs(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_void_p) for n in ("x", "idx", "w", "b", "winners", "coef", "dx", "dw", "db")] + \
+               [(n, ctypes.c_int64) for n in ("B", "D", "NB", "C", "g0", "g1", "ldx", "ldwin", "ldc", "lddx")] + \
+               [(n, ctypes.c_int32) for n in ("shared", "packed", "act", "reserved")]
 
 
 class GlK16Args(ctypes.Structure):
@@ -107,7 +114,8 @@ def load(path=None) -> ctypes.CDLL:
         lib.gl_launch_count.restype = ctypes.c_int64
         for name, st in (("gl_fwd_f32", GlFwdArgs), ("gl_bwd_f32", GlBwdArgs), ("gl_adam_f32", GlAdamArgs),
                          ("gl_k16_fwd_f32", GlK16Args), ("gl_k16_bwd_f32", GlK16Args),
-                         ("gl_fwd_shared_f32", GlSharedArgs), ("gl_bwd_shared_f32", GlSharedArgs)):
+                         ("gl_fwd_shared_f32", GlSharedArgs), ("gl_bwd_shared_f32", GlSharedArgs),
+                         ("gl_bwd_events_f32", GlEventArgs)):
             fn = getattr(lib, name)
             fn.restype = ctypes.c_int
             fn.argtypes = [ctypes.POINTER(st), ctypes.c_void_p]
@@ -165,16 +173,18 @@ def _require_cuda(*ts):
 
 
 def fwd(x, idx, w, b, counts, pre, NB: int, g0: int, g1: int, pool: int, act: int, tokens: int = 0,
-        groups_per_cta: int = 0, wabsmax=None, order=None, local=None):
+        groups_per_cta: int = 0, wabsmax=None, order=None, local=None, winners=None):
     """pre[:, :g1-g0] = pooled act(z) of groups [g0, g1); optionally wabsmax[g-g0] = max |w|; ``order``
     is an optional processing order (group_order); ``local`` = (lidx, fmap, nfeat) from
-    group_feature_map turns on the per-group input staging.  See GlFwdArgs."""
+    group_feature_map turns on the per-group input staging; ``winners`` [B, g1-g0] int32 receives
+    the winning slots of max pooling.  See GlFwdArgs."""
     lidx, fmap, nfeat = local if local is not None else (None, None, None)
-    _require_cuda(x, idx, w, b, counts, pre, wabsmax, order, lidx, fmap, nfeat)
+    _require_cuda(x, idx, w, b, counts, pre, wabsmax, order, lidx, fmap, nfeat, winners)
     lib = load()
     a = GlFwdArgs(_ptr(x), _ptr(idx), _ptr(w), _ptr(b), _ptr(counts), _ptr(pre), x.shape[0], x.shape[1], NB,
                   g0, g1, x.stride(0), pre.stride(0), pool, act, tokens, groups_per_cta, _ptr(wabsmax), _ptr(order),
-                  _ptr(lidx), _ptr(fmap), _ptr(nfeat), fmap.shape[1] if fmap is not None else 0)
+                  _ptr(lidx), _ptr(fmap), _ptr(nfeat), fmap.shape[1] if fmap is not None else 0, _ptr(winners),
+                  winners.stride(0) if winners is not None else 0)
     with torch.cuda.device(x.device):
         _check(lib, lib.gl_fwd_f32(ctypes.byref(a), _stream(x.device)), "gl_fwd_f32")
 
@@ -204,12 +214,14 @@ def _shared_args(x, idx, w, b, counts, NB, C, g0, g1, pool, act, packed, tokens,
 
 
 def fwd_shared(x, idx, w, b, counts, pre, NB: int, C: int, g0: int, g1: int, pool: int, act: int, packed: bool,
-               tokens: int = 0, groups_per_cta: int = 0):
-    """Mode B forward: pre[:, :g1-g0] = pooled act(z) (GlSharedArgs)."""
-    _require_cuda(x, idx, w, b, counts, pre)
+               tokens: int = 0, groups_per_cta: int = 0, winners=None):
+    """Mode B forward: pre[:, :g1-g0] = pooled act(z); ``winners`` as in ``fwd`` (GlSharedArgs)."""
+    _require_cuda(x, idx, w, b, counts, pre, winners)
     lib = load()
     a = _shared_args(x, idx, w, b, counts, NB, C, g0, g1, pool, act, packed, tokens, groups_per_cta)
     a.pre, a.ldp = _ptr(pre), pre.stride(0)
+    if winners is not None:
+        a.winners, a.ldwin = _ptr(winners), winners.stride(0)
     with torch.cuda.device(x.device):
         _check(lib, lib.gl_fwd_shared_f32(ctypes.byref(a), _stream(x.device)), "gl_fwd_shared_f32")
 
@@ -224,6 +236,18 @@ def bwd_shared(x, idx, w, b, counts, gpre, dx, dw, db, NB: int, C: int, g0: int,
     a.ldg, a.lddx = gpre.stride(0), dx.stride(0)
     with torch.cuda.device(x.device):
         _check(lib, lib.gl_bwd_shared_f32(ctypes.byref(a), _stream(x.device)), "gl_bwd_shared_f32")
+
+
+def bwd_events(x, idx, w, b, winners, coef, dx, dw, db, NB: int, C: int, shared: bool, packed: bool, g0: int,
+               g1: int, act: int):
+    """Winner-event backward of max pooling (GlEventArgs): dx, dw, db += the winners' gradients."""
+    _require_cuda(x, idx, w, b, winners, coef, dx, dw, db)
+    lib = load()
+    a = GlEventArgs(_ptr(x), _ptr(idx), _ptr(w), _ptr(b), _ptr(winners), _ptr(coef), _ptr(dx), _ptr(dw), _ptr(db),
+                    x.shape[0], x.shape[1], NB, C, g0, g1, x.stride(0), winners.stride(0), coef.stride(0),
+                    dx.stride(0), int(bool(shared)), int(bool(packed)), act, 0)
+    with torch.cuda.device(x.device):
+        _check(lib, lib.gl_bwd_events_f32(ctypes.byref(a), _stream(x.device)), "gl_bwd_events_f32")
 
 
 def group_absmax(w, counts, NB: int, g0: int, g1: int, out):

@@ -92,7 +92,8 @@ class Level1Runtime:
         if self.counts_i32.numel() != G:
             raise ValueError(f"counts has {self.counts_i32.numel()} entries for {G} groups")
         self.counts_f32 = self.counts_i32.to(torch.float32)
-        self.pool = _native.POOL_MEAN if level.type == "mean" else _native.POOL_SUM
+        self.pool = {"mean": _native.POOL_MEAN, "sum": _native.POOL_SUM, "max": _native.POOL_MAX}.get(
+            level.type, _native.POOL_MEAN)
         self.act = _native.ACT_IDS[level.activation]
         self.last_info: Dict = {}
         self.det = False
@@ -215,28 +216,53 @@ class Level1Runtime:
             "batch": B,
         }
 
+    @property
+    def is_max(self) -> bool:
+        return self.pool == _native.POOL_MAX
+
     def forward(self, x: torch.Tensor, w: torch.Tensor, b: torch.Tensor, track_ids: bool = False):
-        """{"pre": [B, G] pooled values, "wabsmax": [G] max |w| per group (for the backward)}."""
+        """{"pre": [B, G] pooled values, "wabsmax": [G] max |w| per group (Mode A mean/sum, for the
+        backward), "winner": [B, G] int32 winning slots (max pooling, when ``track_ids``)}."""
         B = x.shape[0]
         self.check_devices(x, w, b)
         self.resolve_reduction(B)
         pre = torch.empty((B, self.groups), device=x.device, dtype=torch.float32)
+        winners = (torch.empty((B, self.groups), device=x.device, dtype=torch.int32)
+                   if self.is_max and track_ids else None)
+        out = {"pre": pre}
+        if winners is not None:
+            out["winner"] = winners
         if self.layout.shared_indices:
             _native.fwd_shared(x, self.idx, w, b, self.counts_i32, pre, self.layout.blocks_per_group,
                                self.layout.block, 0, self.groups, self.pool, self.act, self.layout.packed,
-                               tokens=self.plan.b200_fwd_tokens)
+                               tokens=self.plan.b200_fwd_tokens, winners=winners)
             self.last_info.update(forward_backend="b200", forward_kernel="gl_fwd_shared_f32", workspace_bytes=0)
-            return {"pre": pre}
-        wabsmax = torch.empty(self.groups, device=x.device, dtype=torch.float32) if B > 0 else None
+            return out
+        wabsmax = torch.empty(self.groups, device=x.device, dtype=torch.float32) if B > 0 and not self.is_max else None
         _native.fwd(x, self.idx, w, b, self.counts_i32, pre, self.layout.blocks_per_group, 0, self.groups,
                     self.pool, self.act, tokens=self.plan.b200_fwd_tokens, wabsmax=wabsmax,
                     order=self.order(self.tokens(False)) if B > 0 else None,
-                    local=self.locality() if B > 0 else None)
+                    local=self.locality() if B > 0 else None, winners=winners)
         self.last_info.update(forward_backend="b200", workspace_bytes=0)
-        out = {"pre": pre}
         if wabsmax is not None:
             out["wabsmax"] = wabsmax
         return out
+
+    def _event_backward(self, x, w, b, g_pre, saved, dw_buf, db_buf) -> torch.Tensor:
+        """Max pooling: one winner event per (token, group) (autograd.py:280-290); winners come from
+        the forward (save_winners) or are recomputed here (minimal_stats)."""
+        winners = saved.get("winner")
+        recomputed = winners is None
+        if recomputed:
+            winners = self.forward(x, w, b, track_ids=True)["winner"]
+        self.last_info["recomputed_stats"] = recomputed
+        dx = torch.zeros(x.shape, device=x.device, dtype=torch.float32)
+        L = self.layout
+        _native.bwd_events(x, self.idx, w, b, winners, g_pre, dx, dw_buf, db_buf, L.blocks_per_group, L.block,
+                           L.shared_indices, L.packed, 0, self.groups, self.act)
+        self.last_info["backward_backend"] = "b200"
+        self.last_info["backward_kernel"] = "gl_bwd_events_f32"
+        return dx
 
     def backward(self, x, w, b, g_pre: torch.Tensor, saved: Dict, policy: str, dw_buf: torch.Tensor,
                  db_buf: torch.Tensor, recomputed: bool = False) -> torch.Tensor:
@@ -245,6 +271,8 @@ class Level1Runtime:
         self.last_info["recomputed_stats"] = recomputed
         self.check_devices(x, w, b, g_pre, dw_buf, db_buf)
         self.resolve_reduction(B)
+        if self.is_max:
+            return self._event_backward(x, w, b, g_pre, saved, dw_buf, db_buf)
         dx = torch.zeros((B, D), device=x.device, dtype=torch.float32)
         if self.layout.shared_indices:
             _native.bwd_shared(x, self.idx, w, b, self.counts_i32, g_pre, dx, dw_buf, db_buf,
@@ -293,13 +321,14 @@ class SparsePoolFunction(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, w, b, rt: Level1Runtime, policy: str, compute_dtype):
         xc, wc, bc = _compute_operands(x, w, b)
-        out = rt.forward(xc, wc, bc, track_ids=False)
+        out = rt.forward(xc, wc, bc, track_ids=(policy == "save_winners"))
         pre = out["pre"]
         y = act_torch(pre, rt.level.out_activation)
         ctx.rt, ctx.policy = rt, policy
-        ctx.has_wmax = "wabsmax" in out
-        ctx.save_for_backward(x, w, b, pre, *([out["wabsmax"]] if ctx.has_wmax else []))
-        rt.last_info["checkpoint_bytes"] = pre.numel() * pre.element_size()
+        ctx.extra = [k for k in ("wabsmax", "winner") if k in out]
+        ctx.save_for_backward(x, w, b, pre, *[out[k] for k in ctx.extra])
+        rt.last_info["checkpoint_bytes"] = sum(t.numel() * t.element_size() for t in [pre] + [out[k] for k in ctx.extra
+                                                                                           if k == "winner"])
         return y
 
     @staticmethod
@@ -310,8 +339,7 @@ class SparsePoolFunction(torch.autograd.Function):
         g_pre = (dy.float() * dact_torch(pre, rt.level.out_activation)).contiguous()
         dw_buf, db_buf, use_main = _grad_buffers(w, b)
         saved = {"pre": pre}
-        if ctx.has_wmax:
-            saved["wabsmax"] = rest[0]
+        saved.update(zip(ctx.extra, rest))
         dx = rt.backward(xc, wc, bc, g_pre, saved, ctx.policy, dw_buf, db_buf)
         gw = None if use_main else dw_buf.to(w.dtype)
         gb = None if use_main else db_buf.to(b.dtype)

@@ -105,6 +105,35 @@ __device__ __forceinline__ void stage_tile(float* __restrict__ xs, const float* 
   }
 }
 
+// Element offsets of the fragment-packed layout (layout.py:146-179): with NT = C/8,
+// Q = NB*NT/4, UB = max(1, 4/NT), fragment f = j*NT + c/8, quad = f/4, fi = f%4, n = c%8:
+//   w (g, j, c, k = 2 kh + e) at [g, quad, n*4 + kh, fi, e];  b (g, j, c = 8*(f%NT) + 2 l4 + e) at
+//   [g, quad, l4, fi, e];  idx (g, j, k) at [g, j / UB, k, j % UB].
+struct MbPacked {
+  int64_t Q;
+  int NT, UB;
+};
+
+__host__ __device__ __forceinline__ MbPacked mb_packed(int C, int64_t NB) {
+  MbPacked m;
+  m.NT = C >> 3;
+  m.Q = NB * m.NT / 4;
+  m.UB = m.NT >= 4 ? 1 : 4 / m.NT;
+  return m;
+}
+
+// Offset of w (g, j, c, k = 2 kh) in the packed layout (the pair k, k+1 is contiguous).
+__device__ __forceinline__ int64_t mb_packed_w(const MbPacked& m, int64_t g, int j, int c, int kh) {
+  const int f = j * m.NT + (c >> 3);
+  return ((((g * m.Q + (f >> 2)) * 32) + (c & 7) * 4 + kh) * 4 + (f & 3)) * 2;
+}
+
+// Offset of b (g, j, c) for even c (the pair c, c+1 is contiguous).
+__device__ __forceinline__ int64_t mb_packed_b(const MbPacked& m, int64_t g, int j, int c) {
+  const int f = j * m.NT + (c >> 3);
+  return (((g * m.Q + (f >> 2)) * 4 + ((c & 7) >> 1)) * 4 + (f & 3)) * 2;
+}
+
 // Per-group input feature maps (gl_group_feature_map): when given, a block processes one group
 // and stages only the group's features, fmap[g][0 .. nfeat[g]-1], reading the records' inputs as
 // positions in that list (lidx, same shape as the indices).

@@ -26,12 +26,16 @@ namespace gl {
 
 constexpr int kFwdThreads = 512;
 
-template <int T, int ACT, bool LOCAL>
+// MAXP: max pooling (the largest act(z) over the valid slots; winner = the smallest slot attaining
+// it, kernels/triton_fused.py:129-140), with the winner slots written to `winners`; otherwise the
+// additive pools (mean, sum).
+template <int T, int ACT, bool LOCAL, bool MAXP>
 __global__ void __launch_bounds__(kFwdThreads, 1)
     fwd_kernel(const float* __restrict__ x, const int16_t* __restrict__ idx, const float* __restrict__ w,
                const float* __restrict__ bias, const int32_t* __restrict__ counts, float* __restrict__ pre,
                int B, int D, int64_t NB, int64_t g0, int64_t g1, int64_t ldx, int64_t ldp, int pool, int gpc,
-               float* __restrict__ wabsmax, const int32_t* __restrict__ order, const LocalMap lm) {
+               float* __restrict__ wabsmax, const int32_t* __restrict__ order, const LocalMap lm,
+               int32_t* __restrict__ winners, int64_t ldwin) {
   constexpr int V = T < 4 ? T : 4;   // tokens per lane
   constexpr int LPN = T / V;         // lanes per neuron
   constexpr int NPW = 32 / LPN;      // neurons per warp step
@@ -39,6 +43,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   constexpr int UNR = 2;             // neurons in flight per lane
   extern __shared__ __align__(16) float xs[];
   __shared__ float red[NW][T];
+  __shared__ int redi[MAXP ? NW : 1][T];
   __shared__ float redw[NW];
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -66,8 +71,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     const int ng = min(counts[g], slots);
     const int64_t fbase = g * (int64_t)slots;
     float acc[V];
+    int wid[V];
 #pragma unroll
-    for (int v = 0; v < V; ++v) acc[v] = 0.f;
+    for (int v = 0; v < V; ++v) {
+      acc[v] = MAXP ? -INFINITY : 0.f;
+      wid[v] = 0x7fffffff;
+    }
     float wmx = 0.f;  // max |w| over the valid slots this lane reads (for the backward's fixed-point scale)
 
     for (int s0 = warp * NPW * UNR; s0 < ng; s0 += NW * NPW * UNR) {
@@ -75,6 +84,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       W8 wr[UNR];
       float bb[UNR];
       bool ok[UNR];
+      int sl[UNR];
 #pragma unroll
       for (int u = 0; u < UNR; ++u) {
         const int s = s0 + u * NPW + nsub;
@@ -82,6 +92,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         int slot = ok[u] ? s : 0;
         if (order != nullptr && ok[u]) slot = min(max(__ldg(order + (g - g0) * (int64_t)slots + s), 0), slots - 1);
         const int64_t f = fbase + slot;
+        sl[u] = slot;
         r[u] = load_rec8(ridx + f * 8, dmax);
         wr[u] = load_w8(w + f * 8);
         bb[u] = __ldg(bias + f);
@@ -110,7 +121,17 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         }
         if (ok[u]) {
 #pragma unroll
-          for (int v = 0; v < V; ++v) acc[v] += act_f<ACT>(z[v]);
+          for (int v = 0; v < V; ++v) {
+            const float a = act_f<ACT>(z[v]);
+            if constexpr (MAXP) {
+              if (a > acc[v] || (a == acc[v] && sl[u] < wid[v])) {
+                acc[v] = a;
+                wid[v] = sl[u];
+              }
+            } else {
+              acc[v] += a;
+            }
+          }
 #pragma unroll
           for (int k = 0; k < 8; ++k) wmx = fmaxf(wmx, fabsf(wr[u].w[k]));
         }
@@ -120,10 +141,24 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 #pragma unroll
     for (int off = LPN; off < 32; off <<= 1)
 #pragma unroll
-      for (int v = 0; v < V; ++v) acc[v] += __shfl_xor_sync(kFullMask, acc[v], off);
+      for (int v = 0; v < V; ++v) {
+        const float ov = __shfl_xor_sync(kFullMask, acc[v], off);
+        if constexpr (MAXP) {
+          const int ow = __shfl_xor_sync(kFullMask, wid[v], off);
+          if (ov > acc[v] || (ov == acc[v] && ow < wid[v])) {
+            acc[v] = ov;
+            wid[v] = ow;
+          }
+        } else {
+          acc[v] += ov;
+        }
+      }
     if (lane < LPN)
 #pragma unroll
-      for (int v = 0; v < V; ++v) red[warp][lane * V + v] = acc[v];
+      for (int v = 0; v < V; ++v) {
+        red[warp][lane * V + v] = acc[v];
+        if constexpr (MAXP) redi[warp][lane * V + v] = wid[v];
+      }
     const bool want_w = wabsmax != nullptr && blockIdx.x == 0;
     if (want_w) {
 #pragma unroll
@@ -132,11 +167,29 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     }
     __syncthreads();
     if (threadIdx.x < T) {
-      float s = 0.f;
-#pragma unroll
-      for (int i = 0; i < NW; ++i) s += red[i][threadIdx.x];
       const int t = t0 + threadIdx.x;
-      if (t < B) pre[(int64_t)t * ldp + (g - g0)] = (pool == GL_POOL_MEAN) ? s / (float)ng : s;
+      if constexpr (MAXP) {
+        float m = -INFINITY;
+        int wi = 0x7fffffff;
+#pragma unroll
+        for (int i = 0; i < NW; ++i) {
+          const float v = red[i][threadIdx.x];
+          const int vi = redi[i][threadIdx.x];
+          if (v > m || (v == m && vi < wi)) {
+            m = v;
+            wi = vi;
+          }
+        }
+        if (t < B) {
+          pre[(int64_t)t * ldp + (g - g0)] = m;
+          if (winners != nullptr) winners[(int64_t)t * ldwin + (g - g0)] = wi;
+        }
+      } else {
+        float s = 0.f;
+#pragma unroll
+        for (int i = 0; i < NW; ++i) s += red[i][threadIdx.x];
+        if (t < B) pre[(int64_t)t * ldp + (g - g0)] = (pool == GL_POOL_MEAN) ? s / (float)ng : s;
+      }
     }
     if (want_w && threadIdx.x == 32) {
       float m = 0.f;
@@ -148,10 +201,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   }
 }
 
-template <int T, int ACT, bool LOCAL>
+template <int T, int ACT, bool LOCAL, bool MAXP>
 static int launch_fwd(const GlFwdArgs& a, int gpc, cudaStream_t st) {
   const size_t smem = (size_t)(LOCAL ? a.fcap : a.D) * T * sizeof(float);
-  auto kern = fwd_kernel<T, ACT, LOCAL>;
+  auto kern = fwd_kernel<T, ACT, LOCAL, MAXP>;
   int rc = ensure_dynamic_smem((const void*)kern, smem);
   if (rc) return rc;
   const int64_t tiles = (a.B + T - 1) / T;
@@ -160,21 +213,27 @@ static int launch_fwd(const GlFwdArgs& a, int gpc, cudaStream_t st) {
   dim3 grid((unsigned)tiles, (unsigned)chunks);
   const LocalMap lm{a.lidx, a.fmap, a.nfeat, (int)a.fcap};
   kern<<<grid, kFwdThreads, smem, st>>>(a.x, a.idx, a.w, a.b, a.counts, a.pre, (int)a.B, (int)a.D, a.NB, a.g0,
-                                        a.g1, a.ldx, a.ldp, a.pool, gpc, a.wabsmax, a.order, lm);
+                                        a.g1, a.ldx, a.ldp, a.pool, gpc, a.wabsmax, a.order, lm, a.winners, a.ldwin);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_cuda_error(e);
   count_launches(1);
   return GL_OK;
 }
 
-template <int T, bool LOCAL>
-static int dispatch_act_fwd(const GlFwdArgs& a, int gpc, cudaStream_t st) {
+template <int T, bool LOCAL, bool MAXP>
+static int dispatch_act_fwd2(const GlFwdArgs& a, int gpc, cudaStream_t st) {
   switch (a.act) {
-    case GL_ACT_IDENTITY: return launch_fwd<T, GL_ACT_IDENTITY, LOCAL>(a, gpc, st);
-    case GL_ACT_RELU: return launch_fwd<T, GL_ACT_RELU, LOCAL>(a, gpc, st);
-    case GL_ACT_GELU: return launch_fwd<T, GL_ACT_GELU, LOCAL>(a, gpc, st);
+    case GL_ACT_IDENTITY: return launch_fwd<T, GL_ACT_IDENTITY, LOCAL, MAXP>(a, gpc, st);
+    case GL_ACT_RELU: return launch_fwd<T, GL_ACT_RELU, LOCAL, MAXP>(a, gpc, st);
+    case GL_ACT_GELU: return launch_fwd<T, GL_ACT_GELU, LOCAL, MAXP>(a, gpc, st);
     default: return GL_ERR_UNSUPPORTED;
   }
+}
+
+template <int T, bool LOCAL>
+static int dispatch_act_fwd(const GlFwdArgs& a, int gpc, cudaStream_t st) {
+  return a.pool == GL_POOL_MAX ? dispatch_act_fwd2<T, LOCAL, true>(a, gpc, st)
+                               : dispatch_act_fwd2<T, LOCAL, false>(a, gpc, st);
 }
 
 // Largest token tile in {tmax, ..., 2, 1} whose staged input (D rows) fits the opt-in shared
@@ -205,7 +264,8 @@ extern "C" int gl_fwd_f32(const GlFwdArgs* args, void* stream) {
   if (!a.x || !a.idx || !a.w || !a.b || !a.counts || !a.pre) return GL_ERR_NULL;
   if (a.B > 2147483647LL || a.ldx < a.D || a.ldp < a.g1 - a.g0) return GL_ERR_SHAPE;
   if (((uintptr_t)a.idx & 15) || ((uintptr_t)a.w & 15)) return GL_ERR_ALIGN;
-  if (a.pool != GL_POOL_MEAN && a.pool != GL_POOL_SUM) return GL_ERR_UNSUPPORTED;
+  if (a.pool != GL_POOL_MEAN && a.pool != GL_POOL_SUM && a.pool != GL_POOL_MAX) return GL_ERR_UNSUPPORTED;
+  if (a.winners && a.ldwin < a.g1 - a.g0) return GL_ERR_SHAPE;
   int optin = 0, sms = 0;
   int rc = device_smem_optin(&optin);
   if (rc) return rc;

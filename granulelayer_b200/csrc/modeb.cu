@@ -44,24 +44,9 @@ struct MbParams {
   int B, D, C, lgLPR;  // lgLPR = log2(C / 4): lanes per record
   int64_t NB, g0, g1, ldx, ldp, ldg, lddx;
   int pool, gpc;
+  int32_t* winners;
+  int64_t ldwin;
 };
-
-// Element offsets of the fragment-packed layout (layout.py:146-179): with NT = C/8,
-// Q = NB*NT/4, UB = max(1, 4/NT), fragment f = j*NT + c/8, quad = f/4, fi = f%4, n = c%8:
-//   w (g, j, c, k = 2 kh + e) at [g, quad, n*4 + kh, fi, e];  b (g, j, c = 8*(f%NT) + 2 l4 + e) at
-//   [g, quad, l4, fi, e];  idx (g, j, k) at [g, j / UB, k, j % UB].
-struct MbPacked {
-  int64_t Q;
-  int NT, UB;
-};
-
-__device__ __forceinline__ MbPacked mb_packed(int C, int64_t NB) {
-  MbPacked m;
-  m.NT = C >> 3;
-  m.Q = NB * m.NT / 4;
-  m.UB = m.NT >= 4 ? 1 : 4 / m.NT;
-  return m;
-}
 
 template <bool PACKED>
 __device__ __forceinline__ Rec8 mb_load_rec(const MbParams& p, int64_t g, int j) {
@@ -75,18 +60,6 @@ __device__ __forceinline__ Rec8 mb_load_rec(const MbParams& p, int64_t g, int j)
     for (int k = 0; k < 8; ++k) r.i[k] = min((int)(uint16_t)__ldg(base + k * m.UB), p.D - 1);
     return r;
   }
-}
-
-// Offset of w (g, j, c, k = 2 kh) in the packed layout (the pair k, k+1 is contiguous).
-__device__ __forceinline__ int64_t mb_packed_w(const MbPacked& m, int64_t g, int j, int c, int kh) {
-  const int f = j * m.NT + (c >> 3);
-  return ((((g * m.Q + (f >> 2)) * 32) + (c & 7) * 4 + kh) * 4 + (f & 3)) * 2;
-}
-
-// Offset of b (g, j, c) for even c (the pair c, c+1 is contiguous).
-__device__ __forceinline__ int64_t mb_packed_b(const MbPacked& m, int64_t g, int j, int c) {
-  const int f = j * m.NT + (c >> 3);
-  return (((g * m.Q + (f >> 2)) * 4 + ((c & 7) >> 1)) * 4 + (f & 3)) * 2;
 }
 
 // Weights and bias of neurons c0 .. c0+3 of block j.
@@ -165,12 +138,14 @@ __device__ __forceinline__ void mb_row(const float* __restrict__ row, float (&v)
   }
 }
 
-template <int T, int ACT, bool PACKED>
+// MAXP: max pooling with the winning slot (smallest on ties) written to p.winners.
+template <int T, int ACT, bool PACKED, bool MAXP>
 __global__ void __launch_bounds__(kMbFwdThreads, 1) mb_fwd_kernel(const MbParams p) {
   constexpr int NW = kMbFwdThreads / 32;
   constexpr int TS = T < 8 ? T : 8;  // tokens per sub-chunk (registers per lane stay fixed as T grows)
   extern __shared__ __align__(16) float xs[];
   __shared__ float red[NW][T];
+  __shared__ int redi[MAXP ? NW : 1][T];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int t0 = blockIdx.x * T;
   constexpr int XLD = mb_xld<T>();
@@ -185,8 +160,12 @@ __global__ void __launch_bounds__(kMbFwdThreads, 1) mb_fwd_kernel(const MbParams
     const int ng = min(p.counts[g], slots);
     const int nbv = (ng + C - 1) / C;
     float acc[T];
+    int wid[MAXP ? T : 1];
 #pragma unroll
-    for (int t = 0; t < T; ++t) acc[t] = 0.f;
+    for (int t = 0; t < T; ++t) {
+      acc[t] = MAXP ? -INFINITY : 0.f;
+      if constexpr (MAXP) wid[t] = 0x7fffffff;
+    }
     for (int base = warp * RPW; base < nbv; base += NW * RPW) {
       const int j = base + r;
       const bool okr = j < nbv;
@@ -215,23 +194,66 @@ __global__ void __launch_bounds__(kMbFwdThreads, 1) mb_fwd_kernel(const MbParams
         for (int n = 0; n < 4; ++n)
           if (n < nv)
 #pragma unroll
-            for (int t = 0; t < TS; ++t) acc[tc + t] += act_f<ACT>(z[n][t]);
+            for (int t = 0; t < TS; ++t) {
+              const float a = act_f<ACT>(z[n][t]);
+              if constexpr (MAXP) {
+                const int slot = j * C + nq * 4 + n;
+                if (a > acc[tc + t] || (a == acc[tc + t] && slot < wid[tc + t])) {
+                  acc[tc + t] = a;
+                  wid[tc + t] = slot;
+                }
+              } else {
+                acc[tc + t] += a;
+              }
+            }
       }
     }
 #pragma unroll
     for (int off = 16; off; off >>= 1)
 #pragma unroll
-      for (int t = 0; t < T; ++t) acc[t] += __shfl_xor_sync(kFullMask, acc[t], off);
+      for (int t = 0; t < T; ++t) {
+        const float ov = __shfl_xor_sync(kFullMask, acc[t], off);
+        if constexpr (MAXP) {
+          const int ow = __shfl_xor_sync(kFullMask, wid[t], off);
+          if (ov > acc[t] || (ov == acc[t] && ow < wid[t])) {
+            acc[t] = ov;
+            wid[t] = ow;
+          }
+        } else {
+          acc[t] += ov;
+        }
+      }
     if (lane == 0)
 #pragma unroll
-      for (int t = 0; t < T; ++t) red[warp][t] = acc[t];
+      for (int t = 0; t < T; ++t) {
+        red[warp][t] = acc[t];
+        if constexpr (MAXP) redi[warp][t] = wid[t];
+      }
     __syncthreads();
     if (threadIdx.x < T) {
-      float s = 0.f;
-#pragma unroll
-      for (int i = 0; i < NW; ++i) s += red[i][threadIdx.x];
       const int t = t0 + threadIdx.x;
-      if (t < p.B) p.pre[(int64_t)t * p.ldp + (g - p.g0)] = p.pool == GL_POOL_MEAN ? s / (float)ng : s;
+      if constexpr (MAXP) {
+        float m = -INFINITY;
+        int wi = 0x7fffffff;
+#pragma unroll
+        for (int i = 0; i < NW; ++i) {
+          const float v = red[i][threadIdx.x];
+          const int vi = redi[i][threadIdx.x];
+          if (v > m || (v == m && vi < wi)) {
+            m = v;
+            wi = vi;
+          }
+        }
+        if (t < p.B) {
+          p.pre[(int64_t)t * p.ldp + (g - p.g0)] = m;
+          if (p.winners != nullptr) p.winners[(int64_t)t * p.ldwin + (g - p.g0)] = wi;
+        }
+      } else {
+        float s = 0.f;
+#pragma unroll
+        for (int i = 0; i < NW; ++i) s += red[i][threadIdx.x];
+        if (t < p.B) p.pre[(int64_t)t * p.ldp + (g - p.g0)] = p.pool == GL_POOL_MEAN ? s / (float)ng : s;
+      }
     }
     __syncthreads();
   }
@@ -388,7 +410,10 @@ static int64_t mb_smem_bytes(int64_t D, int T, bool bwd) {
 template <int T, int ACT, bool PACKED>
 static int mb_launch(const MbParams& p, bool bwd, cudaStream_t st) {
   const size_t smem = (size_t)mb_smem_bytes(p.D, T, bwd);
-  const void* kern = bwd ? (const void*)mb_bwd_kernel<T, ACT, PACKED> : (const void*)mb_fwd_kernel<T, ACT, PACKED>;
+  const bool maxp = !bwd && p.pool == GL_POOL_MAX;
+  const void* kern = bwd ? (const void*)mb_bwd_kernel<T, ACT, PACKED>
+                         : (maxp ? (const void*)mb_fwd_kernel<T, ACT, PACKED, true>
+                                 : (const void*)mb_fwd_kernel<T, ACT, PACKED, false>);
   int rc = ensure_dynamic_smem(kern, smem);
   if (rc) return rc;
   const int64_t tiles = (p.B + T - 1) / T;
@@ -396,7 +421,8 @@ static int mb_launch(const MbParams& p, bool bwd, cudaStream_t st) {
   if (tiles > 2147483647LL || chunks > 65535) return GL_ERR_SHAPE;
   const dim3 grid((unsigned)tiles, (unsigned)chunks);
   if (bwd) mb_bwd_kernel<T, ACT, PACKED><<<grid, kMbBwdThreads, smem, st>>>(p);
-  else mb_fwd_kernel<T, ACT, PACKED><<<grid, kMbFwdThreads, smem, st>>>(p);
+  else if (maxp) mb_fwd_kernel<T, ACT, PACKED, true><<<grid, kMbFwdThreads, smem, st>>>(p);
+  else mb_fwd_kernel<T, ACT, PACKED, false><<<grid, kMbFwdThreads, smem, st>>>(p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_cuda_error(e);
   count_launches(1);
@@ -434,7 +460,8 @@ static int mb_run(const GlSharedArgs& a, bool bwd, void* stream) {
   if (!a.x || !a.idx || !a.w || !a.b || !a.counts) return GL_ERR_NULL;
   if (a.B > 2147483647LL || a.ldx < a.D || a.NB * a.C > 2147483647LL) return GL_ERR_SHAPE;
   if (((uintptr_t)a.idx & 15) || ((uintptr_t)a.w & 15) || ((uintptr_t)a.b & 15)) return GL_ERR_ALIGN;
-  if (a.pool != GL_POOL_MEAN && a.pool != GL_POOL_SUM) return GL_ERR_UNSUPPORTED;
+  if (a.pool != GL_POOL_MEAN && a.pool != GL_POOL_SUM && !(a.pool == GL_POOL_MAX && !bwd)) return GL_ERR_UNSUPPORTED;
+  if (a.winners && a.ldwin < a.g1 - a.g0) return GL_ERR_SHAPE;
   if (!bwd) {
     if (!a.pre) return GL_ERR_NULL;
     if (a.ldp < a.g1 - a.g0) return GL_ERR_SHAPE;
@@ -451,6 +478,7 @@ static int mb_run(const GlSharedArgs& a, bool bwd, void* stream) {
   if (T == 0) {
     T = mb_pick_tokens(a.D, bwd, optin);
     if (T < 0) return T;
+    if (a.pool == GL_POOL_MAX && T > 16) T = 16;  // max keeps a winner per token in registers
   } else if (T != 1 && T != 2 && T != 4 && T != 8 && T != 16 && T != 32) {
     return GL_ERR_UNSUPPORTED;
   }
@@ -469,7 +497,7 @@ static int mb_run(const GlSharedArgs& a, bool bwd, void* stream) {
   p.B = (int)a.B; p.D = (int)a.D; p.C = (int)a.C;
   p.lgLPR = a.C == 8 ? 1 : a.C == 16 ? 2 : a.C == 32 ? 3 : 4;
   p.NB = a.NB; p.g0 = a.g0; p.g1 = a.g1; p.ldx = a.ldx; p.ldp = a.ldp; p.ldg = a.ldg; p.lddx = a.lddx;
-  p.pool = a.pool; p.gpc = gpc;
+  p.pool = a.pool; p.gpc = gpc; p.winners = a.winners; p.ldwin = a.ldwin;
   cudaStream_t st = (cudaStream_t)stream;
   const bool packed = a.packed != 0;
   switch (T) {

@@ -44,7 +44,7 @@
 extern "C" {
 #endif
 
-#define GL_ABI_VERSION 6
+#define GL_ABI_VERSION 7
 
 typedef enum GlStatus {
   GL_OK = 0,
@@ -57,9 +57,11 @@ typedef enum GlStatus {
   GL_ERR_DEVICE = -7         /* no usable device / attribute query failed */
 } GlStatus;
 
-/* Pool ids: the reference's "mean" (sparse_pooling/config.py:22-29) and the
-   "sum" extension.  Activation ids follow config.py:33. */
-enum { GL_POOL_MEAN = 0, GL_POOL_SUM = 1 };
+/* Pool ids: the reference's "mean" and "max" (sparse_pooling/config.py:22-29) and the
+   "sum" extension.  Activation ids follow config.py:33.  Max pools act(z) over the valid
+   slots; its winner is the smallest slot attaining the maximum (kernels/triton_fused.py:129-140)
+   and its backward is the winner-event kernel gl_bwd_events_f32. */
+enum { GL_POOL_MEAN = 0, GL_POOL_SUM = 1, GL_POOL_MAX = 2 };
 enum { GL_ACT_IDENTITY = 0, GL_ACT_RELU = 1, GL_ACT_GELU = 2 };
 
 /* Forward: pre[t, g - g0] = pool_{valid s of g} act(z[t, g, s]),
@@ -88,6 +90,8 @@ typedef struct GlFwdArgs {
   const int16_t* fmap;      /*   in their group's feature list fmap [g1-g0, fcap], nfeat [g1-g0] entries */
   const int32_t* nfeat;     /*   each; a block then stages only its group's features.  NULL = off */
   int64_t fcap;             /* row length of fmap (>= max nfeat) */
+  int32_t* winners;         /* GL_POOL_MAX: optional [B, ldwin] output, the winning slot of each (t, g) */
+  int64_t ldwin;
 } GlFwdArgs;
 
 /* Backward: with c1[t, g] = gpre[t, g - g0] / counts[g] (mean) or gpre (sum) and
@@ -210,12 +214,41 @@ typedef struct GlSharedArgs {
   int32_t tokens;           /* token tile (0 = automatic; else 1, 2, 4 or 8) */
   int32_t groups_per_cta;   /* 0 = automatic */
   int32_t reserved;         /* 0 */
+  int32_t* winners;         /* forward, GL_POOL_MAX: optional [B, ldwin] winning slots */
+  int64_t ldwin;
 } GlSharedArgs;
 
 int gl_fwd_shared_f32(const GlSharedArgs* args, void* stream);
 int gl_bwd_shared_f32(const GlSharedArgs* args, void* stream);
 /* Token tile the automatic choice would use for input_dim D, or a negative status. */
 int gl_shared_auto_tokens(int64_t D, int32_t backward);
+
+/* Winner-event backward of max pooling, Mode A or Mode B (replaces kernels/triton_fused.py:476-520
+ * bwd_events_kernel, launched by kernels/ops.py:281-293).  For each (t, g) in [0, B) x [g0, g1),
+ * with s = winners[t, g-g0] (the slot the forward's max chose) and c = coef[t, g-g0] (dL/dpre):
+ *   dz = c * act'(z[t, g, s]); db[s] += dz; dw[s][k] += dz * x[t, idx_k]; dx[t, idx_k] += dz * w[s][k]
+ * Events with s < 0 or c == 0 are skipped.  Storage as in GlBwdArgs (Mode A) or GlSharedArgs (Mode B:
+ * shared = 1, C, packed); dx, dw, db are accumulated. */
+typedef struct GlEventArgs {
+  const float* x;           /* [B, ldx] */
+  const int16_t* idx;       /* 16-byte aligned */
+  const float* w;           /* 16-byte aligned */
+  const float* b;
+  const int32_t* winners;   /* [B, ldwin] */
+  const float* coef;        /* [B, ldc] */
+  float* dx;                /* [B, lddx] */
+  float* dw;                /* 8-byte aligned */
+  float* db;
+  int64_t B, D, NB, C;      /* C: neurons per block (Mode B) */
+  int64_t g0, g1;
+  int64_t ldx, ldwin, ldc, lddx;
+  int32_t shared;           /* 0 = Mode A, 1 = Mode B */
+  int32_t packed;           /* Mode B storage: 0 = canonical, 1 = fragment-packed */
+  int32_t act;              /* GL_ACT_* */
+  int32_t reserved;         /* 0 */
+} GlEventArgs;
+
+int gl_bwd_events_f32(const GlEventArgs* args, void* stream);
 
 /* Compact K16/C16 execution of the Cover-TopK/16 layer, fp32.
  * Replaces the reference's kgen entry points at K = 16 (experimental/kgen/kgen_abi.cu,

@@ -60,7 +60,23 @@ def load_case(name):
 
 def case_names():
     """Mode-A golden cases."""
-    return sorted(p.stem[len("fwdbwd_"):] for p in GOLDEN.glob("fwdbwd_*.npz") if not p.stem.startswith("fwdbwd_modeb_"))
+    return sorted(p.stem[len("fwdbwd_"):] for p in GOLDEN.glob("fwdbwd_*.npz")
+                  if not p.stem.startswith(("fwdbwd_modeb_", "fwdbwd_max_")))
+
+
+def max_case_names():
+    """Max-pooling golden cases (Mode A and Mode B)."""
+    return sorted(p.stem[len("fwdbwd_"):] for p in GOLDEN.glob("fwdbwd_max_*.npz"))
+
+
+def max_case_params(meta):
+    """(layout, idx, w, b) of a max-pooling golden case in the layer's storage layout."""
+    from granulelayer_b200.layout import SparseLayout, init_parameters
+
+    C = meta["C"]
+    L = SparseLayout(meta["D"], meta["H"], meta["G"], 8, C or 8, C is not None, packed=meta["packed"])
+    idx, w, b = init_parameters(L, "cpu", dtype=torch.float32, seed=meta["seed"], bias_std=meta["bias_std"])
+    return L, idx, w, b
 
 
 def modeb_case_names():

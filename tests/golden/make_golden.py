@@ -22,6 +22,9 @@ What it writes (all from the reference's own code on the CPU):
   fragment-packed storage) rebuilt from seeds, with the reference's float64
   ``reference_forward`` output and autograd gradients (dw/db in the layer's own
   storage layout, first groups only).
+* ``fwdbwd_max_<case>.npz`` — max pooling (Mode A and Mode B) with the reference's
+  ``reference_forward`` (winner = smallest slot attaining the max) and autograd gradients,
+  plus the winner slots.
 * ``graph_hashes.json`` — sha256 of the reference's input-supergroup graphs: Mode-B
   ``supergroups.generate_indices`` (indices, feature sets, buckets) and the generalized
   ``experimental/kgen_graph.generate`` (K = 64 / C = 256 envelope, K = 16 / C = 16).
@@ -66,6 +69,13 @@ MODEB_CASES = [
     ("modeb_c16_gelu", 300, 5000, 3, 16, False, 19, 7, 0.2, "mean", "gelu"),
     ("modeb_c32_packed_sum", 1024, 12288, 4, 32, True, 9, 8, 0.1, "sum", "relu"),
     ("modeb_c8_packed_identity", 128, 3001, 5, 8, True, 1, 9, 0.3, "mean", "identity"),
+]
+
+# Max pooling: (name, D, H, G, C (None = Mode A), packed, B, seed, bias_std, activation)
+MAX_CASES = [
+    ("max_modea_relu", 128, 6000, 12, None, False, 23, 11, 0.2, "relu"),
+    ("max_modea_identity_ragged", 96, 1001, 7, None, False, 9, 12, 0.1, "identity"),
+    ("max_modeb_c8_packed_gelu", 256, 7000, 5, 8, True, 17, 13, 0.2, "gelu"),
 ]
 
 # (D, H, G, C, S, R, generation, seed): Mode-B input-supergroup graphs
@@ -180,6 +190,30 @@ def main():
                                  b_sha=sha(b))),
             idx=np.zeros(0, np.int16), x=x.numpy(), dy=dy.numpy(), y=y.detach().float().numpy(),
             dx=xd.grad.float().numpy(), dw=wd.grad[:GSUB].float().numpy(), db=bd.grad[:GSUB].float().numpy())
+
+    for name, D, H, G, C, packed, B, seed, bstd, act in MAX_CASES:
+        L = SparseLayout(D, H, G, 8, C or 8, C is not None, packed=packed)
+        idx, w, b = init_parameters(L, "cpu", dtype=torch.float32, seed=seed, bias_std=bstd)
+        gen = torch.Generator().manual_seed(3000 + seed)
+        x = torch.randn(B, D, generator=gen)
+        xd = x.double().requires_grad_(True)
+        wd = w.double().requires_grad_(True)
+        bd = b.double().requires_grad_(True)
+        y = ref.reference_forward(xd, idx, wd, bd, L, PoolingConfig([LevelSpec("max", activation=act)]))
+        z = ref.hidden_preactivations(xd.detach(), idx, wd.detach(), bd.detach(), L)
+        a = ref.activation(z, act)
+        a = torch.where(L.canonical.valid_mask("cpu")[None], a, torch.full_like(a, float("-inf")))
+        winner = torch.argmax(a, dim=-1).to(torch.int32)
+        dy = torch.randn(y.shape, generator=gen)
+        (y * dy.double()).sum().backward()
+        np.savez_compressed(
+            HERE / f"fwdbwd_{name}.npz",
+            meta=json.dumps(dict(name=name, D=D, H=H, G=G, C=C, packed=packed, B=B, seed=seed, bias_std=bstd,
+                                 pool="max", act=act, rule="distinct", mode="A" if C is None else "B",
+                                 idx_sha=sha(idx), w_sha=sha(w), b_sha=sha(b))),
+            idx=np.zeros(0, np.int16), x=x.numpy(), dy=dy.numpy(), y=y.detach().float().numpy(),
+            winner=winner.numpy(), dx=xd.grad.float().numpy(), dw=wd.grad[:GSUB].float().numpy(),
+            db=bd.grad[:GSUB].float().numpy())
 
     # input-supergroup graphs (supergroups.py generate_indices; kgen_graph.py generate)
     from sparse_pooling.experimental import kgen_graph as KG

@@ -37,7 +37,7 @@ def test_mode_b_cpu_forward_has_no_fallback(kw):
         lay(torch.randn(2, 64))
 
 
-@pytest.mark.parametrize("kw", [dict(pooling="max"), dict(dtype=torch.bfloat16),
+@pytest.mark.parametrize("kw", [dict(pooling="topk_mean"), dict(dtype=torch.bfloat16),
                                 dict(pooling={"levels": [{"type": "mean", "neurons_per_shard": 128},
                                                          {"type": "weighted_sum"}]})])
 def test_unsupported_configurations_raise(kw):
