@@ -38,8 +38,8 @@ once with the reference's uniform index rule and once with windowed indices (eac
 
 ``--workload modeb`` times Mode B (C neurons share one index record; the reference's
 production mode and the configuration of its published RTX 3090 table): H = 100,000,000,
-D = G = 1024, B = 8192, Mean(ReLU), fragment-packed storage, fwd + bwd + fused Adam (fp32),
-for C = 8 and C = 64.
+D = G = 1024, B = 8192, Mean(ReLU) and Max (identity, save_winners), fragment-packed storage,
+fwd + bwd + fused Adam (fp32), for C = 8 and C = 64.
 
 ``--impl reference`` times the reference's CPU path (the oracle port: the
 reference's materialising PyTorch path does not fit 100M neurons) on the same
@@ -452,21 +452,23 @@ def bench_fwdbwd256(args):
 
 
 MB_METRIC = "neuron-samples/s fwd+bwd+opt, Mode B C=64, H=1e8, D=G=1024, B=8192"
-MB_PUBLISHED_MS = {8: 4898.4, 64: 2360.8}   # RTX 3090, BF16 (results/TABLES.md:14, 35): context only
+MB_PUBLISHED_MS = {("mean", 8): 4898.4, ("mean", 64): 2360.8,   # RTX 3090, BF16 (results/TABLES.md:14, 35,
+                   ("max", 8): 513.2, ("max", 64): 409.9}      # 8, 29): context only
 
 
 def bench_modeb(args):
     """Mode-B step at the published table's configuration (module docstring); rank 0 only."""
     from granulelayer_b200 import FusedAdamW, SparsePoolingLayer, _native
 
-    Hm, Dm, Gm, Bm = 100_000_000, 1024, 1024, 8192
+    Hm, Dm, Gm, Bm = args.modeb_neurons, 1024, 1024, 8192
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     rows = []
     launches = 0
     with ClockSampler(dev.index) as clk:
-        for C in (8, 64):
-            lay = SparsePoolingLayer(Dm, Hm, Gm, shared_neurons=C, pooling="mean", dtype=torch.float32, device=dev,
+        for pool, C in (("mean", 8), ("mean", 64), ("max", 8), ("max", 64)):
+            pooling = pool   # the operators' default activations: Mean(ReLU), Max(identity)
+            lay = SparsePoolingLayer(Dm, Hm, Gm, shared_neurons=C, pooling=pooling, dtype=torch.float32, device=dev,
                                      seed=0, weight_layout="packed")
             lay.enable_main_grad()
             opt = FusedAdamW([lay.weight, lay.bias], lr=1e-3, betas=(0.9, 0.999), eps=1e-8, moments="fp32")
@@ -474,7 +476,8 @@ def bench_modeb(args):
             x = torch.randn(Bm, Dm, device=dev, generator=gen)
             dy = torch.randn(Bm, Gm, device=dev, generator=gen)
             ev = {"fwd": [], "bwd": []}
-            orig = {"fwd": _native.fwd_shared, "bwd": _native.bwd_shared}
+            bwd_name = "bwd_events" if pool == "max" else "bwd_shared"
+            orig = {"fwd": _native.fwd_shared, "bwd": getattr(_native, bwd_name)}
 
             def timed(name):
                 def wrap(*a, **k):
@@ -492,7 +495,8 @@ def bench_modeb(args):
             for _ in range(max(3, args.warmup)):
                 step()
             torch.cuda.synchronize(dev)
-            _native.fwd_shared, _native.bwd_shared = timed("fwd"), timed("bwd")
+            _native.fwd_shared = timed("fwd")
+            setattr(_native, bwd_name, timed("bwd"))
             n0 = _native.launch_count()
             steps = max(1, min(args.steps, 5))
             s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -503,25 +507,27 @@ def bench_modeb(args):
                 e_ev.record()
                 torch.cuda.synchronize(dev)
             finally:
-                _native.fwd_shared, _native.bwd_shared = orig["fwd"], orig["bwd"]
+                _native.fwd_shared = orig["fwd"]
+                setattr(_native, bwd_name, orig["bwd"])
             launches += _native.launch_count() - n0
             ms = s_ev.elapsed_time(e_ev) / steps
-            rows.append({"C": C, "steps": steps, "ms_per_step": ms, "neuron_samples_per_s": Bm * Hm / (ms / 1e3),
+            rows.append({"pool": pool, "C": C, "steps": steps, "ms_per_step": ms,
+                         "neuron_samples_per_s": Bm * Hm / (ms / 1e3),
                          "fwd_ms": statistics.mean(a.elapsed_time(b) for a, b in ev["fwd"]),
                          "bwd_ms": statistics.mean(a.elapsed_time(b) for a, b in ev["bwd"]),
                          "fwd_tflops": 2 * 8 * Hm * Bm / (statistics.mean(a.elapsed_time(b) for a, b in ev["fwd"])
                                                           * 1e-3) / 1e12,
-                         "published_rtx3090_bf16_ms": MB_PUBLISHED_MS[C]})
+                         "published_rtx3090_bf16_ms": MB_PUBLISHED_MS[(pool, C)]})
             del lay, opt
             torch.cuda.empty_cache()
-    head = rows[-1]
+    head = next(r for r in rows if r["pool"] == "mean" and r["C"] == 64)
     line = {
         "metric": MB_METRIC, "value": head["neuron_samples_per_s"], "unit": UNIT, "n_gpus": 1,
         "steps": head["steps"], "warmup": max(3, args.warmup), "ms_per_step": head["ms_per_step"],
         "higher_is_better": True, "scaling": "none", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "Mode B (shared index records), Mean(ReLU), fwd+bwd+fused Adam, fragment-packed "
-                               "storage, fp32 (the reference's published table runs BF16 on an RTX 3090)",
-                   "H": Hm, "D": Dm, "G": Gm, "global_batch": Bm, "C": [8, 64]},
+        "config": {"workload": "Mode B (shared index records), Mean(ReLU) and Max, fwd+bwd+fused Adam, "
+                               "fragment-packed storage, fp32 (the reference's published table runs BF16 on an "
+                               "RTX 3090)", "H": Hm, "D": Dm, "G": Gm, "global_batch": Bm, "C": [8, 64]},
         "rows": rows, "clocks": clk.summary(), "gpu_launches": launches,
     }
     print(json.dumps(line), flush=True)
@@ -608,6 +614,8 @@ def main():
     ap.add_argument("--ref-seconds", type=float, default=4.0)
     ap.add_argument("--workload", default="layer100m", choices=["layer100m", "fwdbwd256", "cover16", "locality", "modeb"])
     ap.add_argument("--batches", default="1,32,256,1024,4096", help="locality: batch sizes of the sweep")
+    ap.add_argument("--modeb-neurons", type=int, default=100_000_000,
+                    help="modeb: neurons (default 1e8 = the published table; fewer for ncu captures)")
     ap.add_argument("--cover-outputs", type=int, default=2048,
                     help="cover16: outputs of 24,576 neurons (default 2048 = config 4; fewer for ncu captures)")
     ap.add_argument("--groups", type=int, default=G,
