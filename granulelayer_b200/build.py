@@ -7,7 +7,8 @@ into one shared object that exports the C ABI declared in
 instance; outside one it finds the toolkit's copy through its rpath.
 
 Run ``python -m granulelayer_b200.build`` (or ``__graft_entry__.build()``).
-Objects are rebuilt when a source or header is newer than the library.
+Objects are rebuilt when a source or header is newer than the library; the
+sources compile in parallel (one nvcc per core).
 """
 from __future__ import annotations
 
@@ -15,6 +16,7 @@ import os
 import shutil
 import subprocess
 import sys
+from concurrent.futures import ThreadPoolExecutor
 from pathlib import Path
 
 PKG = Path(__file__).resolve().parent
@@ -54,15 +56,21 @@ def build(verbose: bool = False, force: bool = False) -> Path:
     obj_dir.mkdir(exist_ok=True)
     headers = list(CSRC.glob("*.cuh")) + list(INCLUDE.glob("*.h"))
     flags = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", f"-I{INCLUDE}", f"-I{CSRC}", *ARCH]
-    objs = []
+    objs, cmds = [], []
     for src in sources():
         obj = obj_dir / (src.stem + ".o")
         objs.append(obj)
         if force or _stale(obj, [src, *headers]):
-            cmd = [nvcc(), "-c", str(src), "-o", str(obj), *flags]
-            if verbose:
-                print(" ".join(cmd), flush=True)
-            subprocess.run(cmd, check=True)
+            cmds.append([nvcc(), "-c", str(src), "-o", str(obj), *flags])
+
+    def compile_one(cmd):
+        if verbose:
+            print(" ".join(cmd), flush=True)
+        subprocess.run(cmd, check=True)
+
+    if cmds:
+        with ThreadPoolExecutor(max_workers=max(1, min(len(cmds), os.cpu_count() or 1))) as ex:
+            list(ex.map(compile_one, cmds))
     if force or _stale(LIB, objs):
         cmd = [nvcc(), "-shared", "-o", str(LIB), *map(str, objs), *ARCH, "-cudart", "shared",
                "-Xlinker", f"-rpath={CUDA_HOME / 'lib64'}"]
