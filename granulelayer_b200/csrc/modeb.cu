@@ -27,8 +27,9 @@ __global__ void __launch_bounds__(kMbFwdThreads, 1) mb_fwd_kernel(const MbParams
   constexpr int NW = kMbFwdThreads / 32;
   constexpr int TS = T < 8 ? T : 8;  // tokens per sub-chunk (registers per lane stay fixed as T grows)
   extern __shared__ __align__(16) float xs[];
-  __shared__ float red[NW][T];
-  __shared__ int redi[MAXP ? NW : 1][T];
+  // per-warp partials, double-buffered by group parity: one barrier per group
+  __shared__ float red[2][NW][T];
+  __shared__ int redi[2][MAXP ? NW : 1][T];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int t0 = blockIdx.x * T;
   constexpr int XLD = mb_xld<T>();
@@ -42,6 +43,7 @@ __global__ void __launch_bounds__(kMbFwdThreads, 1) mb_fwd_kernel(const MbParams
   for (int64_t g = gb; g < ge; ++g) {
     const int ng = min(p.counts[g], slots);
     const int nbv = (ng + C - 1) / C;
+    const int buf = (int)((g - gb) & 1);
     float acc[T];
     int wid[MAXP ? T : 1];
 #pragma unroll
@@ -109,8 +111,8 @@ __global__ void __launch_bounds__(kMbFwdThreads, 1) mb_fwd_kernel(const MbParams
     if (lane == 0)
 #pragma unroll
       for (int t = 0; t < T; ++t) {
-        red[warp][t] = acc[t];
-        if constexpr (MAXP) redi[warp][t] = wid[t];
+        red[buf][warp][t] = acc[t];
+        if constexpr (MAXP) redi[buf][warp][t] = wid[t];
       }
     __syncthreads();
     if (threadIdx.x < T) {
@@ -120,8 +122,8 @@ __global__ void __launch_bounds__(kMbFwdThreads, 1) mb_fwd_kernel(const MbParams
         int wi = 0x7fffffff;
 #pragma unroll
         for (int i = 0; i < NW; ++i) {
-          const float v = red[i][threadIdx.x];
-          const int vi = redi[i][threadIdx.x];
+          const float v = red[buf][i][threadIdx.x];
+          const int vi = redi[buf][i][threadIdx.x];
           if (v > m || (v == m && vi < wi)) {
             m = v;
             wi = vi;
@@ -134,11 +136,12 @@ __global__ void __launch_bounds__(kMbFwdThreads, 1) mb_fwd_kernel(const MbParams
       } else {
         float s = 0.f;
 #pragma unroll
-        for (int i = 0; i < NW; ++i) s += red[i][threadIdx.x];
+        for (int i = 0; i < NW; ++i) s += red[buf][i][threadIdx.x];
         if (t < p.B) p.pre[(int64_t)t * p.ldp + (g - p.g0)] = p.pool == GL_POOL_MEAN ? s / (float)ng : s;
       }
     }
-    __syncthreads();
+    // no second barrier: the next group writes the other buffer, and a warp can write this one
+    // again only after the next group's barrier, which the reducing threads reach after reading it
   }
 }
 
@@ -181,7 +184,7 @@ static int mb_dispatch(const MbParams& p, int act, bool packed, bool bwd, cudaSt
 // Largest token tile in {32, 16, 8, 4, 2, 1} whose tiles (1 forward, 2 backward) fit the opt-in shared memory.
 static int mb_pick_tokens(int64_t D, bool bwd, int optin) {
   for (int T = 32; T >= 1; T >>= 1)
-    if (mb_smem_bytes(D, T, bwd) + 2048 <= optin) return T;
+    if (mb_smem_bytes(D, T, bwd) + kMbStaticSmem <= optin) return T;
   return GL_ERR_SMEM;
 }
 
@@ -212,11 +215,10 @@ static int mb_run(const GlSharedArgs& a, bool bwd, void* stream) {
   if (T == 0) {
     T = mb_pick_tokens(a.D, bwd, optin);
     if (T < 0) return T;
-    if (a.pool == GL_POOL_MAX && T > 16) T = 16;  // max keeps a winner per token in registers
   } else if (T != 1 && T != 2 && T != 4 && T != 8 && T != 16 && T != 32) {
     return GL_ERR_UNSUPPORTED;
   }
-  if (mb_smem_bytes(a.D, T, bwd) + 2048 > optin) return GL_ERR_SMEM;
+  if (mb_smem_bytes(a.D, T, bwd) + kMbStaticSmem > optin) return GL_ERR_SMEM;
   const int64_t G = a.g1 - a.g0;
   int gpc = a.groups_per_cta;
   if (gpc <= 0) {

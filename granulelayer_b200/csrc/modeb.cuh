@@ -7,6 +7,7 @@ namespace gl {
 
 constexpr int kMbFwdThreads = 384;
 constexpr int kMbBwdThreads = 256;
+constexpr int kMbStaticSmem = 8192;  // bound on either kernel's static shared memory (reduction buffers)
 
 struct MbParams {
   const float* x;

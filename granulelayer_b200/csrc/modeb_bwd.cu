@@ -13,12 +13,14 @@
 // flushed to dx once per block.
 //
 // Select-free transpose-reduction.  At stage s the lanes whose lane bit s is set keep the upper
-// half of their partials and send the lower half.  Each lane instead holds its partials with k
-// XOR-permuted by a mask of its own lane bits (kmask): a[k'][t] is the partial of k' ^ kmask.  It
-// gets that order for free by permuting its record's input rows and its weight columns once per
-// record; every lane then keeps the lower half and sends the upper half, and the sum it ends with
-// belongs to row ri[k'] of its permuted record.  The stage over a token bit (C = 64, the fourth
-// stage) uses explicit selects.
+// half of their partials and send the lower half.  Each lane instead forms its partials with k
+// XOR-permuted by a mask of its own lane bits (kmask): a[k'][t] is the partial of k' ^ kmask,
+// computed from a second copy of its weights loaded with permuted columns (the pair index
+// permutation is an address change, the bit-0 swap a select).  Every lane then keeps the lower
+// half and sends the upper half, and the sum it ends with belongs to row idx[k' ^ kmask].  The x
+// reads, z and dW keep the natural order, so the record's lanes read the same x row at the same
+// time (one shared-memory broadcast).  The stage over a token bit (C = 64, the fourth stage) uses
+// explicit selects.
 #include "modeb.cuh"
 
 namespace gl {
@@ -40,11 +42,10 @@ __device__ __forceinline__ void mb_xor_perm8(V (&v)[8], int km) {
   }
 }
 
-// Weights of neurons c0 .. c0+3 of block j with the k index permuted: w[n][k] = W[c0+n][k ^ km],
-// read as pairs (the pair index permutation is an address change, the bit-0 swap a select).
+// Weights of neurons c0 .. c0+3 of block j with the k index permuted: w[n][k] = W[c0+n][k ^ km].
 template <bool PACKED>
 __device__ __forceinline__ void mb_load_w4_perm(const MbParams& p, int64_t g, int j, int c0, int km,
-                                                float (&w)[4][8], float (&bb)[4]) {
+                                                float (&w)[4][8]) {
   const int khm = km >> 1;
   const bool sw = km & 1;
   const MbPacked m = mb_packed(p.C, p.NB);
@@ -58,14 +59,6 @@ __device__ __forceinline__ void mb_load_w4_perm(const MbParams& p, int64_t g, in
       w[n][2 * khp] = sw ? v.y : v.x;
       w[n][2 * khp + 1] = sw ? v.x : v.y;
     }
-  if constexpr (!PACKED) {
-    const float4 b4 = __ldg(reinterpret_cast<const float4*>(p.b + (g * p.NB + j) * p.C + c0));
-    bb[0] = b4.x; bb[1] = b4.y; bb[2] = b4.z; bb[3] = b4.w;
-  } else {
-    const float2 b0 = __ldg(reinterpret_cast<const float2*>(p.b + mb_packed_b(m, g, j, c0)));
-    const float2 b1 = __ldg(reinterpret_cast<const float2*>(p.b + mb_packed_b(m, g, j, c0 + 2)));
-    bb[0] = b0.x; bb[1] = b0.y; bb[2] = b1.x; bb[3] = b1.y;
-  }
 }
 
 template <int T, int ACT, bool PACKED, int LG>
@@ -116,11 +109,12 @@ __global__ void __launch_bounds__(kMbBwdThreads, 1) mb_bwd_kernel(const MbParams
       mb_xor_perm8<LGK>(ri, km);
       int xrow[8], drow[NK];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) xrow[k] = ri[k] * XLD;
+      for (int k = 0; k < 8; ++k) xrow[k] = rec.i[k] * XLD;
 #pragma unroll
       for (int k = 0; k < NK; ++k) drow[k] = ri[k] * DLD;
-      float w[4][8], bb[4];
-      mb_load_w4_perm<PACKED>(p, g, jj, nq * 4, km, w, bb);
+      float w[4][8], bb[4], wp[4][8];
+      mb_load_w4<PACKED>(p, g, jj, nq * 4, w, bb);
+      mb_load_w4_perm<PACKED>(p, g, jj, nq * 4, km, wp);
       const int nv = okr ? min(max(ng - (j * C + nq * 4), 0), 4) : 0;
       float dwacc[4][8], dbacc[4];
 #pragma unroll
@@ -160,7 +154,7 @@ __global__ void __launch_bounds__(kMbBwdThreads, 1) mb_bwd_kernel(const MbParams
           for (int t = 0; t < TS; ++t) {
             float sum = 0.f;
 #pragma unroll
-            for (int n = 0; n < 4; ++n) sum = fmaf(dz[n][t], w[n][k], sum);
+            for (int n = 0; n < 4; ++n) sum = fmaf(dz[n][t], wp[n][k], sum);
             a[k * TS + t] = sum;
           }
 #pragma unroll
@@ -195,23 +189,21 @@ __global__ void __launch_bounds__(kMbBwdThreads, 1) mb_bwd_kernel(const MbParams
         }
       }
       if (nv > 0) {
-        const int khm = km >> 1;
-        const bool sw = km & 1;
-        const MbPacked m = mb_packed(C, p.NB);
-#pragma unroll
-        for (int n = 0; n < 4; ++n)
-#pragma unroll
-          for (int khp = 0; khp < 4; ++khp) {
-            const int kh = khp ^ khm;
-            const float lo = sw ? dwacc[n][2 * khp + 1] : dwacc[n][2 * khp];
-            const float hi = sw ? dwacc[n][2 * khp] : dwacc[n][2 * khp + 1];
-            const int64_t off = PACKED ? mb_packed_w(m, g, j, nq * 4 + n, kh)
-                                       : ((g * p.NB + j) * C + nq * 4 + n) * 8 + 2 * kh;
-            red_add2(p.dw + off, lo, hi);
-          }
         if constexpr (!PACKED) {
+          float* dwp = p.dw + ((g * p.NB + j) * C + nq * 4) * 8;
+#pragma unroll
+          for (int n = 0; n < 4; ++n) {
+            red_add4(dwp + 8 * n, dwacc[n][0], dwacc[n][1], dwacc[n][2], dwacc[n][3]);
+            red_add4(dwp + 8 * n + 4, dwacc[n][4], dwacc[n][5], dwacc[n][6], dwacc[n][7]);
+          }
           red_add4(p.db + (g * p.NB + j) * C + nq * 4, dbacc[0], dbacc[1], dbacc[2], dbacc[3]);
         } else {
+          const MbPacked m = mb_packed(C, p.NB);
+#pragma unroll
+          for (int n = 0; n < 4; ++n)
+#pragma unroll
+            for (int kh = 0; kh < 4; ++kh)
+              red_add2(p.dw + mb_packed_w(m, g, j, nq * 4 + n, kh), dwacc[n][2 * kh], dwacc[n][2 * kh + 1]);
           red_add2(p.db + mb_packed_b(m, g, j, nq * 4), dbacc[0], dbacc[1]);
           red_add2(p.db + mb_packed_b(m, g, j, nq * 4 + 2), dbacc[2], dbacc[3]);
         }
