@@ -16,10 +16,10 @@ from pathlib import Path
 
 import torch
 
-ABI_VERSION = 7
+ABI_VERSION = 8
 LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libgranule_b200.so"
 
-POOL_MEAN, POOL_SUM, POOL_MAX = 0, 1, 2
+POOL_MEAN, POOL_SUM, POOL_MAX, POOL_LME, POOL_POWER, POOL_SOFTMAX = 0, 1, 2, 3, 4, 5
 ACT_IDS = {"identity": 0, "relu": 1, "gelu": 2}
 
 # The exported entry points, in header order (checked by the CPU test suite).
@@ -42,7 +42,9 @@ class GlFwdArgs(ctypes.Structure):
                 ("pool", ctypes.c_int32), ("act", ctypes.c_int32), ("tokens", ctypes.c_int32),
                 ("groups_per_cta", ctypes.c_int32), ("wabsmax", ctypes.c_void_p), ("order", ctypes.c_void_p),
                 ("lidx", ctypes.c_void_p), ("fmap", ctypes.c_void_p), ("nfeat", ctypes.c_void_p),
-                ("fcap", ctypes.c_int64), ("winners", ctypes.c_void_p), ("ldwin", ctypes.c_int64)]
+                ("fcap", ctypes.c_int64), ("winners", ctypes.c_void_p), ("ldwin", ctypes.c_int64),
+                ("stat", ctypes.c_void_p), ("ldstat", ctypes.c_int64), ("param", ctypes.c_float),
+                ("reserved2", ctypes.c_int32)]
 
 
 class GlBwdArgs(ctypes.Structure):
@@ -55,7 +57,8 @@ class GlBwdArgs(ctypes.Structure):
                 ("pool", ctypes.c_int32), ("act", ctypes.c_int32), ("tokens", ctypes.c_int32),
                 ("groups_per_cta", ctypes.c_int32), ("wabsmax", ctypes.c_void_p), ("rowmax", ctypes.c_void_p),
                 ("order", ctypes.c_void_p), ("lidx", ctypes.c_void_p), ("fmap", ctypes.c_void_p),
-                ("nfeat", ctypes.c_void_p), ("fcap", ctypes.c_int64)]
+                ("nfeat", ctypes.c_void_p), ("fcap", ctypes.c_int64), ("c2", ctypes.c_void_p),
+                ("c3", ctypes.c_void_p), ("param", ctypes.c_float), ("reserved2", ctypes.c_int32)]
 
 
 class GlAdamArgs(ctypes.Structure):
@@ -70,7 +73,9 @@ class GlSharedArgs(ctypes.Structure):
     _fields_ = [(n, ctypes.c_void_p) for n in ("x", "idx", "w", "b", "counts", "pre", "gpre", "dx", "dw", "db")] + \
                [(n, ctypes.c_int64) for n in ("B", "D", "NB", "C", "g0", "g1", "ldx", "ldp", "ldg", "lddx")] + \
                [(n, ctypes.c_int32) for n in ("pool", "act", "packed", "tokens", "groups_per_cta", "reserved")] + \
-               [("winners", ctypes.c_void_p), ("ldwin", ctypes.c_int64)]
+               [("winners", ctypes.c_void_p), ("ldwin", ctypes.c_int64), ("stat", ctypes.c_void_p),
+                ("ldstat", ctypes.c_int64), ("c2", ctypes.c_void_p), ("c3", ctypes.c_void_p),
+                ("param", ctypes.c_float), ("reserved2", ctypes.c_int32)]
 
 
 class GlEventArgs(ctypes.Structure):
@@ -173,34 +178,42 @@ def _require_cuda(*ts):
 
 
 def fwd(x, idx, w, b, counts, pre, NB: int, g0: int, g1: int, pool: int, act: int, tokens: int = 0,
-        groups_per_cta: int = 0, wabsmax=None, order=None, local=None, winners=None):
+        groups_per_cta: int = 0, wabsmax=None, order=None, local=None, winners=None, stat=None,
+        param: float = 0.0):
     """pre[:, :g1-g0] = pooled act(z) of groups [g0, g1); optionally wabsmax[g-g0] = max |w|; ``order``
     is an optional processing order (group_order); ``local`` = (lidx, fmap, nfeat) from
     group_feature_map turns on the per-group input staging; ``winners`` [B, g1-g0] int32 receives
-    the winning slots of max pooling.  See GlFwdArgs."""
+    the winning slots of max pooling; ``stat`` [B, g1-g0] the log2-normaliser of LME / softmax
+    pooling, whose parameter (or power mean's p) is ``param``.  See GlFwdArgs."""
     lidx, fmap, nfeat = local if local is not None else (None, None, None)
-    _require_cuda(x, idx, w, b, counts, pre, wabsmax, order, lidx, fmap, nfeat, winners)
+    _require_cuda(x, idx, w, b, counts, pre, wabsmax, order, lidx, fmap, nfeat, winners, stat)
     lib = load()
     a = GlFwdArgs(_ptr(x), _ptr(idx), _ptr(w), _ptr(b), _ptr(counts), _ptr(pre), x.shape[0], x.shape[1], NB,
                   g0, g1, x.stride(0), pre.stride(0), pool, act, tokens, groups_per_cta, _ptr(wabsmax), _ptr(order),
                   _ptr(lidx), _ptr(fmap), _ptr(nfeat), fmap.shape[1] if fmap is not None else 0, _ptr(winners),
-                  winners.stride(0) if winners is not None else 0)
+                  winners.stride(0) if winners is not None else 0, _ptr(stat),
+                  stat.stride(0) if stat is not None else 0, float(param), 0)
     with torch.cuda.device(x.device):
         _check(lib, lib.gl_fwd_f32(ctypes.byref(a), _stream(x.device)), "gl_fwd_f32")
 
 
 def bwd(x, idx, w, b, counts, gpre, dx, dw, db, NB: int, g0: int, g1: int, pool: int, act: int, tokens: int = 0,
-        groups_per_cta: int = 0, wabsmax=None, rowmax=None, order=None, local=None):
+        groups_per_cta: int = 0, wabsmax=None, rowmax=None, order=None, local=None, c2=None, c3=None,
+        param: float = 0.0):
     """dx += ..., dw += ..., db += ... for groups [g0, g1); fixed-point dX tiles when the
     per-group bounds ``wabsmax``/``rowmax`` are given; optional processing ``order`` and input
-    ``local``ity maps as in ``fwd``.  See GlBwdArgs."""
+    ``local``ity maps as in ``fwd``; the smooth pools take ``gpre`` = c1 and the coefficients
+    ``c2``, ``c3`` (same strides as ``gpre``) and ``param``.  See GlBwdArgs."""
     lidx, fmap, nfeat = local if local is not None else (None, None, None)
-    _require_cuda(x, idx, w, b, counts, gpre, dx, dw, db, wabsmax, rowmax, order, lidx, fmap, nfeat)
+    _require_cuda(x, idx, w, b, counts, gpre, dx, dw, db, wabsmax, rowmax, order, lidx, fmap, nfeat, c2, c3)
+    for c in (c2, c3):
+        if c is not None and c.stride(0) != gpre.stride(0):
+            raise ValueError("c2/c3 must have gpre's row stride")
     lib = load()
     a = GlBwdArgs(_ptr(x), _ptr(idx), _ptr(w), _ptr(b), _ptr(counts), _ptr(gpre), _ptr(dx), _ptr(dw), _ptr(db),
                   x.shape[0], x.shape[1], NB, g0, g1, x.stride(0), gpre.stride(0), dx.stride(0), pool, act,
                   tokens, groups_per_cta, _ptr(wabsmax), _ptr(rowmax), _ptr(order), _ptr(lidx), _ptr(fmap),
-                  _ptr(nfeat), fmap.shape[1] if fmap is not None else 0)
+                  _ptr(nfeat), fmap.shape[1] if fmap is not None else 0, _ptr(c2), _ptr(c3), float(param), 0)
     with torch.cuda.device(x.device):
         _check(lib, lib.gl_bwd_f32(ctypes.byref(a), _stream(x.device)), "gl_bwd_f32")
 
@@ -214,26 +227,34 @@ def _shared_args(x, idx, w, b, counts, NB, C, g0, g1, pool, act, packed, tokens,
 
 
 def fwd_shared(x, idx, w, b, counts, pre, NB: int, C: int, g0: int, g1: int, pool: int, act: int, packed: bool,
-               tokens: int = 0, groups_per_cta: int = 0, winners=None):
-    """Mode B forward: pre[:, :g1-g0] = pooled act(z); ``winners`` as in ``fwd`` (GlSharedArgs)."""
-    _require_cuda(x, idx, w, b, counts, pre, winners)
+               tokens: int = 0, groups_per_cta: int = 0, winners=None, stat=None, param: float = 0.0):
+    """Mode B forward: pre[:, :g1-g0] = pooled act(z); ``winners``, ``stat`` and ``param`` as in
+    ``fwd`` (GlSharedArgs)."""
+    _require_cuda(x, idx, w, b, counts, pre, winners, stat)
     lib = load()
     a = _shared_args(x, idx, w, b, counts, NB, C, g0, g1, pool, act, packed, tokens, groups_per_cta)
-    a.pre, a.ldp = _ptr(pre), pre.stride(0)
+    a.pre, a.ldp, a.param = _ptr(pre), pre.stride(0), float(param)
     if winners is not None:
         a.winners, a.ldwin = _ptr(winners), winners.stride(0)
+    if stat is not None:
+        a.stat, a.ldstat = _ptr(stat), stat.stride(0)
     with torch.cuda.device(x.device):
         _check(lib, lib.gl_fwd_shared_f32(ctypes.byref(a), _stream(x.device)), "gl_fwd_shared_f32")
 
 
 def bwd_shared(x, idx, w, b, counts, gpre, dx, dw, db, NB: int, C: int, g0: int, g1: int, pool: int, act: int,
-               packed: bool, tokens: int = 0, groups_per_cta: int = 0):
-    """Mode B backward: dx, dw, db += gradients for dL/dpre ``gpre`` (GlSharedArgs)."""
-    _require_cuda(x, idx, w, b, counts, gpre, dx, dw, db)
+               packed: bool, tokens: int = 0, groups_per_cta: int = 0, c2=None, c3=None, param: float = 0.0):
+    """Mode B backward: dx, dw, db += gradients for dL/dpre ``gpre`` (or, for the smooth pools, the
+    coefficients ``gpre`` = c1, ``c2``, ``c3`` and ``param`` as in ``bwd``) (GlSharedArgs)."""
+    _require_cuda(x, idx, w, b, counts, gpre, dx, dw, db, c2, c3)
+    for c in (c2, c3):
+        if c is not None and c.stride(0) != gpre.stride(0):
+            raise ValueError("c2/c3 must have gpre's row stride")
     lib = load()
     a = _shared_args(x, idx, w, b, counts, NB, C, g0, g1, pool, act, packed, tokens, groups_per_cta)
     a.gpre, a.dx, a.dw, a.db = _ptr(gpre), _ptr(dx), _ptr(dw), _ptr(db)
     a.ldg, a.lddx = gpre.stride(0), dx.stride(0)
+    a.c2, a.c3, a.param = _ptr(c2), _ptr(c3), float(param)
     with torch.cuda.device(x.device):
         _check(lib, lib.gl_bwd_shared_f32(ctypes.byref(a), _stream(x.device)), "gl_bwd_shared_f32")
 

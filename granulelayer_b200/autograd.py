@@ -18,6 +18,8 @@ from __future__ import annotations
 
 from typing import Dict, Optional
 
+import math
+
 import torch
 
 from . import _native
@@ -58,6 +60,21 @@ def dact_torch(x: torch.Tensor, name: str) -> torch.Tensor:
     return cdf + x * 0.3989422804014327 * torch.exp(-0.5 * x * x)
 
 
+def kernel_param(level: LevelSpec) -> float:
+    """The kernels' pool parameter: log2(e)/tau (LogMeanExp), log2(e)*beta (softmax-weighted), p (power
+    mean); kernels/ops.py:74-79."""
+    if level.type == "logmeanexp":
+        return LOG2E / level.temperature
+    if level.type == "softmax_weighted":
+        return LOG2E * level.beta
+    if level.type == "power_mean":
+        return float(level.p)
+    return 0.0
+
+
+LOG2E = 1.0 / math.log(2.0)
+
+
 class UnsupportedOnB200(NotImplementedError):
     """The layer configuration is outside the sm_100a hot path."""
 
@@ -92,8 +109,10 @@ class Level1Runtime:
         if self.counts_i32.numel() != G:
             raise ValueError(f"counts has {self.counts_i32.numel()} entries for {G} groups")
         self.counts_f32 = self.counts_i32.to(torch.float32)
-        self.pool = {"mean": _native.POOL_MEAN, "sum": _native.POOL_SUM, "max": _native.POOL_MAX}.get(
-            level.type, _native.POOL_MEAN)
+        self.pool = {"mean": _native.POOL_MEAN, "sum": _native.POOL_SUM, "max": _native.POOL_MAX,
+                     "logmeanexp": _native.POOL_LME, "power_mean": _native.POOL_POWER,
+                     "softmax_weighted": _native.POOL_SOFTMAX}.get(level.type, _native.POOL_MEAN)
+        self.param = kernel_param(level)
         self.act = _native.ACT_IDS[level.activation]
         self.last_info: Dict = {}
         self.det = False
@@ -137,8 +156,10 @@ class Level1Runtime:
 
     def locality(self):
         """(lidx, fmap, nfeat) when every group reads at most a quarter of the input features (the
-        kernels then stage only each group's features), else None.  Built once per index tensor."""
-        if self.plan.b200_locality == "off" or self.layout.shared_indices or not self.idx.is_cuda:
+        kernels then stage only each group's features), else None.  Built once per index tensor.
+        The smooth pools (LogMeanExp, power mean, softmax-weighted) run on the full-row staging."""
+        if (self.plan.b200_locality == "off" or self.layout.shared_indices or not self.idx.is_cuda
+                or self.smooth):
             return None
         G, D, NB = self.groups, self.layout.input_dim, self.layout.blocks_per_group
         if G == 0 or G > 65535 or D < 256:
@@ -220,6 +241,30 @@ class Level1Runtime:
     def is_max(self) -> bool:
         return self.pool == _native.POOL_MAX
 
+    @property
+    def smooth(self) -> bool:
+        """LogMeanExp, power mean or softmax-weighted: dense backward from per-(token, group)
+        coefficients (kernels/ops.py:242-262)."""
+        return self.pool in (_native.POOL_LME, _native.POOL_POWER, _native.POOL_SOFTMAX)
+
+    def coefficients(self, g_pre: torch.Tensor, stats: Dict):
+        """(c1, c2, c3) of the smooth pools (kernels/ops.py:242-262); L2 comes from the forward (softmax)
+        or from pre (LogMeanExp)."""
+        n = self.counts_f32[None, :]
+        pre = stats["pre"]
+        if self.pool == _native.POOL_LME:
+            L2 = stats.get("L2")
+            if L2 is None:
+                L2 = pre * self.param + torch.log2(n)
+            return g_pre, L2.contiguous(), None
+        if self.pool == _native.POOL_POWER:
+            pos = pre > 0
+            zero = torch.zeros_like(g_pre)
+            c1 = torch.where(pos, g_pre / n, zero)
+            c2 = torch.where(pos, 1.0 / torch.where(pos, pre, torch.ones_like(pre)), zero)
+            return c1.contiguous(), c2.contiguous(), None
+        return g_pre, stats["L2"].contiguous(), pre.contiguous()
+
     def forward(self, x: torch.Tensor, w: torch.Tensor, b: torch.Tensor, track_ids: bool = False):
         """{"pre": [B, G] pooled values, "wabsmax": [G] max |w| per group (Mode A mean/sum, for the
         backward), "winner": [B, G] int32 winning slots (max pooling, when ``track_ids``)}."""
@@ -229,20 +274,25 @@ class Level1Runtime:
         pre = torch.empty((B, self.groups), device=x.device, dtype=torch.float32)
         winners = (torch.empty((B, self.groups), device=x.device, dtype=torch.int32)
                    if self.is_max and track_ids else None)
+        stat = (torch.empty((B, self.groups), device=x.device, dtype=torch.float32)
+                if self.pool in (_native.POOL_LME, _native.POOL_SOFTMAX) else None)
         out = {"pre": pre}
         if winners is not None:
             out["winner"] = winners
+        if stat is not None:
+            out["L2"] = stat
         if self.layout.shared_indices:
             _native.fwd_shared(x, self.idx, w, b, self.counts_i32, pre, self.layout.blocks_per_group,
                                self.layout.block, 0, self.groups, self.pool, self.act, self.layout.packed,
-                               tokens=self.plan.b200_fwd_tokens, winners=winners)
+                               tokens=self.plan.b200_fwd_tokens, winners=winners, stat=stat, param=self.param)
             self.last_info.update(forward_backend="b200", forward_kernel="gl_fwd_shared_f32", workspace_bytes=0)
             return out
-        wabsmax = torch.empty(self.groups, device=x.device, dtype=torch.float32) if B > 0 and not self.is_max else None
+        wabsmax = (torch.empty(self.groups, device=x.device, dtype=torch.float32)
+                   if B > 0 and not self.is_max and not self.smooth else None)
         _native.fwd(x, self.idx, w, b, self.counts_i32, pre, self.layout.blocks_per_group, 0, self.groups,
                     self.pool, self.act, tokens=self.plan.b200_fwd_tokens, wabsmax=wabsmax,
                     order=self.order(self.tokens(False)) if B > 0 else None,
-                    local=self.locality() if B > 0 else None, winners=winners)
+                    local=self.locality() if B > 0 else None, winners=winners, stat=stat, param=self.param)
         self.last_info.update(forward_backend="b200", workspace_bytes=0)
         if wabsmax is not None:
             out["wabsmax"] = wabsmax
@@ -273,25 +323,32 @@ class Level1Runtime:
         self.resolve_reduction(B)
         if self.is_max:
             return self._event_backward(x, w, b, g_pre, saved, dw_buf, db_buf)
+        c1, c2, c3 = g_pre, None, None
+        if self.smooth:
+            stats = dict(saved)
+            if self.pool == _native.POOL_SOFTMAX and "L2" not in stats:   # autograd.py:246-261
+                stats.update(self.forward(x, w, b))
+                self.last_info["recomputed_stats"] = True
+            c1, c2, c3 = self.coefficients(g_pre, stats)
         dx = torch.zeros((B, D), device=x.device, dtype=torch.float32)
         if self.layout.shared_indices:
-            _native.bwd_shared(x, self.idx, w, b, self.counts_i32, g_pre, dx, dw_buf, db_buf,
+            _native.bwd_shared(x, self.idx, w, b, self.counts_i32, c1, dx, dw_buf, db_buf,
                                self.layout.blocks_per_group, self.layout.block, 0, self.groups, self.pool, self.act,
-                               self.layout.packed, tokens=self.plan.b200_dx_tokens)
+                               self.layout.packed, tokens=self.plan.b200_dx_tokens, c2=c2, c3=c3, param=self.param)
             self.last_info["backward_backend"] = "b200"
             self.last_info["dx_accumulation"] = "fp32 shared-memory reductions (Mode B)"
             return dx
         wabsmax = rowmax = None
-        if self.fixed_point and B > 0:
+        if self.fixed_point and B > 0 and not self.smooth:
             wabsmax = saved.get("wabsmax")
             if wabsmax is None:
                 wabsmax = torch.empty(self.groups, device=x.device, dtype=torch.float32)
                 _native.group_absmax(w, self.counts_i32, self.layout.blocks_per_group, 0, self.groups, wabsmax)
             rowmax = self.rowmax()
-        _native.bwd(x, self.idx, w, b, self.counts_i32, g_pre, dx, dw_buf, db_buf, self.layout.blocks_per_group,
+        _native.bwd(x, self.idx, w, b, self.counts_i32, c1, dx, dw_buf, db_buf, self.layout.blocks_per_group,
                     0, self.groups, self.pool, self.act, tokens=self.plan.b200_dx_tokens, wabsmax=wabsmax,
                     rowmax=rowmax, order=self.order(self.tokens(True)) if B > 0 else None,
-                    local=self.locality() if B > 0 else None)
+                    local=self.locality() if B > 0 else None, c2=c2, c3=c3, param=self.param)
         self.last_info["backward_backend"] = "b200"
         self.last_info["dx_accumulation"] = "int32 fixed point" if wabsmax is not None else "fp32 atomics"
         return dx
@@ -325,10 +382,12 @@ class SparsePoolFunction(torch.autograd.Function):
         pre = out["pre"]
         y = act_torch(pre, rt.level.out_activation)
         ctx.rt, ctx.policy = rt, policy
-        ctx.extra = [k for k in ("wabsmax", "winner") if k in out]
+        # softmax-weighted keeps its log2-normaliser under minimal_stats (autograd.py:364-377)
+        keep = ("wabsmax", "winner", "L2") if policy != "recompute_stats" else ("wabsmax",)
+        ctx.extra = [k for k in keep if k in out and (k != "L2" or rt.pool == _native.POOL_SOFTMAX)]
         ctx.save_for_backward(x, w, b, pre, *[out[k] for k in ctx.extra])
         rt.last_info["checkpoint_bytes"] = sum(t.numel() * t.element_size() for t in [pre] + [out[k] for k in ctx.extra
-                                                                                           if k == "winner"])
+                                                                                           if k in ("winner", "L2")])
         return y
 
     @staticmethod

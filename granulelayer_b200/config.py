@@ -29,7 +29,7 @@ POOL_ID = {name: i for i, name in enumerate(POOL_TYPES)}
 ACT_ID = {name: i for i, name in enumerate(ACTIVATIONS)}
 
 # Operators the B200 kernels execute (the hot path); the rest are parsed only.
-B200_POOLS = ("mean", "sum", "max")
+B200_POOLS = ("mean", "sum", "max", "logmeanexp", "power_mean", "softmax_weighted")
 
 # per-neuron activation used when the spec leaves it empty (config.py:42-49)
 DEFAULT_ACTIVATION = {

@@ -96,6 +96,10 @@ struct BwdParams {
   int B, D;
   int64_t NB, g0, g1, ldx, ldg, lddx;
   int pool, gpc;
+  const float* c2;  // smooth pools: coefficients c2, c3 [B, ldg] and the pool's parameter
+  const float* c3;
+  float param;
+  int ipm1;         // integer code of the power mean's p - 1 (-1: general)
 };
 
 // FIXED = false: fp32 tile.  FIXED = true: int32 tile + fp32 fold tile.  LOCAL: one group per block,
@@ -142,8 +146,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const BwdParams p) 
   for (int64_t g = gb; g < ge; ++g) {
     const int ng = min(p.counts[g], slots);
     const int64_t fbase = g * (int64_t)slots;
-    float c1 = tok_ok ? __ldg(p.gpre + (int64_t)(t0 + t) * p.ldg + (g - p.g0)) : 0.f;
+    const int64_t ci = (int64_t)(t0 + t) * p.ldg + (g - p.g0);
+    float c1 = tok_ok ? __ldg(p.gpre + ci) : 0.f;
     if (p.pool == GL_POOL_MEAN) c1 = c1 / (float)ng;
+    const bool smooth = p.pool >= GL_POOL_LME;  // uniform: dz through pool_dz
+    const float c2 = smooth && tok_ok && p.c2 != nullptr ? __ldg(p.c2 + ci) : 0.f;
+    const float c3 = smooth && tok_ok && p.c3 != nullptr ? __ldg(p.c3 + ci) : 0.f;
     float c1s = 0.f;
     if constexpr (FIXED) {
       const float wm = __ldg(p.wabsmax + (g - p.g0));
@@ -176,7 +184,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const BwdParams p) 
           z = fmaf(wr.w[k], xv[k], z);
         }
         const float da = dact_f<ACT>(z);
-        const float dz = c1 * da;
+        const float dz = smooth ? pool_dz<ACT>(p.pool, z, c1, c2, c3, p.param, p.ipm1) : c1 * da;
         if constexpr (FIXED) {
           const float dzs = c1s * da;
           if (dzs != 0.f) {
@@ -320,7 +328,13 @@ extern "C" int gl_bwd_f32(const GlBwdArgs* args, void* stream) {
   if ((a.wabsmax == nullptr) != (a.rowmax == nullptr)) return GL_ERR_NULL;
   if (a.B > 2147483647LL || a.ldx < a.D || a.ldg < a.g1 - a.g0 || a.lddx < a.D) return GL_ERR_SHAPE;
   if (((uintptr_t)a.idx & 15) || ((uintptr_t)a.w & 15) || ((uintptr_t)a.dw & 31)) return GL_ERR_ALIGN;
-  if (a.pool != GL_POOL_MEAN && a.pool != GL_POOL_SUM) return GL_ERR_UNSUPPORTED;
+  if (a.pool != GL_POOL_MEAN && a.pool != GL_POOL_SUM && a.pool != GL_POOL_LME && a.pool != GL_POOL_POWER &&
+      a.pool != GL_POOL_SOFTMAX)
+    return GL_ERR_UNSUPPORTED;
+  const bool smooth = a.pool >= GL_POOL_LME;
+  if (smooth && (!a.c2 || (a.pool == GL_POOL_SOFTMAX && !a.c3))) return GL_ERR_NULL;
+  if ((a.pool == GL_POOL_LME || a.pool == GL_POOL_SOFTMAX) && !(a.param > 0.f)) return GL_ERR_SHAPE;
+  if (a.pool == GL_POOL_POWER && !(a.param >= 1.f)) return GL_ERR_SHAPE;
   int optin = 0, sms = 0;
   int rc = device_smem_optin(&optin);
   if (rc) return rc;
@@ -333,8 +347,9 @@ extern "C" int gl_bwd_f32(const GlBwdArgs* args, void* stream) {
     if (a.g1 - a.g0 > 65535) return GL_ERR_SHAPE;  // one group per block
   }
   const int64_t rows = local ? a.fcap : a.D;
-  // fixed-point tiles when the caller supplied the two per-group bounds and they fit
-  bool fixed = a.wabsmax != nullptr;
+  // fixed-point tiles when the caller supplied the two per-group bounds and they fit (mean / sum:
+  // their |dz| <= |c1| max|act'| bound the terms)
+  bool fixed = a.wabsmax != nullptr && !smooth;
   int T = a.tokens;
   if (T == 0) {
     T = pick_bwd_tokens(rows, optin, fixed);
@@ -359,7 +374,8 @@ extern "C" int gl_bwd_f32(const GlBwdArgs* args, void* stream) {
   while ((G + gpc - 1) / gpc > 65535) gpc *= 2;
   BwdParams p{a.x, a.idx, a.w, a.b, a.counts, a.gpre, a.dx, a.dw, a.db, a.wabsmax, a.rowmax, a.order,
               LocalMap{a.lidx, a.fmap, a.nfeat, (int)a.fcap}, (int)a.B, (int)a.D,
-              a.NB, a.g0, a.g1, a.ldx, a.ldg, a.lddx, a.pool, gpc};
+              a.NB, a.g0, a.g1, a.ldx, a.ldg, a.lddx, a.pool, gpc, a.c2, a.c3, a.param,
+              pow_code(a.param) >= 1 ? pow_code(a.param) - 1 : -1};
   cudaStream_t st = (cudaStream_t)stream;
   if (local)
     return fixed ? dispatch_tokens_bwd<true, true>(p, a.B, a.act, T, st)

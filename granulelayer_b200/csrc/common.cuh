@@ -37,6 +37,119 @@ __device__ __forceinline__ float dact_f(float z) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// Pooling states (the reference's per-(token, group) states, kernels/triton_fused.py:121-225, and
+// their merge / finalisation, kernels/ops.py:182-239).  Forward kinds:
+//   PK_ADD  mean / sum: s0 = sum a
+//   PK_MAX  max: s0 = max a and the winning slot
+//   PK_LSE  LogMeanExp / softmax-weighted, base-2 log-sum-exp of u = a * param:
+//           s0 = m = max u, s1 = sum 2^(u - m), s2 = sum a 2^(u - m) (softmax only)
+//   PK_POW  power mean of a = relu(z) >= 0: s0 = m = max a, s1 = sum (a / m)^p, s2 = 1 / m
+// A lane folds its values in one at a time and rescales its sums only when a new maximum
+// arrives; lanes and warps then merge their states.
+enum { PK_ADD = 0, PK_MAX = 1, PK_LSE = 2, PK_POW = 3 };
+
+inline int pool_kind(int pool) {
+  return pool == GL_POOL_MAX ? PK_MAX
+       : (pool == GL_POOL_LME || pool == GL_POOL_SOFTMAX) ? PK_LSE
+       : pool == GL_POOL_POWER ? PK_POW : PK_ADD;
+}
+
+// Integer exponent code of a power-mean exponent: p itself for p in {1, 2, 4, 8} (the reference's
+// P_INT, kernels/ops.py:68-71), else -1 (the general 2^(p log2 r) form).
+__host__ __device__ __forceinline__ int pow_code(float p) {
+  return (p == 1.f || p == 2.f || p == 4.f || p == 8.f) ? (int)p : -1;
+}
+
+// r^e for r >= 0, by products for the exponents the power mean uses (ie = e in {0, 1, 2, 3, 4, 7, 8},
+// in the reference's multiplication order) and 2^(e log2 r) otherwise (0^e = 0 for e > 0).
+__device__ __forceinline__ float powr(float r, int ie, float e) {
+  switch (ie) {
+    case 0: return 1.f;
+    case 1: return r;
+    case 2: return r * r;
+    case 3: return r * r * r;
+    case 4: { const float r2 = r * r; return r2 * r2; }
+    case 7: { const float r2 = r * r, r4 = r2 * r2; return r4 * r2 * r; }
+    case 8: { const float r2 = r * r, r4 = r2 * r2; return r4 * r4; }
+    default: return exp2f(e * log2f(r));
+  }
+}
+
+struct PoolParam {
+  float param;  // LME: log2(e) / tau; softmax: log2(e) * beta; power: p
+  int ip;       // power: pow_code(p)
+  bool want_t;  // softmax: track sum a 2^(u - m)
+};
+
+__device__ __forceinline__ void lse_push(float& m, float& s, float& t, float u, float a, bool want_t) {
+  const float d = u - m;
+  const float e = exp2f(-fabsf(d));  // 2^(m - u) for a new maximum, else 2^(u - m)
+  const bool up = d > 0.f;
+  s = up ? fmaf(s, e, 1.f) : s + e;
+  if (want_t) t = up ? fmaf(t, e, a) : fmaf(a, e, t);
+  m = up ? u : m;
+}
+
+__device__ __forceinline__ void lse_merge(float& m, float& s, float& t, float m2, float s2, float t2) {
+  const float M = fmaxf(m, m2);
+  const float e1 = M == -INFINITY ? 0.f : exp2f(m - M);
+  const float e2 = M == -INFINITY ? 0.f : exp2f(m2 - M);
+  s = fmaf(s, e1, s2 * e2);
+  t = fmaf(t, e1, t2 * e2);
+  m = M;
+}
+
+__device__ __forceinline__ void pow_push(float& m, float& s, float& inv, float a, const PoolParam& pp) {
+  if (a > m) {
+    const float ia = 1.f / a;
+    s = fmaf(s, powr(m * ia, pp.ip, pp.param), 1.f);
+    m = a;
+    inv = ia;
+  } else {
+    s += powr(a * inv, pp.ip, pp.param);
+  }
+}
+
+__device__ __forceinline__ void pow_merge(float& m, float& s, float m2, float s2, const PoolParam& pp) {
+  const float M = fmaxf(m, m2);
+  if (M > 0.f) {
+    const float iM = 1.f / M;
+    s = fmaf(s, powr(m * iM, pp.ip, pp.param), s2 * powr(m2 * iM, pp.ip, pp.param));
+  } else {
+    s = 0.f;
+  }
+  m = M;
+}
+
+// pre (and the log2-normaliser L2 of the LSE kinds) of a merged state over n valid slots
+// (kernels/ops.py:200-217).
+__device__ __forceinline__ float pool_finalize(int pool, float s0, float s1, float s2, int n, float param,
+                                               float* l2) {
+  if (pool == GL_POOL_LME || pool == GL_POOL_SOFTMAX) {
+    const float L2 = s0 + log2f(s1);
+    *l2 = L2;
+    return pool == GL_POOL_LME ? (L2 - log2f((float)n)) / param : s2 / s1;
+  }
+  // power mean
+  return s0 > 0.f ? s0 * powf(s1 / (float)n, 1.f / param) : 0.f;
+}
+
+// dz = c1 * h * act'(z) of the pools with a dense backward (kernels/triton_fused.py:365-399).
+template <int ACT>
+__device__ __forceinline__ float pool_dz(int pool, float z, float c1, float c2, float c3, float param, int ipm1) {
+  if (pool == GL_POOL_MEAN || pool == GL_POOL_SUM) return c1 * dact_f<ACT>(z);
+  if (pool == GL_POOL_POWER) {
+    const float q = fmaxf(z, 0.f) * c2;
+    return z > 0.f ? c1 * powr(q, ipm1, param - 1.f) : 0.f;
+  }
+  const float a = act_f<ACT>(z);
+  const float pw = exp2f(fmaf(a, param, -c2));
+  if (pool == GL_POOL_LME) return c1 * pw * dact_f<ACT>(z);
+  const float beta = param * 0.6931471805599453f;
+  return c1 * pw * fmaf(beta, a - c3, 1.f) * dact_f<ACT>(z);
+}
+
 // Eight int16 indices of one neuron record, loaded as one 16-byte vector and
 // widened; every index is clamped to [0, dmax] so that a corrupt record can
 // never address outside the staged input tile.

@@ -26,16 +26,20 @@ namespace gl {
 
 constexpr int kFwdThreads = 512;
 
-// MAXP: max pooling (the largest act(z) over the valid slots; winner = the smallest slot attaining
-// it, kernels/triton_fused.py:129-140), with the winner slots written to `winners`; otherwise the
-// additive pools (mean, sum).
-template <int T, int ACT, bool LOCAL, bool MAXP>
+// PK (the pooling state, common.cuh): PK_ADD mean / sum; PK_MAX max (the largest act(z) over the
+// valid slots; winner = the smallest slot attaining it, kernels/triton_fused.py:129-140, written to
+// `winners`); PK_LSE LogMeanExp / softmax-weighted and PK_POW power mean (their log2-normaliser
+// written to `stat`).
+template <int T, int ACT, bool LOCAL, int PK>
 __global__ void __launch_bounds__(kFwdThreads, 1)
     fwd_kernel(const float* __restrict__ x, const int16_t* __restrict__ idx, const float* __restrict__ w,
                const float* __restrict__ bias, const int32_t* __restrict__ counts, float* __restrict__ pre,
                int B, int D, int64_t NB, int64_t g0, int64_t g1, int64_t ldx, int64_t ldp, int pool, int gpc,
                float* __restrict__ wabsmax, const int32_t* __restrict__ order, const LocalMap lm,
-               int32_t* __restrict__ winners, int64_t ldwin) {
+               int32_t* __restrict__ winners, int64_t ldwin, float* __restrict__ stat, int64_t ldstat,
+               const PoolParam pp) {
+  constexpr bool MAXP = PK == PK_MAX;
+  constexpr bool SM = PK == PK_LSE || PK == PK_POW;  // three-word states
   constexpr int V = T < 4 ? T : 4;   // tokens per lane
   constexpr int LPN = T / V;         // lanes per neuron
   constexpr int NPW = 32 / LPN;      // neurons per warp step
@@ -44,6 +48,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   extern __shared__ __align__(16) float xs[];
   __shared__ float red[NW][T];
   __shared__ int redi[MAXP ? NW : 1][T];
+  __shared__ float red1[SM ? NW : 1][T], red2[SM ? NW : 1][T];
   __shared__ float redw[NW];
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -70,11 +75,13 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   for (int64_t g = gb; g < ge; ++g) {
     const int ng = min(counts[g], slots);
     const int64_t fbase = g * (int64_t)slots;
-    float acc[V];
+    float acc[V], st1[V], st2[V];  // st1, st2: the second and third words of the SM states
     int wid[V];
 #pragma unroll
     for (int v = 0; v < V; ++v) {
-      acc[v] = MAXP ? -INFINITY : 0.f;
+      acc[v] = (MAXP || PK == PK_LSE) ? -INFINITY : 0.f;
+      st1[v] = 0.f;
+      st2[v] = 0.f;
       wid[v] = 0x7fffffff;
     }
     float wmx = 0.f;  // max |w| over the valid slots this lane reads (for the backward's fixed-point scale)
@@ -128,6 +135,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                 acc[v] = a;
                 wid[v] = sl[u];
               }
+            } else if constexpr (PK == PK_LSE) {
+              lse_push(acc[v], st1[v], st2[v], a * pp.param, a, pp.want_t);
+            } else if constexpr (PK == PK_POW) {
+              pow_push(acc[v], st1[v], st2[v], a, pp);
             } else {
               acc[v] += a;
             }
@@ -149,6 +160,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             acc[v] = ov;
             wid[v] = ow;
           }
+        } else if constexpr (PK == PK_LSE) {
+          const float o1 = __shfl_xor_sync(kFullMask, st1[v], off), o2 = __shfl_xor_sync(kFullMask, st2[v], off);
+          lse_merge(acc[v], st1[v], st2[v], ov, o1, o2);
+        } else if constexpr (PK == PK_POW) {
+          pow_merge(acc[v], st1[v], ov, __shfl_xor_sync(kFullMask, st1[v], off), pp);
         } else {
           acc[v] += ov;
         }
@@ -158,6 +174,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       for (int v = 0; v < V; ++v) {
         red[warp][lane * V + v] = acc[v];
         if constexpr (MAXP) redi[warp][lane * V + v] = wid[v];
+        if constexpr (SM) {
+          red1[warp][lane * V + v] = st1[v];
+          red2[warp][lane * V + v] = st2[v];
+        }
       }
     const bool want_w = wabsmax != nullptr && blockIdx.x == 0;
     if (want_w) {
@@ -184,6 +204,19 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           pre[(int64_t)t * ldp + (g - g0)] = m;
           if (winners != nullptr) winners[(int64_t)t * ldwin + (g - g0)] = wi;
         }
+      } else if constexpr (SM) {
+        float m = red[0][threadIdx.x], s1 = red1[0][threadIdx.x], s2 = red2[0][threadIdx.x];
+#pragma unroll
+        for (int i = 1; i < NW; ++i) {
+          if constexpr (PK == PK_LSE) lse_merge(m, s1, s2, red[i][threadIdx.x], red1[i][threadIdx.x], red2[i][threadIdx.x]);
+          else pow_merge(m, s1, red[i][threadIdx.x], red1[i][threadIdx.x], pp);
+        }
+        float l2 = 0.f;
+        const float y = pool_finalize(pool, m, s1, s2, ng, pp.param, &l2);
+        if (t < B) {
+          pre[(int64_t)t * ldp + (g - g0)] = y;
+          if (PK == PK_LSE && stat != nullptr) stat[(int64_t)t * ldstat + (g - g0)] = l2;
+        }
       } else {
         float s = 0.f;
 #pragma unroll
@@ -201,10 +234,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   }
 }
 
-template <int T, int ACT, bool LOCAL, bool MAXP>
+template <int T, int ACT, bool LOCAL, int PK>
 static int launch_fwd(const GlFwdArgs& a, int gpc, cudaStream_t st) {
   const size_t smem = (size_t)(LOCAL ? a.fcap : a.D) * T * sizeof(float);
-  auto kern = fwd_kernel<T, ACT, LOCAL, MAXP>;
+  auto kern = fwd_kernel<T, ACT, LOCAL, PK>;
   int rc = ensure_dynamic_smem((const void*)kern, smem);
   if (rc) return rc;
   const int64_t tiles = (a.B + T - 1) / T;
@@ -213,35 +246,49 @@ static int launch_fwd(const GlFwdArgs& a, int gpc, cudaStream_t st) {
   dim3 grid((unsigned)tiles, (unsigned)chunks);
   const LocalMap lm{a.lidx, a.fmap, a.nfeat, (int)a.fcap};
   kern<<<grid, kFwdThreads, smem, st>>>(a.x, a.idx, a.w, a.b, a.counts, a.pre, (int)a.B, (int)a.D, a.NB, a.g0,
-                                        a.g1, a.ldx, a.ldp, a.pool, gpc, a.wabsmax, a.order, lm, a.winners, a.ldwin);
+                                        a.g1, a.ldx, a.ldp, a.pool, gpc, a.wabsmax, a.order, lm, a.winners, a.ldwin,
+                                        a.stat, a.ldstat, PoolParam{a.param, pow_code(a.param),
+                                                                    a.pool == GL_POOL_SOFTMAX});
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_cuda_error(e);
   count_launches(1);
   return GL_OK;
 }
 
-template <int T, bool LOCAL, bool MAXP>
+template <int T, bool LOCAL, int PK>
 static int dispatch_act_fwd2(const GlFwdArgs& a, int gpc, cudaStream_t st) {
   switch (a.act) {
-    case GL_ACT_IDENTITY: return launch_fwd<T, GL_ACT_IDENTITY, LOCAL, MAXP>(a, gpc, st);
-    case GL_ACT_RELU: return launch_fwd<T, GL_ACT_RELU, LOCAL, MAXP>(a, gpc, st);
-    case GL_ACT_GELU: return launch_fwd<T, GL_ACT_GELU, LOCAL, MAXP>(a, gpc, st);
+    case GL_ACT_IDENTITY: return launch_fwd<T, GL_ACT_IDENTITY, LOCAL, PK>(a, gpc, st);
+    case GL_ACT_RELU: return launch_fwd<T, GL_ACT_RELU, LOCAL, PK>(a, gpc, st);
+    case GL_ACT_GELU: return launch_fwd<T, GL_ACT_GELU, LOCAL, PK>(a, gpc, st);
     default: return GL_ERR_UNSUPPORTED;
   }
 }
 
+// The smooth pools (LSE, POW kinds) run on the full-row staging only (no locality maps).
 template <int T, bool LOCAL>
 static int dispatch_act_fwd(const GlFwdArgs& a, int gpc, cudaStream_t st) {
-  return a.pool == GL_POOL_MAX ? dispatch_act_fwd2<T, LOCAL, true>(a, gpc, st)
-                               : dispatch_act_fwd2<T, LOCAL, false>(a, gpc, st);
+  switch (pool_kind(a.pool)) {
+    case PK_MAX: return dispatch_act_fwd2<T, LOCAL, PK_MAX>(a, gpc, st);
+    case PK_LSE:
+      if constexpr (LOCAL) return GL_ERR_UNSUPPORTED;
+      else return dispatch_act_fwd2<T, false, PK_LSE>(a, gpc, st);
+    case PK_POW:
+      if constexpr (LOCAL) return GL_ERR_UNSUPPORTED;
+      else return dispatch_act_fwd2<T, false, PK_POW>(a, gpc, st);
+    default: return dispatch_act_fwd2<T, LOCAL, PK_ADD>(a, gpc, st);
+  }
 }
 
+// Bound on the forward kernel's static shared memory (its reduction buffers).
+constexpr int kFwdStaticSmem = 9216;
+
 // Largest token tile in {tmax, ..., 2, 1} whose staged input (D rows) fits the opt-in shared
-// memory (leaving room for the static reduction buffer).  tmax is 8 for the full input row and
+// memory (leaving room for the static reduction buffers).  tmax is 8 for the full input row and
 // 32 for a group's feature map.
 static int pick_fwd_tokens(int64_t D, int smem_optin, int tmax = 8) {
   for (int T = tmax; T >= 1; T >>= 1)
-    if ((int64_t)D * T * 4 + 2048 <= smem_optin) return T;
+    if ((int64_t)D * T * 4 + kFwdStaticSmem <= smem_optin) return T;
   return GL_ERR_SMEM;
 }
 
@@ -264,8 +311,11 @@ extern "C" int gl_fwd_f32(const GlFwdArgs* args, void* stream) {
   if (!a.x || !a.idx || !a.w || !a.b || !a.counts || !a.pre) return GL_ERR_NULL;
   if (a.B > 2147483647LL || a.ldx < a.D || a.ldp < a.g1 - a.g0) return GL_ERR_SHAPE;
   if (((uintptr_t)a.idx & 15) || ((uintptr_t)a.w & 15)) return GL_ERR_ALIGN;
-  if (a.pool != GL_POOL_MEAN && a.pool != GL_POOL_SUM && a.pool != GL_POOL_MAX) return GL_ERR_UNSUPPORTED;
+  if (a.pool < GL_POOL_MEAN || a.pool > GL_POOL_SOFTMAX) return GL_ERR_UNSUPPORTED;
+  if ((a.pool == GL_POOL_LME || a.pool == GL_POOL_SOFTMAX) && !(a.param > 0.f)) return GL_ERR_SHAPE;
+  if (a.pool == GL_POOL_POWER && !(a.param >= 1.f)) return GL_ERR_SHAPE;
   if (a.winners && a.ldwin < a.g1 - a.g0) return GL_ERR_SHAPE;
+  if (a.stat && a.ldstat < a.g1 - a.g0) return GL_ERR_SHAPE;
   int optin = 0, sms = 0;
   int rc = device_smem_optin(&optin);
   if (rc) return rc;
@@ -285,7 +335,7 @@ extern "C" int gl_fwd_f32(const GlFwdArgs* args, void* stream) {
   } else if (T != 1 && T != 2 && T != 4 && T != 8 && T != 16 && T != 32) {
     return GL_ERR_UNSUPPORTED;
   }
-  if (rows * T * 4 + 2048 > optin) return GL_ERR_SMEM;
+  if (rows * T * 4 + kFwdStaticSmem > optin) return GL_ERR_SMEM;
   const int64_t G = a.g1 - a.g0;
   int gpc = local ? 1 : a.groups_per_cta;
   if (gpc <= 0) {

@@ -21,15 +21,19 @@
 
 namespace gl {
 
-// MAXP: max pooling with the winning slot (smallest on ties) written to p.winners.
-template <int T, int ACT, bool PACKED, bool MAXP>
+// PK (the pooling state, common.cuh): PK_MAX writes the winning slot (smallest on ties) to
+// p.winners; PK_LSE / PK_POW hold three-word states (their tiles stay at 8 tokens or fewer).
+template <int T, int ACT, bool PACKED, int PK>
 __global__ void __launch_bounds__(kMbFwdThreads, 1) mb_fwd_kernel(const MbParams p) {
+  constexpr bool MAXP = PK == PK_MAX;
+  constexpr bool SM = PK == PK_LSE || PK == PK_POW;
   constexpr int NW = kMbFwdThreads / 32;
   constexpr int TS = T < 8 ? T : 8;  // tokens per sub-chunk (registers per lane stay fixed as T grows)
   extern __shared__ __align__(16) float xs[];
   // per-warp partials, double-buffered by group parity: one barrier per group
   __shared__ float red[2][NW][T];
   __shared__ int redi[2][MAXP ? NW : 1][T];
+  __shared__ float red1[2][SM ? NW : 1][T], red2[2][SM ? NW : 1][T];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int t0 = blockIdx.x * T;
   constexpr int XLD = mb_xld<T>();
@@ -46,10 +50,12 @@ __global__ void __launch_bounds__(kMbFwdThreads, 1) mb_fwd_kernel(const MbParams
     const int buf = (int)((g - gb) & 1);
     float acc[T];
     int wid[MAXP ? T : 1];
+    float st1[SM ? T : 1], st2[SM ? T : 1];
 #pragma unroll
     for (int t = 0; t < T; ++t) {
-      acc[t] = MAXP ? -INFINITY : 0.f;
+      acc[t] = (MAXP || PK == PK_LSE) ? -INFINITY : 0.f;
       if constexpr (MAXP) wid[t] = 0x7fffffff;
+      if constexpr (SM) st1[t] = st2[t] = 0.f;
     }
     for (int base = warp * RPW; base < nbv; base += NW * RPW) {
       const int j = base + r;
@@ -87,6 +93,10 @@ __global__ void __launch_bounds__(kMbFwdThreads, 1) mb_fwd_kernel(const MbParams
                 const bool up = a > acc[tc + t];
                 acc[tc + t] = up ? a : acc[tc + t];
                 wid[tc + t] = up ? j * C + nq * 4 + n : wid[tc + t];
+              } else if constexpr (PK == PK_LSE) {
+                lse_push(acc[tc + t], st1[tc + t], st2[tc + t], a * p.pp.param, a, p.pp.want_t);
+              } else if constexpr (PK == PK_POW) {
+                pow_push(acc[tc + t], st1[tc + t], st2[tc + t], a, p.pp);
               } else {
                 acc[tc + t] += a;
               }
@@ -104,6 +114,11 @@ __global__ void __launch_bounds__(kMbFwdThreads, 1) mb_fwd_kernel(const MbParams
             acc[t] = ov;
             wid[t] = ow;
           }
+        } else if constexpr (PK == PK_LSE) {
+          const float o1 = __shfl_xor_sync(kFullMask, st1[t], off), o2 = __shfl_xor_sync(kFullMask, st2[t], off);
+          lse_merge(acc[t], st1[t], st2[t], ov, o1, o2);
+        } else if constexpr (PK == PK_POW) {
+          pow_merge(acc[t], st1[t], ov, __shfl_xor_sync(kFullMask, st1[t], off), p.pp);
         } else {
           acc[t] += ov;
         }
@@ -113,6 +128,10 @@ __global__ void __launch_bounds__(kMbFwdThreads, 1) mb_fwd_kernel(const MbParams
       for (int t = 0; t < T; ++t) {
         red[buf][warp][t] = acc[t];
         if constexpr (MAXP) redi[buf][warp][t] = wid[t];
+        if constexpr (SM) {
+          red1[buf][warp][t] = st1[t];
+          red2[buf][warp][t] = st2[t];
+        }
       }
     __syncthreads();
     if (threadIdx.x < T) {
@@ -133,6 +152,21 @@ __global__ void __launch_bounds__(kMbFwdThreads, 1) mb_fwd_kernel(const MbParams
           p.pre[(int64_t)t * p.ldp + (g - p.g0)] = m;
           if (p.winners != nullptr) p.winners[(int64_t)t * p.ldwin + (g - p.g0)] = wi;
         }
+      } else if constexpr (SM) {
+        float m = red[buf][0][threadIdx.x], s1 = red1[buf][0][threadIdx.x], s2 = red2[buf][0][threadIdx.x];
+#pragma unroll
+        for (int i = 1; i < NW; ++i) {
+          if constexpr (PK == PK_LSE)
+            lse_merge(m, s1, s2, red[buf][i][threadIdx.x], red1[buf][i][threadIdx.x], red2[buf][i][threadIdx.x]);
+          else
+            pow_merge(m, s1, red[buf][i][threadIdx.x], red1[buf][i][threadIdx.x], p.pp);
+        }
+        float l2 = 0.f;
+        const float y = pool_finalize(p.pool, m, s1, s2, ng, p.pp.param, &l2);
+        if (t < p.B) {
+          p.pre[(int64_t)t * p.ldp + (g - p.g0)] = y;
+          if (PK == PK_LSE && p.stat != nullptr) p.stat[(int64_t)t * p.ldstat + (g - p.g0)] = l2;
+        }
       } else {
         float s = 0.f;
 #pragma unroll
@@ -145,32 +179,42 @@ __global__ void __launch_bounds__(kMbFwdThreads, 1) mb_fwd_kernel(const MbParams
   }
 }
 
-template <int T, int ACT, bool PACKED>
+template <int T, int ACT, bool PACKED, int PK>
 static int mb_fwd_launch(const MbParams& p, cudaStream_t st) {
   const size_t smem = (size_t)mb_smem_bytes(p.D, T, false);
-  const bool maxp = p.pool == GL_POOL_MAX;
-  const void* kern = maxp ? (const void*)mb_fwd_kernel<T, ACT, PACKED, true>
-                          : (const void*)mb_fwd_kernel<T, ACT, PACKED, false>;
+  const void* kern = (const void*)mb_fwd_kernel<T, ACT, PACKED, PK>;
   int rc = ensure_dynamic_smem(kern, smem);
   if (rc) return rc;
   const int64_t tiles = (p.B + T - 1) / T;
   const int64_t chunks = (p.g1 - p.g0 + p.gpc - 1) / p.gpc;
   if (tiles > 2147483647LL || chunks > 65535) return GL_ERR_SHAPE;
-  const dim3 grid((unsigned)tiles, (unsigned)chunks);
-  if (maxp) mb_fwd_kernel<T, ACT, PACKED, true><<<grid, kMbFwdThreads, smem, st>>>(p);
-  else mb_fwd_kernel<T, ACT, PACKED, false><<<grid, kMbFwdThreads, smem, st>>>(p);
+  mb_fwd_kernel<T, ACT, PACKED, PK><<<dim3((unsigned)tiles, (unsigned)chunks), kMbFwdThreads, smem, st>>>(p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_cuda_error(e);
   count_launches(1);
   return GL_OK;
 }
 
+template <int T, int ACT, bool PACKED>
+static int mb_fwd_pk(const MbParams& p, cudaStream_t st) {
+  switch (pool_kind(p.pool)) {
+    case PK_MAX: return mb_fwd_launch<T, ACT, PACKED, PK_MAX>(p, st);
+    case PK_LSE:
+      if constexpr (T > 8) return GL_ERR_UNSUPPORTED;
+      else return mb_fwd_launch<T, ACT, PACKED, PK_LSE>(p, st);
+    case PK_POW:
+      if constexpr (T > 8) return GL_ERR_UNSUPPORTED;
+      else return mb_fwd_launch<T, ACT, PACKED, PK_POW>(p, st);
+    default: return mb_fwd_launch<T, ACT, PACKED, PK_ADD>(p, st);
+  }
+}
+
 template <int T, bool PACKED>
 static int mb_fwd_act(const MbParams& p, int act, cudaStream_t st) {
   switch (act) {
-    case GL_ACT_IDENTITY: return mb_fwd_launch<T, GL_ACT_IDENTITY, PACKED>(p, st);
-    case GL_ACT_RELU: return mb_fwd_launch<T, GL_ACT_RELU, PACKED>(p, st);
-    case GL_ACT_GELU: return mb_fwd_launch<T, GL_ACT_GELU, PACKED>(p, st);
+    case GL_ACT_IDENTITY: return mb_fwd_pk<T, GL_ACT_IDENTITY, PACKED>(p, st);
+    case GL_ACT_RELU: return mb_fwd_pk<T, GL_ACT_RELU, PACKED>(p, st);
+    case GL_ACT_GELU: return mb_fwd_pk<T, GL_ACT_GELU, PACKED>(p, st);
     default: return GL_ERR_UNSUPPORTED;
   }
 }
@@ -197,8 +241,13 @@ static int mb_run(const GlSharedArgs& a, bool bwd, void* stream) {
   if (!a.x || !a.idx || !a.w || !a.b || !a.counts) return GL_ERR_NULL;
   if (a.B > 2147483647LL || a.ldx < a.D || a.NB * a.C > 2147483647LL) return GL_ERR_SHAPE;
   if (((uintptr_t)a.idx & 15) || ((uintptr_t)a.w & 15) || ((uintptr_t)a.b & 15)) return GL_ERR_ALIGN;
-  if (a.pool != GL_POOL_MEAN && a.pool != GL_POOL_SUM && !(a.pool == GL_POOL_MAX && !bwd)) return GL_ERR_UNSUPPORTED;
+  if (a.pool < GL_POOL_MEAN || a.pool > GL_POOL_SOFTMAX || (a.pool == GL_POOL_MAX && bwd)) return GL_ERR_UNSUPPORTED;
+  const bool smooth = a.pool >= GL_POOL_LME;
+  if ((a.pool == GL_POOL_LME || a.pool == GL_POOL_SOFTMAX) && !(a.param > 0.f)) return GL_ERR_SHAPE;
+  if (a.pool == GL_POOL_POWER && !(a.param >= 1.f)) return GL_ERR_SHAPE;
+  if (bwd && smooth && (!a.c2 || (a.pool == GL_POOL_SOFTMAX && !a.c3))) return GL_ERR_NULL;
   if (a.winners && a.ldwin < a.g1 - a.g0) return GL_ERR_SHAPE;
+  if (a.stat && a.ldstat < a.g1 - a.g0) return GL_ERR_SHAPE;
   if (!bwd) {
     if (!a.pre) return GL_ERR_NULL;
     if (a.ldp < a.g1 - a.g0) return GL_ERR_SHAPE;
@@ -215,6 +264,7 @@ static int mb_run(const GlSharedArgs& a, bool bwd, void* stream) {
   if (T == 0) {
     T = mb_pick_tokens(a.D, bwd, optin);
     if (T < 0) return T;
+    if (!bwd && smooth && T > 8) T = 8;  // three-word states per token in registers
   } else if (T != 1 && T != 2 && T != 4 && T != 8 && T != 16 && T != 32) {
     return GL_ERR_UNSUPPORTED;
   }
@@ -234,6 +284,9 @@ static int mb_run(const GlSharedArgs& a, bool bwd, void* stream) {
   p.lgLPR = a.C == 8 ? 1 : a.C == 16 ? 2 : a.C == 32 ? 3 : 4;
   p.NB = a.NB; p.g0 = a.g0; p.g1 = a.g1; p.ldx = a.ldx; p.ldp = a.ldp; p.ldg = a.ldg; p.lddx = a.lddx;
   p.pool = a.pool; p.gpc = gpc; p.winners = a.winners; p.ldwin = a.ldwin;
+  p.stat = a.stat; p.ldstat = a.ldstat; p.c2 = a.c2; p.c3 = a.c3;
+  p.pp = PoolParam{a.param, pow_code(a.param), a.pool == GL_POOL_SOFTMAX};
+  p.ipm1 = pow_code(a.param) >= 1 ? pow_code(a.param) - 1 : -1;
   cudaStream_t st = (cudaStream_t)stream;
   const bool packed = a.packed != 0;
   switch (T) {

@@ -25,6 +25,12 @@ struct MbParams {
   int pool, gpc;
   int32_t* winners;
   int64_t ldwin;
+  float* stat;      // forward, LME / softmax: the log2-normaliser [B, ldstat]
+  int64_t ldstat;
+  const float* c2;  // backward, smooth pools: coefficients c2, c3 [B, ldg]
+  const float* c3;
+  PoolParam pp;
+  int ipm1;         // integer code of the power mean's p - 1 (-1: general)
 };
 
 template <bool PACKED>

@@ -73,7 +73,7 @@ __global__ void __launch_bounds__(kMbBwdThreads, 1) mb_bwd_kernel(const MbParams
   constexpr int HELD = LG < 4 ? HK : (HK >= 2 ? HK / 2 : 1);
   constexpr int XLD = mb_xld<T>(), DLD = mb_dld<T>();
   extern __shared__ __align__(16) float smem[];
-  __shared__ float c1s[NW][T];
+  __shared__ float c1s[NW][T], c2s[NW][T], c3s[NW][T];  // per-warp copies of the group's coefficients
   float* xs = smem;
   float* dxs = smem + (((size_t)p.D * XLD + 3) & ~(size_t)3);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -86,6 +86,7 @@ __global__ void __launch_bounds__(kMbBwdThreads, 1) mb_bwd_kernel(const MbParams
 #pragma unroll
   for (int s = 0; s < LGK; ++s) km |= ((nq >> s) & 1) << (2 - s);
   const bool hi3 = LG >= 4 && ((nq >> 3) & 1);  // the token-bit stage: this lane keeps the upper tokens
+  const bool smooth = p.pool >= GL_POOL_LME;     // uniform: dz through pool_dz
   const int slots = (int)(p.NB * C);
   const int64_t gb = p.g0 + (int64_t)blockIdx.y * p.gpc;
   const int64_t ge = gb + p.gpc < p.g1 ? gb + p.gpc : p.g1;
@@ -94,8 +95,12 @@ __global__ void __launch_bounds__(kMbBwdThreads, 1) mb_bwd_kernel(const MbParams
     const int nbv = (ng + C - 1) / C;
     __syncwarp();
     if (lane < T) {
-      const float v = t0 + lane < p.B ? __ldg(p.gpre + (int64_t)(t0 + lane) * p.ldg + (g - p.g0)) : 0.f;
+      const bool ok = t0 + lane < p.B;
+      const int64_t ci = (int64_t)(t0 + lane) * p.ldg + (g - p.g0);
+      const float v = ok ? __ldg(p.gpre + ci) : 0.f;
       c1s[warp][lane] = p.pool == GL_POOL_MEAN ? v / (float)ng : v;
+      c2s[warp][lane] = ok && p.c2 != nullptr ? __ldg(p.c2 + ci) : 0.f;
+      c3s[warp][lane] = ok && p.c3 != nullptr ? __ldg(p.c3 + ci) : 0.f;
     }
     __syncwarp();
     for (int base = warp * RPW; base < nbv; base += NW * RPW) {
@@ -139,7 +144,10 @@ __global__ void __launch_bounds__(kMbBwdThreads, 1) mb_bwd_kernel(const MbParams
             float z = bb[n];
 #pragma unroll
             for (int k = 0; k < 8; ++k) z = fmaf(w[n][k], xv[k][t], z);
-            dz[n][t] = n < nv ? c1[t] * dact_f<ACT>(z) : 0.f;
+            float d;
+            if (smooth) d = pool_dz<ACT>(p.pool, z, c1[t], c2s[warp][tc + t], c3s[warp][tc + t], p.pp.param, p.ipm1);
+            else d = c1[t] * dact_f<ACT>(z);
+            dz[n][t] = n < nv ? d : 0.f;
             dbacc[n] += dz[n][t];
           }
 #pragma unroll

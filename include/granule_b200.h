@@ -44,7 +44,7 @@
 extern "C" {
 #endif
 
-#define GL_ABI_VERSION 7
+#define GL_ABI_VERSION 8
 
 typedef enum GlStatus {
   GL_OK = 0,
@@ -57,16 +57,30 @@ typedef enum GlStatus {
   GL_ERR_DEVICE = -7         /* no usable device / attribute query failed */
 } GlStatus;
 
-/* Pool ids: the reference's "mean" and "max" (sparse_pooling/config.py:22-29) and the
-   "sum" extension.  Activation ids follow config.py:33.  Max pools act(z) over the valid
-   slots; its winner is the smallest slot attaining the maximum (kernels/triton_fused.py:129-140)
-   and its backward is the winner-event kernel gl_bwd_events_f32. */
-enum { GL_POOL_MEAN = 0, GL_POOL_SUM = 1, GL_POOL_MAX = 2 };
+/* Pool ids: the reference's operators (sparse_pooling/config.py:22-29) and the "sum"
+   extension.  Activation ids follow config.py:33.  With a = act(z) over the valid slots of a
+   group (n of them):
+     MEAN     pre = sum a / n                          SUM  pre = sum a
+     MAX      pre = max a; its winner is the smallest slot attaining the maximum
+              (kernels/triton_fused.py:129-140); backward: gl_bwd_events_f32
+     LME      pre = tau * (log sum e^(a/tau) - log n); param = log2(e) / tau;
+              stat = L2 = log2 sum 2^(a * param)        (pytorch_reference.py:80-85)
+     POWER    pre = (sum a^p / n)^(1/p), a = relu(z) >= 0; param = p >= 1   (:86-92)
+     SOFTMAX  pre = sum a e^(beta a) / sum e^(beta a); param = log2(e) * beta;
+              stat = L2 = log2 sum 2^(a * param)        (:93-98)
+   The smooth pools' backward is gl_bwd_f32 / gl_bwd_shared_f32 with the reference's
+   per-(token, group) coefficients (kernels/ops.py:242-262): dz = c1 * h * act'(z) with
+     MEAN/SUM h = 1 (c1 = gpre / n for MEAN, computed by the kernel; gpre for SUM)
+     LME      h = 2^(a * param - c2)                  c1 = gpre, c2 = L2
+     POWER    h = (a * c2)^(p - 1), 0 where z <= 0    c1 = gpre / n (0 where pre = 0), c2 = 1 / pre
+     SOFTMAX  h = 2^(a * param - c2) (1 + beta (a - c3)), beta = param * ln 2
+                                                      c1 = gpre, c2 = L2, c3 = pre */
+enum { GL_POOL_MEAN = 0, GL_POOL_SUM = 1, GL_POOL_MAX = 2, GL_POOL_LME = 3, GL_POOL_POWER = 4, GL_POOL_SOFTMAX = 5 };
 enum { GL_ACT_IDENTITY = 0, GL_ACT_RELU = 1, GL_ACT_GELU = 2 };
 
 /* Forward: pre[t, g - g0] = pool_{valid s of g} act(z[t, g, s]),
  *   z[t, g, s] = b[f] + sum_k w[8f+k] * x[t, idx[8f+k]],
- * pool = mean (divide by counts[g]) or sum.  `pre` is written, not accumulated.
+ * pool = one of the pool ids above.  `pre` is written, not accumulated.
  * Replaces fused_forward_states + merge_finalize (kernels/ops.py:104-199). */
 typedef struct GlFwdArgs {
   const float* x;           /* [B, ldx] token-major input, D used columns */
@@ -92,10 +106,14 @@ typedef struct GlFwdArgs {
   int64_t fcap;             /* row length of fmap (>= max nfeat) */
   int32_t* winners;         /* GL_POOL_MAX: optional [B, ldwin] output, the winning slot of each (t, g) */
   int64_t ldwin;
+  float* stat;              /* GL_POOL_LME / SOFTMAX: optional [B, ldstat] output, the log2-normaliser L2 */
+  int64_t ldstat;
+  float param;              /* the pool's parameter (see the pool ids); unused otherwise */
+  int32_t reserved2;        /* 0 */
 } GlFwdArgs;
 
-/* Backward: with c1[t, g] = gpre[t, g - g0] / counts[g] (mean) or gpre (sum) and
- *   dz[t, f] = c1[t, g] * act'(z[t, f]) for valid slots (0 for padding):
+/* Backward: with c1[t, g] = gpre[t, g - g0] / counts[g] (mean) or gpre (the other pools) and
+ *   dz[t, f] = c1[t, g] * h * act'(z[t, f]) for valid slots (0 for padding; h as for the pool ids):
  *   dx[t, d]   += sum_{f, k: idx[8f+k] = d} dz[t, f] * w[8f+k]
  *   dw[8f + k] += sum_t dz[t, f] * x[t, idx[8f+k]]
  *   db[f]      += sum_t dz[t, f]
@@ -131,6 +149,10 @@ typedef struct GlBwdArgs {
   const int16_t* fmap;
   const int32_t* nfeat;
   int64_t fcap;
+  const float* c2;          /* smooth pools: [B, ldg] coefficients c2, c3 (see the pool ids); else NULL */
+  const float* c3;
+  float param;              /* the pool's parameter */
+  int32_t reserved2;        /* 0 */
 } GlBwdArgs;
 
 /* Adam(W) step over n fp32 elements, in place (sparse_pooling/optim.py:26-64):
@@ -216,6 +238,12 @@ typedef struct GlSharedArgs {
   int32_t reserved;         /* 0 */
   int32_t* winners;         /* forward, GL_POOL_MAX: optional [B, ldwin] winning slots */
   int64_t ldwin;
+  float* stat;              /* forward, GL_POOL_LME / SOFTMAX: optional [B, ldstat] L2 output */
+  int64_t ldstat;
+  const float* c2;          /* backward, smooth pools: [B, ldg] coefficients c2, c3 */
+  const float* c3;
+  float param;              /* the pool's parameter */
+  int32_t reserved2;        /* 0 */
 } GlSharedArgs;
 
 int gl_fwd_shared_f32(const GlSharedArgs* args, void* stream);

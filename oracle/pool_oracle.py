@@ -1,12 +1,19 @@
-"""Float64 oracle of max pooling — TEST INFRASTRUCTURE ONLY.
+"""Float64 oracle of the max and smooth pooling operators — TEST INFRASTRUCTURE ONLY.
 
-Restates the reference's max operator on Mode-A tensors (Mode B through the equivalent Mode-A
-expansion): pytorch_reference.py:29-48 (pre-activations) and :51-75 (``pool``, "max": the
-maximum of act(z) over each group's valid slots, the winner being the smallest slot attaining
-it, kernels/triton_fused.py:129-140), with the backward of the winner-event kernel
-(triton_fused.py:476-520): per (token, group) one event dz = dy * act'(z_winner) on the winning
-neuron only.  Pinned by tests/test_oracle_golden.py to fixtures made by the reference itself
-(tests/golden/fwdbwd_max_*.npz).  Materialises z [B, G, slots]: small cases only.
+Restates the reference's operators on Mode-A tensors (Mode B through the equivalent Mode-A
+expansion): pytorch_reference.py:29-48 (pre-activations) and :51-98 (``pool``):
+
+* max: the maximum of act(z) over each group's valid slots, the winner being the smallest slot
+  attaining it (kernels/triton_fused.py:129-140), with the backward of the winner-event kernel
+  (triton_fused.py:476-520): per (token, group) one event dz = dy * act'(z_winner);
+* logmeanexp: tau (logsumexp(a / tau) - log n); dz = dy softmax(a / tau) act'(z);
+* softmax_weighted: sum softmax(beta a) a; dz = dy p (1 + beta (a - y)) act'(z);
+* power_mean (a = relu(z)): max-scaled (mean a^p)^(1/p); dz = dy a^(p-1) y^(1-p) / n for z > 0,
+  the derivatives the reference's dense backward uses (kernels/triton_fused.py:365-399).
+
+Pinned by tests/test_oracle_golden.py to fixtures made by the reference itself
+(tests/golden/fwdbwd_max_*.npz, fwdbwd_smooth_*.npz).  Materialises z [B, G, slots]: small cases
+only.
 """
 from __future__ import annotations
 
@@ -65,4 +72,62 @@ def max_backward(x, idx, w, b, counts, gy, act="relu", winner=None):
     np.add.at(dw, (g, s), dz[:, None] * xg[t, g, s])
     for k in range(8):
         np.add.at(dx, (t, i[g, s, k]), dz * wv[g, s, k])
+    return dx, dw.reshape(np.asarray(w).shape), db.reshape(np.asarray(b).shape)
+
+
+def _valid(i, counts):
+    return np.arange(i.shape[1])[None, :] < np.asarray(counts).reshape(-1, 1)
+
+
+def smooth_forward(x, idx, w, b, counts, kind, act, tau=1.0, beta=1.0, p=2.0):
+    """y [B, G] (float64) of the logmeanexp / softmax_weighted / power_mean operators."""
+    z, _, i, _ = _z(x, idx, w, b)
+    valid = _valid(i, counts)[None]
+    a = _act(z, act)
+    n = np.asarray(counts, np.float64)[None, :]
+    if kind == "power_mean":
+        am = np.where(valid, a, 0.0)
+        m = am.max(-1)
+        safe = np.where(m > 0, m, 1.0)
+        s = ((am / safe[..., None]) ** p).sum(-1) / n
+        return np.where(m > 0, safe * s ** (1.0 / p), 0.0)
+    u = np.where(valid, a / tau if kind == "logmeanexp" else beta * a, -np.inf)
+    m = u.max(-1, keepdims=True)
+    e = np.exp(u - m)
+    lse = m[..., 0] + np.log(e.sum(-1))
+    if kind == "logmeanexp":
+        return tau * (lse - np.log(n))
+    pw = e / e.sum(-1, keepdims=True)
+    return (pw * np.where(valid, a, 0.0)).sum(-1)
+
+
+def smooth_backward(x, idx, w, b, counts, gy, kind, act, tau=1.0, beta=1.0, p=2.0):
+    """(dx, dw, db) float64 of the smooth operators for upstream gy = dL/dpre [B, G]."""
+    z, xg, i, wv = _z(x, idx, w, b)
+    valid = _valid(i, counts)[None]
+    a = _act(z, act)
+    gy = np.asarray(gy, np.float64)[..., None]
+    if kind == "power_mean":
+        y = smooth_forward(x, idx, w, b, counts, kind, act, p=p)[..., None]
+        n = np.asarray(counts, np.float64)[None, :, None]
+        ys = np.where(y > 0, y, 1.0)
+        h = np.where((z > 0) & (y > 0), (np.maximum(a, 0.0) / ys) ** (p - 1.0) / n, 0.0)
+        dz = np.where(valid, gy * h, 0.0)
+    else:
+        u = np.where(valid, a / tau if kind == "logmeanexp" else beta * a, -np.inf)
+        e = np.exp(u - u.max(-1, keepdims=True))
+        pw = e / e.sum(-1, keepdims=True)
+        if kind == "logmeanexp":
+            h = pw
+        else:
+            y = (pw * np.where(valid, a, 0.0)).sum(-1, keepdims=True)
+            h = pw * (1.0 + beta * (a - y))
+        dz = np.where(valid, gy * h * _dact(z, act), 0.0)
+    db = dz.sum(0)                                                   # [G, slots]
+    dw = (dz[..., None] * xg).sum(0)                                 # [G, slots, 8]
+    B = dz.shape[0]
+    dx = np.zeros(np.asarray(x).shape)
+    contrib = dz[..., None] * wv[None]                               # [B, G, slots, 8]
+    tt = np.broadcast_to(np.arange(B)[:, None, None, None], contrib.shape)
+    np.add.at(dx, (tt.reshape(-1), np.broadcast_to(i[None], contrib.shape).reshape(-1)), contrib.reshape(-1))
     return dx, dw.reshape(np.asarray(w).shape), db.reshape(np.asarray(b).shape)

@@ -61,7 +61,7 @@ def load_case(name):
 def case_names():
     """Mode-A golden cases."""
     return sorted(p.stem[len("fwdbwd_"):] for p in GOLDEN.glob("fwdbwd_*.npz")
-                  if not p.stem.startswith(("fwdbwd_modeb_", "fwdbwd_max_")))
+                  if not p.stem.startswith(("fwdbwd_modeb_", "fwdbwd_max_", "fwdbwd_smooth_")))
 
 
 def max_case_names():
@@ -69,8 +69,19 @@ def max_case_names():
     return sorted(p.stem[len("fwdbwd_"):] for p in GOLDEN.glob("fwdbwd_max_*.npz"))
 
 
+def smooth_case_names():
+    """LogMeanExp / power-mean / softmax-weighted golden cases (Mode A and Mode B)."""
+    return sorted(p.stem[len("fwdbwd_"):] for p in GOLDEN.glob("fwdbwd_smooth_*.npz"))
+
+
+def oracle_params(meta):
+    """Keyword arguments of oracle/pool_oracle.py for a golden case's pooling parameters."""
+    prm = meta.get("params", {})
+    return {{"temperature": "tau", "beta": "beta", "p": "p"}[k]: v for k, v in prm.items()}
+
+
 def max_case_params(meta):
-    """(layout, idx, w, b) of a max-pooling golden case in the layer's storage layout."""
+    """(layout, idx, w, b) of a max- or smooth-pooling golden case in the layer's storage layout."""
     from granulelayer_b200.layout import SparseLayout, init_parameters
 
     C = meta["C"]

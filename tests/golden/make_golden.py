@@ -25,6 +25,8 @@ What it writes (all from the reference's own code on the CPU):
 * ``fwdbwd_max_<case>.npz`` — max pooling (Mode A and Mode B) with the reference's
   ``reference_forward`` (winner = smallest slot attaining the max) and autograd gradients,
   plus the winner slots.
+* ``fwdbwd_smooth_<case>.npz`` — LogMeanExp, power-mean and softmax-weighted pooling (Mode A
+  and Mode B) with the reference's float64 ``reference_forward`` and autograd gradients.
 * ``graph_hashes.json`` — sha256 of the reference's input-supergroup graphs: Mode-B
   ``supergroups.generate_indices`` (indices, feature sets, buckets) and the generalized
   ``experimental/kgen_graph.generate`` (K = 64 / C = 256 envelope, K = 16 / C = 16).
@@ -78,6 +80,17 @@ MAX_CASES = [
     ("max_modeb_c8_packed_gelu", 256, 7000, 5, 8, True, 17, 13, 0.2, "gelu"),
 ]
 
+# Smooth pools: (name, D, H, G, C (None = Mode A), packed, B, seed, bias_std, type, parameters, activation)
+SMOOTH_CASES = [
+    ("lme_modea_t05", 128, 6000, 12, None, False, 23, 21, 0.2, "logmeanexp", {"temperature": 0.5}, "identity"),
+    ("lme_modeb_c8_packed_t2", 256, 7000, 5, 8, True, 17, 22, 0.2, "logmeanexp", {"temperature": 2.0}, "relu"),
+    ("power_modea_p2", 96, 1001, 7, None, False, 9, 23, 0.1, "power_mean", {"p": 2.0}, "relu"),
+    ("power_modea_p3", 128, 4000, 6, None, False, 13, 24, 0.2, "power_mean", {"p": 3.0}, "relu"),
+    ("power_modeb_c64_p4", 512, 20000, 3, 64, False, 11, 25, 0.2, "power_mean", {"p": 4.0}, "relu"),
+    ("softmax_modea_b15", 128, 6000, 12, None, False, 23, 26, 0.2, "softmax_weighted", {"beta": 1.5}, "identity"),
+    ("softmax_modeb_c16_gelu", 300, 5000, 3, 16, False, 19, 27, 0.2, "softmax_weighted", {"beta": 0.7}, "gelu"),
+]
+
 # (D, H, G, C, S, R, generation, seed): Mode-B input-supergroup graphs
 GRAPH_CASES = [
     (256, 40000, 16, 8, 64, 2, "balanced_permutation", 0),
@@ -111,6 +124,7 @@ def sha(t: torch.Tensor) -> str:
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="directory that contains the sparse_pooling package")
+    ap.add_argument("--only", choices=["smooth"], help="write only this group of fixtures")
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
     from sparse_pooling.config import LevelSpec, PoolingConfig
@@ -118,6 +132,9 @@ def main():
     from sparse_pooling.reference import pytorch_reference as ref
 
     torch.set_num_threads(8)
+    if args.only == "smooth":
+        smooth_fixtures(ref, LevelSpec, PoolingConfig, SparseLayout, init_parameters)
+        return
     hashes = []
     for D, H, G, C, shared, packed, seed, bstd, chunk in INIT_CASES:
         L = SparseLayout(D, H, G, 8, C, shared, packed=packed)
@@ -215,6 +232,8 @@ def main():
             winner=winner.numpy(), dx=xd.grad.float().numpy(), dw=wd.grad[:GSUB].float().numpy(),
             db=bd.grad[:GSUB].float().numpy())
 
+    smooth_fixtures(ref, LevelSpec, PoolingConfig, SparseLayout, init_parameters)
+
     # input-supergroup graphs (supergroups.py generate_indices; kgen_graph.py generate)
     from sparse_pooling.experimental import kgen_graph as KG
     from sparse_pooling.supergroups import ConnectivityPlan, generate_indices
@@ -279,6 +298,27 @@ def main():
     np.savez_compressed(HERE / "adam.npz", lr=np.array(1e-2), beta1=np.array(0.9), beta2=np.array(0.999),
                         eps=np.array(1e-8), **out)
     print("wrote", sorted(p.name for p in HERE.iterdir() if p.suffix in (".npz", ".json")))
+
+
+def smooth_fixtures(ref, LevelSpec, PoolingConfig, SparseLayout, init_parameters):
+    for name, D, H, G, C, packed, B, seed, bstd, kind, params, act in SMOOTH_CASES:
+        L = SparseLayout(D, H, G, 8, C or 8, C is not None, packed=packed)
+        idx, w, b = init_parameters(L, "cpu", dtype=torch.float32, seed=seed, bias_std=bstd)
+        gen = torch.Generator().manual_seed(4000 + seed)
+        x = torch.randn(B, D, generator=gen)
+        xd = x.double().requires_grad_(True)
+        wd = w.double().requires_grad_(True)
+        bd = b.double().requires_grad_(True)
+        y = ref.reference_forward(xd, idx, wd, bd, L, PoolingConfig([LevelSpec(kind, activation=act, **params)]))
+        dy = torch.randn(y.shape, generator=gen)
+        (y * dy.double()).sum().backward()
+        np.savez_compressed(
+            HERE / f"fwdbwd_smooth_{name}.npz",
+            meta=json.dumps(dict(name=name, D=D, H=H, G=G, C=C, packed=packed, B=B, seed=seed, bias_std=bstd,
+                                 pool=kind, params=params, act=act, rule="distinct", mode="A" if C is None else "B",
+                                 idx_sha=sha(idx), w_sha=sha(w), b_sha=sha(b))),
+            idx=np.zeros(0, np.int16), x=x.numpy(), dy=dy.numpy(), y=y.detach().float().numpy(),
+            dx=xd.grad.float().numpy(), dw=wd.grad[:GSUB].float().numpy(), db=bd.grad[:GSUB].float().numpy())
 
 
 if __name__ == "__main__":
