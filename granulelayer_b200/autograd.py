@@ -79,13 +79,14 @@ class UnsupportedOnB200(NotImplementedError):
     """The layer configuration is outside the sm_100a hot path."""
 
 
-def check_supported(layout: SparseLayout, level: LevelSpec, dtype: torch.dtype):
+def check_supported(layout: SparseLayout, level: LevelSpec, dtype: torch.dtype, semantic: bool = False):
+    """Raise UnsupportedOnB200 for a level-1 configuration the kernels do not run."""
     if not layout.shared_indices and layout.block != 8:
         raise UnsupportedOnB200("Mode A layers store blocks of 8 neurons")
     if level.type not in B200_POOLS:
         raise UnsupportedOnB200(f"pooling {level.type!r} is not on the B200 path (supported: {B200_POOLS})")
-    if level.neurons_per_shard is not None:
-        raise UnsupportedOnB200("semantic two-level pooling is not on the B200 path")
+    if level.neurons_per_shard is not None and not semantic:
+        raise UnsupportedOnB200("neurons_per_shard belongs to a two-level configuration")
     if dtype != torch.float32:
         raise UnsupportedOnB200(f"the B200 kernels compute in float32 (layer dtype {dtype})")
 

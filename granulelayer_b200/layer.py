@@ -15,6 +15,7 @@ still constructs (so checkpoints load) but ``forward`` raises
 """
 from __future__ import annotations
 
+import math
 from typing import Optional, Union
 
 import torch
@@ -79,19 +80,36 @@ class SparsePoolingLayer(nn.Module):
         self.weight = nn.Parameter(w)
         self.bias = nn.Parameter(b)
         self._tnames = []
+        if self.cfg.is_semantic_hierarchy:   # layer.py:90-101: level-1 transform / level-2 weights
+            l1, l2 = self.cfg.levels
+            S = math.ceil(self.layout.max_group / l1.neurons_per_shard)
+            self.num_shards = S
+            G = output_dim
+            if l1.transform in ("affine", "gate"):
+                self.t_alpha = nn.Parameter(torch.ones(G, S, device=device))
+                self.t_beta = nn.Parameter(torch.zeros(G, S, device=device))
+                self._tnames += ["alpha", "beta"]
+            if l2.type == "weighted_sum":
+                self.t_v = nn.Parameter(torch.full((G, S), 1.0 / S, device=device))
+                self._tnames += ["v"]
         self._rt = None
         self._rt_key = None
+        self._units = None
 
     def _runtime(self) -> Level1Runtime:
         key = (self.indices.device, self.indices.data_ptr(), id(self.plan))
         if self._rt is None or self._rt_key != key:
-            check_supported(self.layout, self.cfg.levels[0] if not self.cfg.is_semantic_hierarchy
-                            else self.cfg.levels[0], self.compute_dtype)
+            check_supported(self.layout, self.cfg.levels[0], self.compute_dtype,
+                            semantic=self.cfg.is_semantic_hierarchy)
             if self.cfg.is_semantic_hierarchy:
-                from .autograd import UnsupportedOnB200
+                from .semantic import UnitLayout
 
-                raise UnsupportedOnB200("semantic two-level pooling is not on the B200 path")
-            self._rt = Level1Runtime(self.layout, self.indices, self.cfg.levels[0], self.plan)
+                units = UnitLayout(self.layout, self.cfg.levels[0].neurons_per_shard)
+                self._rt = Level1Runtime(units, units.view(self.indices), self.cfg.levels[0], self.plan,
+                                         counts=units.counts_tensor(self.indices.device))
+                self._units = units
+            else:
+                self._rt = Level1Runtime(self.layout, self.indices, self.cfg.levels[0], self.plan)
             self._rt_key = key
         return self._rt
 
@@ -143,7 +161,14 @@ class SparsePoolingLayer(nn.Module):
         lead = x.shape[:-1]
         x2 = x.reshape(-1, x.shape[-1])
         rt = self._runtime()
-        y = SparsePoolFunction.apply(x2, self.weight, self.bias, rt, self.effective_policy, self.compute_dtype)
+        if self.cfg.is_semantic_hierarchy:   # layer.py:186-195
+            from .semantic import SemanticPoolFunction
+
+            tparams = [getattr(self, "t_" + n) for n in self._tnames]
+            y = SemanticPoolFunction.apply(x2, self.weight, self.bias, rt, self._units, self.cfg, self.effective_policy,
+                                           self._tnames, *tparams)
+        else:
+            y = SparsePoolFunction.apply(x2, self.weight, self.bias, rt, self.effective_policy, self.compute_dtype)
         return y.reshape(*lead, y.shape[-1])
 
     def extra_repr(self) -> str:

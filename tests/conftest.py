@@ -61,7 +61,7 @@ def load_case(name):
 def case_names():
     """Mode-A golden cases."""
     return sorted(p.stem[len("fwdbwd_"):] for p in GOLDEN.glob("fwdbwd_*.npz")
-                  if not p.stem.startswith(("fwdbwd_modeb_", "fwdbwd_max_", "fwdbwd_smooth_")))
+                  if not p.stem.startswith(("fwdbwd_modeb_", "fwdbwd_max_", "fwdbwd_smooth_", "fwdbwd_semantic_")))
 
 
 def max_case_names():

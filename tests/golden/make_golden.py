@@ -27,6 +27,9 @@ What it writes (all from the reference's own code on the CPU):
   plus the winner slots.
 * ``fwdbwd_smooth_<case>.npz`` — LogMeanExp, power-mean and softmax-weighted pooling (Mode A
   and Mode B) with the reference's float64 ``reference_forward`` and autograd gradients.
+* ``fwdbwd_semantic_<case>.npz`` — two-level (semantic) pooling: level-1 shards, transform and
+  level-2 operator, with the reference's float64 ``reference_forward`` and autograd gradients,
+  including the transform / weighted-sum parameters' gradients.
 * ``graph_hashes.json`` — sha256 of the reference's input-supergroup graphs: Mode-B
   ``supergroups.generate_indices`` (indices, feature sets, buckets) and the generalized
   ``experimental/kgen_graph.generate`` (K = 64 / C = 256 envelope, K = 16 / C = 16).
@@ -91,6 +94,20 @@ SMOOTH_CASES = [
     ("softmax_modeb_c16_gelu", 300, 5000, 3, 16, False, 19, 27, 0.2, "softmax_weighted", {"beta": 0.7}, "gelu"),
 ]
 
+# Two-level pooling: (name, D, H, G, C (None = Mode A), packed, B, seed, bias_std, level 1, level 2,
+# level1_checkpoint)
+SEMANTIC_CASES = [
+    ("modea_mean_max", 128, 6000, 12, None, False, 23, 31, 0.2,
+     {"type": "mean", "neurons_per_shard": 128}, {"type": "max"}, "save"),
+    ("modea_max_affine_wsum", 128, 6000, 12, None, False, 19, 32, 0.2,
+     {"type": "max", "neurons_per_shard": 64, "transform": "affine"}, {"type": "weighted_sum"}, "save"),
+    ("modeb_c8_lme_gate_softmax", 256, 6400, 5, 8, True, 17, 33, 0.2,
+     {"type": "logmeanexp", "neurons_per_shard": 256, "transform": "gate", "temperature": 0.5},
+     {"type": "softmax_weighted", "beta": 2.0}, "recompute"),
+    ("modeb_c64_mean_act_topk", 512, 12288, 3, 64, False, 11, 34, 0.2,
+     {"type": "mean", "neurons_per_shard": 512, "transform": "activation"}, {"type": "topk_mean", "k": 2}, "save"),
+]
+
 # (D, H, G, C, S, R, generation, seed): Mode-B input-supergroup graphs
 GRAPH_CASES = [
     (256, 40000, 16, 8, 64, 2, "balanced_permutation", 0),
@@ -124,7 +141,7 @@ def sha(t: torch.Tensor) -> str:
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="directory that contains the sparse_pooling package")
-    ap.add_argument("--only", choices=["smooth"], help="write only this group of fixtures")
+    ap.add_argument("--only", choices=["smooth", "semantic"], help="write only this group of fixtures")
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
     from sparse_pooling.config import LevelSpec, PoolingConfig
@@ -134,6 +151,9 @@ def main():
     torch.set_num_threads(8)
     if args.only == "smooth":
         smooth_fixtures(ref, LevelSpec, PoolingConfig, SparseLayout, init_parameters)
+        return
+    if args.only == "semantic":
+        semantic_fixtures(ref, LevelSpec, PoolingConfig, SparseLayout, init_parameters)
         return
     hashes = []
     for D, H, G, C, shared, packed, seed, bstd, chunk in INIT_CASES:
@@ -233,6 +253,7 @@ def main():
             db=bd.grad[:GSUB].float().numpy())
 
     smooth_fixtures(ref, LevelSpec, PoolingConfig, SparseLayout, init_parameters)
+    semantic_fixtures(ref, LevelSpec, PoolingConfig, SparseLayout, init_parameters)
 
     # input-supergroup graphs (supergroups.py generate_indices; kgen_graph.py generate)
     from sparse_pooling.experimental import kgen_graph as KG
@@ -319,6 +340,40 @@ def smooth_fixtures(ref, LevelSpec, PoolingConfig, SparseLayout, init_parameters
                                  idx_sha=sha(idx), w_sha=sha(w), b_sha=sha(b))),
             idx=np.zeros(0, np.int16), x=x.numpy(), dy=dy.numpy(), y=y.detach().float().numpy(),
             dx=xd.grad.float().numpy(), dw=wd.grad[:GSUB].float().numpy(), db=bd.grad[:GSUB].float().numpy())
+
+
+def semantic_fixtures(ref, LevelSpec, PoolingConfig, SparseLayout, init_parameters):
+    import math
+
+    for name, D, H, G, C, packed, B, seed, bstd, l1, l2, ckpt in SEMANTIC_CASES:
+        L = SparseLayout(D, H, G, 8, C or 8, C is not None, packed=packed)
+        idx, w, b = init_parameters(L, "cpu", dtype=torch.float32, seed=seed, bias_std=bstd)
+        cfg = PoolingConfig([LevelSpec(**l1), LevelSpec(**l2)], level1_checkpoint=ckpt)
+        S = math.ceil(L.max_group / l1["neurons_per_shard"])
+        gen = torch.Generator().manual_seed(5000 + seed)
+        x = torch.randn(B, D, generator=gen)
+        tp = {}
+        if l1.get("transform") in ("affine", "gate"):
+            tp["alpha"] = 1.0 + 0.3 * torch.randn(G, S, generator=gen, dtype=torch.float64)
+            tp["beta"] = 0.2 * torch.randn(G, S, generator=gen, dtype=torch.float64)
+        if l2["type"] == "weighted_sum":
+            tp["v"] = torch.randn(G, S, generator=gen, dtype=torch.float64) / S
+        xd = x.double().requires_grad_(True)
+        wd = w.double().requires_grad_(True)
+        bd = b.double().requires_grad_(True)
+        tpd = {k: v.clone().requires_grad_(True) for k, v in tp.items()}
+        y = ref.reference_forward(xd, idx, wd, bd, L, cfg, tpd)
+        dy = torch.randn(y.shape, generator=gen)
+        (y * dy.double()).sum().backward()
+        extra = {f"t_{k}": v.float().numpy() for k, v in tp.items()}
+        extra.update({f"dt_{k}": v.grad.float().numpy() for k, v in tpd.items()})
+        np.savez_compressed(
+            HERE / f"fwdbwd_semantic_{name}.npz",
+            meta=json.dumps(dict(name=name, D=D, H=H, G=G, C=C, packed=packed, B=B, seed=seed, bias_std=bstd,
+                                 levels=[l1, l2], level1_checkpoint=ckpt, mode="A" if C is None else "B",
+                                 idx_sha=sha(idx), w_sha=sha(w), b_sha=sha(b))),
+            x=x.numpy(), dy=dy.numpy(), y=y.detach().float().numpy(), dx=xd.grad.float().numpy(),
+            dw=wd.grad[:GSUB].float().numpy(), db=bd.grad[:GSUB].float().numpy(), **extra)
 
 
 if __name__ == "__main__":

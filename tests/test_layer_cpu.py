@@ -38,7 +38,8 @@ def test_mode_b_cpu_forward_has_no_fallback(kw):
 
 
 @pytest.mark.parametrize("kw", [dict(pooling="topk_mean"), dict(dtype=torch.bfloat16),
-                                dict(pooling={"levels": [{"type": "mean", "neurons_per_shard": 128},
+                                # 3 shards of 20 blocks do not tile the 48 stored blocks of a group
+                                dict(pooling={"levels": [{"type": "mean", "neurons_per_shard": 160},
                                                          {"type": "weighted_sum"}]})])
 def test_unsupported_configurations_raise(kw):
     lay = _layer(**kw)
@@ -128,3 +129,27 @@ def test_connectivity_state_dict_checks():
     assert torch.equal(c.weight, a.weight)
     with pytest.raises(ValueError):
         SparsePoolingLayer(256, 20000, 8, shared_neurons=None, connectivity=ConnectivityPlan(64, 2, seed=1))
+
+
+SEMANTIC = {"levels": [{"type": "max", "neurons_per_shard": 128, "transform": "affine"}, {"type": "weighted_sum"}]}
+
+
+def test_semantic_layer_parameters():
+    """Two-level layers hold the reference's level-1 transform and level-2 weights (layer.py:90-101)."""
+    lay = _layer(pooling=SEMANTIC)
+    assert lay.num_shards == 3
+    assert set(lay.state_dict()) == {"indices", "weight", "bias", "t_alpha", "t_beta", "t_v"}
+    assert lay.t_alpha.shape == (8, 3) and float(lay.t_v.detach().sum()) == pytest.approx(8.0)
+    with pytest.raises(NativeLibraryError):        # level 1 still runs only on the GPU kernels
+        lay(torch.randn(2, 64))
+
+
+def test_semantic_state_dict_interchanges_with_reference(reference_path):
+    sys.path.insert(0, reference_path)
+    from sparse_pooling import SparsePoolingLayer as RefLayer
+
+    ref = RefLayer(64, 3000, 8, shared_neurons=None, pooling=SEMANTIC, dtype=torch.float32, seed=3, bias_std=0.1)
+    ours = _layer(pooling=SEMANTIC, seed=3, bias_std=0.1)
+    assert set(ref.state_dict()) == set(ours.state_dict())
+    for k, v in ref.state_dict().items():
+        assert torch.equal(v, ours.state_dict()[k]), k
