@@ -16,10 +16,10 @@ from pathlib import Path
 
 import torch
 
-ABI_VERSION = 8
+ABI_VERSION = 9
 LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libgranule_b200.so"
 
-POOL_MEAN, POOL_SUM, POOL_MAX, POOL_LME, POOL_POWER, POOL_SOFTMAX = 0, 1, 2, 3, 4, 5
+POOL_MEAN, POOL_SUM, POOL_MAX, POOL_LME, POOL_POWER, POOL_SOFTMAX, POOL_TOPK = 0, 1, 2, 3, 4, 5, 6
 ACT_IDS = {"identity": 0, "relu": 1, "gelu": 2}
 
 # The exported entry points, in header order (checked by the CPU test suite).
@@ -44,7 +44,7 @@ class GlFwdArgs(ctypes.Structure):
                 ("lidx", ctypes.c_void_p), ("fmap", ctypes.c_void_p), ("nfeat", ctypes.c_void_p),
                 ("fcap", ctypes.c_int64), ("winners", ctypes.c_void_p), ("ldwin", ctypes.c_int64),
                 ("stat", ctypes.c_void_p), ("ldstat", ctypes.c_int64), ("param", ctypes.c_float),
-                ("reserved2", ctypes.c_int32)]
+                ("k", ctypes.c_int32)]
 
 
 class GlBwdArgs(ctypes.Structure):
@@ -75,13 +75,13 @@ class GlSharedArgs(ctypes.Structure):
                [(n, ctypes.c_int32) for n in ("pool", "act", "packed", "tokens", "groups_per_cta", "reserved")] + \
                [("winners", ctypes.c_void_p), ("ldwin", ctypes.c_int64), ("stat", ctypes.c_void_p),
                 ("ldstat", ctypes.c_int64), ("c2", ctypes.c_void_p), ("c3", ctypes.c_void_p),
-                ("param", ctypes.c_float), ("reserved2", ctypes.c_int32)]
+                ("param", ctypes.c_float), ("k", ctypes.c_int32)]
 
 
 class GlEventArgs(ctypes.Structure):
     _fields_ = [(n, ctypes.c_void_p) for n in ("x", "idx", "w", "b", "winners", "coef", "dx", "dw", "db")] + \
                [(n, ctypes.c_int64) for n in ("B", "D", "NB", "C", "g0", "g1", "ldx", "ldwin", "ldc", "lddx")] + \
-               [(n, ctypes.c_int32) for n in ("shared", "packed", "act", "reserved")]
+               [(n, ctypes.c_int32) for n in ("shared", "packed", "act", "kev")]
 
 
 class GlK16Args(ctypes.Structure):
@@ -179,12 +179,13 @@ def _require_cuda(*ts):
 
 def fwd(x, idx, w, b, counts, pre, NB: int, g0: int, g1: int, pool: int, act: int, tokens: int = 0,
         groups_per_cta: int = 0, wabsmax=None, order=None, local=None, winners=None, stat=None,
-        param: float = 0.0):
+        param: float = 0.0, k: int = 0):
     """pre[:, :g1-g0] = pooled act(z) of groups [g0, g1); optionally wabsmax[g-g0] = max |w|; ``order``
     is an optional processing order (group_order); ``local`` = (lidx, fmap, nfeat) from
     group_feature_map turns on the per-group input staging; ``winners`` [B, g1-g0] int32 receives
     the winning slots of max pooling; ``stat`` [B, g1-g0] the log2-normaliser of LME / softmax
-    pooling, whose parameter (or power mean's p) is ``param``.  See GlFwdArgs."""
+    pooling, whose parameter (or power mean's p) is ``param``; top-K keeps ``k`` slots (``winners``
+    then [B, (g1-g0) k]).  See GlFwdArgs."""
     lidx, fmap, nfeat = local if local is not None else (None, None, None)
     _require_cuda(x, idx, w, b, counts, pre, wabsmax, order, lidx, fmap, nfeat, winners, stat)
     lib = load()
@@ -192,7 +193,7 @@ def fwd(x, idx, w, b, counts, pre, NB: int, g0: int, g1: int, pool: int, act: in
                   g0, g1, x.stride(0), pre.stride(0), pool, act, tokens, groups_per_cta, _ptr(wabsmax), _ptr(order),
                   _ptr(lidx), _ptr(fmap), _ptr(nfeat), fmap.shape[1] if fmap is not None else 0, _ptr(winners),
                   winners.stride(0) if winners is not None else 0, _ptr(stat),
-                  stat.stride(0) if stat is not None else 0, float(param), 0)
+                  stat.stride(0) if stat is not None else 0, float(param), int(k))
     with torch.cuda.device(x.device):
         _check(lib, lib.gl_fwd_f32(ctypes.byref(a), _stream(x.device)), "gl_fwd_f32")
 
@@ -227,13 +228,13 @@ def _shared_args(x, idx, w, b, counts, NB, C, g0, g1, pool, act, packed, tokens,
 
 
 def fwd_shared(x, idx, w, b, counts, pre, NB: int, C: int, g0: int, g1: int, pool: int, act: int, packed: bool,
-               tokens: int = 0, groups_per_cta: int = 0, winners=None, stat=None, param: float = 0.0):
+               tokens: int = 0, groups_per_cta: int = 0, winners=None, stat=None, param: float = 0.0, k: int = 0):
     """Mode B forward: pre[:, :g1-g0] = pooled act(z); ``winners``, ``stat`` and ``param`` as in
     ``fwd`` (GlSharedArgs)."""
     _require_cuda(x, idx, w, b, counts, pre, winners, stat)
     lib = load()
     a = _shared_args(x, idx, w, b, counts, NB, C, g0, g1, pool, act, packed, tokens, groups_per_cta)
-    a.pre, a.ldp, a.param = _ptr(pre), pre.stride(0), float(param)
+    a.pre, a.ldp, a.param, a.k = _ptr(pre), pre.stride(0), float(param), int(k)
     if winners is not None:
         a.winners, a.ldwin = _ptr(winners), winners.stride(0)
     if stat is not None:
@@ -260,13 +261,14 @@ def bwd_shared(x, idx, w, b, counts, gpre, dx, dw, db, NB: int, C: int, g0: int,
 
 
 def bwd_events(x, idx, w, b, winners, coef, dx, dw, db, NB: int, C: int, shared: bool, packed: bool, g0: int,
-               g1: int, act: int):
-    """Winner-event backward of max pooling (GlEventArgs): dx, dw, db += the winners' gradients."""
+               g1: int, act: int, kev: int = 1):
+    """Winner-event backward of max / top-K pooling (GlEventArgs): dx, dw, db += the gradients of the
+    ``kev`` chosen slots per (token, group) in ``winners`` [B, (g1-g0) kev]."""
     _require_cuda(x, idx, w, b, winners, coef, dx, dw, db)
     lib = load()
     a = GlEventArgs(_ptr(x), _ptr(idx), _ptr(w), _ptr(b), _ptr(winners), _ptr(coef), _ptr(dx), _ptr(dw), _ptr(db),
                     x.shape[0], x.shape[1], NB, C, g0, g1, x.stride(0), winners.stride(0), coef.stride(0),
-                    dx.stride(0), int(bool(shared)), int(bool(packed)), act, 0)
+                    dx.stride(0), int(bool(shared)), int(bool(packed)), act, int(kev))
     with torch.cuda.device(x.device):
         _check(lib, lib.gl_bwd_events_f32(ctypes.byref(a), _stream(x.device)), "gl_bwd_events_f32")
 

@@ -112,7 +112,9 @@ class Level1Runtime:
         self.counts_f32 = self.counts_i32.to(torch.float32)
         self.pool = {"mean": _native.POOL_MEAN, "sum": _native.POOL_SUM, "max": _native.POOL_MAX,
                      "logmeanexp": _native.POOL_LME, "power_mean": _native.POOL_POWER,
-                     "softmax_weighted": _native.POOL_SOFTMAX}.get(level.type, _native.POOL_MEAN)
+                     "softmax_weighted": _native.POOL_SOFTMAX, "topk_mean": _native.POOL_TOPK}.get(
+                         level.type, _native.POOL_MEAN)
+        self.k = level.k if level.type == "topk_mean" else 1   # slots per (token, group) of the event pools
         self.param = kernel_param(level)
         self.act = _native.ACT_IDS[level.activation]
         self.last_info: Dict = {}
@@ -158,9 +160,10 @@ class Level1Runtime:
     def locality(self):
         """(lidx, fmap, nfeat) when every group reads at most a quarter of the input features (the
         kernels then stage only each group's features), else None.  Built once per index tensor.
-        The smooth pools (LogMeanExp, power mean, softmax-weighted) run on the full-row staging."""
+        The smooth pools (LogMeanExp, power mean, softmax-weighted) and top-K run on the full-row
+        staging."""
         if (self.plan.b200_locality == "off" or self.layout.shared_indices or not self.idx.is_cuda
-                or self.smooth):
+                or self.smooth or self.pool == _native.POOL_TOPK):
             return None
         G, D, NB = self.groups, self.layout.input_dim, self.layout.blocks_per_group
         if G == 0 or G > 65535 or D < 256:
@@ -240,7 +243,8 @@ class Level1Runtime:
 
     @property
     def is_max(self) -> bool:
-        return self.pool == _native.POOL_MAX
+        """Max or top-K: winner slots in the forward, the winner-event backward."""
+        return self.pool in (_native.POOL_MAX, _native.POOL_TOPK)
 
     @property
     def smooth(self) -> bool:
@@ -273,7 +277,7 @@ class Level1Runtime:
         self.check_devices(x, w, b)
         self.resolve_reduction(B)
         pre = torch.empty((B, self.groups), device=x.device, dtype=torch.float32)
-        winners = (torch.empty((B, self.groups), device=x.device, dtype=torch.int32)
+        winners = (torch.empty((B, self.groups * self.k), device=x.device, dtype=torch.int32)
                    if self.is_max and track_ids else None)
         stat = (torch.empty((B, self.groups), device=x.device, dtype=torch.float32)
                 if self.pool in (_native.POOL_LME, _native.POOL_SOFTMAX) else None)
@@ -285,7 +289,8 @@ class Level1Runtime:
         if self.layout.shared_indices:
             _native.fwd_shared(x, self.idx, w, b, self.counts_i32, pre, self.layout.blocks_per_group,
                                self.layout.block, 0, self.groups, self.pool, self.act, self.layout.packed,
-                               tokens=self.plan.b200_fwd_tokens, winners=winners, stat=stat, param=self.param)
+                               tokens=self.plan.b200_fwd_tokens, winners=winners, stat=stat, param=self.param,
+                               k=self.k)
             self.last_info.update(forward_backend="b200", forward_kernel="gl_fwd_shared_f32", workspace_bytes=0)
             return out
         wabsmax = (torch.empty(self.groups, device=x.device, dtype=torch.float32)
@@ -293,24 +298,29 @@ class Level1Runtime:
         _native.fwd(x, self.idx, w, b, self.counts_i32, pre, self.layout.blocks_per_group, 0, self.groups,
                     self.pool, self.act, tokens=self.plan.b200_fwd_tokens, wabsmax=wabsmax,
                     order=self.order(self.tokens(False)) if B > 0 else None,
-                    local=self.locality() if B > 0 else None, winners=winners, stat=stat, param=self.param)
+                    local=self.locality() if B > 0 else None, winners=winners, stat=stat, param=self.param,
+                    k=self.k)
         self.last_info.update(forward_backend="b200", workspace_bytes=0)
         if wabsmax is not None:
             out["wabsmax"] = wabsmax
         return out
 
     def _event_backward(self, x, w, b, g_pre, saved, dw_buf, db_buf) -> torch.Tensor:
-        """Max pooling: one winner event per (token, group) (autograd.py:280-290); winners come from
-        the forward (save_winners) or are recomputed here (minimal_stats)."""
+        """Max / top-K pooling: one event per chosen slot of each (token, group), coefficient
+        dL/dpre (divided by min(k, n) for top-K) (autograd.py:280-290); the slots come from the forward
+        (save_winners) or are recomputed here (minimal_stats)."""
         winners = saved.get("winner")
         recomputed = winners is None
         if recomputed:
             winners = self.forward(x, w, b, track_ids=True)["winner"]
         self.last_info["recomputed_stats"] = recomputed
+        coef = g_pre
+        if self.pool == _native.POOL_TOPK:
+            coef = (g_pre / torch.clamp(self.counts_f32, max=float(self.k))[None, :]).contiguous()
         dx = torch.zeros(x.shape, device=x.device, dtype=torch.float32)
         L = self.layout
-        _native.bwd_events(x, self.idx, w, b, winners, g_pre, dx, dw_buf, db_buf, L.blocks_per_group, L.block,
-                           L.shared_indices, L.packed, 0, self.groups, self.act)
+        _native.bwd_events(x, self.idx, w, b, winners, coef, dx, dw_buf, db_buf, L.blocks_per_group, L.block,
+                           L.shared_indices, L.packed, 0, self.groups, self.act, kev=self.k)
         self.last_info["backward_backend"] = "b200"
         self.last_info["backward_kernel"] = "gl_bwd_events_f32"
         return dx

@@ -6,11 +6,13 @@ validation so that code constructing them for the reference constructs them
 here unchanged.  Fields that only steer the reference's RTX 3090 tuning tables
 are accepted and recorded but do not change what the B200 kernels do.
 
-B200 execution covers the fan-in-8, Mode-A (independent indices) path with the
-``mean`` pool (the reference's default activation for it is ReLU) and the
-``sum`` extension (``sum = n_g * mean``; the reference has no sum operator).
-The other operators parse (so configs round-trip) and are refused at run time
-with a clear error.
+B200 execution covers fan-in-8 layers in Mode A (independent indices) and Mode B
+(shared index records) with every single-level operator of the reference (mean,
+max, top-K mean, LogMeanExp, power mean, softmax-weighted), the ``sum``
+extension (``sum = n_g * mean``; the reference has no sum operator) and two-level
+(semantic) hierarchies whose level-1 shards tile the stored blocks.  Anything
+else parses (so configs round-trip) and is refused at run time with a clear
+error.
 """
 from __future__ import annotations
 
@@ -29,7 +31,7 @@ POOL_ID = {name: i for i, name in enumerate(POOL_TYPES)}
 ACT_ID = {name: i for i, name in enumerate(ACTIVATIONS)}
 
 # Operators the B200 kernels execute (the hot path); the rest are parsed only.
-B200_POOLS = ("mean", "sum", "max", "logmeanexp", "power_mean", "softmax_weighted")
+B200_POOLS = ("mean", "sum", "max", "logmeanexp", "power_mean", "softmax_weighted", "topk_mean")
 
 # per-neuron activation used when the spec leaves it empty (config.py:42-49)
 DEFAULT_ACTIVATION = {

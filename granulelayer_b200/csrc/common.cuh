@@ -45,12 +45,14 @@ __device__ __forceinline__ float dact_f(float z) {
 //   PK_LSE  LogMeanExp / softmax-weighted, base-2 log-sum-exp of u = a * param:
 //           s0 = m = max u, s1 = sum 2^(u - m), s2 = sum a 2^(u - m) (softmax only)
 //   PK_POW  power mean of a = relu(z) >= 0: s0 = m = max a, s1 = sum (a / m)^p, s2 = 1 / m
+//   PK_TOPK top-K mean: per-warp lists of the best keys (below); PK_TOPK64 for k = 64
 // A lane folds its values in one at a time and rescales its sums only when a new maximum
 // arrives; lanes and warps then merge their states.
-enum { PK_ADD = 0, PK_MAX = 1, PK_LSE = 2, PK_POW = 3 };
+enum { PK_ADD = 0, PK_MAX = 1, PK_LSE = 2, PK_POW = 3, PK_TOPK = 4, PK_TOPK64 = 5 };
 
-inline int pool_kind(int pool) {
+inline int pool_kind(int pool, int k = 0) {
   return pool == GL_POOL_MAX ? PK_MAX
+       : pool == GL_POOL_TOPK ? (k > 32 ? PK_TOPK64 : PK_TOPK)
        : (pool == GL_POOL_LME || pool == GL_POOL_SOFTMAX) ? PK_LSE
        : pool == GL_POOL_POWER ? PK_POW : PK_ADD;
 }
@@ -80,7 +82,11 @@ struct PoolParam {
   float param;  // LME: log2(e) / tau; softmax: log2(e) * beta; power: p
   int ip;       // power: pow_code(p)
   bool want_t;  // softmax: track sum a 2^(u - m)
+  int k;        // top-K: slots kept
 };
+
+// A valid top-K count: a power of two in [1, 64] (config.py:117-119).
+inline bool topk_k_ok(int k) { return k >= 1 && k <= 64 && (k & (k - 1)) == 0; }
 
 __device__ __forceinline__ void lse_push(float& m, float& s, float& t, float u, float a, bool want_t) {
   const float d = u - m;
@@ -148,6 +154,69 @@ __device__ __forceinline__ float pool_dz(int pool, float z, float c1, float c2, 
   if (pool == GL_POOL_LME) return c1 * pw * dact_f<ACT>(z);
   const float beta = param * 0.6931471805599453f;
   return c1 * pw * fmaf(beta, a - c3, 1.f) * dact_f<ACT>(z);
+}
+
+// ---------------------------------------------------------------------------
+// Top-K pooling (kernels/triton_fused.py:51-55, 141-173): candidates are ranked by 64-bit keys, the
+// order-preserving bits of z above the complemented slot, so a larger key is a larger z and, on
+// ties, the smaller slot.  A warp keeps one sorted (descending) list per token: position p at lane
+// p % 32 of word p / 32 (KW = 1 word for k <= 32, 2 for k = 64), LLONG_MIN past the entries.
+__device__ __forceinline__ long long topk_key(float z, int slot) {
+  const int zb = __float_as_int(z);
+  const unsigned s = (unsigned)(zb >= 0 ? zb : zb ^ 0x7FFFFFFF);
+  return (long long)(((unsigned long long)s << 32) | (unsigned long long)(0xFFFFFFFFu - (unsigned)slot));
+}
+
+__device__ __forceinline__ float topk_value(long long key) {
+  const int hi = (int)(key >> 32);
+  return __int_as_float(hi >= 0 ? hi : hi ^ 0x7FFFFFFF);
+}
+
+__device__ __forceinline__ int topk_slot(long long key) {
+  return (int)(0xFFFFFFFFu - (unsigned)(key & 0xFFFFFFFFll));
+}
+
+// The key at position k - 1 (the entry a candidate must beat).
+template <int KW>
+__device__ __forceinline__ long long topk_last(const long long (&w)[KW], int k) {
+  return KW == 1 ? __shfl_sync(kFullMask, w[0], k - 1) : __shfl_sync(kFullMask, w[KW - 1], 31);
+}
+
+// Insert the warp-uniform key c (keys in a list are distinct: their slots differ).
+template <int KW>
+__device__ __forceinline__ void topk_insert(long long (&w)[KW], long long c, int k, int lane) {
+  const unsigned live = k >= 32 ? kFullMask : (1u << k) - 1u;
+  int pos = __popc(__ballot_sync(kFullMask, w[0] > c) & live);
+  if constexpr (KW == 2) pos += __popc(__ballot_sync(kFullMask, w[1] > c));
+  if (pos >= k) return;
+  const long long up0 = __shfl_up_sync(kFullMask, w[0], 1);
+  if constexpr (KW == 1) {
+    w[0] = lane > pos ? up0 : (lane == pos ? c : w[0]);
+  } else {
+    const long long carry = __shfl_sync(kFullMask, w[0], 31);
+    const long long up1 = __shfl_up_sync(kFullMask, w[1], 1);
+    if (pos < 32) {
+      w[1] = lane == 0 ? carry : up1;
+      w[0] = lane > pos ? up0 : (lane == pos ? c : w[0]);
+    } else {
+      const int p1 = pos - 32;
+      w[1] = lane > p1 ? up1 : (lane == p1 ? c : w[1]);
+    }
+  }
+}
+
+// Offer each lane's candidate key (where `has`) to the warp's list; thr tracks topk_last.
+template <int KW>
+__device__ __forceinline__ void topk_offer(long long (&w)[KW], long long& thr, bool has, long long key, int k,
+                                           int lane) {
+  unsigned m = __ballot_sync(kFullMask, has && key > thr);
+  while (m) {
+    const int src = __ffs(m) - 1;
+    topk_insert<KW>(w, __shfl_sync(kFullMask, key, src), k, lane);
+    thr = topk_last<KW>(w, k);
+    m &= ~(1u << src);
+    m &= __ballot_sync(kFullMask, has && key > thr);
+  }
 }
 
 // Eight int16 indices of one neuron record, loaded as one 16-byte vector and

@@ -1,12 +1,13 @@
-// Winner-event backward of max pooling (Mode A and Mode B), fp32.
+// Winner-event backward of max and top-K pooling (Mode A and Mode B), fp32.
 //
 // Replaces the reference's sparse winner-event backward (kernels/triton_fused.py:476-520
-// bwd_events_kernel, launched by ops.py:281-293): each (token t, group g) event names one neuron,
-// the winner slot s of the forward, and a coefficient c (dL/dpre[t, g]); the neuron's z is
-// recomputed (8 FMAs, only act'(z) is needed) and
+// bwd_events_kernel, launched by ops.py:281-293): each event (token t, group g, j < kev) names one
+// neuron, a slot s the forward chose (the max's winner, or one of the top-K), and the coefficient
+// c of (t, g) (dL/dpre[t, g], divided by min(k, n) for top-K); the neuron's z is recomputed
+// (8 FMAs, only act'(z) is needed) and
 //   dz = c * act'(z),  db[s] += dz,  dw[s][k] += dz * x[t, idx_k],  dx[t, idx_k] += dz * w[s][k].
-// One thread per event; events with s < 0 or c == 0 do nothing.  The B*G events touch B*G neurons
-// (not B*N): the whole backward is a few global reductions per event.
+// One thread per event; events with s < 0 or c == 0 do nothing.  The B*G*kev events touch that
+// many neurons (not B*N): the whole backward is a few global reductions per event.
 #include "common.cuh"
 
 namespace gl {
@@ -17,10 +18,11 @@ template <int ACT, int MODE>  // MODE 0: Mode A; 1: Mode B canonical; 2: Mode B 
 __global__ void __launch_bounds__(kEventThreads) event_bwd_kernel(const GlEventArgs a, int64_t n_events) {
   const int64_t e = (int64_t)blockIdx.x * kEventThreads + threadIdx.x;
   if (e >= n_events) return;
-  const int64_t Gl = a.g1 - a.g0;
-  const int64_t t = e / Gl, gl = e - t * Gl, g = a.g0 + gl;
+  const int64_t kev = a.kev > 0 ? a.kev : 1;
+  const int64_t per_t = (a.g1 - a.g0) * kev;
+  const int64_t t = e / per_t, re = e - t * per_t, gl = re / kev, g = a.g0 + gl;
   const int slots = (int)(a.NB * (MODE == 0 ? 8 : a.C));
-  const int s = __ldg(a.winners + t * a.ldwin + gl);
+  const int s = __ldg(a.winners + t * a.ldwin + re);
   const float c = __ldg(a.coef + t * a.ldc + gl);
   if (s < 0 || s >= slots || c == 0.f) return;
   const int D = (int)a.D;
@@ -103,10 +105,12 @@ extern "C" int gl_bwd_events_f32(const GlEventArgs* args, void* stream) {
     return GL_ERR_SHAPE;
   if (a.B == 0 || a.g1 == a.g0) return GL_OK;
   if (!a.x || !a.idx || !a.w || !a.b || !a.winners || !a.coef || !a.dx || !a.dw || !a.db) return GL_ERR_NULL;
-  if (a.ldx < a.D || a.lddx < a.D || a.ldwin < a.g1 - a.g0 || a.ldc < a.g1 - a.g0) return GL_ERR_SHAPE;
+  const int64_t kev = a.kev > 0 ? a.kev : 1;
+  if (kev > 64) return GL_ERR_SHAPE;
+  if (a.ldx < a.D || a.lddx < a.D || a.ldwin < (a.g1 - a.g0) * kev || a.ldc < a.g1 - a.g0) return GL_ERR_SHAPE;
   if (((uintptr_t)a.idx & 15) || ((uintptr_t)a.w & 15) || ((uintptr_t)a.dw & 7)) return GL_ERR_ALIGN;
   const int mode = a.shared ? (a.packed ? 2 : 1) : 0;
-  const int64_t n = a.B * (a.g1 - a.g0);
+  const int64_t n = a.B * (a.g1 - a.g0) * kev;
   cudaStream_t st = (cudaStream_t)stream;
   switch (a.act) {
     case GL_ACT_IDENTITY: return event_launch<GL_ACT_IDENTITY>(a, mode, n, st);

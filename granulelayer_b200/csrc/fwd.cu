@@ -40,6 +40,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                const PoolParam pp) {
   constexpr bool MAXP = PK == PK_MAX;
   constexpr bool SM = PK == PK_LSE || PK == PK_POW;  // three-word states
+  constexpr bool TK = PK == PK_TOPK || PK == PK_TOPK64;
+  constexpr int KW = PK == PK_TOPK64 ? 2 : 1;        // top-K list words per lane
   constexpr int V = T < 4 ? T : 4;   // tokens per lane
   constexpr int LPN = T / V;         // lanes per neuron
   constexpr int NPW = 32 / LPN;      // neurons per warp step
@@ -71,6 +73,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   const int64_t gb = g0 + (int64_t)blockIdx.y * gpc;
   const int64_t ge = gb + gpc < g1 ? gb + gpc : g1;
   const float* xq = xs + q * V;
+  // top-K: each warp's lists, then the block's merge ([NW][T][KW * 32] keys after the staged tile)
+  long long* tks = reinterpret_cast<long long*>(xs + ((((LOCAL ? lm.fcap : D) * T) + 3) & ~3));
 
   for (int64_t g = gb; g < ge; ++g) {
     const int ng = min(counts[g], slots);
@@ -85,6 +89,15 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       wid[v] = 0x7fffffff;
     }
     float wmx = 0.f;  // max |w| over the valid slots this lane reads (for the backward's fixed-point scale)
+    long long tkw[TK ? T : 1][KW], tthr[TK ? T : 1];
+    if constexpr (TK) {
+#pragma unroll
+      for (int t = 0; t < T; ++t) {
+        tthr[t] = LLONG_MIN;
+#pragma unroll
+        for (int wd = 0; wd < KW; ++wd) tkw[t][wd] = LLONG_MIN;
+      }
+    }
 
     for (int s0 = warp * NPW * UNR; s0 < ng; s0 += NW * NPW * UNR) {
       Rec8 r[UNR];
@@ -126,7 +139,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             z[0] = fmaf(wr[u].w[k], row[0], z[0]);
           }
         }
-        if (ok[u]) {
+        if constexpr (TK) {  // every lane takes part in the warp's insertions
+#pragma unroll
+          for (int t = 0; t < T; ++t)
+            topk_offer<KW>(tkw[t], tthr[t], ok[u] && q == t / V, topk_key(z[t % V], sl[u]), pp.k, lane);
+        }
+        if (ok[u] && !TK) {
 #pragma unroll
           for (int v = 0; v < V; ++v) {
             const float a = act_f<ACT>(z[v]);
@@ -148,6 +166,45 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         }
       }
     }
+    if constexpr (TK) {
+      // merge the warps' lists: warp t takes token t
+#pragma unroll
+      for (int t = 0; t < T; ++t)
+#pragma unroll
+        for (int wd = 0; wd < KW; ++wd) tks[((warp * T + t) * KW + wd) * 32 + lane] = tkw[t][wd];
+      __syncthreads();
+      if (warp < T) {
+        const int t = warp;
+        long long wl[KW];
+#pragma unroll
+        for (int wd = 0; wd < KW; ++wd) wl[wd] = tks[(t * KW + wd) * 32 + lane];
+        long long thr = topk_last<KW>(wl, pp.k);
+        for (int i = 1; i < NW; ++i)
+#pragma unroll
+          for (int wd = 0; wd < KW; ++wd) {
+            const long long c = tks[((i * T + t) * KW + wd) * 32 + lane];
+            topk_offer<KW>(wl, thr, c != LLONG_MIN, c, pp.k, lane);
+          }
+        const int kk = min(pp.k, ng);
+        float sum = 0.f;
+#pragma unroll
+        for (int wd = 0; wd < KW; ++wd)
+          if (wd * 32 + lane < kk) sum += act_f<ACT>(topk_value(wl[wd]));
+#pragma unroll
+        for (int off = 16; off; off >>= 1) sum += __shfl_xor_sync(kFullMask, sum, off);
+        if (t0 + t < B) {
+          if (lane == 0) pre[(int64_t)(t0 + t) * ldp + (g - g0)] = sum / (float)kk;
+          if (winners != nullptr)
+#pragma unroll
+            for (int wd = 0; wd < KW; ++wd) {
+              const int pos = wd * 32 + lane;
+              if (pos < pp.k)
+                winners[(int64_t)(t0 + t) * ldwin + (g - g0) * pp.k + pos] = pos < kk ? topk_slot(wl[wd]) : -1;
+            }
+        }
+      }
+      __syncthreads();
+    } else {
     // reduce over the neurons of the warp (lanes with equal q), then over warps
 #pragma unroll
     for (int off = LPN; off < 32; off <<= 1)
@@ -231,12 +288,20 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       wabsmax[g - g0] = m;
     }
     __syncthreads();
+    }
   }
+}
+
+// Dynamic shared memory: the staged tile, plus the top-K lists ([NW][T][KW * 32] keys).
+static size_t fwd_smem(int64_t rows, int T, int pool, int k) {
+  const size_t tile = (size_t)((rows * T + 3) & ~3LL) * sizeof(float);
+  if (pool != GL_POOL_TOPK) return (size_t)rows * T * sizeof(float);
+  return tile + (size_t)(kFwdThreads / 32) * T * (k > 32 ? 64 : 32) * sizeof(long long);
 }
 
 template <int T, int ACT, bool LOCAL, int PK>
 static int launch_fwd(const GlFwdArgs& a, int gpc, cudaStream_t st) {
-  const size_t smem = (size_t)(LOCAL ? a.fcap : a.D) * T * sizeof(float);
+  const size_t smem = fwd_smem(LOCAL ? a.fcap : a.D, T, a.pool, a.k);
   auto kern = fwd_kernel<T, ACT, LOCAL, PK>;
   int rc = ensure_dynamic_smem((const void*)kern, smem);
   if (rc) return rc;
@@ -248,7 +313,7 @@ static int launch_fwd(const GlFwdArgs& a, int gpc, cudaStream_t st) {
   kern<<<grid, kFwdThreads, smem, st>>>(a.x, a.idx, a.w, a.b, a.counts, a.pre, (int)a.B, (int)a.D, a.NB, a.g0,
                                         a.g1, a.ldx, a.ldp, a.pool, gpc, a.wabsmax, a.order, lm, a.winners, a.ldwin,
                                         a.stat, a.ldstat, PoolParam{a.param, pow_code(a.param),
-                                                                    a.pool == GL_POOL_SOFTMAX});
+                                                                    a.pool == GL_POOL_SOFTMAX, a.k});
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_cuda_error(e);
   count_launches(1);
@@ -265,11 +330,18 @@ static int dispatch_act_fwd2(const GlFwdArgs& a, int gpc, cudaStream_t st) {
   }
 }
 
-// The smooth pools (LSE, POW kinds) run on the full-row staging only (no locality maps).
+// The smooth pools (LSE, POW kinds) and top-K run on the full-row staging only (no locality maps);
+// top-K tiles hold at most 4 tokens (its lists live in registers).
 template <int T, bool LOCAL>
 static int dispatch_act_fwd(const GlFwdArgs& a, int gpc, cudaStream_t st) {
-  switch (pool_kind(a.pool)) {
+  switch (pool_kind(a.pool, a.k)) {
     case PK_MAX: return dispatch_act_fwd2<T, LOCAL, PK_MAX>(a, gpc, st);
+    case PK_TOPK:
+      if constexpr (LOCAL || T > 4) return GL_ERR_UNSUPPORTED;
+      else return dispatch_act_fwd2<T, false, PK_TOPK>(a, gpc, st);
+    case PK_TOPK64:
+      if constexpr (LOCAL || T > 4) return GL_ERR_UNSUPPORTED;
+      else return dispatch_act_fwd2<T, false, PK_TOPK64>(a, gpc, st);
     case PK_LSE:
       if constexpr (LOCAL) return GL_ERR_UNSUPPORTED;
       else return dispatch_act_fwd2<T, false, PK_LSE>(a, gpc, st);
@@ -311,10 +383,11 @@ extern "C" int gl_fwd_f32(const GlFwdArgs* args, void* stream) {
   if (!a.x || !a.idx || !a.w || !a.b || !a.counts || !a.pre) return GL_ERR_NULL;
   if (a.B > 2147483647LL || a.ldx < a.D || a.ldp < a.g1 - a.g0) return GL_ERR_SHAPE;
   if (((uintptr_t)a.idx & 15) || ((uintptr_t)a.w & 15)) return GL_ERR_ALIGN;
-  if (a.pool < GL_POOL_MEAN || a.pool > GL_POOL_SOFTMAX) return GL_ERR_UNSUPPORTED;
+  if (a.pool < GL_POOL_MEAN || a.pool > GL_POOL_TOPK) return GL_ERR_UNSUPPORTED;
+  if (a.pool == GL_POOL_TOPK && !topk_k_ok(a.k)) return GL_ERR_SHAPE;
   if ((a.pool == GL_POOL_LME || a.pool == GL_POOL_SOFTMAX) && !(a.param > 0.f)) return GL_ERR_SHAPE;
   if (a.pool == GL_POOL_POWER && !(a.param >= 1.f)) return GL_ERR_SHAPE;
-  if (a.winners && a.ldwin < a.g1 - a.g0) return GL_ERR_SHAPE;
+  if (a.winners && a.ldwin < (a.g1 - a.g0) * (a.pool == GL_POOL_TOPK ? a.k : 1)) return GL_ERR_SHAPE;
   if (a.stat && a.ldstat < a.g1 - a.g0) return GL_ERR_SHAPE;
   int optin = 0, sms = 0;
   int rc = device_smem_optin(&optin);
@@ -330,12 +403,16 @@ extern "C" int gl_fwd_f32(const GlFwdArgs* args, void* stream) {
   const int64_t rows = local ? a.fcap : a.D;
   int T = a.tokens;
   if (T == 0) {
-    T = pick_fwd_tokens(rows, optin, local ? 32 : 8);
+    T = pick_fwd_tokens(rows, optin, local ? 32 : (a.pool == GL_POOL_TOPK ? 4 : 8));
     if (T < 0) return T;
   } else if (T != 1 && T != 2 && T != 4 && T != 8 && T != 16 && T != 32) {
     return GL_ERR_UNSUPPORTED;
   }
-  if (rows * T * 4 + kFwdStaticSmem > optin) return GL_ERR_SMEM;
+  if ((int64_t)fwd_smem(rows, T, a.pool, a.k) + kFwdStaticSmem > optin) {
+    if (a.tokens != 0) return GL_ERR_SMEM;
+    while (T > 1 && (int64_t)fwd_smem(rows, T, a.pool, a.k) + kFwdStaticSmem > optin) T >>= 1;
+    if ((int64_t)fwd_smem(rows, T, a.pool, a.k) + kFwdStaticSmem > optin) return GL_ERR_SMEM;
+  }
   const int64_t G = a.g1 - a.g0;
   int gpc = local ? 1 : a.groups_per_cta;
   if (gpc <= 0) {

@@ -22,11 +22,14 @@
 namespace gl {
 
 // PK (the pooling state, common.cuh): PK_MAX writes the winning slot (smallest on ties) to
-// p.winners; PK_LSE / PK_POW hold three-word states (their tiles stay at 8 tokens or fewer).
+// p.winners; PK_LSE / PK_POW hold three-word states (their tiles stay at 8 tokens or fewer);
+// PK_TOPK / PK_TOPK64 keep per-warp lists (tiles of 4 tokens or fewer) merged per group.
 template <int T, int ACT, bool PACKED, int PK>
 __global__ void __launch_bounds__(kMbFwdThreads, 1) mb_fwd_kernel(const MbParams p) {
   constexpr bool MAXP = PK == PK_MAX;
   constexpr bool SM = PK == PK_LSE || PK == PK_POW;
+  constexpr bool TK = PK == PK_TOPK || PK == PK_TOPK64;
+  constexpr int KW = PK == PK_TOPK64 ? 2 : 1;
   constexpr int NW = kMbFwdThreads / 32;
   constexpr int TS = T < 8 ? T : 8;  // tokens per sub-chunk (registers per lane stay fixed as T grows)
   extern __shared__ __align__(16) float xs[];
@@ -44,10 +47,20 @@ __global__ void __launch_bounds__(kMbFwdThreads, 1) mb_fwd_kernel(const MbParams
   const int slots = (int)(p.NB * C);
   const int64_t gb = p.g0 + (int64_t)blockIdx.y * p.gpc;
   const int64_t ge = gb + p.gpc < p.g1 ? gb + p.gpc : p.g1;
+  long long* tks = reinterpret_cast<long long*>(xs + (((int64_t)p.D * XLD + 3) & ~3LL));  // top-K lists
   for (int64_t g = gb; g < ge; ++g) {
     const int ng = min(p.counts[g], slots);
     const int nbv = (ng + C - 1) / C;
     const int buf = (int)((g - gb) & 1);
+    long long tkw[TK ? T : 1][KW], tthr[TK ? T : 1];
+    if constexpr (TK) {
+#pragma unroll
+      for (int t = 0; t < T; ++t) {
+        tthr[t] = LLONG_MIN;
+#pragma unroll
+        for (int wd = 0; wd < KW; ++wd) tkw[t][wd] = LLONG_MIN;
+      }
+    }
     float acc[T];
     int wid[MAXP ? T : 1];
     float st1[SM ? T : 1], st2[SM ? T : 1];
@@ -81,9 +94,17 @@ __global__ void __launch_bounds__(kMbFwdThreads, 1) mb_fwd_kernel(const MbParams
 #pragma unroll
             for (int t = 0; t < TS; ++t) z[n][t] = fmaf(w[n][k], v[t], z[n][t]);
         }
+        if constexpr (TK) {  // every lane takes part in the warp's insertions
+#pragma unroll
+          for (int n = 0; n < 4; ++n)
+#pragma unroll
+            for (int t = 0; t < TS; ++t)
+              topk_offer<KW>(tkw[tc + t], tthr[tc + t], n < nv, topk_key(z[n][t], j * C + nq * 4 + n), p.pp.k,
+                             lane);
+        }
 #pragma unroll
         for (int n = 0; n < 4; ++n)
-          if (n < nv)
+          if (n < nv && !TK)
 #pragma unroll
             for (int t = 0; t < TS; ++t) {
               const float a = act_f<ACT>(z[n][t]);
@@ -103,6 +124,45 @@ __global__ void __launch_bounds__(kMbFwdThreads, 1) mb_fwd_kernel(const MbParams
             }
       }
     }
+    if constexpr (TK) {
+      // merge the warps' lists: warp t takes token t
+#pragma unroll
+      for (int t = 0; t < T; ++t)
+#pragma unroll
+        for (int wd = 0; wd < KW; ++wd) tks[((warp * T + t) * KW + wd) * 32 + lane] = tkw[t][wd];
+      __syncthreads();
+      if (warp < T) {
+        const int t = warp;
+        long long wl[KW];
+#pragma unroll
+        for (int wd = 0; wd < KW; ++wd) wl[wd] = tks[(t * KW + wd) * 32 + lane];
+        long long thr = topk_last<KW>(wl, p.pp.k);
+        for (int i = 1; i < NW; ++i)
+#pragma unroll
+          for (int wd = 0; wd < KW; ++wd) {
+            const long long c = tks[((i * T + t) * KW + wd) * 32 + lane];
+            topk_offer<KW>(wl, thr, c != LLONG_MIN, c, p.pp.k, lane);
+          }
+        const int kk = min(p.pp.k, ng);
+        float sum = 0.f;
+#pragma unroll
+        for (int wd = 0; wd < KW; ++wd)
+          if (wd * 32 + lane < kk) sum += act_f<ACT>(topk_value(wl[wd]));
+#pragma unroll
+        for (int off = 16; off; off >>= 1) sum += __shfl_xor_sync(kFullMask, sum, off);
+        if (t0 + t < p.B) {
+          if (lane == 0) p.pre[(int64_t)(t0 + t) * p.ldp + (g - p.g0)] = sum / (float)kk;
+          if (p.winners != nullptr)
+#pragma unroll
+            for (int wd = 0; wd < KW; ++wd) {
+              const int pos = wd * 32 + lane;
+              if (pos < p.pp.k)
+                p.winners[(int64_t)(t0 + t) * p.ldwin + (g - p.g0) * p.pp.k + pos] = pos < kk ? topk_slot(wl[wd]) : -1;
+            }
+        }
+      }
+      __syncthreads();
+    } else {
 #pragma unroll
     for (int off = 16; off; off >>= 1)
 #pragma unroll
@@ -176,12 +236,20 @@ __global__ void __launch_bounds__(kMbFwdThreads, 1) mb_fwd_kernel(const MbParams
     }
     // no second barrier: the next group writes the other buffer, and a warp can write this one
     // again only after the next group's barrier, which the reducing threads reach after reading it
+    }
   }
+}
+
+// Dynamic shared memory of the forward: the padded x tile, plus the top-K lists.
+static int64_t mb_fwd_smem(int64_t D, int T, int pool, int k) {
+  const int64_t tile = mb_smem_bytes(D, T, false);
+  if (pool != GL_POOL_TOPK) return tile;
+  return ((tile + 15) & ~15LL) + (int64_t)(kMbFwdThreads / 32) * T * (k > 32 ? 64 : 32) * 8;
 }
 
 template <int T, int ACT, bool PACKED, int PK>
 static int mb_fwd_launch(const MbParams& p, cudaStream_t st) {
-  const size_t smem = (size_t)mb_smem_bytes(p.D, T, false);
+  const size_t smem = (size_t)mb_fwd_smem(p.D, T, p.pool, p.pp.k);
   const void* kern = (const void*)mb_fwd_kernel<T, ACT, PACKED, PK>;
   int rc = ensure_dynamic_smem(kern, smem);
   if (rc) return rc;
@@ -197,8 +265,14 @@ static int mb_fwd_launch(const MbParams& p, cudaStream_t st) {
 
 template <int T, int ACT, bool PACKED>
 static int mb_fwd_pk(const MbParams& p, cudaStream_t st) {
-  switch (pool_kind(p.pool)) {
+  switch (pool_kind(p.pool, p.pp.k)) {
     case PK_MAX: return mb_fwd_launch<T, ACT, PACKED, PK_MAX>(p, st);
+    case PK_TOPK:
+      if constexpr (T > 4) return GL_ERR_UNSUPPORTED;
+      else return mb_fwd_launch<T, ACT, PACKED, PK_TOPK>(p, st);
+    case PK_TOPK64:
+      if constexpr (T > 4) return GL_ERR_UNSUPPORTED;
+      else return mb_fwd_launch<T, ACT, PACKED, PK_TOPK64>(p, st);
     case PK_LSE:
       if constexpr (T > 8) return GL_ERR_UNSUPPORTED;
       else return mb_fwd_launch<T, ACT, PACKED, PK_LSE>(p, st);
@@ -241,12 +315,14 @@ static int mb_run(const GlSharedArgs& a, bool bwd, void* stream) {
   if (!a.x || !a.idx || !a.w || !a.b || !a.counts) return GL_ERR_NULL;
   if (a.B > 2147483647LL || a.ldx < a.D || a.NB * a.C > 2147483647LL) return GL_ERR_SHAPE;
   if (((uintptr_t)a.idx & 15) || ((uintptr_t)a.w & 15) || ((uintptr_t)a.b & 15)) return GL_ERR_ALIGN;
-  if (a.pool < GL_POOL_MEAN || a.pool > GL_POOL_SOFTMAX || (a.pool == GL_POOL_MAX && bwd)) return GL_ERR_UNSUPPORTED;
+  if (a.pool < GL_POOL_MEAN || a.pool > GL_POOL_TOPK || ((a.pool == GL_POOL_MAX || a.pool == GL_POOL_TOPK) && bwd))
+    return GL_ERR_UNSUPPORTED;
+  if (a.pool == GL_POOL_TOPK && !topk_k_ok(a.k)) return GL_ERR_SHAPE;
   const bool smooth = a.pool >= GL_POOL_LME;
   if ((a.pool == GL_POOL_LME || a.pool == GL_POOL_SOFTMAX) && !(a.param > 0.f)) return GL_ERR_SHAPE;
   if (a.pool == GL_POOL_POWER && !(a.param >= 1.f)) return GL_ERR_SHAPE;
   if (bwd && smooth && (!a.c2 || (a.pool == GL_POOL_SOFTMAX && !a.c3))) return GL_ERR_NULL;
-  if (a.winners && a.ldwin < a.g1 - a.g0) return GL_ERR_SHAPE;
+  if (a.winners && a.ldwin < (a.g1 - a.g0) * (a.pool == GL_POOL_TOPK ? a.k : 1)) return GL_ERR_SHAPE;
   if (a.stat && a.ldstat < a.g1 - a.g0) return GL_ERR_SHAPE;
   if (!bwd) {
     if (!a.pre) return GL_ERR_NULL;
@@ -265,10 +341,15 @@ static int mb_run(const GlSharedArgs& a, bool bwd, void* stream) {
     T = mb_pick_tokens(a.D, bwd, optin);
     if (T < 0) return T;
     if (!bwd && smooth && T > 8) T = 8;  // three-word states per token in registers
+    if (!bwd && a.pool == GL_POOL_TOPK && T > 4) T = 4;  // top-K lists per token in registers
   } else if (T != 1 && T != 2 && T != 4 && T != 8 && T != 16 && T != 32) {
     return GL_ERR_UNSUPPORTED;
   }
   if (mb_smem_bytes(a.D, T, bwd) + kMbStaticSmem > optin) return GL_ERR_SMEM;
+  if (!bwd && a.pool == GL_POOL_TOPK) {
+    while (T > 1 && mb_fwd_smem(a.D, T, a.pool, a.k) + kMbStaticSmem > optin) T >>= 1;
+    if (mb_fwd_smem(a.D, T, a.pool, a.k) + kMbStaticSmem > optin) return GL_ERR_SMEM;
+  }
   const int64_t G = a.g1 - a.g0;
   int gpc = a.groups_per_cta;
   if (gpc <= 0) {
@@ -285,7 +366,7 @@ static int mb_run(const GlSharedArgs& a, bool bwd, void* stream) {
   p.NB = a.NB; p.g0 = a.g0; p.g1 = a.g1; p.ldx = a.ldx; p.ldp = a.ldp; p.ldg = a.ldg; p.lddx = a.lddx;
   p.pool = a.pool; p.gpc = gpc; p.winners = a.winners; p.ldwin = a.ldwin;
   p.stat = a.stat; p.ldstat = a.ldstat; p.c2 = a.c2; p.c3 = a.c3;
-  p.pp = PoolParam{a.param, pow_code(a.param), a.pool == GL_POOL_SOFTMAX};
+  p.pp = PoolParam{a.param, pow_code(a.param), a.pool == GL_POOL_SOFTMAX, a.k};
   p.ipm1 = pow_code(a.param) >= 1 ? pow_code(a.param) - 1 : -1;
   cudaStream_t st = (cudaStream_t)stream;
   const bool packed = a.packed != 0;

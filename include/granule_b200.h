@@ -44,7 +44,7 @@
 extern "C" {
 #endif
 
-#define GL_ABI_VERSION 8
+#define GL_ABI_VERSION 9
 
 typedef enum GlStatus {
   GL_OK = 0,
@@ -68,6 +68,10 @@ typedef enum GlStatus {
      POWER    pre = (sum a^p / n)^(1/p), a = relu(z) >= 0; param = p >= 1   (:86-92)
      SOFTMAX  pre = sum a e^(beta a) / sum e^(beta a); param = log2(e) * beta;
               stat = L2 = log2 sum 2^(a * param)        (:93-98)
+     TOPK     pre = sum of act(z) over the k slots with the largest z (ties: the smaller slot)
+              / min(k, n); k a power of two <= 64; `winners` [B, ldwin >= (g1-g0) k] receives
+              the slots, largest first, -1 past min(k, n) (:66-77); backward:
+              gl_bwd_events_f32 with k events per (token, group)
    The smooth pools' backward is gl_bwd_f32 / gl_bwd_shared_f32 with the reference's
    per-(token, group) coefficients (kernels/ops.py:242-262): dz = c1 * h * act'(z) with
      MEAN/SUM h = 1 (c1 = gpre / n for MEAN, computed by the kernel; gpre for SUM)
@@ -75,7 +79,8 @@ typedef enum GlStatus {
      POWER    h = (a * c2)^(p - 1), 0 where z <= 0    c1 = gpre / n (0 where pre = 0), c2 = 1 / pre
      SOFTMAX  h = 2^(a * param - c2) (1 + beta (a - c3)), beta = param * ln 2
                                                       c1 = gpre, c2 = L2, c3 = pre */
-enum { GL_POOL_MEAN = 0, GL_POOL_SUM = 1, GL_POOL_MAX = 2, GL_POOL_LME = 3, GL_POOL_POWER = 4, GL_POOL_SOFTMAX = 5 };
+enum { GL_POOL_MEAN = 0, GL_POOL_SUM = 1, GL_POOL_MAX = 2, GL_POOL_LME = 3, GL_POOL_POWER = 4, GL_POOL_SOFTMAX = 5,
+       GL_POOL_TOPK = 6 };
 enum { GL_ACT_IDENTITY = 0, GL_ACT_RELU = 1, GL_ACT_GELU = 2 };
 
 /* Forward: pre[t, g - g0] = pool_{valid s of g} act(z[t, g, s]),
@@ -109,7 +114,7 @@ typedef struct GlFwdArgs {
   float* stat;              /* GL_POOL_LME / SOFTMAX: optional [B, ldstat] output, the log2-normaliser L2 */
   int64_t ldstat;
   float param;              /* the pool's parameter (see the pool ids); unused otherwise */
-  int32_t reserved2;        /* 0 */
+  int32_t k;                /* GL_POOL_TOPK: the number of slots kept; unused otherwise */
 } GlFwdArgs;
 
 /* Backward: with c1[t, g] = gpre[t, g - g0] / counts[g] (mean) or gpre (the other pools) and
@@ -243,7 +248,7 @@ typedef struct GlSharedArgs {
   const float* c2;          /* backward, smooth pools: [B, ldg] coefficients c2, c3 */
   const float* c3;
   float param;              /* the pool's parameter */
-  int32_t reserved2;        /* 0 */
+  int32_t k;                /* forward, GL_POOL_TOPK: the number of slots kept */
 } GlSharedArgs;
 
 int gl_fwd_shared_f32(const GlSharedArgs* args, void* stream);
@@ -251,9 +256,10 @@ int gl_bwd_shared_f32(const GlSharedArgs* args, void* stream);
 /* Token tile the automatic choice would use for input_dim D, or a negative status. */
 int gl_shared_auto_tokens(int64_t D, int32_t backward);
 
-/* Winner-event backward of max pooling, Mode A or Mode B (replaces kernels/triton_fused.py:476-520
- * bwd_events_kernel, launched by kernels/ops.py:281-293).  For each (t, g) in [0, B) x [g0, g1),
- * with s = winners[t, g-g0] (the slot the forward's max chose) and c = coef[t, g-g0] (dL/dpre):
+/* Winner-event backward of max and top-K pooling, Mode A or Mode B (replaces
+ * kernels/triton_fused.py:476-520 bwd_events_kernel, launched by kernels/ops.py:281-293).  For each
+ * (t, g, j) in [0, B) x [g0, g1) x [0, kev), with s = winners[t, (g-g0) kev + j] (a slot the
+ * forward's max or top-K chose) and c = coef[t, g-g0] (dL/dpre, divided by min(k, n) for top-K):
  *   dz = c * act'(z[t, g, s]); db[s] += dz; dw[s][k] += dz * x[t, idx_k]; dx[t, idx_k] += dz * w[s][k]
  * Events with s < 0 or c == 0 are skipped.  Storage as in GlBwdArgs (Mode A) or GlSharedArgs (Mode B:
  * shared = 1, C, packed); dx, dw, db are accumulated. */
@@ -273,7 +279,7 @@ typedef struct GlEventArgs {
   int32_t shared;           /* 0 = Mode A, 1 = Mode B */
   int32_t packed;           /* Mode B storage: 0 = canonical, 1 = fragment-packed */
   int32_t act;              /* GL_ACT_* */
-  int32_t reserved;         /* 0 */
+  int32_t kev;              /* events per (token, group): 1 (max; 0 reads as 1) or the top-K k */
 } GlEventArgs;
 
 int gl_bwd_events_f32(const GlEventArgs* args, void* stream);

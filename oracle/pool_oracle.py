@@ -9,10 +9,13 @@ expansion): pytorch_reference.py:29-48 (pre-activations) and :51-98 (``pool``):
 * logmeanexp: tau (logsumexp(a / tau) - log n); dz = dy softmax(a / tau) act'(z);
 * softmax_weighted: sum softmax(beta a) a; dz = dy p (1 + beta (a - y)) act'(z);
 * power_mean (a = relu(z)): max-scaled (mean a^p)^(1/p); dz = dy a^(p-1) y^(1-p) / n for z > 0,
-  the derivatives the reference's dense backward uses (kernels/triton_fused.py:365-399).
+  the derivatives the reference's dense backward uses (kernels/triton_fused.py:365-399);
+* topk_mean: the k valid slots with the largest z (a stable descending sort: ties keep the
+  smaller slot), pre = sum act(z) / min(k, n); dz = dy act'(z) / min(k, n) on those slots
+  (pytorch_reference.py:66-77).
 
 Pinned by tests/test_oracle_golden.py to fixtures made by the reference itself
-(tests/golden/fwdbwd_max_*.npz, fwdbwd_smooth_*.npz).  Materialises z [B, G, slots]: small cases
+(tests/golden/fwdbwd_max_*.npz, fwdbwd_smooth_*.npz, fwdbwd_topk_*.npz).  Materialises z [B, G, slots]: small cases
 only.
 """
 from __future__ import annotations
@@ -130,4 +133,38 @@ def smooth_backward(x, idx, w, b, counts, gy, kind, act, tau=1.0, beta=1.0, p=2.
     contrib = dz[..., None] * wv[None]                               # [B, G, slots, 8]
     tt = np.broadcast_to(np.arange(B)[:, None, None, None], contrib.shape)
     np.add.at(dx, (tt.reshape(-1), np.broadcast_to(i[None], contrib.shape).reshape(-1)), contrib.reshape(-1))
+    return dx, dw.reshape(np.asarray(w).shape), db.reshape(np.asarray(b).shape)
+
+
+def topk_forward(x, idx, w, b, counts, k, act="identity"):
+    """(y [B, G], slots [B, G, k] with -1 past min(k, n)) of the top-K mean operator."""
+    z, _, i, _ = _z(x, idx, w, b)
+    valid = _valid(i, counts)[None]
+    zm = np.where(valid, z, -np.inf)
+    order = np.argsort(-zm, axis=-1, kind="stable")[..., :k]
+    n = np.asarray(counts).reshape(1, -1, 1)
+    kk = np.minimum(n, k)
+    sel = np.arange(order.shape[-1])[None, None, :] < kk
+    a = np.take_along_axis(_act(z, act), order, -1)
+    y = np.where(sel, a, 0.0).sum(-1) / kk[..., 0]
+    return y, np.where(sel, order, -1)
+
+
+def topk_backward(x, idx, w, b, counts, gy, k, act="identity", slots=None):
+    """(dx, dw, db) float64 of the top-K mean operator for upstream gy [B, G]."""
+    z, xg, i, wv = _z(x, idx, w, b)
+    if slots is None:
+        slots = topk_forward(x, idx, w, b, counts, k, act)[1]
+    B, G, K = slots.shape
+    t, g, j = np.nonzero(slots >= 0)
+    s = slots[t, g, j]
+    kk = np.minimum(np.asarray(counts), k).astype(np.float64)
+    dz = np.asarray(gy, np.float64)[t, g] / kk[g] * _dact(z[t, g, s], act)
+    dx = np.zeros(np.asarray(x).shape)
+    dw = np.zeros_like(wv)
+    db = np.zeros(wv.shape[:2])
+    np.add.at(db, (g, s), dz)
+    np.add.at(dw, (g, s), dz[:, None] * xg[t, g, s])
+    for q in range(8):
+        np.add.at(dx, (t, i[g, s, q]), dz * wv[g, s, q])
     return dx, dw.reshape(np.asarray(w).shape), db.reshape(np.asarray(b).shape)

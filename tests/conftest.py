@@ -61,12 +61,18 @@ def load_case(name):
 def case_names():
     """Mode-A golden cases."""
     return sorted(p.stem[len("fwdbwd_"):] for p in GOLDEN.glob("fwdbwd_*.npz")
-                  if not p.stem.startswith(("fwdbwd_modeb_", "fwdbwd_max_", "fwdbwd_smooth_", "fwdbwd_semantic_")))
+                  if not p.stem.startswith(("fwdbwd_modeb_", "fwdbwd_max_", "fwdbwd_smooth_", "fwdbwd_semantic_",
+                                             "fwdbwd_topk_")))
 
 
 def max_case_names():
     """Max-pooling golden cases (Mode A and Mode B)."""
     return sorted(p.stem[len("fwdbwd_"):] for p in GOLDEN.glob("fwdbwd_max_*.npz"))
+
+
+def topk_case_names():
+    """Top-K mean golden cases (Mode A and Mode B)."""
+    return sorted(p.stem[len("fwdbwd_"):] for p in GOLDEN.glob("fwdbwd_topk_*.npz"))
 
 
 def smooth_case_names():

@@ -27,6 +27,8 @@ What it writes (all from the reference's own code on the CPU):
   plus the winner slots.
 * ``fwdbwd_smooth_<case>.npz`` — LogMeanExp, power-mean and softmax-weighted pooling (Mode A
   and Mode B) with the reference's float64 ``reference_forward`` and autograd gradients.
+* ``fwdbwd_topk_<case>.npz`` — top-K mean pooling (Mode A and Mode B) with the reference's float64
+  ``reference_forward``, its selected slots and autograd gradients.
 * ``fwdbwd_semantic_<case>.npz`` — two-level (semantic) pooling: level-1 shards, transform and
   level-2 operator, with the reference's float64 ``reference_forward`` and autograd gradients,
   including the transform / weighted-sum parameters' gradients.
@@ -94,6 +96,16 @@ SMOOTH_CASES = [
     ("softmax_modeb_c16_gelu", 300, 5000, 3, 16, False, 19, 27, 0.2, "softmax_weighted", {"beta": 0.7}, "gelu"),
 ]
 
+# Top-K mean: (name, D, H, G, C (None = Mode A), packed, B, seed, bias_std, k, activation)
+TOPK_CASES = [
+    ("modea_k8", 128, 6000, 12, None, False, 23, 41, 0.2, 8, "identity"),
+    ("modea_k64_gelu", 96, 1001, 7, None, False, 9, 42, 0.1, 64, "gelu"),
+    ("modea_k1_ragged", 64, 1003, 9, None, False, 5, 45, 0.3, 1, "relu"),
+    ("modea_k16_small_groups", 64, 100, 9, None, False, 7, 46, 0.2, 16, "identity"),
+    ("modeb_c8_packed_k4", 256, 7000, 5, 8, True, 17, 43, 0.2, 4, "relu"),
+    ("modeb_c64_k32", 512, 20000, 3, 64, False, 11, 44, 0.2, 32, "identity"),
+]
+
 # Two-level pooling: (name, D, H, G, C (None = Mode A), packed, B, seed, bias_std, level 1, level 2,
 # level1_checkpoint)
 SEMANTIC_CASES = [
@@ -141,7 +153,7 @@ def sha(t: torch.Tensor) -> str:
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="directory that contains the sparse_pooling package")
-    ap.add_argument("--only", choices=["smooth", "semantic"], help="write only this group of fixtures")
+    ap.add_argument("--only", choices=["smooth", "semantic", "topk"], help="write only this group of fixtures")
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
     from sparse_pooling.config import LevelSpec, PoolingConfig
@@ -154,6 +166,9 @@ def main():
         return
     if args.only == "semantic":
         semantic_fixtures(ref, LevelSpec, PoolingConfig, SparseLayout, init_parameters)
+        return
+    if args.only == "topk":
+        topk_fixtures(ref, LevelSpec, PoolingConfig, SparseLayout, init_parameters)
         return
     hashes = []
     for D, H, G, C, shared, packed, seed, bstd, chunk in INIT_CASES:
@@ -254,6 +269,7 @@ def main():
 
     smooth_fixtures(ref, LevelSpec, PoolingConfig, SparseLayout, init_parameters)
     semantic_fixtures(ref, LevelSpec, PoolingConfig, SparseLayout, init_parameters)
+    topk_fixtures(ref, LevelSpec, PoolingConfig, SparseLayout, init_parameters)
 
     # input-supergroup graphs (supergroups.py generate_indices; kgen_graph.py generate)
     from sparse_pooling.experimental import kgen_graph as KG
@@ -374,6 +390,29 @@ def semantic_fixtures(ref, LevelSpec, PoolingConfig, SparseLayout, init_paramete
                                  idx_sha=sha(idx), w_sha=sha(w), b_sha=sha(b))),
             x=x.numpy(), dy=dy.numpy(), y=y.detach().float().numpy(), dx=xd.grad.float().numpy(),
             dw=wd.grad[:GSUB].float().numpy(), db=bd.grad[:GSUB].float().numpy(), **extra)
+
+
+def topk_fixtures(ref, LevelSpec, PoolingConfig, SparseLayout, init_parameters):
+    for name, D, H, G, C, packed, B, seed, bstd, k, act in TOPK_CASES:
+        L = SparseLayout(D, H, G, 8, C or 8, C is not None, packed=packed)
+        idx, w, b = init_parameters(L, "cpu", dtype=torch.float32, seed=seed, bias_std=bstd)
+        gen = torch.Generator().manual_seed(6000 + seed)
+        x = torch.randn(B, D, generator=gen)
+        xd = x.double().requires_grad_(True)
+        wd = w.double().requires_grad_(True)
+        bd = b.double().requires_grad_(True)
+        extra = {}
+        y = ref.reference_forward(xd, idx, wd, bd, L, PoolingConfig([LevelSpec("topk_mean", activation=act, k=k)]),
+                                  extra=extra)
+        dy = torch.randn(y.shape, generator=gen)
+        (y * dy.double()).sum().backward()
+        np.savez_compressed(
+            HERE / f"fwdbwd_topk_{name}.npz",
+            meta=json.dumps(dict(name=name, D=D, H=H, G=G, C=C, packed=packed, B=B, seed=seed, bias_std=bstd,
+                                 pool="topk_mean", k=k, act=act, rule="distinct", mode="A" if C is None else "B",
+                                 idx_sha=sha(idx), w_sha=sha(w), b_sha=sha(b))),
+            x=x.numpy(), dy=dy.numpy(), y=y.detach().float().numpy(), topk=extra["topk"].to(torch.int32).numpy(),
+            dx=xd.grad.float().numpy(), dw=wd.grad[:GSUB].float().numpy(), db=bd.grad[:GSUB].float().numpy())
 
 
 if __name__ == "__main__":

@@ -37,7 +37,7 @@ def test_mode_b_cpu_forward_has_no_fallback(kw):
         lay(torch.randn(2, 64))
 
 
-@pytest.mark.parametrize("kw", [dict(pooling="topk_mean"), dict(dtype=torch.bfloat16),
+@pytest.mark.parametrize("kw", [dict(dtype=torch.bfloat16),
                                 # 3 shards of 20 blocks do not tile the 48 stored blocks of a group
                                 dict(pooling={"levels": [{"type": "mean", "neurons_per_shard": 160},
                                                          {"type": "weighted_sum"}]})])

@@ -6,7 +6,7 @@ import pytest
 import torch
 
 from conftest import (GOLDEN, assert_close, case_names, case_params, load_case, max_case_names, max_case_params,
-                      oracle_params, smooth_case_names,
+                      oracle_params, smooth_case_names, topk_case_names,
                       modeb_as_mode_a, modeb_case_names, modeb_case_params)
 from oracle import oracle as O
 
@@ -127,6 +127,36 @@ def test_smooth_oracle_matches_reference(name):
     assert_close(y, arr["y"], 2e-6, 1e-7, "y")
     dx, dw, db = P.smooth_backward(arr["x"], ia.numpy(), wa.numpy(), ba.numpy(), counts, arr["dy"], meta["pool"],
                                    meta["act"], **kw)
+    assert_close(dx, arr["dx"], 2e-6, 1e-7, "dx")
+    dwc = torch.from_numpy(dw).reshape(L.groups, L.blocks_per_group, L.block, 8)
+    dbc = torch.from_numpy(db).reshape(L.groups, L.blocks_per_group, L.block)
+    if L.packed:
+        dwc, dbc = L.pack_weights(dwc), L.pack_bias(dbc)
+    gs = arr["dw"].shape[0]
+    assert_close(dwc[:gs], arr["dw"], 2e-6, 1e-7, "dw")
+    assert_close(dbc[:gs], arr["db"], 2e-6, 1e-7, "db")
+
+
+@pytest.mark.parametrize("name", topk_case_names())
+def test_topk_oracle_matches_reference(name):
+    """Top-K mean: the float64 oracle reproduces the reference's outputs, selected slots and
+    gradients."""
+    from oracle import pool_oracle as P
+
+    meta, arr = load_case(name)
+    L, idx, w, b = max_case_params(meta)
+    if L.shared_indices:
+        ia, wa, ba = modeb_as_mode_a(L, idx, w, b)
+    else:
+        ia, wa, ba = idx, w, b
+    counts = L.counts_tensor("cpu").numpy()
+    y, slots = P.topk_forward(arr["x"], ia.numpy(), wa.numpy(), ba.numpy(), counts, meta["k"], meta["act"])
+    kk = np.minimum(counts, meta["k"])
+    live = np.arange(meta["k"])[None, None, :] < kk[None, :, None]
+    assert np.array_equal(np.where(live, slots, -1), np.where(live, arr["topk"], -1))
+    assert_close(y, arr["y"], 2e-6, 1e-7, "y")
+    dx, dw, db = P.topk_backward(arr["x"], ia.numpy(), wa.numpy(), ba.numpy(), counts, arr["dy"], meta["k"],
+                                 meta["act"])
     assert_close(dx, arr["dx"], 2e-6, 1e-7, "dx")
     dwc = torch.from_numpy(dw).reshape(L.groups, L.blocks_per_group, L.block, 8)
     dbc = torch.from_numpy(db).reshape(L.groups, L.blocks_per_group, L.block)
