@@ -27,7 +27,8 @@ EXPORTS = ("gl_abi_version", "gl_status_string", "gl_last_cuda_error", "gl_fwd_f
            "gl_adam_f32", "gl_group_absmax_f32", "gl_group_index_maxcount", "gl_group_feature_map",
            "gl_group_order", "gl_launch_count",
            "gl_fwd_auto_tokens", "gl_bwd_auto_tokens", "gl_fwd_shared_f32", "gl_bwd_shared_f32", "gl_bwd_events_f32",
-           "gl_shared_auto_tokens", "gl_k16_fwd_f32", "gl_k16_bwd_f32", "gl_k16_auto_tokens")
+           "gl_shared_auto_tokens", "gl_bwd_shared_det_f32", "gl_k16_fwd_f32", "gl_k16_bwd_f32",
+           "gl_k16_auto_tokens")
 
 
 class NativeLibraryError(RuntimeError):
@@ -143,6 +144,9 @@ def load(path=None) -> ctypes.CDLL:
                                        ctypes.c_void_p]
         lib.gl_shared_auto_tokens.restype = ctypes.c_int
         lib.gl_shared_auto_tokens.argtypes = [ctypes.c_int64, ctypes.c_int32]
+        lib.gl_bwd_shared_det_f32.argtypes = [ctypes.POINTER(GlSharedArgs), ctypes.c_void_p, ctypes.c_void_p,
+                                              ctypes.c_void_p, ctypes.c_void_p]
+        lib.gl_bwd_shared_det_f32.restype = ctypes.c_int
         lib.gl_k16_auto_tokens.restype = ctypes.c_int
         lib.gl_k16_auto_tokens.argtypes = [ctypes.c_int64, ctypes.c_int64, ctypes.c_int32]
         if path is None:
@@ -258,6 +262,23 @@ def bwd_shared(x, idx, w, b, counts, gpre, dx, dw, db, NB: int, C: int, g0: int,
     a.c2, a.c3, a.param = _ptr(c2), _ptr(c3), float(param)
     with torch.cuda.device(x.device):
         _check(lib, lib.gl_bwd_shared_f32(ctypes.byref(a), _stream(x.device)), "gl_bwd_shared_f32")
+
+
+def bwd_shared_det(x, idx, w, b, counts, gpre, dx, dw, db, NB: int, C: int, g0: int, g1: int, pool: int, act: int,
+                   packed: bool, dxq, qscale, qinv):
+    """Deterministic Mode-B backward (gl_bwd_shared_det_f32): dx, dw, db += the mean / sum gradients,
+    bitwise repeatable; ``dxq`` a zeroed int64 [B, D] buffer, ``qscale`` / ``qinv`` [B] the per-token
+    fixed-point scales 2^e and 2^-e."""
+    _require_cuda(x, idx, w, b, counts, gpre, dx, dw, db, dxq, qscale, qinv)
+    if dxq.dtype != torch.int64 or not dxq.is_contiguous() or tuple(dxq.shape) != tuple(x.shape):
+        raise ValueError("dxq must be a contiguous int64 tensor shaped like x")
+    lib = load()
+    a = _shared_args(x, idx, w, b, counts, NB, C, g0, g1, pool, act, packed, 0, 0)
+    a.gpre, a.dx, a.dw, a.db = _ptr(gpre), _ptr(dx), _ptr(dw), _ptr(db)
+    a.ldg, a.lddx = gpre.stride(0), dx.stride(0)
+    with torch.cuda.device(x.device):
+        _check(lib, lib.gl_bwd_shared_det_f32(ctypes.byref(a), _ptr(dxq), _ptr(qscale), _ptr(qinv),
+                                              _stream(x.device)), "gl_bwd_shared_det_f32")
 
 
 def bwd_events(x, idx, w, b, winners, coef, dx, dw, db, NB: int, C: int, shared: bool, packed: bool, g0: int,

@@ -202,20 +202,49 @@ class Level1Runtime:
                 raise ValueError(f"tensor on {t.device} but the layer's parameters are on {dev} "
                                  "(move the input or the layer)")
 
+    def deterministic_reason(self) -> Optional[str]:
+        """Why reduction='deterministic' is unavailable for this layer, or None.  The deterministic
+        backward covers Mode-B layers with the mean / sum pools (the reference's deterministic path
+        covers packed Mode-B Mean layers, README "Deterministic execution").  The forwards and Adam
+        already sum in a fixed order; the Mode-A, event (max / top-K) and smooth-pool backwards use
+        FP32 atomics."""
+        if not self.layout.shared_indices:
+            return "Mode-A layers accumulate dX with FP32 atomics"
+        if self.pool not in (_native.POOL_MEAN, _native.POOL_SUM):
+            return f"the deterministic backward covers the mean / sum pools, not {self.level.type}"
+        return None
+
     def resolve_reduction(self, B: int) -> bool:
         mode, why, strict = resolve_reduction(self.plan)
         if mode == "deterministic":
-            msg = (f"reduction='deterministic' ({why}) is unsupported by the B200 kernels: "
-                   "dX is flushed with FP32 atomics")
-            if strict:
-                raise ValueError(msg)
-            import warnings
+            reason = self.deterministic_reason()
+            if reason is not None:
+                msg = f"reduction='deterministic' ({why}) is unsupported for this layer: {reason}"
+                if strict:
+                    raise ValueError(msg)
+                import warnings
 
-            warnings.warn(msg + "; running reduction='fast'", stacklevel=4)
-            mode, why = "fast", why + " -> fast (warn_only)"
-        self.det = False
+                warnings.warn(msg + "; running reduction='fast'", stacklevel=4)
+                mode, why = "fast", why + f"; unsupported ({reason}) -> fast (warn_only)"
+        self.det = mode == "deterministic"
         self.last_info["reduction"] = {"mode": mode, "reason": why}
         return self.det
+
+    def det_scales(self, w: torch.Tensor, g_pre: torch.Tensor):
+        """(qscale, qinv) [B]: the per-token power-of-two scales of the deterministic dX accumulation,
+        2^e with sum_d |dx[t, d]| 2^e <= 2^60 by the bound sum_g |c1[t, g]| n_g 8 max|w|_g max|act'|."""
+        G = self.groups
+        wmax = w.reshape(G, -1).abs().amax(1).float()
+        n = self.counts_f32
+        per = 8.0 * wmax * (1.0 if self.pool == _native.POOL_MEAN else n)   # |c1| n_g = |g_pre| for mean
+        dmax = 1.13 if self.level.activation == "gelu" else 1.0
+        bound = (g_pre.abs() * per[None, :]).sum(1) * dmax
+        e = torch.clamp(torch.floor(60.0 - torch.log2(bound)), min=-126.0, max=126.0)
+        finite = torch.isfinite(bound)
+        e = torch.where(finite, e, torch.zeros_like(e))
+        qscale = torch.where(finite, torch.exp2(e), torch.zeros_like(e)).contiguous()
+        qinv = torch.where(finite, torch.exp2(-e), torch.full_like(e, float("nan"))).contiguous()
+        return qscale, qinv
 
     def describe_execution(self, B: int) -> Dict:
         lib = _native.load()
@@ -342,6 +371,16 @@ class Level1Runtime:
                 self.last_info["recomputed_stats"] = True
             c1, c2, c3 = self.coefficients(g_pre, stats)
         dx = torch.zeros((B, D), device=x.device, dtype=torch.float32)
+        if self.layout.shared_indices and self.det and B > 0:
+            qscale, qinv = self.det_scales(w, g_pre)
+            dxq = torch.zeros((B, D), device=x.device, dtype=torch.int64)
+            _native.bwd_shared_det(x, self.idx, w, b, self.counts_i32, g_pre, dx, dw_buf, db_buf,
+                                   self.layout.blocks_per_group, self.layout.block, 0, self.groups, self.pool,
+                                   self.act, self.layout.packed, dxq, qscale, qinv)
+            self.last_info["backward_backend"] = "b200"
+            self.last_info["backward_kernel"] = "gl_bwd_shared_det_f32"
+            self.last_info["dx_accumulation"] = "int64 fixed point per token (deterministic)"
+            return dx
         if self.layout.shared_indices:
             _native.bwd_shared(x, self.idx, w, b, self.counts_i32, c1, dx, dw_buf, db_buf,
                                self.layout.blocks_per_group, self.layout.block, 0, self.groups, self.pool, self.act,

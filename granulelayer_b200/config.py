@@ -296,9 +296,11 @@ class PhysicalPlan:
 def resolve_reduction(plan: PhysicalPlan):
     """(mode, reason, strict) of the plan's reduction policy (config.py:397-421).
 
-    "fast" uses FP32 atomics in the dX flush; "deterministic" is not offered by
-    the B200 kernels yet, so an explicit request raises and the PyTorch global
-    deterministic setting raises unless warn_only is set (then it warns).
+    "fast" uses FP32 atomics in the backward's reductions; "deterministic" runs
+    the bitwise-repeatable backward where the layer has one (Mode B, mean / sum;
+    ``Level1Runtime.deterministic_reason``), and elsewhere an explicit request
+    raises and the PyTorch global deterministic setting raises unless warn_only
+    is set (then it warns).
     """
     import torch
 

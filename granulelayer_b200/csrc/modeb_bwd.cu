@@ -25,42 +25,6 @@
 
 namespace gl {
 
-// v[k] <- v[k ^ km] for the top NBITS bits of k (bit 2 first); km has no other bits set.
-template <int NBITS, typename V>
-__device__ __forceinline__ void mb_xor_perm8(V (&v)[8], int km) {
-#pragma unroll
-  for (int s = 0; s < NBITS; ++s) {
-    const int bit = 2 - s;
-    const bool f = (km >> bit) & 1;
-#pragma unroll
-    for (int i = 0; i < 8; ++i)
-      if (!((i >> bit) & 1)) {
-        const V lo = v[i], hi = v[i | (1 << bit)];
-        v[i] = f ? hi : lo;
-        v[i | (1 << bit)] = f ? lo : hi;
-      }
-  }
-}
-
-// Weights of neurons c0 .. c0+3 of block j with the k index permuted: w[n][k] = W[c0+n][k ^ km].
-template <bool PACKED>
-__device__ __forceinline__ void mb_load_w4_perm(const MbParams& p, int64_t g, int j, int c0, int km,
-                                                float (&w)[4][8]) {
-  const int khm = km >> 1;
-  const bool sw = km & 1;
-  const MbPacked m = mb_packed(p.C, p.NB);
-#pragma unroll
-  for (int n = 0; n < 4; ++n)
-#pragma unroll
-    for (int khp = 0; khp < 4; ++khp) {
-      const int kh = khp ^ khm;
-      const int64_t off = PACKED ? mb_packed_w(m, g, j, c0 + n, kh) : ((g * p.NB + j) * p.C + c0 + n) * 8 + 2 * kh;
-      const float2 v = __ldg(reinterpret_cast<const float2*>(p.w + off));
-      w[n][2 * khp] = sw ? v.y : v.x;
-      w[n][2 * khp + 1] = sw ? v.x : v.y;
-    }
-}
-
 template <int T, int ACT, bool PACKED, int LG>
 __global__ void __launch_bounds__(kMbBwdThreads, 1) mb_bwd_kernel(const MbParams p) {
   constexpr int NW = kMbBwdThreads / 32;

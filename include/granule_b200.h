@@ -256,6 +256,18 @@ int gl_bwd_shared_f32(const GlSharedArgs* args, void* stream);
 /* Token tile the automatic choice would use for input_dim D, or a negative status. */
 int gl_shared_auto_tokens(int64_t D, int32_t backward);
 
+/* Deterministic Mode-B backward (PhysicalPlan.reduction = "deterministic"; replaces the reference's
+ * deterministic reductions, kernels/cuda/sg_det.cu): the same sums as gl_bwd_shared_f32 for the
+ * mean / sum pools, bitwise repeatable.  dW / db have one owner per record that adds the token tiles
+ * in order; dX is accumulated exactly in 64-bit integers: every (token, record, k) sum is rounded to
+ * an integer at the power-of-two scale qscale[t] and added to dxq, a caller-zeroed int64 [B, D]
+ * (row stride D) buffer, and a second kernel adds dxq[t, d] * qinv[t] to dx.  The caller picks
+ * qscale[t] = 2^e_t with sum_d |dx[t, d]| * 2^e_t < 2^61 (a bound: sum_g |c1[t, g]| * n_g * 8 *
+ * max|w|_g * max|act'| * 2^e_t <= 2^60), qinv[t] = 2^-e_t (NaN for a token whose bound is not
+ * finite, which makes its dx NaN). */
+int gl_bwd_shared_det_f32(const GlSharedArgs* args, int64_t* dxq, const float* qscale, const float* qinv,
+                          void* stream);
+
 /* Winner-event backward of max and top-K pooling, Mode A or Mode B (replaces
  * kernels/triton_fused.py:476-520 bwd_events_kernel, launched by kernels/ops.py:281-293).  For each
  * (t, g, j) in [0, B) x [g0, g1) x [0, kev), with s = winners[t, (g-g0) kev + j] (a slot the
