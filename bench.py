@@ -39,7 +39,8 @@ once with the reference's uniform index rule and once with windowed indices (eac
 ``--workload modeb`` times Mode B (C neurons share one index record; the reference's
 production mode and the configuration of its published RTX 3090 table): H = 100,000,000,
 D = G = 1024, B = 8192, Mean(ReLU) and Max (identity, save_winners), fragment-packed storage,
-fwd + bwd + fused Adam (fp32), for C = 8 and C = 64.
+fwd + bwd + fused Adam (fp32), for C = 8 and C = 64, plus Mean(ReLU) with
+``PhysicalPlan(reduction="deterministic")`` (bitwise-repeatable backward).
 
 ``--impl reference`` times the reference's CPU path (the oracle port: the
 reference's materialising PyTorch path does not fit 100M neurons) on the same
@@ -458,7 +459,7 @@ MB_PUBLISHED_MS = {("mean", 8): 4898.4, ("mean", 64): 2360.8,   # RTX 3090, BF16
 
 def bench_modeb(args):
     """Mode-B step at the published table's configuration (module docstring); rank 0 only."""
-    from granulelayer_b200 import FusedAdamW, SparsePoolingLayer, _native
+    from granulelayer_b200 import FusedAdamW, PhysicalPlan, SparsePoolingLayer, _native
 
     Hm, Dm, Gm, Bm = args.modeb_neurons, 1024, 1024, 8192
     dev = torch.device("cuda", 0)
@@ -466,17 +467,18 @@ def bench_modeb(args):
     rows = []
     launches = 0
     with ClockSampler(dev.index) as clk:
-        for pool, C in (("mean", 8), ("mean", 64), ("max", 8), ("max", 64)):
+        for pool, C, red in (("mean", 8, "fast"), ("mean", 64, "fast"), ("max", 8, "fast"), ("max", 64, "fast"),
+                             ("mean", 8, "deterministic"), ("mean", 64, "deterministic")):
             pooling = pool   # the operators' default activations: Mean(ReLU), Max(identity)
             lay = SparsePoolingLayer(Dm, Hm, Gm, shared_neurons=C, pooling=pooling, dtype=torch.float32, device=dev,
-                                     seed=0, weight_layout="packed")
+                                     seed=0, weight_layout="packed", plan=PhysicalPlan(reduction=red))
             lay.enable_main_grad()
             opt = FusedAdamW([lay.weight, lay.bias], lr=1e-3, betas=(0.9, 0.999), eps=1e-8, moments="fp32")
             gen = torch.Generator(device=dev).manual_seed(C)
             x = torch.randn(Bm, Dm, device=dev, generator=gen)
             dy = torch.randn(Bm, Gm, device=dev, generator=gen)
             ev = {"fwd": [], "bwd": []}
-            bwd_name = "bwd_events" if pool == "max" else "bwd_shared"
+            bwd_name = "bwd_events" if pool == "max" else ("bwd_shared_det" if red == "deterministic" else "bwd_shared")
             orig = {"fwd": _native.fwd_shared, "bwd": getattr(_native, bwd_name)}
 
             def timed(name):
@@ -511,16 +513,16 @@ def bench_modeb(args):
                 setattr(_native, bwd_name, orig["bwd"])
             launches += _native.launch_count() - n0
             ms = s_ev.elapsed_time(e_ev) / steps
-            rows.append({"pool": pool, "C": C, "steps": steps, "ms_per_step": ms,
+            rows.append({"pool": pool, "C": C, "reduction": red, "steps": steps, "ms_per_step": ms,
                          "neuron_samples_per_s": Bm * Hm / (ms / 1e3),
                          "fwd_ms": statistics.mean(a.elapsed_time(b) for a, b in ev["fwd"]),
                          "bwd_ms": statistics.mean(a.elapsed_time(b) for a, b in ev["bwd"]),
                          "fwd_tflops": 2 * 8 * Hm * Bm / (statistics.mean(a.elapsed_time(b) for a, b in ev["fwd"])
                                                           * 1e-3) / 1e12,
-                         "published_rtx3090_bf16_ms": MB_PUBLISHED_MS[(pool, C)]})
+                         "published_rtx3090_bf16_ms": MB_PUBLISHED_MS[(pool, C)] if red == "fast" else None})
             del lay, opt
             torch.cuda.empty_cache()
-    head = next(r for r in rows if r["pool"] == "mean" and r["C"] == 64)
+    head = next(r for r in rows if r["pool"] == "mean" and r["C"] == 64 and r["reduction"] == "fast")
     line = {
         "metric": MB_METRIC, "value": head["neuron_samples_per_s"], "unit": UNIT, "n_gpus": 1,
         "steps": head["steps"], "warmup": max(3, args.warmup), "ms_per_step": head["ms_per_step"],

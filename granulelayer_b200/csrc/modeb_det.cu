@@ -5,7 +5,7 @@
 // workspace owners of its grouped kernels; sparse_pooling/README.md "Deterministic execution"):
 // every sum has a fixed owner and order, or is exact, so repeated runs are bitwise identical.
 //   dW, db  a block owns a run of records of one group and walks the token tiles in order; the lane
-//           that holds a record adds its tile sums to dw/db with plain loads and stores.
+//           that holds a record loads its dw/db, adds the tile's sums and stores them back.
 //   dX      each (token, record, k) sum, reduced over the record's lanes in a fixed butterfly order,
 //           is rounded once to a 64-bit integer at a per-token power-of-two scale qscale[t] = 2^e_t
 //           (the caller picks e_t so that sum_d |dx[t, d]| 2^e_t < 2^61) and added with integer
@@ -85,12 +85,44 @@ __global__ void __launch_bounds__(kDetThreads, 1)
       mb_load_w4<PACKED>(p, g, jj, nq * 4, w, bb);
       mb_load_w4_perm<PACKED>(p, g, jj, nq * 4, km, wp);
       const int nv = okr ? min(max(ng - (j * C + nq * 4), 0), 4) : 0;
+      // this lane owns these neurons' dW / db: the tile's sums accumulate onto the current values,
+      // read here so that the loads overlap the token loop, and are stored back after it
       float dwacc[4][8], dbacc[4];
+      if (nv > 0) {
+        if constexpr (!PACKED) {
+          const float4* dwp = reinterpret_cast<const float4*>(p.dw + ((g * p.NB + j) * C + nq * 4) * 8);
 #pragma unroll
-      for (int n = 0; n < 4; ++n) {
-        dbacc[n] = 0.f;
+          for (int n = 0; n < 4; ++n)
 #pragma unroll
-        for (int k = 0; k < 8; ++k) dwacc[n][k] = 0.f;
+            for (int h = 0; h < 2; ++h) {
+              const float4 v = dwp[2 * n + h];
+              dwacc[n][4 * h] = v.x; dwacc[n][4 * h + 1] = v.y; dwacc[n][4 * h + 2] = v.z; dwacc[n][4 * h + 3] = v.w;
+            }
+          const float4 v = *reinterpret_cast<const float4*>(p.db + (g * p.NB + j) * C + nq * 4);
+          dbacc[0] = v.x; dbacc[1] = v.y; dbacc[2] = v.z; dbacc[3] = v.w;
+        } else {
+#pragma unroll
+          for (int n = 0; n < 4; ++n)
+#pragma unroll
+            for (int kh = 0; kh < 4; ++kh) {
+              const float2 v = *reinterpret_cast<const float2*>(p.dw + mb_packed_w(m, g, j, nq * 4 + n, kh));
+              dwacc[n][2 * kh] = v.x;
+              dwacc[n][2 * kh + 1] = v.y;
+            }
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const float2 v = *reinterpret_cast<const float2*>(p.db + mb_packed_b(m, g, j, nq * 4 + 2 * h));
+            dbacc[2 * h] = v.x;
+            dbacc[2 * h + 1] = v.y;
+          }
+        }
+      } else {
+#pragma unroll
+        for (int n = 0; n < 4; ++n) {
+          dbacc[n] = 0.f;
+#pragma unroll
+          for (int k = 0; k < 8; ++k) dwacc[n][k] = 0.f;
+        }
       }
 #pragma unroll 1
       for (int tc = 0; tc < T; tc += TS) {
@@ -158,41 +190,27 @@ __global__ void __launch_bounds__(kDetThreads, 1)
           }
         }
       }
-      if (nv > 0) {  // this lane owns these neurons' dW / db: plain read-modify-write, tiles in order
+      if (nv > 0) {
         if constexpr (!PACKED) {
-          float* dwp = p.dw + ((g * p.NB + j) * C + nq * 4) * 8;
+          float4* dwp = reinterpret_cast<float4*>(p.dw + ((g * p.NB + j) * C + nq * 4) * 8);
 #pragma unroll
           for (int n = 0; n < 4; ++n)
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              float4* q4 = reinterpret_cast<float4*>(dwp + 8 * n + 4 * h);
-              float4 v = *q4;
-              v.x += dwacc[n][4 * h]; v.y += dwacc[n][4 * h + 1]; v.z += dwacc[n][4 * h + 2]; v.w += dwacc[n][4 * h + 3];
-              *q4 = v;
-            }
-          float4* b4 = reinterpret_cast<float4*>(p.db + (g * p.NB + j) * C + nq * 4);
-          float4 v = *b4;
-          v.x += dbacc[0]; v.y += dbacc[1]; v.z += dbacc[2]; v.w += dbacc[3];
-          *b4 = v;
+            for (int h = 0; h < 2; ++h)
+              dwp[2 * n + h] = make_float4(dwacc[n][4 * h], dwacc[n][4 * h + 1], dwacc[n][4 * h + 2], dwacc[n][4 * h + 3]);
+          *reinterpret_cast<float4*>(p.db + (g * p.NB + j) * C + nq * 4) =
+              make_float4(dbacc[0], dbacc[1], dbacc[2], dbacc[3]);
         } else {
 #pragma unroll
           for (int n = 0; n < 4; ++n)
 #pragma unroll
-            for (int kh = 0; kh < 4; ++kh) {
-              float2* q2 = reinterpret_cast<float2*>(p.dw + mb_packed_w(m, g, j, nq * 4 + n, kh));
-              float2 v = *q2;
-              v.x += dwacc[n][2 * kh];
-              v.y += dwacc[n][2 * kh + 1];
-              *q2 = v;
-            }
+            for (int kh = 0; kh < 4; ++kh)
+              *reinterpret_cast<float2*>(p.dw + mb_packed_w(m, g, j, nq * 4 + n, kh)) =
+                  make_float2(dwacc[n][2 * kh], dwacc[n][2 * kh + 1]);
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            float2* b2 = reinterpret_cast<float2*>(p.db + mb_packed_b(m, g, j, nq * 4 + 2 * h));
-            float2 v = *b2;
-            v.x += dbacc[2 * h];
-            v.y += dbacc[2 * h + 1];
-            *b2 = v;
-          }
+          for (int h = 0; h < 2; ++h)
+            *reinterpret_cast<float2*>(p.db + mb_packed_b(m, g, j, nq * 4 + 2 * h)) =
+                make_float2(dbacc[2 * h], dbacc[2 * h + 1]);
         }
       }
     }
