@@ -104,7 +104,7 @@ struct BwdParams {
 
 // FIXED = false: fp32 tile.  FIXED = true: int32 tile + fp32 fold tile.  LOCAL: one group per block,
 // tiles over the group's feature map only (rows = its features, records read as positions).
-template <int T, int ACT, bool FIXED, bool LOCAL>
+template <int T, int ACT, bool FIXED, bool LOCAL, bool SMOOTH>
 __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const BwdParams p) {
   constexpr int NPW = 32 / T;
   constexpr int NW = kBwdThreads / 32;
@@ -149,7 +149,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const BwdParams p) 
     const int64_t ci = (int64_t)(t0 + t) * p.ldg + (g - p.g0);
     float c1 = tok_ok ? __ldg(p.gpre + ci) : 0.f;
     if (p.pool == GL_POOL_MEAN) c1 = c1 / (float)ng;
-    const bool smooth = p.pool >= GL_POOL_LME;  // uniform: dz through pool_dz
+    constexpr bool smooth = SMOOTH;  // LogMeanExp / power mean / softmax-weighted: dz through pool_dz
     const float c2 = smooth && tok_ok && p.c2 != nullptr ? __ldg(p.c2 + ci) : 0.f;
     const float c3 = smooth && tok_ok && p.c3 != nullptr ? __ldg(p.c3 + ci) : 0.f;
     float c1s = 0.f;
@@ -264,10 +264,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const BwdParams p) 
 // each rounded up to 16 bytes.
 static int64_t bwd_smem(int64_t D, int T, bool fixed) { return ((D * T + 3) & ~3LL) * 4 * (fixed ? 3 : 2); }
 
-template <int T, int ACT, bool FIXED, bool LOCAL>
+template <int T, int ACT, bool FIXED, bool LOCAL, bool SMOOTH>
 static int launch_bwd(const BwdParams& p, int64_t B, cudaStream_t st) {
   const size_t smem = (size_t)bwd_smem(LOCAL ? p.lm.fcap : p.D, T, FIXED);
-  auto kern = bwd_kernel<T, ACT, FIXED, LOCAL>;
+  auto kern = bwd_kernel<T, ACT, FIXED, LOCAL, SMOOTH>;
   int rc = ensure_dynamic_smem((const void*)kern, smem);
   if (rc) return rc;
   const int64_t tiles = (B + T - 1) / T;
@@ -281,23 +281,23 @@ static int launch_bwd(const BwdParams& p, int64_t B, cudaStream_t st) {
   return GL_OK;
 }
 
-template <int T, bool FIXED, bool LOCAL>
+template <int T, bool FIXED, bool LOCAL, bool SMOOTH>
 static int dispatch_act_bwd(const BwdParams& p, int64_t B, int act, cudaStream_t st) {
   switch (act) {
-    case GL_ACT_IDENTITY: return launch_bwd<T, GL_ACT_IDENTITY, FIXED, LOCAL>(p, B, st);
-    case GL_ACT_RELU: return launch_bwd<T, GL_ACT_RELU, FIXED, LOCAL>(p, B, st);
-    case GL_ACT_GELU: return launch_bwd<T, GL_ACT_GELU, FIXED, LOCAL>(p, B, st);
+    case GL_ACT_IDENTITY: return launch_bwd<T, GL_ACT_IDENTITY, FIXED, LOCAL, SMOOTH>(p, B, st);
+    case GL_ACT_RELU: return launch_bwd<T, GL_ACT_RELU, FIXED, LOCAL, SMOOTH>(p, B, st);
+    case GL_ACT_GELU: return launch_bwd<T, GL_ACT_GELU, FIXED, LOCAL, SMOOTH>(p, B, st);
     default: return GL_ERR_UNSUPPORTED;
   }
 }
 
-template <bool FIXED, bool LOCAL>
+template <bool FIXED, bool LOCAL, bool SMOOTH>
 static int dispatch_tokens_bwd(const BwdParams& p, int64_t B, int act, int T, cudaStream_t st) {
   switch (T) {
-    case 8: return dispatch_act_bwd<8, FIXED, LOCAL>(p, B, act, st);
-    case 4: return dispatch_act_bwd<4, FIXED, LOCAL>(p, B, act, st);
-    case 2: return dispatch_act_bwd<2, FIXED, LOCAL>(p, B, act, st);
-    default: return dispatch_act_bwd<1, FIXED, LOCAL>(p, B, act, st);
+    case 8: return dispatch_act_bwd<8, FIXED, LOCAL, SMOOTH>(p, B, act, st);
+    case 4: return dispatch_act_bwd<4, FIXED, LOCAL, SMOOTH>(p, B, act, st);
+    case 2: return dispatch_act_bwd<2, FIXED, LOCAL, SMOOTH>(p, B, act, st);
+    default: return dispatch_act_bwd<1, FIXED, LOCAL, SMOOTH>(p, B, act, st);
   }
 }
 
@@ -377,9 +377,12 @@ extern "C" int gl_bwd_f32(const GlBwdArgs* args, void* stream) {
               a.NB, a.g0, a.g1, a.ldx, a.ldg, a.lddx, a.pool, gpc, a.c2, a.c3, a.param,
               pow_code(a.param) >= 1 ? pow_code(a.param) - 1 : -1};
   cudaStream_t st = (cudaStream_t)stream;
+  if (smooth)
+    return local ? dispatch_tokens_bwd<false, true, true>(p, a.B, a.act, T, st)
+                 : dispatch_tokens_bwd<false, false, true>(p, a.B, a.act, T, st);
   if (local)
-    return fixed ? dispatch_tokens_bwd<true, true>(p, a.B, a.act, T, st)
-                 : dispatch_tokens_bwd<false, true>(p, a.B, a.act, T, st);
-  return fixed ? dispatch_tokens_bwd<true, false>(p, a.B, a.act, T, st)
-               : dispatch_tokens_bwd<false, false>(p, a.B, a.act, T, st);
+    return fixed ? dispatch_tokens_bwd<true, true, false>(p, a.B, a.act, T, st)
+                 : dispatch_tokens_bwd<false, true, false>(p, a.B, a.act, T, st);
+  return fixed ? dispatch_tokens_bwd<true, false, false>(p, a.B, a.act, T, st)
+               : dispatch_tokens_bwd<false, false, false>(p, a.B, a.act, T, st);
 }
