@@ -16,11 +16,21 @@ from pathlib import Path
 
 import torch
 
-ABI_VERSION = 9
+ABI_VERSION = 10
 LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libgranule_b200.so"
 
 POOL_MEAN, POOL_SUM, POOL_MAX, POOL_LME, POOL_POWER, POOL_SOFTMAX, POOL_TOPK = 0, 1, 2, 3, 4, 5, 6
 ACT_IDS = {"identity": 0, "relu": 1, "gelu": 2}
+DTYPE_F32, DTYPE_BF16 = 0, 1
+
+
+def _wdtype(t) -> int:
+    """GL_DTYPE_* of a parameter tensor (fp32 or bf16 storage)."""
+    if t.dtype == torch.float32:
+        return DTYPE_F32
+    if t.dtype == torch.bfloat16:
+        return DTYPE_BF16
+    raise ValueError(f"parameters must be float32 or bfloat16, not {t.dtype}")
 
 # The exported entry points, in header order (checked by the CPU test suite).
 EXPORTS = ("gl_abi_version", "gl_status_string", "gl_last_cuda_error", "gl_fwd_f32", "gl_bwd_f32",
@@ -45,7 +55,7 @@ class GlFwdArgs(ctypes.Structure):
                 ("lidx", ctypes.c_void_p), ("fmap", ctypes.c_void_p), ("nfeat", ctypes.c_void_p),
                 ("fcap", ctypes.c_int64), ("winners", ctypes.c_void_p), ("ldwin", ctypes.c_int64),
                 ("stat", ctypes.c_void_p), ("ldstat", ctypes.c_int64), ("param", ctypes.c_float),
-                ("k", ctypes.c_int32)]
+                ("k", ctypes.c_int32), ("wdtype", ctypes.c_int32), ("reserved3", ctypes.c_int32)]
 
 
 class GlBwdArgs(ctypes.Structure):
@@ -59,7 +69,7 @@ class GlBwdArgs(ctypes.Structure):
                 ("groups_per_cta", ctypes.c_int32), ("wabsmax", ctypes.c_void_p), ("rowmax", ctypes.c_void_p),
                 ("order", ctypes.c_void_p), ("lidx", ctypes.c_void_p), ("fmap", ctypes.c_void_p),
                 ("nfeat", ctypes.c_void_p), ("fcap", ctypes.c_int64), ("c2", ctypes.c_void_p),
-                ("c3", ctypes.c_void_p), ("param", ctypes.c_float), ("reserved2", ctypes.c_int32)]
+                ("c3", ctypes.c_void_p), ("param", ctypes.c_float), ("wdtype", ctypes.c_int32)]
 
 
 class GlAdamArgs(ctypes.Structure):
@@ -67,13 +77,15 @@ class GlAdamArgs(ctypes.Structure):
                 ("n", ctypes.c_int64),
                 ("lr", ctypes.c_float), ("beta1", ctypes.c_float), ("beta2", ctypes.c_float),
                 ("eps", ctypes.c_float), ("weight_decay", ctypes.c_float), ("bc1", ctypes.c_float),
-                ("bc2", ctypes.c_float), ("zero_grad", ctypes.c_int32)]
+                ("bc2", ctypes.c_float), ("zero_grad", ctypes.c_int32), ("master", ctypes.c_void_p),
+                ("pdtype", ctypes.c_int32), ("mdtype", ctypes.c_int32), ("stochastic", ctypes.c_int32),
+                ("seed", ctypes.c_uint32)]
 
 
 class GlSharedArgs(ctypes.Structure):
     _fields_ = [(n, ctypes.c_void_p) for n in ("x", "idx", "w", "b", "counts", "pre", "gpre", "dx", "dw", "db")] + \
                [(n, ctypes.c_int64) for n in ("B", "D", "NB", "C", "g0", "g1", "ldx", "ldp", "ldg", "lddx")] + \
-               [(n, ctypes.c_int32) for n in ("pool", "act", "packed", "tokens", "groups_per_cta", "reserved")] + \
+               [(n, ctypes.c_int32) for n in ("pool", "act", "packed", "tokens", "groups_per_cta", "wdtype")] + \
                [("winners", ctypes.c_void_p), ("ldwin", ctypes.c_int64), ("stat", ctypes.c_void_p),
                 ("ldstat", ctypes.c_int64), ("c2", ctypes.c_void_p), ("c3", ctypes.c_void_p),
                 ("param", ctypes.c_float), ("k", ctypes.c_int32)]
@@ -82,7 +94,7 @@ class GlSharedArgs(ctypes.Structure):
 class GlEventArgs(ctypes.Structure):
     _fields_ = [(n, ctypes.c_void_p) for n in ("x", "idx", "w", "b", "winners", "coef", "dx", "dw", "db")] + \
                [(n, ctypes.c_int64) for n in ("B", "D", "NB", "C", "g0", "g1", "ldx", "ldwin", "ldc", "lddx")] + \
-               [(n, ctypes.c_int32) for n in ("shared", "packed", "act", "kev")]
+               [(n, ctypes.c_int32) for n in ("shared", "packed", "act", "kev", "wdtype", "reserved")]
 
 
 class GlK16Args(ctypes.Structure):
@@ -197,7 +209,7 @@ def fwd(x, idx, w, b, counts, pre, NB: int, g0: int, g1: int, pool: int, act: in
                   g0, g1, x.stride(0), pre.stride(0), pool, act, tokens, groups_per_cta, _ptr(wabsmax), _ptr(order),
                   _ptr(lidx), _ptr(fmap), _ptr(nfeat), fmap.shape[1] if fmap is not None else 0, _ptr(winners),
                   winners.stride(0) if winners is not None else 0, _ptr(stat),
-                  stat.stride(0) if stat is not None else 0, float(param), int(k))
+                  stat.stride(0) if stat is not None else 0, float(param), int(k), _wdtype(w), 0)
     with torch.cuda.device(x.device):
         _check(lib, lib.gl_fwd_f32(ctypes.byref(a), _stream(x.device)), "gl_fwd_f32")
 
@@ -218,7 +230,8 @@ def bwd(x, idx, w, b, counts, gpre, dx, dw, db, NB: int, g0: int, g1: int, pool:
     a = GlBwdArgs(_ptr(x), _ptr(idx), _ptr(w), _ptr(b), _ptr(counts), _ptr(gpre), _ptr(dx), _ptr(dw), _ptr(db),
                   x.shape[0], x.shape[1], NB, g0, g1, x.stride(0), gpre.stride(0), dx.stride(0), pool, act,
                   tokens, groups_per_cta, _ptr(wabsmax), _ptr(rowmax), _ptr(order), _ptr(lidx), _ptr(fmap),
-                  _ptr(nfeat), fmap.shape[1] if fmap is not None else 0, _ptr(c2), _ptr(c3), float(param), 0)
+                  _ptr(nfeat), fmap.shape[1] if fmap is not None else 0, _ptr(c2), _ptr(c3), float(param),
+                  _wdtype(w))
     with torch.cuda.device(x.device):
         _check(lib, lib.gl_bwd_f32(ctypes.byref(a), _stream(x.device)), "gl_bwd_f32")
 
@@ -228,6 +241,7 @@ def _shared_args(x, idx, w, b, counts, NB, C, g0, g1, pool, act, packed, tokens,
     a.x, a.idx, a.w, a.b, a.counts = _ptr(x), _ptr(idx), _ptr(w), _ptr(b), _ptr(counts)
     a.B, a.D, a.NB, a.C, a.g0, a.g1, a.ldx = x.shape[0], x.shape[1], NB, C, g0, g1, x.stride(0)
     a.pool, a.act, a.packed, a.tokens, a.groups_per_cta = pool, act, int(bool(packed)), tokens, groups_per_cta
+    a.wdtype = _wdtype(w)
     return a
 
 
@@ -289,7 +303,7 @@ def bwd_events(x, idx, w, b, winners, coef, dx, dw, db, NB: int, C: int, shared:
     lib = load()
     a = GlEventArgs(_ptr(x), _ptr(idx), _ptr(w), _ptr(b), _ptr(winners), _ptr(coef), _ptr(dx), _ptr(dw), _ptr(db),
                     x.shape[0], x.shape[1], NB, C, g0, g1, x.stride(0), winners.stride(0), coef.stride(0),
-                    dx.stride(0), int(bool(shared)), int(bool(packed)), act, int(kev))
+                    dx.stride(0), int(bool(shared)), int(bool(packed)), act, int(kev), _wdtype(w), 0)
     with torch.cuda.device(x.device):
         _check(lib, lib.gl_bwd_events_f32(ctypes.byref(a), _stream(x.device)), "gl_bwd_events_f32")
 
@@ -332,11 +346,21 @@ def group_order(idx, counts, D: int, NB: int, g0: int, g1: int, unit: int, out):
                                        _stream(idx.device)), "gl_group_order")
 
 
-def adam(p, g, m, v, lr, beta1, beta2, eps, weight_decay, bc1, bc2, zero_grad=True):
-    _require_cuda(p, g, m, v)
+def adam(p, g, m, v, lr, beta1, beta2, eps, weight_decay, bc1, bc2, zero_grad=True, master=None,
+         stochastic=False, seed=0):
+    """One fused Adam(W) step (gl_adam_f32): fp32 gradient ``g`` (zeroed when ``zero_grad``), parameter
+    ``p`` fp32 or bf16, moments ``m``/``v`` fp32 or bf16, optional fp32 ``master`` of a bf16 ``p``,
+    stochastic rounding of a bf16 ``p`` without master from stream ``seed``."""
+    _require_cuda(p, g, m, v, master)
+    if g.dtype != torch.float32 or m.dtype != v.dtype or (master is not None and master.dtype != torch.float32):
+        raise ValueError("adam: fp32 gradient and master, moments of one dtype")
+    for t in (g, m, v) + ((master,) if master is not None else ()):
+        if t.numel() != p.numel() or not t.is_contiguous():
+            raise ValueError("adam: contiguous tensors of the parameter's size")
     lib = load()
     a = GlAdamArgs(_ptr(p), _ptr(g), _ptr(m), _ptr(v), p.numel(), lr, beta1, beta2, eps, weight_decay, bc1, bc2,
-                   int(bool(zero_grad)))
+                   int(bool(zero_grad)), _ptr(master), _wdtype(p), _wdtype(m), int(bool(stochastic)),
+                   int(seed) & 0xFFFFFFFF)
     with torch.cuda.device(p.device):
         _check(lib, lib.gl_adam_f32(ctypes.byref(a), _stream(p.device)), "gl_adam_f32")
 

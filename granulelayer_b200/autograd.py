@@ -87,8 +87,8 @@ def check_supported(layout: SparseLayout, level: LevelSpec, dtype: torch.dtype, 
         raise UnsupportedOnB200(f"pooling {level.type!r} is not on the B200 path (supported: {B200_POOLS})")
     if level.neurons_per_shard is not None and not semantic:
         raise UnsupportedOnB200("neurons_per_shard belongs to a two-level configuration")
-    if dtype != torch.float32:
-        raise UnsupportedOnB200(f"the B200 kernels compute in float32 (layer dtype {dtype})")
+    if dtype not in (torch.float32, torch.bfloat16):
+        raise UnsupportedOnB200(f"the B200 kernels read float32 or bfloat16 parameters (layer dtype {dtype})")
 
 
 class Level1Runtime:
@@ -391,7 +391,9 @@ class Level1Runtime:
         wabsmax = rowmax = None
         if self.fixed_point and B > 0 and not self.smooth:
             wabsmax = saved.get("wabsmax")
-            if wabsmax is None:
+            if wabsmax is None and w.dtype != torch.float32:   # bf16 storage: padding slots hold zeros
+                wabsmax = w.reshape(self.groups, -1).abs().amax(1).float().contiguous()
+            elif wabsmax is None:
                 wabsmax = torch.empty(self.groups, device=x.device, dtype=torch.float32)
                 _native.group_absmax(w, self.counts_i32, self.layout.blocks_per_group, 0, self.groups, wabsmax)
             rowmax = self.rowmax()

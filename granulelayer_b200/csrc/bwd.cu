@@ -100,6 +100,7 @@ struct BwdParams {
   const float* c3;
   float param;
   int ipm1;         // integer code of the power mean's p - 1 (-1: general)
+  bool wbf;         // w and b stored as bf16
 };
 
 // FIXED = false: fp32 tile.  FIXED = true: int32 tile + fp32 fold tile.  LOCAL: one group per block,
@@ -175,8 +176,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const BwdParams p) 
             p.order != nullptr ? min(max(__ldg(p.order + (g - p.g0) * (int64_t)slots + s), 0), slots - 1) : s;
         const int64_t f = fbase + slot;
         const Rec8 r = load_rec8(ridx + f * 8, D - 1);
-        const W8 wr = load_w8(p.w + f * 8);
-        float z = __ldg(p.bias + f);
+        const W8 wr = load_w8_any(p.w, f, p.wbf);
+        float z = load_any(p.bias, f, p.wbf);
         float xv[8];
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
@@ -333,6 +334,7 @@ extern "C" int gl_bwd_f32(const GlBwdArgs* args, void* stream) {
     return GL_ERR_UNSUPPORTED;
   const bool smooth = a.pool >= GL_POOL_LME;
   if (smooth && (!a.c2 || (a.pool == GL_POOL_SOFTMAX && !a.c3))) return GL_ERR_NULL;
+  if (a.wdtype != GL_DTYPE_F32 && a.wdtype != GL_DTYPE_BF16) return GL_ERR_UNSUPPORTED;
   if ((a.pool == GL_POOL_LME || a.pool == GL_POOL_SOFTMAX) && !(a.param > 0.f)) return GL_ERR_SHAPE;
   if (a.pool == GL_POOL_POWER && !(a.param >= 1.f)) return GL_ERR_SHAPE;
   int optin = 0, sms = 0;
@@ -375,7 +377,7 @@ extern "C" int gl_bwd_f32(const GlBwdArgs* args, void* stream) {
   BwdParams p{a.x, a.idx, a.w, a.b, a.counts, a.gpre, a.dx, a.dw, a.db, a.wabsmax, a.rowmax, a.order,
               LocalMap{a.lidx, a.fmap, a.nfeat, (int)a.fcap}, (int)a.B, (int)a.D,
               a.NB, a.g0, a.g1, a.ldx, a.ldg, a.lddx, a.pool, gpc, a.c2, a.c3, a.param,
-              pow_code(a.param) >= 1 ? pow_code(a.param) - 1 : -1};
+              pow_code(a.param) >= 1 ? pow_code(a.param) - 1 : -1, a.wdtype == GL_DTYPE_BF16};
   cudaStream_t st = (cudaStream_t)stream;
   if (smooth)
     return local ? dispatch_tokens_bwd<false, true, true>(p, a.B, a.act, T, st)

@@ -251,6 +251,40 @@ __device__ __forceinline__ W8 load_w8(const float* __restrict__ p) {
   return o;
 }
 
+// bf16 storage (the reference's default parameter dtype): a bf16 value is the upper half of the
+// fp32 with the same bits, so widening is exact.  `bf` is uniform across the launch.
+__device__ __forceinline__ float bf16_lo(unsigned u) { return __uint_as_float(u << 16); }
+__device__ __forceinline__ float bf16_hi(unsigned u) { return __uint_as_float(u & 0xFFFF0000u); }
+
+// Weights of neuron f (8 consecutive values) in fp32 or bf16 storage.
+__device__ __forceinline__ W8 load_w8_any(const float* __restrict__ w, int64_t f, bool bf) {
+  if (!bf) return load_w8(w + f * 8);
+  const uint4 u = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(w) + f * 8));
+  W8 o;
+  o.w[0] = bf16_lo(u.x); o.w[1] = bf16_hi(u.x); o.w[2] = bf16_lo(u.y); o.w[3] = bf16_hi(u.y);
+  o.w[4] = bf16_lo(u.z); o.w[5] = bf16_hi(u.z); o.w[6] = bf16_lo(u.w); o.w[7] = bf16_hi(u.w);
+  return o;
+}
+
+// Element i of an fp32 or bf16 array.
+__device__ __forceinline__ float load_any(const float* __restrict__ a, int64_t i, bool bf) {
+  return bf ? __uint_as_float((unsigned)__ldg(reinterpret_cast<const unsigned short*>(a) + i) << 16) : __ldg(a + i);
+}
+
+// Elements i, i+1 (i even) of an fp32 or bf16 array.
+__device__ __forceinline__ float2 load2_any(const float* __restrict__ a, int64_t i, bool bf) {
+  if (!bf) return __ldg(reinterpret_cast<const float2*>(a + i));
+  const unsigned u = __ldg(reinterpret_cast<const unsigned*>(reinterpret_cast<const uint16_t*>(a) + i));
+  return make_float2(bf16_lo(u), bf16_hi(u));
+}
+
+// Elements i .. i+3 (i a multiple of 4) of an fp32 or bf16 array.
+__device__ __forceinline__ float4 load4_any(const float* __restrict__ a, int64_t i, bool bf) {
+  if (!bf) return __ldg(reinterpret_cast<const float4*>(a + i));
+  const uint2 u = __ldg(reinterpret_cast<const uint2*>(reinterpret_cast<const uint16_t*>(a) + i));
+  return make_float4(bf16_lo(u.x), bf16_hi(u.x), bf16_lo(u.y), bf16_hi(u.y));
+}
+
 // Vector reductions into global memory (sm_90+ PTX vector red).
 __device__ __forceinline__ void red_add(float* p, float a) {
   asm volatile("red.global.add.f32 [%0], %1;" ::"l"(p), "f"(a) : "memory");

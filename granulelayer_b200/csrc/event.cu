@@ -29,10 +29,11 @@ __global__ void __launch_bounds__(kEventThreads) event_bwd_kernel(const GlEventA
   Rec8 r;
   float wv[8], bb;
   int64_t woff[4], boff;  // offsets of the weight pairs (k = 2 kh, 2 kh + 1) and of the bias
+  const bool wbf = a.wdtype == GL_DTYPE_BF16;
   if constexpr (MODE == 0) {
     const int64_t f = g * slots + s;
     r = load_rec8(a.idx + f * 8, D - 1);
-    const W8 w8 = load_w8(a.w + f * 8);
+    const W8 w8 = load_w8_any(a.w, f, wbf);
 #pragma unroll
     for (int k = 0; k < 8; ++k) wv[k] = w8.w[k];
 #pragma unroll
@@ -57,12 +58,12 @@ __global__ void __launch_bounds__(kEventThreads) event_bwd_kernel(const GlEventA
     }
 #pragma unroll
     for (int kh = 0; kh < 4; ++kh) {
-      const float2 v = __ldg(reinterpret_cast<const float2*>(a.w + woff[kh]));
+      const float2 v = load2_any(a.w, woff[kh], wbf);
       wv[2 * kh] = v.x;
       wv[2 * kh + 1] = v.y;
     }
   }
-  bb = __ldg(a.b + boff);
+  bb = load_any(a.b, boff, wbf);
   float xv[8];
   float z = bb;
 #pragma unroll
@@ -107,6 +108,7 @@ extern "C" int gl_bwd_events_f32(const GlEventArgs* args, void* stream) {
   if (!a.x || !a.idx || !a.w || !a.b || !a.winners || !a.coef || !a.dx || !a.dw || !a.db) return GL_ERR_NULL;
   const int64_t kev = a.kev > 0 ? a.kev : 1;
   if (kev > 64) return GL_ERR_SHAPE;
+  if (a.wdtype != GL_DTYPE_F32 && a.wdtype != GL_DTYPE_BF16) return GL_ERR_UNSUPPORTED;
   if (a.ldx < a.D || a.lddx < a.D || a.ldwin < (a.g1 - a.g0) * kev || a.ldc < a.g1 - a.g0) return GL_ERR_SHAPE;
   if (((uintptr_t)a.idx & 15) || ((uintptr_t)a.w & 15) || ((uintptr_t)a.dw & 7)) return GL_ERR_ALIGN;
   const int mode = a.shared ? (a.packed ? 2 : 1) : 0;

@@ -37,7 +37,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                int B, int D, int64_t NB, int64_t g0, int64_t g1, int64_t ldx, int64_t ldp, int pool, int gpc,
                float* __restrict__ wabsmax, const int32_t* __restrict__ order, const LocalMap lm,
                int32_t* __restrict__ winners, int64_t ldwin, float* __restrict__ stat, int64_t ldstat,
-               const PoolParam pp) {
+               const PoolParam pp, const bool wbf) {
   constexpr bool MAXP = PK == PK_MAX;
   constexpr bool SM = PK == PK_LSE || PK == PK_POW;  // three-word states
   constexpr bool TK = PK == PK_TOPK || PK == PK_TOPK64;
@@ -114,8 +114,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         const int64_t f = fbase + slot;
         sl[u] = slot;
         r[u] = load_rec8(ridx + f * 8, dmax);
-        wr[u] = load_w8(w + f * 8);
-        bb[u] = __ldg(bias + f);
+        wr[u] = load_w8_any(w, f, wbf);
+        bb[u] = load_any(bias, f, wbf);
       }
 #pragma unroll
       for (int u = 0; u < UNR; ++u) {
@@ -313,7 +313,8 @@ static int launch_fwd(const GlFwdArgs& a, int gpc, cudaStream_t st) {
   kern<<<grid, kFwdThreads, smem, st>>>(a.x, a.idx, a.w, a.b, a.counts, a.pre, (int)a.B, (int)a.D, a.NB, a.g0,
                                         a.g1, a.ldx, a.ldp, a.pool, gpc, a.wabsmax, a.order, lm, a.winners, a.ldwin,
                                         a.stat, a.ldstat, PoolParam{a.param, pow_code(a.param),
-                                                                    a.pool == GL_POOL_SOFTMAX, a.k});
+                                                                    a.pool == GL_POOL_SOFTMAX, a.k},
+                                        a.wdtype == GL_DTYPE_BF16);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_cuda_error(e);
   count_launches(1);
@@ -384,6 +385,7 @@ extern "C" int gl_fwd_f32(const GlFwdArgs* args, void* stream) {
   if (a.B > 2147483647LL || a.ldx < a.D || a.ldp < a.g1 - a.g0) return GL_ERR_SHAPE;
   if (((uintptr_t)a.idx & 15) || ((uintptr_t)a.w & 15)) return GL_ERR_ALIGN;
   if (a.pool < GL_POOL_MEAN || a.pool > GL_POOL_TOPK) return GL_ERR_UNSUPPORTED;
+  if (a.wdtype != GL_DTYPE_F32 && a.wdtype != GL_DTYPE_BF16) return GL_ERR_UNSUPPORTED;
   if (a.pool == GL_POOL_TOPK && !topk_k_ok(a.k)) return GL_ERR_SHAPE;
   if ((a.pool == GL_POOL_LME || a.pool == GL_POOL_SOFTMAX) && !(a.param > 0.f)) return GL_ERR_SHAPE;
   if (a.pool == GL_POOL_POWER && !(a.param >= 1.f)) return GL_ERR_SHAPE;

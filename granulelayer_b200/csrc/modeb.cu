@@ -318,6 +318,7 @@ static int mb_run(const GlSharedArgs& a, bool bwd, void* stream) {
   if (a.pool < GL_POOL_MEAN || a.pool > GL_POOL_TOPK || ((a.pool == GL_POOL_MAX || a.pool == GL_POOL_TOPK) && bwd))
     return GL_ERR_UNSUPPORTED;
   if (a.pool == GL_POOL_TOPK && !topk_k_ok(a.k)) return GL_ERR_SHAPE;
+  if (a.wdtype != GL_DTYPE_F32 && a.wdtype != GL_DTYPE_BF16) return GL_ERR_UNSUPPORTED;
   const bool smooth = a.pool >= GL_POOL_LME;
   if ((a.pool == GL_POOL_LME || a.pool == GL_POOL_SOFTMAX) && !(a.param > 0.f)) return GL_ERR_SHAPE;
   if (a.pool == GL_POOL_POWER && !(a.param >= 1.f)) return GL_ERR_SHAPE;
@@ -368,6 +369,7 @@ static int mb_run(const GlSharedArgs& a, bool bwd, void* stream) {
   p.stat = a.stat; p.ldstat = a.ldstat; p.c2 = a.c2; p.c3 = a.c3;
   p.pp = PoolParam{a.param, pow_code(a.param), a.pool == GL_POOL_SOFTMAX, a.k};
   p.ipm1 = pow_code(a.param) >= 1 ? pow_code(a.param) - 1 : -1;
+  p.wbf = a.wdtype == GL_DTYPE_BF16;
   cudaStream_t st = (cudaStream_t)stream;
   const bool packed = a.packed != 0;
   switch (T) {

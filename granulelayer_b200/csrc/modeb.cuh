@@ -31,6 +31,7 @@ struct MbParams {
   const float* c3;
   PoolParam pp;
   int ipm1;         // integer code of the power mean's p - 1 (-1: general)
+  bool wbf;         // w and b stored as bf16 (gradients stay fp32)
 };
 
 template <bool PACKED>
@@ -52,14 +53,14 @@ template <bool PACKED>
 __device__ __forceinline__ void mb_load_w4(const MbParams& p, int64_t g, int j, int c0, float (&w)[4][8],
                                            float (&bb)[4]) {
   if constexpr (!PACKED) {
-    const float4* wp = reinterpret_cast<const float4*>(p.w + ((g * p.NB + j) * p.C + c0) * 8);
+    const int64_t base = ((g * p.NB + j) * p.C + c0) * 8;
 #pragma unroll
     for (int n = 0; n < 4; ++n) {
-      const float4 a = __ldg(wp + 2 * n), c = __ldg(wp + 2 * n + 1);
+      const float4 a = load4_any(p.w, base + 8 * n, p.wbf), c = load4_any(p.w, base + 8 * n + 4, p.wbf);
       w[n][0] = a.x; w[n][1] = a.y; w[n][2] = a.z; w[n][3] = a.w;
       w[n][4] = c.x; w[n][5] = c.y; w[n][6] = c.z; w[n][7] = c.w;
     }
-    const float4 b4 = __ldg(reinterpret_cast<const float4*>(p.b + (g * p.NB + j) * p.C + c0));
+    const float4 b4 = load4_any(p.b, (g * p.NB + j) * p.C + c0, p.wbf);
     bb[0] = b4.x; bb[1] = b4.y; bb[2] = b4.z; bb[3] = b4.w;
   } else {
     const MbPacked m = mb_packed(p.C, p.NB);
@@ -67,12 +68,12 @@ __device__ __forceinline__ void mb_load_w4(const MbParams& p, int64_t g, int j, 
     for (int n = 0; n < 4; ++n)
 #pragma unroll
       for (int kh = 0; kh < 4; ++kh) {
-        const float2 v = __ldg(reinterpret_cast<const float2*>(p.w + mb_packed_w(m, g, j, c0 + n, kh)));
+        const float2 v = load2_any(p.w, mb_packed_w(m, g, j, c0 + n, kh), p.wbf);
         w[n][2 * kh] = v.x;
         w[n][2 * kh + 1] = v.y;
       }
-    const float2 b0 = __ldg(reinterpret_cast<const float2*>(p.b + mb_packed_b(m, g, j, c0)));
-    const float2 b1 = __ldg(reinterpret_cast<const float2*>(p.b + mb_packed_b(m, g, j, c0 + 2)));
+    const float2 b0 = load2_any(p.b, mb_packed_b(m, g, j, c0), p.wbf);
+    const float2 b1 = load2_any(p.b, mb_packed_b(m, g, j, c0 + 2), p.wbf);
     bb[0] = b0.x; bb[1] = b0.y; bb[2] = b1.x; bb[3] = b1.y;
   }
 }
@@ -153,7 +154,7 @@ __device__ __forceinline__ void mb_load_w4_perm(const MbParams& p, int64_t g, in
     for (int khp = 0; khp < 4; ++khp) {
       const int kh = khp ^ khm;
       const int64_t off = PACKED ? mb_packed_w(m, g, j, c0 + n, kh) : ((g * p.NB + j) * p.C + c0 + n) * 8 + 2 * kh;
-      const float2 v = __ldg(reinterpret_cast<const float2*>(p.w + off));
+      const float2 v = load2_any(p.w, off, p.wbf);
       w[n][2 * khp] = sw ? v.y : v.x;
       w[n][2 * khp + 1] = sw ? v.x : v.y;
     }

@@ -295,6 +295,7 @@ extern "C" int gl_bwd_shared_det_f32(const GlSharedArgs* args, int64_t* dxq, con
   if (a.packed && (a.NB * (a.C / 8)) % 4) return GL_ERR_SHAPE;
   if (a.packed && (a.C / 8) < 4 && a.NB % (4 / (a.C / 8))) return GL_ERR_SHAPE;
   if (a.pool != GL_POOL_MEAN && a.pool != GL_POOL_SUM) return GL_ERR_UNSUPPORTED;
+  if (a.wdtype != GL_DTYPE_F32 && a.wdtype != GL_DTYPE_BF16) return GL_ERR_UNSUPPORTED;
   if (a.B == 0 || a.g1 == a.g0) return GL_OK;
   if (!a.x || !a.idx || !a.w || !a.b || !a.counts || !a.gpre || !a.dx || !a.dw || !a.db) return GL_ERR_NULL;
   if (!dxq || !qscale || !qinv) return GL_ERR_NULL;
@@ -324,6 +325,7 @@ extern "C" int gl_bwd_shared_det_f32(const GlSharedArgs* args, int64_t* dxq, con
   p.lgLPR = a.C == 8 ? 1 : a.C == 16 ? 2 : a.C == 32 ? 3 : 4;
   p.NB = a.NB; p.g0 = a.g0; p.g1 = a.g1; p.ldx = a.ldx; p.ldg = a.ldg; p.lddx = a.lddx;
   p.pool = a.pool; p.gpc = 1;
+  p.wbf = a.wdtype == GL_DTYPE_BF16;
   cudaStream_t st = (cudaStream_t)stream;
   unsigned long long* q = reinterpret_cast<unsigned long long*>(dxq);
   const bool packed = a.packed != 0;

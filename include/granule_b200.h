@@ -44,7 +44,7 @@
 extern "C" {
 #endif
 
-#define GL_ABI_VERSION 9
+#define GL_ABI_VERSION 10
 
 typedef enum GlStatus {
   GL_OK = 0,
@@ -82,6 +82,9 @@ typedef enum GlStatus {
 enum { GL_POOL_MEAN = 0, GL_POOL_SUM = 1, GL_POOL_MAX = 2, GL_POOL_LME = 3, GL_POOL_POWER = 4, GL_POOL_SOFTMAX = 5,
        GL_POOL_TOPK = 6 };
 enum { GL_ACT_IDENTITY = 0, GL_ACT_RELU = 1, GL_ACT_GELU = 2 };
+/* Storage types of parameters (the reference's default layer dtype is bfloat16); the kernels
+   compute in fp32 and write fp32 gradients. */
+enum { GL_DTYPE_F32 = 0, GL_DTYPE_BF16 = 1 };
 
 /* Forward: pre[t, g - g0] = pool_{valid s of g} act(z[t, g, s]),
  *   z[t, g, s] = b[f] + sum_k w[8f+k] * x[t, idx[8f+k]],
@@ -115,6 +118,8 @@ typedef struct GlFwdArgs {
   int64_t ldstat;
   float param;              /* the pool's parameter (see the pool ids); unused otherwise */
   int32_t k;                /* GL_POOL_TOPK: the number of slots kept; unused otherwise */
+  int32_t wdtype;           /* storage type of w and b: GL_DTYPE_F32 or GL_DTYPE_BF16 */
+  int32_t reserved3;        /* 0 */
 } GlFwdArgs;
 
 /* Backward: with c1[t, g] = gpre[t, g - g0] / counts[g] (mean) or gpre (the other pools) and
@@ -157,22 +162,32 @@ typedef struct GlBwdArgs {
   const float* c2;          /* smooth pools: [B, ldg] coefficients c2, c3 (see the pool ids); else NULL */
   const float* c3;
   float param;              /* the pool's parameter */
-  int32_t reserved2;        /* 0 */
+  int32_t wdtype;           /* storage type of w and b (dw, db, dx stay fp32) */
 } GlBwdArgs;
 
-/* Adam(W) step over n fp32 elements, in place (sparse_pooling/optim.py:26-64):
+/* Adam(W) step over n elements, in place (sparse_pooling/optim.py:26-64), in fp32 arithmetic:
  *   m = b1 m + (1-b1) g ;  v = b2 v + (1-b2) g^2
  *   p = p (1 - lr wd) - lr (m / bc1) / (sqrt(v / bc2) + eps)
  *   g = 0 when zero_grad != 0 (the reference's fused zero_grad).
- * bc1 = 1 - b1^t and bc2 = 1 - b2^t are passed in, as the reference does. */
+ * bc1 = 1 - b1^t and bc2 = 1 - b2^t are passed in, as the reference does.  The gradient g is fp32;
+ * p is fp32 or bf16 (pdtype), m and v fp32 or bf16 (mdtype, stored round-to-nearest-even).  With
+ * `master` (fp32, bf16 parameters) the update runs on the master copy and p receives it rounded to
+ * nearest; without one a bf16 p is rounded stochastically when `stochastic` is set (uniform noise
+ * below the bf16 ulp from a counter-based hash of (seed, element), then truncation, optim.py:55-62),
+ * else to nearest. */
 typedef struct GlAdamArgs {
-  float* p;
+  void* p;
   float* g;
-  float* m;
-  float* v;
+  void* m;
+  void* v;
   int64_t n;
   float lr, beta1, beta2, eps, weight_decay, bc1, bc2;
   int32_t zero_grad;
+  float* master;            /* optional fp32 master weights of a bf16 p; NULL = none */
+  int32_t pdtype;           /* GL_DTYPE_* of p */
+  int32_t mdtype;           /* GL_DTYPE_* of m and v */
+  int32_t stochastic;       /* bf16 p without master: 1 = stochastic rounding, 0 = nearest */
+  uint32_t seed;            /* stochastic rounding stream */
 } GlAdamArgs;
 
 int gl_abi_version(void);
@@ -240,7 +255,7 @@ typedef struct GlSharedArgs {
   int32_t packed;           /* 0 = canonical storage, 1 = fragment-packed */
   int32_t tokens;           /* token tile (0 = automatic; else 1, 2, 4 or 8) */
   int32_t groups_per_cta;   /* 0 = automatic */
-  int32_t reserved;         /* 0 */
+  int32_t wdtype;           /* storage type of w and b (dw, db, dx stay fp32) */
   int32_t* winners;         /* forward, GL_POOL_MAX: optional [B, ldwin] winning slots */
   int64_t ldwin;
   float* stat;              /* forward, GL_POOL_LME / SOFTMAX: optional [B, ldstat] L2 output */
@@ -292,6 +307,8 @@ typedef struct GlEventArgs {
   int32_t packed;           /* Mode B storage: 0 = canonical, 1 = fragment-packed */
   int32_t act;              /* GL_ACT_* */
   int32_t kev;              /* events per (token, group): 1 (max; 0 reads as 1) or the top-K k */
+  int32_t wdtype;           /* storage type of w and b */
+  int32_t reserved;         /* 0 */
 } GlEventArgs;
 
 int gl_bwd_events_f32(const GlEventArgs* args, void* stream);

@@ -78,12 +78,12 @@ def test_argument_validation_needs_no_device():
 
 def test_struct_layout_matches_header():
     # field order and sizes of the ctypes mirrors (pointers 8 B, int64 8 B, int32/float 4 B)
-    assert ctypes.sizeof(_native.GlFwdArgs) == 6 * 8 + 7 * 8 + 4 * 4 + 2 * 8 + 4 * 8 + 2 * 8 + 2 * 8 + 2 * 4
+    assert ctypes.sizeof(_native.GlFwdArgs) == 6 * 8 + 7 * 8 + 4 * 4 + 2 * 8 + 4 * 8 + 2 * 8 + 2 * 8 + 4 * 4
     assert ctypes.sizeof(_native.GlBwdArgs) == 9 * 8 + 8 * 8 + 4 * 4 + 3 * 8 + 4 * 8 + 2 * 8 + 2 * 4
-    assert ctypes.sizeof(_native.GlAdamArgs) == 4 * 8 + 8 + 8 * 4
+    assert ctypes.sizeof(_native.GlAdamArgs) == 4 * 8 + 8 + 8 * 4 + 8 + 4 * 4
     assert ctypes.sizeof(_native.GlK16Args) == 14 * 8 + 11 * 8 + 2 * 4
     assert ctypes.sizeof(_native.GlSharedArgs) == 10 * 8 + 10 * 8 + 6 * 4 + 2 * 8 + 4 * 8 + 2 * 4
-    assert ctypes.sizeof(_native.GlEventArgs) == 9 * 8 + 10 * 8 + 4 * 4
+    assert ctypes.sizeof(_native.GlEventArgs) == 9 * 8 + 10 * 8 + 6 * 4
 
 
 def test_missing_library_fails_loudly(tmp_path):

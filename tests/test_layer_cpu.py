@@ -37,7 +37,7 @@ def test_mode_b_cpu_forward_has_no_fallback(kw):
         lay(torch.randn(2, 64))
 
 
-@pytest.mark.parametrize("kw", [dict(dtype=torch.bfloat16),
+@pytest.mark.parametrize("kw", [dict(dtype=torch.float16),
                                 # 3 shards of 20 blocks do not tile the 48 stored blocks of a group
                                 dict(pooling={"levels": [{"type": "mean", "neurons_per_shard": 160},
                                                          {"type": "weighted_sum"}]})])
@@ -79,10 +79,14 @@ def test_state_dict_interchanges_with_reference(reference_path):
 
 
 def test_optimizer_refuses_unsupported_modes():
-    p = torch.nn.Parameter(torch.zeros(8))
+    p = torch.nn.Parameter(torch.zeros(8, dtype=torch.float16))
     p.main_grad = torch.zeros(8)
     with pytest.raises(UnsupportedOnB200):
-        FusedAdamW([p], moments="bf16").step()
+        FusedAdamW([p]).step()
+    q = torch.nn.Parameter(torch.zeros(8, dtype=torch.bfloat16))   # supported, but only on the GPU
+    q.main_grad = torch.zeros(8)
+    with pytest.raises(NativeLibraryError):
+        FusedAdamW([q], moments="bf16", master_weights=True).step()
 
 
 def test_explain_on_cpu():
