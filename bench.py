@@ -40,7 +40,9 @@ once with the reference's uniform index rule and once with windowed indices (eac
 production mode and the configuration of its published RTX 3090 table): H = 100,000,000,
 D = G = 1024, B = 8192, Mean(ReLU) and Max (identity, save_winners), fragment-packed storage,
 fwd + bwd + fused Adam (fp32), for C = 8 and C = 64, plus Mean(ReLU) with
-``PhysicalPlan(reduction="deterministic")`` (bitwise-repeatable backward).
+``PhysicalPlan(reduction="deterministic")`` (bitwise-repeatable backward) and
+Mean(ReLU) with bf16 parameters and the optimizer's defaults (bf16 moments,
+stochastic rounding), the precision of the published table.
 
 ``--impl reference`` times the reference's CPU path (the oracle port: the
 reference's materialising PyTorch path does not fit 100M neurons) on the same
@@ -467,13 +469,19 @@ def bench_modeb(args):
     rows = []
     launches = 0
     with ClockSampler(dev.index) as clk:
-        for pool, C, red in (("mean", 8, "fast"), ("mean", 64, "fast"), ("max", 8, "fast"), ("max", 64, "fast"),
-                             ("mean", 8, "deterministic"), ("mean", 64, "deterministic")):
+        for pool, C, red, dt in (("mean", 8, "fast", "f32"), ("mean", 64, "fast", "f32"), ("max", 8, "fast", "f32"),
+                                 ("max", 64, "fast", "f32"), ("mean", 8, "deterministic", "f32"),
+                                 ("mean", 64, "deterministic", "f32"), ("mean", 8, "fast", "bf16"),
+                                 ("mean", 64, "fast", "bf16")):
             pooling = pool   # the operators' default activations: Mean(ReLU), Max(identity)
-            lay = SparsePoolingLayer(Dm, Hm, Gm, shared_neurons=C, pooling=pooling, dtype=torch.float32, device=dev,
+            dtype = torch.bfloat16 if dt == "bf16" else torch.float32
+            lay = SparsePoolingLayer(Dm, Hm, Gm, shared_neurons=C, pooling=pooling, dtype=dtype, device=dev,
                                      seed=0, weight_layout="packed", plan=PhysicalPlan(reduction=red))
             lay.enable_main_grad()
-            opt = FusedAdamW([lay.weight, lay.bias], lr=1e-3, betas=(0.9, 0.999), eps=1e-8, moments="fp32")
+            # fp32 layers: fp32 moments; bf16 layers: the reference's optimizer defaults (bf16 moments,
+            # stochastic rounding of the parameters)
+            opt = FusedAdamW([lay.weight, lay.bias], lr=1e-3, betas=(0.9, 0.999), eps=1e-8,
+                             moments="fp32" if dt == "f32" else "bf16")
             gen = torch.Generator(device=dev).manual_seed(C)
             x = torch.randn(Bm, Dm, device=dev, generator=gen)
             dy = torch.randn(Bm, Gm, device=dev, generator=gen)
@@ -513,16 +521,19 @@ def bench_modeb(args):
                 setattr(_native, bwd_name, orig["bwd"])
             launches += _native.launch_count() - n0
             ms = s_ev.elapsed_time(e_ev) / steps
-            rows.append({"pool": pool, "C": C, "reduction": red, "steps": steps, "ms_per_step": ms,
+            rows.append({"pool": pool, "C": C, "reduction": red, "params": dt, "steps": steps, "ms_per_step": ms,
                          "neuron_samples_per_s": Bm * Hm / (ms / 1e3),
                          "fwd_ms": statistics.mean(a.elapsed_time(b) for a, b in ev["fwd"]),
                          "bwd_ms": statistics.mean(a.elapsed_time(b) for a, b in ev["bwd"]),
                          "fwd_tflops": 2 * 8 * Hm * Bm / (statistics.mean(a.elapsed_time(b) for a, b in ev["fwd"])
                                                           * 1e-3) / 1e12,
                          "published_rtx3090_bf16_ms": MB_PUBLISHED_MS[(pool, C)] if red == "fast" else None})
+            if dt == "bf16":
+                rows[-1]["published_rtx3090_bf16_ms"] = MB_PUBLISHED_MS[(pool, C)]
             del lay, opt
             torch.cuda.empty_cache()
-    head = next(r for r in rows if r["pool"] == "mean" and r["C"] == 64 and r["reduction"] == "fast")
+    head = next(r for r in rows if r["pool"] == "mean" and r["C"] == 64 and r["reduction"] == "fast"
+                and r["params"] == "f32")
     line = {
         "metric": MB_METRIC, "value": head["neuron_samples_per_s"], "unit": UNIT, "n_gpus": 1,
         "steps": head["steps"], "warmup": max(3, args.warmup), "ms_per_step": head["ms_per_step"],

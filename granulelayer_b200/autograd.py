@@ -116,6 +116,7 @@ class Level1Runtime:
                          level.type, _native.POOL_MEAN)
         self.k = level.k if level.type == "topk_mean" else 1   # slots per (token, group) of the event pools
         self.param = kernel_param(level)
+        self.param_dtype = torch.float32   # storage type of w and b (set by the layer)
         self.act = _native.ACT_IDS[level.activation]
         self.last_info: Dict = {}
         self.det = False
@@ -160,10 +161,10 @@ class Level1Runtime:
     def locality(self):
         """(lidx, fmap, nfeat) when every group reads at most a quarter of the input features (the
         kernels then stage only each group's features), else None.  Built once per index tensor.
-        The smooth pools (LogMeanExp, power mean, softmax-weighted) and top-K run on the full-row
-        staging."""
+        The smooth pools (LogMeanExp, power mean, softmax-weighted), top-K and bf16 storage run on the
+        full-row staging."""
         if (self.plan.b200_locality == "off" or self.layout.shared_indices or not self.idx.is_cuda
-                or self.smooth or self.pool == _native.POOL_TOPK):
+                or self.smooth or self.pool == _native.POOL_TOPK or self.param_dtype != torch.float32):
             return None
         G, D, NB = self.groups, self.layout.input_dim, self.layout.blocks_per_group
         if G == 0 or G > 65535 or D < 256:

@@ -100,12 +100,11 @@ struct BwdParams {
   const float* c3;
   float param;
   int ipm1;         // integer code of the power mean's p - 1 (-1: general)
-  bool wbf;         // w and b stored as bf16
 };
 
 // FIXED = false: fp32 tile.  FIXED = true: int32 tile + fp32 fold tile.  LOCAL: one group per block,
 // tiles over the group's feature map only (rows = its features, records read as positions).
-template <int T, int ACT, bool FIXED, bool LOCAL, bool SMOOTH>
+template <int T, int ACT, bool FIXED, bool LOCAL, bool SMOOTH, bool BF>
 __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const BwdParams p) {
   constexpr int NPW = 32 / T;
   constexpr int NW = kBwdThreads / 32;
@@ -176,8 +175,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const BwdParams p) 
             p.order != nullptr ? min(max(__ldg(p.order + (g - p.g0) * (int64_t)slots + s), 0), slots - 1) : s;
         const int64_t f = fbase + slot;
         const Rec8 r = load_rec8(ridx + f * 8, D - 1);
-        const W8 wr = load_w8_any(p.w, f, p.wbf);
-        float z = load_any(p.bias, f, p.wbf);
+        const W8 wr = load_w8_any(p.w, f, BF);
+        float z = load_any(p.bias, f, BF);
         float xv[8];
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
@@ -265,10 +264,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const BwdParams p) 
 // each rounded up to 16 bytes.
 static int64_t bwd_smem(int64_t D, int T, bool fixed) { return ((D * T + 3) & ~3LL) * 4 * (fixed ? 3 : 2); }
 
-template <int T, int ACT, bool FIXED, bool LOCAL, bool SMOOTH>
+template <int T, int ACT, bool FIXED, bool LOCAL, bool SMOOTH, bool BF>
 static int launch_bwd(const BwdParams& p, int64_t B, cudaStream_t st) {
   const size_t smem = (size_t)bwd_smem(LOCAL ? p.lm.fcap : p.D, T, FIXED);
-  auto kern = bwd_kernel<T, ACT, FIXED, LOCAL, SMOOTH>;
+  auto kern = bwd_kernel<T, ACT, FIXED, LOCAL, SMOOTH, BF>;
   int rc = ensure_dynamic_smem((const void*)kern, smem);
   if (rc) return rc;
   const int64_t tiles = (B + T - 1) / T;
@@ -282,23 +281,23 @@ static int launch_bwd(const BwdParams& p, int64_t B, cudaStream_t st) {
   return GL_OK;
 }
 
-template <int T, bool FIXED, bool LOCAL, bool SMOOTH>
+template <int T, bool FIXED, bool LOCAL, bool SMOOTH, bool BF>
 static int dispatch_act_bwd(const BwdParams& p, int64_t B, int act, cudaStream_t st) {
   switch (act) {
-    case GL_ACT_IDENTITY: return launch_bwd<T, GL_ACT_IDENTITY, FIXED, LOCAL, SMOOTH>(p, B, st);
-    case GL_ACT_RELU: return launch_bwd<T, GL_ACT_RELU, FIXED, LOCAL, SMOOTH>(p, B, st);
-    case GL_ACT_GELU: return launch_bwd<T, GL_ACT_GELU, FIXED, LOCAL, SMOOTH>(p, B, st);
+    case GL_ACT_IDENTITY: return launch_bwd<T, GL_ACT_IDENTITY, FIXED, LOCAL, SMOOTH, BF>(p, B, st);
+    case GL_ACT_RELU: return launch_bwd<T, GL_ACT_RELU, FIXED, LOCAL, SMOOTH, BF>(p, B, st);
+    case GL_ACT_GELU: return launch_bwd<T, GL_ACT_GELU, FIXED, LOCAL, SMOOTH, BF>(p, B, st);
     default: return GL_ERR_UNSUPPORTED;
   }
 }
 
-template <bool FIXED, bool LOCAL, bool SMOOTH>
+template <bool FIXED, bool LOCAL, bool SMOOTH, bool BF>
 static int dispatch_tokens_bwd(const BwdParams& p, int64_t B, int act, int T, cudaStream_t st) {
   switch (T) {
-    case 8: return dispatch_act_bwd<8, FIXED, LOCAL, SMOOTH>(p, B, act, st);
-    case 4: return dispatch_act_bwd<4, FIXED, LOCAL, SMOOTH>(p, B, act, st);
-    case 2: return dispatch_act_bwd<2, FIXED, LOCAL, SMOOTH>(p, B, act, st);
-    default: return dispatch_act_bwd<1, FIXED, LOCAL, SMOOTH>(p, B, act, st);
+    case 8: return dispatch_act_bwd<8, FIXED, LOCAL, SMOOTH, BF>(p, B, act, st);
+    case 4: return dispatch_act_bwd<4, FIXED, LOCAL, SMOOTH, BF>(p, B, act, st);
+    case 2: return dispatch_act_bwd<2, FIXED, LOCAL, SMOOTH, BF>(p, B, act, st);
+    default: return dispatch_act_bwd<1, FIXED, LOCAL, SMOOTH, BF>(p, B, act, st);
   }
 }
 
@@ -377,14 +376,20 @@ extern "C" int gl_bwd_f32(const GlBwdArgs* args, void* stream) {
   BwdParams p{a.x, a.idx, a.w, a.b, a.counts, a.gpre, a.dx, a.dw, a.db, a.wabsmax, a.rowmax, a.order,
               LocalMap{a.lidx, a.fmap, a.nfeat, (int)a.fcap}, (int)a.B, (int)a.D,
               a.NB, a.g0, a.g1, a.ldx, a.ldg, a.lddx, a.pool, gpc, a.c2, a.c3, a.param,
-              pow_code(a.param) >= 1 ? pow_code(a.param) - 1 : -1, a.wdtype == GL_DTYPE_BF16};
+              pow_code(a.param) >= 1 ? pow_code(a.param) - 1 : -1};
   cudaStream_t st = (cudaStream_t)stream;
+  if (a.wdtype == GL_DTYPE_BF16) {  // bf16 storage: compiled for the full-row staging
+    if (local) return GL_ERR_UNSUPPORTED;
+    if (smooth) return dispatch_tokens_bwd<false, false, true, true>(p, a.B, a.act, T, st);
+    return fixed ? dispatch_tokens_bwd<true, false, false, true>(p, a.B, a.act, T, st)
+                 : dispatch_tokens_bwd<false, false, false, true>(p, a.B, a.act, T, st);
+  }
   if (smooth)
-    return local ? dispatch_tokens_bwd<false, true, true>(p, a.B, a.act, T, st)
-                 : dispatch_tokens_bwd<false, false, true>(p, a.B, a.act, T, st);
+    return local ? dispatch_tokens_bwd<false, true, true, false>(p, a.B, a.act, T, st)
+                 : dispatch_tokens_bwd<false, false, true, false>(p, a.B, a.act, T, st);
   if (local)
-    return fixed ? dispatch_tokens_bwd<true, true, false>(p, a.B, a.act, T, st)
-                 : dispatch_tokens_bwd<false, true, false>(p, a.B, a.act, T, st);
-  return fixed ? dispatch_tokens_bwd<true, false, false>(p, a.B, a.act, T, st)
-               : dispatch_tokens_bwd<false, false, false>(p, a.B, a.act, T, st);
+    return fixed ? dispatch_tokens_bwd<true, true, false, false>(p, a.B, a.act, T, st)
+                 : dispatch_tokens_bwd<false, true, false, false>(p, a.B, a.act, T, st);
+  return fixed ? dispatch_tokens_bwd<true, false, false, false>(p, a.B, a.act, T, st)
+               : dispatch_tokens_bwd<false, false, false, false>(p, a.B, a.act, T, st);
 }

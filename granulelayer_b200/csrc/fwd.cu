@@ -30,14 +30,14 @@ constexpr int kFwdThreads = 512;
 // valid slots; winner = the smallest slot attaining it, kernels/triton_fused.py:129-140, written to
 // `winners`); PK_LSE LogMeanExp / softmax-weighted and PK_POW power mean (their log2-normaliser
 // written to `stat`).
-template <int T, int ACT, bool LOCAL, int PK>
+template <int T, int ACT, bool LOCAL, int PK, bool BF>
 __global__ void __launch_bounds__(kFwdThreads, 1)
     fwd_kernel(const float* __restrict__ x, const int16_t* __restrict__ idx, const float* __restrict__ w,
                const float* __restrict__ bias, const int32_t* __restrict__ counts, float* __restrict__ pre,
                int B, int D, int64_t NB, int64_t g0, int64_t g1, int64_t ldx, int64_t ldp, int pool, int gpc,
                float* __restrict__ wabsmax, const int32_t* __restrict__ order, const LocalMap lm,
                int32_t* __restrict__ winners, int64_t ldwin, float* __restrict__ stat, int64_t ldstat,
-               const PoolParam pp, const bool wbf) {
+               const PoolParam pp) {
   constexpr bool MAXP = PK == PK_MAX;
   constexpr bool SM = PK == PK_LSE || PK == PK_POW;  // three-word states
   constexpr bool TK = PK == PK_TOPK || PK == PK_TOPK64;
@@ -114,8 +114,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         const int64_t f = fbase + slot;
         sl[u] = slot;
         r[u] = load_rec8(ridx + f * 8, dmax);
-        wr[u] = load_w8_any(w, f, wbf);
-        bb[u] = load_any(bias, f, wbf);
+        wr[u] = load_w8_any(w, f, BF);
+        bb[u] = load_any(bias, f, BF);
       }
 #pragma unroll
       for (int u = 0; u < UNR; ++u) {
@@ -299,10 +299,10 @@ static size_t fwd_smem(int64_t rows, int T, int pool, int k) {
   return tile + (size_t)(kFwdThreads / 32) * T * (k > 32 ? 64 : 32) * sizeof(long long);
 }
 
-template <int T, int ACT, bool LOCAL, int PK>
+template <int T, int ACT, bool LOCAL, int PK, bool BF>
 static int launch_fwd(const GlFwdArgs& a, int gpc, cudaStream_t st) {
   const size_t smem = fwd_smem(LOCAL ? a.fcap : a.D, T, a.pool, a.k);
-  auto kern = fwd_kernel<T, ACT, LOCAL, PK>;
+  auto kern = fwd_kernel<T, ACT, LOCAL, PK, BF>;
   int rc = ensure_dynamic_smem((const void*)kern, smem);
   if (rc) return rc;
   const int64_t tiles = (a.B + T - 1) / T;
@@ -313,44 +313,53 @@ static int launch_fwd(const GlFwdArgs& a, int gpc, cudaStream_t st) {
   kern<<<grid, kFwdThreads, smem, st>>>(a.x, a.idx, a.w, a.b, a.counts, a.pre, (int)a.B, (int)a.D, a.NB, a.g0,
                                         a.g1, a.ldx, a.ldp, a.pool, gpc, a.wabsmax, a.order, lm, a.winners, a.ldwin,
                                         a.stat, a.ldstat, PoolParam{a.param, pow_code(a.param),
-                                                                    a.pool == GL_POOL_SOFTMAX, a.k},
-                                        a.wdtype == GL_DTYPE_BF16);
+                                                                    a.pool == GL_POOL_SOFTMAX, a.k});
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_cuda_error(e);
   count_launches(1);
   return GL_OK;
 }
 
-template <int T, bool LOCAL, int PK>
+template <int T, bool LOCAL, int PK, bool BF>
 static int dispatch_act_fwd2(const GlFwdArgs& a, int gpc, cudaStream_t st) {
   switch (a.act) {
-    case GL_ACT_IDENTITY: return launch_fwd<T, GL_ACT_IDENTITY, LOCAL, PK>(a, gpc, st);
-    case GL_ACT_RELU: return launch_fwd<T, GL_ACT_RELU, LOCAL, PK>(a, gpc, st);
-    case GL_ACT_GELU: return launch_fwd<T, GL_ACT_GELU, LOCAL, PK>(a, gpc, st);
+    case GL_ACT_IDENTITY: return launch_fwd<T, GL_ACT_IDENTITY, LOCAL, PK, BF>(a, gpc, st);
+    case GL_ACT_RELU: return launch_fwd<T, GL_ACT_RELU, LOCAL, PK, BF>(a, gpc, st);
+    case GL_ACT_GELU: return launch_fwd<T, GL_ACT_GELU, LOCAL, PK, BF>(a, gpc, st);
     default: return GL_ERR_UNSUPPORTED;
   }
 }
 
-// The smooth pools (LSE, POW kinds) and top-K run on the full-row staging only (no locality maps);
-// top-K tiles hold at most 4 tokens (its lists live in registers).
-template <int T, bool LOCAL>
-static int dispatch_act_fwd(const GlFwdArgs& a, int gpc, cudaStream_t st) {
+template <int T, bool LOCAL, bool BF>
+static int dispatch_pk_fwd(const GlFwdArgs& a, int gpc, cudaStream_t st) {
   switch (pool_kind(a.pool, a.k)) {
-    case PK_MAX: return dispatch_act_fwd2<T, LOCAL, PK_MAX>(a, gpc, st);
+    case PK_MAX: return dispatch_act_fwd2<T, LOCAL, PK_MAX, BF>(a, gpc, st);
     case PK_TOPK:
       if constexpr (LOCAL || T > 4) return GL_ERR_UNSUPPORTED;
-      else return dispatch_act_fwd2<T, false, PK_TOPK>(a, gpc, st);
+      else return dispatch_act_fwd2<T, false, PK_TOPK, BF>(a, gpc, st);
     case PK_TOPK64:
       if constexpr (LOCAL || T > 4) return GL_ERR_UNSUPPORTED;
-      else return dispatch_act_fwd2<T, false, PK_TOPK64>(a, gpc, st);
+      else return dispatch_act_fwd2<T, false, PK_TOPK64, BF>(a, gpc, st);
     case PK_LSE:
       if constexpr (LOCAL) return GL_ERR_UNSUPPORTED;
-      else return dispatch_act_fwd2<T, false, PK_LSE>(a, gpc, st);
+      else return dispatch_act_fwd2<T, false, PK_LSE, BF>(a, gpc, st);
     case PK_POW:
       if constexpr (LOCAL) return GL_ERR_UNSUPPORTED;
-      else return dispatch_act_fwd2<T, false, PK_POW>(a, gpc, st);
-    default: return dispatch_act_fwd2<T, LOCAL, PK_ADD>(a, gpc, st);
+      else return dispatch_act_fwd2<T, false, PK_POW, BF>(a, gpc, st);
+    default: return dispatch_act_fwd2<T, LOCAL, PK_ADD, BF>(a, gpc, st);
   }
+}
+
+// The smooth pools (LSE, POW kinds) and top-K run on the full-row staging only (no locality maps);
+// top-K tiles hold at most 4 tokens (its lists live in registers).  bf16 storage is compiled for
+// the full-row staging (the storage type is a template parameter: no per-load branch).
+template <int T, bool LOCAL>
+static int dispatch_act_fwd(const GlFwdArgs& a, int gpc, cudaStream_t st) {
+  if (a.wdtype == GL_DTYPE_BF16) {
+    if constexpr (LOCAL) return GL_ERR_UNSUPPORTED;
+    else return dispatch_pk_fwd<T, false, true>(a, gpc, st);
+  }
+  return dispatch_pk_fwd<T, LOCAL, false>(a, gpc, st);
 }
 
 // Bound on the forward kernel's static shared memory (its reduction buffers).

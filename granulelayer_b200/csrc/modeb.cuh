@@ -48,19 +48,19 @@ __device__ __forceinline__ Rec8 mb_load_rec(const MbParams& p, int64_t g, int j)
   }
 }
 
-// Weights and bias of neurons c0 .. c0+3 of block j.
-template <bool PACKED>
-__device__ __forceinline__ void mb_load_w4(const MbParams& p, int64_t g, int j, int c0, float (&w)[4][8],
-                                           float (&bb)[4]) {
+// Weights and bias of neurons c0 .. c0+3 of block j, from fp32 or bf16 storage (BF).
+template <bool PACKED, bool BF>
+__device__ __forceinline__ void mb_load_w4_t(const MbParams& p, int64_t g, int j, int c0, float (&w)[4][8],
+                                             float (&bb)[4]) {
   if constexpr (!PACKED) {
     const int64_t base = ((g * p.NB + j) * p.C + c0) * 8;
 #pragma unroll
     for (int n = 0; n < 4; ++n) {
-      const float4 a = load4_any(p.w, base + 8 * n, p.wbf), c = load4_any(p.w, base + 8 * n + 4, p.wbf);
+      const float4 a = load4_any(p.w, base + 8 * n, BF), c = load4_any(p.w, base + 8 * n + 4, BF);
       w[n][0] = a.x; w[n][1] = a.y; w[n][2] = a.z; w[n][3] = a.w;
       w[n][4] = c.x; w[n][5] = c.y; w[n][6] = c.z; w[n][7] = c.w;
     }
-    const float4 b4 = load4_any(p.b, (g * p.NB + j) * p.C + c0, p.wbf);
+    const float4 b4 = load4_any(p.b, (g * p.NB + j) * p.C + c0, BF);
     bb[0] = b4.x; bb[1] = b4.y; bb[2] = b4.z; bb[3] = b4.w;
   } else {
     const MbPacked m = mb_packed(p.C, p.NB);
@@ -68,14 +68,22 @@ __device__ __forceinline__ void mb_load_w4(const MbParams& p, int64_t g, int j, 
     for (int n = 0; n < 4; ++n)
 #pragma unroll
       for (int kh = 0; kh < 4; ++kh) {
-        const float2 v = load2_any(p.w, mb_packed_w(m, g, j, c0 + n, kh), p.wbf);
+        const float2 v = load2_any(p.w, mb_packed_w(m, g, j, c0 + n, kh), BF);
         w[n][2 * kh] = v.x;
         w[n][2 * kh + 1] = v.y;
       }
-    const float2 b0 = load2_any(p.b, mb_packed_b(m, g, j, c0), p.wbf);
-    const float2 b1 = load2_any(p.b, mb_packed_b(m, g, j, c0 + 2), p.wbf);
+    const float2 b0 = load2_any(p.b, mb_packed_b(m, g, j, c0), BF);
+    const float2 b1 = load2_any(p.b, mb_packed_b(m, g, j, c0 + 2), BF);
     bb[0] = b0.x; bb[1] = b0.y; bb[2] = b1.x; bb[3] = b1.y;
   }
+}
+
+// The storage type is uniform over the launch: one branch per record, around all of its loads.
+template <bool PACKED>
+__device__ __forceinline__ void mb_load_w4(const MbParams& p, int64_t g, int j, int c0, float (&w)[4][8],
+                                           float (&bb)[4]) {
+  if (p.wbf) mb_load_w4_t<PACKED, true>(p, g, j, c0, w, bb);
+  else mb_load_w4_t<PACKED, false>(p, g, j, c0, w, bb);
 }
 
 // Row strides of the shared tiles.  Rows of 32 or more bytes start every row on the same banks
@@ -142,9 +150,9 @@ __device__ __forceinline__ void mb_xor_perm8(V (&v)[8], int km) {
 }
 
 // Weights of neurons c0 .. c0+3 of block j with the k index permuted: w[n][k] = W[c0+n][k ^ km].
-template <bool PACKED>
-__device__ __forceinline__ void mb_load_w4_perm(const MbParams& p, int64_t g, int j, int c0, int km,
-                                                float (&w)[4][8]) {
+template <bool PACKED, bool BF>
+__device__ __forceinline__ void mb_load_w4_perm_t(const MbParams& p, int64_t g, int j, int c0, int km,
+                                                  float (&w)[4][8]) {
   const int khm = km >> 1;
   const bool sw = km & 1;
   const MbPacked m = mb_packed(p.C, p.NB);
@@ -154,10 +162,17 @@ __device__ __forceinline__ void mb_load_w4_perm(const MbParams& p, int64_t g, in
     for (int khp = 0; khp < 4; ++khp) {
       const int kh = khp ^ khm;
       const int64_t off = PACKED ? mb_packed_w(m, g, j, c0 + n, kh) : ((g * p.NB + j) * p.C + c0 + n) * 8 + 2 * kh;
-      const float2 v = load2_any(p.w, off, p.wbf);
+      const float2 v = load2_any(p.w, off, BF);
       w[n][2 * khp] = sw ? v.y : v.x;
       w[n][2 * khp + 1] = sw ? v.x : v.y;
     }
+}
+
+template <bool PACKED>
+__device__ __forceinline__ void mb_load_w4_perm(const MbParams& p, int64_t g, int j, int c0, int km,
+                                                float (&w)[4][8]) {
+  if (p.wbf) mb_load_w4_perm_t<PACKED, true>(p, g, j, c0, km, w);
+  else mb_load_w4_perm_t<PACKED, false>(p, g, j, c0, km, w);
 }
 
 // Dynamic shared memory: the padded x tile, plus the padded dX tile for the backward.

@@ -111,6 +111,7 @@ class SparsePoolingLayer(nn.Module):
             else:
                 self._rt = Level1Runtime(self.layout, self.indices, self.cfg.levels[0], self.plan)
             self._rt_key = key
+        self._rt.param_dtype = self.weight.dtype
         return self._rt
 
     def _load_from_state_dict(self, state_dict, prefix, *args, **kwargs):
