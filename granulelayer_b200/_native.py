@@ -16,7 +16,7 @@ from pathlib import Path
 
 import torch
 
-ABI_VERSION = 10
+ABI_VERSION = 11
 LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libgranule_b200.so"
 
 POOL_MEAN, POOL_SUM, POOL_MAX, POOL_LME, POOL_POWER, POOL_SOFTMAX, POOL_TOPK = 0, 1, 2, 3, 4, 5, 6
@@ -37,8 +37,8 @@ EXPORTS = ("gl_abi_version", "gl_status_string", "gl_last_cuda_error", "gl_fwd_f
            "gl_adam_f32", "gl_group_absmax_f32", "gl_group_index_maxcount", "gl_group_feature_map",
            "gl_group_order", "gl_launch_count",
            "gl_fwd_auto_tokens", "gl_bwd_auto_tokens", "gl_fwd_shared_f32", "gl_bwd_shared_f32", "gl_bwd_events_f32",
-           "gl_shared_auto_tokens", "gl_bwd_shared_det_f32", "gl_k16_fwd_f32", "gl_k16_bwd_f32",
-           "gl_k16_auto_tokens")
+           "gl_shared_auto_tokens", "gl_bwd_shared_det_f32", "gl_bwd_shared_det_static_f32", "gl_k16_fwd_f32",
+           "gl_k16_bwd_f32", "gl_k16_auto_tokens")
 
 
 class NativeLibraryError(RuntimeError):
@@ -159,6 +159,9 @@ def load(path=None) -> ctypes.CDLL:
         lib.gl_bwd_shared_det_f32.argtypes = [ctypes.POINTER(GlSharedArgs), ctypes.c_void_p, ctypes.c_void_p,
                                               ctypes.c_void_p, ctypes.c_void_p]
         lib.gl_bwd_shared_det_f32.restype = ctypes.c_int
+        lib.gl_bwd_shared_det_static_f32.argtypes = [ctypes.POINTER(GlSharedArgs), ctypes.c_void_p, ctypes.c_void_p,
+                                                     ctypes.c_void_p]
+        lib.gl_bwd_shared_det_static_f32.restype = ctypes.c_int
         lib.gl_k16_auto_tokens.restype = ctypes.c_int
         lib.gl_k16_auto_tokens.argtypes = [ctypes.c_int64, ctypes.c_int64, ctypes.c_int32]
         if path is None:
@@ -293,6 +296,25 @@ def bwd_shared_det(x, idx, w, b, counts, gpre, dx, dw, db, NB: int, C: int, g0: 
     with torch.cuda.device(x.device):
         _check(lib, lib.gl_bwd_shared_det_f32(ctypes.byref(a), _ptr(dxq), _ptr(qscale), _ptr(qinv),
                                               _stream(x.device)), "gl_bwd_shared_det_f32")
+
+
+# Largest B * D the allocation-free deterministic backward accepts (GL_DET_STATIC_MAX_ELEMS).
+DET_STATIC_MAX_ELEMS = 1 << 20
+
+
+def bwd_shared_det_static(x, idx, w, b, counts, gpre, dx, dw, db, NB: int, C: int, g0: int, g1: int, pool: int,
+                          act: int, packed: bool, qscale, qinv):
+    """Allocation-free deterministic Mode-B backward (gl_bwd_shared_det_static_f32): the results of
+    ``bwd_shared_det`` without a caller scratch buffer, for B * D <= ``DET_STATIC_MAX_ELEMS``.  The
+    library's fixed scratch is shared by every call on a device: calls must not overlap on the GPU."""
+    _require_cuda(x, idx, w, b, counts, gpre, dx, dw, db, qscale, qinv)
+    lib = load()
+    a = _shared_args(x, idx, w, b, counts, NB, C, g0, g1, pool, act, packed, 0, 0)
+    a.gpre, a.dx, a.dw, a.db = _ptr(gpre), _ptr(dx), _ptr(dw), _ptr(db)
+    a.ldg, a.lddx = gpre.stride(0), dx.stride(0)
+    with torch.cuda.device(x.device):
+        _check(lib, lib.gl_bwd_shared_det_static_f32(ctypes.byref(a), _ptr(qscale), _ptr(qinv), _stream(x.device)),
+               "gl_bwd_shared_det_static_f32")
 
 
 def bwd_events(x, idx, w, b, winners, coef, dx, dw, db, NB: int, C: int, shared: bool, packed: bool, g0: int,

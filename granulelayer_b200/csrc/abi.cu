@@ -115,6 +115,7 @@ extern "C" const char* gl_status_string(int status) {
     case GL_ERR_SMEM: return "the token tile does not fit in shared memory";
     case GL_ERR_LAUNCH: return "CUDA launch failed";
     case GL_ERR_DEVICE: return "no usable CUDA device";
+    case GL_ERR_CAPACITY: return "the problem exceeds the fixed scratch of the allocation-free entry point";
     default: return "unknown status";
   }
 }

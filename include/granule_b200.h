@@ -44,7 +44,7 @@
 extern "C" {
 #endif
 
-#define GL_ABI_VERSION 10
+#define GL_ABI_VERSION 11
 
 typedef enum GlStatus {
   GL_OK = 0,
@@ -54,7 +54,8 @@ typedef enum GlStatus {
   GL_ERR_UNSUPPORTED = -4,   /* pool/activation/tile combination not built */
   GL_ERR_SMEM = -5,          /* the tile does not fit in shared memory */
   GL_ERR_LAUNCH = -6,        /* the CUDA launch failed (see gl_last_cuda_error) */
-  GL_ERR_DEVICE = -7         /* no usable device / attribute query failed */
+  GL_ERR_DEVICE = -7,        /* no usable device / attribute query failed */
+  GL_ERR_CAPACITY = -8       /* the problem is larger than an allocation-free entry point's fixed scratch */
 } GlStatus;
 
 /* Pool ids: the reference's operators (sparse_pooling/config.py:22-29) and the "sum"
@@ -282,6 +283,19 @@ int gl_shared_auto_tokens(int64_t D, int32_t backward);
  * finite, which makes its dx NaN). */
 int gl_bwd_shared_det_f32(const GlSharedArgs* args, int64_t* dxq, const float* qscale, const float* qinv,
                           void* stream);
+
+/* Allocation-free deterministic Mode-B backward (no counterpart in the reference): the same
+ * computation and results as gl_bwd_shared_det_f32, for callers that cannot allocate device memory
+ * where the backward runs (a plugin whose host framework owns all device memory through its own
+ * pool, or a loop that cannot afford cudaMalloc's possible device synchronisation).  The int64 dX
+ * scratch lives in a fixed array inside the library instead of a caller buffer, so B * D must be at
+ * most GL_DET_STATIC_MAX_ELEMS (8 MiB of int64; larger problems return GL_ERR_CAPACITY); every
+ * device that loads the library holds that array until exit.  The first call on a device looks up
+ * the array's device address (make it before any stream capture); each call clears the entries it
+ * uses on `stream` first.  All calls on one device share the array: calls whose GPU work can overlap
+ * race on it.  Calls no cudaMalloc, cudaFree or allocating library routine. */
+#define GL_DET_STATIC_MAX_ELEMS (1 << 20)
+int gl_bwd_shared_det_static_f32(const GlSharedArgs* args, const float* qscale, const float* qinv, void* stream);
 
 /* Winner-event backward of max and top-K pooling, Mode A or Mode B (replaces
  * kernels/triton_fused.py:476-520 bwd_events_kernel, launched by kernels/ops.py:281-293).  For each
