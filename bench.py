@@ -47,6 +47,11 @@ stochastic rounding), the precision of the published table.
 ``--impl reference`` times the reference's CPU path (the oracle port: the
 reference's materialising PyTorch path does not fit 100M neurons) on the same
 config, rank 0 only.
+
+``--impl reference-gpu`` (comparator, not part of the driver contract) runs the unmodified
+reference package placed in baseline/_ref on this GPU through its public API: with
+``--workload modeb`` the published table's rows on its BF16 mma.sync CUDA kernels, otherwise
+the headline Mode-A fp32 layer on its Triton kernels.
 """
 from __future__ import annotations
 
@@ -234,6 +239,93 @@ def run_reference(args, rank, world):
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
             "note": "reference CPU path = float64 C oracle restating the reference's algorithm on a bounded "
                     "slice of whole groups; the reference's own PyTorch path materialises [B, H]"}
+    print(json.dumps(line), flush=True)
+
+
+REF_DIR = ROOT / "baseline" / "_ref"
+
+
+def run_reference_gpu(args):
+    """The reference's own GPU path on this GPU, as a comparator (rank 0, 1 GPU): the unmodified
+    package placed in baseline/_ref, driven through its public API (SparsePoolingLayer + FusedAdamW),
+    timed with the same CUDA-event step protocol as our arm.  ``--workload modeb``: the published
+    table's rows (H = 1e8, D = G = 1024, B = 8192, C = 8 / 64, Mean(ReLU) and Max with save_winners,
+    the reference's default BF16 parameters, BF16 x as its bench_end_to_end.py feeds, packed storage,
+    its default backend: the m16n8k8 BF16 mma.sync CUDA kernels, Triton for the event backward).
+    Default workload: the Mode-A fp32 layer of the headline config (its Triton kernels)."""
+    if not (REF_DIR / "sparse_pooling" / "__init__.py").exists():
+        print(json.dumps({"impl": "reference-gpu", "unavailable": "reference package not placed in baseline/_ref"}))
+        return
+    if (REF_DIR / "cache").is_dir():
+        os.environ.setdefault("SPARSE_POOL_CACHE_DIR", str(REF_DIR / "cache"))   # prebuilt sm_100 libraries
+    sys.path.insert(0, str(REF_DIR))
+    from sparse_pooling import SparsePoolingLayer as RefLayer
+    from sparse_pooling.optim import FusedAdamW as RefAdam
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    if args.workload == "modeb":
+        Hm, Dm, Gm, Bm = args.modeb_neurons, 1024, 1024, 8192
+        cases = [(pool, C, torch.bfloat16) for pool, C in (("mean", 8), ("mean", 64), ("max", 8), ("max", 64))]
+        metric, steps = MB_METRIC, max(1, min(args.steps, 5))
+    else:
+        Hm, Dm, Gm, Bm = N, D, G, B
+        cases = [("mean", None, torch.float32)]
+        metric, steps = METRIC, max(1, min(args.steps, 5))
+    rows = []
+    with ClockSampler(dev.index) as clk:
+        for pool, C, dtype in cases:
+            policy = "save_winners" if pool == "max" else "auto"
+            lay = RefLayer(Dm, Hm, Gm, shared_neurons=C, pooling=pool, dtype=dtype, device=dev, seed=0,
+                           checkpoint_policy=policy)
+            lay.enable_main_grad()
+            opt = RefAdam([lay.weight, lay.bias], lr=1e-3, betas=(0.9, 0.999), eps=1e-8,
+                          moments="bf16" if dtype == torch.bfloat16 else "fp32")
+            gen = torch.Generator(device=dev).manual_seed(C or 1)
+            x = torch.randn(Bm, Dm, device=dev, generator=gen).to(dtype)
+            dy = torch.randn(Bm, Gm, device=dev, generator=gen)
+            evs = []
+
+            def step(record):
+                e = [torch.cuda.Event(enable_timing=True) for _ in range(3)] if record else None
+                if e:
+                    e[0].record()
+                y = lay(x.detach().requires_grad_(True))
+                if e:
+                    e[1].record()
+                y.backward(dy.to(y.dtype))
+                if e:
+                    e[2].record()
+                    evs.append(e)
+                opt.step()
+
+            for _ in range(max(3, args.warmup)):
+                step(False)
+            torch.cuda.synchronize(dev)
+            s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s_ev.record()
+            for _ in range(steps):
+                step(True)
+            e_ev.record()
+            torch.cuda.synchronize(dev)
+            ms = s_ev.elapsed_time(e_ev) / steps
+            info = lay.last_info
+            rows.append({"pool": pool, "C": C, "params": "bf16" if dtype == torch.bfloat16 else "f32",
+                         "steps": steps, "ms_per_step": ms, "neuron_samples_per_s": Bm * Hm / (ms / 1e3),
+                         "fwd_ms": statistics.mean(a.elapsed_time(b) for a, b, _ in evs),
+                         "bwd_ms": statistics.mean(b.elapsed_time(c) for _, b, c in evs),
+                         "forward_backend": info.get("forward_backend"),
+                         "backward_backend": info.get("backward_backend"),
+                         "published_rtx3090_bf16_ms": MB_PUBLISHED_MS.get((pool, C))})
+            del lay, opt
+            torch.cuda.empty_cache()
+    head = rows[1] if len(rows) > 1 else rows[0]
+    line = {"impl": "reference-gpu", "metric": metric, "value": head["neuron_samples_per_s"], "unit": UNIT,
+            "n_gpus": 1, "steps": head["steps"], "warmup": max(3, args.warmup), "ms_per_step": head["ms_per_step"],
+            "higher_is_better": True, "data": "synthetic", "device": torch.cuda.get_device_name(dev),
+            "config": {"workload": args.workload, "H": Hm, "D": Dm, "G": Gm, "global_batch": Bm},
+            "rows": rows, "clocks": clk.summary(),
+            "note": "the reference's own GPU kernels (not a B200 build of this repository); comparator only"}
     print(json.dumps(line), flush=True)
 
 
@@ -459,6 +551,12 @@ MB_PUBLISHED_MS = {("mean", 8): 4898.4, ("mean", 64): 2360.8,   # RTX 3090, BF16
                    ("max", 8): 513.2, ("max", 64): 409.9}      # 8, 29): context only
 
 
+# (pool, C, reduction, parameter dtype); bf16 fragment-packed mean / max layers run the tensor-core kernels
+MB_ROWS = (("mean", 8, "fast", "f32"), ("mean", 64, "fast", "f32"), ("max", 8, "fast", "f32"), ("max", 64, "fast", "f32"),
+           ("mean", 8, "deterministic", "f32"), ("mean", 64, "deterministic", "f32"), ("mean", 8, "fast", "bf16"),
+           ("mean", 64, "fast", "bf16"), ("max", 8, "fast", "bf16"), ("max", 64, "fast", "bf16"))
+
+
 def bench_modeb(args):
     """Mode-B step at the published table's configuration (module docstring); rank 0 only."""
     from granulelayer_b200 import FusedAdamW, PhysicalPlan, SparsePoolingLayer, _native
@@ -469,10 +567,9 @@ def bench_modeb(args):
     rows = []
     launches = 0
     with ClockSampler(dev.index) as clk:
-        for pool, C, red, dt in (("mean", 8, "fast", "f32"), ("mean", 64, "fast", "f32"), ("max", 8, "fast", "f32"),
-                                 ("max", 64, "fast", "f32"), ("mean", 8, "deterministic", "f32"),
-                                 ("mean", 64, "deterministic", "f32"), ("mean", 8, "fast", "bf16"),
-                                 ("mean", 64, "fast", "bf16")):
+        for pool, C, red, dt in MB_ROWS:
+            if args.modeb_params and dt not in args.modeb_params.split(","):
+                continue
             pooling = pool   # the operators' default activations: Mean(ReLU), Max(identity)
             dtype = torch.bfloat16 if dt == "bf16" else torch.float32
             lay = SparsePoolingLayer(Dm, Hm, Gm, shared_neurons=C, pooling=pooling, dtype=dtype, device=dev,
@@ -486,8 +583,11 @@ def bench_modeb(args):
             x = torch.randn(Bm, Dm, device=dev, generator=gen)
             dy = torch.randn(Bm, Gm, device=dev, generator=gen)
             ev = {"fwd": [], "bwd": []}
-            bwd_name = "bwd_events" if pool == "max" else ("bwd_shared_det" if red == "deterministic" else "bwd_shared")
-            orig = {"fwd": _native.fwd_shared, "bwd": getattr(_native, bwd_name)}
+            tc = lay._runtime().tensor_cores
+            bwd_name = "bwd_events" if pool == "max" else ("bwd_shared_det" if red == "deterministic" else
+                                                            "bwd_shared_tc" if tc else "bwd_shared")
+            fwd_name = "fwd_shared_tc" if tc else "fwd_shared"
+            orig = {"fwd": getattr(_native, fwd_name), "bwd": getattr(_native, bwd_name)}
 
             def timed(name):
                 def wrap(*a, **k):
@@ -505,7 +605,7 @@ def bench_modeb(args):
             for _ in range(max(3, args.warmup)):
                 step()
             torch.cuda.synchronize(dev)
-            _native.fwd_shared = timed("fwd")
+            setattr(_native, fwd_name, timed("fwd"))
             setattr(_native, bwd_name, timed("bwd"))
             n0 = _native.launch_count()
             steps = max(1, min(args.steps, 5))
@@ -517,11 +617,12 @@ def bench_modeb(args):
                 e_ev.record()
                 torch.cuda.synchronize(dev)
             finally:
-                _native.fwd_shared = orig["fwd"]
+                setattr(_native, fwd_name, orig["fwd"])
                 setattr(_native, bwd_name, orig["bwd"])
             launches += _native.launch_count() - n0
             ms = s_ev.elapsed_time(e_ev) / steps
-            rows.append({"pool": pool, "C": C, "reduction": red, "params": dt, "steps": steps, "ms_per_step": ms,
+            rows.append({"pool": pool, "C": C, "reduction": red, "params": dt, "forward": fwd_name, "backward": bwd_name,
+                         "steps": steps, "ms_per_step": ms,
                          "neuron_samples_per_s": Bm * Hm / (ms / 1e3),
                          "fwd_ms": statistics.mean(a.elapsed_time(b) for a, b in ev["fwd"]),
                          "bwd_ms": statistics.mean(a.elapsed_time(b) for a, b in ev["bwd"]),
@@ -532,8 +633,8 @@ def bench_modeb(args):
                 rows[-1]["published_rtx3090_bf16_ms"] = MB_PUBLISHED_MS[(pool, C)]
             del lay, opt
             torch.cuda.empty_cache()
-    head = next(r for r in rows if r["pool"] == "mean" and r["C"] == 64 and r["reduction"] == "fast"
-                and r["params"] == "f32")
+    head = next((r for r in rows if r["pool"] == "mean" and r["C"] == 64 and r["reduction"] == "fast"
+                 and r["params"] == "f32"), rows[0])
     line = {
         "metric": MB_METRIC, "value": head["neuron_samples_per_s"], "unit": UNIT, "n_gpus": 1,
         "steps": head["steps"], "warmup": max(3, args.warmup), "ms_per_step": head["ms_per_step"],
@@ -621,7 +722,7 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference", "reference-gpu"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ref-seconds", type=float, default=4.0)
@@ -629,6 +730,8 @@ def main():
     ap.add_argument("--batches", default="1,32,256,1024,4096", help="locality: batch sizes of the sweep")
     ap.add_argument("--modeb-neurons", type=int, default=100_000_000,
                     help="modeb: neurons (default 1e8 = the published table; fewer for ncu captures)")
+    ap.add_argument("--modeb-params", default="", help="modeb: only the rows of these parameter dtypes "
+                                                       "(comma list of f32, bf16; default all)")
     ap.add_argument("--cover-outputs", type=int, default=2048,
                     help="cover16: outputs of 24,576 neurons (default 2048 = config 4; fewer for ncu captures)")
     ap.add_argument("--groups", type=int, default=G,
@@ -643,6 +746,10 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference-gpu":
+        if rank == 0:
+            run_reference_gpu(args)
+        return
     if args.workload == "cover16":
         if rank == 0:
             bench_cover16(args, world)

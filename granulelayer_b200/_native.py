@@ -36,7 +36,9 @@ def _wdtype(t) -> int:
 EXPORTS = ("gl_abi_version", "gl_status_string", "gl_last_cuda_error", "gl_fwd_f32", "gl_bwd_f32",
            "gl_adam_f32", "gl_group_absmax_f32", "gl_group_index_maxcount", "gl_group_feature_map",
            "gl_group_order", "gl_launch_count",
-           "gl_fwd_auto_tokens", "gl_bwd_auto_tokens", "gl_fwd_shared_f32", "gl_bwd_shared_f32", "gl_bwd_events_f32",
+           "gl_fwd_auto_tokens", "gl_bwd_auto_tokens", "gl_fwd_shared_f32", "gl_fwd_shared_tc", "gl_bwd_shared_tc", "gl_shared_tc_auto_tokens",
+           "gl_bwd_shared_f32",
+           "gl_bwd_events_f32",
            "gl_shared_auto_tokens", "gl_bwd_shared_det_f32", "gl_bwd_shared_det_static_f32", "gl_k16_fwd_f32",
            "gl_k16_bwd_f32", "gl_k16_auto_tokens")
 
@@ -162,6 +164,11 @@ def load(path=None) -> ctypes.CDLL:
         lib.gl_bwd_shared_det_static_f32.argtypes = [ctypes.POINTER(GlSharedArgs), ctypes.c_void_p, ctypes.c_void_p,
                                                      ctypes.c_void_p]
         lib.gl_bwd_shared_det_static_f32.restype = ctypes.c_int
+        lib.gl_shared_tc_auto_tokens.restype = ctypes.c_int
+        lib.gl_shared_tc_auto_tokens.argtypes = [ctypes.c_int64, ctypes.c_int32]
+        for fn in (lib.gl_fwd_shared_tc, lib.gl_bwd_shared_tc):
+            fn.argtypes = [ctypes.POINTER(GlSharedArgs), ctypes.c_void_p]
+            fn.restype = ctypes.c_int
         lib.gl_k16_auto_tokens.restype = ctypes.c_int
         lib.gl_k16_auto_tokens.argtypes = [ctypes.c_int64, ctypes.c_int64, ctypes.c_int32]
         if path is None:
@@ -262,6 +269,38 @@ def fwd_shared(x, idx, w, b, counts, pre, NB: int, C: int, g0: int, g1: int, poo
         a.stat, a.ldstat = _ptr(stat), stat.stride(0)
     with torch.cuda.device(x.device):
         _check(lib, lib.gl_fwd_shared_f32(ctypes.byref(a), _stream(x.device)), "gl_fwd_shared_f32")
+
+
+def fwd_shared_tc(x, idx, w, b, counts, pre, NB: int, C: int, g0: int, g1: int, pool: int, act: int,
+                  tokens: int = 0, groups_per_cta: int = 0, winners=None):
+    """Mode B, bf16 fragment-packed parameters, on the tensor cores (gl_fwd_shared_tc): pre[:, :g1-g0] =
+    mean / sum / max of act(z) with x rounded to bf16; ``winners`` as in ``fwd``."""
+    _require_cuda(x, idx, w, b, counts, pre, winners)
+    lib = load()
+    a = _shared_args(x, idx, w, b, counts, NB, C, g0, g1, pool, act, True, tokens, groups_per_cta)
+    a.pre, a.ldp = _ptr(pre), pre.stride(0)
+    if winners is not None:
+        a.winners, a.ldwin = _ptr(winners), winners.stride(0)
+    with torch.cuda.device(x.device):
+        _check(lib, lib.gl_fwd_shared_tc(ctypes.byref(a), _stream(x.device)), "gl_fwd_shared_tc")
+
+
+def bwd_shared_tc(x, idx, w, b, counts, gpre, dx, dw, db, NB: int, C: int, g0: int, g1: int, pool: int, act: int,
+                  tokens: int = 0, groups_per_cta: int = 0):
+    """Mode B, bf16 fragment-packed parameters, mean / sum backward on the tensor cores (gl_bwd_shared_tc):
+    dx, dw, db += the gradients for dL/dpre ``gpre`` with x rounded to bf16 and dz in split precision."""
+    _require_cuda(x, idx, w, b, counts, gpre, dx, dw, db)
+    lib = load()
+    a = _shared_args(x, idx, w, b, counts, NB, C, g0, g1, pool, act, True, tokens, groups_per_cta)
+    a.gpre, a.dx, a.dw, a.db = _ptr(gpre), _ptr(dx), _ptr(dw), _ptr(db)
+    a.ldg, a.lddx = gpre.stride(0), dx.stride(0)
+    with torch.cuda.device(x.device):
+        _check(lib, lib.gl_bwd_shared_tc(ctypes.byref(a), _stream(x.device)), "gl_bwd_shared_tc")
+
+
+def shared_tc_tokens(D: int, backward: bool) -> int:
+    """Token tile of the tensor-core kernels for input_dim D, or a negative status when D does not fit."""
+    return load().gl_shared_tc_auto_tokens(D, int(backward))
 
 
 def bwd_shared(x, idx, w, b, counts, gpre, dx, dw, db, NB: int, C: int, g0: int, g1: int, pool: int, act: int,

@@ -126,6 +126,14 @@ class Level1Runtime:
         self._local = None
 
     @property
+    def tensor_cores(self) -> bool:
+        """bf16 fragment-packed Mode-B mean / sum / max layers run the tensor-core kernels, with x rounded
+        to bf16 (the reference's compute dtype for a bf16 layer, autograd.py:349-354)."""
+        return (self.plan.b200_bf16_tensor_cores == "auto" and self.param_dtype == torch.bfloat16
+                and self.layout.shared_indices and self.layout.packed
+                and self.pool in (_native.POOL_MEAN, _native.POOL_SUM, _native.POOL_MAX))
+
+    @property
     def fixed_point(self) -> bool:
         return self.plan.b200_dx_accum in ("auto", "fixed")
 
@@ -316,6 +324,11 @@ class Level1Runtime:
             out["winner"] = winners
         if stat is not None:
             out["L2"] = stat
+        if self.tensor_cores:
+            _native.fwd_shared_tc(x, self.idx, w, b, self.counts_i32, pre, self.layout.blocks_per_group,
+                                  self.layout.block, 0, self.groups, self.pool, self.act, winners=winners)
+            self.last_info.update(forward_backend="b200", forward_kernel="gl_fwd_shared_tc", workspace_bytes=0)
+            return out
         if self.layout.shared_indices:
             _native.fwd_shared(x, self.idx, w, b, self.counts_i32, pre, self.layout.blocks_per_group,
                                self.layout.block, 0, self.groups, self.pool, self.act, self.layout.packed,
@@ -361,6 +374,8 @@ class Level1Runtime:
         self.last_info["policy"] = policy
         self.last_info["recomputed_stats"] = recomputed
         self.check_devices(x, w, b, g_pre, dw_buf, db_buf)
+        if self.tensor_cores:   # the forward computed with x rounded to bf16
+            x = x.to(torch.bfloat16).to(torch.float32)
         self.resolve_reduction(B)
         if self.is_max:
             return self._event_backward(x, w, b, g_pre, saved, dw_buf, db_buf)
@@ -381,6 +396,14 @@ class Level1Runtime:
             self.last_info["backward_backend"] = "b200"
             self.last_info["backward_kernel"] = "gl_bwd_shared_det_f32"
             self.last_info["dx_accumulation"] = "int64 fixed point per token (deterministic)"
+            return dx
+        if (self.tensor_cores and not self.is_max and B > 0
+                and _native.shared_tc_tokens(self.layout.input_dim, True) > 0):
+            _native.bwd_shared_tc(x, self.idx, w, b, self.counts_i32, c1, dx, dw_buf, db_buf,
+                                  self.layout.blocks_per_group, self.layout.block, 0, self.groups, self.pool, self.act)
+            self.last_info["backward_backend"] = "b200"
+            self.last_info["backward_kernel"] = "gl_bwd_shared_tc"
+            self.last_info["dx_accumulation"] = "fp32 shared-memory reductions of tensor-core partials (Mode B)"
             return dx
         if self.layout.shared_indices:
             _native.bwd_shared(x, self.idx, w, b, self.counts_i32, c1, dx, dw_buf, db_buf,

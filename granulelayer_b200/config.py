@@ -265,6 +265,10 @@ class PhysicalPlan:
     # kernels stage only each group's features (gl_group_feature_map, once per index tensor);
     # "off" = always stage the whole input row
     b200_locality: str = "auto"
+    # bf16 Mode-B layers (fragment-packed storage; mean, sum and max pools): "auto" = the tensor-core
+    # kernels with x rounded to bf16, the reference's compute dtype for a bf16 layer; "off" = the fp32
+    # kernels, which read x unrounded and widen the bf16 parameters
+    b200_bf16_tensor_cores: str = "auto"
 
     def __post_init__(self):
         if self.input_layout not in ("feature_major", "token_major"):
@@ -291,6 +295,8 @@ class PhysicalPlan:
             raise ValueError("b200_neuron_order must be 'auto' or 'identity'")
         if self.b200_locality not in ("auto", "off"):
             raise ValueError("b200_locality must be 'auto' or 'off'")
+        if self.b200_bf16_tensor_cores not in ("auto", "off"):
+            raise ValueError("b200_bf16_tensor_cores must be 'auto' or 'off'")
 
 
 def resolve_reduction(plan: PhysicalPlan):

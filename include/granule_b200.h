@@ -268,6 +268,22 @@ typedef struct GlSharedArgs {
 } GlSharedArgs;
 
 int gl_fwd_shared_f32(const GlSharedArgs* args, void* stream);
+/* Mode B with bf16 parameters on the tensor cores (fragment-packed storage, wdtype = GL_DTYPE_BF16),
+ * the reference's bf16 arithmetic (its layers cast x to the layer dtype, sparse_pooling/autograd.py:349-354,
+ * and run m16n8k8 BF16 tiles with fp32 accumulation, kernels/cuda/sparse_pool_fwd.cuh:311): x is rounded
+ * to bf16 (nearest even) as it is staged, every product bf16 x bf16 is exact, sums are fp32.
+ * Forward: pools MEAN, SUM and MAX (winners optional, smallest slot on ties), any activation; `tokens`
+ * = 0 (automatic) or 16, 32, 64.  Other configurations return GL_ERR_UNSUPPORTED. */
+int gl_fwd_shared_tc(const GlSharedArgs* args, void* stream);
+/* Backward of the mean and sum pools on the same path, the reference's default "split" gradient precision
+ * (kernels/cuda/sparse_pool_bwd.cuh:387-876): dz = c1 act'(z) is carried as hi + lo bf16 (16 significant
+ * bits), so dz * w and dz * x are summed in fp32 from exact products; dx, dw, db (fp32, dw / db in the
+ * packed layout) are accumulated as gl_bwd_shared_f32 does.  `tokens` = 0 (automatic), 16 or 32; the
+ * x slab and an fp32 dX tile share the shared memory, so D is bounded (GL_ERR_SMEM beyond). */
+int gl_bwd_shared_tc(const GlSharedArgs* args, void* stream);
+/* Token tile the tensor-core forward (backward = 0) or backward (1) would use for input_dim D, or a
+ * negative status (GL_ERR_SMEM when D does not fit). */
+int gl_shared_tc_auto_tokens(int64_t D, int32_t backward);
 int gl_bwd_shared_f32(const GlSharedArgs* args, void* stream);
 /* Token tile the automatic choice would use for input_dim D, or a negative status. */
 int gl_shared_auto_tokens(int64_t D, int32_t backward);
