@@ -119,6 +119,35 @@ __device__ __forceinline__ void tc_gather(uint32_t (&a)[BM / 16][2], uint32_t sl
   }
 }
 
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void ldsm_x2(uint32_t (&r)[2], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0, %1}, [%2];" : "=r"(r[0]), "=r"(r[1]) : "r"(addr));
+}
+
+// The same rows without the transpose: b[mt][o] is the m16n8k16 B fragment (k = the 8 tokens of octet
+// o of m-tile mt, n = the record's input lane / 4), i.e. x^T of the record's inputs.
+template <int BM>
+__device__ __forceinline__ void tc_gather_nt(uint32_t (&b)[BM / 16][2], uint32_t slab, int row, int lane) {
+  if constexpr (BM == 16) {
+    ldsm_x2(b[0], tc_chunk<BM>(slab, row, (lane >> 3) & 1));
+  } else {
+#pragma unroll
+    for (int h = 0; h < BM / 32; ++h) {
+      uint32_t r[4];
+      ldsm_x4(r, tc_chunk<BM>(slab, row, 4 * h + (lane >> 3)));
+      b[2 * h][0] = r[0];
+      b[2 * h][1] = r[1];
+      b[2 * h + 1][0] = r[2];
+      b[2 * h + 1][1] = r[3];
+    }
+  }
+}
+
 // Operands of fragment quad q of group g (4 n-tiles of 8 neurons = slots 32q .. 32q+31):
 // the lane's B fragments (one per n-tile), its bias pairs (accumulator columns 2 (lane & 3) + {0, 1}),
 // and the quad's index words (lane l < 8 R holds input l / R of the quad's record l % R).
