@@ -16,7 +16,7 @@ from pathlib import Path
 
 import torch
 
-ABI_VERSION = 11
+ABI_VERSION = 12
 LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libgranule_b200.so"
 
 POOL_MEAN, POOL_SUM, POOL_MAX, POOL_LME, POOL_POWER, POOL_SOFTMAX, POOL_TOPK = 0, 1, 2, 3, 4, 5, 6
@@ -166,9 +166,11 @@ def load(path=None) -> ctypes.CDLL:
         lib.gl_bwd_shared_det_static_f32.restype = ctypes.c_int
         lib.gl_shared_tc_auto_tokens.restype = ctypes.c_int
         lib.gl_shared_tc_auto_tokens.argtypes = [ctypes.c_int64, ctypes.c_int32]
-        for fn in (lib.gl_fwd_shared_tc, lib.gl_bwd_shared_tc):
-            fn.argtypes = [ctypes.POINTER(GlSharedArgs), ctypes.c_void_p]
-            fn.restype = ctypes.c_int
+        lib.gl_fwd_shared_tc.argtypes = [ctypes.POINTER(GlSharedArgs), ctypes.c_void_p]
+        lib.gl_fwd_shared_tc.restype = ctypes.c_int
+        lib.gl_bwd_shared_tc.argtypes = [ctypes.POINTER(GlSharedArgs), ctypes.c_void_p, ctypes.c_void_p,
+                                         ctypes.c_void_p]
+        lib.gl_bwd_shared_tc.restype = ctypes.c_int
         lib.gl_k16_auto_tokens.restype = ctypes.c_int
         lib.gl_k16_auto_tokens.argtypes = [ctypes.c_int64, ctypes.c_int64, ctypes.c_int32]
         if path is None:
@@ -286,16 +288,21 @@ def fwd_shared_tc(x, idx, w, b, counts, pre, NB: int, C: int, g0: int, g1: int, 
 
 
 def bwd_shared_tc(x, idx, w, b, counts, gpre, dx, dw, db, NB: int, C: int, g0: int, g1: int, pool: int, act: int,
-                  tokens: int = 0, groups_per_cta: int = 0):
+                  tokens: int = 0, groups_per_cta: int = 0, wabsmax=None, rowmax=None):
     """Mode B, bf16 fragment-packed parameters, mean / sum backward on the tensor cores (gl_bwd_shared_tc):
-    dx, dw, db += the gradients for dL/dpre ``gpre`` with x rounded to bf16 and dz in split precision."""
-    _require_cuda(x, idx, w, b, counts, gpre, dx, dw, db)
+    dx, dw, db += the gradients for dL/dpre ``gpre`` with x rounded to bf16 and dz in split precision.
+    With ``wabsmax`` [g1-g0] fp32 and ``rowmax`` [g1-g0] int32 (both or neither) the dX tile is int32
+    fixed point."""
+    _require_cuda(x, idx, w, b, counts, gpre, dx, dw, db, wabsmax, rowmax)
+    if (wabsmax is None) != (rowmax is None):
+        raise ValueError("wabsmax and rowmax go together")
     lib = load()
     a = _shared_args(x, idx, w, b, counts, NB, C, g0, g1, pool, act, True, tokens, groups_per_cta)
     a.gpre, a.dx, a.dw, a.db = _ptr(gpre), _ptr(dx), _ptr(dw), _ptr(db)
     a.ldg, a.lddx = gpre.stride(0), dx.stride(0)
     with torch.cuda.device(x.device):
-        _check(lib, lib.gl_bwd_shared_tc(ctypes.byref(a), _stream(x.device)), "gl_bwd_shared_tc")
+        _check(lib, lib.gl_bwd_shared_tc(ctypes.byref(a), _ptr(wabsmax), _ptr(rowmax), _stream(x.device)),
+               "gl_bwd_shared_tc")
 
 
 def shared_tc_tokens(D: int, backward: bool) -> int:

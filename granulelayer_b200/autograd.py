@@ -125,6 +125,31 @@ class Level1Runtime:
         self._orders: Dict = {}
         self._local = None
 
+    def record_rowmax(self) -> torch.Tensor:
+        """[G] int32: for each group, the largest number of inputs of its valid Mode-B records (blocks
+        holding a valid slot) on one feature, the bound of the fixed-point dX tile.  Depends only on the
+        indices; computed once per index tensor."""
+        key = (self.idx.data_ptr(), self.idx.shape, self.counts_i32.data_ptr())
+        if getattr(self, "_rec_rowmax_key", None) != key:
+            idx = self.idx
+            if self.layout.packed:   # [G, NB/UB, 8, UB] -> [G, NB, 8]
+                idx = idx.permute(0, 1, 3, 2)
+            G, D, C = idx.shape[0], self.layout.input_dim, self.layout.block
+            idx = idx.reshape(G, -1, 8)
+            NB = idx.shape[1]
+            valid = (torch.arange(NB, device=idx.device) * C)[None, :] < self.counts_i32[:, None]
+            out = torch.zeros(G, device=idx.device, dtype=torch.int32)
+            step = max(1, (1 << 24) // max(1, NB * 8))
+            for a in range(0, G, step):
+                e = min(G, a + step)
+                sub = idx[a:e].long().clamp_(0, D - 1).reshape(e - a, -1)
+                wts = valid[a:e, :, None].expand(e - a, NB, 8).reshape(e - a, -1).to(torch.int32)
+                cnt = torch.zeros(e - a, D, device=idx.device, dtype=torch.int32)
+                cnt.scatter_add_(1, sub, wts)
+                out[a:e] = cnt.amax(1)
+            self._rec_rowmax, self._rec_rowmax_key = out.contiguous(), key
+        return self._rec_rowmax
+
     @property
     def tensor_cores(self) -> bool:
         """bf16 fragment-packed Mode-B mean / sum / max layers run the tensor-core kernels, with x rounded
@@ -399,11 +424,17 @@ class Level1Runtime:
             return dx
         if (self.tensor_cores and not self.is_max and B > 0
                 and _native.shared_tc_tokens(self.layout.input_dim, True) > 0):
+            wabsmax = rowmax = None
+            if self.fixed_point:
+                wabsmax = w.reshape(self.groups, -1).abs().amax(1).float().contiguous()
+                rowmax = self.record_rowmax()
             _native.bwd_shared_tc(x, self.idx, w, b, self.counts_i32, c1, dx, dw_buf, db_buf,
-                                  self.layout.blocks_per_group, self.layout.block, 0, self.groups, self.pool, self.act)
+                                  self.layout.blocks_per_group, self.layout.block, 0, self.groups, self.pool, self.act,
+                                  wabsmax=wabsmax, rowmax=rowmax)
             self.last_info["backward_backend"] = "b200"
             self.last_info["backward_kernel"] = "gl_bwd_shared_tc"
-            self.last_info["dx_accumulation"] = "fp32 shared-memory reductions of tensor-core partials (Mode B)"
+            self.last_info["dx_accumulation"] = ("int32 fixed point" if wabsmax is not None else "fp32 atomics") + \
+                " of tensor-core partials (Mode B)"
             return dx
         if self.layout.shared_indices:
             _native.bwd_shared(x, self.idx, w, b, self.counts_i32, c1, dx, dw_buf, db_buf,

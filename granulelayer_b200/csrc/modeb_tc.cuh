@@ -43,6 +43,8 @@ struct TcParams {
   float* dw;
   float* db;
   int32_t* winners;
+  const float* wabsmax;     // backward, fixed-point dX tile: max |w| per group (g - g0), or NULL
+  const int32_t* rowmax;    // backward, fixed-point dX tile: max record inputs per feature per group
   int B, D, C;
   int64_t NB, g0, g1, ldx, ldp, ldg, lddx, ldwin;
   int pool, gpc;

@@ -67,7 +67,12 @@ __device__ __forceinline__ int dxs_off(int d, int t) {
   return d * BM + (t ^ (d & (BM - 1)));
 }
 
-template <int BM, int NT, int ACT>
+// FIXED: the dX tile holds int32 fixed-point sums (shared int32 atomics run at 2.4x the rate of fp32
+// ones on B200).  Per group and token the partials are scaled by a power of two s with
+// m_g * C * |c1[t, g]| * max|w|_g * max|act'| * s <= 2^30 (m_g = the group's largest number of record
+// inputs on one feature), so no tile word can overflow within the group; the tile is added to dx
+// (times 1 / s) and cleared after every group.  A token with a non-finite bound gets NaN in dx.
+template <int BM, int NT, int ACT, bool FIXED>
 __global__ void __launch_bounds__(kTcBwdThreads, 1) tc_bwd_kernel(const TcParams p) {
   constexpr int MT = BM / 16;
   constexpr int NW = kTcBwdThreads / 32;
@@ -75,6 +80,8 @@ __global__ void __launch_bounds__(kTcBwdThreads, 1) tc_bwd_kernel(const TcParams
   constexpr int NPR = NT < 4 ? NT : 4;        // n-tiles per record within a quad
   extern __shared__ __align__(128) unsigned char tc_smem[];
   float* dxs = reinterpret_cast<float*>(tc_smem + (size_t)p.D * BM * 2);
+  int* dxi = reinterpret_cast<int*>(dxs);  // the same tile, in fixed point
+  __shared__ float qsc[2][FIXED ? BM : 1], qinv[2][FIXED ? BM : 1];  // per-group scales, by group parity
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int t0 = blockIdx.x * BM;
   const uint32_t slab = (uint32_t)__cvta_generic_to_shared(tc_smem);
@@ -89,6 +96,33 @@ __global__ void __launch_bounds__(kTcBwdThreads, 1) tc_bwd_kernel(const TcParams
   for (int64_t g = gb; g < ge; ++g) {
     const int ng = min(p.counts[g], slots);
     const int nq = (ng + 31) >> 5;
+    float sc[MT][2];
+    if constexpr (FIXED) {
+      const int buf = (int)((g - gb) & 1);
+      if (threadIdx.x < BM) {
+        const int t = t0 + threadIdx.x;
+        const float gv = t < p.B ? __ldg(p.gpre + (int64_t)t * p.ldg + (g - p.g0)) : 0.f;
+        const float cv = p.pool == GL_POOL_MEAN ? gv / (float)ng : gv;
+        const float bound = fabsf(cv) * (float)p.C * (float)__ldg(p.rowmax + (g - p.g0)) *
+                            __ldg(p.wabsmax + (g - p.g0)) * (ACT == GL_ACT_GELU ? 1.13f : 1.f);
+        float s_ = 0.f, i_ = 0.f;  // a group without valid slots contributes nothing
+        if (ng == 0) {
+        } else if (!(bound <= 3.0e38f)) {
+          i_ = __int_as_float(0x7fc00000);  // non-finite bound: NaN for the token's dx
+        } else if (bound > 0.f) {
+          const int e = min(max(30 - ilogbf(bound) - 1, -126), 126);
+          s_ = ldexpf(1.f, e);
+          i_ = ldexpf(1.f, -e);
+        }
+        qsc[buf][threadIdx.x] = s_;
+        qinv[buf][threadIdx.x] = i_;
+      }
+      __syncthreads();  // scales visible; the previous group's flush has ended everywhere
+#pragma unroll
+      for (int m = 0; m < MT; ++m)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) sc[m][h] = qsc[buf][16 * m + 8 * h + (lane >> 2)];
+    }
     // c1 of the lane's token rows: 16 m + 8 h + lane / 4
     float c1[MT][2];
 #pragma unroll
@@ -181,8 +215,13 @@ __global__ void __launch_bounds__(kTcBwdThreads, 1) tc_bwd_kernel(const TcParams
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
             const int t = 16 * m + 8 * h + (lane >> 2);
-            atomicAdd(dxs + dxs_off<BM>(f0, t), P[2 * h]);
-            atomicAdd(dxs + dxs_off<BM>(f1, t), P[2 * h + 1]);
+            if constexpr (FIXED) {
+              atomicAdd(dxi + dxs_off<BM>(f0, t), __float2int_rn(P[2 * h] * sc[m][h]));
+              atomicAdd(dxi + dxs_off<BM>(f1, t), __float2int_rn(P[2 * h + 1] * sc[m][h]));
+            } else {
+              atomicAdd(dxs + dxs_off<BM>(f0, t), P[2 * h]);
+              atomicAdd(dxs + dxs_off<BM>(f1, t), P[2 * h + 1]);
+            }
           }
         }
       }
@@ -203,42 +242,62 @@ __global__ void __launch_bounds__(kTcBwdThreads, 1) tc_bwd_kernel(const TcParams
         red_v4(dbp + 4, dba[2][0], dba[2][1], dba[3][0], dba[3][1]);
       }
     }
+    if constexpr (FIXED) {
+      // dx[t0 + t, d] += q / s[t], and clear the tile for the next group
+      const int buf = (int)((g - gb) & 1);
+      __syncthreads();
+      for (int i = threadIdx.x; i < p.D * BM; i += kTcBwdThreads) {
+        const int t = i / p.D, d = i - t * p.D;
+        const int o = dxs_off<BM>(d, t);
+        const int qv = dxi[o];
+        const float inv = qinv[buf][t];
+        if (t0 + t < p.B && (qv != 0 || inv != inv)) atomicAdd(p.dx + (int64_t)(t0 + t) * p.lddx + d, (float)qv * inv);
+        dxi[o] = 0;
+      }
+    }
   }
-  __syncthreads();
-  // dx[t0 + t, d] += tile; consecutive threads take consecutive features of one token row
-  for (int i = threadIdx.x; i < p.D * BM; i += kTcBwdThreads) {
-    const int t = i / p.D, d = i - t * p.D;
-    const float v = dxs[dxs_off<BM>(d, t)];
-    if (t0 + t < p.B && v != 0.f) atomicAdd(p.dx + (int64_t)(t0 + t) * p.lddx + d, v);
+  if constexpr (!FIXED) {
+    __syncthreads();
+    // dx[t0 + t, d] += tile; consecutive threads take consecutive features of one token row
+    for (int i = threadIdx.x; i < p.D * BM; i += kTcBwdThreads) {
+      const int t = i / p.D, d = i - t * p.D;
+      const float v = dxs[dxs_off<BM>(d, t)];
+      if (t0 + t < p.B && v != 0.f) atomicAdd(p.dx + (int64_t)(t0 + t) * p.lddx + d, v);
+    }
   }
 }
 
 static int64_t tc_bwd_smem(int64_t D, int BM) { return D * BM * 2 + D * BM * 4; }
 
-template <int BM, int NT, int ACT>
+template <int BM, int NT, int ACT, bool FIXED>
 static int tc_bwd_launch(const TcParams& p, cudaStream_t st) {
   const size_t smem = (size_t)tc_bwd_smem(p.D, BM);
-  const void* kern = (const void*)tc_bwd_kernel<BM, NT, ACT>;
+  const void* kern = (const void*)tc_bwd_kernel<BM, NT, ACT, FIXED>;
   int rc = ensure_dynamic_smem(kern, smem);
   if (rc) return rc;
   const int64_t tiles = (p.B + BM - 1) / BM;
   const int64_t chunks = (p.g1 - p.g0 + p.gpc - 1) / p.gpc;
   if (tiles > 2147483647LL || chunks > 65535) return GL_ERR_SHAPE;
-  tc_bwd_kernel<BM, NT, ACT><<<dim3((unsigned)tiles, (unsigned)chunks), kTcBwdThreads, smem, st>>>(p);
+  tc_bwd_kernel<BM, NT, ACT, FIXED><<<dim3((unsigned)tiles, (unsigned)chunks), kTcBwdThreads, smem, st>>>(p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_cuda_error(e);
   count_launches(1);
   return GL_OK;
 }
 
-template <int BM, int NT>
-static int tc_bwd_act(const TcParams& p, int act, cudaStream_t st) {
+template <int BM, int NT, bool FIXED>
+static int tc_bwd_act2(const TcParams& p, int act, cudaStream_t st) {
   switch (act) {
-    case GL_ACT_IDENTITY: return tc_bwd_launch<BM, NT, GL_ACT_IDENTITY>(p, st);
-    case GL_ACT_RELU: return tc_bwd_launch<BM, NT, GL_ACT_RELU>(p, st);
-    case GL_ACT_GELU: return tc_bwd_launch<BM, NT, GL_ACT_GELU>(p, st);
+    case GL_ACT_IDENTITY: return tc_bwd_launch<BM, NT, GL_ACT_IDENTITY, FIXED>(p, st);
+    case GL_ACT_RELU: return tc_bwd_launch<BM, NT, GL_ACT_RELU, FIXED>(p, st);
+    case GL_ACT_GELU: return tc_bwd_launch<BM, NT, GL_ACT_GELU, FIXED>(p, st);
     default: return GL_ERR_UNSUPPORTED;
   }
+}
+
+template <int BM, int NT>
+static int tc_bwd_act(const TcParams& p, int act, cudaStream_t st) {
+  return p.wabsmax != nullptr ? tc_bwd_act2<BM, NT, true>(p, act, st) : tc_bwd_act2<BM, NT, false>(p, act, st);
 }
 
 template <int BM>
@@ -265,12 +324,16 @@ int tc_bwd_pick_tokens(int64_t D, int optin) {
 
 using namespace gl;
 
-extern "C" int gl_bwd_shared_tc(const GlSharedArgs* args, void* stream) {
+extern "C" int gl_bwd_shared_tc(const GlSharedArgs* args, const float* wabsmax, const int32_t* rowmax,
+                                void* stream) {
   if (!args) return GL_ERR_NULL;
   const GlSharedArgs& a = *args;
+  if ((wabsmax == nullptr) != (rowmax == nullptr)) return GL_ERR_NULL;
   TcParams p;
   int rc = tc_prepare(a, true, p);
   if (rc) return rc > 0 ? GL_OK : rc;
+  p.wabsmax = wabsmax;
+  p.rowmax = rowmax;
   int optin = 0, sms = 0;
   if ((rc = device_smem_optin(&optin))) return rc;
   if ((rc = device_sm_count(&sms))) return rc;

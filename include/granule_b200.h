@@ -44,7 +44,7 @@
 extern "C" {
 #endif
 
-#define GL_ABI_VERSION 11
+#define GL_ABI_VERSION 12
 
 typedef enum GlStatus {
   GL_OK = 0,
@@ -279,8 +279,12 @@ int gl_fwd_shared_tc(const GlSharedArgs* args, void* stream);
  * (kernels/cuda/sparse_pool_bwd.cuh:387-876): dz = c1 act'(z) is carried as hi + lo bf16 (16 significant
  * bits), so dz * w and dz * x are summed in fp32 from exact products; dx, dw, db (fp32, dw / db in the
  * packed layout) are accumulated as gl_bwd_shared_f32 does.  `tokens` = 0 (automatic), 16 or 32; the
- * x slab and an fp32 dX tile share the shared memory, so D is bounded (GL_ERR_SMEM beyond). */
-int gl_bwd_shared_tc(const GlSharedArgs* args, void* stream);
+ * x slab and a 4-byte dX tile share the shared memory, so D is bounded (GL_ERR_SMEM beyond).
+ * With `wabsmax` ([g1-g0] max |w| over each group's valid slots) and `rowmax` ([g1-g0] the largest number
+ * of valid record inputs of the group on one feature) the dX tile is accumulated in int32 fixed point at
+ * a power-of-two scale per (token, group) with m C |c1| max|w| max|act'| scale <= 2^30 (faster; a token
+ * whose bound is not finite gets NaN); with both NULL it is accumulated with fp32 atomics. */
+int gl_bwd_shared_tc(const GlSharedArgs* args, const float* wabsmax, const int32_t* rowmax, void* stream);
 /* Token tile the tensor-core forward (backward = 0) or backward (1) would use for input_dim D, or a
  * negative status (GL_ERR_SMEM when D does not fit). */
 int gl_shared_tc_auto_tokens(int64_t D, int32_t backward);

@@ -172,26 +172,64 @@ def test_plan_off_keeps_fp32_x():
     assert not torch.equal(y_on, y_off)
 
 
+def _bwd_tc(lay, x, gpre, tokens, fixed, calls=1):
+    L = lay.layout
+    w = lay.weight.detach()
+    rt = lay._runtime()
+    wabsmax = w.reshape(L.groups, -1).abs().amax(1).float().contiguous() if fixed else None
+    rowmax = rt.record_rowmax() if fixed else None
+    dx = torch.zeros(x.shape, device="cuda")
+    dw = torch.zeros(lay.weight.shape, device="cuda")
+    db = torch.zeros(lay.bias.shape, device="cuda")
+    for _ in range(calls):
+        _native.bwd_shared_tc(x, lay.indices, w, lay.bias.detach(), L.counts_tensor("cuda"), gpre, dx, dw, db,
+                              L.blocks_per_group, L.block, 0, L.groups, _native.POOL_MEAN, _native.ACT_IDS["relu"],
+                              tokens=tokens, wabsmax=wabsmax, rowmax=rowmax)
+    torch.cuda.synchronize()
+    return dx.cpu(), dw.cpu(), db.cpu()
+
+
 @pytest.mark.parametrize("C", [8, 64])
-def test_backward_token_tiles_agree(C):
-    """The backward at token tiles 16 and 32 (and through main_grad accumulation) gives the same
-    gradients within the dX tolerance; a second call adds the same amounts again."""
+def test_backward_tiles_and_dx_accumulation_agree(C):
+    """Token tiles 16 and 32, with the fp32-atomic and the int32 fixed-point dX tile, give the same
+    gradients within the dX tolerance; a second call adds the same amounts again (accumulation)."""
     D, H, G, B = 1024, 30000, 5, 50
     lay = _layer(C, "mean", D, H, G, seed=3)
-    L = lay.layout
     gen = torch.Generator().manual_seed(11)
     x = torch.randn(B, D, generator=gen).cuda()
     gpre = torch.randn(B, G, generator=gen).cuda()
-    outs = []
-    for tokens in (16, 32):
-        dx = torch.zeros(B, D, device="cuda")
-        dw = torch.zeros(lay.weight.shape, device="cuda")
-        db = torch.zeros(lay.bias.shape, device="cuda")
-        for _ in range(2):
-            _native.bwd_shared_tc(x, lay.indices, lay.weight.detach(), lay.bias.detach(), L.counts_tensor("cuda"),
-                                  gpre, dx, dw, db, L.blocks_per_group, L.block, 0, L.groups, _native.POOL_MEAN,
-                                  _native.ACT_IDS["relu"], tokens=tokens)
-        torch.cuda.synchronize()
-        outs.append((dx.cpu(), dw.cpu(), db.cpu()))
-    for name, u, v in zip(("dx", "dw", "db"), *outs):
-        assert_close(u, v, what=name, **BWD)
+    ref = _bwd_tc(lay, x, gpre, 32, False)
+    for tokens, fixed in ((16, False), (32, True), (16, True)):
+        out = _bwd_tc(lay, x, gpre, tokens, fixed)
+        for name, u, v in zip(("dx", "dw", "db"), out, ref):
+            assert_close(u, v, what=f"{name} tokens={tokens} fixed={fixed}", **BWD)
+    twice = _bwd_tc(lay, x, gpre, 32, True, calls=2)
+    for name, u, v in zip(("dx", "dw", "db"), twice, ref):
+        assert_close(u, 2 * v, what=f"{name} twice", **BWD)
+
+
+def test_layer_uses_fixed_point_tile_and_fp32_on_request():
+    D, H, G, B = 512, 16000, 4, 20
+    x = torch.randn(B, D, generator=torch.Generator().manual_seed(6)).cuda()
+    for accum, want in (("auto", "int32 fixed point"), ("fp32", "fp32 atomics")):
+        lay = _layer(8, "mean", D, H, G, seed=2, plan=PhysicalPlan(b200_dx_accum=accum))
+        lay(x.clone().requires_grad_(True)).sum().backward()
+        assert lay.last_info["backward_kernel"] == "gl_bwd_shared_tc"
+        assert lay.last_info["dx_accumulation"].startswith(want)
+
+
+def test_fixed_point_nan_token():
+    """A non-finite coefficient makes its token's dx row NaN; the other tokens are unaffected."""
+    D, H, G, B = 512, 16000, 4, 20
+    lay = _layer(8, "mean", D, H, G, seed=5)
+    gen = torch.Generator().manual_seed(7)
+    x = torch.randn(B, D, generator=gen).cuda()
+    gpre = torch.randn(B, G, generator=gen).cuda()
+    clean = _bwd_tc(lay, x, gpre, 32, True)
+    gpre[3, 1] = float("nan")
+    dx, _, _ = _bwd_tc(lay, x, gpre, 32, True)
+    assert torch.isnan(dx[3]).all()
+    keep = torch.arange(B) != 3
+    assert torch.isfinite(dx[keep]).all()
+    # the cross-block fp32 reductions of the fast backward are not bitwise repeatable
+    assert_close(dx[keep], clean[0][keep], what="other tokens", **BWD)
