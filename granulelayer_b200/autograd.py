@@ -399,8 +399,6 @@ class Level1Runtime:
         self.last_info["policy"] = policy
         self.last_info["recomputed_stats"] = recomputed
         self.check_devices(x, w, b, g_pre, dw_buf, db_buf)
-        if self.tensor_cores:   # the forward computed with x rounded to bf16
-            x = x.to(torch.bfloat16).to(torch.float32)
         self.resolve_reduction(B)
         if self.is_max:
             return self._event_backward(x, w, b, g_pre, saved, dw_buf, db_buf)
@@ -462,8 +460,9 @@ class Level1Runtime:
 
 
 def _compute_operands(x, w, b):
-    """The kernels read fp32, unit-stride rows (autograd.py:349-354 casts the same way)."""
-    xc = x.to(torch.float32)
+    """x in the layer's compute dtype, as autograd.py:349-354 casts it (a bf16 layer computes on x rounded
+    to bf16), held as the fp32 unit-stride rows the kernels read (bf16 values widen exactly)."""
+    xc = x.to(w.dtype).to(torch.float32) if w.dtype == torch.bfloat16 else x.to(torch.float32)
     if xc.dim() != 2 or xc.stride(1) != 1:
         xc = xc.contiguous()
     return xc, w.contiguous(), b.contiguous()

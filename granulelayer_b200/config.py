@@ -266,8 +266,8 @@ class PhysicalPlan:
     # "off" = always stage the whole input row
     b200_locality: str = "auto"
     # bf16 Mode-B layers (fragment-packed storage; mean, sum and max pools): "auto" = the tensor-core
-    # kernels with x rounded to bf16, the reference's compute dtype for a bf16 layer; "off" = the fp32
-    # kernels, which read x unrounded and widen the bf16 parameters
+    # kernels; "off" = the fp32 kernels, which widen the bf16 parameters.  Either way a bf16 layer
+    # computes on x rounded to bf16, the reference's compute dtype
     b200_bf16_tensor_cores: str = "auto"
 
     def __post_init__(self):

@@ -1,8 +1,8 @@
 """bf16 parameters (the reference's default layer dtype, layer.py:43) on the GPU: the kernels read
 bf16 weights and biases, compute in fp32 and write fp32 gradients, so a bf16 layer matches the
 float64 oracle evaluated on its exact bf16 values (forward rtol 1e-5 / atol 1e-6; dX, dW, db rtol
-1e-4 / atol 1e-5 on the fp32 main_grad; fragment-packed mean / sum / max layers run the tensor-core
-kernels on x rounded to bf16, and the oracle sees the same rounded x); the fused Adam updates bf16 parameters and moments as the
+1e-4 / atol 1e-5 on the fp32 main_grad; like the reference's, a bf16 layer computes on x rounded to
+bf16 (autograd.py:349-354), and the oracle sees the same rounded x); the fused Adam updates bf16 parameters and moments as the
 reference's optimizer does (optim.py:26-126)."""
 import numpy as np
 import pytest
@@ -55,8 +55,7 @@ def test_bf16_layers_against_oracle(C, packed, pooling):
     kind = pooling if isinstance(pooling, str) else pooling["type"]
     act = lay.cfg.levels[0].activation
     xn, dyn = x.numpy().astype(np.float64), dy.numpy().astype(np.float64)
-    if lay._runtime().tensor_cores:   # packed mean / max: tensor-core kernels on x rounded to bf16
-        xn = x.to(torch.bfloat16).double().numpy()
+    xn = x.to(torch.bfloat16).double().numpy()   # a bf16 layer computes on x rounded to bf16
     if kind == "mean":
         pre = O.forward(xn, idx, w, b, counts, "mean", act)
         odx, odw, odb, sdx, sdw, sdb = O.backward(xn, idx, w, b, counts, dyn, "mean", act, slack=True)
