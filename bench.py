@@ -268,6 +268,10 @@ def run_reference_gpu(args):
         Hm, Dm, Gm, Bm = args.modeb_neurons, 1024, 1024, 8192
         cases = [(pool, C, torch.bfloat16) for pool, C in (("mean", 8), ("mean", 64), ("max", 8), ("max", 64))]
         metric, steps = MB_METRIC, max(1, min(args.steps, 5))
+    elif args.workload == "sets":
+        Hm, Dm, Gm, Bm = args.modeb_neurons, 1024, 1024, 8192
+        cases = [("mean", 64, torch.bfloat16), ("mean", 8, torch.bfloat16)]
+        metric, steps = SETS_METRIC, max(1, min(args.steps, 5))
     else:
         Hm, Dm, Gm, Bm = N, D, G, B
         cases = [("mean", None, torch.float32)]
@@ -276,8 +280,12 @@ def run_reference_gpu(args):
     with ClockSampler(dev.index) as clk:
         for pool, C, dtype in cases:
             policy = "save_winners" if pool == "max" else "auto"
+            extra = {}
+            if args.workload == "sets":
+                from sparse_pooling.supergroups import ConnectivityPlan as RefConnectivity
+                extra["connectivity"] = RefConnectivity(64, 16, seed=0)
             lay = RefLayer(Dm, Hm, Gm, shared_neurons=C, pooling=pool, dtype=dtype, device=dev, seed=0,
-                           checkpoint_policy=policy)
+                           checkpoint_policy=policy, **extra)
             lay.enable_main_grad()
             opt = RefAdam([lay.weight, lay.bias], lr=1e-3, betas=(0.9, 0.999), eps=1e-8,
                           moments="bf16" if dtype == torch.bfloat16 else "fp32")
@@ -319,7 +327,7 @@ def run_reference_gpu(args):
                          "published_rtx3090_bf16_ms": MB_PUBLISHED_MS.get((pool, C))})
             del lay, opt
             torch.cuda.empty_cache()
-    head = rows[1] if len(rows) > 1 else rows[0]
+    head = rows[1] if len(rows) > 1 and args.workload == "modeb" else rows[0]
     line = {"impl": "reference-gpu", "metric": metric, "value": head["neuron_samples_per_s"], "unit": UNIT,
             "n_gpus": 1, "steps": head["steps"], "warmup": max(3, args.warmup), "ms_per_step": head["ms_per_step"],
             "higher_is_better": True, "data": "synthetic", "device": torch.cuda.get_device_name(dev),
@@ -647,6 +655,79 @@ def bench_modeb(args):
     print(json.dumps(line), flush=True)
 
 
+SETS_METRIC = "neuron-samples/s fwd+bwd+opt, Mode B C=64 with input supergroups S=64 R=16, H=1e8, D=G=1024, B=8192"
+
+
+def bench_sets(args):
+    """bf16 Mode-B layers with input-supergroup connectivity at the reference's supergroup benchmark
+    configuration (its bench_supergroups.py defaults: H = 1e8, D = G = 1024, B = 8192, S = 64, R = 16),
+    C = 64 and C = 8, Mean(ReLU), fwd + bwd + fused Adam (bf16 moments): the input-set backward
+    (gl_bwd_shared_tc_sets) against the generic tensor-core backward on the same layer."""
+    from granulelayer_b200 import FusedAdamW, PhysicalPlan, SparsePoolingLayer, _native
+    from granulelayer_b200.supergroups import ConnectivityPlan
+
+    Hm, Dm, Gm, Bm = args.modeb_neurons, 1024, 1024, 8192
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    rows, launches = [], 0
+    with ClockSampler(dev.index) as clk:
+        for C in (64, 8):
+            lay = SparsePoolingLayer(Dm, Hm, Gm, shared_neurons=C, pooling="mean", dtype=torch.bfloat16, device=dev,
+                                     seed=0, weight_layout="packed", connectivity=ConnectivityPlan(64, 16, seed=0))
+            lay.enable_main_grad()
+            opt = FusedAdamW([lay.weight, lay.bias], lr=1e-3, betas=(0.9, 0.999), eps=1e-8, moments="bf16")
+            gen = torch.Generator(device=dev).manual_seed(C)
+            x = torch.randn(Bm, Dm, device=dev, generator=gen)
+            dy = torch.randn(Bm, Gm, device=dev, generator=gen)
+            variants = [("sets", int(t)) for t in args.sets_tokens.split(",")] + [("generic", 0)]
+            for variant, tok in variants:
+                lay.plan = PhysicalPlan(cuda_input_supergroup_backend="auto" if variant == "sets" else "generic",
+                                        b200_dx_tokens=tok)
+                evs = []
+
+                def step(record):
+                    e = [torch.cuda.Event(enable_timing=True) for _ in range(3)] if record else None
+                    if e:
+                        e[0].record()
+                    y = lay(x.detach().requires_grad_(True))
+                    if e:
+                        e[1].record()
+                    y.backward(dy)
+                    if e:
+                        e[2].record()
+                        evs.append(e)
+                    opt.step()
+
+                for _ in range(max(3, args.warmup)):
+                    step(False)
+                torch.cuda.synchronize(dev)
+                n0 = _native.launch_count()
+                steps = max(1, min(args.steps, 5))
+                s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                s_ev.record()
+                for _ in range(steps):
+                    step(True)
+                e_ev.record()
+                torch.cuda.synchronize(dev)
+                launches += _native.launch_count() - n0
+                ms = s_ev.elapsed_time(e_ev) / steps
+                rows.append({"C": C, "variant": variant, "tokens": tok or "auto",
+                             "backward_kernel": lay.last_info.get("backward_kernel"),
+                             "steps": steps, "ms_per_step": ms, "neuron_samples_per_s": Bm * Hm / (ms / 1e3),
+                             "fwd_ms": statistics.mean(a.elapsed_time(b) for a, b, _ in evs),
+                             "bwd_ms": statistics.mean(b.elapsed_time(c) for _, b, c in evs)})
+            del lay, opt
+            torch.cuda.empty_cache()
+    head = rows[0]
+    line = {"metric": SETS_METRIC, "value": head["neuron_samples_per_s"], "unit": UNIT, "n_gpus": 1,
+            "steps": head["steps"], "warmup": max(3, args.warmup), "ms_per_step": head["ms_per_step"],
+            "higher_is_better": True, "scaling": "none", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "bf16 Mode-B Mean(ReLU) layers with input-supergroup connectivity (S=64, R=16), "
+                                   "fwd+bwd+fused Adam", "H": Hm, "D": Dm, "G": Gm, "global_batch": Bm, "C": [64, 8]},
+            "rows": rows, "clocks": clk.summary(), "gpu_launches": launches}
+    print(json.dumps(line), flush=True)
+
+
 LOC_METRIC = ("neuron-samples/s fwd+bwd at B=1024, windowed indices, locality/batch sweep "
               "(D=16384, N=100,663,296, G=8192)")
 
@@ -726,12 +807,15 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ref-seconds", type=float, default=4.0)
-    ap.add_argument("--workload", default="layer100m", choices=["layer100m", "fwdbwd256", "cover16", "locality", "modeb"])
+    ap.add_argument("--workload", default="layer100m",
+                    choices=["layer100m", "fwdbwd256", "cover16", "locality", "modeb", "sets"])
     ap.add_argument("--batches", default="1,32,256,1024,4096", help="locality: batch sizes of the sweep")
     ap.add_argument("--modeb-neurons", type=int, default=100_000_000,
                     help="modeb: neurons (default 1e8 = the published table; fewer for ncu captures)")
     ap.add_argument("--modeb-params", default="", help="modeb: only the rows of these parameter dtypes "
                                                        "(comma list of f32, bf16; default all)")
+    ap.add_argument("--sets-tokens", default="0", help="sets: token tiles of the input-set backward to time "
+                                                      "(comma list; 0 = automatic)")
     ap.add_argument("--cover-outputs", type=int, default=2048,
                     help="cover16: outputs of 24,576 neurons (default 2048 = config 4; fewer for ncu captures)")
     ap.add_argument("--groups", type=int, default=G,
@@ -765,6 +849,10 @@ def main():
     if args.workload == "modeb":
         if rank == 0:
             bench_modeb(args)
+        return
+    if args.workload == "sets":
+        if rank == 0:
+            bench_sets(args)
         return
     if args.impl == "reference":
         run_reference(args, rank, world)

@@ -36,11 +36,18 @@ def _wdtype(t) -> int:
 EXPORTS = ("gl_abi_version", "gl_status_string", "gl_last_cuda_error", "gl_fwd_f32", "gl_bwd_f32",
            "gl_adam_f32", "gl_group_absmax_f32", "gl_group_index_maxcount", "gl_group_feature_map",
            "gl_group_order", "gl_launch_count",
-           "gl_fwd_auto_tokens", "gl_bwd_auto_tokens", "gl_fwd_shared_f32", "gl_fwd_shared_tc", "gl_bwd_shared_tc", "gl_shared_tc_auto_tokens",
+           "gl_fwd_auto_tokens", "gl_bwd_auto_tokens", "gl_fwd_shared_f32", "gl_fwd_shared_tc", "gl_bwd_shared_tc", "gl_bwd_shared_tc_sets",
+           "gl_shared_tc_auto_tokens",
            "gl_bwd_shared_f32",
            "gl_bwd_events_f32",
            "gl_shared_auto_tokens", "gl_bwd_shared_det_f32", "gl_bwd_shared_det_static_f32", "gl_k16_fwd_f32",
            "gl_k16_bwd_f32", "gl_k16_auto_tokens")
+
+
+class GlSetArgs(ctypes.Structure):
+    _fields_ = [("feat", ctypes.c_void_p), ("buckets", ctypes.c_void_p), ("chunks", ctypes.c_void_p),
+                ("rowmax", ctypes.c_void_p), ("wabsmax", ctypes.c_void_p), ("S", ctypes.c_int64),
+                ("nchunks", ctypes.c_int64), ("max_chunk", ctypes.c_int64)]
 
 
 class NativeLibraryError(RuntimeError):
@@ -171,6 +178,8 @@ def load(path=None) -> ctypes.CDLL:
         lib.gl_bwd_shared_tc.argtypes = [ctypes.POINTER(GlSharedArgs), ctypes.c_void_p, ctypes.c_void_p,
                                          ctypes.c_void_p]
         lib.gl_bwd_shared_tc.restype = ctypes.c_int
+        lib.gl_bwd_shared_tc_sets.argtypes = [ctypes.POINTER(GlSharedArgs), ctypes.POINTER(GlSetArgs), ctypes.c_void_p]
+        lib.gl_bwd_shared_tc_sets.restype = ctypes.c_int
         lib.gl_k16_auto_tokens.restype = ctypes.c_int
         lib.gl_k16_auto_tokens.argtypes = [ctypes.c_int64, ctypes.c_int64, ctypes.c_int32]
         if path is None:
@@ -303,6 +312,30 @@ def bwd_shared_tc(x, idx, w, b, counts, gpre, dx, dw, db, NB: int, C: int, g0: i
     with torch.cuda.device(x.device):
         _check(lib, lib.gl_bwd_shared_tc(ctypes.byref(a), _ptr(wabsmax), _ptr(rowmax), _stream(x.device)),
                "gl_bwd_shared_tc")
+
+
+# Largest number of buckets in one chunk of gl_bwd_shared_tc_sets.
+SET_MAX_CHUNK = 256
+
+
+def bwd_shared_tc_sets(x, idx, w, b, counts, gpre, dx, dw, db, NB: int, C: int, g0: int, g1: int, pool: int, act: int,
+                       feat, buckets, chunks, max_chunk: int, rowmax=None, wabsmax=None, tokens: int = 0):
+    """Mode-B mean / sum backward of a bf16 fragment-packed layer with input-supergroup connectivity on the
+    tensor cores, one CTA per token tile and chunk of same-set buckets (gl_bwd_shared_tc_sets): ``feat``
+    [Q, S] int16, ``buckets`` [n, 4] int32, ``chunks`` [m, 3] int32 (set, first bucket, end bucket); with
+    ``rowmax`` [n] int32 and ``wabsmax`` [G] fp32 the dX tile is int32 fixed point."""
+    _require_cuda(x, idx, w, b, counts, gpre, dx, dw, db, feat, buckets, chunks, rowmax, wabsmax)
+    if (rowmax is None) != (wabsmax is None):
+        raise ValueError("rowmax and wabsmax go together")
+    lib = load()
+    a = _shared_args(x, idx, w, b, counts, NB, C, g0, g1, pool, act, True, tokens, 0)
+    a.gpre, a.dx, a.dw, a.db = _ptr(gpre), _ptr(dx), _ptr(dw), _ptr(db)
+    a.ldg, a.lddx = gpre.stride(0), dx.stride(0)
+    sa = GlSetArgs(_ptr(feat), _ptr(buckets), _ptr(chunks), _ptr(rowmax), _ptr(wabsmax), feat.shape[1],
+                   chunks.shape[0], int(max_chunk))
+    with torch.cuda.device(x.device):
+        _check(lib, lib.gl_bwd_shared_tc_sets(ctypes.byref(a), ctypes.byref(sa), _stream(x.device)),
+               "gl_bwd_shared_tc_sets")
 
 
 def shared_tc_tokens(D: int, backward: bool) -> int:

@@ -285,8 +285,8 @@ class PhysicalPlan:
             raise ValueError("deterministic_workspace_bytes must be >= 0")
         for f in ("b200_fwd_tokens", "b200_dx_tokens"):
             v = getattr(self, f)
-            if v and (v & (v - 1) or v > 32):
-                raise ValueError(f"{f} must be 0 or a power of two <= 32")
+            if v and (v & (v - 1) or v > 128):
+                raise ValueError(f"{f} must be 0 or a power of two <= 128 (each kernel documents its own range)")
         if self.b200_dx_splits < 0:
             raise ValueError("b200_dx_splits must be >= 0")
         if self.b200_dx_accum not in ("auto", "fixed", "fp32"):

@@ -112,6 +112,8 @@ class SparsePoolingLayer(nn.Module):
                 self._rt = Level1Runtime(self.layout, self.indices, self.cfg.levels[0], self.plan)
             self._rt_key = key
         self._rt.param_dtype = self.weight.dtype
+        if self.connectivity is not None and not self.cfg.is_semantic_hierarchy:
+            self._rt.sets = (self.sg_feat, self.sg_buckets)
         return self._rt
 
     def _load_from_state_dict(self, state_dict, prefix, *args, **kwargs):

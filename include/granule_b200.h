@@ -285,6 +285,24 @@ int gl_fwd_shared_tc(const GlSharedArgs* args, void* stream);
  * a power-of-two scale per (token, group) with m C |c1| max|w| max|act'| scale <= 2^30 (faster; a token
  * whose bound is not finite gets NaN); with both NULL it is accumulated with fp32 atomics. */
 int gl_bwd_shared_tc(const GlSharedArgs* args, const float* wabsmax, const int32_t* rowmax, void* stream);
+/* The same backward for layers with input-supergroup connectivity (supergroups.py), one CTA per token
+ * tile and chunk of buckets of one input set (replaces the reference's grouped sg_dx / sg_dw kernels,
+ * kernels/cuda/sparse_pool_sg.cuh).  Every record of bucket (q, g, first unit, units) reads only the S
+ * features feat[q], so a CTA stages only those rows and a dX tile of S rows, with a larger token tile
+ * (`tokens` 0 = automatic, 32, 64 or 128).  Buckets of groups outside [g0, g1) are skipped.  With rowmax
+ * ([n] the bucket's largest number of record inputs on one feature) and wabsmax ([g1-g0] max |w| per
+ * group) the dX tile is int32 fixed point at one power-of-two scale per token and chunk; with both NULL
+ * it is fp32. */
+typedef struct GlSetArgs {
+  const int16_t* feat;      /* [Q, S] sorted features of each input set */
+  const int32_t* buckets;   /* [n, 4] int32 (q, g, first unit, units), units of the layout's unit_blocks */
+  const int32_t* chunks;    /* [nchunks, 3] (q, first bucket, end bucket): buckets of set q, at most
+                               max_chunk of them */
+  const int32_t* rowmax;    /* optional [n] */
+  const float* wabsmax;     /* optional [g1-g0] */
+  int64_t S, nchunks, max_chunk;  /* max_chunk <= 256 */
+} GlSetArgs;
+int gl_bwd_shared_tc_sets(const GlSharedArgs* args, const GlSetArgs* sets, void* stream);
 /* Token tile the tensor-core forward (backward = 0) or backward (1) would use for input_dim D, or a
  * negative status (GL_ERR_SMEM when D does not fit). */
 int gl_shared_tc_auto_tokens(int64_t D, int32_t backward);

@@ -12,6 +12,7 @@ import torch
 
 from conftest import assert_close, modeb_as_mode_a
 from granulelayer_b200 import PhysicalPlan, SparsePoolingLayer, _native
+from granulelayer_b200.supergroups import ConnectivityPlan
 from oracle import oracle as O
 from oracle import pool_oracle as P
 
@@ -116,14 +117,11 @@ def test_token_tile_does_not_change_the_output(C, pool):
             assert torch.equal(win, outs[0][1])
 
 
-@pytest.mark.parametrize("C", [8, 16, 32, 64])
-@pytest.mark.parametrize("pooling", ["mean", "sum", "max", {"type": "mean", "activation": "gelu"}])
-@pytest.mark.parametrize("D", [512, 2048])
-def test_layer_gradients_on_rounded_x(C, pooling, D):
-    H, G, B = 24000 - 3 * C - 1, 6, 45
-    lay = _layer(C, pooling, D, H, G, seed=C)
+def _layer_grads_against_oracle(lay, B, seed=5):
+    """Forward + backward of a bf16 layer against the float64 oracle on x rounded to bf16."""
+    D, G = lay.layout.input_dim, lay.layout.groups
     lay.enable_main_grad()
-    gen = torch.Generator().manual_seed(5)
+    gen = torch.Generator().manual_seed(seed)
     x = torch.randn(B, D, generator=gen)
     dy = torch.randn(B, G, generator=gen)
     xg = x.cuda().requires_grad_(True)
@@ -131,12 +129,9 @@ def test_layer_gradients_on_rounded_x(C, pooling, D):
     y.backward(dy.cuda())
     torch.cuda.synchronize()
     assert lay.last_info["forward_kernel"] == "gl_fwd_shared_tc"
-    kind = pooling if isinstance(pooling, str) else pooling["type"]
-    if kind != "max":
-        assert lay.last_info["backward_kernel"] == "gl_bwd_shared_tc"
     L, idx, w, b, counts = _oracle_params(lay)
     xn, dyn = _rounded(x), dy.double().numpy()
-    act = lay.cfg.levels[0].activation
+    kind, act = lay.cfg.levels[0].type, lay.cfg.levels[0].activation
     if kind == "max":
         pre, win = P.max_forward(xn, idx, w, b, counts, act)
         g_pre = dyn * (pre > 0)                                  # default out-activation ReLU
@@ -157,6 +152,58 @@ def test_layer_gradients_on_rounded_x(C, pooling, D):
     assert_close(xg.grad.cpu(), odx, what="dx", slack=sdx, **BWD)
     assert_close(lay.weight.main_grad.cpu(), odw, what="dw", slack=sdw, **BWD)
     assert_close(lay.bias.main_grad.cpu(), odb, what="db", slack=sdb, **BWD)
+
+
+@pytest.mark.parametrize("C", [8, 16, 32, 64])
+@pytest.mark.parametrize("pooling", ["mean", "sum", "max", {"type": "mean", "activation": "gelu"}])
+@pytest.mark.parametrize("D", [512, 2048])
+def test_layer_gradients_on_rounded_x(C, pooling, D):
+    lay = _layer(C, pooling, D, 24000 - 3 * C - 1, 6, seed=C)
+    _layer_grads_against_oracle(lay, 45)
+    kind = pooling if isinstance(pooling, str) else pooling["type"]
+    if kind != "max":
+        assert lay.last_info["backward_kernel"] == "gl_bwd_shared_tc"
+
+
+@pytest.mark.parametrize("C", [8, 16, 64])
+@pytest.mark.parametrize("pooling,accum", [("mean", "auto"), ("sum", "auto"), ("mean", "fp32"),
+                                           ({"type": "mean", "activation": "gelu"}, "auto")])
+@pytest.mark.parametrize("S,R,B", [(64, 4, 45), (128, 2, 150)])
+def test_input_set_backward_against_oracle(C, pooling, accum, S, R, B):
+    """Layers with input-supergroup connectivity run the input-set backward (gl_bwd_shared_tc_sets):
+    a CTA stages only its set's S rows; the gradients match the oracle as the generic kernel's do,
+    with the int32 fixed-point and the fp32 dX tile, over ragged groups and several token tiles."""
+    lay = SparsePoolingLayer(1024, 30000 - 5 * C - 3, 7, shared_neurons=C, weight_layout="packed", pooling=pooling,
+                             dtype=torch.bfloat16, seed=C + S, bias_std=0.2, connectivity=ConnectivityPlan(S, R, seed=3),
+                             plan=PhysicalPlan(b200_dx_accum=accum, cuda_input_supergroup_backend="grouped")).cuda()
+    _layer_grads_against_oracle(lay, B, seed=S)
+    assert lay.last_info["backward_kernel"] == "gl_bwd_shared_tc_sets"
+    assert lay.last_info["dx_accumulation"].startswith("int32" if accum == "auto" else "fp32")
+
+
+@pytest.mark.parametrize("mode", ["generic", "auto"])
+def test_input_set_layers_take_the_generic_kernel_where_it_fits(mode):
+    lay = SparsePoolingLayer(1024, 20000, 5, shared_neurons=8, weight_layout="packed", pooling="mean",
+                             dtype=torch.bfloat16, seed=1, connectivity=ConnectivityPlan(64, 4, seed=3),
+                             plan=PhysicalPlan(cuda_input_supergroup_backend=mode)).cuda()
+    _layer_grads_against_oracle(lay, 33)
+    assert lay.last_info["backward_kernel"] == "gl_bwd_shared_tc"
+
+
+@pytest.mark.parametrize("C", [8, 64])
+def test_large_input_dim_sets_and_fallbacks(C):
+    """D = 4096: the generic tensor-core backward's tiles do not fit, so "auto" runs the input-set
+    backward (S = 256 rows per CTA); the forward still fits its 16-token slab.  Without connectivity
+    the same layer's backward falls back to the fp32 kernels on the rounded x."""
+    D = 4096
+    with_sets = SparsePoolingLayer(D, 40000, 6, shared_neurons=C, weight_layout="packed", pooling="mean",
+                                   dtype=torch.bfloat16, seed=7, bias_std=0.2,
+                                   connectivity=ConnectivityPlan(256, 2, seed=1)).cuda()
+    _layer_grads_against_oracle(with_sets, 40)
+    assert with_sets.last_info["backward_kernel"] == "gl_bwd_shared_tc_sets"
+    plain = _layer(C, "mean", D, 40000, 6, seed=8)
+    _layer_grads_against_oracle(plain, 40)
+    assert plain.last_info["backward_kernel"] == "gl_bwd_shared_f32"
 
 
 def test_plan_off_runs_the_fp32_kernels_on_the_same_rounded_x():
