@@ -666,23 +666,24 @@ def bench_sets(args):
     from granulelayer_b200 import FusedAdamW, PhysicalPlan, SparsePoolingLayer, _native
     from granulelayer_b200.supergroups import ConnectivityPlan
 
-    Hm, Dm, Gm, Bm = args.modeb_neurons, 1024, 1024, 8192
+    Hm, Gm, Bm = args.modeb_neurons, 1024, 8192
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     rows, launches = [], 0
+    # (C, D, S, R): the reference's supergroup benchmark configuration at C = 64 and 8, and a large-D layer
+    # where only the input-set kernel's tiles fit
     with ClockSampler(dev.index) as clk:
-        for C in (64, 8):
+        for C, Dm, S, R in ((64, 1024, 64, 16), (8, 1024, 64, 16), (64, 4096, 256, 4)):
             lay = SparsePoolingLayer(Dm, Hm, Gm, shared_neurons=C, pooling="mean", dtype=torch.bfloat16, device=dev,
-                                     seed=0, weight_layout="packed", connectivity=ConnectivityPlan(64, 16, seed=0))
+                                     seed=0, weight_layout="packed", connectivity=ConnectivityPlan(S, R, seed=0))
             lay.enable_main_grad()
             opt = FusedAdamW([lay.weight, lay.bias], lr=1e-3, betas=(0.9, 0.999), eps=1e-8, moments="bf16")
             gen = torch.Generator(device=dev).manual_seed(C)
             x = torch.randn(Bm, Dm, device=dev, generator=gen)
             dy = torch.randn(Bm, Gm, device=dev, generator=gen)
-            variants = [("sets", int(t)) for t in args.sets_tokens.split(",")] + [("generic", 0)]
+            variants = [("grouped", int(t)) for t in args.sets_tokens.split(",")] + [("generic", 0)]
             for variant, tok in variants:
-                lay.plan = PhysicalPlan(cuda_input_supergroup_backend="auto" if variant == "sets" else "generic",
-                                        b200_dx_tokens=tok)
+                lay.plan = PhysicalPlan(cuda_input_supergroup_backend=variant, b200_dx_tokens=tok)
                 evs = []
 
                 def step(record):
@@ -711,7 +712,7 @@ def bench_sets(args):
                 torch.cuda.synchronize(dev)
                 launches += _native.launch_count() - n0
                 ms = s_ev.elapsed_time(e_ev) / steps
-                rows.append({"C": C, "variant": variant, "tokens": tok or "auto",
+                rows.append({"C": C, "D": Dm, "S": S, "R": R, "variant": variant, "tokens": tok or "auto",
                              "backward_kernel": lay.last_info.get("backward_kernel"),
                              "steps": steps, "ms_per_step": ms, "neuron_samples_per_s": Bm * Hm / (ms / 1e3),
                              "fwd_ms": statistics.mean(a.elapsed_time(b) for a, b, _ in evs),
@@ -722,8 +723,9 @@ def bench_sets(args):
     line = {"metric": SETS_METRIC, "value": head["neuron_samples_per_s"], "unit": UNIT, "n_gpus": 1,
             "steps": head["steps"], "warmup": max(3, args.warmup), "ms_per_step": head["ms_per_step"],
             "higher_is_better": True, "scaling": "none", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "bf16 Mode-B Mean(ReLU) layers with input-supergroup connectivity (S=64, R=16), "
-                                   "fwd+bwd+fused Adam", "H": Hm, "D": Dm, "G": Gm, "global_batch": Bm, "C": [64, 8]},
+            "config": {"workload": "bf16 Mode-B Mean(ReLU) layers with input-supergroup connectivity, "
+                                   "fwd+bwd+fused Adam", "H": Hm, "G": Gm, "global_batch": Bm,
+                       "rows": "(C, D, S, R) = (64, 1024, 64, 16), (8, 1024, 64, 16), (64, 4096, 256, 4)"},
             "rows": rows, "clocks": clk.summary(), "gpu_launches": launches}
     print(json.dumps(line), flush=True)
 
