@@ -37,7 +37,7 @@ EXPORTS = ("gl_abi_version", "gl_status_string", "gl_last_cuda_error", "gl_fwd_f
            "gl_adam_f32", "gl_group_absmax_f32", "gl_group_index_maxcount", "gl_group_feature_map",
            "gl_group_order", "gl_launch_count",
            "gl_fwd_auto_tokens", "gl_bwd_auto_tokens", "gl_fwd_shared_f32", "gl_fwd_shared_tc", "gl_bwd_shared_tc", "gl_bwd_shared_tc_sets",
-           "gl_shared_tc_auto_tokens",
+           "gl_fwd_shared_tc_sets", "gl_shared_tc_auto_tokens",
            "gl_bwd_shared_f32",
            "gl_bwd_events_f32",
            "gl_shared_auto_tokens", "gl_bwd_shared_det_f32", "gl_bwd_shared_det_static_f32", "gl_k16_fwd_f32",
@@ -180,6 +180,8 @@ def load(path=None) -> ctypes.CDLL:
         lib.gl_bwd_shared_tc.restype = ctypes.c_int
         lib.gl_bwd_shared_tc_sets.argtypes = [ctypes.POINTER(GlSharedArgs), ctypes.POINTER(GlSetArgs), ctypes.c_void_p]
         lib.gl_bwd_shared_tc_sets.restype = ctypes.c_int
+        lib.gl_fwd_shared_tc_sets.argtypes = [ctypes.POINTER(GlSharedArgs), ctypes.POINTER(GlSetArgs), ctypes.c_void_p]
+        lib.gl_fwd_shared_tc_sets.restype = ctypes.c_int
         lib.gl_k16_auto_tokens.restype = ctypes.c_int
         lib.gl_k16_auto_tokens.argtypes = [ctypes.c_int64, ctypes.c_int64, ctypes.c_int32]
         if path is None:
@@ -316,6 +318,20 @@ def bwd_shared_tc(x, idx, w, b, counts, gpre, dx, dw, db, NB: int, C: int, g0: i
 
 # Largest number of buckets in one chunk of gl_bwd_shared_tc_sets.
 SET_MAX_CHUNK = 256
+
+
+def fwd_shared_tc_sets(x, idx, w, b, counts, pre, NB: int, C: int, g0: int, g1: int, pool: int, act: int,
+                       feat, buckets, chunks, max_chunk: int, tokens: int = 0):
+    """Mode-B mean / sum forward of a bf16 fragment-packed layer with input-supergroup connectivity on the
+    tensor cores over chunks of same-set buckets (gl_fwd_shared_tc_sets): pre[:, :g1-g0] is written."""
+    _require_cuda(x, idx, w, b, counts, pre, feat, buckets, chunks)
+    lib = load()
+    a = _shared_args(x, idx, w, b, counts, NB, C, g0, g1, pool, act, True, tokens, 0)
+    a.pre, a.ldp = _ptr(pre), pre.stride(0)
+    sa = GlSetArgs(_ptr(feat), _ptr(buckets), _ptr(chunks), 0, 0, feat.shape[1], chunks.shape[0], int(max_chunk))
+    with torch.cuda.device(x.device):
+        _check(lib, lib.gl_fwd_shared_tc_sets(ctypes.byref(a), ctypes.byref(sa), _stream(x.device)),
+               "gl_fwd_shared_tc_sets")
 
 
 def bwd_shared_tc_sets(x, idx, w, b, counts, gpre, dx, dw, db, NB: int, C: int, g0: int, g1: int, pool: int, act: int,

@@ -205,11 +205,11 @@ class Level1Runtime:
                 and self.pool in (_native.POOL_MEAN, _native.POOL_SUM, _native.POOL_MAX)
                 and self.idx.is_cuda and _native.shared_tc_tokens(self.layout.input_dim, False) > 0)
 
-    def input_set_backward(self) -> bool:
-        """Layers with input-supergroup connectivity: the input-set backward runs when requested
-        (cuda_input_supergroup_backend = "grouped") or, under "auto", when the generic tensor-core
-        backward's full-row tiles do not fit in shared memory (large D); at D = 1024 the two measure
-        the same (C = 64) or the generic one is 4% faster (C = 8)."""
+    def input_sets(self) -> bool:
+        """Layers with input-supergroup connectivity: the input-set kernels (forward for mean / sum,
+        backward) run when requested (cuda_input_supergroup_backend = "grouped") or, under "auto", when
+        the generic tensor-core backward's full-row tiles do not fit in shared memory (large D); at
+        D = 1024 the two backwards measure the same (C = 64) or the generic one is 4% faster (C = 8)."""
         mode = self.plan.cuda_input_supergroup_backend
         if self.sets is None or mode == "generic":
             return False
@@ -406,6 +406,13 @@ class Level1Runtime:
             out["winner"] = winners
         if stat is not None:
             out["L2"] = stat
+        if self.tensor_cores and B > 0 and self.pool in (_native.POOL_MEAN, _native.POOL_SUM) and self.input_sets():
+            chunks, largest, _ = self.set_plan()
+            _native.fwd_shared_tc_sets(x, self.idx, w, b, self.counts_i32, pre, self.layout.blocks_per_group,
+                                       self.layout.block, 0, self.groups, self.pool, self.act, self.sets[0],
+                                       self.sets[1], chunks, largest, tokens=self.plan.b200_fwd_tokens)
+            self.last_info.update(forward_backend="b200", forward_kernel="gl_fwd_shared_tc_sets", workspace_bytes=0)
+            return out
         if self.tensor_cores:
             _native.fwd_shared_tc(x, self.idx, w, b, self.counts_i32, pre, self.layout.blocks_per_group,
                                   self.layout.block, 0, self.groups, self.pool, self.act, winners=winners)
@@ -477,7 +484,7 @@ class Level1Runtime:
             self.last_info["backward_kernel"] = "gl_bwd_shared_det_f32"
             self.last_info["dx_accumulation"] = "int64 fixed point per token (deterministic)"
             return dx
-        if self.tensor_cores and not self.is_max and B > 0 and self.input_set_backward():
+        if self.tensor_cores and not self.is_max and B > 0 and self.input_sets():
             chunks, largest, brow = self.set_plan()
             wabsmax = rowmax = None
             if self.fixed_point:

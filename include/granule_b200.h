@@ -303,6 +303,10 @@ typedef struct GlSetArgs {
   int64_t S, nchunks, max_chunk;  /* max_chunk <= 256 */
 } GlSetArgs;
 int gl_bwd_shared_tc_sets(const GlSharedArgs* args, const GlSetArgs* sets, void* stream);
+/* Forward of the mean and sum pools on the same chunks (replaces the reference's grouped sg_fwd): pre is
+ * zeroed (NaN for the mean of a group without valid slots), then every (token, bucket) partial, divided by
+ * the group's count for the mean, is added with one fp32 atomic, so the sum order is not fixed. */
+int gl_fwd_shared_tc_sets(const GlSharedArgs* args, const GlSetArgs* sets, void* stream);
 /* Token tile the tensor-core forward (backward = 0) or backward (1) would use for input_dim D, or a
  * negative status (GL_ERR_SMEM when D does not fit). */
 int gl_shared_tc_auto_tokens(int64_t D, int32_t backward);

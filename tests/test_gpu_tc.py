@@ -128,7 +128,7 @@ def _layer_grads_against_oracle(lay, B, seed=5):
     y = lay(xg)
     y.backward(dy.cuda())
     torch.cuda.synchronize()
-    assert lay.last_info["forward_kernel"] == "gl_fwd_shared_tc"
+    assert lay.last_info["forward_kernel"].startswith("gl_fwd_shared_tc")
     L, idx, w, b, counts = _oracle_params(lay)
     xn, dyn = _rounded(x), dy.double().numpy()
     kind, act = lay.cfg.levels[0].type, lay.cfg.levels[0].activation
@@ -148,7 +148,11 @@ def _layer_grads_against_oracle(lay, B, seed=5):
     if sdw is not None:
         sdw = L.pack_weights(torch.from_numpy(np.asarray(sdw)).reshape(shape_w))
         sdb = L.pack_bias(torch.from_numpy(np.asarray(sdb)).reshape(shape_b))
-    assert_close(y.detach().cpu(), y_ref, what="y", **FWD)
+    yv, yr = y.detach().cpu().double(), torch.as_tensor(np.asarray(y_ref))
+    if kind == "sum":   # compared per neuron: the fp32 error of a sum grows with the group size
+        n = torch.from_numpy(np.asarray(counts)).double()
+        yv, yr = yv / n, yr / n
+    assert_close(yv, yr, what="y", **FWD)
     assert_close(xg.grad.cpu(), odx, what="dx", slack=sdx, **BWD)
     assert_close(lay.weight.main_grad.cpu(), odw, what="dw", slack=sdw, **BWD)
     assert_close(lay.bias.main_grad.cpu(), odb, what="db", slack=sdb, **BWD)
@@ -167,7 +171,8 @@ def test_layer_gradients_on_rounded_x(C, pooling, D):
 
 @pytest.mark.parametrize("C", [8, 16, 64])
 @pytest.mark.parametrize("pooling,accum", [("mean", "auto"), ("sum", "auto"), ("mean", "fp32"),
-                                           ({"type": "mean", "activation": "gelu"}, "auto")])
+                                           ({"type": "mean", "activation": "gelu"}, "auto"),
+                                           ({"type": "sum", "activation": "identity"}, "auto")])
 @pytest.mark.parametrize("S,R,B", [(64, 4, 45), (128, 2, 150)])
 def test_input_set_backward_against_oracle(C, pooling, accum, S, R, B):
     """Layers with input-supergroup connectivity run the input-set backward (gl_bwd_shared_tc_sets):
@@ -177,6 +182,7 @@ def test_input_set_backward_against_oracle(C, pooling, accum, S, R, B):
                              dtype=torch.bfloat16, seed=C + S, bias_std=0.2, connectivity=ConnectivityPlan(S, R, seed=3),
                              plan=PhysicalPlan(b200_dx_accum=accum, cuda_input_supergroup_backend="grouped")).cuda()
     _layer_grads_against_oracle(lay, B, seed=S)
+    assert lay.last_info["forward_kernel"] == "gl_fwd_shared_tc_sets"
     assert lay.last_info["backward_kernel"] == "gl_bwd_shared_tc_sets"
     assert lay.last_info["dx_accumulation"].startswith("int32" if accum == "auto" else "fp32")
 
@@ -200,6 +206,7 @@ def test_large_input_dim_sets_and_fallbacks(C):
                                    dtype=torch.bfloat16, seed=7, bias_std=0.2,
                                    connectivity=ConnectivityPlan(256, 2, seed=1)).cuda()
     _layer_grads_against_oracle(with_sets, 40)
+    assert with_sets.last_info["forward_kernel"] == "gl_fwd_shared_tc_sets"
     assert with_sets.last_info["backward_kernel"] == "gl_bwd_shared_tc_sets"
     plain = _layer(C, "mean", D, 40000, 6, seed=8)
     _layer_grads_against_oracle(plain, 40)
