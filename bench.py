@@ -50,8 +50,9 @@ config, rank 0 only.
 
 ``--impl reference-gpu`` (comparator, not part of the driver contract) runs the unmodified
 reference package placed in baseline/_ref on this GPU through its public API: with
-``--workload modeb`` the published table's rows on its BF16 mma.sync CUDA kernels, otherwise
-the headline Mode-A fp32 layer on its Triton kernels.
+``--workload modeb`` the published table's rows on its BF16 mma.sync CUDA kernels, with
+``--workload sets`` its input-supergroup layers, with ``--workload cover16`` its Cover-TopK/16
+layer on its BF16 K16 kernels, otherwise the headline Mode-A fp32 layer on its Triton kernels.
 """
 from __future__ import annotations
 
@@ -245,6 +246,67 @@ def run_reference(args, rank, world):
 REF_DIR = ROOT / "baseline" / "_ref"
 
 
+def run_reference_gpu_cover16(args):
+    """The reference's Cover-TopK/16 layer (its BF16 kgen K16 kernels) at BASELINE config 4, built its own
+    way (experimental/kgen_layout.init_parameters, CoverTopK16Layer.from_envelope), fwd + bwd per step as
+    --workload cover16 times ours; rank 0, 1 GPU, comparator only."""
+    from sparse_pooling.cover_topk16 import CoverTopK16Layer as RefCT
+    from sparse_pooling.experimental.kgen_layout import KLayout as RefKL
+    from sparse_pooling.experimental.kgen_layout import init_parameters as ref_init
+    from sparse_pooling.supergroups import ConnectivityPlan as RefCP
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    Dc, Gc, Bc = 4096, args.cover_outputs, 512
+    Hc = Gc * 24576
+    w64, b64 = ref_init(RefKL(Dc, Hc, Gc, 64, 256), dev, dtype=torch.bfloat16, seed=3)
+    lay = RefCT.from_envelope(w64, b64, input_dim=Dc, hidden_dim=Hc, output_dim=Gc, connectivity=RefCP(64, 64, seed=3),
+                              device=dev)
+    del w64, b64
+    torch.cuda.empty_cache()
+    gen = torch.Generator(device=dev).manual_seed(3)
+    x = torch.randn(Bc, Dc, device=dev, generator=gen).to(torch.bfloat16)
+    dy = torch.randn(Bc, Gc, device=dev, generator=gen)
+    evs = []
+
+    def step(record):
+        e = [torch.cuda.Event(enable_timing=True) for _ in range(3)] if record else None
+        if e:
+            e[0].record()
+        y = lay(x.detach().requires_grad_(True))
+        if e:
+            e[1].record()
+        y.backward(dy.to(y.dtype))
+        if e:
+            e[2].record()
+            evs.append(e)
+        for prm in lay.parameters():
+            prm.grad = None
+
+    with ClockSampler(dev.index) as clk:
+        for _ in range(max(3, args.warmup)):
+            step(False)
+        torch.cuda.synchronize(dev)
+        steps = max(1, args.steps)
+        s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s_ev.record()
+        for _ in range(steps):
+            step(True)
+        e_ev.record()
+        torch.cuda.synchronize(dev)
+    ms = s_ev.elapsed_time(e_ev) / steps
+    line = {"impl": "reference-gpu", "metric": COVER_METRIC, "value": Bc * Hc / (ms / 1e3), "unit": UNIT,
+            "n_gpus": 1, "steps": steps, "warmup": max(3, args.warmup), "ms_per_step": ms, "higher_is_better": True,
+            "data": "synthetic", "device": torch.cuda.get_device_name(dev),
+            "config": {"workload": "cover16", "N": Hc, "D": Dc, "G": Gc, "global_batch": Bc},
+            "fwd_ms": statistics.mean(a.elapsed_time(b) for a, b, _ in evs),
+            "bwd_ms": statistics.mean(b.elapsed_time(c) for _, b, c in evs),
+            "last_info": {k: str(v)[:120] for k, v in getattr(lay, "last_info", {}).items()} if hasattr(lay, "last_info")
+            else None, "clocks": clk.summary(),
+            "note": "the reference's own BF16 K16 kernels (not a B200 build of this repository); comparator only"}
+    print(json.dumps(line), flush=True)
+
+
 def run_reference_gpu(args):
     """The reference's own GPU path on this GPU, as a comparator (rank 0, 1 GPU): the unmodified
     package placed in baseline/_ref, driven through its public API (SparsePoolingLayer + FusedAdamW),
@@ -259,6 +321,9 @@ def run_reference_gpu(args):
     if (REF_DIR / "cache").is_dir():
         os.environ.setdefault("SPARSE_POOL_CACHE_DIR", str(REF_DIR / "cache"))   # prebuilt sm_100 libraries
     sys.path.insert(0, str(REF_DIR))
+    if args.workload == "cover16":
+        run_reference_gpu_cover16(args)
+        return
     from sparse_pooling import SparsePoolingLayer as RefLayer
     from sparse_pooling.optim import FusedAdamW as RefAdam
 
