@@ -411,8 +411,8 @@ def cover16_cpu_baseline(lay, x, dy, target_s=8.0):
     from oracle import kc_oracle
 
     idx = lay.indices.cpu().numpy()
-    w = lay.weight.detach().cpu().numpy()
-    b = lay.bias.detach().cpu().numpy()
+    w = lay.weight.detach().double().cpu().numpy()
+    b = lay.bias.detach().double().cpu().numpy()
     counts = lay.counts.cpu().numpy()
     xs, dys = x.cpu().numpy(), dy.cpu().numpy()
     Bs = 64
@@ -440,8 +440,9 @@ def bench_cover16(args, world):
     torch.cuda.set_device(dev)
     t0 = time.perf_counter()
     w64, b64 = init_envelope_parameters(KLayout(Dc, Hc, Gc, 64, 256), dev, dtype=torch.bfloat16, seed=3)
+    pdt = torch.bfloat16 if args.cover_dtype == "bf16" else torch.float32
     lay = CoverTopK16Layer.from_envelope(w64, b64, input_dim=Dc, hidden_dim=Hc, output_dim=Gc,
-                                         connectivity=ConnectivityPlan(64, 64, seed=3), device=dev)
+                                         connectivity=ConnectivityPlan(64, 64, seed=3), device=dev, dtype=pdt)
     del w64, b64
     torch.cuda.synchronize(dev)
     torch.cuda.empty_cache()
@@ -529,13 +530,16 @@ def bench_cover16(args, world):
     line = {
         "metric": COVER_METRIC, "value": Bc * Hc / (ms / 1e3), "unit": UNIT, "n_gpus": 1, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "none",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "Cover-TopK16 opt-in layer, compact K16/C16 execution, fwd+bwd (BASELINE config 4)",
+        "vs_baseline": None, "dtype": "f32" if pdt == torch.float32 else "bf16", "data": "synthetic",
+        "config": {"workload": "Cover-TopK16 opt-in layer, compact K16/C16 execution, fwd+bwd (BASELINE config 4)"
+                               + ("" if pdt == torch.float32 else "; bf16 parameters on the tensor cores (the "
+                                  "reference's arithmetic), not config 4's fp32"),
                    "D": Dc, "N": Hc, "G": Gc, "global_batch": Bc, "envelope": "K64/C256, w64 ~ N(0,1/64) BF16",
                    "S": 64, "R": 64, "Q": int(lay.sg_feat.shape[0]), "records_16": int(Hc // 16),
                    "l2": f"weights {Hc * 64 / 1e9:.1f} GB fp32 > L2: streamed from HBM every pass",
                    "build_seconds": build_s},
-        "roofline": {"bound": "fp32", "kernel": "gl_k16_bwd_f32 (k16_bwd_kernel<relu>)", "achieved": achieved,
+        "roofline": {"bound": "fp32", "kernel": "gl_k16_bwd_f32 (k16_bwd_kernel<relu>)" if pdt == torch.float32
+                     else "gl_k16_bwd_tc (fp32 FMA rate shown for comparison)", "achieved": achieved,
                      "peak": peak_tflops, "unit": "TFLOP/s", "frac": achieved / peak_tflops,
                      "peak_source": f"nominal fp32 FMA rate: {sms} SMs x 128 lanes x 2 flop at the median "
                                     f"sampled SM clock {mhz} MHz",
@@ -883,6 +887,8 @@ def main():
                                                        "(comma list of f32, bf16; default all)")
     ap.add_argument("--sets-tokens", default="0", help="sets: token tiles of the input-set backward to time "
                                                       "(comma list; 0 = automatic)")
+    ap.add_argument("--cover-dtype", default="fp32", choices=["fp32", "bf16"],
+                    help="cover16: parameter storage (fp32 = config 4; bf16 = the reference's, on the tensor cores)")
     ap.add_argument("--cover-outputs", type=int, default=2048,
                     help="cover16: outputs of 24,576 neurons (default 2048 = config 4; fewer for ncu captures)")
     ap.add_argument("--groups", type=int, default=G,

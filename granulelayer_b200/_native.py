@@ -41,7 +41,7 @@ EXPORTS = ("gl_abi_version", "gl_status_string", "gl_last_cuda_error", "gl_fwd_f
            "gl_bwd_shared_f32",
            "gl_bwd_events_f32",
            "gl_shared_auto_tokens", "gl_bwd_shared_det_f32", "gl_bwd_shared_det_static_f32", "gl_k16_fwd_f32",
-           "gl_k16_bwd_f32", "gl_k16_auto_tokens")
+           "gl_k16_bwd_f32", "gl_k16_auto_tokens", "gl_k16_fwd_tc", "gl_k16_bwd_tc")
 
 
 class GlSetArgs(ctypes.Structure):
@@ -141,6 +141,7 @@ def load(path=None) -> ctypes.CDLL:
         lib.gl_launch_count.restype = ctypes.c_int64
         for name, st in (("gl_fwd_f32", GlFwdArgs), ("gl_bwd_f32", GlBwdArgs), ("gl_adam_f32", GlAdamArgs),
                          ("gl_k16_fwd_f32", GlK16Args), ("gl_k16_bwd_f32", GlK16Args),
+                         ("gl_k16_fwd_tc", GlK16Args), ("gl_k16_bwd_tc", GlK16Args),
                          ("gl_fwd_shared_f32", GlSharedArgs), ("gl_bwd_shared_f32", GlSharedArgs),
                          ("gl_bwd_events_f32", GlEventArgs)):
             fn = getattr(lib, name)
@@ -492,24 +493,28 @@ def _k16_args(x, sched, w, b, counts, NB16: int, act: int, tokens: int):
 
 def k16_fwd(x, sched: dict, w, b, counts, pre, NB16: int, act: int = 1, tokens: int = 0):
     """pre[t, g] += Mean-pooled act(z) of the K16/C16 layer (GlK16Args); ``sched`` holds env, feat,
-    buckets (sorted by set), q_off and rec_off."""
+    buckets (sorted by set), q_off and rec_off.  bf16 parameters run the tensor-core entry
+    (gl_k16_fwd_tc, x rounded to bf16), fp32 ones gl_k16_fwd_f32."""
     _require_cuda(x, w, b, counts, pre, *sched.values())
     lib = load()
     a = _k16_args(x, sched, w, b, counts, NB16, act, tokens)
     a.pre, a.ldp = _ptr(pre), pre.stride(0)
+    name = "gl_k16_fwd_tc" if w.dtype == torch.bfloat16 else "gl_k16_fwd_f32"
     with torch.cuda.device(x.device):
-        _check(lib, lib.gl_k16_fwd_f32(ctypes.byref(a), _stream(x.device)), "gl_k16_fwd_f32")
+        _check(lib, getattr(lib, name)(ctypes.byref(a), _stream(x.device)), name)
 
 
 def k16_bwd(x, sched: dict, w, b, counts, c1t, dx, dw, db, NB16: int, act: int = 1, tokens: int = 0):
-    """dx, dw, db += the K16/C16 layer's gradients for coefficients c1t [G, B] (GlK16Args)."""
+    """dx, dw, db += the K16/C16 layer's gradients for coefficients c1t [G, B] (GlK16Args); bf16 parameters
+    run gl_k16_bwd_tc (split-precision dz on the tensor cores)."""
     _require_cuda(x, w, b, counts, c1t, dx, dw, db, *sched.values())
     lib = load()
     a = _k16_args(x, sched, w, b, counts, NB16, act, tokens)
     a.c1t, a.dx, a.dw, a.db = _ptr(c1t), _ptr(dx), _ptr(dw), _ptr(db)
     a.ldc, a.lddx = c1t.stride(0), dx.stride(0)
+    name = "gl_k16_bwd_tc" if w.dtype == torch.bfloat16 else "gl_k16_bwd_f32"
     with torch.cuda.device(x.device):
-        _check(lib, lib.gl_k16_bwd_f32(ctypes.byref(a), _stream(x.device)), "gl_k16_bwd_f32")
+        _check(lib, getattr(lib, name)(ctypes.byref(a), _stream(x.device)), name)
 
 
 def k16_auto_tokens(B: int, S: int, backward: bool) -> int:

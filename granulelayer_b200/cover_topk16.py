@@ -58,10 +58,16 @@ def _fp_tensor(t: torch.Tensor):
     return h.hexdigest(), list(c.shape), str(c.dtype)
 
 
+def _operand(x, w):
+    """x in the layer's compute dtype (a bf16 layer computes on x rounded to bf16, as the reference's
+    kgen path does), as the fp32 rows the kernels read."""
+    return x.to(torch.bfloat16).to(torch.float32) if w.dtype == torch.bfloat16 else x.to(torch.float32)
+
+
 class _K16Function(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, w, b, layer: "CoverTopK16Layer"):
-        xc = x.to(torch.float32)
+        xc = _operand(x, w)
         if xc.stride(-1) != 1:
             xc = xc.contiguous()
         B = xc.shape[0]
@@ -69,14 +75,15 @@ class _K16Function(torch.autograd.Function):
         _native.k16_fwd(xc, layer._work(), w, b, layer.counts, pre, layer.layout.blocks_per_group)
         ctx.layer = layer
         ctx.save_for_backward(x, w, b)
-        layer.last_info.update(forward_backend="b200-k16", checkpoint_bytes=0)
+        layer.last_info.update(forward_backend="b200-k16", checkpoint_bytes=0,
+                               forward_kernel="gl_k16_fwd_tc" if w.dtype == torch.bfloat16 else "gl_k16_fwd_f32")
         return pre
 
     @staticmethod
     def backward(ctx, dy):
         layer: CoverTopK16Layer = ctx.layer
         x, w, b = ctx.saved_tensors
-        xc = x.to(torch.float32).contiguous()
+        xc = _operand(x, w).contiguous()
         c1t = (dy.float() / layer.counts_f[None, :]).t().contiguous()     # Mean: dL/dpre / n_g, [G, B]
         mg_w, mg_b = getattr(w, "main_grad", None), getattr(b, "main_grad", None)
         use_main = mg_w is not None and mg_b is not None
@@ -84,7 +91,8 @@ class _K16Function(torch.autograd.Function):
         db = mg_b if use_main else torch.zeros(b.shape, device=b.device, dtype=torch.float32)
         dx = torch.zeros_like(xc)
         _native.k16_bwd(xc, layer._work(), w, b, layer.counts, c1t, dx, dw, db, layer.layout.blocks_per_group)
-        layer.last_info.update(backward_backend="b200-k16")
+        layer.last_info.update(backward_backend="b200-k16",
+                               backward_kernel="gl_k16_bwd_tc" if w.dtype == torch.bfloat16 else "gl_k16_bwd_f32")
         gw = None if use_main else dw.to(w.dtype)
         gb = None if use_main else db.to(b.dtype)
         return dx.to(x.dtype), gw, gb, None
@@ -128,9 +136,12 @@ class CoverTopK16Layer(nn.Module):
     def from_envelope(cls, weight: torch.Tensor, bias: torch.Tensor, *, input_dim: int, hidden_dim: int,
                       output_dim: int, connectivity: ConnectivityPlan, envelope_C: int = 256,
                       normalization: str = "none", plan: Optional[PhysicalPlan] = None, device=None,
-                      dx_variant: str = "auto", envelope: Optional[Envelope] = None) -> "CoverTopK16Layer":
+                      dx_variant: str = "auto", envelope: Optional[Envelope] = None,
+                      dtype=torch.float32) -> "CoverTopK16Layer":
         """Select the Cover-TopK/16 support from BF16 K64 envelope values ``weight [G, NB, C, 64]`` /
-        ``bias [G, NB, C]`` (KLayout order) and lower it (cover_topk16.py:80-146)."""
+        ``bias [G, NB, C]`` (KLayout order) and lower it (cover_topk16.py:80-146).  ``dtype`` is the
+        parameters' storage: float32 (fp32 kernels) or bfloat16 (the reference's storage and arithmetic,
+        on the tensor cores)."""
         if normalization not in NORMALIZATIONS:
             raise ValueError(f"normalization {normalization!r} (one of {NORMALIZATIONS})")
         if connectivity.input_supergroup_dim != 64:
@@ -158,7 +169,7 @@ class CoverTopK16Layer(nn.Module):
         menv = Envelope(L, w_new, b_new, env.sg_feat, env.kg_buckets, env.spec, connectivity, mask=em,
                         graph_stats=dict(env.graph_stats, normalized=normalization == "energy"))
         low = lower_env(menv, sup.env, source=f"local-support-{POLICY}-of-K64")
-        lay = cls(low, env.sg_feat, connectivity, plan)
+        lay = cls(low, env.sg_feat, connectivity, plan, dtype=dtype)
         lay.graph_stats.update(lowered_from_policy=POLICY, local_support=sup.fingerprint(), tile_width=FAN_IN)
         lay.dx_variant = dx_variant
         lay.cover_meta = dict(
@@ -289,8 +300,8 @@ class CoverTopK16Layer(nn.Module):
                 p.main_grad.zero_()
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        if self.weight.dtype != torch.float32:
-            raise NotImplementedError("the B200 K16 kernels run fp32 parameters")
+        if self.weight.dtype not in (torch.float32, torch.bfloat16):
+            raise NotImplementedError("the B200 K16 kernels run fp32 or bf16 parameters")
         lead = x.shape[:-1]
         y = _K16Function.apply(x.reshape(-1, x.shape[-1]), self.weight, self.bias, self)
         return y.reshape(*lead, y.shape[-1])

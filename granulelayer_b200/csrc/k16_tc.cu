@@ -1,0 +1,397 @@
+// Compact K16/C16 execution of the Cover-TopK/16 layer with bf16 parameters, on the tensor cores.
+//
+// Replaces the reference's kgen K = 16 kernels (sparse_pooling/experimental/kgen/kgen.cuh:142-536,
+// launched by experimental/kgen_layer.py:61-143) with their arithmetic: bf16 parameters, x rounded to
+// bf16 (the layer's compute dtype), fp32 accumulation, and the backward's "split" gradient precision
+// (dz carried as hi + lo bf16).  Model as csrc/k16.cu:
+//   z[t, f, n] = b[f, n] + sum_k w[f, n, k] * x[t, feat[q][env[f, k]]]      (record f of set q)
+//   pre[t, g] += sum_{valid n of the records of g} act(z) / n_g
+//   dz = c1t[g, t] act'(z), dW[f, n, k] += sum_t dz x, db[f, n] += sum_t dz, dx += sum_n dz w.
+//
+// A record is a 16-input x 16-neuron tile, one K step of mma.m16n8k16: per 16 tokens the forward is
+// one ldmatrix.x4.trans (the lanes point at the record's 16 slab rows) and two MMAs (neurons 0-7,
+// 8-15).  A CTA owns one input set q and BM tokens: the set's S rows of x are staged once as a bf16
+// slab (modeb_tc.cuh layout); the set's records (its buckets, in order) are split into one
+// contiguous run per warp, so a warp changes output (bucket) rarely.  The forward folds each warp's
+// per-token sums of an output over the lane quad and adds them to pre with one atomic per (token,
+// warp, output).  The backward keeps, per record, z again, the split dz, the dX partials
+// P = dz w (A = the dz accumulator fragments, B = w^T by movmatrix) added to an fp32 [S][BM] tile with
+// shared atomics, and dW += dz^T x (A = dz^T, B = x^T, both by movmatrix), whose fragments are reduced
+// into the fp32 gradients once per record and token tile.
+#include "modeb_tc_bwd.cuh"
+
+namespace gl {
+
+constexpr int kK16TcThreads = 384;
+
+struct K16TcParams {
+  const float* x;
+  const uint8_t* env;
+  const int16_t* feat;
+  const int32_t* buckets;
+  const int32_t* q_off;
+  const int32_t* rec_off;
+  const uint16_t* w;        // bf16 [G*NB16, 16, 16]
+  const uint16_t* b;        // bf16 [G*NB16, 16]
+  const int32_t* counts;
+  float* pre;
+  const float* c1t;
+  float* dx;
+  float* dw;
+  float* db;
+  int B, D, G, NB16, S, nbk;
+  int64_t ldx, ldp, ldc, lddx;
+};
+
+// Stage x[t0 .. t0+BM, feat[q][s]] (fp32) as the bf16 slab rows s = 0 .. S-1 and the set's features.
+template <int BM>
+__device__ __forceinline__ void k16tc_stage(uint32_t slab, int* fq, const K16TcParams& p, int q, int t0) {
+  constexpr int CH = BM / 8;
+  for (int s = threadIdx.x; s < p.S; s += kK16TcThreads) {
+    const int d = (int)(uint16_t)__ldg(p.feat + (int64_t)q * p.S + s);
+    fq[s] = d < p.D ? d : p.D - 1;
+  }
+  __syncthreads();
+  for (int it = threadIdx.x; it < p.S * CH; it += kK16TcThreads) {
+    const int i = it % p.S, k = it / p.S;
+    const int f = fq[i];
+    float v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int t = t0 + 8 * k + u;
+      v[u] = t < p.B ? __ldg(p.x + (int64_t)t * p.ldx + f) : 0.f;
+    }
+    uint32_t w4[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) w4[u] = pack_bf16(v[2 * u], v[2 * u + 1]);
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(tc_chunk<BM>(slab, i, k)), "r"(w4[0]), "r"(w4[1]),
+                 "r"(w4[2]), "r"(w4[3])
+                 : "memory");
+  }
+}
+
+// One record's operands for lane l: B fragments wf[nt][kh] (neurons 8 nt + l/4, inputs 8 kh + 2 (l%4) + {0,1}),
+// bias pairs bb[nt] (neurons 8 nt + 2 (l%4) + {0,1}), and the record's 16 local positions (4 words).
+struct K16TcRec {
+  uint32_t wf[2][2], bb[2];
+  uint4 env;
+};
+
+__device__ __forceinline__ K16TcRec k16tc_load(const K16TcParams& p, int64_t f, int lane) {
+  K16TcRec r;
+  const uint32_t* w32 = reinterpret_cast<const uint32_t*>(p.w + f * 256);
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+    for (int kh = 0; kh < 2; ++kh) r.wf[nt][kh] = __ldg(w32 + (8 * nt + (lane >> 2)) * 8 + 4 * kh + (lane & 3));
+  const uint32_t* b32 = reinterpret_cast<const uint32_t*>(p.b + f * 16);
+  r.bb[0] = __ldg(b32 + (lane & 3));
+  r.bb[1] = __ldg(b32 + 4 + (lane & 3));
+  r.env = __ldg(reinterpret_cast<const uint4*>(p.env + f * 16));
+  return r;
+}
+
+// Local position of input k of the record (clamped to the set).
+__device__ __forceinline__ int k16tc_pos(const uint4& env, int k, int smax) {
+  const uint32_t wd = k < 4 ? env.x : k < 8 ? env.y : k < 12 ? env.z : env.w;
+  return min((int)((wd >> (8 * (k & 3))) & 0xffu), smax);
+}
+
+// The warp's run of the set's records: [r0, r1) in flat record numbers, and the bucket walk.
+struct K16TcWalk {
+  int bk, bend;  // current bucket index, end of the set's buckets
+  int r, r1;
+};
+
+__device__ __forceinline__ K16TcWalk k16tc_walk(const K16TcParams& p, int q, int warp, int nw) {
+  K16TcWalk w;
+  const int qa = min(max(__ldg(p.q_off + q), 0), p.nbk), qb = min(max(__ldg(p.q_off + q + 1), qa), p.nbk);
+  const int ra = __ldg(p.rec_off + qa), rb = __ldg(p.rec_off + qb);
+  const int per = (rb - ra + nw - 1) / nw;
+  w.r = ra + warp * per;
+  w.r1 = min(w.r + per, rb);
+  w.bk = qa;
+  w.bend = qb;
+  while (w.bk < w.bend && __ldg(p.rec_off + w.bk + 1) <= w.r) ++w.bk;
+  return w;
+}
+
+// Record f and output g of flat record r (the walk advances monotonically); false for a malformed row.
+__device__ __forceinline__ bool k16tc_at(const K16TcParams& p, K16TcWalk& w, int r, int& g, int& j16) {
+  while (w.bk < w.bend && __ldg(p.rec_off + w.bk + 1) <= r) ++w.bk;
+  if (w.bk >= w.bend) return false;
+  const int4 bk = __ldg(reinterpret_cast<const int4*>(p.buckets) + w.bk);
+  g = bk.y;
+  j16 = bk.z + (r - __ldg(p.rec_off + w.bk));
+  return g >= 0 && g < p.G && j16 >= 0 && j16 < p.NB16;
+}
+
+template <int BM, int ACT>
+__global__ void __launch_bounds__(kK16TcThreads, 1) k16tc_fwd_kernel(const K16TcParams p) {
+  constexpr int MT = BM / 16, NW = kK16TcThreads / 32;
+  extern __shared__ __align__(128) unsigned char tc_smem[];
+  __shared__ int fq[256];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int q = blockIdx.y, t0 = blockIdx.x * BM;
+  const uint32_t slab = (uint32_t)__cvta_generic_to_shared(tc_smem);
+  k16tc_stage<BM>(slab, fq, p, q, t0);
+  __syncthreads();
+  K16TcWalk wk = k16tc_walk(p, q, warp, NW);
+  const int cq = 2 * (lane & 3), smax = p.S - 1;
+  float acc[MT][2];
+  int gcur = -1;
+  auto flush = [&]() {
+#pragma unroll
+    for (int m = 0; m < MT; ++m)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        acc[m][h] += __shfl_xor_sync(kFullMask, acc[m][h], 1);
+        acc[m][h] += __shfl_xor_sync(kFullMask, acc[m][h], 2);
+      }
+    if ((lane & 3) == 0) {
+      const float inv = 1.f / (float)max(__ldg(p.counts + gcur), 1);
+#pragma unroll
+      for (int m = 0; m < MT; ++m)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int t = t0 + 16 * m + 8 * h + (lane >> 2);
+          if (t < p.B) atomicAdd(p.pre + (int64_t)t * p.ldp + gcur, acc[m][h] * inv);
+        }
+    }
+  };
+  for (int r = wk.r; r < wk.r1; ++r) {
+    int g, j16;
+    if (!k16tc_at(p, wk, r, g, j16)) continue;  // warp-uniform
+    if (g != gcur) {
+      if (gcur >= 0) flush();
+      gcur = g;
+#pragma unroll
+      for (int m = 0; m < MT; ++m) acc[m][0] = acc[m][1] = 0.f;
+    }
+    const int64_t f = (int64_t)g * p.NB16 + j16;
+    const K16TcRec rc = k16tc_load(p, f, lane);
+    const int nv = __ldg(p.counts + g) - 16 * j16;  // valid neurons of this record (<= 0: none)
+    const int row = k16tc_pos(rc.env, (lane & 7) + 8 * (lane >> 4), smax);
+    float bias[2][2];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      bias[nt][0] = bf16_lo(rc.bb[nt]);
+      bias[nt][1] = bf16_hi(rc.bb[nt]);
+    }
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+      uint32_t a[4];
+      ldsm_x4_t(a, tc_chunk<BM>(slab, row, 2 * m + ((lane >> 3) & 1)));
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+        float z[4];
+        const float c[4] = {bias[nt][0], bias[nt][1], bias[nt][0], bias[nt][1]};
+        mma_bf16_k16(z, a, rc.wf[nt][0], rc.wf[nt][1], c);
+        const bool v0 = 8 * nt + cq < nv, v1 = 8 * nt + cq + 1 < nv;
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+          acc[m][h] += (v0 ? act_f<ACT>(z[2 * h]) : 0.f) + (v1 ? act_f<ACT>(z[2 * h + 1]) : 0.f);
+      }
+    }
+  }
+  if (gcur >= 0) flush();
+}
+
+// fp32 dX tile [S][BM]: element (s, t) at s * BM + (t ^ (s & (BM - 1))), as dxs_off.
+template <int BM, int ACT>
+__global__ void __launch_bounds__(kK16TcThreads, 1) k16tc_bwd_kernel(const K16TcParams p) {
+  constexpr int MT = BM / 16, NW = kK16TcThreads / 32;
+  extern __shared__ __align__(128) unsigned char tc_smem[];
+  __shared__ int fq[256];
+  float* dxs = reinterpret_cast<float*>(tc_smem + (size_t)p.S * BM * 2);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int q = blockIdx.y, t0 = blockIdx.x * BM;
+  const uint32_t slab = (uint32_t)__cvta_generic_to_shared(tc_smem);
+  k16tc_stage<BM>(slab, fq, p, q, t0);
+  for (int i = threadIdx.x; i < p.S * BM; i += kK16TcThreads) dxs[i] = 0.f;
+  __syncthreads();
+  K16TcWalk wk = k16tc_walk(p, q, warp, NW);
+  const int cq = 2 * (lane & 3), smax = p.S - 1;
+  float c1[MT][2];
+  int gcur = -1;
+  for (int r = wk.r; r < wk.r1; ++r) {
+    int g, j16;
+    if (!k16tc_at(p, wk, r, g, j16)) continue;
+    if (g != gcur) {
+      gcur = g;
+#pragma unroll
+      for (int m = 0; m < MT; ++m)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int t = t0 + 16 * m + 8 * h + (lane >> 2);
+          c1[m][h] = t < p.B ? __ldg(p.c1t + (int64_t)g * p.ldc + t) : 0.f;
+        }
+    }
+    const int64_t f = (int64_t)g * p.NB16 + j16;
+    const K16TcRec rc = k16tc_load(p, f, lane);
+    const int nv = __ldg(p.counts + g) - 16 * j16;
+    const int row = k16tc_pos(rc.env, (lane & 7) + 8 * (lane >> 4), smax);
+    int prow[2][2];  // slab rows of the inputs 8 kh + cq + e this lane's dX partials belong to
+#pragma unroll
+    for (int kh = 0; kh < 2; ++kh)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) prow[kh][e] = k16tc_pos(rc.env, 8 * kh + cq + e, smax);
+    uint32_t wt[2][2];  // w^T fragments: (k = neurons 8 nt + cq + {0,1}, n = input 8 kh + lane / 4)
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int kh = 0; kh < 2; ++kh) wt[nt][kh] = movt(rc.wf[nt][kh]);
+    float bias[2][2];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      bias[nt][0] = bf16_lo(rc.bb[nt]);
+      bias[nt][1] = bf16_hi(rc.bb[nt]);
+    }
+    float dwa[2][4] = {};   // [kh]: (neuron lane/4, inputs 8 kh + cq + {0,1}), (neuron lane/4 + 8, same)
+    float dba[2][2] = {};   // [nt][e]: neuron 8 nt + cq + e, this lane's tokens
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+      uint32_t a[4];
+      ldsm_x4_t(a, tc_chunk<BM>(slab, row, 2 * m + ((lane >> 3) & 1)));
+      uint32_t dh[2][2], dl[2][2];  // [nt][rows 0-7 | 8-15]
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+        float z[4];
+        const float c[4] = {bias[nt][0], bias[nt][1], bias[nt][0], bias[nt][1]};
+        mma_bf16_k16(z, a, rc.wf[nt][0], rc.wf[nt][1], c);
+        const bool v0 = 8 * nt + cq < nv, v1 = 8 * nt + cq + 1 < nv;
+        float dz[4];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          dz[2 * h] = v0 ? c1[m][h] * dact_f<ACT>(z[2 * h]) : 0.f;
+          dz[2 * h + 1] = v1 ? c1[m][h] * dact_f<ACT>(z[2 * h + 1]) : 0.f;
+        }
+        dba[nt][0] += dz[0] + dz[2];
+        dba[nt][1] += dz[1] + dz[3];
+        split2(dz[0], dz[1], dh[nt][0], dl[nt][0]);
+        split2(dz[2], dz[3], dh[nt][1], dl[nt][1]);
+      }
+      // dX partials of the record's 16 inputs: P_kh = dz (tokens x neurons) w^T (neurons x inputs 8 kh ..)
+      const uint32_t ah[4] = {dh[0][0], dh[0][1], dh[1][0], dh[1][1]}, al[4] = {dl[0][0], dl[0][1], dl[1][0], dl[1][1]};
+#pragma unroll
+      for (int kh = 0; kh < 2; ++kh) {
+        float P[4] = {0.f, 0.f, 0.f, 0.f};
+        mma_bf16_k16(P, ah, wt[0][kh], wt[1][kh], P);
+        mma_bf16_k16(P, al, wt[0][kh], wt[1][kh], P);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int t = 16 * m + 8 * h + (lane >> 2);
+          atomicAdd(dxs + dxs_off<BM>(prow[kh][0], t), P[2 * h]);
+          atomicAdd(dxs + dxs_off<BM>(prow[kh][1], t), P[2 * h + 1]);
+        }
+      }
+      // dW: A = dz^T (neurons x tokens), B = x^T (tokens x inputs 8 kh ..), both transposed in registers
+      const uint32_t th[4] = {movt(dh[0][0]), movt(dh[1][0]), movt(dh[0][1]), movt(dh[1][1])};
+      const uint32_t tl[4] = {movt(dl[0][0]), movt(dl[1][0]), movt(dl[0][1]), movt(dl[1][1])};
+#pragma unroll
+      for (int kh = 0; kh < 2; ++kh) {
+        const uint32_t x0 = movt(a[2 * kh]), x1 = movt(a[2 * kh + 1]);
+        mma_bf16_k16(dwa[kh], th, x0, x1, dwa[kh]);
+        mma_bf16_k16(dwa[kh], tl, x0, x1, dwa[kh]);
+      }
+    }
+    // dw[f][n][k]: lane holds (n = lane/4, k = 8 kh + cq + {0,1}) and (n + 8, same k)
+    float* dwp = p.dw + f * 256;
+#pragma unroll
+    for (int kh = 0; kh < 2; ++kh) {
+      const int k = 8 * kh + cq;
+      atomicAdd(reinterpret_cast<float2*>(dwp + (lane >> 2) * 16 + k), make_float2(dwa[kh][0], dwa[kh][1]));
+      atomicAdd(reinterpret_cast<float2*>(dwp + ((lane >> 2) + 8) * 16 + k), make_float2(dwa[kh][2], dwa[kh][3]));
+    }
+#pragma unroll
+    for (int off = 4; off < 32; off <<= 1)
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+        dba[nt][0] += __shfl_xor_sync(kFullMask, dba[nt][0], off);
+        dba[nt][1] += __shfl_xor_sync(kFullMask, dba[nt][1], off);
+      }
+    if (lane < 4) {
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+        atomicAdd(reinterpret_cast<float2*>(p.db + f * 16 + 8 * nt + 2 * lane), make_float2(dba[nt][0], dba[nt][1]));
+    }
+  }
+  __syncthreads();
+  // dx[t0 + t, feat[q][s]] += tile; consecutive threads take consecutive set rows of one token
+  for (int it = threadIdx.x; it < p.S * BM; it += kK16TcThreads) {
+    const int t = it / p.S, s = it - t * p.S;
+    const float v = dxs[dxs_off<BM>(s, t)];
+    if (t0 + t < p.B && v != 0.f) atomicAdd(p.dx + (int64_t)(t0 + t) * p.lddx + fq[s], v);
+  }
+}
+
+static int k16tc_prepare(const GlK16Args& a, bool bwd, K16TcParams& p) {
+  if (a.B < 0 || a.D < 1 || a.D > 32767 || a.G < 1 || a.NB16 < 1 || a.Q < 1 || a.S < 16 || a.S > 256 ||
+      a.nbuckets < 0)
+    return GL_ERR_SHAPE;
+  if (a.act != GL_ACT_RELU && a.act != GL_ACT_IDENTITY) return GL_ERR_UNSUPPORTED;
+  if (a.B == 0 || a.nbuckets == 0) return 1;
+  if (!a.x || !a.env || !a.feat || !a.buckets || !a.q_off || !a.rec_off || !a.w || !a.b || !a.counts)
+    return GL_ERR_NULL;
+  if (a.B > 2147483647LL || a.ldx < a.D || a.Q > 65535 || a.G * a.NB16 > 2147483647LL) return GL_ERR_SHAPE;
+  if (((uintptr_t)a.env & 15) || ((uintptr_t)a.buckets & 15) || ((uintptr_t)a.w & 15) || ((uintptr_t)a.b & 15))
+    return GL_ERR_ALIGN;
+  if (!bwd) {
+    if (!a.pre) return GL_ERR_NULL;
+    if (a.ldp < a.G) return GL_ERR_SHAPE;
+  } else {
+    if (!a.c1t || !a.dx || !a.dw || !a.db) return GL_ERR_NULL;
+    if (a.ldc < a.B || a.lddx < a.D) return GL_ERR_SHAPE;
+    if (((uintptr_t)a.dw & 7) || ((uintptr_t)a.db & 7)) return GL_ERR_ALIGN;
+  }
+  p = K16TcParams{a.x, a.env, a.feat, a.buckets, a.q_off, a.rec_off, reinterpret_cast<const uint16_t*>(a.w),
+                  reinterpret_cast<const uint16_t*>(a.b), a.counts, a.pre, a.c1t, a.dx, a.dw, a.db,
+                  (int)a.B, (int)a.D, (int)a.G, (int)a.NB16, (int)a.S, (int)a.nbuckets,
+                  a.ldx, a.ldp, a.ldc, a.lddx};
+  return GL_OK;
+}
+
+template <int BM, int ACT, bool BWD>
+static int k16tc_launch(const K16TcParams& p, int64_t Q, cudaStream_t st) {
+  const size_t smem = (size_t)p.S * BM * (BWD ? 6 : 2);
+  const void* kern = BWD ? (const void*)k16tc_bwd_kernel<BM, ACT> : (const void*)k16tc_fwd_kernel<BM, ACT>;
+  int rc = ensure_dynamic_smem(kern, smem);
+  if (rc) return rc;
+  const dim3 grid((unsigned)((p.B + BM - 1) / BM), (unsigned)Q);
+  if constexpr (BWD) k16tc_bwd_kernel<BM, ACT><<<grid, kK16TcThreads, smem, st>>>(p);
+  else k16tc_fwd_kernel<BM, ACT><<<grid, kK16TcThreads, smem, st>>>(p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_cuda_error(e);
+  count_launches(1);
+  return GL_OK;
+}
+
+template <bool BWD>
+static int k16tc_run(const GlK16Args* args, void* stream) {
+  if (!args) return GL_ERR_NULL;
+  K16TcParams p;
+  int rc = k16tc_prepare(*args, BWD, p);
+  if (rc) return rc > 0 ? GL_OK : rc;
+  int BM = args->tokens;
+  if (BM == 0) BM = BWD ? 64 : 128;
+  if (BM != 32 && BM != 64 && BM != 128) return GL_ERR_UNSUPPORTED;
+  int optin = 0;
+  if ((rc = device_smem_optin(&optin))) return rc;
+  if ((int64_t)p.S * BM * (BWD ? 6 : 2) + 8192 > optin) return GL_ERR_SMEM;
+  cudaStream_t st = (cudaStream_t)stream;
+  const bool relu = args->act == GL_ACT_RELU;
+  switch (BM) {
+    case 128: return relu ? k16tc_launch<128, GL_ACT_RELU, BWD>(p, args->Q, st)
+                          : k16tc_launch<128, GL_ACT_IDENTITY, BWD>(p, args->Q, st);
+    case 64: return relu ? k16tc_launch<64, GL_ACT_RELU, BWD>(p, args->Q, st)
+                         : k16tc_launch<64, GL_ACT_IDENTITY, BWD>(p, args->Q, st);
+    default: return relu ? k16tc_launch<32, GL_ACT_RELU, BWD>(p, args->Q, st)
+                         : k16tc_launch<32, GL_ACT_IDENTITY, BWD>(p, args->Q, st);
+  }
+}
+
+}  // namespace gl
+
+extern "C" int gl_k16_fwd_tc(const GlK16Args* args, void* stream) { return gl::k16tc_run<false>(args, stream); }
+
+extern "C" int gl_k16_bwd_tc(const GlK16Args* args, void* stream) { return gl::k16tc_run<true>(args, stream); }

@@ -412,6 +412,13 @@ int gl_k16_fwd_f32(const GlK16Args* args, void* stream);
 int gl_k16_bwd_f32(const GlK16Args* args, void* stream);
 /* Token chunk the automatic choice would use (backward != 0: the backward's), or a negative status. */
 int gl_k16_auto_tokens(int64_t B, int64_t S, int32_t backward);
+/* The same layer with bf16 parameters (w, b point to bf16 [G*NB16, 16, 16] / [G*NB16, 16]) on the tensor
+ * cores, the reference's kgen arithmetic (experimental/kgen/kgen.cuh): x rounded to bf16 as it is staged,
+ * every bf16 x bf16 product exact in fp32, the backward's dz carried as hi + lo bf16 ("split" precision).
+ * Same arguments, layouts and accumulation as gl_k16_fwd_f32 / gl_k16_bwd_f32 (dw, db fp32); `tokens` =
+ * 0 (automatic), 32, 64 or 128 tokens per block; S <= 256. */
+int gl_k16_fwd_tc(const GlK16Args* args, void* stream);
+int gl_k16_bwd_tc(const GlK16Args* args, void* stream);
 
 /* Number of kernels this library has launched successfully in this process
    (all devices).  Benchmarks difference it around a timed region. */
