@@ -16,7 +16,7 @@ from pathlib import Path
 
 import torch
 
-ABI_VERSION = 12
+ABI_VERSION = 13
 LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libgranule_b200.so"
 
 POOL_MEAN, POOL_SUM, POOL_MAX, POOL_LME, POOL_POWER, POOL_SOFTMAX, POOL_TOPK = 0, 1, 2, 3, 4, 5, 6
@@ -141,7 +141,7 @@ def load(path=None) -> ctypes.CDLL:
         lib.gl_launch_count.restype = ctypes.c_int64
         for name, st in (("gl_fwd_f32", GlFwdArgs), ("gl_bwd_f32", GlBwdArgs), ("gl_adam_f32", GlAdamArgs),
                          ("gl_k16_fwd_f32", GlK16Args), ("gl_k16_bwd_f32", GlK16Args),
-                         ("gl_k16_fwd_tc", GlK16Args), ("gl_k16_bwd_tc", GlK16Args),
+                         ("gl_k16_fwd_tc", GlK16Args),
                          ("gl_fwd_shared_f32", GlSharedArgs), ("gl_bwd_shared_f32", GlSharedArgs),
                          ("gl_bwd_events_f32", GlEventArgs)):
             fn = getattr(lib, name)
@@ -179,6 +179,8 @@ def load(path=None) -> ctypes.CDLL:
         lib.gl_bwd_shared_tc.argtypes = [ctypes.POINTER(GlSharedArgs), ctypes.c_void_p, ctypes.c_void_p,
                                          ctypes.c_void_p]
         lib.gl_bwd_shared_tc.restype = ctypes.c_int
+        lib.gl_k16_bwd_tc.argtypes = [ctypes.POINTER(GlK16Args), ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+        lib.gl_k16_bwd_tc.restype = ctypes.c_int
         lib.gl_bwd_shared_tc_sets.argtypes = [ctypes.POINTER(GlSharedArgs), ctypes.POINTER(GlSetArgs), ctypes.c_void_p]
         lib.gl_bwd_shared_tc_sets.restype = ctypes.c_int
         lib.gl_fwd_shared_tc_sets.argtypes = [ctypes.POINTER(GlSharedArgs), ctypes.POINTER(GlSetArgs), ctypes.c_void_p]
@@ -504,7 +506,8 @@ def k16_fwd(x, sched: dict, w, b, counts, pre, NB16: int, act: int = 1, tokens: 
         _check(lib, getattr(lib, name)(ctypes.byref(a), _stream(x.device)), name)
 
 
-def k16_bwd(x, sched: dict, w, b, counts, c1t, dx, dw, db, NB16: int, act: int = 1, tokens: int = 0):
+def k16_bwd(x, sched: dict, w, b, counts, c1t, dx, dw, db, NB16: int, act: int = 1, tokens: int = 0,
+            wabsmax=None, rowmax=None):
     """dx, dw, db += the K16/C16 layer's gradients for coefficients c1t [G, B] (GlK16Args); bf16 parameters
     run gl_k16_bwd_tc (split-precision dz on the tensor cores)."""
     _require_cuda(x, w, b, counts, c1t, dx, dw, db, *sched.values())
@@ -512,9 +515,13 @@ def k16_bwd(x, sched: dict, w, b, counts, c1t, dx, dw, db, NB16: int, act: int =
     a = _k16_args(x, sched, w, b, counts, NB16, act, tokens)
     a.c1t, a.dx, a.dw, a.db = _ptr(c1t), _ptr(dx), _ptr(dw), _ptr(db)
     a.ldc, a.lddx = c1t.stride(0), dx.stride(0)
-    name = "gl_k16_bwd_tc" if w.dtype == torch.bfloat16 else "gl_k16_bwd_f32"
     with torch.cuda.device(x.device):
-        _check(lib, getattr(lib, name)(ctypes.byref(a), _stream(x.device)), name)
+        if w.dtype == torch.bfloat16:   # with wabsmax [G] / rowmax [nb] the dX tile is int32 fixed point
+            _require_cuda(wabsmax, rowmax)
+            _check(lib, lib.gl_k16_bwd_tc(ctypes.byref(a), _ptr(wabsmax), _ptr(rowmax), _stream(x.device)),
+                   "gl_k16_bwd_tc")
+        else:
+            _check(lib, lib.gl_k16_bwd_f32(ctypes.byref(a), _stream(x.device)), "gl_k16_bwd_f32")
 
 
 def k16_auto_tokens(B: int, S: int, backward: bool) -> int:

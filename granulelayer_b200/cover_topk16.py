@@ -90,7 +90,13 @@ class _K16Function(torch.autograd.Function):
         dw = mg_w if use_main else torch.zeros(w.shape, device=w.device, dtype=torch.float32)
         db = mg_b if use_main else torch.zeros(b.shape, device=b.device, dtype=torch.float32)
         dx = torch.zeros_like(xc)
-        _native.k16_bwd(xc, layer._work(), w, b, layer.counts, c1t, dx, dw, db, layer.layout.blocks_per_group)
+        wabsmax = rowmax = None
+        if w.dtype == torch.bfloat16 and layer.plan.b200_dx_accum in ("auto", "fixed"):
+            wabsmax = w.reshape(w.shape[0], -1).abs().amax(1).float().contiguous()
+            rowmax = layer._bucket_rowmax()
+        _native.k16_bwd(xc, layer._work(), w, b, layer.counts, c1t, dx, dw, db, layer.layout.blocks_per_group,
+                        wabsmax=wabsmax, rowmax=rowmax)
+        layer.last_info["dx_accumulation"] = "int32 fixed point" if wabsmax is not None else "fp32"
         layer.last_info.update(backward_backend="b200-k16",
                                backward_kernel="gl_k16_bwd_tc" if w.dtype == torch.bfloat16 else "gl_k16_bwd_f32")
         gw = None if use_main else dw.to(w.dtype)
@@ -288,6 +294,24 @@ class CoverTopK16Layer(nn.Module):
                          feat=self.sg_feat.to(torch.int16).contiguous())
             self._work_cache = (key, sched)
         return self._work_cache[1]
+
+    def _bucket_rowmax(self) -> torch.Tensor:
+        """[nb] int32, per row of the schedule's bucket list: the largest number of the bucket's record
+        inputs on one local position (the bound of the tensor-core backward's fixed-point dX tile).
+        Depends only on the graph; cached with the schedule."""
+        sched = self._work()
+        if "rowmax" not in sched:
+            bk = sched["buckets"].to(torch.int64)
+            S, NB16 = int(self.sg_feat.shape[1]), self.layout.blocks_per_group
+            nrec = bk[:, 3].clamp(min=0)
+            bid = torch.repeat_interleave(torch.arange(bk.shape[0], device=bk.device), nrec)
+            within = torch.arange(int(nrec.sum()), device=bk.device) - torch.repeat_interleave(
+                torch.cumsum(nrec, 0) - nrec, nrec)
+            f = (bk[:, 1] * NB16 + bk[:, 2])[bid] + within
+            pos = self.env.reshape(-1, 16)[f].long().clamp(max=S - 1)
+            cnt = torch.bincount((bid[:, None] * S + pos).reshape(-1), minlength=bk.shape[0] * S)
+            sched["rowmax"] = cnt.reshape(-1, S).amax(1).to(torch.int32).contiguous()
+        return sched["rowmax"]
 
     def enable_main_grad(self):
         for p in (self.weight, self.bias):

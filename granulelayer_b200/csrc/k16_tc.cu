@@ -15,8 +15,8 @@
 // contiguous run per warp, so a warp changes output (bucket) rarely.  The forward folds each warp's
 // per-token sums of an output over the lane quad and adds them to pre with one atomic per (token,
 // warp, output).  The backward keeps, per record, z again, the split dz, the dX partials
-// P = dz w (A = the dz accumulator fragments, B = w^T by movmatrix) added to an fp32 [S][BM] tile with
-// shared atomics, and dW += dz^T x (A = dz^T, B = x^T, both by movmatrix), whose fragments are reduced
+// P = dz w (A = the dz accumulator fragments, B = w^T by movmatrix) added to an [S][BM] tile (int32
+// fixed point with the bounds, else fp32) with shared atomics, and dW += dz^T x (A = dz^T, B = x^T, both by movmatrix), whose fragments are reduced
 // into the fp32 gradients once per record and token tile.
 #include "modeb_tc_bwd.cuh"
 
@@ -39,6 +39,9 @@ struct K16TcParams {
   float* dx;
   float* dw;
   float* db;
+  const float* wabsmax;     // backward, fixed-point dX tile: [G] max |w| per output, or NULL
+  const int32_t* brow;      // backward, fixed-point dX tile: [nb] per bucket, its largest number of record
+                            // inputs on one set row
   int B, D, G, NB16, S, nbk;
   int64_t ldx, ldp, ldc, lddx;
 };
@@ -126,6 +129,25 @@ __device__ __forceinline__ bool k16tc_at(const K16TcParams& p, K16TcWalk& w, int
   return g >= 0 && g < p.G && j16 >= 0 && j16 < p.NB16;
 }
 
+// The warp's next valid record, with its operands already requested.
+struct K16TcNext {
+  int r, g, j16;
+  bool have;
+  K16TcRec rec;
+  __device__ __forceinline__ K16TcNext(const K16TcParams& p, K16TcWalk& w, int lane) : r(w.r - 1), have(false) {
+    advance(p, w, lane);
+  }
+  __device__ __forceinline__ void advance(const K16TcParams& p, K16TcWalk& w, int lane) {
+    have = false;
+    while (++r < w.r1)
+      if (k16tc_at(p, w, r, g, j16)) {
+        have = true;
+        rec = k16tc_load(p, (int64_t)g * p.NB16 + j16, lane);
+        return;
+      }
+  }
+};
+
 template <int BM, int ACT>
 __global__ void __launch_bounds__(kK16TcThreads, 1) k16tc_fwd_kernel(const K16TcParams p) {
   constexpr int MT = BM / 16, NW = kK16TcThreads / 32;
@@ -159,17 +181,17 @@ __global__ void __launch_bounds__(kK16TcThreads, 1) k16tc_fwd_kernel(const K16Tc
         }
     }
   };
-  for (int r = wk.r; r < wk.r1; ++r) {
-    int g, j16;
-    if (!k16tc_at(p, wk, r, g, j16)) continue;  // warp-uniform
+  K16TcNext nx(p, wk, lane);
+  while (nx.have) {
+    const int g = nx.g, j16 = nx.j16;
+    const K16TcRec rc = nx.rec;
+    nx.advance(p, wk, lane);  // the next record's operands load while this one computes
     if (g != gcur) {
       if (gcur >= 0) flush();
       gcur = g;
 #pragma unroll
       for (int m = 0; m < MT; ++m) acc[m][0] = acc[m][1] = 0.f;
     }
-    const int64_t f = (int64_t)g * p.NB16 + j16;
-    const K16TcRec rc = k16tc_load(p, f, lane);
     const int nv = __ldg(p.counts + g) - 16 * j16;  // valid neurons of this record (<= 0: none)
     const int row = k16tc_pos(rc.env, (lane & 7) + 8 * (lane >> 4), smax);
     float bias[2][2];
@@ -197,26 +219,63 @@ __global__ void __launch_bounds__(kK16TcThreads, 1) k16tc_fwd_kernel(const K16Tc
   if (gcur >= 0) flush();
 }
 
-// fp32 dX tile [S][BM]: element (s, t) at s * BM + (t ^ (s & (BM - 1))), as dxs_off.
-template <int BM, int ACT>
+// dX tile [S][BM]: element (s, t) at s * BM + (t ^ (s & (BM - 1))), as dxs_off.  FIXED: int32 fixed
+// point at one power-of-two scale per token for the CTA's set, with
+//   16 * max|act'| * sum over the set's buckets b of m_b * |c1t[g_b, t]| * max|w|_{g_b} * scale <= 2^30
+// (m_b = the bucket's largest number of record inputs on one set row), so no word can overflow; shared
+// int32 atomics run at 2.4x the rate of fp32 ones.  A token whose bound is not finite gets NaN in dx.
+template <int BM, int ACT, bool FIXED>
 __global__ void __launch_bounds__(kK16TcThreads, 1) k16tc_bwd_kernel(const K16TcParams p) {
   constexpr int MT = BM / 16, NW = kK16TcThreads / 32;
   extern __shared__ __align__(128) unsigned char tc_smem[];
   __shared__ int fq[256];
+  __shared__ float qsc[FIXED ? BM : 1], qinv[FIXED ? BM : 1];
   float* dxs = reinterpret_cast<float*>(tc_smem + (size_t)p.S * BM * 2);
+  int* dxi = reinterpret_cast<int*>(dxs);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int q = blockIdx.y, t0 = blockIdx.x * BM;
   const uint32_t slab = (uint32_t)__cvta_generic_to_shared(tc_smem);
   k16tc_stage<BM>(slab, fq, p, q, t0);
   for (int i = threadIdx.x; i < p.S * BM; i += kK16TcThreads) dxs[i] = 0.f;
+  if constexpr (FIXED) {
+    if (threadIdx.x < BM) {
+      const int t = t0 + threadIdx.x;
+      const int qa = min(max(__ldg(p.q_off + q), 0), p.nbk), qb = min(max(__ldg(p.q_off + q + 1), qa), p.nbk);
+      float bound = 0.f;
+      if (t < p.B)
+        for (int b = qa; b < qb; ++b) {
+          const int g = __ldg(p.buckets + 4 * b + 1);
+          if (g < 0 || g >= p.G) continue;
+          bound += fabsf(__ldg(p.c1t + (int64_t)g * p.ldc + t)) * (float)__ldg(p.brow + b) * __ldg(p.wabsmax + g);
+        }
+      bound *= 16.f * (ACT == GL_ACT_GELU ? 1.13f : 1.f);
+      float s_ = 0.f, i_ = 0.f;
+      if (!(bound <= 3.0e38f)) {
+        i_ = __int_as_float(0x7fc00000);
+      } else if (bound > 0.f) {
+        const int e = min(max(30 - ilogbf(bound) - 1, -126), 126);
+        s_ = ldexpf(1.f, e);
+        i_ = ldexpf(1.f, -e);
+      }
+      qsc[threadIdx.x] = s_;
+      qinv[threadIdx.x] = i_;
+    }
+  }
   __syncthreads();
+  float sc[MT][2];
+#pragma unroll
+  for (int m = 0; m < MT; ++m)
+#pragma unroll
+    for (int h = 0; h < 2; ++h) sc[m][h] = FIXED ? qsc[16 * m + 8 * h + (lane >> 2)] : 0.f;
   K16TcWalk wk = k16tc_walk(p, q, warp, NW);
   const int cq = 2 * (lane & 3), smax = p.S - 1;
   float c1[MT][2];
   int gcur = -1;
-  for (int r = wk.r; r < wk.r1; ++r) {
-    int g, j16;
-    if (!k16tc_at(p, wk, r, g, j16)) continue;
+  K16TcNext nx(p, wk, lane);
+  while (nx.have) {
+    const int g = nx.g, j16 = nx.j16;
+    const K16TcRec rc = nx.rec;
+    nx.advance(p, wk, lane);
     if (g != gcur) {
       gcur = g;
 #pragma unroll
@@ -228,7 +287,6 @@ __global__ void __launch_bounds__(kK16TcThreads, 1) k16tc_bwd_kernel(const K16Tc
         }
     }
     const int64_t f = (int64_t)g * p.NB16 + j16;
-    const K16TcRec rc = k16tc_load(p, f, lane);
     const int nv = __ldg(p.counts + g) - 16 * j16;
     const int row = k16tc_pos(rc.env, (lane & 7) + 8 * (lane >> 4), smax);
     int prow[2][2];  // slab rows of the inputs 8 kh + cq + e this lane's dX partials belong to
@@ -281,8 +339,13 @@ __global__ void __launch_bounds__(kK16TcThreads, 1) k16tc_bwd_kernel(const K16Tc
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           const int t = 16 * m + 8 * h + (lane >> 2);
-          atomicAdd(dxs + dxs_off<BM>(prow[kh][0], t), P[2 * h]);
-          atomicAdd(dxs + dxs_off<BM>(prow[kh][1], t), P[2 * h + 1]);
+          if constexpr (FIXED) {
+            atomicAdd(dxi + dxs_off<BM>(prow[kh][0], t), __float2int_rn(P[2 * h] * sc[m][h]));
+            atomicAdd(dxi + dxs_off<BM>(prow[kh][1], t), __float2int_rn(P[2 * h + 1] * sc[m][h]));
+          } else {
+            atomicAdd(dxs + dxs_off<BM>(prow[kh][0], t), P[2 * h]);
+            atomicAdd(dxs + dxs_off<BM>(prow[kh][1], t), P[2 * h + 1]);
+          }
         }
       }
       // dW: A = dz^T (neurons x tokens), B = x^T (tokens x inputs 8 kh ..), both transposed in registers
@@ -320,12 +383,21 @@ __global__ void __launch_bounds__(kK16TcThreads, 1) k16tc_bwd_kernel(const K16Tc
   // dx[t0 + t, feat[q][s]] += tile; consecutive threads take consecutive set rows of one token
   for (int it = threadIdx.x; it < p.S * BM; it += kK16TcThreads) {
     const int t = it / p.S, s = it - t * p.S;
-    const float v = dxs[dxs_off<BM>(s, t)];
-    if (t0 + t < p.B && v != 0.f) atomicAdd(p.dx + (int64_t)(t0 + t) * p.lddx + fq[s], v);
+    float v;
+    bool add;
+    if constexpr (FIXED) {
+      const int qv = dxi[dxs_off<BM>(s, t)];
+      v = (float)qv * qinv[t];
+      add = qv != 0 || qinv[t] != qinv[t];
+    } else {
+      v = dxs[dxs_off<BM>(s, t)];
+      add = v != 0.f;
+    }
+    if (t0 + t < p.B && add) atomicAdd(p.dx + (int64_t)(t0 + t) * p.lddx + fq[s], v);
   }
 }
 
-static int k16tc_prepare(const GlK16Args& a, bool bwd, K16TcParams& p) {
+static int k16tc_prepare(const GlK16Args& a, bool bwd, K16TcParams& p, const float* wabsmax, const int32_t* brow) {
   if (a.B < 0 || a.D < 1 || a.D > 32767 || a.G < 1 || a.NB16 < 1 || a.Q < 1 || a.S < 16 || a.S > 256 ||
       a.nbuckets < 0)
     return GL_ERR_SHAPE;
@@ -345,20 +417,20 @@ static int k16tc_prepare(const GlK16Args& a, bool bwd, K16TcParams& p) {
     if (((uintptr_t)a.dw & 7) || ((uintptr_t)a.db & 7)) return GL_ERR_ALIGN;
   }
   p = K16TcParams{a.x, a.env, a.feat, a.buckets, a.q_off, a.rec_off, reinterpret_cast<const uint16_t*>(a.w),
-                  reinterpret_cast<const uint16_t*>(a.b), a.counts, a.pre, a.c1t, a.dx, a.dw, a.db,
+                  reinterpret_cast<const uint16_t*>(a.b), a.counts, a.pre, a.c1t, a.dx, a.dw, a.db, wabsmax, brow,
                   (int)a.B, (int)a.D, (int)a.G, (int)a.NB16, (int)a.S, (int)a.nbuckets,
                   a.ldx, a.ldp, a.ldc, a.lddx};
   return GL_OK;
 }
 
-template <int BM, int ACT, bool BWD>
+template <int BM, int ACT, bool BWD, bool FIXED>
 static int k16tc_launch(const K16TcParams& p, int64_t Q, cudaStream_t st) {
   const size_t smem = (size_t)p.S * BM * (BWD ? 6 : 2);
-  const void* kern = BWD ? (const void*)k16tc_bwd_kernel<BM, ACT> : (const void*)k16tc_fwd_kernel<BM, ACT>;
+  const void* kern = BWD ? (const void*)k16tc_bwd_kernel<BM, ACT, FIXED> : (const void*)k16tc_fwd_kernel<BM, ACT>;
   int rc = ensure_dynamic_smem(kern, smem);
   if (rc) return rc;
   const dim3 grid((unsigned)((p.B + BM - 1) / BM), (unsigned)Q);
-  if constexpr (BWD) k16tc_bwd_kernel<BM, ACT><<<grid, kK16TcThreads, smem, st>>>(p);
+  if constexpr (BWD) k16tc_bwd_kernel<BM, ACT, FIXED><<<grid, kK16TcThreads, smem, st>>>(p);
   else k16tc_fwd_kernel<BM, ACT><<<grid, kK16TcThreads, smem, st>>>(p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_cuda_error(e);
@@ -366,11 +438,20 @@ static int k16tc_launch(const K16TcParams& p, int64_t Q, cudaStream_t st) {
   return GL_OK;
 }
 
+template <int BM, bool BWD>
+static int k16tc_act(const K16TcParams& p, int64_t Q, bool relu, bool fixed, cudaStream_t st) {
+  if (fixed) return relu ? k16tc_launch<BM, GL_ACT_RELU, BWD, true>(p, Q, st)
+                         : k16tc_launch<BM, GL_ACT_IDENTITY, BWD, true>(p, Q, st);
+  return relu ? k16tc_launch<BM, GL_ACT_RELU, BWD, false>(p, Q, st)
+              : k16tc_launch<BM, GL_ACT_IDENTITY, BWD, false>(p, Q, st);
+}
+
 template <bool BWD>
-static int k16tc_run(const GlK16Args* args, void* stream) {
+static int k16tc_run(const GlK16Args* args, const float* wabsmax, const int32_t* brow, void* stream) {
   if (!args) return GL_ERR_NULL;
+  if ((wabsmax == nullptr) != (brow == nullptr)) return GL_ERR_NULL;
   K16TcParams p;
-  int rc = k16tc_prepare(*args, BWD, p);
+  int rc = k16tc_prepare(*args, BWD, p, wabsmax, brow);
   if (rc) return rc > 0 ? GL_OK : rc;
   int BM = args->tokens;
   if (BM == 0) BM = BWD ? 64 : 128;
@@ -379,19 +460,20 @@ static int k16tc_run(const GlK16Args* args, void* stream) {
   if ((rc = device_smem_optin(&optin))) return rc;
   if ((int64_t)p.S * BM * (BWD ? 6 : 2) + 8192 > optin) return GL_ERR_SMEM;
   cudaStream_t st = (cudaStream_t)stream;
-  const bool relu = args->act == GL_ACT_RELU;
+  const bool relu = args->act == GL_ACT_RELU, fixed = BWD && wabsmax != nullptr;
   switch (BM) {
-    case 128: return relu ? k16tc_launch<128, GL_ACT_RELU, BWD>(p, args->Q, st)
-                          : k16tc_launch<128, GL_ACT_IDENTITY, BWD>(p, args->Q, st);
-    case 64: return relu ? k16tc_launch<64, GL_ACT_RELU, BWD>(p, args->Q, st)
-                         : k16tc_launch<64, GL_ACT_IDENTITY, BWD>(p, args->Q, st);
-    default: return relu ? k16tc_launch<32, GL_ACT_RELU, BWD>(p, args->Q, st)
-                         : k16tc_launch<32, GL_ACT_IDENTITY, BWD>(p, args->Q, st);
+    case 128: return k16tc_act<128, BWD>(p, args->Q, relu, fixed, st);
+    case 64: return k16tc_act<64, BWD>(p, args->Q, relu, fixed, st);
+    default: return k16tc_act<32, BWD>(p, args->Q, relu, fixed, st);
   }
 }
 
 }  // namespace gl
 
-extern "C" int gl_k16_fwd_tc(const GlK16Args* args, void* stream) { return gl::k16tc_run<false>(args, stream); }
+extern "C" int gl_k16_fwd_tc(const GlK16Args* args, void* stream) {
+  return gl::k16tc_run<false>(args, nullptr, nullptr, stream);
+}
 
-extern "C" int gl_k16_bwd_tc(const GlK16Args* args, void* stream) { return gl::k16tc_run<true>(args, stream); }
+extern "C" int gl_k16_bwd_tc(const GlK16Args* args, const float* wabsmax, const int32_t* rowmax, void* stream) {
+  return gl::k16tc_run<true>(args, wabsmax, rowmax, stream);
+}

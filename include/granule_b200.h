@@ -44,7 +44,7 @@
 extern "C" {
 #endif
 
-#define GL_ABI_VERSION 12
+#define GL_ABI_VERSION 13
 
 typedef enum GlStatus {
   GL_OK = 0,
@@ -418,7 +418,11 @@ int gl_k16_auto_tokens(int64_t B, int64_t S, int32_t backward);
  * Same arguments, layouts and accumulation as gl_k16_fwd_f32 / gl_k16_bwd_f32 (dw, db fp32); `tokens` =
  * 0 (automatic), 32, 64 or 128 tokens per block; S <= 256. */
 int gl_k16_fwd_tc(const GlK16Args* args, void* stream);
-int gl_k16_bwd_tc(const GlK16Args* args, void* stream);
+/* With `wabsmax` ([G] max |w| over each output's records) and `rowmax` ([nbuckets] per row of `buckets`, the
+ * bucket's largest number of record inputs on one local position) the dX tile is int32 fixed point at one
+ * power-of-two scale per token and set (16 max|act'| sum_b rowmax_b |c1t[g_b, t]| wabsmax_{g_b} scale <=
+ * 2^30; a token whose bound is not finite gets NaN); with both NULL it is fp32. */
+int gl_k16_bwd_tc(const GlK16Args* args, const float* wabsmax, const int32_t* rowmax, void* stream);
 
 /* Number of kernels this library has launched successfully in this process
    (all devices).  Benchmarks difference it around a timed region. */

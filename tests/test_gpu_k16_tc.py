@@ -63,6 +63,7 @@ def _check(lay, x, gy):
     torch.cuda.synchronize()
     assert lay.last_info["forward_kernel"] == "gl_k16_fwd_tc"
     assert lay.last_info["backward_kernel"] == "gl_k16_bwd_tc"
+    assert lay.last_info["dx_accumulation"] == "int32 fixed point"
     xr = x.to(torch.bfloat16).double().numpy()
     idx = lay.indices.cpu().numpy()
     w = lay.weight.detach().double().cpu().numpy()
@@ -95,15 +96,18 @@ def test_bf16_config4_shape_slice():
 
 
 def test_token_tiles_agree():
-    """Explicit token tiles of the forward (32, 64, 128) and backward (32, 64, 128) give the same results
-    within the tolerances (the order of the fp32 atomics differs)."""
+    """Explicit token tiles of the forward (32, 64, 128) and backward (32, 64, 128), and the backward's
+    fp32 and int32 fixed-point dX tiles, give the same results within the tolerances (the order of the
+    fp32 atomics differs)."""
     lay = _layer(512, 20000, 16, 16, seed=5)
     sched, L = lay._work(), lay.layout
     gen = torch.Generator().manual_seed(9)
     x = torch.randn(200, 512, generator=gen).to(torch.bfloat16).float().cuda()
     c1t = torch.randn(16, 200, generator=gen).cuda()
+    wabsmax = lay.weight.detach().reshape(16, -1).abs().amax(1).float().contiguous()
+    rowmax = lay._bucket_rowmax()
     outs = []
-    for tok in (32, 64, 128):
+    for tok, fixed in ((32, False), (64, False), (128, False), (64, True), (32, True)):
         pre = torch.zeros(200, 16, device="cuda")
         _native.k16_fwd(x, sched, lay.weight.detach(), lay.bias.detach(), lay.counts, pre, L.blocks_per_group,
                         tokens=tok)
@@ -111,7 +115,8 @@ def test_token_tiles_agree():
         dw = torch.zeros(lay.weight.shape, device="cuda")
         db = torch.zeros(lay.bias.shape, device="cuda")
         _native.k16_bwd(x, sched, lay.weight.detach(), lay.bias.detach(), lay.counts, c1t, dx, dw, db,
-                        L.blocks_per_group, tokens=tok)
+                        L.blocks_per_group, tokens=tok, wabsmax=wabsmax if fixed else None,
+                        rowmax=rowmax if fixed else None)
         torch.cuda.synchronize()
         outs.append((pre.cpu(), dx.cpu(), dw.cpu(), db.cpu()))
     for o in outs[1:]:
