@@ -331,7 +331,8 @@ def run_reference_gpu(args):
     torch.cuda.set_device(dev)
     if args.workload == "modeb":
         Hm, Dm, Gm, Bm = args.modeb_neurons, 1024, 1024, 8192
-        cases = [(pool, C, torch.bfloat16) for pool, C in (("mean", 8), ("mean", 64), ("max", 8), ("max", 64))]
+        rdt = torch.float32 if args.ref_dtype == "fp32" else torch.bfloat16
+        cases = [(pool, C, rdt) for pool, C in (("mean", 8), ("mean", 64), ("max", 8), ("max", 64))]
         metric, steps = MB_METRIC, max(1, min(args.steps, 5))
     elif args.workload == "sets":
         Hm, Dm, Gm, Bm = args.modeb_neurons, 1024, 1024, 8192
@@ -349,6 +350,8 @@ def run_reference_gpu(args):
             if args.workload == "sets":
                 from sparse_pooling.supergroups import ConnectivityPlan as RefConnectivity
                 extra["connectivity"] = RefConnectivity(64, 16, seed=0)
+            if args.workload == "modeb" and dtype == torch.float32:
+                extra["backend"] = "triton"   # its CUDA kernels are BF16-only; fp32 layers run its Triton path
             lay = RefLayer(Dm, Hm, Gm, shared_neurons=C, pooling=pool, dtype=dtype, device=dev, seed=0,
                            checkpoint_policy=policy, **extra)
             lay.enable_main_grad()
@@ -887,6 +890,8 @@ def main():
                                                        "(comma list of f32, bf16; default all)")
     ap.add_argument("--sets-tokens", default="0", help="sets: token tiles of the input-set backward to time "
                                                       "(comma list; 0 = automatic)")
+    ap.add_argument("--ref-dtype", default="bf16", choices=["fp32", "bf16"],
+                    help="--impl reference-gpu --workload modeb: the reference layer's parameter dtype")
     ap.add_argument("--cover-dtype", default="fp32", choices=["fp32", "bf16"],
                     help="cover16: parameter storage (fp32 = config 4; bf16 = the reference's, on the tensor cores)")
     ap.add_argument("--cover-outputs", type=int, default=2048,
