@@ -76,6 +76,47 @@ def test_argument_validation_needs_no_device():
     assert lib.gl_k16_auto_tokens(0, 64, 0) == -2
 
 
+def test_tensor_core_entry_points_validate_before_the_device():
+    """The bf16 tensor-core entry points (Mode B generic and input-set, K16) reject bad arguments and
+    run empty problems as no-ops without touching a device."""
+    lib = _native.load()
+    for fn in (lib.gl_fwd_shared_tc,):
+        assert fn(None, None) == -1
+    assert lib.gl_bwd_shared_tc(None, None, None, None) == -1
+    sa = _native.GlSharedArgs()
+    sa.B, sa.D, sa.NB, sa.C, sa.g0, sa.g1, sa.packed, sa.wdtype = 4, 64, 4, 8, 0, 1, 1, _native.DTYPE_BF16
+    sa.pool, sa.act = _native.POOL_MEAN, _native.ACT_IDS["relu"]
+    assert lib.gl_fwd_shared_tc(ctypes.byref(sa), None) == -1          # null pointers
+    sa.packed = 0                                                       # canonical storage: not this path
+    assert lib.gl_fwd_shared_tc(ctypes.byref(sa), None) == -4
+    sa.packed, sa.wdtype = 1, _native.DTYPE_F32                         # fp32 storage: not this path
+    assert lib.gl_fwd_shared_tc(ctypes.byref(sa), None) == -4
+    sa.wdtype, sa.pool = _native.DTYPE_BF16, _native.POOL_MAX           # no max backward here
+    assert lib.gl_bwd_shared_tc(ctypes.byref(sa), None, None, None) == -4
+    sa.pool, sa.C = _native.POOL_MEAN, 12
+    assert lib.gl_fwd_shared_tc(ctypes.byref(sa), None) == -2
+    sa.C, sa.B = 8, 0                                                   # empty batch: a no-op
+    assert lib.gl_fwd_shared_tc(ctypes.byref(sa), None) == 0
+    assert lib.gl_bwd_shared_tc_sets(None, None, None) == -1
+    assert lib.gl_fwd_shared_tc_sets(None, None, None) == -1
+    st = _native.GlSetArgs()
+    sa.B = 4
+    assert lib.gl_bwd_shared_tc_sets(ctypes.byref(sa), ctypes.byref(st), None) == -1   # null pointers
+    sa.pool = _native.POOL_MAX
+    assert lib.gl_fwd_shared_tc_sets(ctypes.byref(sa), ctypes.byref(st), None) == -4   # mean / sum only
+    assert lib.gl_k16_fwd_tc(None, None) == -1
+    assert lib.gl_k16_bwd_tc(None, None, None, None) == -1
+    k = _native.GlK16Args()
+    k.B, k.D, k.G, k.NB16, k.Q, k.S, k.nbuckets, k.act = 4, 64, 2, 3, 1, 300, 1, _native.ACT_IDS["relu"]
+    assert lib.gl_k16_fwd_tc(ctypes.byref(k), None) == -2                # S beyond uint8 local positions
+    k.S = 64
+    assert lib.gl_k16_fwd_tc(ctypes.byref(k), None) == -1                # null pointers
+    k.act = _native.ACT_IDS["gelu"]
+    assert lib.gl_k16_bwd_tc(ctypes.byref(k), None, None, None) == -4    # ReLU / identity only
+    k.act, k.B = _native.ACT_IDS["relu"], 0                              # empty batch: a no-op
+    assert lib.gl_k16_bwd_tc(ctypes.byref(k), None, None, None) == 0
+
+
 def test_struct_layout_matches_header():
     # field order and sizes of the ctypes mirrors (pointers 8 B, int64 8 B, int32/float 4 B)
     assert ctypes.sizeof(_native.GlFwdArgs) == 6 * 8 + 7 * 8 + 4 * 4 + 2 * 8 + 4 * 8 + 2 * 8 + 2 * 8 + 4 * 4
@@ -84,6 +125,7 @@ def test_struct_layout_matches_header():
     assert ctypes.sizeof(_native.GlK16Args) == 14 * 8 + 11 * 8 + 2 * 4
     assert ctypes.sizeof(_native.GlSharedArgs) == 10 * 8 + 10 * 8 + 6 * 4 + 2 * 8 + 4 * 8 + 2 * 4
     assert ctypes.sizeof(_native.GlEventArgs) == 9 * 8 + 10 * 8 + 6 * 4
+    assert ctypes.sizeof(_native.GlSetArgs) == 5 * 8 + 3 * 8
 
 
 def test_missing_library_fails_loudly(tmp_path):
