@@ -100,6 +100,15 @@ def peak_hbm():
         return FALLBACK_HBM_GBS, "fallback"
 
 
+def peak_bf16():
+    """Dense bf16 tensor rate (TFLOP/s): the burst figure of MEASURED_PEAKS.json, else the fallback."""
+    p = ROOT / "MEASURED_PEAKS.json"
+    try:
+        return float(json.loads(p.read_text())["bf16_tflops"]), "measured"
+    except Exception:
+        return 1590.0, "fallback"
+
+
 def config_dict(world):
     return {"workload": "100M-neuron fan-in-8 Mode-A fp32 mean-ReLU layer: fwd+bwd+fused Adam step "
                         "(D=4096, N=100,663,296, G=4096 groups of 24,576, B=1024)",
@@ -433,6 +442,7 @@ def cover16_cpu_baseline(lay, x, dy, target_s=8.0):
 def bench_cover16(args, world):
     """BASELINE config 4 (module docstring); rank 0 only."""
     from granulelayer_b200 import _native
+    from granulelayer_b200.config import PhysicalPlan
     from granulelayer_b200.cover_topk16 import CoverTopK16Layer
     from granulelayer_b200.kgen import KLayout, init_envelope_parameters
     from granulelayer_b200.supergroups import ConnectivityPlan
@@ -444,8 +454,10 @@ def bench_cover16(args, world):
     t0 = time.perf_counter()
     w64, b64 = init_envelope_parameters(KLayout(Dc, Hc, Gc, 64, 256), dev, dtype=torch.bfloat16, seed=3)
     pdt = torch.bfloat16 if args.cover_dtype == "bf16" else torch.float32
+    plan = PhysicalPlan(grad_precision="split", b200_f32_tensor_cores="off" if args.cover_kernels == "simt" else "auto")
     lay = CoverTopK16Layer.from_envelope(w64, b64, input_dim=Dc, hidden_dim=Hc, output_dim=Gc,
-                                         connectivity=ConnectivityPlan(64, 64, seed=3), device=dev, dtype=pdt)
+                                         connectivity=ConnectivityPlan(64, 64, seed=3), device=dev, dtype=pdt,
+                                         plan=plan)
     del w64, b64
     torch.cuda.synchronize(dev)
     torch.cuda.empty_cache()
@@ -461,9 +473,10 @@ def bench_cover16(args, world):
         def wrap(*a, **k):
             s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             s.record()
-            orig[name](*a, **k)
+            r = orig[name](*a, **k)
             e.record()
             ev[name].append((s, e))
+            return r
         return wrap
 
     def step():
@@ -529,26 +542,40 @@ def bench_cover16(args, world):
     fwd_flop = 2 * 16 * Hc * Bc
     achieved = bwd_flop / (bwd_ms * 1e-3) / 1e12
     hbm, hbm_kind = peak_hbm()
+    fkern, bkern = lay.last_info.get("forward_kernel"), lay.last_info.get("backward_kernel")
+    if lay.tensor_cores:
+        # bf16 MMA flops the backward executes: z once, dX and dW from the bf16 terms -- bf16 layer:
+        # 1 + 2 + 2 products (dz as hi + lo); fp32 layer: 6 + 6 + 6 (three-term splits, pairs i + j <= 2)
+        mma_flop = bwd_flop / 3 * (5 if pdt == torch.bfloat16 else 18)
+        tc_peak, tc_kind = peak_bf16()
+        roof = {"bound": "tensor", "kernel": bkern, "achieved": mma_flop / (bwd_ms * 1e-3) / 1e12, "peak": tc_peak,
+                "unit": "TFLOP/s", "frac": mma_flop / (bwd_ms * 1e-3) / 1e12 / tc_peak,
+                "peak_source": f"{tc_kind} dense bf16 (cuBLAS, burst) -- these are mma.sync tiles",
+                "algorithmic_flop_per_launch": mma_flop, "flop_definition": "bf16 MMA flops of the term products",
+                "fp32_equivalent_tflops": achieved}
+    else:
+        roof = {"bound": "fp32", "kernel": bkern, "achieved": achieved, "peak": peak_tflops, "unit": "TFLOP/s",
+                "frac": achieved / peak_tflops,
+                "peak_source": f"nominal fp32 FMA rate: {sms} SMs x 128 lanes x 2 flop at the median "
+                               f"sampled SM clock {mhz} MHz",
+                "algorithmic_flop_per_launch": bwd_flop}
     wbytes = Hc * (16 * 4 + 4) + (Hc // 16) * 16
     line = {
         "metric": COVER_METRIC, "value": Bc * Hc / (ms / 1e3), "unit": UNIT, "n_gpus": 1, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "none",
         "vs_baseline": None, "dtype": "f32" if pdt == torch.float32 else "bf16", "data": "synthetic",
         "config": {"workload": "Cover-TopK16 opt-in layer, compact K16/C16 execution, fwd+bwd (BASELINE config 4)"
-                               + ("" if pdt == torch.float32 else "; bf16 parameters on the tensor cores (the "
-                                  "reference's arithmetic), not config 4's fp32"),
+                               + (("; fp32 on the tensor cores (three-term bf16 splits of x, w, dz)" if lay.tensor_cores
+                                   else "; fp32 SIMT kernels") if pdt == torch.float32
+                                  else "; bf16 parameters on the tensor cores (the reference's arithmetic), not "
+                                       "config 4's fp32"),
+                   "kernels": [fkern, bkern],
                    "D": Dc, "N": Hc, "G": Gc, "global_batch": Bc, "envelope": "K64/C256, w64 ~ N(0,1/64) BF16",
                    "S": 64, "R": 64, "Q": int(lay.sg_feat.shape[0]), "records_16": int(Hc // 16),
                    "l2": f"weights {Hc * 64 / 1e9:.1f} GB fp32 > L2: streamed from HBM every pass",
                    "build_seconds": build_s},
-        "roofline": {"bound": "fp32", "kernel": "gl_k16_bwd_f32 (k16_bwd_kernel<relu>)" if pdt == torch.float32
-                     else "gl_k16_bwd_tc (fp32 FMA rate shown for comparison)", "achieved": achieved,
-                     "peak": peak_tflops, "unit": "TFLOP/s", "frac": achieved / peak_tflops,
-                     "peak_source": f"nominal fp32 FMA rate: {sms} SMs x 128 lanes x 2 flop at the median "
-                                    f"sampled SM clock {mhz} MHz",
-                     "algorithmic_flop_per_launch": bwd_flop,
-                     "hbm_fraction_bwd": (2 * wbytes) / (bwd_ms * 1e-3) / (hbm * 1e9), "hbm_peak_source": hbm_kind,
-                     "traffic": None},
+        "roofline": dict(roof, hbm_fraction_bwd=(2 * wbytes) / (bwd_ms * 1e-3) / (hbm * 1e9),
+                         hbm_peak_source=hbm_kind, traffic=None),
         "kernels_ms": {"fwd": fwd_ms, "bwd": bwd_ms,
                        "fwd_tflops": fwd_flop / (fwd_ms * 1e-3) / 1e12, "bwd_tflops": achieved},
         "clocks": clocks, "gpu_launches": launches, "e2e": e2e, "cpu_baseline": cb,
@@ -894,6 +921,8 @@ def main():
                     help="--impl reference-gpu --workload modeb: the reference layer's parameter dtype")
     ap.add_argument("--cover-dtype", default="fp32", choices=["fp32", "bf16"],
                     help="cover16: parameter storage (fp32 = config 4; bf16 = the reference's, on the tensor cores)")
+    ap.add_argument("--cover-kernels", default="tc", choices=["tc", "simt"],
+                    help="cover16, fp32: tensor-core kernels on three-term bf16 splits (default) or the fp32 SIMT ones")
     ap.add_argument("--cover-outputs", type=int, default=2048,
                     help="cover16: outputs of 24,576 neurons (default 2048 = config 4; fewer for ncu captures)")
     ap.add_argument("--groups", type=int, default=G,

@@ -16,7 +16,7 @@ from pathlib import Path
 
 import torch
 
-ABI_VERSION = 13
+ABI_VERSION = 14
 LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libgranule_b200.so"
 
 POOL_MEAN, POOL_SUM, POOL_MAX, POOL_LME, POOL_POWER, POOL_SOFTMAX, POOL_TOPK = 0, 1, 2, 3, 4, 5, 6
@@ -41,7 +41,8 @@ EXPORTS = ("gl_abi_version", "gl_status_string", "gl_last_cuda_error", "gl_fwd_f
            "gl_bwd_shared_f32",
            "gl_bwd_events_f32",
            "gl_shared_auto_tokens", "gl_bwd_shared_det_f32", "gl_bwd_shared_det_static_f32", "gl_k16_fwd_f32",
-           "gl_k16_bwd_f32", "gl_k16_auto_tokens", "gl_k16_fwd_tc", "gl_k16_bwd_tc")
+           "gl_k16_bwd_f32", "gl_k16_auto_tokens", "gl_k16_fwd_tc", "gl_k16_bwd_tc", "gl_k16_fwd_tc_f32",
+           "gl_k16_bwd_tc_f32")
 
 
 class GlSetArgs(ctypes.Structure):
@@ -141,7 +142,7 @@ def load(path=None) -> ctypes.CDLL:
         lib.gl_launch_count.restype = ctypes.c_int64
         for name, st in (("gl_fwd_f32", GlFwdArgs), ("gl_bwd_f32", GlBwdArgs), ("gl_adam_f32", GlAdamArgs),
                          ("gl_k16_fwd_f32", GlK16Args), ("gl_k16_bwd_f32", GlK16Args),
-                         ("gl_k16_fwd_tc", GlK16Args),
+                         ("gl_k16_fwd_tc", GlK16Args), ("gl_k16_fwd_tc_f32", GlK16Args),
                          ("gl_fwd_shared_f32", GlSharedArgs), ("gl_bwd_shared_f32", GlSharedArgs),
                          ("gl_bwd_events_f32", GlEventArgs)):
             fn = getattr(lib, name)
@@ -179,8 +180,9 @@ def load(path=None) -> ctypes.CDLL:
         lib.gl_bwd_shared_tc.argtypes = [ctypes.POINTER(GlSharedArgs), ctypes.c_void_p, ctypes.c_void_p,
                                          ctypes.c_void_p]
         lib.gl_bwd_shared_tc.restype = ctypes.c_int
-        lib.gl_k16_bwd_tc.argtypes = [ctypes.POINTER(GlK16Args), ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
-        lib.gl_k16_bwd_tc.restype = ctypes.c_int
+        for name in ("gl_k16_bwd_tc", "gl_k16_bwd_tc_f32"):
+            getattr(lib, name).argtypes = [ctypes.POINTER(GlK16Args), ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+            getattr(lib, name).restype = ctypes.c_int
         lib.gl_bwd_shared_tc_sets.argtypes = [ctypes.POINTER(GlSharedArgs), ctypes.POINTER(GlSetArgs), ctypes.c_void_p]
         lib.gl_bwd_shared_tc_sets.restype = ctypes.c_int
         lib.gl_fwd_shared_tc_sets.argtypes = [ctypes.POINTER(GlSharedArgs), ctypes.POINTER(GlSetArgs), ctypes.c_void_p]
@@ -493,35 +495,52 @@ def _k16_args(x, sched, w, b, counts, NB16: int, act: int, tokens: int):
                      sched["buckets"].shape[0], x.stride(0), 0, 0, 0, act, tokens)
 
 
-def k16_fwd(x, sched: dict, w, b, counts, pre, NB16: int, act: int = 1, tokens: int = 0):
+def _k16_entry(w, tensor_cores: bool, bwd: bool) -> str:
+    """bf16 parameters: the tensor-core entry; fp32 ones: the tensor-core entry on three-term bf16 splits
+    when ``tensor_cores``, else the SIMT one."""
+    kind = "bwd" if bwd else "fwd"
+    if w.dtype == torch.bfloat16:
+        return f"gl_k16_{kind}_tc"
+    return f"gl_k16_{kind}_tc_f32" if tensor_cores else f"gl_k16_{kind}_f32"
+
+
+def k16_fwd(x, sched: dict, w, b, counts, pre, NB16: int, act: int = 1, tokens: int = 0,
+            tensor_cores: bool = False) -> str:
     """pre[t, g] += Mean-pooled act(z) of the K16/C16 layer (GlK16Args); ``sched`` holds env, feat,
     buckets (sorted by set), q_off and rec_off.  bf16 parameters run the tensor-core entry
-    (gl_k16_fwd_tc, x rounded to bf16), fp32 ones gl_k16_fwd_f32."""
+    (gl_k16_fwd_tc, x rounded to bf16); fp32 ones gl_k16_fwd_tc_f32 with ``tensor_cores``, else
+    gl_k16_fwd_f32.  Returns the entry's name."""
     _require_cuda(x, w, b, counts, pre, *sched.values())
     lib = load()
     a = _k16_args(x, sched, w, b, counts, NB16, act, tokens)
     a.pre, a.ldp = _ptr(pre), pre.stride(0)
-    name = "gl_k16_fwd_tc" if w.dtype == torch.bfloat16 else "gl_k16_fwd_f32"
+    name = _k16_entry(w, tensor_cores, False)
     with torch.cuda.device(x.device):
         _check(lib, getattr(lib, name)(ctypes.byref(a), _stream(x.device)), name)
+    return name
 
 
 def k16_bwd(x, sched: dict, w, b, counts, c1t, dx, dw, db, NB16: int, act: int = 1, tokens: int = 0,
-            wabsmax=None, rowmax=None):
-    """dx, dw, db += the K16/C16 layer's gradients for coefficients c1t [G, B] (GlK16Args); bf16 parameters
-    run gl_k16_bwd_tc (split-precision dz on the tensor cores)."""
+            wabsmax=None, rowmax=None, tensor_cores: bool = False) -> str:
+    """dx, dw, db += the K16/C16 layer's gradients for coefficients c1t [G, B] (GlK16Args).  The tensor-core
+    entries (bf16 parameters; fp32 ones with ``tensor_cores``) take the optional fixed-point dX bounds
+    wabsmax [G] / rowmax [nb]; the fp32 SIMT entry takes none.  Returns the entry's name."""
     _require_cuda(x, w, b, counts, c1t, dx, dw, db, *sched.values())
     lib = load()
     a = _k16_args(x, sched, w, b, counts, NB16, act, tokens)
     a.c1t, a.dx, a.dw, a.db = _ptr(c1t), _ptr(dx), _ptr(dw), _ptr(db)
     a.ldc, a.lddx = c1t.stride(0), dx.stride(0)
+    name = _k16_entry(w, tensor_cores, True)
     with torch.cuda.device(x.device):
-        if w.dtype == torch.bfloat16:   # with wabsmax [G] / rowmax [nb] the dX tile is int32 fixed point
-            _require_cuda(wabsmax, rowmax)
-            _check(lib, lib.gl_k16_bwd_tc(ctypes.byref(a), _ptr(wabsmax), _ptr(rowmax), _stream(x.device)),
-                   "gl_k16_bwd_tc")
+        if name == "gl_k16_bwd_f32":
+            if wabsmax is not None or rowmax is not None:
+                raise ValueError("gl_k16_bwd_f32 takes no fixed-point dX bounds")
+            _check(lib, lib.gl_k16_bwd_f32(ctypes.byref(a), _stream(x.device)), name)
         else:
-            _check(lib, lib.gl_k16_bwd_f32(ctypes.byref(a), _stream(x.device)), "gl_k16_bwd_f32")
+            if wabsmax is not None or rowmax is not None:
+                _require_cuda(wabsmax, rowmax)
+            _check(lib, getattr(lib, name)(ctypes.byref(a), _ptr(wabsmax), _ptr(rowmax), _stream(x.device)), name)
+    return name
 
 
 def k16_auto_tokens(B: int, S: int, backward: bool) -> int:

@@ -269,6 +269,9 @@ class PhysicalPlan:
     # kernels; "off" = the fp32 kernels, which widen the bf16 parameters.  Either way a bf16 layer
     # computes on x rounded to bf16, the reference's compute dtype
     b200_bf16_tensor_cores: str = "auto"
+    # fp32 Cover-TopK16 layers: "auto" = the tensor-core kernels on three-term bf16 splits of x, w and dz
+    # (gl_k16_*_tc_f32, fp32-level results); "off" = the fp32 SIMT kernels (gl_k16_*_f32)
+    b200_f32_tensor_cores: str = "auto"
 
     def __post_init__(self):
         if self.input_layout not in ("feature_major", "token_major"):
@@ -297,6 +300,8 @@ class PhysicalPlan:
             raise ValueError("b200_locality must be 'auto' or 'off'")
         if self.b200_bf16_tensor_cores not in ("auto", "off"):
             raise ValueError("b200_bf16_tensor_cores must be 'auto' or 'off'")
+        if self.b200_f32_tensor_cores not in ("auto", "off"):
+            raise ValueError("b200_f32_tensor_cores must be 'auto' or 'off'")
 
 
 def resolve_reduction(plan: PhysicalPlan):

@@ -72,11 +72,11 @@ class _K16Function(torch.autograd.Function):
             xc = xc.contiguous()
         B = xc.shape[0]
         pre = torch.zeros((B, layer.layout.groups), device=x.device, dtype=torch.float32)
-        _native.k16_fwd(xc, layer._work(), w, b, layer.counts, pre, layer.layout.blocks_per_group)
+        name = _native.k16_fwd(xc, layer._work(), w, b, layer.counts, pre, layer.layout.blocks_per_group,
+                               tensor_cores=layer.tensor_cores)
         ctx.layer = layer
         ctx.save_for_backward(x, w, b)
-        layer.last_info.update(forward_backend="b200-k16", checkpoint_bytes=0,
-                               forward_kernel="gl_k16_fwd_tc" if w.dtype == torch.bfloat16 else "gl_k16_fwd_f32")
+        layer.last_info.update(forward_backend="b200-k16", checkpoint_bytes=0, forward_kernel=name)
         return pre
 
     @staticmethod
@@ -91,14 +91,14 @@ class _K16Function(torch.autograd.Function):
         db = mg_b if use_main else torch.zeros(b.shape, device=b.device, dtype=torch.float32)
         dx = torch.zeros_like(xc)
         wabsmax = rowmax = None
-        if w.dtype == torch.bfloat16 and layer.plan.b200_dx_accum in ("auto", "fixed"):
+        tc = layer.tensor_cores
+        if tc and layer.plan.b200_dx_accum in ("auto", "fixed"):
             wabsmax = w.reshape(w.shape[0], -1).abs().amax(1).float().contiguous()
             rowmax = layer._bucket_rowmax()
-        _native.k16_bwd(xc, layer._work(), w, b, layer.counts, c1t, dx, dw, db, layer.layout.blocks_per_group,
-                        wabsmax=wabsmax, rowmax=rowmax)
+        name = _native.k16_bwd(xc, layer._work(), w, b, layer.counts, c1t, dx, dw, db,
+                               layer.layout.blocks_per_group, wabsmax=wabsmax, rowmax=rowmax, tensor_cores=tc)
         layer.last_info["dx_accumulation"] = "int32 fixed point" if wabsmax is not None else "fp32"
-        layer.last_info.update(backward_backend="b200-k16",
-                               backward_kernel="gl_k16_bwd_tc" if w.dtype == torch.bfloat16 else "gl_k16_bwd_f32")
+        layer.last_info.update(backward_backend="b200-k16", backward_kernel=name)
         gw = None if use_main else dw.to(w.dtype)
         gb = None if use_main else db.to(b.dtype)
         return dx.to(x.dtype), gw, gb, None
@@ -312,6 +312,12 @@ class CoverTopK16Layer(nn.Module):
             cnt = torch.bincount((bid[:, None] * S + pos).reshape(-1), minlength=bk.shape[0] * S)
             sched["rowmax"] = cnt.reshape(-1, S).amax(1).to(torch.int32).contiguous()
         return sched["rowmax"]
+
+    @property
+    def tensor_cores(self) -> bool:
+        """Whether the layer runs the tensor-core kernels: always for bf16 parameters; for fp32 ones, the
+        three-term bf16 split kernels unless ``plan.b200_f32_tensor_cores == "off"``."""
+        return self.weight.dtype == torch.bfloat16 or self.plan.b200_f32_tensor_cores == "auto"
 
     def enable_main_grad(self):
         for p in (self.weight, self.bias):

@@ -115,6 +115,17 @@ def test_tensor_core_entry_points_validate_before_the_device():
     assert lib.gl_k16_bwd_tc(ctypes.byref(k), None, None, None) == -4    # ReLU / identity only
     k.act, k.B = _native.ACT_IDS["relu"], 0                              # empty batch: a no-op
     assert lib.gl_k16_bwd_tc(ctypes.byref(k), None, None, None) == 0
+    # the fp32 split entries validate the same way
+    assert lib.gl_k16_fwd_tc_f32(None, None) == -1
+    assert lib.gl_k16_bwd_tc_f32(None, None, None, None) == -1
+    k.B, k.S = 4, 300
+    assert lib.gl_k16_fwd_tc_f32(ctypes.byref(k), None) == -2
+    k.S = 64
+    assert lib.gl_k16_fwd_tc_f32(ctypes.byref(k), None) == -1
+    k.act = _native.ACT_IDS["gelu"]
+    assert lib.gl_k16_bwd_tc_f32(ctypes.byref(k), None, None, None) == -4
+    k.act, k.B = _native.ACT_IDS["relu"], 0
+    assert lib.gl_k16_bwd_tc_f32(ctypes.byref(k), None, None, None) == 0
 
 
 def test_struct_layout_matches_header():
