@@ -20,9 +20,9 @@
 // into the fp32 gradients once per record and token tile.
 //
 // fp32 parameters (gl_k16_fwd_tc_f32 / gl_k16_bwd_tc_f32, NS = 3) run the same tiles on three-term
-// bf16 splits: v = v1 + v2 + v3 with v1 = bf16(v), v2 = bf16(v - v1), v3 = v - v1 - v2, exact for
-// every finite fp32 v below bf16's largest value (each step leaves at most 8 significant bits fewer;
-// bf16 has fp32's exponent range).  x is split while it is staged (three slab planes), w when its
+// bf16 splits: v = v1 + v2 + v3 with v1 = bf16(v), v2 = bf16(v - v1), v3 = bf16(v - v1 - v2), exact
+// for 2^-110 <= |v| below bf16's largest value (each step takes 8 more significant bits; bf16 has fp32's
+// exponent range, its smallest subnormal is 2^-133, and smaller v lose only what lies below that).  x is split while it is staged (three slab planes), w when its
 // record is used, dz when it is formed.  A product sum a.b is the six MMAs of the term pairs
 // i + j <= 2 (the smallest first); the three dropped pairs are below 2^-23 |a||b| together, the
 // rounding of an fp32 FMA chain, and every product of bf16 terms is exact in the fp32 accumulator.

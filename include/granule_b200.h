@@ -424,7 +424,7 @@ int gl_k16_fwd_tc(const GlK16Args* args, void* stream);
  * 2^30; a token whose bound is not finite gets NaN); with both NULL it is fp32. */
 int gl_k16_bwd_tc(const GlK16Args* args, const float* wabsmax, const int32_t* rowmax, void* stream);
 /* The layer with fp32 parameters (w, b fp32, as gl_k16_fwd_f32 / gl_k16_bwd_f32) on the tensor cores: x, w and
- * dz are each split into three bf16 terms (v = v1 + v2 + v3, exact for finite |v| below bf16's largest value)
+ * dz are each split into three bf16 terms (v = v1 + v2 + v3, exact for 2^-110 <= |v| below bf16's largest value)
  * and every product sum is the six MMAs of the term pairs i + j <= 2, so the results agree with the fp32 SIMT
  * kernels to fp32 rounding (the dropped pairs are below 2^-23 of each |a||b|).  Arguments, `tokens`, S and
  * the optional fixed-point dX bounds as gl_k16_fwd_tc / gl_k16_bwd_tc.  An infinite x, w or dz gives NaN (its
