@@ -552,7 +552,10 @@ def bench_cover16(args, world):
                 "unit": "TFLOP/s", "frac": mma_flop / (bwd_ms * 1e-3) / 1e12 / tc_peak,
                 "peak_source": f"{tc_kind} dense bf16 (cuBLAS, burst) -- these are mma.sync tiles",
                 "algorithmic_flop_per_launch": mma_flop, "flop_definition": "bf16 MMA flops of the term products",
-                "fp32_equivalent_tflops": achieved}
+                "fp32_equivalent_tflops": achieved,
+                # mma.sync bf16 -> fp32 peaks at 2048 flop / clk / SM (ncu peak_sustained), a quarter of tcgen05
+                "mma_sync_peak_tflops": sms * 2048 * mhz * 1e6 / 1e12,
+                "frac_of_mma_sync_peak": mma_flop / (bwd_ms * 1e-3) / (sms * 2048 * mhz * 1e6)}
     else:
         roof = {"bound": "fp32", "kernel": bkern, "achieved": achieved, "peak": peak_tflops, "unit": "TFLOP/s",
                 "frac": achieved / peak_tflops,
