@@ -557,12 +557,17 @@ static int k16tc_run(const GlK16Args* args, const float* wabsmax, const int32_t*
   K16TcParams p;
   int rc = k16tc_prepare(*args, BWD, p, wabsmax, brow);
   if (rc) return rc > 0 ? GL_OK : rc;
-  int BM = args->tokens;
-  if (BM == 0) BM = BWD ? 64 : 128;
-  if (BM != 32 && BM != 64 && BM != 128) return GL_ERR_UNSUPPORTED;
   int optin = 0;
   if ((rc = device_smem_optin(&optin))) return rc;
-  if ((int64_t)p.S * BM * (2 * NS + (BWD ? 4 : 0)) + 8192 > optin) return GL_ERR_SMEM;
+  const int64_t row_bytes = (int64_t)p.S * (2 * NS + (BWD ? 4 : 0));  // shared bytes per token of a tile
+  int BM = args->tokens;
+  if (BM == 0) {
+    // measured at config 4: forward 128; backward 64 for bf16, 128 for the split kernels (51.8 ms
+    // against 58.2 ms at 64) where its tile fits
+    BM = !BWD ? 128 : (NS > 1 && row_bytes * 128 + 8192 <= optin) ? 128 : 64;
+  }
+  if (BM != 32 && BM != 64 && BM != 128) return GL_ERR_UNSUPPORTED;
+  if (row_bytes * BM + 8192 > optin) return GL_ERR_SMEM;
   cudaStream_t st = (cudaStream_t)stream;
   const bool relu = args->act == GL_ACT_RELU, fixed = BWD && wabsmax != nullptr;
   switch (BM) {

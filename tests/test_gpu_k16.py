@@ -131,7 +131,8 @@ def test_token_chunks_and_identity(tokens):
         assert_close(db, rdb, what=f"db {act_name}", slack=sdb, **GRAD_TOL)
 
 
-@pytest.mark.parametrize("tiles", [(32, 32, False), (64, 64, True), (128, 32, True), (128, 64, False)])
+@pytest.mark.parametrize("tiles", [(32, 32, False), (64, 64, True), (128, 32, True), (128, 64, False),
+                                   (128, 128, True), (64, 128, False)])
 def test_split_token_tiles_and_identity(tiles):
     """The split tensor-core entries at explicit token tiles (32, 64, 128) with the int32 fixed-point or the
     fp32 dX tile, ReLU and identity, over a ragged batch of 200, against the oracle."""
