@@ -562,9 +562,9 @@ static int k16tc_run(const GlK16Args* args, const float* wabsmax, const int32_t*
   const int64_t row_bytes = (int64_t)p.S * (2 * NS + (BWD ? 4 : 0));  // shared bytes per token of a tile
   int BM = args->tokens;
   if (BM == 0) {
-    // measured at config 4: forward 128; backward 64 for bf16, 128 for the split kernels (51.8 ms
-    // against 58.2 ms at 64) where its tile fits
-    BM = !BWD ? 128 : (NS > 1 && row_bytes * 128 + 8192 <= optin) ? 128 : 64;
+    // measured at config 4: 128 tokens, the backward's where its tile fits (split kernels 51.8 ms against
+    // 58.2 ms at 64; bf16 25.9 against 30.8 ms), else 64
+    BM = (!BWD || row_bytes * 128 + 8192 <= optin) ? 128 : 64;
   }
   if (BM != 32 && BM != 64 && BM != 128) return GL_ERR_UNSUPPORTED;
   if (row_bytes * BM + 8192 > optin) return GL_ERR_SMEM;

@@ -107,7 +107,7 @@ def test_token_tiles_agree():
     wabsmax = lay.weight.detach().reshape(16, -1).abs().amax(1).float().contiguous()
     rowmax = lay._bucket_rowmax()
     outs = []
-    for tok, fixed in ((32, False), (64, False), (128, False), (64, True), (32, True)):
+    for tok, fixed in ((32, False), (64, False), (128, False), (64, True), (32, True), (128, True)):
         pre = torch.zeros(200, 16, device="cuda")
         _native.k16_fwd(x, sched, lay.weight.detach(), lay.bias.detach(), lay.counts, pre, L.blocks_per_group,
                         tokens=tok)
