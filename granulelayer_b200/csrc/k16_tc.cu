@@ -1,4 +1,5 @@
-// Compact K16/C16 execution of the Cover-TopK/16 layer with bf16 parameters, on the tensor cores.
+// Compact K16/C16 execution of the Cover-TopK/16 layer on the tensor cores: bf16 parameters, and fp32
+// ones through three-term bf16 splits (below).
 //
 // Replaces the reference's kgen K = 16 kernels (sparse_pooling/experimental/kgen/kgen.cuh:142-536,
 // launched by experimental/kgen_layer.py:61-143) with their arithmetic: bf16 parameters, x rounded to
