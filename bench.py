@@ -25,7 +25,9 @@ a bounded slice of the same workload on the host cores (rank 0, N = 1).
 ``--workload cover16`` times instead BASELINE config 4, the Cover-TopK/16 opt-in layer
 (N = 50,331,648 neurons selected from a K64 envelope with w64 ~ N(0, 1/64) in BF16, D = 4096,
 G = 2048 outputs, S = 64, R = 64, batch 512, seed 3): forward + backward through the layer on
-1 GPU, with the forward and backward (dX-carrying) kernels timed separately.
+1 GPU, with the forward and backward (dX-carrying) kernels timed separately.  fp32 parameters run
+the tensor-core kernels on three-term bf16 splits by default (``--cover-kernels simt``: the fp32
+SIMT kernels); ``--cover-dtype bf16`` stores bf16 parameters (the reference's arithmetic).
 
 ``--workload fwdbwd256`` times BASELINE config 2: the same 100M-neuron layer (seed 1, bias_std 0.1)
 forward + backward at batch 256 through the layer API (no optimizer), forward and backward
