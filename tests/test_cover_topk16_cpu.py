@@ -95,3 +95,28 @@ def test_rejects_bad_inputs():
     with pytest.raises(ValueError):
         CoverTopK16Layer.from_envelope(w, b, connectivity=ConnectivityPlan(64, 16), normalization="fanin",
                                        device="cpu", **SMALL)
+
+
+def test_kernel_family_follows_dtype_and_plan():
+    """fp32 layers run the split tensor-core entries unless the plan turns them off; bf16 layers always run
+    the bf16 tensor-core entries (the routing itself; the kernels are covered by the GPU tests)."""
+    from granulelayer_b200 import _native
+    from granulelayer_b200.config import PhysicalPlan
+
+    w, b = _envelope()
+    kw = dict(connectivity=ConnectivityPlan(64, 16, seed=0), device="cpu", **SMALL)
+    f32 = CoverTopK16Layer.from_envelope(w, b, **kw)
+    off = CoverTopK16Layer.from_envelope(w, b, plan=PhysicalPlan(b200_f32_tensor_cores="off"), **kw)
+    b16 = CoverTopK16Layer.from_envelope(w, b, plan=PhysicalPlan(b200_f32_tensor_cores="off"),
+                                         dtype=torch.bfloat16, **kw)
+    assert f32.tensor_cores and not off.tensor_cores and b16.tensor_cores
+    assert [_native._k16_entry(f32.weight, f32.tensor_cores, bwd) for bwd in (False, True)] == \
+        ["gl_k16_fwd_tc_f32", "gl_k16_bwd_tc_f32"]
+    assert [_native._k16_entry(off.weight, off.tensor_cores, bwd) for bwd in (False, True)] == \
+        ["gl_k16_fwd_f32", "gl_k16_bwd_f32"]
+    assert [_native._k16_entry(b16.weight, b16.tensor_cores, bwd) for bwd in (False, True)] == \
+        ["gl_k16_fwd_tc", "gl_k16_bwd_tc"]
+    with pytest.raises(ValueError):
+        PhysicalPlan(b200_f32_tensor_cores="split")
+    with pytest.raises(_native.NativeLibraryError):      # no CPU fallback on this path
+        f32(torch.randn(2, SMALL["input_dim"]))
