@@ -16,7 +16,7 @@ from pathlib import Path
 
 import torch
 
-ABI_VERSION = 14
+ABI_VERSION = 15
 LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libgranule_b200.so"
 
 POOL_MEAN, POOL_SUM, POOL_MAX, POOL_LME, POOL_POWER, POOL_SOFTMAX, POOL_TOPK = 0, 1, 2, 3, 4, 5, 6
@@ -42,7 +42,7 @@ EXPORTS = ("gl_abi_version", "gl_status_string", "gl_last_cuda_error", "gl_fwd_f
            "gl_bwd_events_f32",
            "gl_shared_auto_tokens", "gl_bwd_shared_det_f32", "gl_bwd_shared_det_static_f32", "gl_k16_fwd_f32",
            "gl_k16_bwd_f32", "gl_k16_auto_tokens", "gl_k16_fwd_tc", "gl_k16_bwd_tc", "gl_k16_fwd_tc_f32",
-           "gl_k16_bwd_tc_f32")
+           "gl_k16_bwd_tc_f32", "gl_struct_layout", "gl_struct_fields")
 
 
 class GlSetArgs(ctypes.Structure):
@@ -115,6 +115,28 @@ class GlK16Args(ctypes.Structure):
                [("act", ctypes.c_int32), ("tokens", ctypes.c_int32)]
 
 
+# gl_struct_layout ids 0 .. GL_STRUCT_COUNT-1, in header order.
+STRUCTS = (GlFwdArgs, GlBwdArgs, GlAdamArgs, GlSharedArgs, GlSetArgs, GlEventArgs, GlK16Args)
+
+
+def check_struct_layouts(lib, path="library"):
+    """Refuse a library whose argument structs differ from these ctypes declarations: sizeof, every
+    field's offset (gl_struct_layout) and every field's name (gl_struct_fields), in declaration order.
+    The reference's bridge makes the same check with sp_struct_layout (backends/cuda/runtime.py:103-121)."""
+    lib.gl_struct_layout.restype = ctypes.c_int
+    lib.gl_struct_layout.argtypes = [ctypes.c_int, ctypes.POINTER(ctypes.c_int64), ctypes.c_int]
+    lib.gl_struct_fields.restype = ctypes.c_char_p
+    lib.gl_struct_fields.argtypes = [ctypes.c_int]
+    for which, st in enumerate(STRUCTS):
+        buf = (ctypes.c_int64 * 64)()
+        n = lib.gl_struct_layout(which, buf, 64)
+        want = [ctypes.sizeof(st)] + [getattr(st, name).offset for name, _ in st._fields_]
+        names = (lib.gl_struct_fields(which) or b"").decode().rstrip(",").split(",")
+        if n != len(want) or list(buf[:n]) != want or names != [name for name, _ in st._fields_]:
+            raise NativeLibraryError(f"{path}: {st.__name__} layout mismatch (native sizeof/offsets "
+                                     f"{list(buf[:max(n, 0)])}, fields {names}; ctypes {want})")
+
+
 _lock = threading.Lock()
 _lib = None
 
@@ -136,6 +158,7 @@ def load(path=None) -> ctypes.CDLL:
         lib.gl_abi_version.restype = ctypes.c_int
         if lib.gl_abi_version() != ABI_VERSION:
             raise NativeLibraryError(f"{p}: ABI version {lib.gl_abi_version()} != {ABI_VERSION}; rebuild it")
+        check_struct_layouts(lib, p)
         lib.gl_status_string.restype = ctypes.c_char_p
         lib.gl_status_string.argtypes = [ctypes.c_int]
         lib.gl_last_cuda_error.restype = ctypes.c_int

@@ -3,6 +3,7 @@
 // query, negative status codes, a per-device cache of kernel attributes
 // guarded by a mutex).
 #include <atomic>
+#include <cstddef>
 #include <mutex>
 #include <unordered_map>
 #include <utility>
@@ -117,5 +118,85 @@ extern "C" const char* gl_status_string(int status) {
     case GL_ERR_DEVICE: return "no usable CUDA device";
     case GL_ERR_CAPACITY: return "the problem exceeds the fixed scratch of the allocation-free entry point";
     default: return "unknown status";
+  }
+}
+
+// ---- argument-struct layouts (gl_struct_layout / gl_struct_fields) ----
+// One list of fields per struct, in declaration order; the offsets and the names are both generated
+// from it, so a binding that compares both against its own declarations catches a missing, added,
+// reordered or resized field.
+#define GL_FWD_FIELDS(F)                                                                                         \
+  F(x) F(idx) F(w) F(b) F(counts) F(pre) F(B) F(D) F(NB) F(g0) F(g1) F(ldx) F(ldp) F(pool) F(act) F(tokens)       \
+  F(groups_per_cta) F(wabsmax) F(order) F(lidx) F(fmap) F(nfeat) F(fcap) F(winners) F(ldwin) F(stat) F(ldstat)   \
+  F(param) F(k) F(wdtype) F(reserved3)
+#define GL_BWD_FIELDS(F)                                                                                         \
+  F(x) F(idx) F(w) F(b) F(counts) F(gpre) F(dx) F(dw) F(db) F(B) F(D) F(NB) F(g0) F(g1) F(ldx) F(ldg) F(lddx)     \
+  F(pool) F(act) F(tokens) F(groups_per_cta) F(wabsmax) F(rowmax) F(order) F(lidx) F(fmap) F(nfeat) F(fcap)      \
+  F(c2) F(c3) F(param) F(wdtype)
+#define GL_ADAM_FIELDS(F)                                                                                        \
+  F(p) F(g) F(m) F(v) F(n) F(lr) F(beta1) F(beta2) F(eps) F(weight_decay) F(bc1) F(bc2) F(zero_grad) F(master)   \
+  F(pdtype) F(mdtype) F(stochastic) F(seed)
+#define GL_SHARED_FIELDS(F)                                                                                      \
+  F(x) F(idx) F(w) F(b) F(counts) F(pre) F(gpre) F(dx) F(dw) F(db) F(B) F(D) F(NB) F(C) F(g0) F(g1) F(ldx) F(ldp) \
+  F(ldg) F(lddx) F(pool) F(act) F(packed) F(tokens) F(groups_per_cta) F(wdtype) F(winners) F(ldwin) F(stat)      \
+  F(ldstat) F(c2) F(c3) F(param) F(k)
+#define GL_SET_FIELDS(F) F(feat) F(buckets) F(chunks) F(rowmax) F(wabsmax) F(S) F(nchunks) F(max_chunk)
+#define GL_EVENT_FIELDS(F)                                                                                       \
+  F(x) F(idx) F(w) F(b) F(winners) F(coef) F(dx) F(dw) F(db) F(B) F(D) F(NB) F(C) F(g0) F(g1) F(ldx) F(ldwin)    \
+  F(ldc) F(lddx) F(shared) F(packed) F(act) F(kev) F(wdtype) F(reserved)
+#define GL_K16_FIELDS(F)                                                                                         \
+  F(x) F(env) F(feat) F(buckets) F(q_off) F(rec_off) F(w) F(b) F(counts) F(pre) F(c1t) F(dx) F(dw) F(db) F(B)    \
+  F(D) F(G) F(NB16) F(Q) F(S) F(nbuckets) F(ldx) F(ldp) F(ldc) F(lddx) F(act) F(tokens)
+
+#define GL_NAME(f) #f ","
+
+namespace {
+
+template <typename S>
+int write_layout(const int64_t* off, int nf, int64_t* out, int n) {
+  if (!out || n < nf + 1) return GL_ERR_SHAPE;
+  out[0] = (int64_t)sizeof(S);
+  for (int i = 0; i < nf; ++i) out[i + 1] = off[i];
+  return nf + 1;
+}
+
+#define GL_LAYOUT_CASE(ID, S, LIST)                                                  \
+  case ID: {                                                                         \
+    const int64_t off[] = {LIST(GL_OFF_##S)};                                        \
+    return write_layout<S>(off, (int)(sizeof(off) / sizeof(off[0])), out, n);        \
+  }
+#define GL_OFF_GlFwdArgs(f) (int64_t) offsetof(GlFwdArgs, f),
+#define GL_OFF_GlBwdArgs(f) (int64_t) offsetof(GlBwdArgs, f),
+#define GL_OFF_GlAdamArgs(f) (int64_t) offsetof(GlAdamArgs, f),
+#define GL_OFF_GlSharedArgs(f) (int64_t) offsetof(GlSharedArgs, f),
+#define GL_OFF_GlSetArgs(f) (int64_t) offsetof(GlSetArgs, f),
+#define GL_OFF_GlEventArgs(f) (int64_t) offsetof(GlEventArgs, f),
+#define GL_OFF_GlK16Args(f) (int64_t) offsetof(GlK16Args, f),
+
+}  // namespace
+
+extern "C" int gl_struct_layout(int which, int64_t* out, int n) {
+  switch (which) {
+    GL_LAYOUT_CASE(0, GlFwdArgs, GL_FWD_FIELDS)
+    GL_LAYOUT_CASE(1, GlBwdArgs, GL_BWD_FIELDS)
+    GL_LAYOUT_CASE(2, GlAdamArgs, GL_ADAM_FIELDS)
+    GL_LAYOUT_CASE(3, GlSharedArgs, GL_SHARED_FIELDS)
+    GL_LAYOUT_CASE(4, GlSetArgs, GL_SET_FIELDS)
+    GL_LAYOUT_CASE(5, GlEventArgs, GL_EVENT_FIELDS)
+    GL_LAYOUT_CASE(6, GlK16Args, GL_K16_FIELDS)
+    default: return GL_ERR_UNSUPPORTED;
+  }
+}
+
+extern "C" const char* gl_struct_fields(int which) {
+  switch (which) {
+    case 0: return GL_FWD_FIELDS(GL_NAME);
+    case 1: return GL_BWD_FIELDS(GL_NAME);
+    case 2: return GL_ADAM_FIELDS(GL_NAME);
+    case 3: return GL_SHARED_FIELDS(GL_NAME);
+    case 4: return GL_SET_FIELDS(GL_NAME);
+    case 5: return GL_EVENT_FIELDS(GL_NAME);
+    case 6: return GL_K16_FIELDS(GL_NAME);
+    default: return nullptr;
   }
 }

@@ -390,4 +390,6 @@ void count_launches(int n);                             // adds n to gl_launch_c
 int device_smem_optin(int* bytes);                      // max dynamic smem per block, current device
 int device_sm_count(int* sms);
 int ensure_dynamic_smem(const void* func, size_t bytes);  // raises the kernel's opt-in once per device
+// argument checks of gl_bwd_shared_det_f32 (defined in modeb_det.cu)
+int det_check_args(const GlSharedArgs& a, const float* qscale, const float* qinv, int* T);
 }  // namespace gl

@@ -10,14 +10,16 @@
 //
 // The array (GL_DET_STATIC_MAX_ELEMS int64 entries, 8 MiB) is part of the library's device image:
 // every GPU that loads the library holds it until the process exits.  Host code may not pass the
-// array's name to a kernel (on the host it names a stand-in, not device memory), so the first call
-// on each device looks up its device address with cudaGetSymbolAddress while that device is current
-// and caches it; that first call should come before any stream capture.  Every call clears the
-// B * D entries it uses on the caller's stream before the backward runs, because the array keeps the
-// previous call's sums.  All calls on a device share the one array: calls whose GPU work overlaps
-// (different streams without ordering between them) race on it and give wrong results.
-#include <mutex>
-
+// array's name to a kernel (on the host it names a stand-in, not device memory), so every call looks
+// up the array's device address with cudaGetSymbolAddress in the CUDA context current on the calling
+// thread.  The lookup allocates nothing; it is made on every call rather than cached because the
+// address belongs to a context, and a caller may run in a context of its own (a framework that
+// creates contexts with the driver API) or after cudaDeviceReset.  The first call in a context can
+// load the library's device code into that context, so make it before any stream capture.  Every
+// call validates all its arguments first and then clears the B * D entries it uses on the caller's
+// stream before the backward runs, because the array keeps the previous call's sums.  All calls on a
+// device share the one array: calls whose GPU work overlaps (different streams without ordering
+// between them) race on it and give wrong results.
 #include "common.cuh"
 
 namespace gl {
@@ -25,30 +27,15 @@ namespace {
 
 __device__ __align__(256) static int64_t g_det_dxq_scratch[GL_DET_STATIC_MAX_ELEMS];
 
-constexpr int kMaxDevices = 64;
-std::mutex g_scratch_mu;
-int64_t* g_scratch_ptr[kMaxDevices] = {};
-
-// Device address of the scratch array on the current device, looked up once per device.
+// Device address of the scratch array in the current context.
 int scratch_address(int64_t** out) {
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) {
-    set_cuda_error(e);
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_det_dxq_scratch);
+  if (e != cudaSuccess || p == nullptr) {
+    set_cuda_error(e != cudaSuccess ? e : cudaErrorInvalidSymbol);
     return GL_ERR_DEVICE;
   }
-  if (dev < 0 || dev >= kMaxDevices) return GL_ERR_DEVICE;
-  std::lock_guard<std::mutex> lk(g_scratch_mu);
-  if (!g_scratch_ptr[dev]) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_det_dxq_scratch);
-    if (e != cudaSuccess || p == nullptr) {
-      set_cuda_error(e != cudaSuccess ? e : cudaErrorInvalidSymbol);
-      return GL_ERR_DEVICE;
-    }
-    g_scratch_ptr[dev] = static_cast<int64_t*>(p);
-  }
-  *out = g_scratch_ptr[dev];
+  *out = static_cast<int64_t*>(p);
   return GL_OK;
 }
 
@@ -59,14 +46,14 @@ extern "C" int gl_bwd_shared_det_static_f32(const GlSharedArgs* args, const floa
                                             void* stream) {
   if (!args) return GL_ERR_NULL;
   const GlSharedArgs& a = *args;
-  if (a.B < 0 || a.D < 1) return GL_ERR_SHAPE;
-  if (a.B > 0 && a.D > GL_DET_STATIC_MAX_ELEMS / a.B) return GL_ERR_CAPACITY;
-  if (a.B == 0 || a.g1 <= a.g0) return gl_bwd_shared_det_f32(args, nullptr, qscale, qinv, stream);
+  int T = 0;
+  int rc = gl::det_check_args(a, qscale, qinv, &T);  // nothing touches the shared scratch before this passes
+  if (rc || !T) return rc;
+  if (a.D > GL_DET_STATIC_MAX_ELEMS / a.B) return GL_ERR_CAPACITY;
   int64_t* dxq = nullptr;
-  int rc = gl::scratch_address(&dxq);
-  if (rc) return rc;
+  if ((rc = gl::scratch_address(&dxq))) return rc;
   cudaStream_t st = (cudaStream_t)stream;
-  cudaError_t e = cudaMemsetAsync(dxq, 0, (size_t)(a.B * a.D) * sizeof(int64_t), st);
+  const cudaError_t e = cudaMemsetAsync(dxq, 0, (size_t)(a.B * a.D) * sizeof(int64_t), st);
   if (e != cudaSuccess) return gl::set_cuda_error(e);
   return gl_bwd_shared_det_f32(args, dxq, qscale, qinv, stream);
 }

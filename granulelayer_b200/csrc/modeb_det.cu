@@ -286,10 +286,13 @@ static int det_t(const MbParams& p, int act, bool packed, unsigned long long* dx
 
 using namespace gl;
 
-extern "C" int gl_bwd_shared_det_f32(const GlSharedArgs* args, int64_t* dxq, const float* qscale, const float* qinv,
-                                     void* stream) {
-  if (!args) return GL_ERR_NULL;
-  const GlSharedArgs& a = *args;
+namespace gl {
+
+// Every argument check of gl_bwd_shared_det_f32 except its scratch pointer, and the token tile the
+// shared memory allows (*T).  GL_OK with *T = 0 means there is nothing to do (B = 0 or an empty
+// group range).  The allocation-free variant runs it before it touches its shared scratch.
+int det_check_args(const GlSharedArgs& a, const float* qscale, const float* qinv, int* T) {
+  *T = 0;
   if (a.B < 0 || a.D < 1 || a.D > 32767 || a.NB < 1 || a.g0 < 0 || a.g1 < a.g0) return GL_ERR_SHAPE;
   if (a.C != 8 && a.C != 16 && a.C != 32 && a.C != 64) return GL_ERR_SHAPE;
   if (a.packed && (a.NB * (a.C / 8)) % 4) return GL_ERR_SHAPE;
@@ -298,20 +301,32 @@ extern "C" int gl_bwd_shared_det_f32(const GlSharedArgs* args, int64_t* dxq, con
   if (a.wdtype != GL_DTYPE_F32 && a.wdtype != GL_DTYPE_BF16) return GL_ERR_UNSUPPORTED;
   if (a.B == 0 || a.g1 == a.g0) return GL_OK;
   if (!a.x || !a.idx || !a.w || !a.b || !a.counts || !a.gpre || !a.dx || !a.dw || !a.db) return GL_ERR_NULL;
-  if (!dxq || !qscale || !qinv) return GL_ERR_NULL;
+  if (!qscale || !qinv) return GL_ERR_NULL;
   if (a.B > 2147483647LL || a.ldx < a.D || a.ldg < a.g1 - a.g0 || a.lddx < a.D) return GL_ERR_SHAPE;
   if (((uintptr_t)a.idx & 15) || ((uintptr_t)a.w & 15) || ((uintptr_t)a.b & 15) || ((uintptr_t)a.dw & 15) ||
-      ((uintptr_t)a.db & 15) || ((uintptr_t)dxq & 7))
+      ((uintptr_t)a.db & 15))
     return GL_ERR_ALIGN;
-  int optin = 0, sms = 0;
+  int optin = 0;
   int rc = device_smem_optin(&optin);
   if (rc) return rc;
-  if ((rc = device_sm_count(&sms))) return rc;
+  for (int c = 16; c >= 1 && !*T; c >>= 1)
+    if (det_smem_bytes(a.D, c) + 2048 <= optin) *T = c;
+  return *T ? GL_OK : GL_ERR_SMEM;
+}
+
+}  // namespace gl
+
+extern "C" int gl_bwd_shared_det_f32(const GlSharedArgs* args, int64_t* dxq, const float* qscale, const float* qinv,
+                                     void* stream) {
+  if (!args) return GL_ERR_NULL;
+  const GlSharedArgs& a = *args;
   int T = 0;
-  for (int c = 16; c >= 1 && !T; c >>= 1)
-    if (det_smem_bytes(a.D, c) + 2048 <= optin) T = c;
-  if (!T) return GL_ERR_SMEM;
-  // records per block: whole groups when there are enough of them, else enough blocks for the SMs
+  int rc = det_check_args(a, qscale, qinv, &T);
+  if (rc || !T) return rc;
+  if (!dxq) return GL_ERR_NULL;
+  if ((uintptr_t)dxq & 7) return GL_ERR_ALIGN;
+  int sms = 0;
+  if ((rc = device_sm_count(&sms))) return rc;
   const int64_t G = a.g1 - a.g0;
   const int64_t total = G * a.NB;
   int64_t rpb = (total + (int64_t)sms * 2 - 1) / ((int64_t)sms * 2);

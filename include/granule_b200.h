@@ -44,7 +44,7 @@
 extern "C" {
 #endif
 
-#define GL_ABI_VERSION 14
+#define GL_ABI_VERSION 15
 
 typedef enum GlStatus {
   GL_OK = 0,
@@ -332,10 +332,12 @@ int gl_bwd_shared_det_f32(const GlSharedArgs* args, int64_t* dxq, const float* q
  * pool, or a loop that cannot afford cudaMalloc's possible device synchronisation).  The int64 dX
  * scratch lives in a fixed array inside the library instead of a caller buffer, so B * D must be at
  * most GL_DET_STATIC_MAX_ELEMS (8 MiB of int64; larger problems return GL_ERR_CAPACITY); every
- * device that loads the library holds that array until exit.  The first call on a device looks up
- * the array's device address (make it before any stream capture); each call clears the entries it
- * uses on `stream` first.  All calls on one device share the array: calls whose GPU work can overlap
- * race on it.  Calls no cudaMalloc, cudaFree or allocating library routine. */
+ * device that loads the library holds that array until exit.  Each call checks all its arguments
+ * before it touches the array, looks up the array's device address in the calling thread's current
+ * context (the first call in a context may load the library's device code: make it before any stream
+ * capture), and clears the entries it uses on `stream`.  All calls on one device share the array:
+ * calls whose GPU work can overlap race on it.  Calls no cudaMalloc, cudaFree or allocating library
+ * routine. */
 #define GL_DET_STATIC_MAX_ELEMS (1 << 20)
 int gl_bwd_shared_det_static_f32(const GlSharedArgs* args, const float* qscale, const float* qinv, void* stream);
 
@@ -431,6 +433,17 @@ int gl_k16_bwd_tc(const GlK16Args* args, const float* wabsmax, const int32_t* ro
  * second term is inf - inf), where the SIMT kernels may give an infinity. */
 int gl_k16_fwd_tc_f32(const GlK16Args* args, void* stream);
 int gl_k16_bwd_tc_f32(const GlK16Args* args, const float* wabsmax, const int32_t* rowmax, void* stream);
+
+/* Layout of the argument structs, for bindings that declare them field by field (replaces the
+ * reference's sp_struct_layout, sparse_pooling/kernels/cuda/abi.cu:25, which its ctypes bridge checks
+ * at load, backends/cuda/runtime.py:103-121).  which: 0 GlFwdArgs, 1 GlBwdArgs, 2 GlAdamArgs,
+ * 3 GlSharedArgs, 4 GlSetArgs, 5 GlEventArgs, 6 GlK16Args.  gl_struct_layout writes sizeof(struct)
+ * and then every field's offset, in declaration order, into out[0 .. n) and returns the number of
+ * values (GL_ERR_SHAPE when n is too small, GL_ERR_UNSUPPORTED for an unknown id); gl_struct_fields
+ * returns the field names in declaration order, each followed by a comma (NULL for an unknown id). */
+#define GL_STRUCT_COUNT 7
+int gl_struct_layout(int which, int64_t* out, int n);
+const char* gl_struct_fields(int which);
 
 /* Number of kernels this library has launched successfully in this process
    (all devices).  Benchmarks difference it around a timed region. */

@@ -139,6 +139,51 @@ def test_struct_layout_matches_header():
     assert ctypes.sizeof(_native.GlSetArgs) == 5 * 8 + 3 * 8
 
 
+def test_library_struct_layouts_match_ctypes_declarations():
+    """gl_struct_layout / gl_struct_fields agree with every ctypes mirror: sizeof, offsets and names
+    (the load-time check of the reference's bridge, backends/cuda/runtime.py:103-121)."""
+    lib = _native.load()
+    _native.check_struct_layouts(lib)          # raises on any difference
+    buf = (ctypes.c_int64 * 64)()
+    assert lib.gl_struct_layout(len(_native.STRUCTS), buf, 64) == -4      # unknown id
+    assert lib.gl_struct_fields(len(_native.STRUCTS)) is None
+    assert lib.gl_struct_layout(0, buf, 3) == -2                          # buffer too small
+    header = (ROOT / "include" / "granule_b200.h").read_text()
+    assert f"#define GL_STRUCT_COUNT {len(_native.STRUCTS)}" in header
+
+
+def test_struct_layout_check_catches_a_drifted_binding():
+    """A binding that dropped the trailing wdtype / reserved3 fields of GlFwdArgs (the drift the check
+    exists for) is refused."""
+    lib = _native.load()
+
+    class Short(ctypes.Structure):
+        _fields_ = [f for f in _native.GlFwdArgs._fields_ if f[0] not in ("wdtype", "reserved3")]
+
+    saved = _native.STRUCTS
+    try:
+        _native.STRUCTS = (Short,) + saved[1:]
+        with pytest.raises(_native.NativeLibraryError, match="layout mismatch"):
+            _native.check_struct_layouts(lib)
+    finally:
+        _native.STRUCTS = saved
+
+
 def test_missing_library_fails_loudly(tmp_path):
     with pytest.raises(_native.NativeLibraryError):
         _native.load(tmp_path / "nope.so")
+
+
+def test_reference_backend_module_is_the_integration_stub_and_loads():
+    """INTEGRATION.md section 2 reproduces granulelayer_b200/reference_backend.py verbatim, and the module's
+    own loader accepts this library (ABI version and struct layouts; no device needed)."""
+    from granulelayer_b200 import reference_backend
+
+    src = (ROOT / "granulelayer_b200" / "reference_backend.py").read_text()
+    doc = (ROOT / "INTEGRATION.md").read_text()
+    assert "```python\n" + src + "```" in doc
+    assert "granulelayer_b200" not in src.split('"""', 2)[2]       # no imports from this package
+    lib = reference_backend.load_library(_native.library_path())
+    assert lib.gl_abi_version() == reference_backend.ABI_VERSION == _native.ABI_VERSION
+    for st, which in reference_backend.STRUCT_IDS.items():
+        assert [f for f, _ in st._fields_] == [f for f, _ in _native.STRUCTS[which]._fields_]

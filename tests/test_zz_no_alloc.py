@@ -1,7 +1,9 @@
 """The allocation-free deterministic Mode-B backward (gl_bwd_shared_det_static_f32), called through
-the C ABI, gives the results of gl_bwd_shared_det_f32 (which takes a caller-allocated int64 dX
-buffer) within the backward tolerance (rtol 1e-4 / atol 1e-5), on two calls in a row with
-different batch sizes and gradients, so a second call cannot lean on zeros left by the first.
+the C ABI, gives bit for bit the results of gl_bwd_shared_det_f32 (which takes a caller-allocated
+int64 dX buffer): both run the same deterministic kernels on the same inputs, so any difference
+means the fixed scratch was not fully cleared or was addressed wrongly.  Two calls in a row use
+different batch sizes and gradients, so a second call cannot lean on zeros left by the first; fp32
+and bf16 parameters are both covered.
 
 It serves callers that cannot allocate device memory where the backward runs (a plugin whose host
 framework owns all device memory, a loop that cannot afford cudaMalloc's synchronisation); its
@@ -12,17 +14,14 @@ across calls, and the test must pass both alone in a fresh process and after eve
 import pytest
 import torch
 
-from conftest import assert_close
 from granulelayer_b200 import PhysicalPlan, SparsePoolingLayer, _native
 
 pytestmark = pytest.mark.gpu
 
-BWD = dict(rtol=1e-4, atol=1e-5)
 
-
-def _layer(C=16, packed=True, D=512, H=30000, G=6):
+def _layer(C=16, packed=True, D=512, H=30000, G=6, dtype=torch.float32):
     return SparsePoolingLayer(D, H, G, shared_neurons=C, weight_layout="packed" if packed else "canonical",
-                              pooling={"type": "mean", "activation": "relu"}, dtype=torch.float32, seed=5,
+                              pooling={"type": "mean", "activation": "relu"}, dtype=dtype, seed=5,
                               bias_std=0.2, plan=PhysicalPlan(reduction="deterministic")).cuda()
 
 
@@ -39,7 +38,8 @@ def _run(lay, x, gpre, static):
     w, b = lay.weight.detach(), lay.bias.detach()
     qscale, qinv = rt.det_scales(w, gpre)
     dx = torch.zeros_like(x)
-    dw, db = torch.zeros_like(w), torch.zeros_like(b)
+    dw = torch.zeros(w.shape, device=w.device, dtype=torch.float32)
+    db = torch.zeros(b.shape, device=b.device, dtype=torch.float32)
     args = (x, lay.indices, w, b, rt.counts_i32, gpre, dx, dw, db, L.blocks_per_group, L.block, 0, L.groups,
             _native.POOL_MEAN, _native.ACT_IDS["relu"], L.packed)
     if static:
@@ -51,16 +51,17 @@ def _run(lay, x, gpre, static):
     return dx, dw, db
 
 
-@pytest.mark.parametrize("C,packed", [(16, True), (64, False)])
-def test_static_scratch_matches_caller_scratch_twice(C, packed):
-    lay = _layer(C, packed)
+@pytest.mark.parametrize("C,packed,dtype", [(16, True, torch.float32), (64, False, torch.float32),
+                                            (16, True, torch.bfloat16)])
+def test_static_scratch_matches_caller_scratch_twice(C, packed, dtype):
+    lay = _layer(C, packed, dtype=dtype)
     n0 = _native.launch_count()
     for B, seed in ((37, 1), (96, 2)):      # the second call uses more of the scratch than the first
         x, gpre = _inputs(lay, B, seed)
         want = _run(lay, x, gpre, static=False)
         got = _run(lay, x, gpre, static=True)
         for name, g, e in zip(("dx", "dw", "db"), got, want):
-            assert_close(g.cpu(), e.cpu(), what=f"B={B} {name}", **BWD)
+            assert torch.equal(g, e), f"B={B} {name}: max |diff| {float((g - e).abs().max())}"
         assert float(got[0].abs().sum()) > 0
     assert _native.launch_count() - n0 >= 8     # both entry points ran the library's kernels
 
