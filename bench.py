@@ -242,6 +242,7 @@ def run_reference(args, rank, world):
             times.append(time.perf_counter() - t0)
     dt = sum(times) / len(times)
     value = B * n_g * groups / dt
+    own = reference_own_cpu()
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
@@ -249,12 +250,66 @@ def run_reference(args, rank, world):
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
                              "sample": cb["sample"].split(";")[0]},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "reference_own_cpu": own,
             "note": "reference CPU path = float64 C oracle restating the reference's algorithm on a bounded "
-                    "slice of whole groups; the reference's own PyTorch path materialises [B, H]"}
+                    "slice of whole groups; the reference's own PyTorch path materialises [B, H] and is timed "
+                    "beside it on one whole group (reference_own_cpu)"}
     print(json.dumps(line), flush=True)
 
 
 REF_DIR = ROOT / "baseline" / "_ref"
+
+
+def reference_own_cpu(target_s=10.0):
+    """The reference's own CPU path on this host, timed beside the port: its materialising PyTorch model
+    (reference/pytorch_reference.py reference_forward, fp32) with torch.autograd for dX / dW / db and its
+    Adam update (optim.py:39-42, fp32 torch ops), on whole groups of this workload at the full batch, all
+    host threads; scaled to neuron-samples/s.  None when the reference is not placed in baseline/_ref."""
+    if not (REF_DIR / "sparse_pooling" / "__init__.py").exists():
+        return None
+    sys.path.insert(0, str(REF_DIR))
+    try:
+        from sparse_pooling.config import PoolingConfig as RefCfg
+        from sparse_pooling.layout import SparseLayout as RefLayout
+        from sparse_pooling.layout import init_parameters as ref_init
+        from sparse_pooling.reference.pytorch_reference import reference_forward
+    except Exception as e:  # noqa: BLE001
+        return {"unavailable": f"{type(e).__name__}: {e}"}
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    n_g = N // G
+    L = RefLayout(D, n_g, 1, 8, 8, False)
+    idx, w, b = ref_init(L, "cpu", dtype=torch.float32, seed=2, bias_std=0.1)
+    w, b = w.clone().requires_grad_(True), b.clone().requires_grad_(True)
+    cfg = RefCfg.parse("mean")
+    gen = torch.Generator().manual_seed(5)
+    x = torch.randn(B, D, generator=gen).requires_grad_(True)
+    dy = torch.randn(B, 1, generator=gen)
+    m = [torch.zeros_like(w), torch.zeros_like(b)]
+    v = [torch.zeros_like(w), torch.zeros_like(b)]
+    times = []
+    t_end = time.perf_counter() + target_s
+    step = 0
+    while step < 2 or (time.perf_counter() < t_end and step < 20):
+        t0 = time.perf_counter()
+        y = reference_forward(x, idx, w, b, L, cfg)
+        (y * dy).sum().backward()
+        step += 1
+        with torch.no_grad():
+            for i, p_ in enumerate((w, b)):
+                g_ = p_.grad
+                m[i].mul_(0.9).add_(g_, alpha=0.1)
+                v[i].mul_(0.999).addcmul_(g_, g_, value=0.001)
+                p_.sub_(1e-3 * (m[i] / (1 - 0.9 ** step)) / ((v[i] / (1 - 0.999 ** step)).sqrt() + 1e-8))
+                p_.grad = None
+        x.grad = None
+        if step > 1:
+            times.append(time.perf_counter() - t0)
+    dt = sum(times) / len(times)
+    return {"value": B * n_g / dt, "unit": UNIT, "cores": cores, "kind": "reference",
+            "sample": f"1 of {G} groups ({n_g} neurons) x {B} tokens: the reference's reference_forward + "
+                      f"torch.autograd + its Adam update in fp32 torch ops, {cores} threads; {dt:.2f} s per step, "
+                      f"{len(times)} timed steps"}
 
 
 def run_reference_gpu_cover16(args):

@@ -42,7 +42,8 @@ EXPORTS = ("gl_abi_version", "gl_status_string", "gl_last_cuda_error", "gl_fwd_f
            "gl_bwd_events_f32",
            "gl_shared_auto_tokens", "gl_bwd_shared_det_f32", "gl_bwd_shared_det_static_f32", "gl_k16_fwd_f32",
            "gl_k16_bwd_f32", "gl_k16_auto_tokens", "gl_k16_fwd_tc", "gl_k16_bwd_tc", "gl_k16_fwd_tc_f32",
-           "gl_k16_bwd_tc_f32", "gl_struct_layout", "gl_struct_fields")
+           "gl_k16_bwd_tc_f32", "gl_struct_layout", "gl_struct_fields", "gl_group_octets", "gl_fwd_octet_f32",
+           "gl_bwd_octet_f32")
 
 
 class GlSetArgs(ctypes.Structure):
@@ -164,6 +165,7 @@ def load(path=None) -> ctypes.CDLL:
         lib.gl_last_cuda_error.restype = ctypes.c_int
         lib.gl_launch_count.restype = ctypes.c_int64
         for name, st in (("gl_fwd_f32", GlFwdArgs), ("gl_bwd_f32", GlBwdArgs), ("gl_adam_f32", GlAdamArgs),
+                         ("gl_fwd_octet_f32", GlFwdArgs), ("gl_bwd_octet_f32", GlBwdArgs),
                          ("gl_k16_fwd_f32", GlK16Args), ("gl_k16_bwd_f32", GlK16Args),
                          ("gl_k16_fwd_tc", GlK16Args), ("gl_k16_fwd_tc_f32", GlK16Args),
                          ("gl_fwd_shared_f32", GlSharedArgs), ("gl_bwd_shared_f32", GlSharedArgs),
@@ -184,6 +186,10 @@ def load(path=None) -> ctypes.CDLL:
         lib.gl_group_feature_map.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
                                              ctypes.c_int64, ctypes.c_int64, ctypes.c_int32, ctypes.c_void_p,
                                              ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+        lib.gl_group_octets.restype = ctypes.c_int
+        lib.gl_group_octets.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
+                                        ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p,
+                                        ctypes.c_void_p]
         lib.gl_group_order.restype = ctypes.c_int
         lib.gl_group_order.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
                                        ctypes.c_int64, ctypes.c_int64, ctypes.c_int32, ctypes.c_void_p,
@@ -480,6 +486,45 @@ def group_feature_map(idx, counts, D: int, NB: int, g0: int, g1: int, nf, fmap=N
     with torch.cuda.device(idx.device):
         _check(lib, lib.gl_group_feature_map(_ptr(idx), _ptr(counts), D, NB, g0, g1, cap, _ptr(nf), _ptr(fmap),
                                              _ptr(lidx), _stream(idx.device)), "gl_group_feature_map")
+
+
+def fwd_octet(x, idx, w, b, counts, pre, NB: int, g0: int, g1: int, pool: int, act: int, groups_per_cta: int = 0,
+              wabsmax=None):
+    """Lane-per-neuron forward (gl_fwd_octet_f32): pre[:, :g1-g0] of the mean / sum pool; optionally
+    wabsmax[g-g0] = max |w|.  For octet-arranged storage (group_octets); correct on any order."""
+    _require_cuda(x, idx, w, b, counts, pre, wabsmax)
+    lib = load()
+    a = GlFwdArgs(_ptr(x), _ptr(idx), _ptr(w), _ptr(b), _ptr(counts), _ptr(pre), x.shape[0], x.shape[1], NB,
+                  g0, g1, x.stride(0), pre.stride(0), pool, act, 0, groups_per_cta, _ptr(wabsmax), None, None, None,
+                  None, 0, None, 0, None, 0, 0.0, 0, _wdtype(w), 0)
+    with torch.cuda.device(x.device):
+        _check(lib, lib.gl_fwd_octet_f32(ctypes.byref(a), _stream(x.device)), "gl_fwd_octet_f32")
+
+
+def bwd_octet(x, idx, w, b, counts, gpre, dx, dw, db, NB: int, g0: int, g1: int, pool: int, act: int, wabsmax,
+              rowmax, groups_per_cta: int = 0):
+    """Lane-per-neuron backward (gl_bwd_octet_f32): dx, dw, db += the mean / sum gradients, int32
+    fixed-point dX tile from the per-group bounds ``wabsmax`` / ``rowmax``."""
+    _require_cuda(x, idx, w, b, counts, gpre, dx, dw, db, wabsmax, rowmax)
+    lib = load()
+    a = GlBwdArgs(_ptr(x), _ptr(idx), _ptr(w), _ptr(b), _ptr(counts), _ptr(gpre), _ptr(dx), _ptr(dw), _ptr(db),
+                  x.shape[0], x.shape[1], NB, g0, g1, x.stride(0), gpre.stride(0), dx.stride(0), pool, act, 0,
+                  groups_per_cta, _ptr(wabsmax), _ptr(rowmax), None, None, None, None, 0, None, None, 0.0,
+                  _wdtype(w))
+    with torch.cuda.device(x.device):
+        _check(lib, lib.gl_bwd_octet_f32(ctypes.byref(a), _stream(x.device)), "gl_bwd_octet_f32")
+
+
+def group_octets(idx, counts, D: int, NB: int, g0: int, g1: int, order, kperm):
+    """order, kperm [g1-g0, NB*8] int32: the octet arrangement of each group (gl_group_octets)."""
+    _require_cuda(idx, counts, order, kperm)
+    for t in (order, kperm):
+        if t.dtype != torch.int32 or not t.is_contiguous() or tuple(t.shape) != (g1 - g0, NB * 8):
+            raise ValueError("order and kperm must be contiguous int32 [g1-g0, NB*8]")
+    lib = load()
+    with torch.cuda.device(idx.device):
+        _check(lib, lib.gl_group_octets(_ptr(idx), _ptr(counts), D, NB, g0, g1, _ptr(order), _ptr(kperm),
+                                        _stream(idx.device)), "gl_group_octets")
 
 
 def group_order(idx, counts, D: int, NB: int, g0: int, g1: int, unit: int, out):

@@ -124,6 +124,7 @@ class Level1Runtime:
         self._rowmax_key = None
         self._orders: Dict = {}
         self.sets = None   # (feat [Q, S], buckets [n, 4]) of a layer with input-supergroup connectivity
+        self.octets = False   # storage in octet order (gl_group_octets): the lane-per-neuron kernels
         self._local = None
 
     def set_plan(self):
@@ -274,6 +275,17 @@ class Level1Runtime:
             maps = (lidx, fmap, nf)
         self._local = (key, maps)
         return maps
+
+    def octet_kernels(self, B: int, D: int) -> bool:
+        """Whether this call runs the lane-per-neuron kernels (gl_fwd_octet_f32 / gl_bwd_octet_f32): storage
+        in octet order, Mode A, mean / sum, fp32 parameters, and two 16-byte-per-feature tiles in shared
+        memory."""
+        if not self.octets or B == 0 or self.layout.shared_indices or self.param_dtype != torch.float32:
+            return False
+        if self.pool not in (_native.POOL_MEAN, _native.POOL_SUM) or not self.idx.is_cuda:
+            return False
+        optin = torch.cuda.get_device_properties(self.idx.device).shared_memory_per_block_optin
+        return 32 * D + 1024 <= optin
 
     def tokens(self, backward: bool) -> int:
         lib = _native.load()
@@ -427,6 +439,12 @@ class Level1Runtime:
             return out
         wabsmax = (torch.empty(self.groups, device=x.device, dtype=torch.float32)
                    if B > 0 and not self.is_max and not self.smooth else None)
+        if self.octet_kernels(B, x.shape[1]):
+            _native.fwd_octet(x, self.idx, w, b, self.counts_i32, pre, self.layout.blocks_per_group, 0, self.groups,
+                              self.pool, self.act, wabsmax=wabsmax)
+            self.last_info.update(forward_backend="b200", forward_kernel="gl_fwd_octet_f32", workspace_bytes=0)
+            out["wabsmax"] = wabsmax
+            return out
         _native.fwd(x, self.idx, w, b, self.counts_i32, pre, self.layout.blocks_per_group, 0, self.groups,
                     self.pool, self.act, tokens=self.plan.b200_fwd_tokens, wabsmax=wabsmax,
                     order=self.order(self.tokens(False)) if B > 0 else None,
@@ -530,6 +548,13 @@ class Level1Runtime:
                 wabsmax = torch.empty(self.groups, device=x.device, dtype=torch.float32)
                 _native.group_absmax(w, self.counts_i32, self.layout.blocks_per_group, 0, self.groups, wabsmax)
             rowmax = self.rowmax()
+            if self.octet_kernels(B, D):
+                _native.bwd_octet(x, self.idx, w, b, self.counts_i32, c1, dx, dw_buf, db_buf,
+                                  self.layout.blocks_per_group, 0, self.groups, self.pool, self.act, wabsmax, rowmax)
+                self.last_info["backward_backend"] = "b200"
+                self.last_info["backward_kernel"] = "gl_bwd_octet_f32"
+                self.last_info["dx_accumulation"] = "int32 fixed point"
+                return dx
         _native.bwd(x, self.idx, w, b, self.counts_i32, c1, dx, dw_buf, db_buf, self.layout.blocks_per_group,
                     0, self.groups, self.pool, self.act, tokens=self.plan.b200_dx_tokens, wabsmax=wabsmax,
                     rowmax=rowmax, order=self.order(self.tokens(True)) if B > 0 else None,

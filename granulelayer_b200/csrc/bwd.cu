@@ -74,11 +74,6 @@ __device__ __forceinline__ void reduce_dw(float (&a)[8], float dz, int t, unsign
   if (t == 0) red_add(db + f, dbs);
 }
 
-template <int ACT>
-__host__ __device__ constexpr float dact_bound() {
-  return ACT == GL_ACT_GELU ? 1.13f : 1.f;  // max |gelu'(z)| = 1.1289 at z ~ 1.41
-}
-
 struct BwdParams {
   const float* x;
   const int16_t* idx;

@@ -37,6 +37,12 @@ __device__ __forceinline__ float dact_f(float z) {
   }
 }
 
+// Bound of |act'(z)| (the fixed-point dX scales divide by it).
+template <int ACT>
+__host__ __device__ constexpr float dact_bound() {
+  return ACT == GL_ACT_GELU ? 1.13f : 1.f;  // max |gelu'(z)| = 1.1289 at z ~ 1.41
+}
+
 // ---------------------------------------------------------------------------
 // Pooling states (the reference's per-(token, group) states, kernels/triton_fused.py:121-225, and
 // their merge / finalisation, kernels/ops.py:182-239).  Forward kinds:

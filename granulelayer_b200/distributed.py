@@ -17,13 +17,17 @@ dX all-reduce before the optimizer kernels so that they overlap it.
 Nothing here touches another GPU's memory directly: remote data arrives only
 through the collectives into local buffers.
 
-Storage order.  A shard on a GPU stores its neurons, by default, in the bank-aware
-processing order of ``gl_group_order`` (unit 48): within each group the records are
-permuted so that the neurons one shared-memory wavefront serves read rows in distinct
-bank groups, which cuts the kernels' bank conflicts while keeping their record loads
-coalesced.  The permutation is within groups, so pooled outputs and dX are unchanged;
-``neuron_order[g][p]`` is the slot stored at position p, and ``canonical`` /
-``canonical_shard`` return tensors in slot order (the layout of ``SparsePoolingLayer``).
+Storage order.  A shard on a GPU stores its neurons, by default, in octet order (``gl_group_octets``):
+within each group the records are permuted so that every 8 consecutive records ("octet") cover the
+residues d mod 8 of their inputs evenly, and each record's 8 (index, weight) pairs are permuted so that at
+every input position the octet's records read 8 distinct residues; the lane-per-neuron kernels
+(``gl_fwd_octet_f32`` / ``gl_bwd_octet_f32``) then gather and scatter without shared-memory bank
+conflicts.  ``neuron_order="bank"`` keeps the earlier bank-aware processing order of ``gl_group_order``
+(unit 48, neurons only) with the generic kernels, ``"slot"`` the reference's order.  The permutations are
+within groups and within records, so pooled outputs and dX are unchanged; ``neuron_order[g][p]`` is the
+slot stored at position p, ``input_order[g][p]`` (octet order) the record's input permutation (bits
+3c .. 3c+2: the original input placed at position c), and ``canonical`` / ``canonical_shard`` return
+tensors in slot order (the layout of ``SparsePoolingLayer``).
 """
 from __future__ import annotations
 
@@ -36,6 +40,18 @@ from torch import nn
 from .autograd import Level1Runtime, _compute_operands, _grad_buffers, act_torch, check_supported, dact_torch
 from .config import PhysicalPlan, PoolingConfig
 from .layout import SparseLayout, init_parameters
+
+
+def _default_runtime(lay):
+    rt = Level1Runtime(lay.layout, lay.indices, lay.cfg.levels[0], lay.plan, counts=lay.counts)
+    rt.octets = lay.input_order is not None
+    return rt
+
+
+def _input_index(kperm: torch.Tensor) -> torch.Tensor:
+    """[G, slots, 8] int64: the original input index placed at each position (bits 3c .. 3c+2 of kperm)."""
+    sh = torch.arange(0, 24, 3, device=kperm.device, dtype=torch.int32)
+    return ((kperm[:, :, None] >> sh) & 7).long()
 
 
 def shard_range(G: int, rank: int, world: int):
@@ -103,7 +119,7 @@ class GroupShardedLayer(nn.Module):
 
     def __init__(self, input_dim: int, hidden_dim: int, output_dim: int, pooling="mean",
                  plan: Optional[PhysicalPlan] = None, device=None, seed: int = 0, bias_std: float = 0.0,
-                 group=None, runtime_factory: Optional[Callable] = None, _params=None, neuron_order: str = "bank"):
+                 group=None, runtime_factory: Optional[Callable] = None, _params=None, neuron_order: str = "octet"):
         super().__init__()
         self.group = group
         self.rank = dist.get_rank(group)
@@ -129,38 +145,51 @@ class GroupShardedLayer(nn.Module):
         self.weight = nn.Parameter(w)
         self.bias = nn.Parameter(b)
         self.register_buffer("counts", counts.to(idx.device))
-        factory = runtime_factory or (lambda lay: Level1Runtime(lay.layout, lay.indices, lay.cfg.levels[0],
-                                                                lay.plan, counts=lay.counts))
+        factory = runtime_factory or _default_runtime
         self._factory = factory
         self._rt = None
-        if neuron_order not in ("bank", "slot"):
-            raise ValueError("neuron_order must be 'bank' or 'slot'")
+        if neuron_order not in ("octet", "bank", "slot"):
+            raise ValueError("neuron_order must be 'octet', 'bank' or 'slot'")
+        self.order_kind = neuron_order
         self.register_buffer("neuron_order", None)
-        if neuron_order == "bank":
+        self.register_buffer("input_order", None)
+        if neuron_order != "slot":
             self.reorder_neurons()
 
     @torch.no_grad()
     def reorder_neurons(self):
-        """Store this shard's neurons in bank-aware processing order (module docstring).  Needs CUDA
+        """Store this shard's records in octet (or bank-aware) order (module docstring).  Needs CUDA
         tensors (a no-op otherwise) and must run before optimizer state exists: parameters and any
         ``main_grad`` buffers are permuted in place."""
-        if self.neuron_order is not None or not self.indices.is_cuda or self.indices.shape[0] == 0:
+        if (self.order_kind == "slot" or self.neuron_order is not None or not self.indices.is_cuda
+                or self.indices.shape[0] == 0):
             return
         from . import _native
 
         G_l, NB = self.indices.shape[0], self.layout.blocks_per_group
         slots = NB * 8
-        o = torch.empty((G_l, slots), dtype=torch.int32, device=self.indices.device)
-        _native.group_order(self.indices, self.counts.to(torch.int32).contiguous(), self.layout.input_dim, NB, 0,
-                            G_l, 48, o)
+        dev = self.indices.device
+        counts = self.counts.to(torch.int32).contiguous()
+        o = torch.empty((G_l, slots), dtype=torch.int32, device=dev)
+        kp = None
+        if self.order_kind == "octet":
+            kp = torch.empty((G_l, slots), dtype=torch.int32, device=dev)
+            _native.group_octets(self.indices, counts, self.layout.input_dim, NB, 0, G_l, o, kp)
+        else:
+            _native.group_order(self.indices, counts, self.layout.input_dim, NB, 0, G_l, 48, o)
         ol = o.long()
+        kidx = _input_index(kp) if kp is not None else None
         for t in (self.indices, self.weight.data, self.bias.data, getattr(self.weight, "main_grad", None),
                   getattr(self.bias, "main_grad", None)):
             if t is not None:
                 per = t.numel() // (G_l * slots)
                 v = t.view(G_l, slots, per)
-                v.copy_(torch.gather(v, 1, ol[:, :, None].expand(G_l, slots, per)))
+                r = torch.gather(v, 1, ol[:, :, None].expand(G_l, slots, per))
+                if kidx is not None and per == 8:
+                    r = torch.gather(r, 2, kidx)
+                v.copy_(r)
         self.neuron_order = o
+        self.input_order = kp
         self._rt = None
 
     def canonical(self, t: torch.Tensor) -> torch.Tensor:
@@ -169,9 +198,14 @@ class GroupShardedLayer(nn.Module):
             return t
         G_l, slots = self.neuron_order.shape
         per = t.numel() // (G_l * slots)
+        src = t.reshape(G_l, slots, per)
+        if self.input_order is not None and per == 8:
+            rec = torch.empty_like(src)
+            rec.scatter_(2, _input_index(self.input_order.to(t.device)), src)
+            src = rec
         ol = self.neuron_order.long().to(t.device)[:, :, None].expand(G_l, slots, per)
         out = torch.empty_like(t)
-        out.view(G_l, slots, per).scatter_(1, ol, t.reshape(G_l, slots, per))
+        out.view(G_l, slots, per).scatter_(1, ol, src)
         return out
 
     def canonical_shard(self):
@@ -208,15 +242,15 @@ class GroupShardedLayer(nn.Module):
             if tuple(src.shape[1:]) != tuple(dst.shape[1:]) or src.shape[0] != self.layout.groups:
                 raise ValueError(f"{name}: full shape {tuple(src.shape)} does not match this layer")
             dst.copy_(src[self.g0:self.g1])
-        order, self.neuron_order = self.neuron_order, None
+        order, self.neuron_order, self.input_order = self.neuron_order, None, None
         self._rt = None
         if order is not None:
             self.reorder_neurons()
 
     @classmethod
-    def from_full(cls, layer, group=None, runtime_factory=None, neuron_order: str = "bank"):
+    def from_full(cls, layer, group=None, runtime_factory=None, neuron_order: str = "octet"):
         """Shard an existing (full) ``SparsePoolingLayer``: slices of its tensors (reordered into the
-        bank-aware storage order when they are on a GPU; ``reorder_neurons`` after moving otherwise)."""
+        octet storage order when they are on a GPU; ``reorder_neurons`` after moving otherwise)."""
         L = layer.layout
         world, rank = dist.get_world_size(group), dist.get_rank(group)
         g0, g1 = shard_range(L.groups, rank, world)

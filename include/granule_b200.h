@@ -227,6 +227,30 @@ int gl_group_feature_map(const int16_t* idx, const int32_t* counts, int64_t D, i
 int gl_group_order(const int16_t* idx, const int32_t* counts, int64_t D, int64_t NB, int64_t g0, int64_t g1,
                    int32_t unit, int32_t* out, void* stream);
 
+/* Octet arrangement of Mode-A storage (no counterpart in the reference), for the lane-per-neuron kernels
+ * below: out order[g-g0][p] (p < NB*8) = the slot stored at position p, a permutation of group g's valid
+ * slots (padding slots keep their place), chosen so that every 8 consecutive positions ("octet") hold
+ * records whose 64 inputs cover each residue d mod 8 as evenly as possible; kperm[g-g0][p] = that record's
+ * input order: bits 3c .. 3c+2 are the original input index k placed in column c, chosen so that at each
+ * column the octet's 8 records read 8 distinct residues where the octet allows it.  A caller stores
+ * idx / w (and their gradients) as rec'[p][c] = rec[order[p]][k_c] and b as b'[p] = b[order[p]].  Depends
+ * only on the indices; callers compute it once per layer.  kperm doubles as the kernel's scratch until it
+ * is written. */
+int gl_group_octets(const int16_t* idx, const int32_t* counts, int64_t D, int64_t NB, int64_t g0, int64_t g1,
+                    int32_t* order, int32_t* kperm, void* stream);
+
+/* Lane-per-neuron forward / backward (no counterpart in the reference; the sums of gl_fwd_f32 /
+ * gl_bwd_f32 for the mean and sum pools, fp32 parameters, any activation), tuned for octet-arranged
+ * storage and correct on any storage order.  One lane per record, a warp step = 4 octets: the forward
+ * stages 8 tokens as two 4-token half tiles, the backward 4 tokens and an int32 dX tile at one fixed-point
+ * scale per token for the block's groups (`wabsmax`, `rowmax` required; K = min(2^22, 0.9 2^31 / sum of
+ * the block's rowmax)), so D <= (shared memory per block - 1 KiB) / 32 (7,232 on B200; GL_ERR_SMEM beyond).
+ * `tokens` must be 0 (or 8 / 4); order, locality, winners and stat must be NULL; other pools and bf16
+ * storage return GL_ERR_UNSUPPORTED.  dx, dw, db are accumulated as in gl_bwd_f32; the forward writes pre
+ * (and wabsmax when given) as gl_fwd_f32 does. */
+int gl_fwd_octet_f32(const GlFwdArgs* args, void* stream);
+int gl_bwd_octet_f32(const GlBwdArgs* args, void* stream);
+
 /* Mode B (shared index records), fp32.  Block j of group g holds C neurons (C = 8, 16, 32 or 64)
  * sharing one 8-input record; slot s = j*C + c is valid iff s < counts[g]:
  *   z[t, g, j, c] = b[g][j][c] + sum_k w[g][j][c][k] * x[t, idx[g][j][k]]
