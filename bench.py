@@ -80,9 +80,10 @@ IDX_BYTES = 2
 METRIC = "neuron-samples/s fwd+bwd+opt @100M fan-in-8, B=1024; % HBM roofline; 1/2/4/8 GPU"
 UNIT = "neuron-samples/s"
 FALLBACK_HBM_GBS = 6650.0
-# DRAM bytes (read + write) per neuron per backward launch at B = 1024, from the ncu
-# capture in profiles/bwd_kernel_fixed_g512.md (1.765 GB for 512 x 24,576 neurons); the
-# traffic grows with the neuron count, so a full launch is this figure times N.
+# DRAM bytes (read + write) per neuron per backward launch at B = 1024, from the ncu capture in
+# BWD_PROFILE (512 x 24,576 neurons); the traffic grows with the neuron count, so a full launch is
+# this figure times N.
+BWD_PROFILE = "profiles/bwd_kernel_fixed_g512.md"
 BWD_DRAM_BYTES_PER_NEURON = 1.764587e9 / (512 * 24576)
 
 
@@ -167,6 +168,18 @@ class ClockSampler:
         self._stop.set()
         if self._t:
             self._t.join(timeout=2)
+
+    @staticmethod
+    def max_clock_hz(index) -> float:
+        """The GPU's maximum SM clock (NVML, read-only), else the B200's 1965 MHz."""
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            return 1e6 * pynvml.nvmlDeviceGetMaxClockInfo(pynvml.nvmlDeviceGetHandleByIndex(index),
+                                                          pynvml.NVML_CLOCK_SM)
+        except Exception:  # noqa: BLE001
+            return 1.965e9
 
     def summary(self):
         if not self.ok or not self.samples:
@@ -1131,18 +1144,27 @@ def main():
         achieved = bwd_bytes / (bwd_ms * 1e-3) / 1e9
         step_bytes = 2 * param_bytes(N) + 2 * gather_bytes(B, N)
         traffic = BWD_DRAM_BYTES_PER_NEURON * n_local if B == 1024 else None
+        # physical limiter: the shared-memory data path.  Per (neuron, input, 4 tokens) the backward moves a
+        # 16-byte x gather and a 16-byte dX scatter through it, 128 bytes per SM clock at best.
+        sms = torch.cuda.get_device_properties(dev).multi_processor_count
+        smem_floor_ms = (B * n_local * K_FAN * 8) / (128 * sms * ClockSampler.max_clock_hz(dev.index)) * 1e3
         line = {
             "metric": METRIC, "value": B * N / (ms / 1e3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": config_dict(world),
             "hbm_roofline_step_frac": (step_bytes / (peak * 1e9)) / (ms / 1e3),
-            "roofline": {"bound": "hbm", "kernel": "gl_bwd_f32 (bwd_kernel<4,relu>)", "achieved": achieved,
-                         "peak": peak, "unit": "GB/s", "frac": achieved / peak, "peak_source": peak_kind,
-                         "traffic": traffic, "traffic_source": "ncu dram bytes of a 512-group capture, "
-                                                              "scaled by neuron count (profiles/bwd_kernel_fixed_g512.md)",
+            "roofline": {"bound": "hbm", "kernel": rt.last_info.get("backward_kernel", "gl_bwd_f32"),
+                         "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "peak_source": peak_kind, "traffic": traffic,
+                         "traffic_source": f"ncu dram bytes of a 512-group capture, scaled by neuron count "
+                                           f"({BWD_PROFILE})",
                          "algorithmic_bytes_per_launch": bwd_bytes,
                          "definition": "(param + x-gather bytes) per launch / CUDA-event launch time; "
-                                       "gathers count as logical HBM bytes per the baseline definition"},
+                                       "gathers count as logical HBM bytes per the baseline definition, "
+                                       "although they are served from shared memory",
+                         "smem_floor_ms": smem_floor_ms, "smem_floor_frac": smem_floor_ms / bwd_ms,
+                         "smem_floor_definition": "B*N*8 x (16-byte gather + 16-byte scatter) / 4 tokens, at "
+                                                  "128 bytes per SM clock, all SMs at the maximum SM clock"},
             "kernels_ms": {"fwd": fwd_ms, "bwd": bwd_ms, "fwd_max_rank": fwd_max, "bwd_max_rank": bwd_max},
             "clocks": clk.summary(), "gpu_launches": launches,
             "e2e": e2e, "cpu_baseline": cb,
