@@ -83,8 +83,8 @@ FALLBACK_HBM_GBS = 6650.0
 # DRAM bytes (read + write) per neuron per backward launch at B = 1024, from the ncu capture in
 # BWD_PROFILE (512 x 24,576 neurons); the traffic grows with the neuron count, so a full launch is
 # this figure times N.
-BWD_PROFILE = "profiles/bwd_kernel_fixed_g512.md"
-BWD_DRAM_BYTES_PER_NEURON = 1.764587e9 / (512 * 24576)
+BWD_PROFILE = "profiles/octet_kernels_g512.md"
+BWD_DRAM_BYTES_PER_NEURON = 1.874112e9 / (512 * 24576)
 
 
 def param_bytes(n):
