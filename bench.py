@@ -660,52 +660,76 @@ FB_METRIC = "neuron-samples/s fwd+bwd @100M fan-in-8, B=256 (D=4096, G=4096)"
 
 
 def bench_fwdbwd256(args):
-    """BASELINE config 2 (module docstring); rank 0 only, 1 GPU."""
+    """BASELINE config 2 (module docstring); rank 0 only, 1 GPU.  Two rows: the drop-in
+    SparsePoolingLayer (the reference's storage order, the generic kernels) and the training engine's
+    single-rank GroupShardedLayer (octet storage, the lane-per-neuron kernels); the line's value is the
+    faster one."""
+    import torch.distributed as dist
+
     from granulelayer_b200 import SparsePoolingLayer, _native
+    from granulelayer_b200.distributed import GroupShardedLayer
 
     Bc = 256
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    lay = SparsePoolingLayer(D, N, G, shared_neurons=None, pooling="mean", dtype=torch.float32, device=dev, seed=1,
-                             bias_std=0.1)
-    lay.enable_main_grad()
+    if not dist.is_initialized():
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        os.environ.setdefault("MASTER_PORT", str(29500 + (os.getpid() % 1000)))
+        dist.init_process_group("nccl", rank=0, world_size=1, timeout=timedelta(seconds=300), device_id=dev)
     gen = torch.Generator(device=dev).manual_seed(1)
     x = torch.randn(Bc, D, device=dev, generator=gen)
     dy = torch.randn(Bc, G, device=dev, generator=gen)
-    ev = {"fwd": [], "bwd": []}
-    orig = {"fwd": _native.fwd, "bwd": _native.bwd}
+    rows = {}
+    for kind in ("layer", "engine"):
+        if kind == "layer":
+            lay = SparsePoolingLayer(D, N, G, shared_neurons=None, pooling="mean", dtype=torch.float32, device=dev,
+                                     seed=1, bias_std=0.1)
+            names = ("fwd", "bwd")
+        else:
+            lay = GroupShardedLayer(D, N, G, pooling="mean", device=dev, seed=1, bias_std=0.1)
+            names = ("fwd_octet", "bwd_octet")
+        lay.enable_main_grad()
+        ev = {"fwd": [], "bwd": []}
+        orig = {n: getattr(_native, n) for n in names}
 
-    def timed(name):
-        def wrap(*a, **k):
-            s_, e_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            s_.record()
-            orig[name](*a, **k)
-            e_.record()
-            ev[name].append((s_, e_))
-        return wrap
+        def timed(fn, slot):
+            def wrap(*a, **k):
+                s_, e_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                s_.record()
+                fn(*a, **k)
+                e_.record()
+                ev[slot].append((s_, e_))
+            return wrap
 
-    def step():
-        lay(x.detach().requires_grad_(True)).backward(dy)
+        def step():
+            lay(x.detach().requires_grad_(True)).backward(dy)
 
-    for _ in range(max(3, args.warmup)):
-        step()
-    torch.cuda.synchronize(dev)
-    _native.fwd, _native.bwd = timed("fwd"), timed("bwd")
-    n0 = _native.launch_count()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    try:
-        with ClockSampler(dev.index) as clk:
-            start.record()
-            for _ in range(args.steps):
-                step()
-            end.record()
-            torch.cuda.synchronize(dev)
-    finally:
-        _native.fwd, _native.bwd = orig["fwd"], orig["bwd"]
-    launches = _native.launch_count() - n0
-    ms = start.elapsed_time(end) / args.steps
-    fwd_ms = statistics.mean(a.elapsed_time(b) for a, b in ev["fwd"])
-    bwd_ms = statistics.mean(a.elapsed_time(b) for a, b in ev["bwd"])
+        for _ in range(max(3, args.warmup)):
+            step()
+        torch.cuda.synchronize(dev)
+        for n, slot in zip(names, ("fwd", "bwd")):
+            setattr(_native, n, timed(orig[n], slot))
+        n0 = _native.launch_count()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        try:
+            with ClockSampler(dev.index) as clk:
+                start.record()
+                for _ in range(args.steps):
+                    step()
+                end.record()
+                torch.cuda.synchronize(dev)
+        finally:
+            for n in names:
+                setattr(_native, n, orig[n])
+        rows[kind] = {"ms": start.elapsed_time(end) / args.steps,
+                      "fwd_ms": statistics.mean(a.elapsed_time(b) for a, b in ev["fwd"]),
+                      "bwd_ms": statistics.mean(a.elapsed_time(b) for a, b in ev["bwd"]),
+                      "kernels": names, "launches": _native.launch_count() - n0, "clocks": clk.summary()}
+        del lay
+        torch.cuda.empty_cache()
+    head_kind = min(rows, key=lambda k: rows[k]["ms"])
+    head = rows[head_kind]
+    ms, fwd_ms, bwd_ms = head["ms"], head["fwd_ms"], head["bwd_ms"]
     peak, peak_kind = peak_hbm()
     pass_bytes = param_bytes(N) + gather_bytes(Bc, N)
     achieved = pass_bytes / (bwd_ms * 1e-3) / 1e9
@@ -715,15 +739,17 @@ def bench_fwdbwd256(args):
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": "100M-neuron fan-in-8 Mode-A fp32 mean-ReLU layer, fwd+bwd at B=256 "
                                "(BASELINE config 2)", "D": D, "N": N, "G": G, "global_batch": Bc, "seed": 1,
-                   "bias_std": 0.1, "l2": "parameters (5.2 GB) larger than L2"},
+                   "bias_std": 0.1, "l2": "parameters (5.2 GB) larger than L2", "timed": head_kind},
         "hbm_roofline_step_frac": (2 * pass_bytes / (peak * 1e9)) / (ms / 1e3),
         "fwd_hbm_roofline_frac": (pass_bytes / (peak * 1e9)) / (fwd_ms / 1e3),
-        "roofline": {"bound": "hbm", "kernel": "gl_bwd_f32", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": achieved / peak, "peak_source": peak_kind, "traffic": None,
-                     "algorithmic_bytes_per_launch": pass_bytes},
-        "kernels_ms": {"fwd": fwd_ms, "bwd": bwd_ms}, "clocks": clk.summary(), "gpu_launches": launches,
+        "roofline": {"bound": "hbm", "kernel": "gl_" + head["kernels"][1] + "_f32", "achieved": achieved,
+                     "peak": peak, "unit": "GB/s", "frac": achieved / peak, "peak_source": peak_kind,
+                     "traffic": None, "algorithmic_bytes_per_launch": pass_bytes},
+        "kernels_ms": {"fwd": fwd_ms, "bwd": bwd_ms}, "clocks": head["clocks"], "gpu_launches": head["launches"],
+        "rows": rows,
     }
     print(json.dumps(line), flush=True)
+    dist.destroy_process_group()
 
 
 MB_METRIC = "neuron-samples/s fwd+bwd+opt, Mode B C=64, H=1e8, D=G=1024, B=8192"
