@@ -43,7 +43,7 @@ EXPORTS = ("gl_abi_version", "gl_status_string", "gl_last_cuda_error", "gl_fwd_f
            "gl_shared_auto_tokens", "gl_bwd_shared_det_f32", "gl_bwd_shared_det_static_f32", "gl_k16_fwd_f32",
            "gl_k16_bwd_f32", "gl_k16_auto_tokens", "gl_k16_fwd_tc", "gl_k16_bwd_tc", "gl_k16_fwd_tc_f32",
            "gl_k16_bwd_tc_f32", "gl_struct_layout", "gl_struct_fields", "gl_group_octets", "gl_fwd_octet_f32",
-           "gl_bwd_octet_f32")
+           "gl_bwd_octet_f32", "gl_k16_fwd_t5", "gl_k16_fwd_t5_f32")
 
 
 class GlSetArgs(ctypes.Structure):
@@ -216,6 +216,9 @@ def load(path=None) -> ctypes.CDLL:
         lib.gl_bwd_shared_tc_sets.restype = ctypes.c_int
         lib.gl_fwd_shared_tc_sets.argtypes = [ctypes.POINTER(GlSharedArgs), ctypes.POINTER(GlSetArgs), ctypes.c_void_p]
         lib.gl_fwd_shared_tc_sets.restype = ctypes.c_int
+        for name in ("gl_k16_fwd_t5", "gl_k16_fwd_t5_f32"):
+            getattr(lib, name).argtypes = [ctypes.POINTER(GlK16Args), ctypes.c_void_p, ctypes.c_void_p]
+            getattr(lib, name).restype = ctypes.c_int
         lib.gl_k16_auto_tokens.restype = ctypes.c_int
         lib.gl_k16_auto_tokens.argtypes = [ctypes.c_int64, ctypes.c_int64, ctypes.c_int32]
         if path is None:
@@ -608,6 +611,20 @@ def k16_bwd(x, sched: dict, w, b, counts, c1t, dx, dw, db, NB16: int, act: int =
             if wabsmax is not None or rowmax is not None:
                 _require_cuda(wabsmax, rowmax)
             _check(lib, getattr(lib, name)(ctypes.byref(a), _ptr(wabsmax), _ptr(rowmax), _stream(x.device)), name)
+    return name
+
+
+def k16_fwd_t5(x, sched: dict, w, b, counts, pre, NB16: int, act: int = 1, status=None) -> str:
+    """pre[t, g] += Mean-pooled act(z) of the K16/C16 layer on the tcgen05 tensor cores (gl_k16_fwd_t5 for
+    bf16 parameters, gl_k16_fwd_t5_f32 for fp32 ones, three-term splits); ``status`` (int32 [1], device,
+    optional) receives 1 if a wait for the tensor cores ran out.  Returns the entry's name."""
+    _require_cuda(x, w, b, counts, pre, status, *sched.values())
+    lib = load()
+    a = _k16_args(x, sched, w, b, counts, NB16, act, 0)
+    a.pre, a.ldp = _ptr(pre), pre.stride(0)
+    name = "gl_k16_fwd_t5" if w.dtype == torch.bfloat16 else "gl_k16_fwd_t5_f32"
+    with torch.cuda.device(x.device):
+        _check(lib, getattr(lib, name)(ctypes.byref(a), _ptr(status), _stream(x.device)), name)
     return name
 
 

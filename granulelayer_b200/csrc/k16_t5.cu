@@ -1,0 +1,317 @@
+// Cover-TopK16 forward on the 5th-generation tensor cores (tcgen05, TMEM accumulators), bf16 parameters
+// and fp32 ones through three-term bf16 splits.  Same model and arguments as gl_k16_fwd_tc /
+// gl_k16_fwd_tc_f32 (k16_tc.cu), i.e. the reference's kgen K = 16 forward
+// (sparse_pooling/experimental/kgen/kgen.cuh:142-200, launched by experimental/kgen_layer.py:61-143):
+//   pre[t, g] += sum over the valid neurons n of g's records f of act(z[t, f, n]) / n_g,
+//   z[t, f, n] = b[f, n] + sum_k w[f, n, k] x[t, feat[q][env[f, k]]].
+//
+// Formulation.  A CTA owns one input set q (S = 64 features) and 128 tokens.  The set's x rows are staged
+// once as the MMA's A operand X [128 tokens x 64 positions] (bf16, 128-byte swizzled, K-major).  The
+// set's records are taken 8 at a time: their weights are written, expanded over the set's 64 positions
+// (zeros where a record has no input), as the B operand W [8 records x 16 neurons = 128 x 64 positions]
+// (K-major), and one 128 x 128 x 64 product X W^T lands in a TMEM accumulator (128 lanes = tokens, 128
+// fp32 columns = the batch's neurons).  Each record's inputs are 16 distinct positions of its set (the
+// reference's lowering requires sorted distinct positions, kgen_lowered.py:175-176), so the expanded
+// weights hold each weight once and every product of the MMA is a product of the model (or zero): the
+// MMA does 4x the useful multiply-adds at tcgen05's rate, in exchange for no gathers.  Eight warps then
+// read the accumulator (warp w: TMEM lanes 32 (w % 4) .., columns 64 (w / 4) ..), add the bias, apply the
+// activation, sum each record's valid neurons per token and keep one partial per token and output,
+// added to pre with one atomic when the output changes (records come in the set's bucket order).
+//
+// fp32 parameters: x and w are each split into three bf16 terms (v = v1 + v2 + v3, as k16_tc.cu), and
+// the accumulator receives the six products of term pairs i + j <= 2 (smallest first) per 16-wide K
+// step, which agrees with the fp32 SIMT kernels to fp32 rounding.
+//
+// Synchronisation: one mbarrier, armed by tcgen05.commit after each batch's MMAs; all threads wait on it
+// with an iteration limit (on expiry the CTA records a timeout in *status, stops issuing work and still
+// frees its TMEM).  Several CTAs share an SM (TMEM 128 columns each, at most 4 resident by their shared
+// memory), so one CTA's MMAs overlap another's weight expansion and epilogue.
+#include <cuda_bf16.h>
+
+#include "common.cuh"
+#include "tc5.cuh"
+
+namespace gl {
+
+constexpr int kT5Threads = 256;
+constexpr int kT5Tokens = 128;
+constexpr int kT5Set = 64;              // positions per set (the MMA's K)
+constexpr uint32_t kT5Plane = 16384;    // one 128 x 64 bf16 operand plane
+constexpr uint32_t kT5WaitLimit = 1u << 20;
+
+struct K16T5Params {
+  const float* x;
+  const uint8_t* env;
+  const int16_t* feat;
+  const int32_t* buckets;
+  const int32_t* q_off;
+  const int32_t* rec_off;
+  const void* w;
+  const void* b;
+  const int32_t* counts;
+  float* pre;
+  int32_t* status;
+  int B, D, G, NB16, nbk;
+  int64_t ldx, ldp;
+};
+
+// The three bf16 terms of v (NS = 3), or its bf16 rounding (NS = 1), as raw bits.
+template <int NS>
+__device__ __forceinline__ void t5_terms(float v, uint16_t (&t)[NS]) {
+  float r = v;
+#pragma unroll
+  for (int j = 0; j < NS; ++j) {
+    const __nv_bfloat16 h = __float2bfloat16_rn(r);
+    t[j] = __bfloat16_as_ushort(h);
+    r -= __bfloat162float(h);
+  }
+}
+
+template <int NS, int ACT>
+__global__ void __launch_bounds__(kT5Threads) k16t5_fwd_kernel(const K16T5Params p) {
+  extern __shared__ unsigned char t5_raw[];
+  __shared__ __align__(8) uint64_t mbar;
+  __shared__ uint32_t tmem_s;
+  __shared__ int abort_s;
+  __shared__ int fq[kT5Set];
+  __shared__ float bias_s[8][16];
+  __shared__ int rg_s[8], rnv_s[8];
+  __shared__ long long rf_s[8];
+  unsigned char* smem = reinterpret_cast<unsigned char*>(((uintptr_t)t5_raw + 1023) & ~(uintptr_t)1023);
+  unsigned char* xpl = smem;                    // NS planes: X [128 tokens][64 positions]
+  unsigned char* wpl = smem + NS * kT5Plane;    // NS planes: W [128 batch neurons][64 positions]
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int q = blockIdx.y, t0 = blockIdx.x * kT5Tokens;
+  if (warp == 0) t5_tmem_alloc(t5_smem_u32(&tmem_s), 128);
+  if (tid == 0) {
+    t5_mbar_init(t5_smem_u32(&mbar), 1);
+    abort_s = 0;
+  }
+  if (tid < kT5Set) {
+    const int d = (int)(uint16_t)__ldg(p.feat + (int64_t)q * kT5Set + tid);
+    fq[tid] = d < p.D ? d : p.D - 1;
+  }
+  __syncthreads();
+  // stage X: 128 rows x 8 chunks of 8 positions per plane
+  for (int c = tid; c < kT5Tokens * 8; c += kT5Threads) {
+    const int row = c >> 3, ch = c & 7, t = t0 + row;
+    uint16_t terms[8][NS];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float v = t < p.B ? __ldg(p.x + (int64_t)t * p.ldx + fq[8 * ch + e]) : 0.f;
+      t5_terms<NS>(v, terms[e]);
+    }
+#pragma unroll
+    for (int j = 0; j < NS; ++j) {
+      uint4 u;
+      u.x = (uint32_t)terms[0][j] | ((uint32_t)terms[1][j] << 16);
+      u.y = (uint32_t)terms[2][j] | ((uint32_t)terms[3][j] << 16);
+      u.z = (uint32_t)terms[4][j] | ((uint32_t)terms[5][j] << 16);
+      u.w = (uint32_t)terms[6][j] | ((uint32_t)terms[7][j] << 16);
+      *reinterpret_cast<uint4*>(xpl + j * kT5Plane + t5_sw128_off(row, 8 * ch)) = u;
+    }
+  }
+  t5_fence_smem_to_async();
+  t5_fence_before_sync();
+  __syncthreads();
+  t5_fence_after_sync();
+  const uint32_t tmem = tmem_s;
+  const int qa = min(max(__ldg(p.q_off + q), 0), p.nbk), qb = min(max(__ldg(p.q_off + q + 1), qa), p.nbk);
+  const int ra = __ldg(p.rec_off + qa), rb = __ldg(p.rec_off + qb);
+  const int nbatch = rb > ra ? (rb - ra + 7) / 8 : 0;
+  const uint32_t idesc = t5_idesc_bf16(128, 128, 0, 0);
+  const uint32_t xs_u = t5_smem_u32(xpl), ws_u = t5_smem_u32(wpl), mbar_u = t5_smem_u32(&mbar);
+  // epilogue geometry: this thread's token row and its warp's 64 columns (4 records)
+  const int erow = 32 * (warp & 3) + lane, et = t0 + erow, ecol = 64 * (warp >> 2);
+  float acc = 0.f;
+  int gcur = -1;
+  auto flush = [&]() {
+    if (gcur >= 0 && et < p.B)
+      atomicAdd(p.pre + (int64_t)et * p.ldp + gcur, acc / (float)max(__ldg(p.counts + gcur), 1));
+  };
+  for (int bt = 0; bt < nbatch; ++bt) {
+    if (tid < 8) {  // record tid of the batch: its output, storage index and valid neurons
+      const int r = ra + 8 * bt + tid;
+      int g = -1, nv = 0;
+      long long f = 0;
+      if (r < rb) {
+        int lo = qa, hi = qb - 1;  // the bucket b with rec_off[b] <= r < rec_off[b + 1]
+        while (lo < hi) {
+          const int mid = (lo + hi + 1) >> 1;
+          if (__ldg(p.rec_off + mid) <= r) lo = mid;
+          else hi = mid - 1;
+        }
+        const int4 bk = __ldg(reinterpret_cast<const int4*>(p.buckets) + lo);
+        const int j16 = bk.z + (r - __ldg(p.rec_off + lo));
+        if (bk.y >= 0 && bk.y < p.G && j16 >= 0 && j16 < p.NB16) {
+          g = bk.y;
+          f = (long long)g * p.NB16 + j16;
+          nv = min(max(__ldg(p.counts + g) - 16 * j16, 0), 16);
+        }
+      }
+      rg_s[tid] = g;
+      rf_s[tid] = f;
+      rnv_s[tid] = nv;
+    }
+    for (int i = tid; i < NS * (int)kT5Plane / 16; i += kT5Threads)
+      reinterpret_cast<uint4*>(wpl)[i] = make_uint4(0, 0, 0, 0);
+    __syncthreads();
+    {  // expand the weights: warp r = record r, lane = (neuron lane / 2, inputs 8 (lane % 2) ..)
+      const int r = warp, n = lane >> 1, kh = lane & 1;
+      if (rg_s[r] >= 0) {
+        const long long f = rf_s[r];
+        const uint2 ev = __ldg(reinterpret_cast<const uint2*>(p.env + f * 16 + 8 * kh));
+        float wv[8];
+        if constexpr (NS == 1) {
+          const uint4 u = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.w) + f * 256 + n * 16 + 8 * kh));
+          const uint32_t uu[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            wv[2 * e] = bf16_lo(uu[e]);
+            wv[2 * e + 1] = bf16_hi(uu[e]);
+          }
+        } else {
+          const float4* w4 = reinterpret_cast<const float4*>(static_cast<const float*>(p.w) + f * 256 + n * 16 + 8 * kh);
+          const float4 a = __ldg(w4), c = __ldg(w4 + 1);
+          wv[0] = a.x; wv[1] = a.y; wv[2] = a.z; wv[3] = a.w;
+          wv[4] = c.x; wv[5] = c.y; wv[6] = c.z; wv[7] = c.w;
+        }
+        const int row = 16 * r + n;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const uint32_t word = e < 4 ? ev.x : ev.y;
+          const int s = min((int)((word >> (8 * (e & 3))) & 0xffu), kT5Set - 1);
+          uint16_t terms[NS];
+          t5_terms<NS>(wv[e], terms);
+#pragma unroll
+          for (int j = 0; j < NS; ++j)
+            *reinterpret_cast<uint16_t*>(wpl + j * kT5Plane + t5_sw128_off(row, s)) = terms[j];
+        }
+      }
+      if (tid < 128) {
+        const int rr = tid >> 4, nn = tid & 15;
+        float bv = 0.f;
+        if (rg_s[rr] >= 0) {
+          const long long bi = rf_s[rr] * 16 + nn;
+          bv = NS == 1 ? __uint_as_float((uint32_t)__ldg(static_cast<const uint16_t*>(p.b) + bi) << 16)
+                       : __ldg(static_cast<const float*>(p.b) + bi);
+        }
+        bias_s[rr][nn] = bv;
+      }
+    }
+    t5_fence_smem_to_async();
+    __syncthreads();
+    if (tid == 0 && !abort_s) {
+      t5_fence_after_sync();
+      uint32_t first = 1;
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk)
+#pragma unroll
+        for (int sum = NS - 1; sum >= 0; --sum)
+#pragma unroll
+          for (int i = 0; i <= sum; ++i) {
+            const uint64_t ad = t5_desc_sw128(xs_u + i * kT5Plane + 32 * kk, 16, 1024);
+            const uint64_t bd = t5_desc_sw128(ws_u + (sum - i) * kT5Plane + 32 * kk, 16, 1024);
+            t5_mma_bf16(tmem, ad, bd, idesc, first ? 0u : 1u);
+            first = 0;
+          }
+      t5_commit(mbar_u);
+    }
+    const bool ok = abort_s == 0 && t5_mbar_wait(mbar_u, (uint32_t)(bt & 1), kT5WaitLimit);
+    if (!ok) {
+      if (p.status) atomicExch(p.status, 1);
+      abort_s = 1;
+    }
+    t5_fence_after_sync();
+    if (__all_sync(kFullMask, ok)) {  // warp-uniform: the TMEM loads below are .sync.aligned
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        float v[32];
+        t5_ld32(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)(ecol + 32 * c), v);
+#pragma unroll
+        for (int rr = 0; rr < 2; ++rr) {
+          const int r = (ecol >> 4) + 2 * c + rr;
+          const int g = rg_s[r], nv = rnv_s[r];
+          if (g < 0) continue;
+          float s = 0.f;
+#pragma unroll
+          for (int n = 0; n < 16; ++n)
+            if (n < nv) s += act_f<ACT>(v[16 * rr + n] + bias_s[r][n]);
+          if (g != gcur) {
+            flush();
+            gcur = g;
+            acc = 0.f;
+          }
+          acc += s;
+        }
+      }
+    }
+    t5_fence_before_sync();
+    __syncthreads();
+    if (abort_s) break;
+  }
+  flush();
+  t5_fence_before_sync();
+  __syncthreads();
+  if (warp == 0) {
+    t5_fence_after_sync();
+    t5_tmem_dealloc(tmem, 128);
+  }
+}
+
+// Shared memory of the forward: the X and W planes (1 KiB alignment slack), at least 47 KiB so that at most
+// four CTAs (4 x 128 TMEM columns) are resident on an SM.
+template <int NS>
+static size_t t5_fwd_smem() {
+  const size_t need = 2u * NS * kT5Plane + 1024;
+  return need < 48128 ? 48128 : need;
+}
+
+template <int NS, int ACT>
+static int t5_fwd_launch(const K16T5Params& p, int64_t Q, cudaStream_t st) {
+  const size_t smem = t5_fwd_smem<NS>();
+  auto kern = k16t5_fwd_kernel<NS, ACT>;
+  int rc = ensure_dynamic_smem((const void*)kern, smem);
+  if (rc) return rc;
+  const dim3 grid((unsigned)((p.B + kT5Tokens - 1) / kT5Tokens), (unsigned)Q);
+  kern<<<grid, kT5Threads, smem, st>>>(p);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_cuda_error(e);
+  count_launches(1);
+  return GL_OK;
+}
+
+template <int NS>
+static int t5_fwd_run(const GlK16Args* args, int32_t* status, void* stream) {
+  if (!args) return GL_ERR_NULL;
+  const GlK16Args& a = *args;
+  if (a.B < 0 || a.D < 1 || a.D > 32767 || a.G < 1 || a.NB16 < 1 || a.Q < 1 || a.nbuckets < 0) return GL_ERR_SHAPE;
+  if (a.S != kT5Set) return GL_ERR_UNSUPPORTED;
+  if (a.act != GL_ACT_RELU && a.act != GL_ACT_IDENTITY) return GL_ERR_UNSUPPORTED;
+  if (a.tokens != 0 && a.tokens != kT5Tokens) return GL_ERR_UNSUPPORTED;
+  if (a.B == 0 || a.nbuckets == 0) return GL_OK;
+  if (!a.x || !a.env || !a.feat || !a.buckets || !a.q_off || !a.rec_off || !a.w || !a.b || !a.counts || !a.pre)
+    return GL_ERR_NULL;
+  if (a.B > 2147483647LL || a.ldx < a.D || a.Q > 65535 || a.G * a.NB16 > 2147483647LL || a.ldp < a.G)
+    return GL_ERR_SHAPE;
+  if (((uintptr_t)a.env & 15) || ((uintptr_t)a.buckets & 15) || ((uintptr_t)a.w & 15) || ((uintptr_t)a.b & 15))
+    return GL_ERR_ALIGN;
+  int optin = 0;
+  int rc = device_smem_optin(&optin);
+  if (rc) return rc;
+  if ((int64_t)t5_fwd_smem<NS>() > optin) return GL_ERR_SMEM;
+  const K16T5Params p{a.x, a.env, a.feat, a.buckets, a.q_off, a.rec_off, a.w, a.b, a.counts, a.pre, status,
+                      (int)a.B, (int)a.D, (int)a.G, (int)a.NB16, (int)a.nbuckets, a.ldx, a.ldp};
+  cudaStream_t st = (cudaStream_t)stream;
+  return a.act == GL_ACT_RELU ? t5_fwd_launch<NS, GL_ACT_RELU>(p, a.Q, st) : t5_fwd_launch<NS, GL_ACT_IDENTITY>(p, a.Q, st);
+}
+
+}  // namespace gl
+
+extern "C" int gl_k16_fwd_t5(const GlK16Args* args, int32_t* status, void* stream) {
+  return gl::t5_fwd_run<1>(args, status, stream);
+}
+
+extern "C" int gl_k16_fwd_t5_f32(const GlK16Args* args, int32_t* status, void* stream) {
+  return gl::t5_fwd_run<3>(args, status, stream);
+}

@@ -458,6 +458,16 @@ int gl_k16_bwd_tc(const GlK16Args* args, const float* wabsmax, const int32_t* ro
 int gl_k16_fwd_tc_f32(const GlK16Args* args, void* stream);
 int gl_k16_bwd_tc_f32(const GlK16Args* args, const float* wabsmax, const int32_t* rowmax, void* stream);
 
+/* The same forward on the 5th-generation tensor cores (tcgen05 MMAs into TMEM accumulators; no counterpart
+ * in the reference, whose kgen kernels use mma.sync): bf16 parameters (gl_k16_fwd_t5, the reference's
+ * arithmetic as gl_k16_fwd_tc) or fp32 ones (gl_k16_fwd_t5_f32, three-term bf16 splits as
+ * gl_k16_fwd_tc_f32).  Each record's weights are expanded over its set's S positions, so S must be 64
+ * (GL_ERR_UNSUPPORTED otherwise) and a record's 16 positions must be distinct (the reference's lowering
+ * guarantees both); 128 tokens per block (`tokens` 0 or 128).  `status` (optional, device int32) is set
+ * to 1 if a wait for the tensor cores exceeded its iteration limit (the results are then incomplete). */
+int gl_k16_fwd_t5(const GlK16Args* args, int32_t* status, void* stream);
+int gl_k16_fwd_t5_f32(const GlK16Args* args, int32_t* status, void* stream);
+
 /* Layout of the argument structs, for bindings that declare them field by field (replaces the
  * reference's sp_struct_layout, sparse_pooling/kernels/cuda/abi.cu:25, which its ctypes bridge checks
  * at load, backends/cuda/runtime.py:103-121).  which: 0 GlFwdArgs, 1 GlBwdArgs, 2 GlAdamArgs,
