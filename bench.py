@@ -524,7 +524,8 @@ def bench_cover16(args, world):
     t0 = time.perf_counter()
     w64, b64 = init_envelope_parameters(KLayout(Dc, Hc, Gc, 64, 256), dev, dtype=torch.bfloat16, seed=3)
     pdt = torch.bfloat16 if args.cover_dtype == "bf16" else torch.float32
-    plan = PhysicalPlan(grad_precision="split", b200_f32_tensor_cores="off" if args.cover_kernels == "simt" else "auto")
+    plan = PhysicalPlan(grad_precision="split", b200_f32_tensor_cores="off" if args.cover_kernels == "simt" else "auto",
+                        b200_tcgen05="on" if args.cover_kernels == "t5" else "off")
     lay = CoverTopK16Layer.from_envelope(w64, b64, input_dim=Dc, hidden_dim=Hc, output_dim=Gc,
                                          connectivity=ConnectivityPlan(64, 64, seed=3), device=dev, dtype=pdt,
                                          plan=plan)
@@ -537,15 +538,15 @@ def bench_cover16(args, world):
     dy = torch.randn(Bc, Gc, device=dev, generator=gen)
 
     ev = {"fwd": [], "bwd": []}
-    orig = {"fwd": _native.k16_fwd, "bwd": _native.k16_bwd}
+    orig = {"fwd": _native.k16_fwd, "fwd_t5": _native.k16_fwd_t5, "bwd": _native.k16_bwd}
 
-    def timed(name):
+    def timed(name, slot):
         def wrap(*a, **k):
             s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             s.record()
             r = orig[name](*a, **k)
             e.record()
-            ev[name].append((s, e))
+            ev[slot].append((s, e))
             return r
         return wrap
 
@@ -557,7 +558,7 @@ def bench_cover16(args, world):
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize(dev)
-    _native.k16_fwd, _native.k16_bwd = timed("fwd"), timed("bwd")
+    _native.k16_fwd, _native.k16_fwd_t5, _native.k16_bwd = timed("fwd", "fwd"), timed("fwd_t5", "fwd"), timed("bwd", "bwd")
     n0 = _native.launch_count()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     try:
@@ -568,7 +569,7 @@ def bench_cover16(args, world):
             end.record()
             torch.cuda.synchronize(dev)
     finally:
-        _native.k16_fwd, _native.k16_bwd = orig["fwd"], orig["bwd"]
+        _native.k16_fwd, _native.k16_fwd_t5, _native.k16_bwd = orig["fwd"], orig["fwd_t5"], orig["bwd"]
     launches = _native.launch_count() - n0
     ms = start.elapsed_time(end) / args.steps
     fwd_ms = statistics.mean(s.elapsed_time(e) for s, e in ev["fwd"])
@@ -1020,8 +1021,9 @@ def main():
                     help="--impl reference-gpu --workload modeb: the reference layer's parameter dtype")
     ap.add_argument("--cover-dtype", default="fp32", choices=["fp32", "bf16"],
                     help="cover16: parameter storage (fp32 = config 4; bf16 = the reference's, on the tensor cores)")
-    ap.add_argument("--cover-kernels", default="tc", choices=["tc", "simt"],
-                    help="cover16, fp32: tensor-core kernels on three-term bf16 splits (default) or the fp32 SIMT ones")
+    ap.add_argument("--cover-kernels", default="tc", choices=["tc", "t5", "simt"],
+                    help="cover16: mma.sync tensor-core kernels (default); t5 = the forward on tcgen05 (TMEM); "
+                         "simt = the fp32 SIMT kernels (fp32 parameters)")
     ap.add_argument("--cover-outputs", type=int, default=2048,
                     help="cover16: outputs of 24,576 neurons (default 2048 = config 4; fewer for ncu captures)")
     ap.add_argument("--groups", type=int, default=G,

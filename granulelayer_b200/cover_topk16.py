@@ -72,8 +72,11 @@ class _K16Function(torch.autograd.Function):
             xc = xc.contiguous()
         B = xc.shape[0]
         pre = torch.zeros((B, layer.layout.groups), device=x.device, dtype=torch.float32)
-        name = _native.k16_fwd(xc, layer._work(), w, b, layer.counts, pre, layer.layout.blocks_per_group,
-                               tensor_cores=layer.tensor_cores)
+        if layer.tcgen05:
+            name = _native.k16_fwd_t5(xc, layer._work(), w, b, layer.counts, pre, layer.layout.blocks_per_group)
+        else:
+            name = _native.k16_fwd(xc, layer._work(), w, b, layer.counts, pre, layer.layout.blocks_per_group,
+                                   tensor_cores=layer.tensor_cores)
         ctx.layer = layer
         ctx.save_for_backward(x, w, b)
         layer.last_info.update(forward_backend="b200-k16", checkpoint_bytes=0, forward_kernel=name)
@@ -318,6 +321,13 @@ class CoverTopK16Layer(nn.Module):
         """Whether the layer runs the tensor-core kernels: always for bf16 parameters; for fp32 ones, the
         three-term bf16 split kernels unless ``plan.b200_f32_tensor_cores == "off"``."""
         return self.weight.dtype == torch.bfloat16 or self.plan.b200_f32_tensor_cores == "auto"
+
+    @property
+    def tcgen05(self) -> bool:
+        """Whether the forward runs on the tcgen05 tensor cores (gl_k16_fwd_t5 / gl_k16_fwd_t5_f32): tensor-core
+        layers whose input sets have S = 64 positions, when ``plan.b200_tcgen05 == "on"`` (off by default: the
+        mma.sync forward is faster at config 4)."""
+        return self.tensor_cores and self.plan.b200_tcgen05 == "on" and int(self.sg_feat.shape[1]) == 64
 
     def enable_main_grad(self):
         for p in (self.weight, self.bias):

@@ -22,10 +22,13 @@
 // the accumulator receives the six products of term pairs i + j <= 2 (smallest first) per 16-wide K
 // step, which agrees with the fp32 SIMT kernels to fp32 rounding.
 //
-// Synchronisation: one mbarrier, armed by tcgen05.commit after each batch's MMAs; all threads wait on it
-// with an iteration limit (on expiry the CTA records a timeout in *status, stops issuing work and still
-// frees its TMEM).  Several CTAs share an SM (TMEM 128 columns each, at most 4 resident by their shared
-// memory), so one CTA's MMAs overlap another's weight expansion and epilogue.
+// Pipeline: each thread loads its share of the next batch's weights, positions and bias into registers
+// while the current batch's MMAs run and its epilogue reads the accumulator; the expanded weight planes
+// are cleared position by position after use (no bulk clearing), and the set's bucket table sits in
+// shared memory, so a batch costs two barriers.  One mbarrier, armed by tcgen05.commit after each batch's
+// MMAs; all threads wait on it with an iteration limit (on expiry the CTA records a timeout in *status,
+// stops issuing work and still frees its TMEM).  Several CTAs share an SM (TMEM 128 columns each, at most
+// 4 resident by their shared memory), so one CTA's MMAs overlap another's expansion and epilogue.
 #include <cuda_bf16.h>
 
 #include "common.cuh"
@@ -67,30 +70,124 @@ __device__ __forceinline__ void t5_terms(float v, uint16_t (&t)[NS]) {
   }
 }
 
+constexpr int kT5MaxBuckets = 512;     // buckets of one set cached in shared memory (else global lookups)
+
+// Output g, storage index f and valid neurons nv of flat record r of set (qa .. qb): g = -1 when r is past
+// the set's records or its bucket row is malformed.  Bucket rows come from the shared-memory copy when the
+// set has at most kT5MaxBuckets of them.
+struct T5Rec {
+  int g, nv;
+  long long f;
+};
+
+__device__ __forceinline__ T5Rec t5_record(const K16T5Params& p, int qa, int qb, int rb, int r, bool cached,
+                                           const int* bk_rec, const int4* bk_row) {
+  T5Rec o{-1, 0, 0};
+  if (r >= rb || qb <= qa) return o;
+  int lo = qa, hi = qb - 1;  // the bucket b with rec_off[b] <= r < rec_off[b + 1]
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    const int v = cached ? bk_rec[mid - qa] : __ldg(p.rec_off + mid);
+    if (v <= r) lo = mid;
+    else hi = mid - 1;
+  }
+  const int4 bk = cached ? bk_row[lo - qa] : __ldg(reinterpret_cast<const int4*>(p.buckets) + lo);
+  const int j16 = bk.z + (r - (cached ? bk_rec[lo - qa] : __ldg(p.rec_off + lo)));
+  if (bk.y >= 0 && bk.y < p.G && j16 >= 0 && j16 < p.NB16) {
+    o.g = bk.y;
+    o.f = (long long)bk.y * p.NB16 + j16;
+    o.nv = min(max(__ldg(p.counts + bk.y) - 16 * j16, 0), 16);
+  }
+  return o;
+}
+
+// One thread's share of a batch's operands, loaded one batch ahead: the 8 weights of (record warp,
+// neuron lane / 2, inputs 8 (lane % 2) ..), their 8 positions, and (threads < 128) one bias value.
+struct T5Ops {
+  uint2 env;
+  float w[8];
+  float bias;
+};
+
+template <int NS>
+__device__ __forceinline__ T5Ops t5_load_ops(const K16T5Params& p, const int* rg, const long long* rf, int tid) {
+  T5Ops o;
+  const int r = tid >> 5, n = (tid & 31) >> 1, kh = tid & 1;
+  o.env = make_uint2(0, 0);
+#pragma unroll
+  for (int e = 0; e < 8; ++e) o.w[e] = 0.f;
+  if (rg[r] >= 0) {
+    const long long f = rf[r];
+    o.env = __ldg(reinterpret_cast<const uint2*>(p.env + f * 16 + 8 * kh));
+    if constexpr (NS == 1) {
+      const uint4 u = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.w) + f * 256 + n * 16 + 8 * kh));
+      const uint32_t uu[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        o.w[2 * e] = bf16_lo(uu[e]);
+        o.w[2 * e + 1] = bf16_hi(uu[e]);
+      }
+    } else {
+      const float4* w4 = reinterpret_cast<const float4*>(static_cast<const float*>(p.w) + f * 256 + n * 16 + 8 * kh);
+      const float4 a = __ldg(w4), c = __ldg(w4 + 1);
+      o.w[0] = a.x; o.w[1] = a.y; o.w[2] = a.z; o.w[3] = a.w;
+      o.w[4] = c.x; o.w[5] = c.y; o.w[6] = c.z; o.w[7] = c.w;
+    }
+  }
+  o.bias = 0.f;
+  if (tid < 128) {
+    const int rr = tid >> 4, nn = tid & 15;
+    if (rg[rr] >= 0) {
+      const long long bi = rf[rr] * 16 + nn;
+      o.bias = NS == 1 ? __uint_as_float((uint32_t)__ldg(static_cast<const uint16_t*>(p.b) + bi) << 16)
+                       : __ldg(static_cast<const float*>(p.b) + bi);
+    }
+  }
+  return o;
+}
+
+// Position (bytes into a plane) of input e of this thread's share of a row, from the packed positions.
+__device__ __forceinline__ uint32_t t5_wpos(const uint2& env, int e, int row) {
+  const uint32_t word = e < 4 ? env.x : env.y;
+  return t5_sw128_off((uint32_t)row, min((word >> (8 * (e & 3))) & 0xffu, (uint32_t)(kT5Set - 1)));
+}
+
 template <int NS, int ACT>
 __global__ void __launch_bounds__(kT5Threads) k16t5_fwd_kernel(const K16T5Params p) {
   extern __shared__ unsigned char t5_raw[];
-  __shared__ __align__(8) uint64_t mbar;
+  __shared__ __align__(8) uint64_t mbar[2];
   __shared__ uint32_t tmem_s;
   __shared__ int abort_s;
   __shared__ int fq[kT5Set];
-  __shared__ float bias_s[8][16];
-  __shared__ int rg_s[8], rnv_s[8];
-  __shared__ long long rf_s[8];
+  __shared__ __align__(16) float bias_s[2][8][16];
+  __shared__ int rg_s[3][8], rnv_s[3][8];
+  __shared__ long long rf_s[3][8];
+  __shared__ int bk_rec[kT5MaxBuckets + 1];
+  __shared__ int4 bk_row[kT5MaxBuckets];
   unsigned char* smem = reinterpret_cast<unsigned char*>(((uintptr_t)t5_raw + 1023) & ~(uintptr_t)1023);
   unsigned char* xpl = smem;                    // NS planes: X [128 tokens][64 positions]
-  unsigned char* wpl = smem + NS * kT5Plane;    // NS planes: W [128 batch neurons][64 positions]
+  unsigned char* wpl = smem + NS * kT5Plane;    // 2 buffers x NS planes: W [128 batch neurons][64 positions]
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int q = blockIdx.y, t0 = blockIdx.x * kT5Tokens;
-  if (warp == 0) t5_tmem_alloc(t5_smem_u32(&tmem_s), 128);
+  if (warp == 0) t5_tmem_alloc(t5_smem_u32(&tmem_s), 256);
   if (tid == 0) {
-    t5_mbar_init(t5_smem_u32(&mbar), 1);
+    t5_mbar_init(t5_smem_u32(&mbar[0]), 1);
+    t5_mbar_init(t5_smem_u32(&mbar[1]), 1);
     abort_s = 0;
   }
   if (tid < kT5Set) {
     const int d = (int)(uint16_t)__ldg(p.feat + (int64_t)q * kT5Set + tid);
     fq[tid] = d < p.D ? d : p.D - 1;
   }
+  const int qa = min(max(__ldg(p.q_off + q), 0), p.nbk), qb = min(max(__ldg(p.q_off + q + 1), qa), p.nbk);
+  const int ra = __ldg(p.rec_off + qa), rb = __ldg(p.rec_off + qb);
+  const bool cached = qb - qa <= kT5MaxBuckets;
+  if (cached) {
+    for (int i = tid; i <= qb - qa; i += kT5Threads) bk_rec[i] = __ldg(p.rec_off + qa + i);
+    for (int i = tid; i < qb - qa; i += kT5Threads) bk_row[i] = __ldg(reinterpret_cast<const int4*>(p.buckets) + qa + i);
+  }
+  for (int i = tid; i < 2 * NS * (int)kT5Plane / 16; i += kT5Threads)
+    reinterpret_cast<uint4*>(wpl)[i] = make_uint4(0, 0, 0, 0);
   __syncthreads();
   // stage X: 128 rows x 8 chunks of 8 positions per plane
   for (int c = tid; c < kT5Tokens * 8; c += kT5Threads) {
@@ -111,98 +208,57 @@ __global__ void __launch_bounds__(kT5Threads) k16t5_fwd_kernel(const K16T5Params
       *reinterpret_cast<uint4*>(xpl + j * kT5Plane + t5_sw128_off(row, 8 * ch)) = u;
     }
   }
+  const int nbatch = rb > ra ? (rb - ra + 7) / 8 : 0;
+  if (tid < 8) {  // batch 0's records
+    const T5Rec rc = t5_record(p, qa, qb, rb, ra + tid, cached, bk_rec, bk_row);
+    rg_s[0][tid] = rc.g;
+    rf_s[0][tid] = rc.f;
+    rnv_s[0][tid] = rc.nv;
+  }
   t5_fence_smem_to_async();
   t5_fence_before_sync();
   __syncthreads();
   t5_fence_after_sync();
   const uint32_t tmem = tmem_s;
-  const int qa = min(max(__ldg(p.q_off + q), 0), p.nbk), qb = min(max(__ldg(p.q_off + q + 1), qa), p.nbk);
-  const int ra = __ldg(p.rec_off + qa), rb = __ldg(p.rec_off + qb);
-  const int nbatch = rb > ra ? (rb - ra + 7) / 8 : 0;
   const uint32_t idesc = t5_idesc_bf16(128, 128, 0, 0);
-  const uint32_t xs_u = t5_smem_u32(xpl), ws_u = t5_smem_u32(wpl), mbar_u = t5_smem_u32(&mbar);
+  const uint32_t xs_u = t5_smem_u32(xpl), ws_u = t5_smem_u32(wpl);
   // epilogue geometry: this thread's token row and its warp's 64 columns (4 records)
   const int erow = 32 * (warp & 3) + lane, et = t0 + erow, ecol = 64 * (warp >> 2);
+  const int wrow = 16 * warp + ((tid & 31) >> 1);  // the W row this thread expands
   float acc = 0.f;
   int gcur = -1;
   auto flush = [&]() {
     if (gcur >= 0 && et < p.B)
       atomicAdd(p.pre + (int64_t)et * p.ldp + gcur, acc / (float)max(__ldg(p.counts + gcur), 1));
   };
-  for (int bt = 0; bt < nbatch; ++bt) {
-    if (tid < 8) {  // record tid of the batch: its output, storage index and valid neurons
-      const int r = ra + 8 * bt + tid;
-      int g = -1, nv = 0;
-      long long f = 0;
-      if (r < rb) {
-        int lo = qa, hi = qb - 1;  // the bucket b with rec_off[b] <= r < rec_off[b + 1]
-        while (lo < hi) {
-          const int mid = (lo + hi + 1) >> 1;
-          if (__ldg(p.rec_off + mid) <= r) lo = mid;
-          else hi = mid - 1;
-        }
-        const int4 bk = __ldg(reinterpret_cast<const int4*>(p.buckets) + lo);
-        const int j16 = bk.z + (r - __ldg(p.rec_off + lo));
-        if (bk.y >= 0 && bk.y < p.G && j16 >= 0 && j16 < p.NB16) {
-          g = bk.y;
-          f = (long long)g * p.NB16 + j16;
-          nv = min(max(__ldg(p.counts + g) - 16 * j16, 0), 16);
-        }
+  T5Ops ops = t5_load_ops<NS>(p, rg_s[0], rf_s[0], tid);
+  uint2 env_prev = make_uint2(0, 0);
+  // iteration b: expand and multiply batch b (buffer b & 1) while the epilogue reads batch b - 1
+  for (int b = 0; b <= nbatch; ++b) {
+    const uint2 env_cur = ops.env;
+    if (b < nbatch) {
+      unsigned char* wb = wpl + (b & 1) * NS * kT5Plane;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        uint16_t terms[NS];
+        t5_terms<NS>(ops.w[e], terms);
+        const uint32_t off = t5_wpos(env_cur, e, wrow);
+#pragma unroll
+        for (int j = 0; j < NS; ++j) *reinterpret_cast<uint16_t*>(wb + j * kT5Plane + off) = terms[j];
       }
-      rg_s[tid] = g;
-      rf_s[tid] = f;
-      rnv_s[tid] = nv;
-    }
-    for (int i = tid; i < NS * (int)kT5Plane / 16; i += kT5Threads)
-      reinterpret_cast<uint4*>(wpl)[i] = make_uint4(0, 0, 0, 0);
-    __syncthreads();
-    {  // expand the weights: warp r = record r, lane = (neuron lane / 2, inputs 8 (lane % 2) ..)
-      const int r = warp, n = lane >> 1, kh = lane & 1;
-      if (rg_s[r] >= 0) {
-        const long long f = rf_s[r];
-        const uint2 ev = __ldg(reinterpret_cast<const uint2*>(p.env + f * 16 + 8 * kh));
-        float wv[8];
-        if constexpr (NS == 1) {
-          const uint4 u = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.w) + f * 256 + n * 16 + 8 * kh));
-          const uint32_t uu[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            wv[2 * e] = bf16_lo(uu[e]);
-            wv[2 * e + 1] = bf16_hi(uu[e]);
-          }
-        } else {
-          const float4* w4 = reinterpret_cast<const float4*>(static_cast<const float*>(p.w) + f * 256 + n * 16 + 8 * kh);
-          const float4 a = __ldg(w4), c = __ldg(w4 + 1);
-          wv[0] = a.x; wv[1] = a.y; wv[2] = a.z; wv[3] = a.w;
-          wv[4] = c.x; wv[5] = c.y; wv[6] = c.z; wv[7] = c.w;
-        }
-        const int row = 16 * r + n;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const uint32_t word = e < 4 ? ev.x : ev.y;
-          const int s = min((int)((word >> (8 * (e & 3))) & 0xffu), kT5Set - 1);
-          uint16_t terms[NS];
-          t5_terms<NS>(wv[e], terms);
-#pragma unroll
-          for (int j = 0; j < NS; ++j)
-            *reinterpret_cast<uint16_t*>(wpl + j * kT5Plane + t5_sw128_off(row, s)) = terms[j];
-        }
-      }
-      if (tid < 128) {
-        const int rr = tid >> 4, nn = tid & 15;
-        float bv = 0.f;
-        if (rg_s[rr] >= 0) {
-          const long long bi = rf_s[rr] * 16 + nn;
-          bv = NS == 1 ? __uint_as_float((uint32_t)__ldg(static_cast<const uint16_t*>(p.b) + bi) << 16)
-                       : __ldg(static_cast<const float*>(p.b) + bi);
-        }
-        bias_s[rr][nn] = bv;
+      if (tid < 128) bias_s[b & 1][tid >> 4][tid & 15] = ops.bias;
+      if (tid < 8) {  // the next batch's records
+        const T5Rec rc = t5_record(p, qa, qb, rb, ra + 8 * (b + 1) + tid, cached, bk_rec, bk_row);
+        rg_s[(b + 1) % 3][tid] = rc.g;
+        rf_s[(b + 1) % 3][tid] = rc.f;
+        rnv_s[(b + 1) % 3][tid] = rc.nv;
       }
     }
     t5_fence_smem_to_async();
     __syncthreads();
-    if (tid == 0 && !abort_s) {
+    if (b < nbatch && tid == 0 && !abort_s) {
       t5_fence_after_sync();
+      const uint32_t wb_u = ws_u + (b & 1) * NS * kT5Plane, d_t = tmem + (uint32_t)((b & 1) * 128);
       uint32_t first = 1;
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk)
@@ -211,41 +267,65 @@ __global__ void __launch_bounds__(kT5Threads) k16t5_fwd_kernel(const K16T5Params
 #pragma unroll
           for (int i = 0; i <= sum; ++i) {
             const uint64_t ad = t5_desc_sw128(xs_u + i * kT5Plane + 32 * kk, 16, 1024);
-            const uint64_t bd = t5_desc_sw128(ws_u + (sum - i) * kT5Plane + 32 * kk, 16, 1024);
-            t5_mma_bf16(tmem, ad, bd, idesc, first ? 0u : 1u);
+            const uint64_t bd = t5_desc_sw128(wb_u + (sum - i) * kT5Plane + 32 * kk, 16, 1024);
+            t5_mma_bf16(d_t, ad, bd, idesc, first ? 0u : 1u);
             first = 0;
           }
-      t5_commit(mbar_u);
+      t5_commit(t5_smem_u32(&mbar[b & 1]));
     }
-    const bool ok = abort_s == 0 && t5_mbar_wait(mbar_u, (uint32_t)(bt & 1), kT5WaitLimit);
-    if (!ok) {
-      if (p.status) atomicExch(p.status, 1);
-      abort_s = 1;
-    }
-    t5_fence_after_sync();
-    if (__all_sync(kFullMask, ok)) {  // warp-uniform: the TMEM loads below are .sync.aligned
+    if (b + 1 < nbatch) ops = t5_load_ops<NS>(p, rg_s[(b + 1) % 3], rf_s[(b + 1) % 3], tid);  // under the MMAs
+    if (b >= 1) {  // epilogue of batch b - 1
+      const int pb = b - 1, sl = pb & 1, is = pb % 3;
+      const bool ok = abort_s == 0 &&
+                      t5_mbar_wait(t5_smem_u32(&mbar[sl]), (uint32_t)((pb >> 1) & 1), kT5WaitLimit);
+      if (!ok) {
+        if (p.status) atomicExch(p.status, 1);
+        abort_s = 1;
+      }
+      t5_fence_after_sync();
+      if (__all_sync(kFullMask, ok)) {  // warp-uniform: the TMEM loads below are .sync.aligned
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        float v[32];
-        t5_ld32(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)(ecol + 32 * c), v);
+        for (int c = 0; c < 2; ++c) {
+          float v[32];
+          t5_ld32(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)(sl * 128 + ecol + 32 * c), v);
 #pragma unroll
-        for (int rr = 0; rr < 2; ++rr) {
-          const int r = (ecol >> 4) + 2 * c + rr;
-          const int g = rg_s[r], nv = rnv_s[r];
-          if (g < 0) continue;
-          float s = 0.f;
+          for (int rr = 0; rr < 2; ++rr) {
+            const int r = (ecol >> 4) + 2 * c + rr;
+            const int g = rg_s[is][r], nv = rnv_s[is][r];
+            if (g < 0) continue;
+            const float4* bq = reinterpret_cast<const float4*>(bias_s[sl][r]);
+            float sm = 0.f;
 #pragma unroll
-          for (int n = 0; n < 16; ++n)
-            if (n < nv) s += act_f<ACT>(v[16 * rr + n] + bias_s[r][n]);
-          if (g != gcur) {
-            flush();
-            gcur = g;
-            acc = 0.f;
+            for (int n4 = 0; n4 < 4; ++n4) {
+              const float4 bb = bq[n4];
+              const float a0 = act_f<ACT>(v[16 * rr + 4 * n4] + bb.x), a1 = act_f<ACT>(v[16 * rr + 4 * n4 + 1] + bb.y);
+              const float a2 = act_f<ACT>(v[16 * rr + 4 * n4 + 2] + bb.z), a3 = act_f<ACT>(v[16 * rr + 4 * n4 + 3] + bb.w);
+              if (nv == 16) {
+                sm += (a0 + a1) + (a2 + a3);
+              } else {
+                sm += (4 * n4 < nv ? a0 : 0.f) + (4 * n4 + 1 < nv ? a1 : 0.f) + (4 * n4 + 2 < nv ? a2 : 0.f) +
+                      (4 * n4 + 3 < nv ? a3 : 0.f);
+              }
+            }
+            if (g != gcur) {
+              flush();
+              gcur = g;
+              acc = 0.f;
+            }
+            acc += sm;
           }
-          acc += s;
         }
       }
+      // clear the positions batch b - 1 wrote (its MMAs have completed)
+      unsigned char* wb = wpl + sl * NS * kT5Plane;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const uint32_t off = t5_wpos(env_prev, e, wrow);
+#pragma unroll
+        for (int j = 0; j < NS; ++j) *reinterpret_cast<uint16_t*>(wb + j * kT5Plane + off) = 0;
+      }
     }
+    env_prev = env_cur;
     t5_fence_before_sync();
     __syncthreads();
     if (abort_s) break;
@@ -255,16 +335,16 @@ __global__ void __launch_bounds__(kT5Threads) k16t5_fwd_kernel(const K16T5Params
   __syncthreads();
   if (warp == 0) {
     t5_fence_after_sync();
-    t5_tmem_dealloc(tmem, 128);
+    t5_tmem_dealloc(tmem, 256);
   }
 }
 
-// Shared memory of the forward: the X and W planes (1 KiB alignment slack), at least 47 KiB so that at most
-// four CTAs (4 x 128 TMEM columns) are resident on an SM.
+// Shared memory of the forward: the X planes and two buffers of W planes (1 KiB alignment slack), at least
+// 80 KiB so that at most two CTAs (2 x 256 TMEM columns) are resident on an SM.
 template <int NS>
 static size_t t5_fwd_smem() {
-  const size_t need = 2u * NS * kT5Plane + 1024;
-  return need < 48128 ? 48128 : need;
+  const size_t need = 3u * NS * kT5Plane + 1024;
+  return need < 81920 ? 81920 : need;
 }
 
 template <int NS, int ACT>

@@ -116,6 +116,14 @@ def test_kernel_family_follows_dtype_and_plan():
         ["gl_k16_fwd_f32", "gl_k16_bwd_f32"]
     assert [_native._k16_entry(b16.weight, b16.tensor_cores, bwd) for bwd in (False, True)] == \
         ["gl_k16_fwd_tc", "gl_k16_bwd_tc"]
+    # S = 64 sets: the tensor-core layers' forward runs on tcgen05 when the plan asks for it
+    assert not f32.tcgen05 and not b16.tcgen05 and not off.tcgen05
+    t5 = CoverTopK16Layer.from_envelope(w, b, plan=PhysicalPlan(b200_tcgen05="on"), **kw)
+    t5simt = CoverTopK16Layer.from_envelope(w, b, plan=PhysicalPlan(b200_tcgen05="on", b200_f32_tensor_cores="off"),
+                                            **kw)
+    assert t5.tcgen05 and not t5simt.tcgen05
+    with pytest.raises(ValueError):
+        PhysicalPlan(b200_tcgen05="auto")
     with pytest.raises(ValueError):
         PhysicalPlan(b200_f32_tensor_cores="split")
     with pytest.raises(_native.NativeLibraryError):      # no CPU fallback on this path
