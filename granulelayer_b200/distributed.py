@@ -37,6 +37,7 @@ import torch
 import torch.distributed as dist
 from torch import nn
 
+from . import octet_storage
 from .autograd import Level1Runtime, _compute_operands, _grad_buffers, act_torch, check_supported, dact_torch
 from .config import PhysicalPlan, PoolingConfig
 from .layout import SparseLayout, init_parameters
@@ -46,12 +47,6 @@ def _default_runtime(lay):
     rt = Level1Runtime(lay.layout, lay.indices, lay.cfg.levels[0], lay.plan, counts=lay.counts)
     rt.octets = lay.input_order is not None
     return rt
-
-
-def _input_index(kperm: torch.Tensor) -> torch.Tensor:
-    """[G, slots, 8] int64: the original input index placed at each position (bits 3c .. 3c+2 of kperm)."""
-    sh = torch.arange(0, 24, 3, device=kperm.device, dtype=torch.int32)
-    return ((kperm[:, :, None] >> sh) & 7).long()
 
 
 def shard_range(G: int, rank: int, world: int):
@@ -168,45 +163,24 @@ class GroupShardedLayer(nn.Module):
 
         G_l, NB = self.indices.shape[0], self.layout.blocks_per_group
         slots = NB * 8
-        dev = self.indices.device
         counts = self.counts.to(torch.int32).contiguous()
-        o = torch.empty((G_l, slots), dtype=torch.int32, device=dev)
         kp = None
         if self.order_kind == "octet":
-            kp = torch.empty((G_l, slots), dtype=torch.int32, device=dev)
-            _native.group_octets(self.indices, counts, self.layout.input_dim, NB, 0, G_l, o, kp)
+            o, kp = octet_storage.arrange(self.indices, counts, self.layout.input_dim, NB)
         else:
+            o = torch.empty((G_l, slots), dtype=torch.int32, device=self.indices.device)
             _native.group_order(self.indices, counts, self.layout.input_dim, NB, 0, G_l, 48, o)
-        ol = o.long()
-        kidx = _input_index(kp) if kp is not None else None
         for t in (self.indices, self.weight.data, self.bias.data, getattr(self.weight, "main_grad", None),
                   getattr(self.bias, "main_grad", None)):
             if t is not None:
-                per = t.numel() // (G_l * slots)
-                v = t.view(G_l, slots, per)
-                r = torch.gather(v, 1, ol[:, :, None].expand(G_l, slots, per))
-                if kidx is not None and per == 8:
-                    r = torch.gather(r, 2, kidx)
-                v.copy_(r)
+                octet_storage.apply_(t, o, kp)
         self.neuron_order = o
         self.input_order = kp
         self._rt = None
 
     def canonical(self, t: torch.Tensor) -> torch.Tensor:
         """``t`` (indices-, weight- or bias-shaped, in this shard's storage order) in slot order."""
-        if self.neuron_order is None:
-            return t
-        G_l, slots = self.neuron_order.shape
-        per = t.numel() // (G_l * slots)
-        src = t.reshape(G_l, slots, per)
-        if self.input_order is not None and per == 8:
-            rec = torch.empty_like(src)
-            rec.scatter_(2, _input_index(self.input_order.to(t.device)), src)
-            src = rec
-        ol = self.neuron_order.long().to(t.device)[:, :, None].expand(G_l, slots, per)
-        out = torch.empty_like(t)
-        out.view(G_l, slots, per).scatter_(1, ol, src)
-        return out
+        return octet_storage.canonical(t, self.neuron_order, self.input_order)
 
     def canonical_shard(self):
         """(indices, weight, bias) of this shard in slot order."""

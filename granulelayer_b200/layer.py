@@ -6,6 +6,13 @@ parameter/buffer names and shapes (``indices``, ``weight``, ``bias``),
 ``enable_main_grad``/``zero_main_grad`` and ``effective_policy``, so that
 model code and state dicts move between the two unchanged.
 
+``weight_layout="octet"`` (a B200 extension, Mode A) stores the parameters in
+octet order (``octet_storage``) once they are on a GPU, which lets the
+lane-per-neuron kernels run them without shared-memory bank conflicts.  The
+state dict stays the reference's (slot order, converted on save and load), and
+``canonical_parameters()`` returns slot-order tensors; ``layer.weight`` itself
+then holds the permuted storage.
+
 Execution is the B200 path only: Mode A (``shared_neurons=None``) and Mode B
 (``shared_neurons=C``, canonical or fragment-packed storage, with or without
 input-supergroup ``connectivity``), fp32, single-level ``mean`` or ``sum``
@@ -35,8 +42,9 @@ class SparsePoolingLayer(nn.Module):
     operator name, a level dict or a ``PoolingConfig``; ``plan`` is an
     execution-only ``PhysicalPlan``; ``seed`` and ``bias_std`` drive the
     bit-exact seeded initialisation of ``layout.init_parameters``.
-    ``backend``, ``weight_layout`` and ``workspace_budget`` are accepted for
-    compatibility.  ``connectivity`` (a ``ConnectivityPlan``, Mode B only) draws
+    ``backend`` and ``workspace_budget`` are accepted for compatibility;
+    ``weight_layout`` takes the reference's values and ``"octet"`` (Mode A:
+    octet storage, the module docstring).  ``connectivity`` (a ``ConnectivityPlan``, Mode B only) draws
     the indices from input supergroups with the reference's generator
     (supergroups.py:200-271, bit-exact) and registers its ``sg_feat``,
     ``sg_buckets`` and ``sg_plan`` buffers (layer.py:78-84); the kernels run such
@@ -56,8 +64,12 @@ class SparsePoolingLayer(nn.Module):
         mode_b = shared_neurons is not None
         if weight_layout == "auto":
             weight_layout = "packed" if (mode_b and backend != "triton") else "canonical"
-        if weight_layout not in ("packed", "canonical"):
-            raise ValueError("weight_layout must be 'auto', 'packed' or 'canonical'")
+        if weight_layout not in ("packed", "canonical", "octet"):
+            raise ValueError("weight_layout must be 'auto', 'packed', 'canonical' or 'octet'")
+        if weight_layout == "octet" and (mode_b or self.cfg.is_semantic_hierarchy):
+            raise ValueError("weight_layout='octet' is defined for single-level Mode-A layers")
+        self.octet = weight_layout == "octet"
+        self._order = self._kperm = None   # the octet arrangement, once applied
         self.layout = SparseLayout(input_dim, hidden_dim, output_dim, fan_in, shared_neurons if mode_b else 8,
                                    mode_b, packed=(weight_layout == "packed"))
         self.compute_dtype = dtype
@@ -96,7 +108,44 @@ class SparsePoolingLayer(nn.Module):
         self._rt_key = None
         self._units = None
 
+    @torch.no_grad()
+    def arrange_storage(self):
+        """Octet layouts: store the records in octet order now (a no-op for other layouts, on the CPU or when
+        already arranged).  The first forward on a GPU does this; call it earlier if optimizer state is
+        created before that forward (parameters and ``main_grad`` are permuted in place)."""
+        if not self.octet or self._order is not None or not self.indices.is_cuda:
+            return
+        from . import octet_storage
+
+        L = self.layout
+        order, kperm = octet_storage.arrange(self.indices, L.counts_tensor(self.indices.device), L.input_dim,
+                                             L.blocks_per_group)
+        for t in (self.indices, self.weight.data, self.bias.data, getattr(self.weight, "main_grad", None),
+                  getattr(self.bias, "main_grad", None)):
+            if t is not None:
+                octet_storage.apply_(t, order, kperm)
+        self._order, self._kperm = order, kperm
+        self._rt = None
+
+    def canonical_parameters(self):
+        """(indices, weight, bias) in slot order (the reference's storage), whatever the layout."""
+        from . import octet_storage
+
+        return tuple(octet_storage.canonical(t, self._order, self._kperm)
+                     for t in (self.indices, self.weight.detach(), self.bias.detach()))
+
+    def _save_to_state_dict(self, destination, prefix, keep_vars):
+        super()._save_to_state_dict(destination, prefix, keep_vars)
+        if self._order is not None:   # octet storage: checkpoints hold the reference's slot order
+            from . import octet_storage
+
+            for name in ("indices", "weight", "bias"):
+                destination[prefix + name] = octet_storage.canonical(destination[prefix + name].detach(),
+                                                                     self._order, self._kperm)
+
     def _runtime(self) -> Level1Runtime:
+        if self.octet and self._order is None and self.indices.is_cuda:
+            self.arrange_storage()
         key = (self.indices.device, self.indices.data_ptr(), id(self.plan))
         if self._rt is None or self._rt_key != key:
             check_supported(self.layout, self.cfg.levels[0], self.compute_dtype,
@@ -110,6 +159,7 @@ class SparsePoolingLayer(nn.Module):
                 self._units = units
             else:
                 self._rt = Level1Runtime(self.layout, self.indices, self.cfg.levels[0], self.plan)
+                self._rt.octets = self._order is not None
             self._rt_key = key
         self._rt.param_dtype = self.weight.dtype
         if self.connectivity is not None and not self.cfg.is_semantic_hierarchy:
@@ -127,6 +177,14 @@ class SparsePoolingLayer(nn.Module):
                 raise ValueError(f"checkpoint connectivity {got} != layer connectivity {self.connectivity}")
         if (self.connectivity is None) != (plan is None):
             raise ValueError("checkpoint and layer disagree on input-supergroup connectivity")
+        if self._order is not None:   # octet storage: back to slot order; arranged again at the next forward
+            from . import octet_storage
+
+            with torch.no_grad():
+                for t in (getattr(self.weight, "main_grad", None), getattr(self.bias, "main_grad", None)):
+                    if t is not None:
+                        t.copy_(octet_storage.canonical(t, self._order, self._kperm))
+            self._order = self._kperm = None
         super()._load_from_state_dict(state_dict, prefix, *args, **kwargs)
         self._rt = None
 

@@ -183,3 +183,43 @@ def test_octet_entry_points_reject_what_they_do_not_run():
         i2, w2, b2 = init_parameters(L2, dev, dtype=torch.float32, seed=1)
         _native.fwd_octet(big, i2, w2, b2, L2.counts_tensor(dev).to(torch.int32), pre, L2.blocks_per_group, 0, 2,
                           _native.POOL_MEAN, 1)
+
+
+def test_drop_in_layer_with_octet_layout():
+    """SparsePoolingLayer(weight_layout="octet"): the same outputs and gradients as the reference-layout layer
+    (through the octet kernels), its state dict in the reference's slot order bit for bit, and a state dict
+    loaded into it runs the loaded parameters."""
+    from granulelayer_b200 import SparsePoolingLayer
+
+    D, H, G, B = 4096, 2 * 24576 + 1003, 3, 64
+    kw = dict(shared_neurons=None, pooling="mean", dtype=torch.float32, seed=9, bias_std=0.1)
+    ref = SparsePoolingLayer(D, H, G, **kw).cuda()
+    lay = SparsePoolingLayer(D, H, G, weight_layout="octet", **kw).cuda()
+    gen = torch.Generator().manual_seed(4)
+    x = torch.randn(B, D, generator=gen).cuda()
+    dy = torch.randn(B, G, generator=gen).cuda()
+    outs = []
+    for m in (ref, lay):
+        xr = x.clone().requires_grad_(True)
+        y = m(xr)
+        y.backward(dy)
+        outs.append((y.detach(), xr.grad))
+    assert lay.last_info["forward_kernel"] == "gl_fwd_octet_f32"
+    assert lay.last_info["backward_kernel"] == "gl_bwd_octet_f32"
+    assert_close(outs[1][0], outs[0][0], what="y", **FWD)
+    assert_close(outs[1][1], outs[0][1], what="dx", **BWD)
+    from granulelayer_b200 import octet_storage
+    assert_close(octet_storage.canonical(lay.weight.grad, lay._order, lay._kperm), ref.weight.grad, what="dw", **BWD)
+    assert_close(octet_storage.canonical(lay.bias.grad, lay._order, lay._kperm), ref.bias.grad, what="db", **BWD)
+    assert not torch.equal(lay.weight.detach(), ref.weight.detach()), "the octet layer stores permuted records"
+    sd, rsd = lay.state_dict(), ref.state_dict()
+    assert sd.keys() == rsd.keys()
+    for k in rsd:
+        assert torch.equal(sd[k].cpu(), rsd[k].cpu()), f"{k}: the octet layer's checkpoint differs"
+    ci, cw, cb = lay.canonical_parameters()
+    assert torch.equal(ci, ref.indices) and torch.equal(cw, ref.weight.detach()) and torch.equal(cb, ref.bias.detach())
+    other = SparsePoolingLayer(D, H, G, **dict(kw, seed=10)).cuda()
+    lay.load_state_dict(other.state_dict())
+    y2, y3 = lay(x), other(x)
+    assert lay.last_info["forward_kernel"] == "gl_fwd_octet_f32"
+    assert_close(y2.detach(), y3.detach(), what="y after load", **FWD)
