@@ -277,15 +277,18 @@ class Level1Runtime:
         return maps
 
     def octet_kernels(self, B: int, D: int) -> bool:
-        """Whether this call runs the lane-per-neuron kernels (gl_fwd_octet_f32 / gl_bwd_octet_f32): storage
-        in octet order, Mode A, mean / sum, fp32 parameters, and two 16-byte-per-feature tiles in shared
-        memory."""
-        if not self.octets or B == 0 or self.layout.shared_indices or self.param_dtype != torch.float32:
+        """Whether this call runs the lane-per-neuron kernels (gl_fwd_octet_f32 / gl_bwd_octet_f32): every
+        non-empty call on octet storage does, since no other kernel reads its interleaved weights; a layer
+        changed after its storage was arranged (parameter dtype, pool, plan) raises instead of running
+        another kernel on that storage."""
+        if not self.octets or B == 0:
             return False
-        if self.pool not in (_native.POOL_MEAN, _native.POOL_SUM) or not self.idx.is_cuda:
-            return False
-        optin = torch.cuda.get_device_properties(self.idx.device).shared_memory_per_block_optin
-        return 32 * D + 1024 <= optin
+        from . import octet_storage
+
+        why = octet_storage.unsupported(self.layout, self.level.type, self.param_dtype, self.idx.device, self.plan)
+        if why is not None:
+            raise RuntimeError(f"octet storage cannot run this call: {why}")
+        return True
 
     def tokens(self, backward: bool) -> int:
         lib = _native.load()
@@ -542,7 +545,7 @@ class Level1Runtime:
         wabsmax = rowmax = None
         if self.fixed_point and B > 0 and not self.smooth:
             wabsmax = saved.get("wabsmax")
-            if wabsmax is None and w.dtype != torch.float32:   # bf16 storage: padding slots hold zeros
+            if wabsmax is None and (w.dtype != torch.float32 or self.octets):   # padding slots hold zeros
                 wabsmax = w.reshape(self.groups, -1).abs().amax(1).float().contiguous()
             elif wabsmax is None:
                 wabsmax = torch.empty(self.groups, device=x.device, dtype=torch.float32)

@@ -18,7 +18,9 @@
 //            of an int32 dX tile: the quarters use disjoint bank offsets and each quarter's rows distinct
 //            bank quads, so the 32 lanes of one atomic instruction hit 32 distinct banks.
 // One lane per record reads the record once per 4 (backward) or 8 (forward) tokens, keeps the gathered
-// inputs in registers and sums dW / db over its tokens without shuffles.
+// inputs in registers and sums dW / db over its tokens without shuffles.  Weights and dW use the octet
+// weight layout (oct_woff: per block of 32 records, weights 0-3 then weights 4-7), so the warp's 16-byte
+// weight loads and dW reductions cover whole sectors.
 //
 // Backward dX accumulation: int32 fixed point at one scale per token for the whole thread block (all
 // its groups), s[t] = K / (max_g |c1[t, g]| max|w|_g max|act'|), K = min(2^22, 0.9 * 2^31 / sum_g rowmax_g)
@@ -39,12 +41,19 @@ struct OctRec {
   float b;
 };
 
+// Offset (in floats) of record f's weights 0-3 in the octet weight layout: within each block of 32 records
+// (f = 32 q + j, blocks aligned since a group's slot count is a multiple of 32) the records' weights 0-3
+// come first, 16 bytes each, then their weights 4-7 at +128 floats; a warp's loads and reductions of one
+// half then cover 512 contiguous bytes.
+__device__ __forceinline__ int64_t oct_woff(int64_t f) { return (f & ~(int64_t)31) * 8 + (f & 31) * 4; }
+
 __device__ __forceinline__ OctRec oct_load(const int16_t* __restrict__ idx, const float* __restrict__ w,
                                            const float* __restrict__ bias, int64_t f) {
   OctRec r;
   r.i = __ldg(reinterpret_cast<const int4*>(idx + f * 8));
-  r.w0 = __ldg(reinterpret_cast<const float4*>(w + f * 8));
-  r.w1 = __ldg(reinterpret_cast<const float4*>(w + f * 8) + 1);
+  const float* wp = w + oct_woff(f);
+  r.w0 = __ldg(reinterpret_cast<const float4*>(wp));
+  r.w1 = __ldg(reinterpret_cast<const float4*>(wp + 128));
   r.b = __ldg(bias + f);
   return r;
 }
@@ -295,8 +304,9 @@ __global__ void __launch_bounds__(kOctThreads, 1) bwd_octet_kernel(const OctBwdP
       const float gb_ = (dz[0] + dz[1]) + (dz[2] + dz[3]);
       if (dz[0] != 0.f || dz[1] != 0.f || dz[2] != 0.f || dz[3] != 0.f) {
         const int64_t f = fbase + n;
-        red_add4(p.dw + f * 8, gw[0], gw[1], gw[2], gw[3]);
-        red_add4(p.dw + f * 8 + 4, gw[4], gw[5], gw[6], gw[7]);
+        float* dwp = p.dw + oct_woff(f);
+        red_add4(dwp, gw[0], gw[1], gw[2], gw[3]);
+        red_add4(dwp + 128, gw[4], gw[5], gw[6], gw[7]);
         red_add(p.db + f, gb_);
       }
       cur = nxt;

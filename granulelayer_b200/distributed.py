@@ -22,8 +22,11 @@ within each group the records are permuted so that every 8 consecutive records (
 residues d mod 8 of their inputs evenly, and each record's 8 (index, weight) pairs are permuted so that at
 every input position the octet's records read 8 distinct residues; the lane-per-neuron kernels
 (``gl_fwd_octet_f32`` / ``gl_bwd_octet_f32``) then gather and scatter without shared-memory bank
-conflicts.  ``neuron_order="bank"`` keeps the earlier bank-aware processing order of ``gl_group_order``
-(unit 48, neurons only) with the generic kernels, ``"slot"`` the reference's order.  The permutations are
+conflicts.  Octet storage also interleaves each 32-record block's weights (``octet_storage``), which only
+those kernels read, so a shard they cannot run (``octet_storage.unsupported``: e.g. an input_dim too wide
+for their shared-memory tiles) gets the bank-aware order instead.  ``neuron_order="bank"`` keeps the
+earlier bank-aware processing order of ``gl_group_order`` (unit 48, neurons only) with the generic
+kernels, ``"slot"`` the reference's order.  The permutations are
 within groups and within records, so pooled outputs and dX are unchanged; ``neuron_order[g][p]`` is the
 slot stored at position p, ``input_order[g][p]`` (octet order) the record's input permutation (bits
 3c .. 3c+2: the original input placed at position c), and ``canonical`` / ``canonical_shard`` return
@@ -165,7 +168,8 @@ class GroupShardedLayer(nn.Module):
         slots = NB * 8
         counts = self.counts.to(torch.int32).contiguous()
         kp = None
-        if self.order_kind == "octet":
+        if self.order_kind == "octet" and octet_storage.unsupported(
+                self.layout, self.cfg.levels[0].type, self.weight.dtype, self.indices.device, self.plan) is None:
             o, kp = octet_storage.arrange(self.indices, counts, self.layout.input_dim, NB)
         else:
             o = torch.empty((G_l, slots), dtype=torch.int32, device=self.indices.device)

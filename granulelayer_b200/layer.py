@@ -7,8 +7,9 @@ parameter/buffer names and shapes (``indices``, ``weight``, ``bias``),
 model code and state dicts move between the two unchanged.
 
 ``weight_layout="octet"`` (a B200 extension, Mode A) stores the parameters in
-octet order (``octet_storage``) once they are on a GPU, which lets the
-lane-per-neuron kernels run them without shared-memory bank conflicts.  The
+octet order (``octet_storage``) once they are on a GPU and the lane-per-neuron
+kernels can run the layer (``octet_storage.unsupported``), which lets those
+kernels run it without shared-memory bank conflicts.  The
 state dict stays the reference's (slot order, converted on save and load), and
 ``canonical_parameters()`` returns slot-order tensors; ``layer.weight`` itself
 then holds the permuted storage.
@@ -110,12 +111,18 @@ class SparsePoolingLayer(nn.Module):
 
     @torch.no_grad()
     def arrange_storage(self):
-        """Octet layouts: store the records in octet order now (a no-op for other layouts, on the CPU or when
-        already arranged).  The first forward on a GPU does this; call it earlier if optimizer state is
-        created before that forward (parameters and ``main_grad`` are permuted in place)."""
+        """Octet layouts: store the records in octet order now (a no-op for other layouts, on the CPU, when
+        already arranged, or when the lane-per-neuron kernels cannot run the layer: ``octet_storage.
+        unsupported`` says why, and the layer then keeps slot order).  The first forward on a GPU does
+        this; call it earlier if optimizer state is created before that forward (parameters and
+        ``main_grad`` are permuted in place)."""
         if not self.octet or self._order is not None or not self.indices.is_cuda:
             return
         from . import octet_storage
+
+        if octet_storage.unsupported(self.layout, self.cfg.levels[0].type, self.weight.dtype, self.indices.device,
+                                     self.plan) is not None:
+            return
 
         L = self.layout
         order, kperm = octet_storage.arrange(self.indices, L.counts_tensor(self.indices.device), L.input_dim,

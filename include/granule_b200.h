@@ -247,7 +247,10 @@ int gl_group_octets(const int16_t* idx, const int32_t* counts, int64_t D, int64_
  * the block's rowmax)), so D <= (shared memory per block - 1 KiB) / 32 (7,232 on B200; GL_ERR_SMEM beyond).
  * `tokens` must be 0 (or 8 / 4); order, locality, winners and stat must be NULL; other pools and bf16
  * storage return GL_ERR_UNSUPPORTED.  dx, dw, db are accumulated as in gl_bwd_f32; the forward writes pre
- * (and wabsmax when given) as gl_fwd_f32 does. */
+ * (and wabsmax when given) as gl_fwd_f32 does.  w and dw use the octet weight layout: within a group, each
+ * block of 32 consecutive records (slot counts are multiples of 32) stores the records' weights 0-3 (16
+ * bytes each, record j at byte 16 j) and then their weights 4-7 (at byte 512 + 16 j); idx and b keep the
+ * record layout. */
 int gl_fwd_octet_f32(const GlFwdArgs* args, void* stream);
 int gl_bwd_octet_f32(const GlBwdArgs* args, void* stream);
 

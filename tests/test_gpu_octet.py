@@ -61,6 +61,13 @@ def _apply(t, order, kp):
     return v.reshape(t.shape)
 
 
+def _interleave(t):
+    """Weights / dW in the octet weight layout the kernels read: per block of 32 records, the records'
+    weights 0-3 (16 bytes each), then their weights 4-7."""
+    G = t.shape[0]
+    return t.reshape(G, -1, 32, 2, 4).transpose(2, 3).reshape(t.shape).contiguous()
+
+
 @pytest.mark.parametrize("rule", ["distinct", "uniform"])
 def test_octet_arrangement_is_valid_deterministic_and_balanced(rule):
     D, G = 4096, 3
@@ -141,6 +148,7 @@ def test_octet_kernels_match_oracle(D, H, G, B, pool, act, arranged):
         idx, w, b = _apply(idx, order, kp), _apply(w, order, kp), _apply(b, order, kp)
         odw, sdw = _apply(odw, order, kp), _apply(sdw, order, kp)
         odb, sdb = _apply(odb, order, kp), _apply(sdb, order, kp)
+    w, odw, sdw = _interleave(w), _interleave(odw), _interleave(sdw)
     y, dx, dw, db = _run(L, idx, w, b, x, dy, pool, act)
     assert_close(y, pre, what="y", **FWD)
     assert_close(dx, odx, what="dx", slack=sdx, **BWD)
@@ -223,3 +231,20 @@ def test_drop_in_layer_with_octet_layout():
     y2, y3 = lay(x), other(x)
     assert lay.last_info["forward_kernel"] == "gl_fwd_octet_f32"
     assert_close(y2.detach(), y3.detach(), what="y after load", **FWD)
+
+
+@pytest.mark.parametrize("D,pool,accum", [(8000, "mean", "auto"), (256, "max", "auto"), (256, "mean", "fp32")])
+def test_octet_layout_keeps_slot_order_where_its_kernels_do_not_run(D, pool, accum):
+    """An octet layer that the lane-per-neuron kernels cannot run (input too wide for their tiles, a pool
+    other than mean / sum, fp32 dX atomics asked for) keeps the reference's storage and the generic kernels."""
+    from granulelayer_b200 import PhysicalPlan, SparsePoolingLayer
+
+    kw = dict(shared_neurons=None, pooling=pool, dtype=torch.float32, seed=2, bias_std=0.1,
+              plan=PhysicalPlan(b200_dx_accum=accum))
+    ref = SparsePoolingLayer(D, 4096, 4, **kw).cuda()
+    lay = SparsePoolingLayer(D, 4096, 4, weight_layout="octet", **kw).cuda()
+    x = torch.randn(8, D, device="cuda")
+    y, yr = lay(x), ref(x)
+    assert lay._order is None and torch.equal(lay.weight.detach(), ref.weight.detach())
+    assert lay.last_info.get("forward_kernel") != "gl_fwd_octet_f32"
+    assert_close(y.detach(), yr.detach(), what="y", **FWD)
