@@ -84,7 +84,7 @@ FALLBACK_HBM_GBS = 6650.0
 # BWD_PROFILE (512 x 24,576 neurons); the traffic grows with the neuron count, so a full launch is
 # this figure times N.
 BWD_PROFILE = "profiles/octet_kernels_g512.md"
-BWD_DRAM_BYTES_PER_NEURON = 1.874112e9 / (512 * 24576)
+BWD_DRAM_BYTES_PER_NEURON = (1.318228e9 + 0.513619e9) / (512 * 24576)
 
 
 def param_bytes(n):
