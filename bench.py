@@ -525,7 +525,7 @@ def bench_cover16(args, world):
     w64, b64 = init_envelope_parameters(KLayout(Dc, Hc, Gc, 64, 256), dev, dtype=torch.bfloat16, seed=3)
     pdt = torch.bfloat16 if args.cover_dtype == "bf16" else torch.float32
     plan = PhysicalPlan(grad_precision="split", b200_f32_tensor_cores="off" if args.cover_kernels == "simt" else "auto",
-                        b200_tcgen05="on" if args.cover_kernels == "t5" else "off")
+                        b200_tcgen05={"t5": "on", "t5fwd": "fwd", "t5bwd": "bwd"}.get(args.cover_kernels, "off"))
     lay = CoverTopK16Layer.from_envelope(w64, b64, input_dim=Dc, hidden_dim=Hc, output_dim=Gc,
                                          connectivity=ConnectivityPlan(64, 64, seed=3), device=dev, dtype=pdt,
                                          plan=plan)
@@ -538,7 +538,7 @@ def bench_cover16(args, world):
     dy = torch.randn(Bc, Gc, device=dev, generator=gen)
 
     ev = {"fwd": [], "bwd": []}
-    orig = {"fwd": _native.k16_fwd, "fwd_t5": _native.k16_fwd_t5, "bwd": _native.k16_bwd}
+    orig = {"fwd": _native.k16_fwd, "fwd_t5": _native.k16_fwd_t5, "bwd": _native.k16_bwd, "bwd_t5": _native.k16_bwd_t5}
 
     def timed(name, slot):
         def wrap(*a, **k):
@@ -558,7 +558,8 @@ def bench_cover16(args, world):
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize(dev)
-    _native.k16_fwd, _native.k16_fwd_t5, _native.k16_bwd = timed("fwd", "fwd"), timed("fwd_t5", "fwd"), timed("bwd", "bwd")
+    _native.k16_fwd, _native.k16_fwd_t5 = timed("fwd", "fwd"), timed("fwd_t5", "fwd")
+    _native.k16_bwd, _native.k16_bwd_t5 = timed("bwd", "bwd"), timed("bwd_t5", "bwd")
     n0 = _native.launch_count()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     try:
@@ -569,7 +570,8 @@ def bench_cover16(args, world):
             end.record()
             torch.cuda.synchronize(dev)
     finally:
-        _native.k16_fwd, _native.k16_fwd_t5, _native.k16_bwd = orig["fwd"], orig["fwd_t5"], orig["bwd"]
+        _native.k16_fwd, _native.k16_fwd_t5 = orig["fwd"], orig["fwd_t5"]
+        _native.k16_bwd, _native.k16_bwd_t5 = orig["bwd"], orig["bwd_t5"]
     launches = _native.launch_count() - n0
     ms = start.elapsed_time(end) / args.steps
     fwd_ms = statistics.mean(s.elapsed_time(e) for s, e in ev["fwd"])
@@ -621,7 +623,9 @@ def bench_cover16(args, world):
         tc_peak, tc_kind = peak_bf16()
         roof = {"bound": "tensor", "kernel": bkern, "achieved": mma_flop / (bwd_ms * 1e-3) / 1e12, "peak": tc_peak,
                 "unit": "TFLOP/s", "frac": mma_flop / (bwd_ms * 1e-3) / 1e12 / tc_peak,
-                "peak_source": f"{tc_kind} dense bf16 (cuBLAS, burst) -- these are mma.sync tiles",
+                "peak_source": f"{tc_kind} dense bf16 (cuBLAS, burst) -- " + (
+                    "tcgen05 MMAs over each set's 64 positions: they execute 4x these flops (a record reads 16)"
+                    if "t5" in (bkern or "") else "these are mma.sync tiles"),
                 "algorithmic_flop_per_launch": mma_flop, "flop_definition": "bf16 MMA flops of the term products",
                 "fp32_equivalent_tflops": achieved,
                 # mma.sync bf16 -> fp32 peaks at 2048 flop / clk / SM (ncu peak_sustained), a quarter of tcgen05
@@ -1021,9 +1025,9 @@ def main():
                     help="--impl reference-gpu --workload modeb: the reference layer's parameter dtype")
     ap.add_argument("--cover-dtype", default="fp32", choices=["fp32", "bf16"],
                     help="cover16: parameter storage (fp32 = config 4; bf16 = the reference's, on the tensor cores)")
-    ap.add_argument("--cover-kernels", default="tc", choices=["tc", "t5", "simt"],
-                    help="cover16: mma.sync tensor-core kernels (default); t5 = the forward on tcgen05 (TMEM); "
-                         "simt = the fp32 SIMT kernels (fp32 parameters)")
+    ap.add_argument("--cover-kernels", default="tc", choices=["tc", "t5", "t5fwd", "t5bwd", "simt"],
+                    help="cover16: mma.sync tensor-core kernels (default); t5 = forward and backward on tcgen05 "
+                         "(TMEM), t5fwd / t5bwd = one of them; simt = the fp32 SIMT kernels (fp32 parameters)")
     ap.add_argument("--cover-outputs", type=int, default=2048,
                     help="cover16: outputs of 24,576 neurons (default 2048 = config 4; fewer for ncu captures)")
     ap.add_argument("--groups", type=int, default=G,

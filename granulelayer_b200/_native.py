@@ -16,7 +16,7 @@ from pathlib import Path
 
 import torch
 
-ABI_VERSION = 15
+ABI_VERSION = 16
 LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libgranule_b200.so"
 
 POOL_MEAN, POOL_SUM, POOL_MAX, POOL_LME, POOL_POWER, POOL_SOFTMAX, POOL_TOPK = 0, 1, 2, 3, 4, 5, 6
@@ -43,7 +43,7 @@ EXPORTS = ("gl_abi_version", "gl_status_string", "gl_last_cuda_error", "gl_fwd_f
            "gl_shared_auto_tokens", "gl_bwd_shared_det_f32", "gl_bwd_shared_det_static_f32", "gl_k16_fwd_f32",
            "gl_k16_bwd_f32", "gl_k16_auto_tokens", "gl_k16_fwd_tc", "gl_k16_bwd_tc", "gl_k16_fwd_tc_f32",
            "gl_k16_bwd_tc_f32", "gl_struct_layout", "gl_struct_fields", "gl_group_octets", "gl_fwd_octet_f32",
-           "gl_bwd_octet_f32", "gl_k16_fwd_t5", "gl_k16_fwd_t5_f32")
+           "gl_bwd_octet_f32", "gl_k16_fwd_t5", "gl_k16_fwd_t5_f32", "gl_k16_bwd_t5", "gl_k16_bwd_t5_f32")
 
 
 class GlSetArgs(ctypes.Structure):
@@ -216,7 +216,7 @@ def load(path=None) -> ctypes.CDLL:
         lib.gl_bwd_shared_tc_sets.restype = ctypes.c_int
         lib.gl_fwd_shared_tc_sets.argtypes = [ctypes.POINTER(GlSharedArgs), ctypes.POINTER(GlSetArgs), ctypes.c_void_p]
         lib.gl_fwd_shared_tc_sets.restype = ctypes.c_int
-        for name in ("gl_k16_fwd_t5", "gl_k16_fwd_t5_f32"):
+        for name in ("gl_k16_fwd_t5", "gl_k16_fwd_t5_f32", "gl_k16_bwd_t5", "gl_k16_bwd_t5_f32"):
             getattr(lib, name).argtypes = [ctypes.POINTER(GlK16Args), ctypes.c_void_p, ctypes.c_void_p]
             getattr(lib, name).restype = ctypes.c_int
         lib.gl_k16_auto_tokens.restype = ctypes.c_int
@@ -623,6 +623,21 @@ def k16_fwd_t5(x, sched: dict, w, b, counts, pre, NB16: int, act: int = 1, statu
     a = _k16_args(x, sched, w, b, counts, NB16, act, 0)
     a.pre, a.ldp = _ptr(pre), pre.stride(0)
     name = "gl_k16_fwd_t5" if w.dtype == torch.bfloat16 else "gl_k16_fwd_t5_f32"
+    with torch.cuda.device(x.device):
+        _check(lib, getattr(lib, name)(ctypes.byref(a), _ptr(status), _stream(x.device)), name)
+    return name
+
+
+def k16_bwd_t5(x, sched: dict, w, b, counts, c1t, dx, dw, db, NB16: int, act: int = 1, status=None) -> str:
+    """dx, dw, db += the K16/C16 layer's gradients for coefficients c1t [G, B] on the tcgen05 tensor cores
+    (gl_k16_bwd_t5 for bf16 parameters, gl_k16_bwd_t5_f32 for fp32 ones, three-term splits); dX is summed in
+    fp32 in the tensor memory (no fixed-point bounds).  ``status`` as k16_fwd_t5.  Returns the entry's name."""
+    _require_cuda(x, w, b, counts, c1t, dx, dw, db, status, *sched.values())
+    lib = load()
+    a = _k16_args(x, sched, w, b, counts, NB16, act, 0)
+    a.c1t, a.dx, a.dw, a.db = _ptr(c1t), _ptr(dx), _ptr(dw), _ptr(db)
+    a.ldc, a.lddx = c1t.stride(0), dx.stride(0)
+    name = "gl_k16_bwd_t5" if w.dtype == torch.bfloat16 else "gl_k16_bwd_t5_f32"
     with torch.cuda.device(x.device):
         _check(lib, getattr(lib, name)(ctypes.byref(a), _ptr(status), _stream(x.device)), name)
     return name

@@ -272,8 +272,8 @@ class PhysicalPlan:
     # fp32 Cover-TopK16 layers: "auto" = the tensor-core kernels on three-term bf16 splits of x, w and dz
     # (gl_k16_*_tc_f32, fp32-level results); "off" = the fp32 SIMT kernels (gl_k16_*_f32)
     b200_f32_tensor_cores: str = "auto"
-    # Cover-TopK16 layers on the tensor cores with S = 64 sets: "on" = the forward on tcgen05 with TMEM
-    # accumulators (gl_k16_fwd_t5*); "off" (default, measured faster) = the mma.sync kernels
+    # Cover-TopK16 layers on the tensor cores with S = 64 sets: which passes run on tcgen05 with TMEM
+    # accumulators (gl_k16_fwd_t5* / gl_k16_bwd_t5*): "on" (both), "fwd", "bwd", or "off" (the mma.sync kernels)
     b200_tcgen05: str = "off"
 
     def __post_init__(self):
@@ -305,8 +305,8 @@ class PhysicalPlan:
             raise ValueError("b200_bf16_tensor_cores must be 'auto' or 'off'")
         if self.b200_f32_tensor_cores not in ("auto", "off"):
             raise ValueError("b200_f32_tensor_cores must be 'auto' or 'off'")
-        if self.b200_tcgen05 not in ("on", "off"):
-            raise ValueError("b200_tcgen05 must be 'on' or 'off'")
+        if self.b200_tcgen05 not in ("on", "off", "fwd", "bwd"):
+            raise ValueError("b200_tcgen05 must be 'on', 'off', 'fwd' or 'bwd'")
 
 
 def resolve_reduction(plan: PhysicalPlan):

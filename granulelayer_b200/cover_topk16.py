@@ -93,6 +93,14 @@ class _K16Function(torch.autograd.Function):
         dw = mg_w if use_main else torch.zeros(w.shape, device=w.device, dtype=torch.float32)
         db = mg_b if use_main else torch.zeros(b.shape, device=b.device, dtype=torch.float32)
         dx = torch.zeros_like(xc)
+        if layer.tcgen05_bwd:
+            name = _native.k16_bwd_t5(xc, layer._work(), w, b, layer.counts, c1t, dx, dw, db,
+                                      layer.layout.blocks_per_group)
+            layer.last_info["dx_accumulation"] = "fp32 in tensor memory"
+            layer.last_info.update(backward_backend="b200-k16", backward_kernel=name)
+            gw = None if use_main else dw.to(w.dtype)
+            gb = None if use_main else db.to(b.dtype)
+            return dx.to(x.dtype), gw, gb, None
         wabsmax = rowmax = None
         tc = layer.tensor_cores
         if tc and layer.plan.b200_dx_accum in ("auto", "fixed"):
@@ -325,9 +333,15 @@ class CoverTopK16Layer(nn.Module):
     @property
     def tcgen05(self) -> bool:
         """Whether the forward runs on the tcgen05 tensor cores (gl_k16_fwd_t5 / gl_k16_fwd_t5_f32): tensor-core
-        layers whose input sets have S = 64 positions, when ``plan.b200_tcgen05 == "on"`` (off by default: the
-        mma.sync forward is faster at config 4)."""
-        return self.tensor_cores and self.plan.b200_tcgen05 == "on" and int(self.sg_feat.shape[1]) == 64
+        layers whose input sets have S = 64 positions, when ``plan.b200_tcgen05`` is "on" or "fwd" (off by
+        default: the mma.sync forward is faster at config 4)."""
+        return self.tensor_cores and self.plan.b200_tcgen05 in ("on", "fwd") and int(self.sg_feat.shape[1]) == 64
+
+    @property
+    def tcgen05_bwd(self) -> bool:
+        """Whether the backward runs on the tcgen05 tensor cores (gl_k16_bwd_t5 / gl_k16_bwd_t5_f32): as
+        ``tcgen05``, for ``plan.b200_tcgen05`` "on" or "bwd"."""
+        return self.tensor_cores and self.plan.b200_tcgen05 in ("on", "bwd") and int(self.sg_feat.shape[1]) == 64
 
     def enable_main_grad(self):
         for p in (self.weight, self.bias):

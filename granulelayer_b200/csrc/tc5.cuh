@@ -111,4 +111,16 @@ __device__ __forceinline__ void t5_ld32(uint32_t taddr, float (&v)[32]) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// One fp32 column of this warp's 32 TMEM lanes (load and completion wait in one statement, as t5_ld32).
+__device__ __forceinline__ float t5_ld1(uint32_t taddr) {
+  uint32_t r;
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r)
+      : "r"(taddr)
+      : "memory");
+  return __uint_as_float(r);
+}
+
 }  // namespace gl

@@ -44,7 +44,7 @@
 extern "C" {
 #endif
 
-#define GL_ABI_VERSION 15
+#define GL_ABI_VERSION 16
 
 typedef enum GlStatus {
   GL_OK = 0,
@@ -470,6 +470,15 @@ int gl_k16_bwd_tc_f32(const GlK16Args* args, const float* wabsmax, const int32_t
  * to 1 if a wait for the tensor cores exceeded its iteration limit (the results are then incomplete). */
 int gl_k16_fwd_t5(const GlK16Args* args, int32_t* status, void* stream);
 int gl_k16_fwd_t5_f32(const GlK16Args* args, int32_t* status, void* stream);
+/* The backward on tcgen05 (replaces the reference's kgen K = 16 backward, experimental/kgen/kgen.cuh:202-536;
+ * same arguments, layouts and accumulation into dx, dw, db as gl_k16_bwd_tc / gl_k16_bwd_tc_f32, S = 64,
+ * distinct positions per record, `tokens` 0 or 128).  dX is summed for each input set in the tensor
+ * memory in fp32 (no fixed-point bounds) and added to dx once per set and 128 tokens; dW = dz^T X and
+ * db = dz^T 1 are products of the tensor cores as well.  bf16 parameters
+ * (gl_k16_bwd_t5): x and w one bf16 term, dz two (hi + lo, the reference's split precision); fp32 ones
+ * (gl_k16_bwd_t5_f32): three terms each.  `status` as gl_k16_fwd_t5. */
+int gl_k16_bwd_t5(const GlK16Args* args, int32_t* status, void* stream);
+int gl_k16_bwd_t5_f32(const GlK16Args* args, int32_t* status, void* stream);
 
 /* Layout of the argument structs, for bindings that declare them field by field (replaces the
  * reference's sp_struct_layout, sparse_pooling/kernels/cuda/abi.cu:25, which its ctypes bridge checks

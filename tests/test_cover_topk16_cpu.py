@@ -122,6 +122,10 @@ def test_kernel_family_follows_dtype_and_plan():
     t5simt = CoverTopK16Layer.from_envelope(w, b, plan=PhysicalPlan(b200_tcgen05="on", b200_f32_tensor_cores="off"),
                                             **kw)
     assert t5.tcgen05 and not t5simt.tcgen05
+    assert t5.tcgen05_bwd and not t5simt.tcgen05_bwd and not f32.tcgen05_bwd
+    fwd_only = CoverTopK16Layer.from_envelope(w, b, plan=PhysicalPlan(b200_tcgen05="fwd"), **kw)
+    bwd_only = CoverTopK16Layer.from_envelope(w, b, plan=PhysicalPlan(b200_tcgen05="bwd"), **kw)
+    assert (fwd_only.tcgen05, fwd_only.tcgen05_bwd, bwd_only.tcgen05, bwd_only.tcgen05_bwd) == (True, False, False, True)
     with pytest.raises(ValueError):
         PhysicalPlan(b200_tcgen05="auto")
     with pytest.raises(ValueError):
