@@ -53,11 +53,20 @@ __device__ __forceinline__ void t5_tmem_dealloc(uint32_t taddr, uint32_t ncols) 
 // D (TMEM) = A * B (+ D when accumulate != 0), A and B described in shared memory.  One thread issues.
 __device__ __forceinline__ void t5_mma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                             uint32_t accumulate) {
-  const uint32_t z = 0;
   asm volatile(
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(z), "r"(z), "r"(z), "r"(z));
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+
+// D (TMEM) = A * B (+ D), A read from TMEM (rows = the 128 lanes; column c of the A address holds K elements
+// 2c and 2c + 1, the even one in the low half), B described in shared memory.  One thread issues.
+__device__ __forceinline__ void t5_mma_bf16_ta(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                               uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate));
 }
 
 // Arrive on the mbarrier once every MMA this thread issued before has completed.
@@ -111,6 +120,19 @@ __device__ __forceinline__ void t5_ld32(uint32_t taddr, float (&v)[32]) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// 16 consecutive 32-bit columns of this warp's 32 TMEM lanes from registers (lane i of the warp writes lane
+// base + i); completion is awaited with t5_wait_st.
+__device__ __forceinline__ void t5_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+
+__device__ __forceinline__ void t5_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
 // One fp32 column of this warp's 32 TMEM lanes (load and completion wait in one statement, as t5_ld32).
 __device__ __forceinline__ float t5_ld1(uint32_t taddr) {
   uint32_t r;
@@ -121,6 +143,37 @@ __device__ __forceinline__ float t5_ld1(uint32_t taddr) {
       : "r"(taddr)
       : "memory");
   return __uint_as_float(r);
+}
+
+// 16 fp32 values of this warp's 32 TMEM lanes at 16 columns given by address (taddr[i] = lanes | column),
+// with one completion wait for all of them.
+__device__ __forceinline__ void t5_ld16_cols(const uint32_t (&a)[16], float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%16];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x1.b32 {%1}, [%17];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x1.b32 {%2}, [%18];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x1.b32 {%3}, [%19];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x1.b32 {%4}, [%20];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x1.b32 {%5}, [%21];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x1.b32 {%6}, [%22];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x1.b32 {%7}, [%23];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x1.b32 {%8}, [%24];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x1.b32 {%9}, [%25];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x1.b32 {%10}, [%26];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x1.b32 {%11}, [%27];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x1.b32 {%12}, [%28];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x1.b32 {%13}, [%29];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x1.b32 {%14}, [%30];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x1.b32 {%15}, [%31];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(a[4]), "r"(a[5]), "r"(a[6]), "r"(a[7]), "r"(a[8]),
+        "r"(a[9]), "r"(a[10]), "r"(a[11]), "r"(a[12]), "r"(a[13]), "r"(a[14]), "r"(a[15])
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
 }  // namespace gl
