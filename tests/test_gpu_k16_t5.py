@@ -160,3 +160,32 @@ def test_t5_backward_config4_slice(dtype):
     lay = _layer(4096, 6 * 24576, 6, 64, dtype, seed=3)
     gen = torch.Generator().manual_seed(4)
     _check_backward(lay, torch.randn(512, 4096, generator=gen), torch.randn(512, 6, generator=gen))
+
+
+@pytest.mark.parametrize("mode", ["bwd", "on"])
+def test_t5_layer_routing_through_autograd(mode):
+    """PhysicalPlan(b200_tcgen05="bwd" | "on") routes the fp32 layer's autograd backward (and, for "on", its
+    forward) to the tcgen05 entries; outputs and gradients match the float64 oracle."""
+    from granulelayer_b200.config import PhysicalPlan
+
+    D, H, G, R, B = 512, 20000, 16, 16, 200
+    w, b = init_envelope_parameters(KLayout(D, H, G, 64, 256), "cuda", dtype=torch.bfloat16, seed=6, bias_std=0.1)
+    lay = CoverTopK16Layer.from_envelope(w, b, input_dim=D, hidden_dim=H, output_dim=G,
+                                         connectivity=ConnectivityPlan(64, R, seed=9), device="cuda",
+                                         plan=PhysicalPlan(grad_precision="split", b200_tcgen05=mode))
+    gen = torch.Generator().manual_seed(2)
+    x, gy = torch.randn(B, D, generator=gen), torch.randn(B, G, generator=gen)
+    xg = x.cuda().requires_grad_(True)
+    y = lay(xg)
+    y.backward(gy.cuda())
+    assert lay.last_info["backward_kernel"] == "gl_k16_bwd_t5_f32"
+    assert lay.last_info["forward_kernel"] == ("gl_k16_fwd_t5_f32" if mode == "on" else "gl_k16_fwd_tc_f32")
+    assert lay.last_info["dx_accumulation"] == "fp32 in tensor memory"
+    ry, rdx, rdw, rdb, (sdx, sdw, sdb) = kc_oracle.grads(
+        x.double().numpy(), lay.indices.cpu().numpy(), lay.weight.detach().double().cpu().numpy(),
+        lay.bias.detach().double().cpu().numpy(), lay.counts.cpu().numpy(), gy.double().numpy(), act="relu",
+        slack=True)
+    assert_close(y.detach(), ry, what="y", **FWD_TOL)
+    assert_close(xg.grad, rdx, what="dx", slack=sdx, **GRAD_TOL)
+    assert_close(lay.weight.grad, rdw, what="dw", slack=sdw, **GRAD_TOL)
+    assert_close(lay.bias.grad, rdb, what="db", slack=sdb, **GRAD_TOL)
