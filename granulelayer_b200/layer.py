@@ -134,12 +134,17 @@ class SparsePoolingLayer(nn.Module):
         self._order, self._kperm = order, kperm
         self._rt = None
 
-    def canonical_parameters(self):
-        """(indices, weight, bias) in slot order (the reference's storage), whatever the layout."""
+    def canonical(self, t: torch.Tensor) -> torch.Tensor:
+        """An index-, weight- or bias-shaped tensor of this layer's storage (a parameter, its gradient,
+        ``main_grad`` or an optimizer moment) in slot order, the reference's storage; ``t`` itself when the
+        layer stores slot order."""
         from . import octet_storage
 
-        return tuple(octet_storage.canonical(t, self._order, self._kperm)
-                     for t in (self.indices, self.weight.detach(), self.bias.detach()))
+        return octet_storage.canonical(t, self._order, self._kperm)
+
+    def canonical_parameters(self):
+        """(indices, weight, bias) in slot order (the reference's storage), whatever the layout."""
+        return tuple(self.canonical(t) for t in (self.indices, self.weight.detach(), self.bias.detach()))
 
     def _save_to_state_dict(self, destination, prefix, keep_vars):
         super()._save_to_state_dict(destination, prefix, keep_vars)

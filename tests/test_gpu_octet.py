@@ -216,9 +216,8 @@ def test_drop_in_layer_with_octet_layout():
     assert lay.last_info["backward_kernel"] == "gl_bwd_octet_f32"
     assert_close(outs[1][0], outs[0][0], what="y", **FWD)
     assert_close(outs[1][1], outs[0][1], what="dx", **BWD)
-    from granulelayer_b200 import octet_storage
-    assert_close(octet_storage.canonical(lay.weight.grad, lay._order, lay._kperm), ref.weight.grad, what="dw", **BWD)
-    assert_close(octet_storage.canonical(lay.bias.grad, lay._order, lay._kperm), ref.bias.grad, what="db", **BWD)
+    assert_close(lay.canonical(lay.weight.grad), ref.weight.grad, what="dw", **BWD)
+    assert_close(lay.canonical(lay.bias.grad), ref.bias.grad, what="db", **BWD)
     assert not torch.equal(lay.weight.detach(), ref.weight.detach()), "the octet layer stores permuted records"
     sd, rsd = lay.state_dict(), ref.state_dict()
     assert sd.keys() == rsd.keys()
