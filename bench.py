@@ -27,7 +27,8 @@ a bounded slice of the same workload on the host cores (rank 0, N = 1).
 G = 2048 outputs, S = 64, R = 64, batch 512, seed 3): forward + backward through the layer on
 1 GPU, with the forward and backward (dX-carrying) kernels timed separately.  fp32 parameters run
 the tensor-core kernels on three-term bf16 splits by default (``--cover-kernels simt``: the fp32
-SIMT kernels); ``--cover-dtype bf16`` stores bf16 parameters (the reference's arithmetic).
+SIMT kernels; ``t5`` / ``t5fwd`` / ``t5bwd``: the forward and / or backward on tcgen05 with TMEM
+accumulators); ``--cover-dtype bf16`` stores bf16 parameters (the reference's arithmetic).
 
 ``--workload fwdbwd256`` times BASELINE config 2: the same 100M-neuron layer (seed 1, bias_std 0.1)
 forward + backward at batch 256 through the layer API (no optimizer), forward and backward
