@@ -76,6 +76,32 @@ import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
 D, N, G, B = 4096, 100_663_296, 4096, 1024
+INDEX_RULE = "distinct"   # --index-rule: "distinct" (the reference's init) or "uniform" (configs 2 / 3 as written)
+INDEX_RULES = {"distinct": "int16, distinct sorted per neuron (reference init rule)",
+               "uniform": "int16 storage of the configs' uniform int32 rule: every index uniform in [0, D) with "
+                          "replacement (D = 4096 fits int16)"}
+
+
+@torch.no_grad()
+def uniform_indices_(idx, seed):
+    """Overwrite a Mode-A index tensor [G, NB, 8, 8] with BASELINE configs 2 / 3's rule as written: every index
+    uniform in [0, D) with replacement, from a seeded generator on the tensor's device."""
+    gen = torch.Generator(device=idx.device).manual_seed(seed)
+    idx.copy_(torch.randint(0, D, idx.shape, generator=gen, device=idx.device).to(torch.int16))
+
+
+def shard_layer(D_, N_, G_, dev, seed, bias_std=0.1, group=None):
+    """The benchmarked GroupShardedLayer with the --index-rule's indices, in octet storage."""
+    from granulelayer_b200.distributed import GroupShardedLayer
+
+    if INDEX_RULE == "distinct":
+        return GroupShardedLayer(D_, N_, G_, pooling="mean", device=dev, seed=seed, bias_std=bias_std, group=group)
+    lay = GroupShardedLayer(D_, N_, G_, pooling="mean", device=dev, seed=seed, bias_std=bias_std, group=group,
+                            neuron_order="slot")
+    uniform_indices_(lay.indices, 1000 + seed + lay.rank)
+    lay.order_kind = "octet"
+    lay.reorder_neurons()
+    return lay
 K_FAN = 8
 IDX_BYTES = 2
 METRIC = "neuron-samples/s fwd+bwd+opt @100M fan-in-8, B=1024; % HBM roofline; 1/2/4/8 GPU"
@@ -117,7 +143,7 @@ def config_dict(world):
     return {"workload": "100M-neuron fan-in-8 Mode-A fp32 mean-ReLU layer: fwd+bwd+fused Adam step "
                         "(D=4096, N=100,663,296, G=4096 groups of 24,576, B=1024)",
             "D": D, "N": N, "G": G, "global_batch": B, "fan_in": K_FAN, "pool": "mean", "activation": "relu",
-            "indices": "int16, distinct sorted per neuron (reference init rule)",
+            "indices": INDEX_RULES[INDEX_RULE],
             "l2": "inputs larger than L2: 5.2 GB of parameters streamed from HBM every pass",
             "parallelism": f"group-shard x{world}" if world > 1 else "single GPU"}
 
@@ -202,6 +228,8 @@ def cpu_baseline(target_s=12.0, steps=1):
     def run(groups):
         L = SparseLayout(D, n_g * groups, groups, 8, 8, False)
         idx, w, b = init_parameters(L, "cpu", dtype=torch.float32, seed=2, bias_std=0.1)
+        if INDEX_RULE == "uniform":
+            uniform_indices_(idx, 1002)
         gen = torch.Generator().manual_seed(5)
         x = torch.randn(B, D, generator=gen).numpy()
         dy = torch.randn(B, groups, generator=gen).numpy()
@@ -236,6 +264,8 @@ def run_reference(args, rank, world):
     n_g = N // G
     L = SparseLayout(D, n_g * groups, groups, 8, 8, False)
     idx, w, b = init_parameters(L, "cpu", dtype=torch.float32, seed=2, bias_std=0.1)
+    if INDEX_RULE == "uniform":
+        uniform_indices_(idx, 1002)
     gen = torch.Generator().manual_seed(5)
     x = torch.randn(B, D, generator=gen).numpy()
     dy = torch.randn(B, groups, generator=gen).numpy()
@@ -690,9 +720,11 @@ def bench_fwdbwd256(args):
         if kind == "layer":
             lay = SparsePoolingLayer(D, N, G, shared_neurons=None, pooling="mean", dtype=torch.float32, device=dev,
                                      seed=1, bias_std=0.1)
+            if INDEX_RULE == "uniform":
+                uniform_indices_(lay.indices, 1001)
             names = ("fwd", "bwd")
         else:
-            lay = GroupShardedLayer(D, N, G, pooling="mean", device=dev, seed=1, bias_std=0.1)
+            lay = shard_layer(D, N, G, dev, seed=1)
             names = ("fwd_octet", "bwd_octet")
         lay.enable_main_grad()
         ev = {"fwd": [], "bwd": []}
@@ -1004,7 +1036,7 @@ def bench_locality(args):
 
 
 def main():
-    global N, G
+    global N, G, INDEX_RULE
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
@@ -1031,10 +1063,14 @@ def main():
                          "(TMEM), t5fwd / t5bwd = one of them; simt = the fp32 SIMT kernels (fp32 parameters)")
     ap.add_argument("--cover-outputs", type=int, default=2048,
                     help="cover16: outputs of 24,576 neurons (default 2048 = config 4; fewer for ncu captures)")
+    ap.add_argument("--index-rule", default=INDEX_RULE, choices=sorted(INDEX_RULES),
+                    help="layer100m / fwdbwd256: the reference's distinct-sorted init, or the configs' uniform "
+                         "rule with replacement")
     ap.add_argument("--groups", type=int, default=G,
                     help="pooling groups of 24,576 neurons (default 4096 = the full 100M layer; smaller values "
                          "give the reduced cases used for ncu captures)")
     args = ap.parse_args()
+    INDEX_RULE = args.index_rule
     if args.groups != G:
         N, G = args.groups * (N // G), args.groups
     if args.warmup < 3 and args.impl == "ours":
@@ -1085,7 +1121,7 @@ def main():
         os.environ.setdefault("MASTER_PORT", str(29500 + (os.getpid() % 1000)))
         dist.init_process_group("nccl", rank=0, world_size=1, timeout=timedelta(seconds=300), device_id=dev)
 
-    lay = GroupShardedLayer(D, N, G, pooling="mean", device=dev, seed=2 + 0, bias_std=0.1)
+    lay = shard_layer(D, N, G, dev, seed=2)
     opt = FusedAdamW([lay.weight, lay.bias], lr=1e-3, betas=(0.9, 0.999), eps=1e-8, moments="fp32")
     trainer = ShardedTrainStep(lay, opt)
     n_local = int(lay.counts.sum())
