@@ -76,7 +76,7 @@ import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
 D, N, G, B = 4096, 100_663_296, 4096, 1024
-INDEX_RULE = "distinct"   # --index-rule: "distinct" (the reference's init) or "uniform" (configs 2 / 3 as written)
+INDEX_RULE = "uniform"    # --index-rule: "uniform" (configs 2 / 3 as written) or "distinct" (the reference's init)
 INDEX_RULES = {"distinct": "int16, distinct sorted per neuron (reference init rule)",
                "uniform": "int16 storage of the configs' uniform int32 rule: every index uniform in [0, D) with "
                           "replacement (D = 4096 fits int16)"}
