@@ -468,7 +468,7 @@ __device__ __forceinline__ void t5_mma_terms(uint32_t d_t, uint32_t idesc, FA ad
     }
 }
 
-// The bf16 terms of (a, b) as packed pairs (a in the low half): ND rounds of round-to-nearest and subtract.
+// The bf16 terms of (a, b) as packed pairs (a in the low half): ND steps of round-to-nearest and subtract.
 template <int ND>
 __device__ __forceinline__ void t5_pair_terms(float a, float b, uint32_t (&u)[ND]) {
 #pragma unroll
