@@ -410,7 +410,7 @@ static int t5_fwd_run(const GlK16Args* args, int32_t* status, void* stream) {
 // parameters (NS = 1): x and w one bf16 term, dz two (hi + lo, the reference's split precision); fp32
 // parameters (NS = 3): three terms each, term pairs i + j <= 2 per product, as the forward.
 //
-// Warp roles (416 threads), handing work over through mbarriers (every wait has an iteration limit; on
+// Warp roles (448 threads), handing work over through mbarriers (every wait has an iteration limit; on
 // expiry the CTA records a timeout in *status, every role leaves its loop, and the TMEM is still freed):
 //   warps 0-7   dz epilogue: warp w reads TMEM lanes 32 (w % 4) .. (tokens) and computes dz for the 64
 //               neurons of records 4 (w / 4) ..; at the end they add dXs to dx;
@@ -418,7 +418,9 @@ static int t5_fwd_run(const GlK16Args* args, int32_t* status, void* stream) {
 //               half x neuron): it finds the records and loads their operands a batch ahead, expands the
 //               weights into W, and after the batch's products reads the 16 dWs columns of each record
 //               (one tcgen05.ld per column, one wait) and db;
-//   warp 12     allocates TMEM, and its lane 0 issues the MMAs.
+//   warp 12     allocates TMEM, and its lane 0 issues the Z and dX MMAs;
+//   warp 13     its lane 0 issues the dW | db MMAs (narrow products whose issue, not the tensor pipe, bounds a
+//               single issuing thread), committing to the same barrier as warp 12.
 // bf16 parameters keep three W buffers and two dz buffers, so the next batch's Z product runs ahead of the
 // current batch's products while its dz epilogue runs; fp32 ones (three-term planes) fit one buffer of each,
 // and then only Z and dWs (in TMEM) are double-buffered.  With bf16 parameters the epilogue also writes the
@@ -430,8 +432,8 @@ static int t5_fwd_run(const GlK16Args* args, int32_t* status, void* stream) {
 constexpr uint32_t kT5DzPlane = 32768;    // dz [128 tokens][128 neurons]: two 64-neuron halves of 16 KiB
 constexpr uint32_t kT5DzHalf = 16384;
 constexpr int kB5EpiWarps = 8;                       // dz epilogue: warps 0-7
-constexpr int kB5Issuer = kB5EpiWarps + 4;            // producer: warps 8-11; MMA issuer: warp 12
-constexpr int kB5Threads = 32 * (kB5Issuer + 1);
+constexpr int kB5Issuer = kB5EpiWarps + 4;            // producer: warps 8-11; MMA issuers: warps 12 and 13
+constexpr int kB5Threads = 32 * (kB5Issuer + 2);
 constexpr int kB5EpiArrivals = 32 * kB5EpiWarps, kB5ProdArrivals = 128;   // one arrival per thread
 constexpr int kB5Meta = 4;                            // batches whose record data is kept (ring)
 constexpr uint32_t kB5TZ = 0, kB5TdX = 256, kB5TdW = 320, kB5DWCols = 80;
@@ -487,7 +489,7 @@ struct B5Shared {   // 16-byte members first: bias and env are read as 16-byte v
   uint4 env[kB5Meta][8];
   int4 bk_row[kB5Buckets];
   long long rf[kB5Meta][8];
-  uint64_t w_full[3], z_full[2], z_empty[2], dz_full[2], mma2[2], dw_empty[2], fin;
+  uint64_t w_full[3], z_full[2], z_empty[2], dz_full[2], mma2[2], dw_empty[2], fin[2];
   int bk_rec[kB5Buckets + 1];
   int rg[kB5Meta][8], rnv[kB5Meta][8];
   int fq[kT5Set];
@@ -570,10 +572,11 @@ __global__ void __launch_bounds__(kB5Threads, 1) k16t5_bwd_kernel(const K16T5Par
       t5_mbar_init(t5_smem_u32(&sh.z_full[i]), 1);
       t5_mbar_init(t5_smem_u32(&sh.z_empty[i]), kB5EpiArrivals);
       t5_mbar_init(t5_smem_u32(&sh.dz_full[i]), kB5EpiArrivals);
-      t5_mbar_init(t5_smem_u32(&sh.mma2[i]), 1);
+      t5_mbar_init(t5_smem_u32(&sh.mma2[i]), 2);   // the dX and the dW issuer commit
       t5_mbar_init(t5_smem_u32(&sh.dw_empty[i]), kB5ProdArrivals);
     }
-    t5_mbar_init(t5_smem_u32(&sh.fin), 1);
+    t5_mbar_init(t5_smem_u32(&sh.fin[0]), 1);
+    t5_mbar_init(t5_smem_u32(&sh.fin[1]), 1);
     sh.abort = 0;
   }
   if (tid < kT5Set) {
@@ -823,10 +826,13 @@ __global__ void __launch_bounds__(kB5Threads, 1) k16t5_bwd_kernel(const K16T5Par
       }
     }
   } else {
-    // ---- MMA issuer (lane 0 issues; the warp waits)
+    // ---- MMA issuers (lane 0 issues; the warp waits): warp 12 the Z and dX products, warp 13 the dW | db
+    // products, each committing to mma2 (two arrivals per batch)
+    const bool dw_role = warp == kB5Issuer + 1;
     const uint32_t xs_u = t5_smem_u32(xpl), ws_u = t5_smem_u32(wpl), ds_u = t5_smem_u32(dpl);
     const uint32_t idz = t5_idesc_bf16(128, 128, 0, 0), idx_ = t5_idesc_bf16(128, 64, 0, 1),
                    idw = t5_idesc_bf16(128, 64, 1, 1), idw80 = t5_idesc_bf16(128, 80, 1, 1);
+    constexpr int top = (ND > NS ? ND : NS) - 1;
     bool issued = false;
     auto issue_z = [&](int b) -> bool {
       if (!b5_wait(sh, sh.w_full[b % NWB], (uint32_t)((b / NWB) & 1), p.status)) return false;
@@ -845,15 +851,13 @@ __global__ void __launch_bounds__(kB5Threads, 1) k16t5_bwd_kernel(const K16T5Par
       issued = true;
       return true;
     };
-    auto issue_2 = [&](int c) -> bool {
+    // dXs += dz W: term pairs (dz i, w j), i + j <= max(ND, NS) - 1, the smallest first
+    auto issue_dx = [&](int c) -> bool {
       if (!b5_wait(sh, sh.dz_full[c % NZB], (uint32_t)((c / NZB) & 1), p.status)) return false;
-      if (c >= 2 && !b5_wait(sh, sh.dw_empty[c & 1], (uint32_t)(((c >> 1) - 1) & 1), p.status)) return false;
       if (lane == 0) {
         const uint32_t wsb = ws_u + (uint32_t)((c % NWB) * NS) * kT5Plane;
         const uint32_t dsb = ds_u + (uint32_t)((c % NZB) * ND) * kT5DzPlane;
-        // dXs += dz W: term pairs (dz i, w j), i + j <= ND - 1 ... the smallest first
         uint32_t first = c == 0 ? 1u : 0u;
-        constexpr int top = (ND > NS ? ND : NS) - 1;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
 #pragma unroll
@@ -872,10 +876,20 @@ __global__ void __launch_bounds__(kB5Threads, 1) k16t5_bwd_kernel(const K16T5Par
               }
               first = 0;
             }
-        // dWs | db = dz^T [X | 1]: term pairs (dz i, x j); x term 0 carries the ones column (N = 80).  Within a
-        // sum the pair with j = 0 comes first, so the MMA that clears the accumulator also clears db's column
-        // (an MMA with accumulate = 0 clears only the N columns it writes).
-        first = 1;
+        t5_commit(t5_smem_u32(&sh.mma2[c & 1]));
+      }
+      __syncwarp();
+      return true;
+    };
+    // dWs | db = dz^T [X | 1]: term pairs (dz i, x j); x term 0 carries the ones column (N = 80).  Within a sum
+    // the pair with j = 0 comes first, so the MMA that clears the accumulator also clears db's column (an MMA
+    // with accumulate = 0 clears only the N columns it writes).
+    auto issue_dw = [&](int c) -> bool {
+      if (!b5_wait(sh, sh.dz_full[c % NZB], (uint32_t)((c / NZB) & 1), p.status)) return false;
+      if (c >= 2 && !b5_wait(sh, sh.dw_empty[c & 1], (uint32_t)(((c >> 1) - 1) & 1), p.status)) return false;
+      if (lane == 0) {
+        const uint32_t dsb = ds_u + (uint32_t)((c % NZB) * ND) * kT5DzPlane;
+        uint32_t first = 1;
         const uint32_t dwt = tmem + kB5TdW + kB5DWCols * (uint32_t)(c & 1);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
@@ -893,23 +907,28 @@ __global__ void __launch_bounds__(kB5Threads, 1) k16t5_bwd_kernel(const K16T5Par
         t5_commit(t5_smem_u32(&sh.mma2[c & 1]));
       }
       __syncwarp();
+      issued = true;
       return true;
     };
-    if (NWB >= 2 && NZB >= 2) {   // Z of the next batch ahead of this batch's products
+    if (dw_role) {
+      for (int c = 0; c < nbatch; ++c)
+        if (!issue_dw(c)) break;
+    } else if (NWB >= 2 && NZB >= 2) {   // Z of the next batch ahead of this batch's dX product
       if (nbatch > 0 && issue_z(0)) {
         for (int c = 0; c < nbatch; ++c) {
           if (c + 1 < nbatch && !issue_z(c + 1)) break;
-          if (!issue_2(c)) break;
+          if (!issue_dx(c)) break;
         }
       }
     } else {
       for (int c = 0; c < nbatch; ++c)
-        if (!issue_z(c) || !issue_2(c)) break;
+        if (!issue_z(c) || !issue_dx(c)) break;
     }
     if (issued) {   // every MMA this thread issued has completed before the TMEM is freed
-      if (lane == 0) t5_commit(t5_smem_u32(&sh.fin));
+      uint64_t& fin = sh.fin[dw_role ? 1 : 0];
+      if (lane == 0) t5_commit(t5_smem_u32(&fin));
       __syncwarp();
-      const bool done = t5_mbar_wait(t5_smem_u32(&sh.fin), 0, kT5WaitLimit);
+      const bool done = t5_mbar_wait(t5_smem_u32(&fin), 0, kT5WaitLimit);
       if (!__all_sync(kFullMask, done) && lane == 0) {
         if (p.status) atomicExch(p.status, 1);
         *abort_v = 1;
