@@ -231,6 +231,19 @@ class Level1Runtime:
             self._rowmax, self._rowmax_key = out, key
         return self._rowmax
 
+    def feature_prefix(self) -> torch.Tensor:
+        """Record inputs per feature cumulated over the groups ((G+1) x D int32, gl_group_feature_prefix), which
+        the lane-per-neuron backward subtracts its rounding offsets by; depends only on the indices and counts,
+        recomputed when the index tensor changes."""
+        key = (self.idx.data_ptr(), self.idx._version, self.counts_i32.data_ptr())
+        if getattr(self, "_fprefix_key", None) != key:
+            D = self.layout.input_dim
+            out = torch.empty((self.groups + 1) * D, device=self.idx.device, dtype=torch.int32)
+            _native.group_feature_prefix(self.idx, self.counts_i32, D, self.layout.blocks_per_group, 0, self.groups,
+                                         out)
+            self._fprefix, self._fprefix_key = out, key
+        return self._fprefix
+
     def order(self, tokens: int) -> Optional[torch.Tensor]:
         """Bank-aware processing order for a kernel running token tiles of ``tokens`` (one wavefront
         serves 32 / tokens neurons; orders are built for 4 and 8), or None for slot order.  Depends
@@ -553,9 +566,10 @@ class Level1Runtime:
             rowmax = self.rowmax()
             if self.octet_kernels(B, D):
                 _native.bwd_octet(x, self.idx, w, b, self.counts_i32, c1, dx, dw_buf, db_buf,
-                                  self.layout.blocks_per_group, 0, self.groups, self.pool, self.act, wabsmax, rowmax)
+                                  self.layout.blocks_per_group, 0, self.groups, self.pool, self.act, wabsmax, rowmax,
+                                  feat_prefix=self.feature_prefix())
                 self.last_info["backward_backend"] = "b200"
-                self.last_info["backward_kernel"] = "gl_bwd_octet_f32"
+                self.last_info["backward_kernel"] = "gl_bwd_octet_prefix_f32"
                 self.last_info["dx_accumulation"] = "int32 fixed point"
                 return dx
         _native.bwd(x, self.idx, w, b, self.counts_i32, c1, dx, dw_buf, db_buf, self.layout.blocks_per_group,

@@ -196,12 +196,19 @@ struct OctBwdParams {
   float* db;
   const float* wabsmax;
   const int32_t* rowmax;
+  const int32_t* fprefix;   // FOLD: [g1-g0+1][D] record inputs per feature over the groups g0 .. g0+i-1
   int B, D;
   int64_t NB, g0, g1, ldx, ldg, lddx;
   int pool, gpc, xoff;
 };
 
-template <int ACT, int XOFF>
+// FOLD: the dX tile accumulates the rounding's raw bits, the fixed-point value plus the magic number's bit
+// pattern 0x4B400000, and the flush subtracts that pattern once per record input of the word's feature in the
+// block's groups (every record input adds to each of the feature's 4 token words once); integer sums modulo
+// 2^32, so dX is bit for bit that of the per-term subtraction, one instruction fewer per shared atomic.
+constexpr uint32_t kOctMagicBits = 0x4B400000u;
+
+template <int ACT, int XOFF, bool FOLD>
 __global__ void __launch_bounds__(kOctThreads, 1) bwd_octet_kernel(const OctBwdParams p) {
   extern __shared__ __align__(16) float smem[];
   __shared__ float s_scale[4], s_inv[4];
@@ -293,7 +300,8 @@ __global__ void __launch_bounds__(kOctThreads, 1) bwd_octet_kernel(const OctBwdP
         int* row = dxi + (d[k] << 2);
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          const int v = __float_as_int(fmaf(dq[j], wk, 12582912.f)) - 0x4B400000;
+          const int v = FOLD ? __float_as_int(fmaf(dq[j], wk, 12582912.f))
+                             : __float_as_int(fmaf(dq[j], wk, 12582912.f)) - (int)kOctMagicBits;
           atomicAdd(row + (j ^ q), v);
         }
       }
@@ -314,10 +322,14 @@ __global__ void __launch_bounds__(kOctThreads, 1) bwd_octet_kernel(const OctBwdP
   }
   __syncthreads();
   const float nan = __int_as_float(0x7fc00000);
+  const int32_t* fp_lo = FOLD ? p.fprefix + (gb - p.g0) * (int64_t)D : nullptr;
+  const int32_t* fp_hi = FOLD ? p.fprefix + (ge - p.g0) * (int64_t)D : nullptr;
   for (int e = threadIdx.x; e < D * 4; e += kOctThreads) {
     const int t = e / D, dd = e - t * D;
     if (t0 + t < p.B) {
-      const float v = s_bad[t] ? nan : (float)dxi[dd * 4 + t] * s_inv[t];
+      int word = dxi[dd * 4 + t];
+      if (FOLD) word = (int)((uint32_t)word - (uint32_t)(__ldg(fp_hi + dd) - __ldg(fp_lo + dd)) * kOctMagicBits);
+      const float v = s_bad[t] ? nan : (float)word * s_inv[t];
       if (v != 0.f) red_add(p.dx + (int64_t)(t0 + t) * p.lddx + dd, v);
     }
   }
@@ -350,7 +362,7 @@ static int launch_fwd_octet(const OctFwdParams& p, dim3 grid, size_t smem, cudaS
 
 template <int ACT, int OFF>
 static int launch_bwd_octet(const OctBwdParams& p, dim3 grid, size_t smem, cudaStream_t st) {
-  auto kern = bwd_octet_kernel<ACT, OFF>;
+  auto kern = p.fprefix ? bwd_octet_kernel<ACT, OFF, true> : bwd_octet_kernel<ACT, OFF, false>;
   int rc = ensure_dynamic_smem((const void*)kern, smem);
   if (rc) return rc;
   kern<<<grid, kOctThreads, smem, st>>>(p);
@@ -403,7 +415,7 @@ extern "C" int gl_fwd_octet_f32(const GlFwdArgs* args, void* stream) {
   }
 }
 
-extern "C" int gl_bwd_octet_f32(const GlBwdArgs* args, void* stream) {
+static int bwd_octet_run(const GlBwdArgs* args, const int32_t* fprefix, void* stream) {
   if (!args) return GL_ERR_NULL;
   const GlBwdArgs& a = *args;
   if (a.B < 0 || a.D < 1 || a.D > 32767 || a.NB < 1 || a.g0 < 0 || a.g1 < a.g0) return GL_ERR_SHAPE;
@@ -425,8 +437,8 @@ extern "C" int gl_bwd_octet_f32(const GlBwdArgs* args, void* stream) {
   const int gpc = oct_groups_per_cta(tiles, G, sms, a.groups_per_cta);
   const int64_t chunks = (G + gpc - 1) / gpc;
   if (tiles > 2147483647LL || chunks > 65535) return GL_ERR_SHAPE;
-  OctBwdParams p{a.x, a.idx, a.w, a.b, a.counts, a.gpre, a.dx, a.dw, a.db, a.wabsmax, a.rowmax, (int)a.B, (int)a.D,
-                 a.NB, a.g0, a.g1, a.ldx, a.ldg, a.lddx, a.pool, gpc, (int)(16 * a.D)};
+  OctBwdParams p{a.x, a.idx, a.w, a.b, a.counts, a.gpre, a.dx, a.dw, a.db, a.wabsmax, a.rowmax, fprefix, (int)a.B,
+                 (int)a.D, a.NB, a.g0, a.g1, a.ldx, a.ldg, a.lddx, a.pool, gpc, (int)(16 * a.D)};
   const dim3 grid((unsigned)tiles, (unsigned)chunks);
   cudaStream_t st = (cudaStream_t)stream;
   const bool fixed_off = a.D == 4096;
@@ -441,4 +453,74 @@ extern "C" int gl_bwd_octet_f32(const GlBwdArgs* args, void* stream) {
       return fixed_off ? launch_bwd_octet<GL_ACT_GELU, 65536>(p, grid, smem, st)
                        : launch_bwd_octet<GL_ACT_GELU, 0>(p, grid, smem, st);
   }
+}
+
+extern "C" int gl_bwd_octet_f32(const GlBwdArgs* args, void* stream) { return bwd_octet_run(args, nullptr, stream); }
+
+extern "C" int gl_bwd_octet_prefix_f32(const GlBwdArgs* args, const int32_t* feat_prefix, void* stream) {
+  if (!feat_prefix) return GL_ERR_NULL;
+  if ((uintptr_t)feat_prefix & 3) return GL_ERR_ALIGN;
+  return bwd_octet_run(args, feat_prefix, stream);
+}
+
+// ---------------------------------------------------------------------------------------------------
+// Record inputs per feature, cumulated over groups: out[i][d] = number of (record, input) pairs of groups
+// g0 .. g0+i-1 whose index (clamped to D-1, as the kernels clamp) is d, over each group's valid records.
+
+namespace gl {
+
+__global__ void __launch_bounds__(512) group_feature_hist_kernel(const int16_t* __restrict__ idx,
+                                                                 const int32_t* __restrict__ counts, int D,
+                                                                 int64_t NB, int64_t g0, int32_t* __restrict__ out) {
+  extern __shared__ int hist[];
+  const int64_t g = g0 + blockIdx.x;
+  for (int d = threadIdx.x; d < D; d += blockDim.x) hist[d] = 0;
+  __syncthreads();
+  const int slots = (int)(NB * 8);
+  const int ng = min(__ldg(counts + g), slots);
+  const int16_t* rec = idx + g * (int64_t)slots * 8;
+  for (int e = threadIdx.x; e < ng * 8; e += blockDim.x) {
+    const int d = min((int)(uint16_t)__ldg(rec + e), D - 1);
+    atomicAdd(&hist[d], 1);
+  }
+  __syncthreads();
+  int32_t* row = out + (int64_t)(blockIdx.x + 1) * D;
+  for (int d = threadIdx.x; d < D; d += blockDim.x) row[d] = hist[d];
+}
+
+__global__ void group_feature_scan_kernel(int32_t* __restrict__ out, int D, int64_t G) {
+  const int d = blockIdx.x * blockDim.x + threadIdx.x;
+  if (d >= D) return;
+  int32_t acc = 0;
+  out[d] = 0;
+  for (int64_t i = 1; i <= G; ++i) {
+    acc += out[i * D + d];
+    out[i * D + d] = acc;
+  }
+}
+
+}  // namespace gl
+
+extern "C" int gl_group_feature_prefix(const int16_t* idx, const int32_t* counts, int64_t D, int64_t NB, int64_t g0,
+                                       int64_t g1, int32_t* out, void* stream) {
+  if (D < 1 || D > 32767 || NB < 1 || g0 < 0 || g1 < g0 || g1 - g0 > 2147483647LL) return GL_ERR_SHAPE;
+  if (!out) return GL_ERR_NULL;
+  cudaStream_t st = (cudaStream_t)stream;
+  const int64_t G = g1 - g0;
+  if (G > 0) {
+    if (!idx || !counts) return GL_ERR_NULL;
+    if ((uintptr_t)idx & 15) return GL_ERR_ALIGN;
+    const size_t smem = (size_t)D * 4;
+    int rc = ensure_dynamic_smem((const void*)group_feature_hist_kernel, smem);
+    if (rc) return rc;
+    group_feature_hist_kernel<<<(unsigned)G, 512, smem, st>>>(idx, counts, (int)D, NB, g0, out);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return set_cuda_error(e);
+    count_launches(1);
+  }
+  group_feature_scan_kernel<<<(unsigned)((D + 255) / 256), 256, 0, st>>>(out, (int)D, G);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_cuda_error(e);
+  count_launches(1);
+  return GL_OK;
 }

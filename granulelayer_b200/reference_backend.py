@@ -31,7 +31,7 @@ from pathlib import Path
 
 import torch
 
-ABI_VERSION = 16
+ABI_VERSION = 17
 P, I64, I32, F32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32, ctypes.c_float
 
 

@@ -44,7 +44,7 @@
 extern "C" {
 #endif
 
-#define GL_ABI_VERSION 16
+#define GL_ABI_VERSION 17
 
 typedef enum GlStatus {
   GL_OK = 0,
@@ -253,6 +253,16 @@ int gl_group_octets(const int16_t* idx, const int32_t* counts, int64_t D, int64_
  * record layout. */
 int gl_fwd_octet_f32(const GlFwdArgs* args, void* stream);
 int gl_bwd_octet_f32(const GlBwdArgs* args, void* stream);
+/* The same backward with `feat_prefix` from gl_group_feature_prefix over the args' group range g0 .. g1: the
+ * int32 dX tile then accumulates the rounding's raw bits and its flush subtracts the magic number's bit pattern
+ * once per record input of the feature in the block's groups, one instruction fewer per shared atomic; dx, dw,
+ * db as gl_bwd_octet_f32 (dX bit for bit: integer sums modulo 2^32).  feat_prefix must describe the current
+ * indices and counts. */
+int gl_bwd_octet_prefix_f32(const GlBwdArgs* args, const int32_t* feat_prefix, void* stream);
+/* out [(g1-g0+1) * D] int32: out[i*D + d] = number of (record, input) pairs of groups g0 .. g0+i-1 (their valid
+ * records) whose index, clamped to D-1, is d.  Mode-A indices [G, NB, 8, 8] int16 (any storage order). */
+int gl_group_feature_prefix(const int16_t* idx, const int32_t* counts, int64_t D, int64_t NB, int64_t g0, int64_t g1,
+                            int32_t* out, void* stream);
 
 /* Mode B (shared index records), fp32.  Block j of group g holds C neurons (C = 8, 16, 32 or 64)
  * sharing one 8-input record; slot s = j*C + c is valid iff s < counts[g]:

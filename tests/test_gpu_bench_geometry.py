@@ -118,7 +118,7 @@ def test_bench_engine_shard_at_bench_geometry(rule, B):
         got = _step(shard, x, dy, canon=shard.canonical)
         assert shard.input_order is not None, "GPU shards are stored in octet order"
         info = shard.runtime().last_info
-        assert (info["forward_kernel"], info["backward_kernel"]) == ("gl_fwd_octet_f32", "gl_bwd_octet_f32")
+        assert (info["forward_kernel"], info["backward_kernel"]) == ("gl_fwd_octet_f32", "gl_bwd_octet_prefix_f32")
         _check(got, _oracle(rule, B, G), f"shard {rule} B={B}")
     finally:
         dist.destroy_process_group()

@@ -213,7 +213,7 @@ def test_drop_in_layer_with_octet_layout():
         y.backward(dy)
         outs.append((y.detach(), xr.grad))
     assert lay.last_info["forward_kernel"] == "gl_fwd_octet_f32"
-    assert lay.last_info["backward_kernel"] == "gl_bwd_octet_f32"
+    assert lay.last_info["backward_kernel"] == "gl_bwd_octet_prefix_f32"
     assert_close(outs[1][0], outs[0][0], what="y", **FWD)
     assert_close(outs[1][1], outs[0][1], what="dx", **BWD)
     assert_close(lay.canonical(lay.weight.grad), ref.weight.grad, what="dw", **BWD)
@@ -247,3 +247,55 @@ def test_octet_layout_keeps_slot_order_where_its_kernels_do_not_run(D, pool, acc
     assert lay._order is None and torch.equal(lay.weight.detach(), ref.weight.detach())
     assert lay.last_info.get("forward_kernel") != "gl_fwd_octet_f32"
     assert_close(y.detach(), yr.detach(), what="y", **FWD)
+
+
+@pytest.mark.parametrize("rule", ["distinct", "uniform"])
+def test_feature_prefix_counts_record_inputs(rule):
+    """gl_group_feature_prefix: per feature, the record inputs of the valid records of groups g0 .. g0+i-1
+    (duplicate indices counted with their multiplicity), over a sub-range of the groups."""
+    D, G = 300, 7
+    L, idx, _, _ = _layer(D, 7 * 900 - 13, G, seed=5, rule=rule)
+    g0, g1 = 2, 6
+    out = torch.empty((g1 - g0 + 1) * D, dtype=torch.int32, device="cuda")
+    _native.group_feature_prefix(idx.cuda(), L.counts_tensor("cuda").to(torch.int32), D, L.blocks_per_group, g0, g1,
+                                 out)
+    counts = L.counts_tensor("cpu")
+    want = torch.zeros(g1 - g0 + 1, D, dtype=torch.int64)
+    for i, g in enumerate(range(g0, g1)):
+        rec = idx[g].reshape(-1, 8)[: int(counts[g])].reshape(-1).long()
+        want[i + 1] = want[i] + torch.bincount(rec, minlength=D)
+    assert torch.equal(out.cpu().reshape(g1 - g0 + 1, D).long(), want)
+
+
+@pytest.mark.parametrize("rule", ["distinct", "uniform"])
+def test_prefix_backward_equals_the_plain_one(rule):
+    """gl_bwd_octet_prefix_f32 accumulates the rounding's raw bits and subtracts the offsets at the flush:
+    with one group chunk per token block (so every dx element receives one flush) its dx is bit for bit that
+    of gl_bwd_octet_f32; dw / db agree within the backward tolerance (their global reductions' order varies)."""
+    D, H, G, B = 512, 4 * 3000 + 77, 4, 37
+    L, idx, w, b = _layer(D, H, G, seed=11, rule=rule)
+    order, kp = _arrange(L, idx)
+    idx, w, b = _apply(idx, order, kp), _interleave(_apply(w, order, kp)), _apply(b, order, kp)
+    dev = "cuda"
+    idx, w, b = idx.to(dev), w.to(dev), b.to(dev)
+    counts = L.counts_tensor(dev).to(torch.int32)
+    gen = torch.Generator().manual_seed(3)
+    x = torch.randn(B, D, generator=gen).to(dev)
+    gpre = torch.randn(B, G, generator=gen).to(dev)
+    NB = L.blocks_per_group
+    wabsmax = w.reshape(G, -1).abs().amax(1).contiguous()
+    rowmax = torch.empty(G, device=dev, dtype=torch.int32)
+    _native.group_index_maxcount(idx, counts, D, NB, 0, G, rowmax)
+    prefix = torch.empty((G + 1) * D, dtype=torch.int32, device=dev)
+    _native.group_feature_prefix(idx, counts, D, NB, 0, G, prefix)
+    outs = []
+    for fp in (None, prefix):
+        dx = torch.zeros(B, D, device=dev)
+        dw, db = torch.zeros_like(w), torch.zeros_like(b)
+        _native.bwd_octet(x, idx, w, b, counts, gpre, dx, dw, db, NB, 0, G, POOLS["mean"], _native.ACT_IDS["relu"],
+                          wabsmax, rowmax, groups_per_cta=G, feat_prefix=fp)
+        torch.cuda.synchronize()
+        outs.append((dx.cpu(), dw.cpu(), db.cpu()))
+    assert torch.equal(outs[0][0], outs[1][0]), "dx of the folded flush"
+    assert_close(outs[1][1], outs[0][1], what="dw", **BWD)
+    assert_close(outs[1][2], outs[0][2], what="db", **BWD)
