@@ -111,7 +111,7 @@ FALLBACK_HBM_GBS = 6650.0
 # BWD_PROFILE (512 x 24,576 neurons); the traffic grows with the neuron count, so a full launch is
 # this figure times N.
 BWD_PROFILE = "profiles/octet_kernels_g512.md"
-BWD_DRAM_BYTES_PER_NEURON = (1.333016e9 + 0.521707e9) / (512 * 24576)   # the uniform-rule capture
+BWD_DRAM_BYTES_PER_NEURON = (1.350285e9 + 0.532295e9) / (512 * 24576)   # the folded backward's capture
 
 
 def param_bytes(n):
